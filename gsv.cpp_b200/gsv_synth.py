@@ -1,0 +1,121 @@
+"""Seeded synthetic AR weights and requests (no checkpoints or datasets exist offline).
+
+`write_model` writes a GGUF file with the tensor names, shapes, dtypes and KV keys of the
+reference exporter (tools/export_gguf/convert_ar.py:91-130, dtype policy :76-89): attention and
+FFN matrices Q8_0 (``--spec attn=q8_0,ffn=q8_0``), everything else F32. Values are random:
+matrices and embeddings N(0, 0.02), LayerNorm weight 1 + N(0, 0.02), biases N(0, 0.02),
+PE alphas 1.0. Requests follow the benchmark shapes of the reference (tests/bench_ar_width.cpp:43-55):
+uniform phone ids in [0, 731], BERT features N(0, 1) laid out [1024][T], prompt codes in [0, 1023].
+"""
+from __future__ import annotations
+
+import os
+from dataclasses import dataclass
+
+import numpy as np
+
+
+@dataclass
+class Dims:
+    D: int = 512
+    NH: int = 16
+    NL: int = 24
+    V: int = 1025
+    PV: int = 732
+    EOS: int = 1024
+    BERT: int = 1024
+
+
+def write_model(path: str, seed: int = 0, dims: Dims | None = None, mat_type: str = "q8_0",
+                ln_noise: float = 0.02) -> str:
+    import gguf
+
+    d = dims or Dims()
+    rng = np.random.default_rng(seed)
+    D, FF = d.D, 4 * d.D
+    qt = {"q8_0": gguf.GGMLQuantizationType.Q8_0, "f32": gguf.GGMLQuantizationType.F32}[mat_type]
+
+    def n(*shape, s=0.02):
+        return (rng.standard_normal(shape, dtype=np.float32) * np.float32(s)).astype(np.float32)
+
+    w = gguf.GGUFWriter(path, "gsv.ar")
+    w.add_uint32("ar.hidden_dim", D)
+    w.add_uint32("ar.head", d.NH)
+    w.add_uint32("ar.n_layer", d.NL)
+    w.add_uint32("ar.vocab_size", d.V)
+    w.add_uint32("ar.phoneme_vocab_size", d.PV)
+    w.add_uint32("ar.eos", d.EOS)
+    w.add_float32("ar.bert_dim", float(d.BERT))
+
+    def add(name, arr, dtype=gguf.GGMLQuantizationType.F32):
+        arr = np.ascontiguousarray(arr, dtype=np.float32)
+        if dtype == gguf.GGMLQuantizationType.F32:
+            w.add_tensor(name, arr, raw_dtype=dtype)
+        else:
+            w.add_tensor(name, gguf.quants.quantize(arr, dtype), raw_dtype=dtype)
+
+    add("ar.text_emb", n(d.PV, D))
+    add("ar.audio_emb", n(d.V, D))
+    add("ar.bert_proj", n(D, d.BERT))
+    add("ar.bert_proj_b", n(D))
+    add("ar.text_pe_alpha", np.ones(1, np.float32))
+    add("ar.audio_pe_alpha", np.ones(1, np.float32))
+    add("ar.predict", n(d.V, D))
+    for li in range(d.NL):
+        p = f"transformer.block{li}"
+        add(f"{p}.qkv_w", n(3 * D, D), qt)
+        add(f"{p}.qkv_b", n(3 * D))
+        add(f"{p}.out_w", n(D, D), qt)
+        add(f"{p}.out_b", n(D))
+        add(f"{p}.norm1_w", 1.0 + n(D, s=ln_noise))
+        add(f"{p}.norm1_b", n(D, s=ln_noise))
+        add(f"{p}.ffn1_w", n(FF, D), qt)
+        add(f"{p}.ffn1_b", n(FF))
+        add(f"{p}.ffn2_w", n(D, FF), qt)
+        add(f"{p}.ffn2_b", n(D))
+        add(f"{p}.norm2_w", 1.0 + n(D, s=ln_noise))
+        add(f"{p}.norm2_b", n(D, s=ln_noise))
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    return path
+
+
+def cached_model(cache_dir: str, seed: int = 0, n_layer: int = 24, mat_type: str = "q8_0") -> str:
+    """Write (once) and return the path of a synthetic model in cache_dir."""
+    os.makedirs(cache_dir, exist_ok=True)
+    path = os.path.join(cache_dir, f"gsv_ar_synth_s{seed}_l{n_layer}_{mat_type}.gguf")
+    if not os.path.exists(path):
+        tmp = path + f".tmp{os.getpid()}"
+        write_model(tmp, seed=seed, dims=Dims(NL=n_layer), mat_type=mat_type)
+        os.replace(tmp, path)
+    return path
+
+
+@dataclass
+class Request:
+    """gsv_ar_request (reference src/gsv_ar.h:13-17)."""
+    phones: np.ndarray   # int32 [T]
+    bert: np.ndarray     # float32 [1024][T]
+    prompt: np.ndarray   # int32 [P]
+
+
+def make_request(rng: np.random.Generator, n_phones: int, n_prompt: int, bert_dim: int = 1024,
+                 phone_vocab: int = 732, code_max: int = 1023) -> Request:
+    return Request(
+        phones=rng.integers(0, phone_vocab, n_phones, dtype=np.int32),
+        bert=rng.standard_normal((bert_dim, n_phones), dtype=np.float32),
+        prompt=rng.integers(0, code_max + 1, n_prompt, dtype=np.int32),
+    )
+
+
+def ragged_requests(seed: int, B: int, lo: int = 80, hi: int = 400, text_frac: float = 0.7):
+    """Prefixes P ~ U[lo, hi] split round(0.7 P) phones / rest prompt codes (BASELINE configs 1 and 4)."""
+    rng = np.random.default_rng(seed)
+    out = []
+    for _ in range(B):
+        P = int(rng.integers(lo, hi + 1))
+        T = int(round(text_frac * P))
+        out.append(make_request(rng, T, P - T))
+    return out

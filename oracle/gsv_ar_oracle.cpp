@@ -1,0 +1,867 @@
+// gsv_ar_oracle.cpp -- TEST INFRASTRUCTURE ONLY (the parity checker, never the product).
+//
+// A CPU restatement of the reference AR path of gsv.cpp (GPT-SoVITS Text2SemanticDecoder):
+// prefill with the text-bidirectional / semantic-causal prefix mask, KV-cached decode, the
+// sampler and the generate loop, with the arithmetic of the ggml CPU ops the reference calls.
+// Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / --impl reference leg may
+// load this library. The CUDA library never links it, calls it or falls back to it.
+//
+// Reference citations are paths inside the gsv.cpp project. "P:<n>" is a line of
+// patches/0001-ggml-audio-patch-port-on-llamacpp.patch.
+//
+// ggml itself (llama.cpp f0c41e0168dfd4b5ef72b21d1a311b24cc7a894a) is not shipped with the
+// reference. The op semantics restated here are ggml's portable C paths:
+//   * Q8_0 mul_mat: src1 rows quantized with quantize_row_q8_0_ref semantics (d = amax/127,
+//     id = 1/d, roundf, d stored as fp16) -- pinned bit-exactly against gguf-py's Q8_0
+//     quantizer, which documents bit-exactness with ggml-quants.c; then per 32-block integer dot,
+//     accumulated in float block by block as sumf = fma((float)sumi, d_w*d_x, sumf).
+//   * F32 mul_mat / F32 vec_dot: float products accumulated in double, rounded once
+//     (ggml_vec_dot_f32 scalar path).
+//   * flash_attn_ext (F32 K/V): per query, keys in order, online softmax with expf, masked keys
+//     skipped, S = S*ms + vs and VKQ = VKQ*ms + v*vs as fused multiply-adds, out = VKQ * (1/S).
+//   * layernorm_affine (P:1535-1585): v = (x + r) + bias, mean / E[v^2] in double,
+//     var = E[v^2] - mean^2, inv = 1/sqrtf(var + eps), y = ((v - mean)*inv)*w + b.
+//   * add_act ReLU (P:1587-1620): y = max(a + b, 0).
+// Where the reference's C++ is compiled with -mavx2 -mfma (CMakeLists.txt:88-92) GCC contracts
+// a*b+c into an FMA; the restatement writes those FMAs out with fmaf() and is itself compiled
+// with -ffp-contract=off so nothing else is fused.
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <numeric>
+#include <string>
+#include <vector>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+namespace {
+
+// ------------------------------------------------------------------ fp16
+// IEEE binary32 -> binary16 with round-to-nearest-even (what GGML_FP32_TO_FP16 does via F16C).
+inline uint16_t f32_to_f16(float f) {
+    uint32_t x;
+    std::memcpy(&x, &f, 4);
+    const uint32_t sign = (x >> 16) & 0x8000u;
+    uint32_t mant = x & 0x7fffffu;
+    const int32_t exp = (int32_t)((x >> 23) & 0xffu);
+    if (exp == 0xff) return (uint16_t)(sign | 0x7c00u | (mant ? (0x200u | (mant >> 13)) : 0u));
+    const int32_t e = exp - 127 + 15;
+    if (e >= 31) return (uint16_t)(sign | 0x7c00u);
+    if (e <= 0) {
+        if (e < -10) return (uint16_t)sign;
+        mant |= 0x800000u;
+        const int shift = 14 - e;
+        uint32_t h = mant >> shift;
+        const uint32_t rem = mant & ((1u << shift) - 1u);
+        const uint32_t halfway = 1u << (shift - 1);
+        if (rem > halfway || (rem == halfway && (h & 1u))) h++;
+        return (uint16_t)(sign | h);
+    }
+    uint32_t h = sign | ((uint32_t)e << 10) | (mant >> 13);
+    const uint32_t rem = mant & 0x1fffu;
+    if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) h++;
+    return (uint16_t)h;
+}
+
+inline float f16_to_f32(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+    const uint32_t exp = (h >> 10) & 0x1fu;
+    uint32_t mant = h & 0x3ffu;
+    uint32_t x;
+    if (exp == 0) {
+        if (mant == 0) {
+            x = sign;
+        } else {
+            int e = -1;
+            do { mant <<= 1; e++; } while (!(mant & 0x400u));
+            mant &= 0x3ffu;
+            x = sign | ((uint32_t)(127 - 15 - e) << 23) | (mant << 13);
+        }
+    } else if (exp == 31) {
+        x = sign | 0x7f800000u | (mant << 13);
+    } else {
+        x = sign | ((exp - 15 + 127) << 23) | (mant << 13);
+    }
+    float f;
+    std::memcpy(&f, &x, 4);
+    return f;
+}
+
+inline float round_f16(float f) { return f16_to_f32(f32_to_f16(f)); }
+
+// ------------------------------------------------------------------ Q8_0
+constexpr int QK = 32;
+constexpr int Q8_BYTES = 34;   // fp16 d + 32 x int8
+
+// quantize_row_q8_0_ref semantics (ggml-quants.c; pinned via gguf-py's Q8_0 quantizer).
+void quantize_q8_0(const float* x, int64_t n, uint8_t* blocks) {
+    const int64_t nb = n / QK;
+    for (int64_t i = 0; i < nb; i++) {
+        float amax = 0.0f;
+        for (int j = 0; j < QK; j++) amax = std::max(amax, std::fabs(x[i * QK + j]));
+        const float d = amax / 127.0f;
+        const float id = d != 0.0f ? 1.0f / d : 0.0f;
+        uint8_t* b = blocks + i * Q8_BYTES;
+        const uint16_t dh = f32_to_f16(d);
+        std::memcpy(b, &dh, 2);
+        for (int j = 0; j < QK; j++) {
+            const float v = x[i * QK + j] * id;
+            b[2 + j] = (uint8_t)(int8_t)std::roundf(v);
+        }
+    }
+}
+
+inline float q8_d(const uint8_t* blk) {
+    uint16_t h;
+    std::memcpy(&h, blk, 2);
+    return f16_to_f32(h);
+}
+
+// ggml_vec_dot_q8_0_q8_0 semantics: exact integer block dot, float accumulation in block order.
+inline float vec_dot_q8_0(int64_t K, const uint8_t* w, const uint8_t* x) {
+    const int64_t nb = K / QK;
+    float sumf = 0.0f;
+    for (int64_t ib = 0; ib < nb; ib++) {
+        const int8_t* a = (const int8_t*)(w + ib * Q8_BYTES + 2);
+        const int8_t* b = (const int8_t*)(x + ib * Q8_BYTES + 2);
+        int32_t sumi = 0;
+        for (int j = 0; j < QK; j++) sumi += (int32_t)a[j] * (int32_t)b[j];
+        const float d = q8_d(w + ib * Q8_BYTES) * q8_d(x + ib * Q8_BYTES);
+        sumf = std::fmaf((float)sumi, d, sumf);
+    }
+    return sumf;
+}
+
+// ggml_vec_dot_f32 scalar semantics: float products, double accumulation, one final rounding.
+inline float vec_dot_f32(int64_t n, const float* x, const float* y) {
+    double s = 0.0;
+    for (int64_t i = 0; i < n; i++) s += (double)(x[i] * y[i]);
+    return (float)s;
+}
+
+int g_threads = 0;
+inline int nthreads() {
+#ifdef _OPENMP
+    return g_threads > 0 ? g_threads : omp_get_max_threads();
+#else
+    return 1;
+#endif
+}
+
+enum { T_F32 = 0, T_F16 = 1, T_Q8_0 = 8 };
+
+// A weight matrix [N][K] (torch [out,in] == ggml ne0=in), either F32 or Q8_0 raw GGUF blocks.
+struct Mat {
+    int type = T_F32;
+    int64_t N = 0, K = 0;
+    std::vector<float> f;
+    std::vector<uint8_t> q;
+};
+
+// Y[M][N] = mul_mat(W, X) for X [M][K]   (src/gsv_ar.cpp:244,260,262,263; ggml mul_mat)
+void mul_mat(const Mat& W, const float* X, int64_t M, float* Y) {
+    const int64_t N = W.N, K = W.K;
+    if (W.type == T_Q8_0) {
+        std::vector<uint8_t> xq((size_t)M * (K / QK) * Q8_BYTES);
+        #pragma omp parallel for num_threads(nthreads()) schedule(static)
+        for (int64_t m = 0; m < M; m++) quantize_q8_0(X + m * K, K, xq.data() + m * (K / QK) * Q8_BYTES);
+        #pragma omp parallel for num_threads(nthreads()) schedule(static)
+        for (int64_t n = 0; n < N; n++) {
+            const uint8_t* w = W.q.data() + n * (K / QK) * Q8_BYTES;
+            for (int64_t m = 0; m < M; m++)
+                Y[m * N + n] = vec_dot_q8_0(K, w, xq.data() + m * (K / QK) * Q8_BYTES);
+        }
+    } else {
+        #pragma omp parallel for num_threads(nthreads()) schedule(static)
+        for (int64_t n = 0; n < N; n++) {
+            const float* w = W.f.data() + n * K;
+            for (int64_t m = 0; m < M; m++) Y[m * N + n] = vec_dot_f32(K, w, X + m * K);
+        }
+    }
+}
+
+// layernorm_affine (P:1535-1585) as called by ln_affine (src/gsv_ar.cpp:157-165).
+void ln_affine(const float* x, const float* r, const float* bias, const float* w, const float* b,
+               int64_t rows, int64_t n, float eps, float* y) {
+    for (int64_t row = 0; row < rows; row++) {
+        const float* xr = x + row * n;
+        const float* rr = r ? r + row * n : nullptr;
+        double sum = 0.0, sum2 = 0.0;
+        for (int64_t i = 0; i < n; i++) {
+            const float v = (xr[i] + (rr ? rr[i] : 0.0f)) + (bias ? bias[i] : 0.0f);
+            sum += v;
+            sum2 += (double)v * (double)v;
+        }
+        const float mean = (float)(sum / (double)n);
+        const float var = std::fmaf(-mean, mean, (float)(sum2 / (double)n));
+        const float inv = 1.0f / std::sqrt(var + eps);
+        float* yr = y + row * n;
+        for (int64_t i = 0; i < n; i++) {
+            const float v = (xr[i] + (rr ? rr[i] : 0.0f)) + (bias ? bias[i] : 0.0f);
+            yr[i] = std::fmaf((v - mean) * inv, w[i], b[i]);
+        }
+    }
+}
+
+// add_act (P:1587-1620): act(a[i] + b[i % n]); act 1 = ReLU, 0 = identity.
+void add_act(const float* a, const float* b, int64_t rows, int64_t n, int act, float* y) {
+    for (int64_t r = 0; r < rows; r++)
+        for (int64_t i = 0; i < n; i++) {
+            const float v = a[r * n + i] + b[i];
+            y[r * n + i] = act == 1 ? (v > 0.0f ? v : 0.0f) : v;
+        }
+}
+
+// flash_attn_ext for one query row of one head (F32 K/V): keys in order, skip masked keys.
+// keep(k) decides visibility (the -inf/0 mask of src/gsv_ar.cpp:215-223, 450).
+template <class Keep>
+void attn_row(const float* q, const float* K, const float* Vv, int64_t kstride, int64_t nk, int hd, float scale,
+              Keep keep, float* out) {
+    float M = -INFINITY, S = 0.0f;
+    float acc[256];
+    for (int d = 0; d < hd; d++) acc[d] = 0.0f;
+    for (int64_t ic = 0; ic < nk; ic++) {
+        if (!keep(ic)) continue;
+        const float s = vec_dot_f32(hd, q, K + ic * kstride) * scale;
+        const float Mold = M;
+        float ms = 1.0f, vs = 1.0f;
+        if (s > M) {
+            M = s;
+            ms = std::exp(Mold - M);
+            for (int d = 0; d < hd; d++) acc[d] *= ms;
+        } else {
+            vs = std::exp(s - M);
+        }
+        const float* v = Vv + ic * kstride;
+        for (int d = 0; d < hd; d++) acc[d] = std::fmaf(v[d], vs, acc[d]);
+        S = std::fmaf(S, ms, vs);
+    }
+    const float S_inv = S == 0.0f ? 0.0f : 1.0f / S;
+    for (int d = 0; d < hd; d++) out[d] = acc[d] * S_inv;
+}
+
+// ------------------------------------------------------------------ sampler (src/gsv_sampler.cpp)
+struct SamplerCfg {
+    int top_k = 15;
+    float top_p = 1.0f, temperature = 1.0f, rep = 1.35f;
+};
+
+// gsv_logits_to_probs (src/gsv_sampler.cpp:8-68). Consumes `logits` in place.
+void logits_to_probs(const SamplerCfg& c, float* logits, int V, const int32_t* prev, int n_prev, float* probs) {
+    // 1) repetition penalty, applied once per occurrence (compounds on repeats), :14-20
+    if (prev && n_prev > 0 && c.rep != 1.0f) {
+        for (int i = 0; i < n_prev; i++) {
+            const int t = prev[i];
+            if (t < 0 || t >= V) continue;
+            const float s = logits[t];
+            logits[t] = s < 0.0f ? s * c.rep : s / c.rep;
+        }
+    }
+    // 2) nucleus: stable descending order, softmax in that order, cumulative sum, rank 0 kept, :23-42
+    if (c.top_p < 1.0f) {
+        std::vector<int> idx(V);
+        std::iota(idx.begin(), idx.end(), 0);
+        std::stable_sort(idx.begin(), idx.end(), [&](int a, int b) { return logits[a] > logits[b]; });
+        const float mx = logits[idx[0]];
+        float sum = 0.0f;
+        for (int k = 0; k < V; k++) sum += std::exp(logits[idx[k]] - mx);
+        const float inv_sum = 1.0f / sum;
+        float cum = 0.0f;
+        for (int k = 0; k < V; k++) {
+            cum = std::fmaf(std::exp(logits[idx[k]] - mx), inv_sum, cum);
+            if (k > 0 && cum > c.top_p) logits[idx[k]] = -INFINITY;
+        }
+    }
+    // 3) temperature, :45-46
+    const float t = std::max(c.temperature, 1e-5f);
+    for (int i = 0; i < V; i++) logits[i] /= t;
+    // 4) top-k: pivot = k-th largest value, strictly smaller -> -inf (ties kept), :49-56
+    if (c.top_k > 0 && c.top_k < V) {
+        std::vector<float> tmp(logits, logits + V);
+        std::sort(tmp.begin(), tmp.end(), std::greater<float>());
+        const float pivot = tmp[c.top_k - 1];
+        for (int i = 0; i < V; i++)
+            if (logits[i] < pivot) logits[i] = -INFINITY;
+    }
+    // 5) softmax, float accumulation in index order, :58-67
+    float mx = -INFINITY;
+    for (int i = 0; i < V; i++) mx = std::max(mx, logits[i]);
+    float sum = 0.0f;
+    for (int i = 0; i < V; i++) {
+        probs[i] = logits[i] == -INFINITY ? 0.0f : std::exp(logits[i] - mx);
+        sum += probs[i];
+    }
+    const float inv = 1.0f / sum;
+    for (int i = 0; i < V; i++) probs[i] *= inv;
+}
+
+// gsv_rng (src/gsv_sampler.h:33-42): xorshift64*, U = (next >> 40) / 2^24, q = -logf(1 - U).
+struct Rng {
+    uint64_t s;
+    explicit Rng(uint64_t seed) : s(seed ? seed : 1) {}
+    uint64_t next() {
+        s ^= s >> 12;
+        s ^= s << 25;
+        s ^= s >> 27;
+        return s * 0x2545F4914F6CDD1Dull;
+    }
+    float uniform01() { return (float)((double)(next() >> 40) * (1.0 / 16777216.0)); }
+    float exponential() { return -std::log(1.0f - uniform01()); }
+};
+
+// gsv_sample + gsv_argmax_probs_over_q (src/gsv_sampler.cpp:70-89).
+int sample(const float* probs, int V, Rng& rng) {
+    std::vector<float> q(V);
+    for (int i = 0; i < V; i++) q[i] = rng.exponential();
+    int best = 0;
+    float bv = -INFINITY;
+    for (int i = 0; i < V; i++) {
+        const float v = probs[i] > 0.0f ? probs[i] / q[i] : 0.0f;
+        if (v > bv) { bv = v; best = i; }
+    }
+    return best;
+}
+
+}  // namespace
+
+// ================================================================== model
+struct orc_layer {
+    Mat qkv_w, out_w, f1w, f2w;
+    std::vector<float> qkv_b, out_b, n1w, n1b, f1b, f2b, n2w, n2b;
+};
+
+struct orc_model {
+    int D = 512, NH = 16, HD = 32, NL = 24, V = 1025, PV = 732, EOS = 1024, BERT = 1024;
+    std::vector<orc_layer> L;
+    std::vector<float> text_emb, audio_emb, bert_proj, bert_proj_b;
+    Mat predict;
+    Mat bert_aug;     // [D][BERT+1] = [W | b]   (src/gsv_ar.cpp:648-656)
+    float text_alpha = 1.0f, audio_alpha = 1.0f;
+    std::vector<float> pe;   // [pe_max][D]  (src/gsv_ar.cpp:173-181)
+    int pe_max = 0;
+    std::string err;
+};
+
+namespace {
+
+bool set_mat(Mat& m, int type, const void* data, int64_t nbytes, int64_t N, int64_t K, std::string& err, const char* name) {
+    m.type = type;
+    m.N = N;
+    m.K = K;
+    if (type == T_F32) {
+        if (nbytes != N * K * 4) { err = std::string("bad size for ") + name; return false; }
+        m.f.assign((const float*)data, (const float*)data + N * K);
+    } else if (type == T_Q8_0) {
+        if (K % QK || nbytes != N * (K / QK) * Q8_BYTES) { err = std::string("bad size for ") + name; return false; }
+        m.q.assign((const uint8_t*)data, (const uint8_t*)data + nbytes);
+    } else {
+        err = std::string("unsupported type for ") + name;
+        return false;
+    }
+    return true;
+}
+
+bool set_vec(std::vector<float>& v, int type, const void* data, int64_t nbytes, int64_t n, std::string& err, const char* name) {
+    if (type != T_F32 || nbytes != n * 4) { err = std::string("expected F32[") + std::to_string(n) + "] for " + name; return false; }
+    v.assign((const float*)data, (const float*)data + n);
+    return true;
+}
+
+// mk_pe (src/gsv_ar.cpp:173-181)
+void make_pe(orc_model& m, int pe_max) {
+    m.pe_max = pe_max;
+    m.pe.assign((size_t)pe_max * m.D, 0.0f);
+    for (int pos = 0; pos < pe_max; pos++)
+        for (int i = 0; i < m.D; i += 2) {
+            const float div = std::exp((float)i * -(std::log(10000.0f) / (float)m.D));
+            m.pe[(size_t)pos * m.D + i] = std::sin((float)pos * div);
+            m.pe[(size_t)pos * m.D + i + 1] = std::cos((float)pos * div);
+        }
+}
+
+// One sequence's request (gsv_ar_request, src/gsv_ar.h:13-17).
+struct Req {
+    const int32_t* phones;
+    int T;
+    const float* bert;   // [BERT][T]
+    const int32_t* prompt;
+    int P;
+};
+
+// Per-sequence KV cache, [layer][pos][D] with head h at dims h*HD.. (F32, or values rounded
+// through fp16 when emulating an F16 cache).
+struct SeqCache {
+    int len = 0, cap = 0;
+    std::vector<float> k, v;
+};
+
+// Prefill of one sequence (build_inputs src/gsv_ar.cpp:186-225 without left padding; run_first
+// :228-293). Left padding keys are always masked in the reference, so a sequence computed alone
+// produces the same values. Returns last-row logits; K/V land in the cache.
+// dump (optional): per layer, last position: [attn out, n1, (n1 + W2 h) + b2, layer out].
+void prefill_one(const orc_model& m, const Req& r, bool kv_f16, SeqCache& cache, float* logits, float* dump) {
+    const int D = m.D, S = r.T + r.P, HD = m.HD, NH = m.NH;
+    std::vector<float> x((size_t)S * D), cur((size_t)S * D);
+    for (int t = 0; t < r.T; t++) {
+        const float* tok = m.text_emb.data() + (size_t)r.phones[t] * D;
+        for (int d = 0; d < D; d++) x[(size_t)t * D + d] = std::fmaf(m.text_alpha, m.pe[(size_t)t * D + d], tok[d]);
+    }
+    for (int t = 0; t < r.P; t++) {
+        const float* e = m.audio_emb.data() + (size_t)r.prompt[t] * D;
+        for (int d = 0; d < D; d++)
+            x[(size_t)(r.T + t) * D + d] = std::fmaf(m.audio_alpha, m.pe[(size_t)t * D + d], e[d]);
+    }
+    // cur = x + bert_aug . feat  (src/gsv_ar.cpp:241); feat = [bert; 1] on text rows, zeros on prompt rows
+    {
+        std::vector<float> feat((size_t)r.T * (m.BERT + 1));
+        for (int t = 0; t < r.T; t++) {
+            for (int k = 0; k < m.BERT; k++) feat[(size_t)t * (m.BERT + 1) + k] = r.bert[(size_t)k * r.T + t];
+            feat[(size_t)t * (m.BERT + 1) + m.BERT] = 1.0f;
+        }
+        std::vector<float> proj((size_t)r.T * D);
+        mul_mat(m.bert_aug, feat.data(), r.T, proj.data());
+        for (int t = 0; t < S; t++)
+            for (int d = 0; d < D; d++)
+                cur[(size_t)t * D + d] = x[(size_t)t * D + d] + (t < r.T ? proj[(size_t)t * D + d] : 0.0f);
+    }
+    cache.len = 0;
+    const float scale = 1.0f / std::sqrt((float)HD);
+    const int FF = (int)m.L[0].f1w.N;
+    std::vector<float> qkv((size_t)S * 3 * D), att((size_t)S * D), o((size_t)S * D), n1((size_t)S * D),
+        h((size_t)S * FF), h2((size_t)S * D);
+    for (int li = 0; li < m.NL; li++) {
+        const orc_layer& w = m.L[li];
+        mul_mat(w.qkv_w, cur.data(), S, qkv.data());
+        for (int t = 0; t < S; t++)
+            for (int j = 0; j < 3 * D; j++) qkv[(size_t)t * 3 * D + j] += w.qkv_b[j];
+        // K/V into the cache (src/gsv_ar.cpp:271-275)
+        for (int t = 0; t < S; t++)
+            for (int d = 0; d < D; d++) {
+                const float kk = qkv[(size_t)t * 3 * D + D + d], vv = qkv[(size_t)t * 3 * D + 2 * D + d];
+                cache.k[((size_t)li * cache.cap + t) * D + d] = kv_f16 ? round_f16(kk) : kk;
+                cache.v[((size_t)li * cache.cap + t) * D + d] = kv_f16 ? round_f16(vv) : vv;
+            }
+        // prefix-masked attention on the F32 K/V of this pass (src/gsv_ar.cpp:257, mask :215-223)
+        const int T = r.T;
+        #pragma omp parallel for collapse(2) num_threads(nthreads()) schedule(static)
+        for (int hh = 0; hh < NH; hh++)
+            for (int qi = 0; qi < S; qi++) {
+                const float* q = qkv.data() + (size_t)qi * 3 * D + hh * HD;
+                const float* K = qkv.data() + D + hh * HD;
+                const float* Vv = qkv.data() + 2 * D + hh * HD;
+                auto keep = [&](int64_t k) { return qi < T ? (k < T) : (k <= qi); };
+                attn_row(q, K, Vv, 3 * D, S, HD, scale, keep, att.data() + (size_t)qi * D + hh * HD);
+            }
+        mul_mat(w.out_w, att.data(), S, o.data());
+        ln_affine(cur.data(), o.data(), w.out_b.data(), w.n1w.data(), w.n1b.data(), S, D, 1e-5f, n1.data());
+        mul_mat(w.f1w, n1.data(), S, h.data());
+        add_act(h.data(), w.f1b.data(), S, FF, 1, h.data());
+        mul_mat(w.f2w, h.data(), S, h2.data());
+        ln_affine(n1.data(), h2.data(), w.f2b.data(), w.n2w.data(), w.n2b.data(), S, D, 1e-5f, cur.data());
+        if (dump) {
+            float* dd = dump + (size_t)li * 4 * D;
+            const size_t lr = (size_t)(S - 1) * D;
+            std::memcpy(dd + 0 * D, att.data() + lr, D * 4);
+            std::memcpy(dd + 1 * D, n1.data() + lr, D * 4);
+            for (int d = 0; d < D; d++) dd[2 * D + d] = (n1[lr + d] + h2[lr + d]) + w.f2b[d];
+            std::memcpy(dd + 3 * D, cur.data() + lr, D * 4);
+        }
+    }
+    cache.len = S;
+    mul_mat(m.predict, cur.data() + (size_t)(S - 1) * D, 1, logits);
+}
+
+// One decode step for a set of sequences (run_decode / run_decode_cached, src/gsv_ar.cpp:296-358,
+// 380-467): x [B][D] -> logits [B][V]. The new K/V are written at index len before attention
+// reads [0, len] (write-before-read, :398-405).
+void decode_step(const orc_model& m, std::vector<SeqCache*>& caches, const float* x_in, bool kv_f16, float* logits,
+                 float* dump) {
+    const int B = (int)caches.size(), D = m.D, HD = m.HD, NH = m.NH;
+    const int FF = (int)m.L[0].f1w.N;
+    std::vector<float> cur(x_in, x_in + (size_t)B * D), qkv((size_t)B * 3 * D), att((size_t)B * D),
+        o((size_t)B * D), n1((size_t)B * D), h((size_t)B * FF), h2((size_t)B * D);
+    const float scale = 1.0f / std::sqrt((float)HD);
+    for (int li = 0; li < m.NL; li++) {
+        const orc_layer& w = m.L[li];
+        mul_mat(w.qkv_w, cur.data(), B, qkv.data());
+        for (int b = 0; b < B; b++)
+            for (int j = 0; j < 3 * D; j++) qkv[(size_t)b * 3 * D + j] += w.qkv_b[j];
+        for (int b = 0; b < B; b++) {
+            SeqCache& c = *caches[b];
+            for (int d = 0; d < D; d++) {
+                const float kk = qkv[(size_t)b * 3 * D + D + d], vv = qkv[(size_t)b * 3 * D + 2 * D + d];
+                c.k[((size_t)li * c.cap + c.len) * D + d] = kv_f16 ? round_f16(kk) : kk;
+                c.v[((size_t)li * c.cap + c.len) * D + d] = kv_f16 ? round_f16(vv) : vv;
+            }
+        }
+        #pragma omp parallel for collapse(2) num_threads(nthreads()) schedule(static)
+        for (int b = 0; b < B; b++)
+            for (int hh = 0; hh < NH; hh++) {
+                SeqCache& c = *caches[b];
+                const float* q = qkv.data() + (size_t)b * 3 * D + hh * HD;
+                const float* K = c.k.data() + (size_t)li * c.cap * D + hh * HD;
+                const float* Vv = c.v.data() + (size_t)li * c.cap * D + hh * HD;
+                auto keep = [](int64_t) { return true; };
+                attn_row(q, K, Vv, D, c.len + 1, HD, scale, keep, att.data() + (size_t)b * D + hh * HD);
+            }
+        mul_mat(w.out_w, att.data(), B, o.data());
+        ln_affine(cur.data(), o.data(), w.out_b.data(), w.n1w.data(), w.n1b.data(), B, D, 1e-5f, n1.data());
+        mul_mat(w.f1w, n1.data(), B, h.data());
+        add_act(h.data(), w.f1b.data(), B, FF, 1, h.data());
+        mul_mat(w.f2w, h.data(), B, h2.data());
+        ln_affine(n1.data(), h2.data(), w.f2b.data(), w.n2w.data(), w.n2b.data(), B, D, 1e-5f, cur.data());
+        if (dump) {
+            for (int b = 0; b < B; b++) {
+                float* dd = dump + ((size_t)b * m.NL + li) * 4 * D;
+                std::memcpy(dd + 0 * D, att.data() + (size_t)b * D, D * 4);
+                std::memcpy(dd + 1 * D, n1.data() + (size_t)b * D, D * 4);
+                for (int d = 0; d < D; d++) dd[2 * D + d] = (n1[(size_t)b * D + d] + h2[(size_t)b * D + d]) + w.f2b[d];
+                std::memcpy(dd + 3 * D, cur.data() + (size_t)b * D, D * 4);
+            }
+        }
+    }
+    for (auto* c : caches) c->len += 1;
+    mul_mat(m.predict, cur.data(), B, logits);
+}
+
+std::vector<Req> make_reqs(const orc_model& m, int B, const int32_t* phones, const int32_t* n_phones, const float* bert,
+                           const int32_t* prompts, const int32_t* n_prompt) {
+    std::vector<Req> reqs(B);
+    size_t po = 0, bo = 0, qo = 0;
+    for (int b = 0; b < B; b++) {
+        reqs[b].phones = phones + po;
+        reqs[b].T = n_phones[b];
+        reqs[b].bert = bert + bo;
+        reqs[b].prompt = prompts + qo;
+        reqs[b].P = n_prompt[b];
+        po += n_phones[b];
+        bo += (size_t)m.BERT * n_phones[b];
+        qo += n_prompt[b];
+    }
+    return reqs;
+}
+
+bool check_reqs(orc_model* m, const std::vector<Req>& reqs) {
+    for (const Req& r : reqs) {
+        if (r.T <= 0) { m->err = "empty phones"; return false; }
+        for (int t = 0; t < r.T; t++)
+            if (r.phones[t] < 0 || r.phones[t] >= m->PV) { m->err = "phone id out of range"; return false; }
+        for (int t = 0; t < r.P; t++)
+            if (r.prompt[t] < 0 || r.prompt[t] >= m->V) { m->err = "prompt code out of range"; return false; }
+    }
+    return true;
+}
+
+void init_cache(const orc_model& m, SeqCache& c, int cap) {
+    c.cap = cap;
+    c.len = 0;
+    c.k.assign((size_t)m.NL * cap * m.D, 0.0f);
+    c.v.assign((size_t)m.NL * cap * m.D, 0.0f);
+}
+
+}  // namespace
+
+extern "C" {
+
+void orc_set_threads(int n) { g_threads = n; }
+int orc_get_threads(void) { return nthreads(); }
+
+// ---------------------------------------------------------------- primitive ops
+void orc_fp32_to_fp16(const float* x, uint16_t* y, int64_t n) { for (int64_t i = 0; i < n; i++) y[i] = f32_to_f16(x[i]); }
+void orc_fp16_to_fp32(const uint16_t* x, float* y, int64_t n) { for (int64_t i = 0; i < n; i++) y[i] = f16_to_f32(x[i]); }
+void orc_quantize_q8_0(const float* x, int64_t n, uint8_t* blocks) { quantize_q8_0(x, n, blocks); }
+
+// Y[M][N] = W[N][K] . X[M][K]^T with W raw Q8_0 blocks (type 8) or F32 (type 0).
+int orc_mul_mat(int type, const void* W, int64_t N, int64_t K, const float* X, int64_t M, float* Y) {
+    Mat w;
+    std::string err;
+    const int64_t nbytes = type == T_Q8_0 ? N * (K / QK) * Q8_BYTES : N * K * 4;
+    if (!set_mat(w, type, W, nbytes, N, K, err, "W")) return -1;
+    mul_mat(w, X, M, Y);
+    return 0;
+}
+
+void orc_ln_affine(const float* x, const float* r, const float* bias, const float* w, const float* b, int64_t rows,
+                   int64_t n, float eps, float* y) {
+    ln_affine(x, r, bias, w, b, rows, n, eps, y);
+}
+
+void orc_add_act(const float* a, const float* b, int64_t rows, int64_t n, int act, float* y) { add_act(a, b, rows, n, act, y); }
+
+// Decode attention over a contiguous per-sequence cache: q [B][NH][HD], k/v [B][Lmax][NH][HD],
+// lens [B] keys visible per sequence; out [B][NH][HD].
+void orc_decode_attention(const float* q, const float* k, const float* v, const int32_t* lens, int B, int Lmax, int NH,
+                          int HD, float scale, float* out) {
+    #pragma omp parallel for collapse(2) num_threads(nthreads()) schedule(dynamic)
+    for (int b = 0; b < B; b++)
+        for (int h = 0; h < NH; h++) {
+            const size_t base = (size_t)b * Lmax * NH * HD + (size_t)h * HD;
+            auto keep = [](int64_t) { return true; };
+            attn_row(q + ((size_t)b * NH + h) * HD, k + base, v + base, (int64_t)NH * HD, lens[b], HD, scale, keep,
+                     out + ((size_t)b * NH + h) * HD);
+        }
+}
+
+// Prefix-masked prefill attention over packed sequences: qkv [Mtot][3*NH*HD] rows (q|k|v),
+// seq b occupies rows [off_b, off_b + S_b) with its first T_b rows text. out [Mtot][NH*HD].
+void orc_prefill_attention(const float* qkv, const int32_t* seq_len, const int32_t* text_len, int B, int NH, int HD,
+                           float scale, float* out) {
+    const int D = NH * HD;
+    std::vector<int64_t> off(B + 1, 0);
+    for (int b = 0; b < B; b++) off[b + 1] = off[b] + seq_len[b];
+    for (int b = 0; b < B; b++) {
+        const int S = seq_len[b], T = text_len[b];
+        const float* base = qkv + off[b] * 3 * D;
+        #pragma omp parallel for collapse(2) num_threads(nthreads()) schedule(static)
+        for (int h = 0; h < NH; h++)
+            for (int qi = 0; qi < S; qi++) {
+                auto keep = [&](int64_t kk) { return qi < T ? (kk < T) : (kk <= qi); };
+                attn_row(base + (size_t)qi * 3 * D + h * HD, base + D + h * HD, base + 2 * D + h * HD, 3 * D, S, HD,
+                         scale, keep, out + (off[b] + qi) * D + h * HD);
+            }
+    }
+}
+
+void orc_logits_to_probs(int top_k, float top_p, float temperature, float rep, float* logits, int V,
+                         const int32_t* prev, int n_prev, float* probs) {
+    SamplerCfg c;
+    c.top_k = top_k;
+    c.top_p = top_p;
+    c.temperature = temperature;
+    c.rep = rep;
+    logits_to_probs(c, logits, V, prev, n_prev, probs);
+}
+
+uint64_t orc_rng_init(uint64_t seed) { return seed ? seed : 1; }
+
+int orc_sample(const float* probs, int V, uint64_t* state) {
+    Rng r(1);
+    r.s = *state;
+    const int t = sample(probs, V, r);
+    *state = r.s;
+    return t;
+}
+
+// ---------------------------------------------------------------- model
+orc_model* orc_model_new(int D, int NH, int NL, int V, int PV, int EOS, int BERT) {
+    orc_model* m = new orc_model();
+    m->D = D; m->NH = NH; m->HD = D / NH; m->NL = NL; m->V = V; m->PV = PV; m->EOS = EOS; m->BERT = BERT;
+    m->L.resize(NL);
+    return m;
+}
+
+void orc_model_free(orc_model* m) { delete m; }
+const char* orc_model_error(orc_model* m) { return m ? m->err.c_str() : "null model"; }
+
+// Tensor names follow tools/export_gguf/convert_ar.py:106-130. type: 0 F32, 8 Q8_0.
+int orc_model_set(orc_model* m, const char* name, int type, const void* data, int64_t nbytes) {
+    const int D = m->D, FF = 4 * D;
+    std::string n(name);
+    if (n == "ar.text_emb") return set_vec(m->text_emb, type, data, nbytes, (int64_t)m->PV * D, m->err, name) ? 0 : -1;
+    if (n == "ar.audio_emb") return set_vec(m->audio_emb, type, data, nbytes, (int64_t)m->V * D, m->err, name) ? 0 : -1;
+    if (n == "ar.bert_proj") return set_vec(m->bert_proj, type, data, nbytes, (int64_t)D * m->BERT, m->err, name) ? 0 : -1;
+    if (n == "ar.bert_proj_b") return set_vec(m->bert_proj_b, type, data, nbytes, D, m->err, name) ? 0 : -1;
+    if (n == "ar.text_pe_alpha" || n == "ar.audio_pe_alpha") {
+        if (type != T_F32 || nbytes != 4) { m->err = "alpha must be F32[1]"; return -1; }
+        (n == "ar.text_pe_alpha" ? m->text_alpha : m->audio_alpha) = *(const float*)data;
+        return 0;
+    }
+    if (n == "ar.predict") return set_mat(m->predict, type, data, nbytes, m->V, D, m->err, name) ? 0 : -1;
+    int li = -1;
+    char field[64] = {0};
+    if (std::sscanf(name, "transformer.block%d.%63s", &li, field) == 2 && li >= 0 && li < m->NL) {
+        orc_layer& L = m->L[li];
+        std::string f(field);
+        if (f == "qkv_w") return set_mat(L.qkv_w, type, data, nbytes, 3 * D, D, m->err, name) ? 0 : -1;
+        if (f == "out_w") return set_mat(L.out_w, type, data, nbytes, D, D, m->err, name) ? 0 : -1;
+        if (f == "ffn1_w") return set_mat(L.f1w, type, data, nbytes, FF, D, m->err, name) ? 0 : -1;
+        if (f == "ffn2_w") return set_mat(L.f2w, type, data, nbytes, D, FF, m->err, name) ? 0 : -1;
+        if (f == "qkv_b") return set_vec(L.qkv_b, type, data, nbytes, 3 * D, m->err, name) ? 0 : -1;
+        if (f == "out_b") return set_vec(L.out_b, type, data, nbytes, D, m->err, name) ? 0 : -1;
+        if (f == "ffn1_b") return set_vec(L.f1b, type, data, nbytes, FF, m->err, name) ? 0 : -1;
+        if (f == "ffn2_b") return set_vec(L.f2b, type, data, nbytes, D, m->err, name) ? 0 : -1;
+        if (f == "norm1_w") return set_vec(L.n1w, type, data, nbytes, D, m->err, name) ? 0 : -1;
+        if (f == "norm1_b") return set_vec(L.n1b, type, data, nbytes, D, m->err, name) ? 0 : -1;
+        if (f == "norm2_w") return set_vec(L.n2w, type, data, nbytes, D, m->err, name) ? 0 : -1;
+        if (f == "norm2_b") return set_vec(L.n2b, type, data, nbytes, D, m->err, name) ? 0 : -1;
+    }
+    return 1;   // unknown tensor: ignored, like the reference loader (src/gsv_ar.cpp:556-559)
+}
+
+// After all tensors: bert_aug [W | b] (src/gsv_ar.cpp:648-656), PE table.
+int orc_model_finalize(orc_model* m, int pe_max) {
+    const int D = m->D, BD = m->BERT;
+    if (m->bert_proj.size() != (size_t)D * BD || m->bert_proj_b.size() != (size_t)D || m->text_emb.empty() ||
+        m->audio_emb.empty() || m->predict.N == 0) {
+        m->err = "missing tensors";
+        return -1;
+    }
+    for (int li = 0; li < m->NL; li++)
+        if (m->L[li].qkv_w.N == 0 || m->L[li].out_w.N == 0 || m->L[li].f1w.N == 0 || m->L[li].f2w.N == 0 ||
+            m->L[li].n2b.empty()) {
+            m->err = "missing layer tensors";
+            return -1;
+        }
+    m->bert_aug.type = T_F32;
+    m->bert_aug.N = D;
+    m->bert_aug.K = BD + 1;
+    m->bert_aug.f.assign((size_t)D * (BD + 1), 0.0f);
+    for (int d = 0; d < D; d++) {
+        std::memcpy(m->bert_aug.f.data() + (size_t)d * (BD + 1), m->bert_proj.data() + (size_t)d * BD, BD * 4);
+        m->bert_aug.f[(size_t)d * (BD + 1) + BD] = m->bert_proj_b[d];
+    }
+    make_pe(*m, pe_max > 0 ? pe_max : 4096);
+    return 0;
+}
+
+// PE table access for tests.
+const float* orc_model_pe(orc_model* m) { return m->pe.data(); }
+
+// first_logits (src/gsv_ar.cpp:707-717) for B requests; dump (optional) gets, per sequence, the
+// last position's [attn out, n1, (n1 + W2 h) + b2, layer out] for each layer: [B][NL][4][D].
+int orc_first_logits(orc_model* m, int B, const int32_t* phones, const int32_t* n_phones, const float* bert,
+                     const int32_t* prompts, const int32_t* n_prompt, int kv_f16, float* logits, float* dump) {
+    std::vector<Req> reqs = make_reqs(*m, B, phones, n_phones, bert, prompts, n_prompt);
+    if (!check_reqs(m, reqs)) return -1;
+    for (int b = 0; b < B; b++) {
+        SeqCache c;
+        init_cache(*m, c, reqs[b].T + reqs[b].P + 1);
+        prefill_one(*m, reqs[b], kv_f16 != 0, c, logits + (size_t)b * m->V,
+                    dump ? dump + (size_t)b * m->NL * 4 * m->D : nullptr);
+    }
+    return 0;
+}
+
+// Teacher-forced decode trace: prefill, then feed `forced` tokens [B][n_steps] (audio_emb + PE at
+// pos = P_b + step, src/gsv_ar.cpp:798-806) and record the raw logits of every step:
+// logits_out [n_steps + 1][B][V] (row 0 = prefill). dump (optional) [n_steps][B][NL][4][D].
+int orc_decode_trace(orc_model* m, int B, const int32_t* phones, const int32_t* n_phones, const float* bert,
+                     const int32_t* prompts, const int32_t* n_prompt, int kv_f16, const int32_t* forced, int n_steps,
+                     float* logits_out, float* dump) {
+    std::vector<Req> reqs = make_reqs(*m, B, phones, n_phones, bert, prompts, n_prompt);
+    if (!check_reqs(m, reqs)) return -1;
+    const int D = m->D, V = m->V;
+    std::vector<SeqCache> caches(B);
+    for (int b = 0; b < B; b++) {
+        init_cache(*m, caches[b], reqs[b].T + reqs[b].P + n_steps + 1);
+        prefill_one(*m, reqs[b], kv_f16 != 0, caches[b], logits_out + (size_t)b * V, nullptr);
+    }
+    std::vector<SeqCache*> ptrs(B);
+    for (int b = 0; b < B; b++) ptrs[b] = &caches[b];
+    std::vector<float> x((size_t)B * D);
+    for (int s = 0; s < n_steps; s++) {
+        for (int b = 0; b < B; b++) {
+            const int tok = forced[(size_t)b * n_steps + s];
+            if (tok < 0 || tok >= V) { m->err = "forced token out of range"; return -1; }
+            const int pos = reqs[b].P + s;
+            for (int d = 0; d < D; d++)
+                x[(size_t)b * D + d] = std::fmaf(m->audio_alpha, m->pe[(size_t)pos * D + d], m->audio_emb[(size_t)tok * D + d]);
+        }
+        decode_step(*m, ptrs, x.data(), kv_f16 != 0, logits_out + (size_t)(s + 1) * B * V,
+                    dump ? dump + (size_t)s * B * m->NL * 4 * D : nullptr);
+    }
+    return 0;
+}
+
+// gsv_ar::generate (src/gsv_ar.cpp:719-824) for B requests.
+//   tokens_out [B][cap]: prompt + generated tokens (without the stopping token), n_tokens_out [B]
+//   lens_out [B]: generated counts in the order sequences finished (res.lens semantics)
+// Sequences are computed independently (equal to the reference's left-padded batch, whose pad keys
+// are always masked); PE of generated token idx is prompt_len_b + idx with prompt_len_b the
+// sequence's own prompt length (the reference requires equal prompt lengths, :730-733).
+int orc_generate(orc_model* m, int B, const int32_t* phones, const int32_t* n_phones, const float* bert,
+                 const int32_t* prompts, const int32_t* n_prompt, int top_k, float top_p, float temperature, float rep,
+                 uint64_t seed_base, int early_stop_num, int max_steps, const int32_t* oracle_tokens, int n_oracle,
+                 const uint64_t* seeds, int n_seeds, int kv_f16, int32_t* tokens_out, int32_t* n_tokens_out,
+                 int32_t* lens_out, int cap, float* first_logits_out) {
+    std::vector<Req> reqs = make_reqs(*m, B, phones, n_phones, bert, prompts, n_prompt);
+    if (!check_reqs(m, reqs)) return -1;
+    const int D = m->D, V = m->V;
+    SamplerCfg sc;
+    sc.top_k = top_k; sc.top_p = top_p; sc.temperature = temperature; sc.rep = rep;
+    std::vector<SeqCache> caches(B);
+    std::vector<float> lg((size_t)B * V);
+    for (int b = 0; b < B; b++) {
+        init_cache(*m, caches[b], reqs[b].T + reqs[b].P + max_steps + 8);
+        prefill_one(*m, reqs[b], kv_f16 != 0, caches[b], lg.data() + (size_t)b * V, nullptr);
+    }
+    if (first_logits_out) std::memcpy(first_logits_out, lg.data(), lg.size() * 4);
+    std::vector<std::vector<int32_t>> y(B);
+    for (int b = 0; b < B; b++) y[b].assign(reqs[b].prompt, reqs[b].prompt + reqs[b].P);
+    std::vector<int> idx_list(B, -1);
+    std::vector<std::vector<int32_t>> res(B);
+    std::vector<int32_t> lens;
+    std::vector<Rng> rng;
+    for (int b = 0; b < B; b++)
+        rng.emplace_back(seeds && b < n_seeds ? seeds[b] : seed_base + 0x9E3779B9ull * (uint64_t)b);
+    const int prompt_len0 = reqs[0].P;
+    std::vector<float> row(V), probs(V), x;
+    std::vector<int32_t> prev;
+    for (int idx = 0; idx < max_steps; idx++) {
+        for (int b = 0; b < B; b++) {
+            if (idx_list[b] >= 0) continue;
+            std::memcpy(row.data(), lg.data() + (size_t)b * V, V * 4);
+            if (idx < 11) row[m->EOS] = -INFINITY;
+            const int np = (int)std::min<size_t>(y[b].size(), 4096);
+            prev.assign(y[b].end() - np, y[b].end());
+            logits_to_probs(sc, row.data(), V, prev.data(), np, probs.data());
+            int tok = sample(probs.data(), V, rng[b]);
+            if (oracle_tokens && idx < n_oracle) tok = oracle_tokens[idx];
+            y[b].push_back(tok);
+            if (tok == m->EOS) {
+                idx_list[b] = idx;
+                res[b].assign(y[b].begin(), y[b].end() - 1);
+                lens.push_back(idx);
+            }
+        }
+        if (early_stop_num != -1 && ((int)y[0].size() - prompt_len0) > early_stop_num) {
+            for (int b = 0; b < B; b++)
+                if (idx_list[b] < 0) {
+                    idx_list[b] = idx;
+                    res[b].assign(y[b].begin(), y[b].end() - 1);
+                    lens.push_back(idx);
+                }
+        }
+        bool any = false;
+        for (int b = 0; b < B; b++) any |= idx_list[b] < 0;
+        if (!any) break;
+        // Only unfinished sequences need the next step: finished ones are never read again.
+        std::vector<SeqCache*> ptrs;
+        std::vector<int> which;
+        for (int b = 0; b < B; b++)
+            if (idx_list[b] < 0) {
+                ptrs.push_back(&caches[b]);
+                which.push_back(b);
+            }
+        x.assign(which.size() * D, 0.0f);
+        for (size_t j = 0; j < which.size(); j++) {
+            const int b = which[j];
+            const int pos = reqs[b].P + idx;
+            const int tok = y[b].back();
+            for (int d = 0; d < D; d++)
+                x[j * D + d] = std::fmaf(m->audio_alpha, m->pe[(size_t)pos * D + d], m->audio_emb[(size_t)tok * D + d]);
+        }
+        std::vector<float> lg2(which.size() * V);
+        decode_step(*m, ptrs, x.data(), kv_f16 != 0, lg2.data(), nullptr);
+        for (size_t j = 0; j < which.size(); j++)
+            std::memcpy(lg.data() + (size_t)which[j] * V, lg2.data() + j * V, V * 4);
+    }
+    for (int b = 0; b < B; b++)
+        if (idx_list[b] < 0) {
+            res[b] = y[b];
+            lens.push_back(max_steps);
+        }
+    for (int b = 0; b < B; b++) {
+        const int n = (int)std::min<size_t>(res[b].size(), (size_t)cap);
+        std::memcpy(tokens_out + (size_t)b * cap, res[b].data(), (size_t)n * 4);
+        n_tokens_out[b] = (int32_t)res[b].size();
+        lens_out[b] = lens[b];
+    }
+    return 0;
+}
+
+}  // extern "C"

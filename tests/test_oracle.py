@@ -1,0 +1,222 @@
+"""The oracle pinned: golden vectors of the reference's own code, and an independent float64 model.
+
+* sampler: bit-exact against the compiled reference src/gsv_sampler.cpp (committed golden fixture,
+  and live when oracle/_ref is built);
+* Q8_0 activation quantization: bit-exact against gguf-py's quantizer (documented bit-exact with
+  ggml's reference quantize_row_q8_0);
+* add_act: the reference's own test inputs and tolerance (tests/test_add_act.cpp:64-65, 86-98);
+* transformer semantics (prefix mask, post-LN layers, PE, BERT projection, KV-cached decode):
+  against a float64 numpy restatement on a model with F32 matrices (no activation quantization).
+"""
+import os
+
+import numpy as np
+import pytest
+
+import gsv_synth as S
+import oracle as O
+from conftest import rel_l2
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def test_sampler_matches_reference_golden():
+    g = np.load(os.path.join(GOLDEN, "sampler_golden.npz"))
+    for i in range(len(g["token"])):
+        top_k, top_p, temp, rep = g["cfg"][i]
+        prev = g["prev"][i][:g["n_prev"][i]]
+        probs = O.logits_to_probs(g["logits"][i], top_k=int(top_k), top_p=float(top_p), temperature=float(temp),
+                                  rep=float(rep), prev=prev)
+        assert np.array_equal(probs.view(np.uint32), g["probs"][i].view(np.uint32)), i
+        tok, st = O.sample(probs, int(g["state0"][i]))
+        assert tok == g["token"][i] and st == int(g["state1"][i]), i
+
+
+@pytest.mark.skipif(not os.path.exists(O.REF_SAMPLER_PATH), reason="reference sampler not built (make -C oracle ref)")
+def test_sampler_matches_live_reference():
+    ref = O.RefSampler()
+    rng = np.random.default_rng(0)
+    for it in range(400):
+        lg = (rng.standard_normal(1025) * rng.choice([0.1, 0.45, 3.0])).astype(np.float32)
+        if it % 7 == 0:
+            lg = (np.round(lg * 4) / 4).astype(np.float32)
+        cfg = dict(top_k=int(rng.choice([0, 1, 5, 15, 1025])), top_p=float(rng.choice([1.0, 0.9, 0.5])),
+                   temperature=float(rng.choice([1.0, 0.7, 1.3])), rep=float(rng.choice([1.35, 1.0, 2.0])))
+        prev = rng.integers(0, 1025, int(rng.integers(0, 300)), dtype=np.int32)
+        p1 = ref.logits_to_probs(lg, prev=prev, **cfg)
+        p2 = O.logits_to_probs(lg, prev=prev, **cfg)
+        assert np.array_equal(p1.view(np.uint32), p2.view(np.uint32))
+        st = int(rng.integers(1, 2**63))
+        assert ref.sample(p1, st) == O.sample(p2, st)
+        assert ref.rng_init(0) == O.rng_init(0) == 1
+
+
+def test_q8_0_quantizer_golden_and_gguf():
+    import gguf
+    g = np.load(os.path.join(GOLDEN, "q8_0_golden.npz"))
+    assert np.array_equal(O.quantize_q8_0(g["x"]), g["blocks"].ravel())
+    rng = np.random.default_rng(1)
+    x = (rng.standard_normal(32 * 2048) * rng.choice([1e-3, 1.0, 50.0], 32 * 2048)).astype(np.float32)
+    ref = gguf.quants.quantize(x.reshape(-1, 32), gguf.GGMLQuantizationType.Q8_0).ravel()
+    assert np.array_equal(O.quantize_q8_0(x), ref)
+
+
+def test_add_act_reference_test_inputs():
+    """tests/test_add_act.cpp:15-16,64-65 inputs; ReLU (act 1) and identity within its 2e-3 bar."""
+    NE0, NR = 64, 7
+    i = np.arange(NE0 * NR)
+    a = (0.02 * ((i * 37 % 101) - 50) + 0.5).astype(np.float32).reshape(NR, NE0)
+    b = (0.01 * ((np.arange(NE0) * 13) % 29 - 14)).astype(np.float32)
+    for act in (0, 1):
+        ref = a + b if act == 0 else np.maximum(a + b, 0)
+        assert np.abs(O.add_act(a, b, act) - ref).max() <= 2e-3
+        assert np.array_equal(O.add_act(a, b, act), ref.astype(np.float32))
+
+
+def test_layernorm_vs_float64():
+    rng = np.random.default_rng(2)
+    x = rng.standard_normal((50, 512)).astype(np.float32) * 3
+    r = rng.standard_normal((50, 512)).astype(np.float32)
+    bias = rng.standard_normal(512).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(512)).astype(np.float32)
+    b = rng.standard_normal(512).astype(np.float32)
+    y = O.ln_affine(x, r, bias, w, b)
+    v = x.astype(np.float64) + r + bias
+    ref = (v - v.mean(1, keepdims=True)) / np.sqrt(v.var(1, keepdims=True) + 1e-5) * w + b
+    assert np.abs(y - ref).max() < 1e-5
+
+
+def test_q8_mul_mat_vs_dequantized_float64():
+    """Q8_0 mul_mat equals the float64 product of the dequantized operands up to float rounding."""
+    rng = np.random.default_rng(3)
+    N, K, M = 64, 512, 5
+    W = (0.02 * rng.standard_normal((N, K))).astype(np.float32)
+    X = rng.standard_normal((M, K)).astype(np.float32)
+    wb, xb = O.quantize_q8_0(W).reshape(N, K // 32, 34), O.quantize_q8_0(X).reshape(M, K // 32, 34)
+
+    def deq(b):
+        d = b[..., :2].copy().view(np.float16).astype(np.float64)
+        q = b[..., 2:].copy().view(np.int8).astype(np.float64)
+        return (q * d).reshape(b.shape[0], -1)
+
+    ref = deq(xb) @ deq(wb).T
+    got = O.mul_mat(O.quantize_q8_0(W), 8, N, K, X)
+    assert np.abs(got - ref).max() <= 1e-5 * np.abs(ref).max()
+
+
+# ------------------------------------------------------------------ float64 model restatement
+def _np_model(path):
+    import gguf
+    rd = gguf.GGUFReader(path)
+    T = {t.name: np.array(t.data, dtype=np.float64) for t in rd.tensors}
+    return T
+
+
+def _np_pe(n, D=512):
+    pe = np.zeros((n, D), np.float64)
+    pos = np.arange(n)[:, None]
+    div = np.exp(np.arange(0, D, 2) * -(np.log(10000.0) / D))
+    pe[:, 0::2] = np.sin(pos * div)
+    pe[:, 1::2] = np.cos(pos * div)
+    return pe
+
+
+def _np_layer(T, li, x, att_fn):
+    p = f"transformer.block{li}."
+    qkv = x @ T[p + "qkv_w"].reshape(1536, 512).T + T[p + "qkv_b"]
+    o = att_fn(qkv) @ T[p + "out_w"].reshape(512, 512).T
+    v = x + o + T[p + "out_b"]
+    n1 = (v - v.mean(-1, keepdims=True)) / np.sqrt(v.var(-1, keepdims=True) + 1e-5) * T[p + "norm1_w"] + T[p + "norm1_b"]
+    h = np.maximum(n1 @ T[p + "ffn1_w"].reshape(2048, 512).T + T[p + "ffn1_b"], 0)
+    v2 = n1 + h @ T[p + "ffn2_w"].reshape(512, 2048).T + T[p + "ffn2_b"]
+    return (v2 - v2.mean(-1, keepdims=True)) / np.sqrt(v2.var(-1, keepdims=True) + 1e-5) * T[p + "norm2_w"] + \
+        T[p + "norm2_b"], qkv
+
+
+def _np_attend(q, k, v, mask):
+    s = np.einsum("qhd,khd->hqk", q, k) / np.sqrt(32.0)
+    s = np.where(mask[None], s, -np.inf)
+    s -= s.max(-1, keepdims=True)
+    p = np.exp(s)
+    p /= p.sum(-1, keepdims=True)
+    return np.einsum("hqk,khd->qhd", p, v)
+
+
+def _np_trace(T, req, forced, NL):
+    """float64 prefill + teacher-forced decode of one sequence -> logits per step."""
+    Tn, P = len(req.phones), len(req.prompt)
+    S = Tn + P
+    pe = _np_pe(P + len(forced) + S + 1)
+    x = np.concatenate([T["ar.text_emb"].reshape(-1, 512)[req.phones] + pe[:Tn],
+                        T["ar.audio_emb"].reshape(-1, 512)[req.prompt] + pe[:P]])
+    feat = np.asarray(req.bert, np.float64).T
+    proj = feat @ T["ar.bert_proj"].reshape(512, 1024).T + T["ar.bert_proj_b"]
+    x[:Tn] += proj
+    qi = np.arange(S)[:, None]
+    ki = np.arange(S)[None, :]
+    mask = np.where(qi < Tn, ki < Tn, ki <= qi)
+    Ks, Vs = [], []
+    for li in range(NL):
+        def att(qkv):
+            q, k, v = (qkv[:, j * 512:(j + 1) * 512].reshape(S, 16, 32) for j in range(3))
+            Ks.append(k)
+            Vs.append(v)
+            return _np_attend(q, k, v, mask).reshape(S, 512)
+        x, _ = _np_layer(T, li, x, att)
+    pred = T["ar.predict"].reshape(-1, 512)
+    out = [x[-1] @ pred.T]
+    for s, tok in enumerate(forced):
+        y = T["ar.audio_emb"].reshape(-1, 512)[tok] + pe[P + s]
+        y = y[None]
+        for li in range(NL):
+            def att(qkv):
+                q, k, v = (qkv[:, j * 512:(j + 1) * 512].reshape(1, 16, 32) for j in range(3))
+                Ks[li] = np.concatenate([Ks[li], k])
+                Vs[li] = np.concatenate([Vs[li], v])
+                return _np_attend(q, Ks[li], Vs[li], np.ones((1, Ks[li].shape[0]), bool)).reshape(1, 512)
+            y, _ = _np_layer(T, li, y, att)
+        out.append(y[0] @ pred.T)
+    return np.array(out)
+
+
+def test_oracle_transformer_vs_float64(model_f32_small):
+    orc = O.OracleModel(model_f32_small)
+    T = _np_model(model_f32_small)
+    rng = np.random.default_rng(4)
+    reqs = [S.make_request(rng, 37, 11), S.make_request(rng, 20, 0)]
+    forced = rng.integers(0, 1024, (2, 5)).astype(np.int32)
+    lg = orc.decode_trace(reqs, forced)
+    for b in range(2):
+        ref = _np_trace(T, reqs[b], forced[b], orc.NL)
+        for s in range(ref.shape[0]):
+            assert rel_l2(lg[s, b], ref[s]) < 2e-5, (b, s)
+
+
+def test_oracle_generate_rules(model_small):
+    """gsv_ar::generate rules: EOS never before step 11, teacher forcing, EOS finish and lens order."""
+    orc = O.OracleModel(model_small)
+    rng = np.random.default_rng(5)
+    reqs = [S.make_request(rng, 12, 6) for _ in range(3)]
+    forced = rng.integers(0, 1024, 20).astype(np.int32)
+    forced[13] = 1024
+    toks, lens = orc.generate(reqs, max_steps=20, oracle_tokens=forced, seed_base=3)
+    assert lens == [13, 13, 13]
+    for t in toks:
+        assert len(t) == 6 + 13 and np.array_equal(t[6:], forced[:13])
+    # early stop keyed on sequence 0: generated count > early_stop finishes every unfinished sequence
+    toks, lens = orc.generate(reqs, max_steps=40, early_stop=7, seed_base=3)
+    assert lens == [7, 7, 7] and all(len(t) == 6 + 7 for t in toks)
+    # max_steps: the whole stream is kept
+    toks, lens = orc.generate(reqs[:1], max_steps=9, top_k=1)
+    assert lens == [9] and len(toks[0]) == 6 + 9
+    assert 1024 not in toks[0][6:6 + 11]
+
+
+def test_oracle_batch_equals_single(model_small):
+    orc = O.OracleModel(model_small)
+    reqs = S.ragged_requests(6, 3, lo=20, hi=60)
+    seeds = [11, 12, 13]
+    tb, _ = orc.generate(reqs, seeds=seeds, max_steps=25)
+    for b in range(3):
+        ts, _ = orc.generate([reqs[b]], seeds=[seeds[b]], max_steps=25)
+        assert np.array_equal(tb[b], ts[0])
