@@ -1,0 +1,1296 @@
+// engine.cu -- the gsvcu context: model upload, paged KV manager, prefill, the CUDA-graph decode
+// step, generate (gsv_ar::generate semantics) and the continuous-batching entry points.
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/gsvcu.h"
+#include "gguf_reader.h"
+#include "kernels.h"
+
+using namespace gsvcu;
+
+namespace {
+
+struct LayerW {
+    uint4* wq[4] = {nullptr, nullptr, nullptr, nullptr};     // qkv, out, ffn1, ffn2 fragment planes
+    uint16_t* wd[4] = {nullptr, nullptr, nullptr, nullptr};  // matching fp16 scale planes
+    float *b_qkv = nullptr, *b_out = nullptr, *n1w = nullptr, *n1b = nullptr;
+    float *b_f1 = nullptr, *b_f2 = nullptr, *n2w = nullptr, *n2b = nullptr;
+};
+
+constexpr int PE_MAX = 8192;          // positional table rows (reference: 4096, src/gsv_ar.cpp:44)
+constexpr int PREFILL_ROWS = 16384;   // rows of one prefill pass
+constexpr int STEP_CHUNK = 16;        // decode steps between host status reads in generate
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+// xorshift64 (without the output multiplier) as a 64x64 GF(2) matrix: column b = image of bit b.
+struct Gf2 {
+    uint64_t c[64];
+};
+uint64_t xs_step_h(uint64_t s) {
+    s ^= s >> 12;
+    s ^= s << 25;
+    s ^= s >> 27;
+    return s;
+}
+uint64_t gf2_apply(const Gf2& m, uint64_t v) {
+    uint64_t r = 0;
+    for (int b = 0; b < 64; b++)
+        if ((v >> b) & 1ull) r ^= m.c[b];
+    return r;
+}
+Gf2 gf2_mul(const Gf2& a, const Gf2& b) {   // a after b
+    Gf2 r;
+    for (int i = 0; i < 64; i++) r.c[i] = gf2_apply(a, b.c[i]);
+    return r;
+}
+Gf2 gf2_identity() {
+    Gf2 r;
+    for (int i = 0; i < 64; i++) r.c[i] = 1ull << i;
+    return r;
+}
+Gf2 gf2_pow(Gf2 base, uint64_t e) {
+    Gf2 r = gf2_identity();
+    while (e) {
+        if (e & 1) r = gf2_mul(base, r);
+        base = gf2_mul(base, base);
+        e >>= 1;
+    }
+    return r;
+}
+// Jump matrices T^(j * dpl), j = 0..31, for the sampler's lane-parallel draws.
+std::vector<uint64_t> jump_matrices(int dpl) {
+    Gf2 T;
+    for (int b = 0; b < 64; b++) T.c[b] = xs_step_h(1ull << b);
+    const Gf2 step = gf2_pow(T, (uint64_t)dpl);
+    std::vector<uint64_t> jm(32 * 64);
+    Gf2 cur = gf2_identity();
+    for (int j = 0; j < 32; j++) {
+        std::memcpy(jm.data() + (size_t)j * 64, cur.c, 64 * 8);
+        cur = gf2_mul(step, cur);
+    }
+    return jm;
+}
+
+// ------------------------------------------------------------------ model validation
+// Checks the GGUF against what gsv_ar::load binds (src/gsv_ar.cpp:571-662): KV hyper-parameters,
+// every tensor name, shape and type (attention/FFN Q8_0, the rest F32, src/gsv_ar.cpp:632-637).
+struct ModelView {
+    gsvcu_hparams hp{};
+    const GgufTensor *te = nullptr, *ae = nullptr, *bp = nullptr, *bb = nullptr, *ta = nullptr, *aa = nullptr,
+                     *pr = nullptr;
+    std::vector<const GgufTensor*> mats, vecs;   // [layer][4], [layer][8]
+};
+
+const char* kMatNames[4] = {"qkv_w", "out_w", "ffn1_w", "ffn2_w"};
+const char* kVecNames[8] = {"qkv_b", "out_b", "norm1_w", "norm1_b", "ffn1_b", "ffn2_b", "norm2_w", "norm2_b"};
+
+int validate_model(const GgufFile& f, ModelView& mv, std::string& err) {
+    uint32_t v = 0;
+    auto kv = [&](const char* k, int def) { return f.get_u32(k, v) ? (int)v : def; };
+    gsvcu_hparams& hp = mv.hp;
+    hp.hidden_dim = kv("ar.hidden_dim", 512);
+    hp.n_head = kv("ar.head", 16);
+    hp.n_layer = kv("ar.n_layer", 24);
+    hp.vocab_size = kv("ar.vocab_size", 1025);
+    hp.phoneme_vocab_size = kv("ar.phoneme_vocab_size", 732);
+    hp.eos = kv("ar.eos", 1024);
+    hp.bert_dim = 1024;
+    hp.head_dim = hp.n_head > 0 ? hp.hidden_dim / hp.n_head : 0;
+    hp.ffn_dim = 4 * hp.hidden_dim;
+    if (hp.hidden_dim != D || hp.n_head != NH) {
+        err = "unsupported AR dims: hidden " + std::to_string(hp.hidden_dim) + ", heads " + std::to_string(hp.n_head) +
+              " (this build: 512 x 16)";
+        return GSVCU_ERR_FORMAT;
+    }
+    if (hp.n_layer < 1 || hp.n_layer > 64 || hp.vocab_size < 2 || hp.vocab_size > 1280 || hp.eos < 0 ||
+        hp.eos >= hp.vocab_size || hp.phoneme_vocab_size < 1) {
+        err = "AR hyper-parameters out of range";
+        return GSVCU_ERR_FORMAT;
+    }
+    const int NL = hp.n_layer, V = hp.vocab_size, PV = hp.phoneme_vocab_size, BD = hp.bert_dim;
+    auto need = [&](const std::string& name, uint32_t type, std::vector<int64_t> dims, const GgufTensor** out) -> int {
+        const GgufTensor* t = f.tensor(name);
+        if (!t) { err = "missing tensor " + name; return GSVCU_ERR_FORMAT; }
+        if (t->type != type) {
+            err = "tensor " + name + " has ggml type " + std::to_string(t->type) + ", expected " + std::to_string(type);
+            return GSVCU_ERR_FORMAT;
+        }
+        int64_t ne = 1, ne_want = 1;
+        for (int64_t d : t->dims) ne *= d;
+        for (int64_t d : dims) ne_want *= d;
+        if (ne != ne_want || t->dims[0] != dims[0] || !t->data) {
+            err = "tensor " + name + " has unexpected shape";
+            return GSVCU_ERR_FORMAT;
+        }
+        *out = t;
+        return GSVCU_OK;
+    };
+    int r;
+    if ((r = need("ar.text_emb", 0, {D, PV}, &mv.te)) || (r = need("ar.audio_emb", 0, {D, V}, &mv.ae)) ||
+        (r = need("ar.bert_proj", 0, {BD, D}, &mv.bp)) || (r = need("ar.bert_proj_b", 0, {D}, &mv.bb)) ||
+        (r = need("ar.text_pe_alpha", 0, {1}, &mv.ta)) || (r = need("ar.audio_pe_alpha", 0, {1}, &mv.aa)) ||
+        (r = need("ar.predict", 0, {D, V}, &mv.pr)))
+        return r;
+    std::memcpy(&hp.text_pe_alpha, mv.ta->data, 4);
+    std::memcpy(&hp.audio_pe_alpha, mv.aa->data, 4);
+    const int NK[4][2] = {{3 * D, D}, {D, D}, {FF, D}, {D, FF}};
+    const int VL[8] = {3 * D, D, D, D, FF, D, D, D};
+    mv.mats.assign((size_t)NL * 4, nullptr);
+    mv.vecs.assign((size_t)NL * 8, nullptr);
+    for (int li = 0; li < NL; li++) {
+        const std::string pfx = "transformer.block" + std::to_string(li) + ".";
+        for (int m = 0; m < 4; m++)
+            if ((r = need(pfx + kMatNames[m], 8, {NK[m][1], NK[m][0]}, &mv.mats[(size_t)li * 4 + m]))) return r;
+        for (int k = 0; k < 8; k++)
+            if ((r = need(pfx + kVecNames[k], 0, {VL[k]}, &mv.vecs[(size_t)li * 8 + k]))) return r;
+    }
+    return GSVCU_OK;
+}
+
+}  // namespace
+
+struct gsvcu_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    std::string err;
+
+    int fail(int code, const std::string& msg) {
+        err = msg;
+        return code;
+    }
+
+    // ------------------------------------------------------------ model
+    std::vector<void*> wallocs;
+    bool loaded = false;
+    gsvcu_hparams hp{};
+    std::vector<LayerW> L;
+    float *predict = nullptr, *bert_aug = nullptr, *text_emb = nullptr, *audio_emb = nullptr, *pe = nullptr;
+    uint64_t* jump = nullptr;
+    int dpl = 0;
+
+    // ------------------------------------------------------------ cache / slots
+    std::vector<void*> callocs;
+    bool reserved = false;
+    int max_slots = 0, max_ctx = 0, kv_f32 = 0, max_pages = 0, n_pages = 0;
+    void* pool = nullptr;
+    int32_t* block_table = nullptr;
+    std::vector<int32_t> h_bt;
+    std::vector<int> free_pages;
+    SlotState* st = nullptr;
+    std::vector<SlotState> h_st;
+    std::vector<char> slot_used;
+    std::vector<std::vector<int>> slot_pages;
+    std::vector<int> slot_tag;
+    uint16_t* counts = nullptr;
+    int32_t* hist = nullptr;
+    int32_t* out_tokens = nullptr;
+    int tok_cap = 0;
+    int32_t* forced = nullptr;
+    int forced_cap = 0;
+    float* logits = nullptr;
+    int Mmax = 0;
+    float *x = nullptr, *qkv = nullptr, *pre = nullptr, *n1 = nullptr, *attn_f32 = nullptr;
+    int8_t *xq = nullptr, *aq = nullptr, *n1q = nullptr, *hq = nullptr;
+    uint16_t *xd = nullptr, *ad = nullptr, *n1d = nullptr, *hd = nullptr;
+    float* part = nullptr;
+    int32_t* counter = nullptr;
+    int max_chunks = 0;
+    // prefill staging
+    int32_t *p_ids = nullptr, *p_pepos = nullptr, *p_istext = nullptr, *p_tslot = nullptr, *p_tpos = nullptr,
+            *p_rowT = nullptr, *p_sstart = nullptr, *p_slen = nullptr, *p_tlen = nullptr, *p_last = nullptr,
+            *p_slots = nullptr;
+    int64_t* p_rowoff = nullptr;
+    PrefillTile* p_tiles = nullptr;
+    float *p_feat = nullptr, *p_xl = nullptr, *p_lg = nullptr;
+    size_t feat_cap = 0;
+
+    // ------------------------------------------------------------ decode graph
+    cudaGraphExec_t graph = nullptr;
+    gsvcu_sampler_cfg graph_cfg{};
+    gsvcu_sampler_cfg cfg{15, 1.0f, 1.0f, 1.35f};
+    int64_t tokens_done = 0;   // generated tokens of finished sequences (serving)
+
+    // op-entry scratch
+    float* op_part = nullptr;
+    int32_t* op_counter = nullptr;
+    size_t op_part_n = 0, op_counter_n = 0;
+
+    ~gsvcu_ctx();
+    int load(const char* path);
+    void free_cache();
+    int reserve(int slots, int ctx, int kvd);
+    int ensure(int need_slots, int need_ctx, int kvd);
+    int set_cfg(const gsvcu_sampler_cfg& c);
+    int admit(const gsvcu_request* reqs, int n, const uint64_t* seeds, const int32_t* tags, int max_steps,
+              int early_stop, bool one_group, const int32_t* forced_tok, int n_forced, bool forced_per_seq,
+              std::vector<int>& slots_out, float* dump);
+    int prefill_pass(const int* slots, const gsvcu_request* reqs, int n, float* dump, int dump_b0, int dump_B);
+    int launch_step(cudaStream_t s, float* dump = nullptr, int dump_row = 0, const int* dump_slots = nullptr,
+                    int dump_B = 0);
+    int run_steps(int n);
+    int read_status();
+    void release_slot(int slot);
+    int alloc_dev(void** p, size_t bytes, std::vector<void*>& owner) {
+        cudaError_t e = cudaMalloc(p, bytes);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            *p = nullptr;
+            return fail(GSVCU_ERR_OOM, "cudaMalloc(" + std::to_string(bytes) + ") failed: " + cudaGetErrorString(e));
+        }
+        owner.push_back(*p);
+        return GSVCU_OK;
+    }
+};
+
+#define CK(call)                                                                                        \
+    do {                                                                                                \
+        cudaError_t e_ = (call);                                                                        \
+        if (e_ != cudaSuccess) return fail(GSVCU_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+    } while (0)
+#define CKC(ctx, call)                                                                                  \
+    do {                                                                                                \
+        cudaError_t e_ = (call);                                                                        \
+        if (e_ != cudaSuccess)                                                                          \
+            return (ctx)->fail(GSVCU_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_));     \
+    } while (0)
+#define TRY(expr)                      \
+    do {                               \
+        int r_ = (expr);               \
+        if (r_ != GSVCU_OK) return r_; \
+    } while (0)
+
+gsvcu_ctx::~gsvcu_ctx() {
+    DeviceGuard g(device);
+    free_cache();
+    for (void* p : wallocs) cudaFree(p);
+    if (op_part) cudaFree(op_part);
+    if (op_counter) cudaFree(op_counter);
+    if (stream) cudaStreamDestroy(stream);
+}
+
+// ------------------------------------------------------------------ model load (src/gsv_ar.cpp:490-705)
+int gsvcu_ctx::load(const char* path) {
+    GgufFile f;
+    std::string e;
+    if (!f.open(path, e)) return fail(GSVCU_ERR_IO, e);
+    ModelView mv;
+    const int vr = validate_model(f, mv, e);
+    if (vr != GSVCU_OK) return fail(vr, e);
+    hp = mv.hp;
+    const int NL = hp.n_layer, V = hp.vocab_size, BD = hp.bert_dim;
+    auto upload = [&](const void* src, size_t bytes, void** dst) -> int {
+        TRY(alloc_dev(dst, bytes, wallocs));
+        CK(cudaMemcpy(*dst, src, bytes, cudaMemcpyHostToDevice));
+        return GSVCU_OK;
+    };
+    TRY(upload(mv.te->data, mv.te->nbytes, (void**)&text_emb));
+    TRY(upload(mv.ae->data, mv.ae->nbytes, (void**)&audio_emb));
+    TRY(upload(mv.pr->data, mv.pr->nbytes, (void**)&predict));
+    {   // [W | b] augmented BERT projection (src/gsv_ar.cpp:648-656)
+        std::vector<float> aug((size_t)D * (BD + 1));
+        const float* w = (const float*)mv.bp->data;
+        const float* b = (const float*)mv.bb->data;
+        for (int d = 0; d < D; d++) {
+            std::memcpy(aug.data() + (size_t)d * (BD + 1), w + (size_t)d * BD, (size_t)BD * 4);
+            aug[(size_t)d * (BD + 1) + BD] = b[d];
+        }
+        TRY(upload(aug.data(), aug.size() * 4, (void**)&bert_aug));
+    }
+    L.assign(NL, LayerW());
+    std::vector<uint8_t> wq_tmp;
+    std::vector<uint16_t> wd_tmp;
+    const int NK[4][2] = {{3 * D, D}, {D, D}, {FF, D}, {D, FF}};
+    for (int li = 0; li < NL; li++) {
+        for (int m = 0; m < 4; m++) {
+            const GgufTensor* t = mv.mats[(size_t)li * 4 + m];
+            const int N = NK[m][0], K = NK[m][1];
+            wq_tmp.resize((size_t)N * K);
+            wd_tmp.resize((size_t)N * K / QK);
+            pack_q8_0_host(t->data, N, K, wq_tmp.data(), wd_tmp.data());
+            TRY(upload(wq_tmp.data(), wq_tmp.size(), (void**)&L[li].wq[m]));
+            TRY(upload(wd_tmp.data(), wd_tmp.size() * 2, (void**)&L[li].wd[m]));
+        }
+        float** dst[8] = {&L[li].b_qkv, &L[li].b_out, &L[li].n1w, &L[li].n1b,
+                          &L[li].b_f1, &L[li].b_f2, &L[li].n2w, &L[li].n2b};
+        for (int k = 0; k < 8; k++) {
+            const GgufTensor* t = mv.vecs[(size_t)li * 8 + k];
+            TRY(upload(t->data, t->nbytes, (void**)dst[k]));
+        }
+    }
+    {   // mk_pe (src/gsv_ar.cpp:173-181), same float expressions, extended to PE_MAX rows
+        std::vector<float> tab((size_t)PE_MAX * D);
+        for (int pos = 0; pos < PE_MAX; pos++)
+            for (int i = 0; i < D; i += 2) {
+                const float div = std::exp((float)i * -(std::log(10000.0f) / (float)D));
+                tab[(size_t)pos * D + i] = std::sin((float)pos * div);
+                tab[(size_t)pos * D + i + 1] = std::cos((float)pos * div);
+            }
+        TRY(upload(tab.data(), tab.size() * 4, (void**)&pe));
+    }
+    dpl = (V + 31) / 32;
+    {
+        std::vector<uint64_t> jm = jump_matrices(dpl);
+        TRY(upload(jm.data(), jm.size() * 8, (void**)&jump));
+    }
+    loaded = true;
+    return GSVCU_OK;
+}
+
+// ------------------------------------------------------------------ KV pool and buffers
+void gsvcu_ctx::free_cache() {
+    if (graph) {
+        cudaGraphExecDestroy(graph);
+        graph = nullptr;
+    }
+    if (stream) cudaStreamSynchronize(stream);
+    for (void* p : callocs) cudaFree(p);
+    callocs.clear();
+    p_feat = nullptr;
+    reserved = false;
+    max_slots = max_ctx = n_pages = max_pages = 0;
+    h_bt.clear();
+    free_pages.clear();
+    h_st.clear();
+    slot_used.clear();
+    slot_pages.clear();
+    slot_tag.clear();
+    feat_cap = 0;
+}
+
+int gsvcu_ctx::reserve(int slots, int ctx, int kvd) {
+    if (!loaded) return fail(GSVCU_ERR_STATE, "no model loaded");
+    if (slots < 1 || slots > 4096 || ctx < 1 || ctx > PE_MAX || (kvd != GSVCU_KV_F16 && kvd != GSVCU_KV_F32))
+        return fail(GSVCU_ERR_ARG, "kv_reserve: slots in [1, 4096], ctx in [1, 8192], kv dtype F16/F32");
+    for (char u : slot_used)
+        if (u) return fail(GSVCU_ERR_STATE, "kv_reserve while sequences are in flight");
+    free_cache();
+    const int NL = hp.n_layer, V = hp.vocab_size;
+    max_slots = (slots + 7) / 8 * 8;
+    max_ctx = ctx;
+    kv_f32 = kvd;
+    max_pages = (ctx + PAGE - 1) / PAGE;
+    n_pages = max_slots * max_pages;
+    max_chunks = (ctx + ATT_CHUNK - 1) / ATT_CHUNK;
+    tok_cap = ctx;
+    forced_cap = ctx;
+    Mmax = std::max(PREFILL_ROWS, max_slots);
+    const size_t page_bytes = (size_t)NL * 2 * NH * PAGE * HD * (kvd == GSVCU_KV_F32 ? 4 : 2);
+    const size_t M = (size_t)Mmax;
+    struct A { void** p; size_t bytes; };
+    const A list[] = {
+        {&pool, page_bytes * n_pages},
+        {(void**)&block_table, (size_t)max_slots * max_pages * 4},
+        {(void**)&st, sizeof(SlotState) * max_slots},
+        {(void**)&counts, (size_t)max_slots * V * 2},
+        {(void**)&hist, (size_t)max_slots * HIST * 4},
+        {(void**)&out_tokens, (size_t)max_slots * tok_cap * 4},
+        {(void**)&forced, (size_t)max_slots * forced_cap * 4},
+        {(void**)&logits, (size_t)max_slots * V * 4},
+        {(void**)&x, M * D * 4}, {(void**)&qkv, M * 3 * D * 4}, {(void**)&pre, M * D * 4},
+        {(void**)&n1, M * D * 4}, {(void**)&attn_f32, M * D * 4},
+        {(void**)&xq, M * D}, {(void**)&aq, M * D}, {(void**)&n1q, M * D}, {(void**)&hq, M * FF},
+        {(void**)&xd, M * D / QK * 2}, {(void**)&ad, M * D / QK * 2}, {(void**)&n1d, M * D / QK * 2},
+        {(void**)&hd, M * FF / QK * 2},
+        {(void**)&part, (size_t)max_slots * NH * max_chunks * (2 + HD) * 4},
+        {(void**)&counter, (size_t)max_slots * NH * 4},
+        {(void**)&p_ids, M * 4}, {(void**)&p_pepos, M * 4}, {(void**)&p_istext, M * 4},
+        {(void**)&p_tslot, M * 4}, {(void**)&p_tpos, M * 4}, {(void**)&p_rowT, M * 4}, {(void**)&p_rowoff, M * 8},
+        {(void**)&p_sstart, (size_t)max_slots * 4}, {(void**)&p_slen, (size_t)max_slots * 4},
+        {(void**)&p_tlen, (size_t)max_slots * 4}, {(void**)&p_last, (size_t)max_slots * 4},
+        {(void**)&p_slots, (size_t)max_slots * 4},
+        {(void**)&p_tiles, (M / PREF_QTILE + max_slots) * sizeof(PrefillTile)},
+        {(void**)&p_xl, (size_t)max_slots * D * 4}, {(void**)&p_lg, (size_t)max_slots * V * 4},
+    };
+    for (const A& a : list) {
+        const int r = alloc_dev(a.p, a.bytes, callocs);
+        if (r != GSVCU_OK) {
+            free_cache();
+            return r;
+        }
+    }
+    CK(cudaMemsetAsync(counter, 0, (size_t)max_slots * NH * 4, stream));
+    CK(cudaMemsetAsync(st, 0, sizeof(SlotState) * max_slots, stream));
+    CK(cudaMemsetAsync(xq, 0, M * D, stream));
+    CK(cudaMemsetAsync(xd, 0, M * D / QK * 2, stream));
+    CK(cudaMemsetAsync(x, 0, M * D * 4, stream));
+    CK(cudaMemsetAsync(block_table, 0, (size_t)max_slots * max_pages * 4, stream));
+    h_bt.assign((size_t)max_slots * max_pages, 0);
+    free_pages.resize(n_pages);
+    for (int i = 0; i < n_pages; i++) free_pages[i] = n_pages - 1 - i;
+    h_st.assign(max_slots, SlotState{});
+    slot_used.assign(max_slots, 0);
+    slot_pages.assign(max_slots, {});
+    slot_tag.assign(max_slots, 0);
+    CK(cudaStreamSynchronize(stream));
+    reserved = true;
+    return GSVCU_OK;
+}
+
+int gsvcu_ctx::ensure(int need_slots, int need_ctx, int kvd) {
+    if (reserved && max_slots >= need_slots && max_ctx >= need_ctx && kv_f32 == kvd) return GSVCU_OK;
+    for (char u : slot_used)
+        if (u) return fail(GSVCU_ERR_OOM, "KV pool too small for this batch while other sequences are in flight");
+    const int slots = std::max(need_slots, reserved ? max_slots : 0);
+    const int ctx = std::max(need_ctx, reserved ? max_ctx : 0);
+    return reserve(slots, ctx, kvd);
+}
+
+int gsvcu_ctx::set_cfg(const gsvcu_sampler_cfg& c) {
+    const bool same = c.top_k == cfg.top_k && c.top_p == cfg.top_p && c.temperature == cfg.temperature &&
+                      c.repetition_penalty == cfg.repetition_penalty;
+    if (same) return GSVCU_OK;
+    for (char u : slot_used)
+        if (u) return fail(GSVCU_ERR_STATE, "sampler settings differ from the sequences in flight");
+    cfg = c;
+    return GSVCU_OK;
+}
+
+void gsvcu_ctx::release_slot(int slot) {
+    for (int pg : slot_pages[slot]) free_pages.push_back(pg);
+    slot_pages[slot].clear();
+    slot_used[slot] = 0;
+}
+
+// ------------------------------------------------------------------ prefill
+// Packs the sequences' rows back to back (no padding; the reference's left-pad keys are always
+// masked, src/gsv_ar.cpp:219, so they contribute nothing) and runs the layers over all rows.
+int gsvcu_ctx::prefill_pass(const int* slots, const gsvcu_request* reqs, int n, float* dump, int dump_b0,
+                            int dump_B) {
+    const int NL = hp.n_layer, V = hp.vocab_size, BD = hp.bert_dim;
+    int M = 0;
+    for (int i = 0; i < n; i++) M += reqs[i].n_phones + reqs[i].n_prompt;
+    std::vector<int32_t> ids(M), pepos(M), istext(M), tslot(M), tpos(M), rowT(M), sstart(n), slen(n), tlen(n), last(n),
+        sl(n);
+    std::vector<int64_t> rowoff(M, 0);
+    std::vector<PrefillTile> tiles;
+    size_t feat_n = 0;
+    for (int i = 0; i < n; i++) feat_n += (size_t)BD * reqs[i].n_phones;
+    std::vector<float> feat(feat_n);
+    int m = 0;
+    size_t fo = 0;
+    for (int i = 0; i < n; i++) {
+        const gsvcu_request& r = reqs[i];
+        const int T = r.n_phones, P = r.n_prompt;
+        sstart[i] = m;
+        slen[i] = T + P;
+        tlen[i] = T;
+        last[i] = m + T + P - 1;
+        sl[i] = slots[i];
+        std::memcpy(feat.data() + fo, r.bert, (size_t)BD * T * 4);
+        for (int t = 0; t < T; t++, m++) {
+            ids[m] = r.phones[t];
+            pepos[m] = t;
+            istext[m] = 1;
+            tslot[m] = slots[i];
+            tpos[m] = t;
+            rowT[m] = T;
+            rowoff[m] = (int64_t)fo + t;
+        }
+        for (int t = 0; t < P; t++, m++) {
+            ids[m] = r.prompt[t];
+            pepos[m] = t;
+            istext[m] = 0;
+            tslot[m] = slots[i];
+            tpos[m] = T + t;
+            rowT[m] = -1;
+        }
+        for (int q0 = 0; q0 < T + P; q0 += PREF_QTILE) tiles.push_back({i, q0});
+        fo += (size_t)BD * T;
+    }
+    cudaStream_t s = stream;
+    if (feat_n > feat_cap) {
+        if (p_feat) {
+            cudaStreamSynchronize(s);
+            cudaFree(p_feat);
+            callocs.erase(std::find(callocs.begin(), callocs.end(), (void*)p_feat));
+            p_feat = nullptr;
+            feat_cap = 0;
+        }
+        TRY(alloc_dev((void**)&p_feat, feat_n * 4, callocs));
+        feat_cap = feat_n;
+    }
+    auto h2d = [&](void* dst, const void* src, size_t bytes) {
+        return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, s);
+    };
+    CK(h2d(p_ids, ids.data(), (size_t)M * 4));
+    CK(h2d(p_pepos, pepos.data(), (size_t)M * 4));
+    CK(h2d(p_istext, istext.data(), (size_t)M * 4));
+    CK(h2d(p_tslot, tslot.data(), (size_t)M * 4));
+    CK(h2d(p_tpos, tpos.data(), (size_t)M * 4));
+    CK(h2d(p_rowT, rowT.data(), (size_t)M * 4));
+    CK(h2d(p_rowoff, rowoff.data(), (size_t)M * 8));
+    CK(h2d(p_sstart, sstart.data(), (size_t)n * 4));
+    CK(h2d(p_slen, slen.data(), (size_t)n * 4));
+    CK(h2d(p_tlen, tlen.data(), (size_t)n * 4));
+    CK(h2d(p_last, last.data(), (size_t)n * 4));
+    CK(h2d(p_slots, sl.data(), (size_t)n * 4));
+    CK(h2d(p_tiles, tiles.data(), tiles.size() * sizeof(PrefillTile)));
+    if (feat_n) CK(h2d(p_feat, feat.data(), feat_n * 4));
+
+    PrefEmbedParams ep;
+    ep.ids = p_ids; ep.pe_pos = p_pepos; ep.is_text = p_istext; ep.text_emb = text_emb; ep.audio_emb = audio_emb;
+    ep.pe = pe; ep.text_alpha = hp.text_pe_alpha; ep.audio_alpha = hp.audio_pe_alpha; ep.M = M; ep.x = x;
+    launch_prefill_embed(ep, s);
+    // cur = x + bert_aug . [bert; 1] on text rows (src/gsv_ar.cpp:241); prompt rows gather zeros
+    F32Gather gth;
+    gth.feat = p_feat; gth.row_off = p_rowoff; gth.row_T = p_rowT; gth.bert_dim = BD;
+    launch_gemm_f32d(nullptr, 0, &gth, M, bert_aug, D, BD + 1, x, D, x, D, s);
+    launch_quantize_q8(x, M, D, xq, xd, s);
+
+    const float scale = 1.0f / std::sqrt((float)HD);
+    auto dump_rows = [&](int li, int item, const float* src) -> int {
+        for (int i = 0; i < n; i++) {
+            float* dst = dump + ((((size_t)0 * dump_B + dump_b0 + i) * NL + li) * 4 + item) * D;
+            CK(cudaMemcpyAsync(dst, src + (size_t)last[i] * D, D * 4, cudaMemcpyDeviceToHost, s));
+        }
+        return GSVCU_OK;
+    };
+    for (int li = 0; li < NL; li++) {
+        const LayerW& w = L[li];
+        GemmQ8Params g;
+        g.xq = xq; g.xd = xd; g.M = M; g.wq = w.wq[0]; g.wd = w.wd[0]; g.N = 3 * D; g.K = D; g.bias = w.b_qkv; g.y = qkv;
+        g.kv.pool = pool; g.kv.kv_f32 = kv_f32; g.kv.n_layer = NL; g.kv.layer = li; g.kv.block_table = block_table;
+        g.kv.max_pages = max_pages; g.kv.tok_slot = p_tslot; g.kv.tok_pos = p_tpos;
+        launch_gemm_q8(g, EPI_BIAS, s);
+        PrefAttnParams a;
+        a.qkv = qkv; a.seq_start = p_sstart; a.seq_len = p_slen; a.text_len = p_tlen; a.tiles = p_tiles;
+        a.n_tiles = (int)tiles.size(); a.scale = scale; a.out_q = aq; a.out_d = ad; a.out_f32 = dump ? attn_f32 : nullptr;
+        launch_prefill_attention(a, s);
+        GemmQ8Params o;
+        o.xq = aq; o.xd = ad; o.M = M; o.wq = w.wq[1]; o.wd = w.wd[1]; o.N = D; o.K = D; o.bias = w.b_out; o.resid = x; o.y = pre;
+        launch_gemm_q8(o, EPI_RESID, s);
+        launch_layernorm_q8(pre, M, w.n1w, w.n1b, n1, n1q, n1d, s);
+        GemmQ8Params f1;
+        f1.xq = n1q; f1.xd = n1d; f1.M = M; f1.wq = w.wq[2]; f1.wd = w.wd[2]; f1.N = FF; f1.K = D; f1.bias = w.b_f1;
+        f1.yq = hq; f1.yd = hd;
+        launch_gemm_q8(f1, EPI_RELU_Q8, s);
+        GemmQ8Params f2;
+        f2.xq = hq; f2.xd = hd; f2.M = M; f2.wq = w.wq[3]; f2.wd = w.wd[3]; f2.N = D; f2.K = FF; f2.bias = w.b_f2;
+        f2.resid = n1; f2.y = pre;
+        launch_gemm_q8(f2, EPI_RESID, s);
+        if (dump) {
+            TRY(dump_rows(li, 0, attn_f32));
+            TRY(dump_rows(li, 1, n1));
+            TRY(dump_rows(li, 2, pre));
+        }
+        launch_layernorm_q8(pre, M, w.n2w, w.n2b, x, xq, xd, s);
+        if (dump) TRY(dump_rows(li, 3, x));
+    }
+    // logits of each sequence's last position (src/gsv_ar.cpp:266-269) into its slot's row
+    launch_copy_rows(p_xl, nullptr, x, p_last, n, D, s);
+    launch_gemm_f32d(p_xl, D, nullptr, n, predict, V, D, nullptr, 0, p_lg, V, s);
+    launch_copy_rows(logits, p_slots, p_lg, nullptr, n, V, s);
+    CK(cudaGetLastError());
+    // host staging vectors die at return: finish the pass before they go
+    CK(cudaStreamSynchronize(s));
+    return GSVCU_OK;
+}
+
+// Admit n sequences into free slots: pages, slot state, repetition window, prefill.
+int gsvcu_ctx::admit(const gsvcu_request* reqs, int n, const uint64_t* seeds, const int32_t* tags, int max_steps,
+                     int early_stop, bool one_group, const int32_t* forced_tok, int n_forced, bool forced_per_seq,
+                     std::vector<int>& slots_out, float* dump) {
+    const int V = hp.vocab_size;
+    slots_out.clear();
+    if (n <= 0) return GSVCU_OK;
+    if (max_steps < 1) return fail(GSVCU_ERR_ARG, "max_steps must be >= 1");
+    int total_rows = 0;
+    for (int i = 0; i < n; i++) {
+        const gsvcu_request& r = reqs[i];
+        if (r.n_phones <= 0 || !r.phones || !r.bert) return fail(GSVCU_ERR_ARG, "request without phones/bert");
+        if (r.n_prompt < 0 || (r.n_prompt > 0 && !r.prompt)) return fail(GSVCU_ERR_ARG, "bad prompt");
+        for (int t = 0; t < r.n_phones; t++)
+            if (r.phones[t] < 0 || r.phones[t] >= hp.phoneme_vocab_size)
+                return fail(GSVCU_ERR_ARG, "phone id out of range");
+        for (int t = 0; t < r.n_prompt; t++)
+            if (r.prompt[t] < 0 || r.prompt[t] >= V) return fail(GSVCU_ERR_ARG, "prompt code out of range");
+        const int S = r.n_phones + r.n_prompt;
+        if (S + max_steps > max_ctx) return fail(GSVCU_ERR_ARG, "sequence longer than the reserved context");
+        if (r.n_prompt + max_steps > PE_MAX || r.n_phones > PE_MAX) return fail(GSVCU_ERR_ARG, "position beyond PE table");
+        if (S > Mmax) return fail(GSVCU_ERR_ARG, "prefix longer than a prefill pass");
+        total_rows += S;
+    }
+    if (dump && total_rows > Mmax) return fail(GSVCU_ERR_ARG, "debug dumps need a single prefill pass");
+    if (forced_tok)
+        for (int i = 0; i < (forced_per_seq ? n * n_forced : n_forced); i++)
+            if (forced_tok[i] < 0 || forced_tok[i] >= V) return fail(GSVCU_ERR_ARG, "forced token out of range");
+    int need_pages = 0;
+    for (int i = 0; i < n; i++) need_pages += (reqs[i].n_phones + reqs[i].n_prompt + max_steps + PAGE - 1) / PAGE;
+    int free_slots = 0;
+    for (char u : slot_used) free_slots += !u;
+    if (free_slots < n) return fail(GSVCU_ERR_OOM, "no free sequence slot");
+    if ((int)free_pages.size() < need_pages) return fail(GSVCU_ERR_OOM, "KV page pool exhausted");
+    int next = 0;
+    for (int i = 0; i < n; i++) {
+        while (slot_used[next]) next++;
+        slots_out.push_back(next);
+        slot_used[next] = 1;
+        next++;
+    }
+    cudaStream_t s = stream;
+    const int first = slots_out[0];
+    std::vector<uint16_t> cnt(V);
+    for (int i = 0; i < n; i++) {
+        const int slot = slots_out[i];
+        const gsvcu_request& r = reqs[i];
+        const int S = r.n_phones + r.n_prompt;
+        const int np = (S + max_steps + PAGE - 1) / PAGE;
+        slot_pages[slot].clear();
+        for (int k = 0; k < np; k++) {
+            slot_pages[slot].push_back(free_pages.back());
+            h_bt[(size_t)slot * max_pages + k] = free_pages.back();
+            free_pages.pop_back();
+        }
+        slot_tag[slot] = tags ? tags[i] : i;
+        CK(cudaMemcpyAsync(block_table + (size_t)slot * max_pages, h_bt.data() + (size_t)slot * max_pages,
+                           (size_t)np * 4, cudaMemcpyHostToDevice, s));
+        // repetition window: the last <= 4096 prompt tokens (src/gsv_ar.cpp:769-771)
+        std::fill(cnt.begin(), cnt.end(), 0);
+        const int nh = std::min(r.n_prompt, HIST);
+        for (int t = r.n_prompt - nh; t < r.n_prompt; t++) cnt[r.prompt[t]]++;
+        CK(cudaMemcpyAsync(counts + (size_t)slot * V, cnt.data(), (size_t)V * 2, cudaMemcpyHostToDevice, s));
+        if (nh) CK(cudaMemcpyAsync(hist + (size_t)slot * HIST, r.prompt + (r.n_prompt - nh), (size_t)nh * 4,
+                                   cudaMemcpyHostToDevice, s));
+        SlotState& ss = h_st[slot];
+        ss = SlotState{};
+        ss.active = 1;
+        ss.kvlen = S;
+        ss.kvpos = 0;
+        ss.prompt_len = r.n_prompt;
+        ss.n_samp = 0;
+        ss.max_steps = max_steps;
+        ss.early_stop = early_stop;
+        ss.group_first = one_group ? first : slot;
+        ss.finish_kind = -1;
+        ss.finish_idx = -1;
+        ss.hist_len = nh;
+        ss.hist_head = 0;
+        ss.decode_now = 0;
+        const uint64_t seed = seeds ? seeds[i] : (uint64_t)i;
+        ss.rng = seed ? seed : 1;   // gsv_rng(seed) (src/gsv_sampler.h:35)
+        ss.n_forced = 0;
+        if (forced_tok && n_forced > 0) {
+            const int nf = std::min(n_forced, forced_cap);
+            ss.n_forced = nf;
+            CK(cudaMemcpyAsync(forced + (size_t)slot * forced_cap,
+                               forced_tok + (forced_per_seq ? (size_t)i * n_forced : 0), (size_t)nf * 4,
+                               cudaMemcpyHostToDevice, s));
+        }
+        CK(cudaMemcpyAsync(st + slot, &ss, sizeof(SlotState), cudaMemcpyHostToDevice, s));
+    }
+    // prefill in passes of at most Mmax rows
+    int i = 0;
+    while (i < n) {
+        int rows = 0, j = i;
+        while (j < n && rows + reqs[j].n_phones + reqs[j].n_prompt <= Mmax) {
+            rows += reqs[j].n_phones + reqs[j].n_prompt;
+            j++;
+        }
+        TRY(prefill_pass(slots_out.data() + i, reqs + i, j - i, dump, i, n));
+        i = j;
+    }
+    return GSVCU_OK;
+}
+
+// ------------------------------------------------------------------ decode step
+// One step for every slot: sample from the current logits, apply the stop rules, embed the new
+// token, run the layers (K/V appended in the QKV epilogue, split-KV attention over the pages),
+// project to logits. All per-step values live on the device, so the sequence is graph-captured.
+// With `dump` (host), every layer's rows of the slots in dump_slots are copied out (no capture).
+int gsvcu_ctx::launch_step(cudaStream_t s, float* dump, int dump_row, const int* dump_slots, int dump_B) {
+    const int NL = hp.n_layer, V = hp.vocab_size, M = max_slots;
+    SamplerParams sp;
+    sp.logits = logits; sp.V = V; sp.eos = hp.eos; sp.nslots = M;
+    sp.top_k = cfg.top_k; sp.top_p = cfg.top_p; sp.temperature = cfg.temperature; sp.rep = cfg.repetition_penalty;
+    sp.st = st; sp.counts = counts; sp.hist = hist; sp.out_tokens = out_tokens; sp.tok_cap = tok_cap;
+    sp.forced = forced; sp.forced_cap = forced_cap; sp.jump = jump; sp.draws_per_lane = dpl;
+    launch_sampler(sp, s);
+    StepPrepParams pp;
+    pp.st = st; pp.nslots = M; pp.eos = hp.eos; pp.out_tokens = out_tokens; pp.tok_cap = tok_cap;
+    pp.audio_emb = audio_emb; pp.pe = pe; pp.audio_alpha = hp.audio_pe_alpha;
+    pp.x = x; pp.xq = xq; pp.xd = xd;
+    launch_step_prep(pp, s);
+    const float scale = 1.0f / std::sqrt((float)HD);
+    for (int li = 0; li < NL; li++) {
+        const LayerW& w = L[li];
+        GemmQ8Params g;
+        g.xq = xq; g.xd = xd; g.M = M; g.wq = w.wq[0]; g.wd = w.wd[0]; g.N = 3 * D; g.K = D; g.bias = w.b_qkv; g.y = qkv;
+        g.kv.pool = pool; g.kv.kv_f32 = kv_f32; g.kv.n_layer = NL; g.kv.layer = li; g.kv.block_table = block_table;
+        g.kv.max_pages = max_pages; g.kv.st = st;
+        launch_gemm_q8(g, EPI_BIAS, s);
+        DecAttnParams a;
+        a.q = qkv; a.q_stride = 3 * D; a.pool = pool; a.kv_f32 = kv_f32; a.n_layer = NL; a.layer = li;
+        a.block_table = block_table; a.max_pages = max_pages; a.st = st; a.B = M; a.max_chunks = max_chunks;
+        a.scale = scale; a.out_q = aq; a.out_d = ad; a.out_f32 = dump ? attn_f32 : nullptr;
+        a.part = part; a.counter = counter;
+        launch_decode_attention(a, s);
+        GemmQ8Params o;
+        o.xq = aq; o.xd = ad; o.M = M; o.wq = w.wq[1]; o.wd = w.wd[1]; o.N = D; o.K = D; o.bias = w.b_out; o.resid = x; o.y = pre;
+        launch_gemm_q8(o, EPI_RESID, s);
+        launch_layernorm_q8(pre, M, w.n1w, w.n1b, n1, n1q, n1d, s);
+        GemmQ8Params f1;
+        f1.xq = n1q; f1.xd = n1d; f1.M = M; f1.wq = w.wq[2]; f1.wd = w.wd[2]; f1.N = FF; f1.K = D; f1.bias = w.b_f1;
+        f1.yq = hq; f1.yd = hd;
+        launch_gemm_q8(f1, EPI_RELU_Q8, s);
+        GemmQ8Params f2;
+        f2.xq = hq; f2.xd = hd; f2.M = M; f2.wq = w.wq[3]; f2.wd = w.wd[3]; f2.N = D; f2.K = FF; f2.bias = w.b_f2;
+        f2.resid = n1; f2.y = pre;
+        launch_gemm_q8(f2, EPI_RESID, s);
+        if (dump) {
+            const float* items[3] = {attn_f32, n1, pre};
+            for (int it = 0; it < 3; it++)
+                for (int b = 0; b < dump_B; b++)
+                    CK(cudaMemcpyAsync(dump + ((((size_t)dump_row * dump_B + b) * NL + li) * 4 + it) * D,
+                                       items[it] + (size_t)dump_slots[b] * D, D * 4, cudaMemcpyDeviceToHost, s));
+        }
+        launch_layernorm_q8(pre, M, w.n2w, w.n2b, x, xq, xd, s);
+        if (dump)
+            for (int b = 0; b < dump_B; b++)
+                CK(cudaMemcpyAsync(dump + ((((size_t)dump_row * dump_B + b) * NL + li) * 4 + 3) * D,
+                                   x + (size_t)dump_slots[b] * D, D * 4, cudaMemcpyDeviceToHost, s));
+    }
+    launch_gemm_f32d(x, D, nullptr, M, predict, V, D, nullptr, 0, logits, V, s);
+    return GSVCU_OK;
+}
+
+int gsvcu_ctx::run_steps(int nsteps) {
+    const bool cfg_same = graph && graph_cfg.top_k == cfg.top_k && graph_cfg.top_p == cfg.top_p &&
+                          graph_cfg.temperature == cfg.temperature &&
+                          graph_cfg.repetition_penalty == cfg.repetition_penalty;
+    if (!cfg_same) {
+        if (graph) {
+            cudaGraphExecDestroy(graph);
+            graph = nullptr;
+        }
+        cudaGraph_t gr;
+        CK(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+        const int lr = launch_step(stream);
+        cudaError_t e = cudaStreamEndCapture(stream, &gr);
+        if (lr != GSVCU_OK) return lr;
+        if (e != cudaSuccess) return fail(GSVCU_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+        e = cudaGraphInstantiate(&graph, gr, 0);
+        cudaGraphDestroy(gr);
+        if (e != cudaSuccess) {
+            graph = nullptr;
+            return fail(GSVCU_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
+        }
+        graph_cfg = cfg;
+    }
+    for (int i = 0; i < nsteps; i++) CK(cudaGraphLaunch(graph, stream));
+    return GSVCU_OK;
+}
+
+int gsvcu_ctx::read_status() {
+    CK(cudaMemcpyAsync(h_st.data(), st, sizeof(SlotState) * max_slots, cudaMemcpyDeviceToHost, stream));
+    CK(cudaStreamSynchronize(stream));
+    return GSVCU_OK;
+}
+
+// ------------------------------------------------------------------ C ABI
+static int max_prefix(const gsvcu_request* reqs, int B) {
+    int m = 0;
+    for (int i = 0; i < B; i++) m = std::max(m, reqs[i].n_phones + reqs[i].n_prompt);
+    return m;
+}
+
+// Generate for one group of sequences (gsv_ar::generate loop, src/gsv_ar.cpp:761-810).
+static int generate_group(gsvcu_ctx* ctx, const gsvcu_request* reqs, int B, const uint64_t* seeds, int early_stop,
+                          int max_steps, const int32_t* forced, int n_forced, bool forced_per_seq,
+                          gsvcu_progress_fn progress, void* user, std::vector<int>& slots) {
+    TRY(ctx->admit(reqs, B, seeds, nullptr, max_steps, early_stop, true, forced, n_forced, forced_per_seq, slots,
+                   nullptr));
+    int done_steps = 0, reported = 0;
+    while (done_steps < max_steps) {
+        const int n = std::min(STEP_CHUNK, max_steps - done_steps);
+        TRY(ctx->run_steps(n));
+        done_steps += n;
+        TRY(ctx->read_status());
+        bool all = true;
+        int iters = 0;
+        for (int sl : slots) {
+            const SlotState& s = ctx->h_st[sl];
+            if (s.active) all = false;
+            iters = std::max(iters, s.finish_kind >= 0 ? s.finish_idx + 1 : s.n_samp);
+        }
+        if (progress && iters > reported) {
+            progress(user, iters);
+            reported = iters;
+        }
+        if (all) break;
+    }
+    return GSVCU_OK;
+}
+
+extern "C" {
+
+int gsvcu_create(int device, gsvcu_ctx** out) {
+    if (!out) return GSVCU_ERR_ARG;
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) {
+        cudaGetLastError();
+        return GSVCU_ERR_DEVICE;
+    }
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess || prop.major != 10) return GSVCU_ERR_DEVICE;
+    DeviceGuard g(device);
+    if (gemm_q8_init_device() != cudaSuccess) {
+        cudaGetLastError();
+        return GSVCU_ERR_CUDA;
+    }
+    gsvcu_ctx* c = new gsvcu_ctx();
+    c->device = device;
+    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        delete c;
+        return GSVCU_ERR_CUDA;
+    }
+    *out = c;
+    return GSVCU_OK;
+}
+
+void gsvcu_destroy(gsvcu_ctx* ctx) { delete ctx; }
+
+const char* gsvcu_last_error(const gsvcu_ctx* ctx) { return ctx ? ctx->err.c_str() : "null context"; }
+
+int gsvcu_load_gguf(gsvcu_ctx* ctx, const char* path) {
+    if (!ctx || !path) return GSVCU_ERR_ARG;
+    if (ctx->loaded) return ctx->fail(GSVCU_ERR_STATE, "model already loaded");
+    DeviceGuard g(ctx->device);
+    const int r = ctx->load(path);
+    if (r != GSVCU_OK) {
+        for (void* p : ctx->wallocs) cudaFree(p);
+        ctx->wallocs.clear();
+        ctx->loaded = false;
+    }
+    return r;
+}
+
+int gsvcu_get_hparams(const gsvcu_ctx* ctx, gsvcu_hparams* out) {
+    if (!ctx || !out) return GSVCU_ERR_ARG;
+    if (!ctx->loaded) return GSVCU_ERR_STATE;
+    *out = ctx->hp;
+    return GSVCU_OK;
+}
+
+int gsvcu_kv_reserve(gsvcu_ctx* ctx, int32_t max_slots, int32_t max_ctx, int32_t kv_dtype) {
+    if (!ctx) return GSVCU_ERR_ARG;
+    DeviceGuard g(ctx->device);
+    return ctx->reserve(max_slots, max_ctx, kv_dtype);
+}
+
+int gsvcu_release_cache(gsvcu_ctx* ctx) {
+    if (!ctx) return GSVCU_ERR_ARG;
+    DeviceGuard g(ctx->device);
+    ctx->free_cache();
+    return GSVCU_OK;
+}
+
+int gsvcu_inspect_gguf(const char* path, gsvcu_hparams* out, char* err, int32_t err_cap) {
+    if (!path) return GSVCU_ERR_ARG;
+    GgufFile f;
+    std::string e;
+    int rc = GSVCU_OK;
+    ModelView mv;
+    if (!f.open(path, e)) rc = GSVCU_ERR_IO;
+    else rc = validate_model(f, mv, e);
+    if (rc == GSVCU_OK && out) *out = mv.hp;
+    if (err && err_cap > 0) {
+        std::strncpy(err, e.c_str(), (size_t)err_cap - 1);
+        err[err_cap - 1] = 0;
+    }
+    return rc;
+}
+
+int gsvcu_first_logits(gsvcu_ctx* ctx, const gsvcu_request* reqs, int32_t B, float* logits_out) {
+    if (!ctx || !reqs || B <= 0 || !logits_out) return GSVCU_ERR_ARG;
+    if (!ctx->loaded) return ctx->fail(GSVCU_ERR_STATE, "no model loaded");
+    DeviceGuard g(ctx->device);
+    TRY(ctx->ensure(B, max_prefix(reqs, B) + 8, ctx->reserved ? ctx->kv_f32 : GSVCU_KV_F16));
+    std::vector<int> slots;
+    const int rc0 = ctx->admit(reqs, B, nullptr, nullptr, 1, -1, true, nullptr, 0, false, slots, nullptr);
+    int rc = rc0;
+    const int V = ctx->hp.vocab_size;
+    for (int b = 0; b < B && rc == GSVCU_OK; b++) {
+        cudaError_t e = cudaMemcpy(logits_out + (size_t)b * V, ctx->logits + (size_t)slots[b] * V, (size_t)V * 4,
+                                   cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) rc = ctx->fail(GSVCU_ERR_CUDA, cudaGetErrorString(e));
+    }
+    for (int sl : slots) ctx->release_slot(sl);
+    return rc;
+}
+
+int gsvcu_generate(gsvcu_ctx* ctx, const gsvcu_request* reqs, int32_t B, const gsvcu_sampler_cfg* sampler,
+                   uint64_t seed_base, int32_t early_stop_num, int32_t max_steps, const int32_t* oracle_tokens,
+                   int32_t n_oracle, const uint64_t* seeds, int32_t n_seeds, int32_t* tokens_out, int32_t* n_tokens_out,
+                   int32_t* lens_out, int32_t cap, gsvcu_progress_fn progress, void* user) {
+    if (!ctx || !reqs || B <= 0 || !tokens_out || !n_tokens_out || !lens_out || cap < 0 || max_steps < 1)
+        return GSVCU_ERR_ARG;
+    if (!ctx->loaded) return ctx->fail(GSVCU_ERR_STATE, "no model loaded");
+    DeviceGuard g(ctx->device);
+    gsvcu_sampler_cfg sc = sampler ? *sampler : gsvcu_sampler_cfg{15, 1.0f, 1.0f, 1.35f};
+    TRY(ctx->ensure(B, max_prefix(reqs, B) + max_steps + 8, ctx->reserved ? ctx->kv_f32 : GSVCU_KV_F16));
+    TRY(ctx->set_cfg(sc));
+    std::vector<uint64_t> sd(B);
+    for (int b = 0; b < B; b++)   // src/gsv_ar.cpp:752-758
+        sd[b] = (seeds && b < n_seeds) ? seeds[b] : seed_base + 0x9E3779B9ull * (uint64_t)b;
+    std::vector<int> slots;
+    int rc = generate_group(ctx, reqs, B, sd.data(), early_stop_num, max_steps, oracle_tokens,
+                            oracle_tokens ? n_oracle : 0, false, progress, user, slots);
+    if (rc == GSVCU_OK) {
+        // results: prompt + generated, lens in finish order (EOS and early stop in step order,
+        // then the sequences that ran to max_steps), src/gsv_ar.cpp:780-815
+        struct Fin { int idx, kind, b; };
+        std::vector<Fin> order;
+        std::vector<int32_t> gen((size_t)max_steps);
+        for (int b = 0; b < B && rc == GSVCU_OK; b++) {
+            const SlotState& s = ctx->h_st[slots[b]];
+            const int ns = s.n_samp;
+            if (ns > 0) {
+                cudaError_t e = cudaMemcpy(gen.data(), ctx->out_tokens + (size_t)slots[b] * ctx->tok_cap,
+                                           (size_t)ns * 4, cudaMemcpyDeviceToHost);
+                if (e != cudaSuccess) { rc = ctx->fail(GSVCU_ERR_CUDA, cudaGetErrorString(e)); break; }
+            }
+            const int kind = s.finish_kind < 0 ? 2 : s.finish_kind;
+            const int keep = kind == 2 ? ns : ns - 1;
+            const int P = reqs[b].n_prompt;
+            const int total = P + keep;
+            n_tokens_out[b] = total;
+            int32_t* row = tokens_out + (size_t)b * cap;
+            for (int t = 0; t < total && t < cap; t++) row[t] = t < P ? reqs[b].prompt[t] : gen[t - P];
+            order.push_back({kind == 2 ? max_steps : s.finish_idx, kind, b});
+        }
+        if (rc == GSVCU_OK) {
+            std::stable_sort(order.begin(), order.end(), [](const Fin& a, const Fin& b) {
+                if ((a.kind == 2) != (b.kind == 2)) return b.kind == 2;
+                if (a.kind == 2) return a.b < b.b;
+                if (a.idx != b.idx) return a.idx < b.idx;
+                if (a.kind != b.kind) return a.kind < b.kind;
+                return a.b < b.b;
+            });
+            for (int i = 0; i < B; i++) lens_out[i] = order[i].idx;
+        }
+    }
+    for (int sl : slots) ctx->release_slot(sl);
+    return rc;
+}
+
+int gsvcu_debug_trace(gsvcu_ctx* ctx, const gsvcu_request* reqs, int32_t B, const int32_t* forced, int32_t n_steps,
+                      float* logits_out, float* dump) {
+    if (!ctx || !reqs || B <= 0 || n_steps < 0 || !logits_out || (n_steps > 0 && !forced)) return GSVCU_ERR_ARG;
+    if (!ctx->loaded) return ctx->fail(GSVCU_ERR_STATE, "no model loaded");
+    DeviceGuard g(ctx->device);
+    for (int i = 0; i < B * n_steps; i++)
+        if (forced[i] == ctx->hp.eos) return ctx->fail(GSVCU_ERR_ARG, "trace tokens must not be EOS");
+    TRY(ctx->ensure(B, max_prefix(reqs, B) + n_steps + 8, ctx->reserved ? ctx->kv_f32 : GSVCU_KV_F16));
+    std::vector<uint64_t> sd(B, 1);
+    std::vector<int> slots;
+    TRY(ctx->admit(reqs, B, sd.data(), nullptr, n_steps + 1, -1, true, forced, n_steps, true, slots, dump));
+    const int V = ctx->hp.vocab_size;
+    auto fetch_logits = [&](int row) -> int {
+        for (int b = 0; b < B; b++)
+            CKC(ctx, cudaMemcpy(logits_out + ((size_t)row * B + b) * V, ctx->logits + (size_t)slots[b] * V,
+                                (size_t)V * 4, cudaMemcpyDeviceToHost));
+        return GSVCU_OK;
+    };
+    int rc = fetch_logits(0);
+    for (int s = 0; s < n_steps && rc == GSVCU_OK; s++) {
+        if (dump) rc = ctx->launch_step(ctx->stream, dump, s + 1, slots.data(), B);   // instrumented, no graph
+        else rc = ctx->run_steps(1);
+        if (rc != GSVCU_OK) break;
+        if (cudaGetLastError() != cudaSuccess) { rc = ctx->fail(GSVCU_ERR_CUDA, "kernel launch failed"); break; }
+        rc = fetch_logits(s + 1);
+    }
+    if (rc == GSVCU_OK && cudaStreamSynchronize(ctx->stream) != cudaSuccess) rc = ctx->fail(GSVCU_ERR_CUDA, "sync");
+    for (int sl : slots) ctx->release_slot(sl);
+    return rc;
+}
+
+int gsvcu_serve_admit(gsvcu_ctx* ctx, const gsvcu_request* reqs, int32_t n, const gsvcu_sampler_cfg* sampler,
+                      const uint64_t* seeds, const int32_t* tags, int32_t max_steps, int32_t early_stop_num) {
+    if (!ctx || (!reqs && n > 0) || n < 0) return GSVCU_ERR_ARG;
+    if (!ctx->loaded) return ctx->fail(GSVCU_ERR_STATE, "no model loaded");
+    if (!ctx->reserved) return ctx->fail(GSVCU_ERR_STATE, "call gsvcu_kv_reserve before serving");
+    DeviceGuard g(ctx->device);
+    gsvcu_sampler_cfg sc = sampler ? *sampler : gsvcu_sampler_cfg{15, 1.0f, 1.0f, 1.35f};
+    TRY(ctx->set_cfg(sc));
+    std::vector<int> slots;
+    return ctx->admit(reqs, n, seeds, tags, max_steps, early_stop_num, false, nullptr, 0, false, slots, nullptr);
+}
+
+int gsvcu_serve_step(gsvcu_ctx* ctx, int32_t n_steps, gsvcu_finished* done, int32_t max_done, int32_t* tokens,
+                     int32_t tok_cap) {
+    if (!ctx || n_steps < 0 || max_done < 0 || (max_done > 0 && !done)) return GSVCU_ERR_ARG;
+    if (!ctx->reserved) return ctx->fail(GSVCU_ERR_STATE, "no KV pool reserved");
+    DeviceGuard g(ctx->device);
+    bool any = false;
+    for (char u : ctx->slot_used) any |= u != 0;
+    if (!any) return 0;
+    if (n_steps > 0) TRY(ctx->run_steps(n_steps));
+    TRY(ctx->read_status());
+    int nd = 0, used = 0;
+    for (int sl = 0; sl < ctx->max_slots; sl++) {
+        if (!ctx->slot_used[sl]) continue;
+        const SlotState& s = ctx->h_st[sl];
+        if (s.active || s.finish_kind < 0) continue;
+        if (nd >= max_done) break;
+        const int keep = s.finish_kind == 2 ? s.n_samp : s.n_samp - 1;
+        gsvcu_finished& f = done[nd++];
+        f.slot = sl;
+        f.tag = ctx->slot_tag[sl];
+        f.finish_kind = s.finish_kind;
+        f.n_generated = s.finish_kind == 2 ? s.max_steps : s.finish_idx;
+        f.n_tokens = 0;
+        if (tokens && keep > 0 && used + keep <= tok_cap) {
+            CKC(ctx, cudaMemcpy(tokens + used, ctx->out_tokens + (size_t)sl * ctx->tok_cap, (size_t)keep * 4,
+                                cudaMemcpyDeviceToHost));
+            f.n_tokens = keep;
+            used += keep;
+        }
+        ctx->tokens_done += keep;
+        ctx->release_slot(sl);
+    }
+    return nd;
+}
+
+int gsvcu_serve_active(const gsvcu_ctx* ctx) {
+    if (!ctx) return GSVCU_ERR_ARG;
+    int n = 0;
+    for (char u : ctx->slot_used) n += u != 0;
+    return n;
+}
+
+int64_t gsvcu_serve_tokens_total(const gsvcu_ctx* ctx) {
+    if (!ctx) return GSVCU_ERR_ARG;
+    int64_t t = ctx->tokens_done;
+    for (int sl = 0; sl < (int)ctx->slot_used.size(); sl++)
+        if (ctx->slot_used[sl]) t += ctx->h_st[sl].n_samp;
+    return t;
+}
+
+// ------------------------------------------------------------------ kernel-level entry points
+int gsvcu_op_quantize_q8_0(gsvcu_ctx* ctx, const float* x_dev, int32_t rows, int32_t K, int8_t* q_dev, uint16_t* d_dev) {
+    if (!ctx || !x_dev || !q_dev || !d_dev || rows < 0 || K <= 0 || K % QK) return GSVCU_ERR_ARG;
+    DeviceGuard g(ctx->device);
+    launch_quantize_q8(x_dev, rows, K, q_dev, d_dev, ctx->stream);
+    CKC(ctx, cudaGetLastError());
+    return GSVCU_OK;
+}
+
+int gsvcu_op_pack_q8_0(gsvcu_ctx* ctx, const uint8_t* raw_host, int32_t N, int32_t K, void* wq_dev, void* wd_dev) {
+    if (!ctx || !raw_host || !wq_dev || !wd_dev || N <= 0 || K <= 0 || N % 32 || K % QK) return GSVCU_ERR_ARG;
+    DeviceGuard g(ctx->device);
+    std::vector<uint8_t> wq((size_t)N * K);
+    std::vector<uint16_t> wd((size_t)N * K / QK);
+    pack_q8_0_host(raw_host, N, K, wq.data(), wd.data());
+    CKC(ctx, cudaMemcpy(wq_dev, wq.data(), wq.size(), cudaMemcpyHostToDevice));
+    CKC(ctx, cudaMemcpy(wd_dev, wd.data(), wd.size() * 2, cudaMemcpyHostToDevice));
+    return GSVCU_OK;
+}
+
+int gsvcu_op_q8_gemm(gsvcu_ctx* ctx, const int8_t* xq_dev, const uint16_t* xd_dev, int32_t M, const void* wq_dev,
+                     const void* wd_dev, int32_t N, int32_t K, const float* bias_dev, const float* resid_dev, int32_t epi,
+                     float* y_dev, int8_t* yq_dev, uint16_t* yd_dev) {
+    if (!ctx || !xq_dev || !xd_dev || !wq_dev || !wd_dev || M <= 0 || N <= 0 || N % 32 || (K != 512 && K != 2048))
+        return GSVCU_ERR_ARG;
+    if (epi < 0 || epi > 2 || (epi < 2 && !y_dev) || (epi == 1 && !resid_dev) || (epi == 2 && (!yq_dev || !yd_dev)))
+        return GSVCU_ERR_ARG;
+    DeviceGuard g(ctx->device);
+    GemmQ8Params p;
+    p.xq = xq_dev; p.xd = xd_dev; p.M = M; p.wq = (const uint4*)wq_dev; p.wd = (const uint16_t*)wd_dev; p.N = N; p.K = K;
+    p.bias = bias_dev; p.resid = resid_dev; p.y = y_dev; p.yq = yq_dev; p.yd = yd_dev;
+    launch_gemm_q8(p, epi, ctx->stream);
+    CKC(ctx, cudaGetLastError());
+    return GSVCU_OK;
+}
+
+int gsvcu_op_layernorm_q8(gsvcu_ctx* ctx, const float* v_dev, int32_t rows, const float* w_dev, const float* b_dev,
+                          float* y_dev, int8_t* yq_dev, uint16_t* yd_dev) {
+    if (!ctx || !v_dev || !w_dev || !b_dev || !y_dev || !yq_dev || !yd_dev || rows < 0) return GSVCU_ERR_ARG;
+    DeviceGuard g(ctx->device);
+    launch_layernorm_q8(v_dev, rows, w_dev, b_dev, y_dev, yq_dev, yd_dev, ctx->stream);
+    CKC(ctx, cudaGetLastError());
+    return GSVCU_OK;
+}
+
+int gsvcu_op_f32_gemm(gsvcu_ctx* ctx, const float* x_dev, int32_t M, const float* w_dev, int32_t N, int32_t K,
+                      const float* add_dev, float* y_dev) {
+    if (!ctx || !x_dev || !w_dev || !y_dev || M < 0 || N <= 0 || K <= 0) return GSVCU_ERR_ARG;
+    DeviceGuard g(ctx->device);
+    launch_gemm_f32d(x_dev, K, nullptr, M, w_dev, N, K, add_dev, N, y_dev, N, ctx->stream);
+    CKC(ctx, cudaGetLastError());
+    return GSVCU_OK;
+}
+
+int gsvcu_op_decode_attention(gsvcu_ctx* ctx, const float* q_dev, int32_t q_stride, const void* pool_dev,
+                              int32_t kv_dtype, int32_t n_layer, int32_t layer, const int32_t* block_table_dev,
+                              int32_t max_pages, const int32_t* kvpos_dev, const int32_t* active_dev, int32_t B,
+                              int8_t* out_q_dev, uint16_t* out_d_dev, float* out_f32_dev) {
+    if (!ctx || !q_dev || !pool_dev || !block_table_dev || !kvpos_dev || !active_dev || !out_q_dev || !out_d_dev ||
+        B <= 0 || max_pages <= 0 || n_layer <= 0 || layer < 0 || layer >= n_layer || q_stride < D ||
+        (kv_dtype != GSVCU_KV_F16 && kv_dtype != GSVCU_KV_F32))
+        return GSVCU_ERR_ARG;
+    DeviceGuard g(ctx->device);
+    const int max_chunks = (max_pages * PAGE + ATT_CHUNK - 1) / ATT_CHUNK;
+    const size_t need_part = (size_t)B * NH * max_chunks * (2 + HD);
+    const size_t need_cnt = (size_t)B * NH;
+    if (need_part > ctx->op_part_n) {
+        if (ctx->op_part) {
+            cudaStreamSynchronize(ctx->stream);
+            cudaFree(ctx->op_part);
+        }
+        ctx->op_part = nullptr;
+        ctx->op_part_n = 0;
+        CKC(ctx, cudaMalloc((void**)&ctx->op_part, need_part * 4));
+        ctx->op_part_n = need_part;
+    }
+    if (need_cnt > ctx->op_counter_n) {
+        if (ctx->op_counter) {
+            cudaStreamSynchronize(ctx->stream);
+            cudaFree(ctx->op_counter);
+        }
+        ctx->op_counter = nullptr;
+        ctx->op_counter_n = 0;
+        CKC(ctx, cudaMalloc((void**)&ctx->op_counter, need_cnt * 4));
+        CKC(ctx, cudaMemsetAsync(ctx->op_counter, 0, need_cnt * 4, ctx->stream));
+        ctx->op_counter_n = need_cnt;
+    }
+    DecAttnParams a;
+    a.q = q_dev; a.q_stride = q_stride; a.pool = pool_dev; a.kv_f32 = kv_dtype; a.n_layer = n_layer; a.layer = layer;
+    a.block_table = block_table_dev; a.max_pages = max_pages; a.kvpos = kvpos_dev; a.active = active_dev; a.B = B;
+    a.max_chunks = max_chunks; a.scale = 1.0f / std::sqrt((float)HD); a.out_q = out_q_dev; a.out_d = out_d_dev;
+    a.out_f32 = out_f32_dev; a.part = ctx->op_part; a.counter = ctx->op_counter;
+    launch_decode_attention(a, ctx->stream);
+    CKC(ctx, cudaGetLastError());
+    return GSVCU_OK;
+}
+
+int gsvcu_op_prefill_attention(gsvcu_ctx* ctx, const float* qkv_dev, int32_t n_seq, const int32_t* seq_start,
+                               const int32_t* seq_len, const int32_t* text_len, int8_t* out_q_dev, uint16_t* out_d_dev,
+                               float* out_f32_dev) {
+    if (!ctx || !qkv_dev || n_seq <= 0 || !seq_start || !seq_len || !text_len || !out_q_dev || !out_d_dev)
+        return GSVCU_ERR_ARG;
+    DeviceGuard g(ctx->device);
+    std::vector<PrefillTile> tiles;
+    for (int i = 0; i < n_seq; i++) {
+        if (seq_len[i] <= 0 || text_len[i] < 0 || text_len[i] > seq_len[i]) return GSVCU_ERR_ARG;
+        for (int q0 = 0; q0 < seq_len[i]; q0 += PREF_QTILE) tiles.push_back({i, q0});
+    }
+    std::vector<int32_t> tab((size_t)3 * n_seq);
+    std::memcpy(tab.data(), seq_start, (size_t)n_seq * 4);
+    std::memcpy(tab.data() + n_seq, seq_len, (size_t)n_seq * 4);
+    std::memcpy(tab.data() + 2 * n_seq, text_len, (size_t)n_seq * 4);
+    const size_t tab_bytes = ((size_t)n_seq * 12 + 15) / 16 * 16;
+    uint8_t* blk = nullptr;
+    CKC(ctx, cudaMalloc((void**)&blk, tab_bytes + tiles.size() * sizeof(PrefillTile)));
+    cudaMemcpyAsync(blk, tab.data(), (size_t)n_seq * 12, cudaMemcpyHostToDevice, ctx->stream);
+    cudaMemcpyAsync(blk + tab_bytes, tiles.data(), tiles.size() * sizeof(PrefillTile), cudaMemcpyHostToDevice,
+                    ctx->stream);
+    PrefAttnParams a;
+    a.qkv = qkv_dev;
+    a.seq_start = (const int32_t*)blk;
+    a.seq_len = a.seq_start + n_seq;
+    a.text_len = a.seq_len + n_seq;
+    a.tiles = (const PrefillTile*)(blk + tab_bytes);
+    a.n_tiles = (int)tiles.size();
+    a.scale = 1.0f / std::sqrt((float)HD);
+    a.out_q = out_q_dev; a.out_d = out_d_dev; a.out_f32 = out_f32_dev;
+    launch_prefill_attention(a, ctx->stream);
+    cudaError_t e = cudaStreamSynchronize(ctx->stream);
+    cudaFree(blk);
+    if (e != cudaSuccess) return ctx->fail(GSVCU_ERR_CUDA, cudaGetErrorString(e));
+    return GSVCU_OK;
+}
+
+int gsvcu_op_sample(gsvcu_ctx* ctx, const float* logits_dev, int32_t B, int32_t V, int32_t eos,
+                    const gsvcu_sampler_cfg* cfg, const int32_t* prev_host, const int32_t* n_prev_host,
+                    int32_t prev_stride, const int32_t* step_host, uint64_t* rng_host, int32_t* tokens_host) {
+    if (!ctx || !logits_dev || B <= 0 || V < 2 || V > 1280 || eos < 0 || eos >= V || !cfg || !step_host || !rng_host ||
+        !tokens_host || (prev_host && (!n_prev_host || prev_stride <= 0)))
+        return GSVCU_ERR_ARG;
+    DeviceGuard g(ctx->device);
+    int cap = 1;
+    for (int b = 0; b < B; b++) {
+        if (step_host[b] < 0) return GSVCU_ERR_ARG;
+        cap = std::max(cap, step_host[b] + 1);
+    }
+    const int dpl = (V + 31) / 32;
+    std::vector<uint64_t> jm = jump_matrices(dpl);
+    std::vector<SlotState> hs(B);
+    std::vector<uint16_t> cnt((size_t)B * V, 0);
+    std::vector<int32_t> ring((size_t)B * HIST, 0);
+    for (int b = 0; b < B; b++) {
+        SlotState& ss = hs[b];
+        ss = SlotState{};
+        ss.active = 1;
+        ss.n_samp = step_host[b];
+        ss.max_steps = cap + 1;
+        ss.early_stop = -1;
+        ss.group_first = b;
+        ss.finish_kind = -1;
+        ss.rng = rng_host[b];
+        const int np = prev_host ? n_prev_host[b] : 0;
+        if (np < 0 || np > prev_stride * (prev_host != nullptr)) return GSVCU_ERR_ARG;
+        const int nh = std::min(np, HIST);
+        for (int i = 0; i < nh; i++) {
+            const int t = prev_host[(size_t)b * prev_stride + (np - nh) + i];
+            ring[(size_t)b * HIST + i] = t;
+            if (t >= 0 && t < V) cnt[(size_t)b * V + t]++;
+        }
+        ss.hist_len = nh;
+    }
+    // one device block: states | counts | ring | tokens | jump
+    const size_t o_st = 0, o_cnt = o_st + sizeof(SlotState) * B, o_ring = (o_cnt + (size_t)B * V * 2 + 15) / 16 * 16,
+                 o_tok = o_ring + (size_t)B * HIST * 4, o_jump = (o_tok + (size_t)B * cap * 4 + 15) / 16 * 16,
+                 total = o_jump + jm.size() * 8;
+    uint8_t* blk = nullptr;
+    CKC(ctx, cudaMalloc((void**)&blk, total));
+    cudaStream_t s = ctx->stream;
+    cudaMemcpyAsync(blk + o_st, hs.data(), sizeof(SlotState) * B, cudaMemcpyHostToDevice, s);
+    cudaMemcpyAsync(blk + o_cnt, cnt.data(), cnt.size() * 2, cudaMemcpyHostToDevice, s);
+    cudaMemcpyAsync(blk + o_ring, ring.data(), ring.size() * 4, cudaMemcpyHostToDevice, s);
+    cudaMemcpyAsync(blk + o_jump, jm.data(), jm.size() * 8, cudaMemcpyHostToDevice, s);
+    SamplerParams sp;
+    sp.logits = logits_dev; sp.V = V; sp.eos = eos; sp.nslots = B;
+    sp.top_k = cfg->top_k; sp.top_p = cfg->top_p; sp.temperature = cfg->temperature; sp.rep = cfg->repetition_penalty;
+    sp.st = (SlotState*)(blk + o_st); sp.counts = (uint16_t*)(blk + o_cnt); sp.hist = (int32_t*)(blk + o_ring);
+    sp.out_tokens = (int32_t*)(blk + o_tok); sp.tok_cap = cap; sp.jump = (const uint64_t*)(blk + o_jump);
+    sp.draws_per_lane = dpl;
+    launch_sampler(sp, s);
+    cudaMemcpyAsync(hs.data(), blk + o_st, sizeof(SlotState) * B, cudaMemcpyDeviceToHost, s);
+    std::vector<int32_t> toks((size_t)B * cap);
+    cudaMemcpyAsync(toks.data(), blk + o_tok, toks.size() * 4, cudaMemcpyDeviceToHost, s);
+    cudaError_t e = cudaStreamSynchronize(s);
+    cudaFree(blk);
+    if (e != cudaSuccess) return ctx->fail(GSVCU_ERR_CUDA, cudaGetErrorString(e));
+    for (int b = 0; b < B; b++) {
+        tokens_host[b] = toks[(size_t)b * cap + step_host[b]];
+        rng_host[b] = hs[b].rng;
+    }
+    return GSVCU_OK;
+}
+
+int gsvcu_sync(gsvcu_ctx* ctx) {
+    if (!ctx) return GSVCU_ERR_ARG;
+    DeviceGuard g(ctx->device);
+    CKC(ctx, cudaStreamSynchronize(ctx->stream));
+    return GSVCU_OK;
+}
+
+}  // extern "C"

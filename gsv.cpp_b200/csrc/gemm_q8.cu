@@ -1,0 +1,265 @@
+// gemm_q8.cu -- Q8_0 x Q8_0 GEMM on the tensor cores (mma.m16n8k32 s8 -> s32) with fused epilogues.
+//
+// Semantics (ggml Q8_0 mul_mat, as used at reference src/gsv_ar.cpp:244,260,262,263): per output
+// (n, m) the integer dot of every 32-element block is exact (int32 MMA with a zero accumulator is
+// one Q8_0 block), and the float result is accumulated block by block, in block order:
+//     acc = fma((float)isum_b, d_w[n][b] * d_x[m][b], acc).
+// So the output is bit-identical to the oracle's restatement.
+//
+// Tiling. A CTA owns 32 output features x 8T tokens. Its activation rows and scales are staged in
+// shared memory; KS warps split every chunk of 4*KS K-blocks (each warp 4 blocks), write the exact
+// int32 block sums into shared memory, and after a barrier every thread runs the sequential float
+// chain for its outputs. Weights stream from HBM once per token tile with 128-bit non-allocating
+// loads in fragment order, prefetched one chunk ahead.
+#include <cstring>
+
+#include "kernels.h"
+
+namespace gsvcu {
+
+__device__ __forceinline__ void mma_s8(int (&c)[4], const uint4& a, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%11,%12,%13};\n"
+        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+        : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+constexpr int SSTR = 33;   // row stride (words) of the int32 block-sum tile
+
+__host__ __device__ constexpr size_t gemm_smem_bytes(int T, int KS, int K) {
+    return (size_t)(8 * T) * (K + 16)                  // Xs
+           + (size_t)(8 * T) * (K / 32) * 2            // Xds
+           + (size_t)(K / 32) * 32 * 2                 // Wds
+           + 16                                        // alignment slack
+           + (size_t)(4 * KS) * (8 * T) * SSTR * 4;    // S
+}
+
+template <int T, int KS, int EPI>
+__global__ void __launch_bounds__(32 * KS) k_gemm_q8(const GemmQ8Params p) {
+    constexpr int TOK = 8 * T;
+    constexpr int NT = 32 * KS;                 // threads
+    constexpr int KC = 4 * KS;                  // K-blocks per chunk
+    constexpr int NOUT = (TOK * 32 + NT - 1) / NT;
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int K = p.K, KB = K / QK;
+    const int XSTR = K + 16;
+    int8_t* Xs = (int8_t*)smem;
+    uint16_t* Xds = (uint16_t*)(smem + (size_t)TOK * XSTR);    // [TOK][KB]
+    uint16_t* Wds = Xds + TOK * KB;                             // [KB][32]
+    int32_t* S = (int32_t*)(((uintptr_t)(Wds + KB * 32) + 15) & ~(uintptr_t)15);   // [KC][TOK][SSTR]
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, t4 = lane & 3;
+    const int f0 = blockIdx.x * 32, tok0 = blockIdx.y * TOK;
+
+    // weight fragments of this warp for chunk c: kb = c*KC + warp*4 + i
+    const uint4* w0 = p.wq + (size_t)(2 * blockIdx.x + 0) * KB * 32 + lane;
+    const uint4* w1 = p.wq + (size_t)(2 * blockIdx.x + 1) * KB * 32 + lane;
+    uint4 fa[4], fb[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int kb = warp * 4 + i;
+        fa[i] = ldg_stream(w0 + (size_t)kb * 32);
+        fb[i] = ldg_stream(w1 + (size_t)kb * 32);
+    }
+
+    // stage activations, their scales and the weight scales
+    const int vpr = K / 16;
+    for (int i = tid; i < TOK * vpr; i += NT) {
+        const int r = i / vpr, c = i - r * vpr;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (tok0 + r < p.M) v = *(const uint4*)(p.xq + (size_t)(tok0 + r) * K + c * 16);
+        *(uint4*)(Xs + (size_t)r * XSTR + c * 16) = v;
+    }
+    for (int i = tid; i < TOK * KB; i += NT) {
+        const int r = i / KB;
+        Xds[i] = tok0 + r < p.M ? p.xd[(size_t)(tok0 + r) * KB + (i - r * KB)] : (uint16_t)0;
+    }
+    for (int i = tid; i < 32 * KB; i += NT) {
+        const int kb = i >> 5, f = i & 31;
+        Wds[i] = p.wd[(size_t)(f0 + f) * KB + kb];
+    }
+    __syncthreads();
+
+    float acc[NOUT];
+#pragma unroll
+    for (int q = 0; q < NOUT; q++) acc[q] = 0.0f;
+
+    const int nchunks = KB / KC;
+    for (int c = 0; c < nchunks; c++) {
+        uint4 ca[4], cb[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) { ca[i] = fa[i]; cb[i] = fb[i]; }
+        if (c + 1 < nchunks) {
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int kb = (c + 1) * KC + warp * 4 + i;
+                fa[i] = ldg_stream(w0 + (size_t)kb * 32);
+                fb[i] = ldg_stream(w1 + (size_t)kb * 32);
+            }
+        }
+        // phase 1: exact int32 block sums -> S[kbl][n][f]
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int kbl = warp * 4 + i, kb = c * KC + kbl;
+            int32_t* s = S + (size_t)kbl * TOK * SSTR;
+#pragma unroll
+            for (int j = 0; j < T; j++) {
+                const int8_t* xr = Xs + (size_t)(j * 8 + g) * XSTR + kb * 32 + t4 * 4;
+                const uint32_t b0 = *(const uint32_t*)xr, b1 = *(const uint32_t*)(xr + 16);
+                int c0[4], c1[4];
+                mma_s8(c0, ca[i], b0, b1);
+                mma_s8(c1, cb[i], b0, b1);
+                const int n0 = j * 8 + 2 * t4;
+                s[n0 * SSTR + g] = c0[0];
+                s[(n0 + 1) * SSTR + g] = c0[1];
+                s[n0 * SSTR + g + 8] = c0[2];
+                s[(n0 + 1) * SSTR + g + 8] = c0[3];
+                s[n0 * SSTR + g + 16] = c1[0];
+                s[(n0 + 1) * SSTR + g + 16] = c1[1];
+                s[n0 * SSTR + g + 24] = c1[2];
+                s[(n0 + 1) * SSTR + g + 24] = c1[3];
+            }
+        }
+        __syncthreads();
+        // phase 2: sequential float chain over the chunk's blocks, block order
+#pragma unroll
+        for (int q = 0; q < NOUT; q++) {
+            const int o = tid + q * NT;
+            if (o < TOK * 32) {
+                const int n = o >> 5, f = o & 31;
+                float a = acc[q];
+#pragma unroll 4
+                for (int kbl = 0; kbl < KC; kbl++) {
+                    const int kb = c * KC + kbl;
+                    const float dw = h2f(Wds[kb * 32 + f]);
+                    const float dx = h2f(Xds[n * KB + kb]);
+                    const int32_t si = S[((size_t)kbl * TOK + n) * SSTR + f];
+                    a = fmaf((float)si, __fmul_rn(dw, dx), a);
+                }
+                acc[q] = a;
+            }
+        }
+        __syncthreads();
+    }
+
+    // epilogue: thread q-th output (n = o/32, f = o%32); a warp holds 32 consecutive features of one row
+#pragma unroll
+    for (int q = 0; q < NOUT; q++) {
+        const int o = tid + q * NT;
+        if (o >= TOK * 32) continue;   // warp-uniform (TOK*32 is a multiple of 32)
+        const int nl = o >> 5, f = f0 + (o & 31), n = tok0 + nl;
+        const bool valid = n < p.M;
+        const float bias = p.bias ? p.bias[f] : 0.0f;
+        if (EPI == EPI_BIAS) {
+            const float y = __fadd_rn(acc[q], bias);
+            if (valid) p.y[(size_t)n * p.N + f] = y;
+            if (valid && p.kv.pool && f >= D) {
+                int slot, pos;
+                bool ok = true;
+                if (p.kv.tok_pos) {
+                    slot = p.kv.tok_slot[n];
+                    pos = p.kv.tok_pos[n];
+                } else {
+                    slot = n;
+                    ok = p.kv.st[n].decode_now != 0;
+                    pos = p.kv.st[n].kvpos;
+                }
+                if (ok) {
+                    const int kvsel = (f - D) >> 9, fh = (f - D) & (D - 1);
+                    const int h = fh >> 5, dd = fh & 31;
+                    const int page = p.kv.block_table[(size_t)slot * p.kv.max_pages + pos / PAGE];
+                    const size_t e = ((((size_t)page * p.kv.n_layer + p.kv.layer) * 2 + kvsel) * NH + h) * (PAGE * HD) +
+                                     (size_t)(pos % PAGE) * HD + dd;
+                    if (p.kv.kv_f32) ((float*)p.kv.pool)[e] = y;
+                    else ((__half*)p.kv.pool)[e] = __float2half_rn(y);
+                }
+            }
+        } else if (EPI == EPI_RESID) {
+            if (valid) {
+                const float r = p.resid[(size_t)n * p.N + f];
+                p.y[(size_t)n * p.N + f] = __fadd_rn(__fadd_rn(r, acc[q]), bias);
+            }
+        } else {   // EPI_RELU_Q8: relu(acc + bias), one Q8_0 block per row across the warp
+            float h = __fadd_rn(acc[q], bias);
+            h = h > 0.0f ? h : 0.0f;
+            float amax = fabsf(h);
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+            float dsc, id;
+            q8_scale(amax, dsc, id);
+            if (valid) {
+                p.yq[(size_t)n * p.N + f] = q8_val(h, id);
+                if ((o & 31) == 0) p.yd[(size_t)n * (p.N / QK) + f / QK] = f2h(dsc);
+            }
+        }
+    }
+}
+
+template <int T, int KS>
+static void launch_t(const GemmQ8Params& p, int epi, cudaStream_t s) {
+    const size_t smem = gemm_smem_bytes(T, KS, p.K);
+    dim3 grid(p.N / 32, (p.M + 8 * T - 1) / (8 * T));
+    dim3 block(32 * KS);
+    switch (epi) {
+        case EPI_BIAS: k_gemm_q8<T, KS, EPI_BIAS><<<grid, block, smem, s>>>(p); break;
+        case EPI_RESID: k_gemm_q8<T, KS, EPI_RESID><<<grid, block, smem, s>>>(p); break;
+        default: k_gemm_q8<T, KS, EPI_RELU_Q8><<<grid, block, smem, s>>>(p); break;
+    }
+}
+
+template <int T, int KS>
+static cudaError_t init_t(int K) {
+    const int smem = (int)gemm_smem_bytes(T, KS, K);
+    cudaError_t e;
+    if ((e = cudaFuncSetAttribute(k_gemm_q8<T, KS, EPI_BIAS>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem))) return e;
+    if ((e = cudaFuncSetAttribute(k_gemm_q8<T, KS, EPI_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem))) return e;
+    return cudaFuncSetAttribute(k_gemm_q8<T, KS, EPI_RELU_Q8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+}
+
+cudaError_t gemm_q8_init_device() {
+    cudaError_t e;
+    if ((e = init_t<1, 4>(512))) return e;
+    if ((e = init_t<1, 8>(2048))) return e;
+    return init_t<4, 4>(2048);
+}
+
+void launch_gemm_q8(const GemmQ8Params& p, int epi, cudaStream_t s) {
+    // K = 512 -> KS 4 (one chunk of 16 blocks); K = 2048 -> KS 8 at small M (two chunks of 32)
+    const int KB = p.K / QK;
+    if (p.M <= 64) {
+        if (KB % 32 == 0) launch_t<1, 8>(p, epi, s);
+        else launch_t<1, 4>(p, epi, s);
+    } else {
+        launch_t<4, 4>(p, epi, s);
+    }
+}
+
+void pack_q8_0_host(const uint8_t* raw, int N, int K, uint8_t* wq_out, uint16_t* wd_out) {
+    const int KB = K / QK;
+    for (int n = 0; n < N; n++)
+        for (int kb = 0; kb < KB; kb++) {
+            uint16_t d;
+            std::memcpy(&d, raw + ((size_t)n * KB + kb) * 34, 2);
+            wd_out[(size_t)n * KB + kb] = d;
+        }
+    // fragment order of the mma.m16n8k32 A operand: lane l = 4g + t holds
+    //   a0: row g,   cols 4t..4t+3     a1: row g+8, cols 4t..4t+3
+    //   a2: row g,   cols 16+4t..      a3: row g+8, cols 16+4t..
+    for (int rg = 0; rg < N / 16; rg++)
+        for (int kb = 0; kb < KB; kb++) {
+            uint8_t* dst = wq_out + (((size_t)rg * KB + kb) * 32) * 16;
+            for (int lane = 0; lane < 32; lane++) {
+                const int g = lane >> 2, t = lane & 3;
+                for (int reg = 0; reg < 4; reg++) {
+                    const int row = rg * 16 + g + ((reg & 1) ? 8 : 0);
+                    const int col = t * 4 + ((reg & 2) ? 16 : 0);
+                    const uint8_t* src = raw + ((size_t)row * KB + kb) * 34 + 2 + col;
+                    std::memcpy(dst + lane * 16 + reg * 4, src, 4);
+                }
+            }
+        }
+}
+
+}  // namespace gsvcu

@@ -1,0 +1,160 @@
+// kernels.h -- host-side launchers of the gsvcu kernels (internal to the library).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace gsvcu {
+
+// ------------------------------------------------------------ Q8_0 GEMM
+// Activation planes: xq int8 [M][K] row-major, xd fp16 [M][K/32].
+// Weight planes: wq = fragment order [N/16][K/32][32 lanes][16 B] (mma.m16n8k32 A operand),
+//                wd = fp16 [N][K/32].
+enum { EPI_BIAS = 0, EPI_RESID = 1, EPI_RELU_Q8 = 2 };
+
+struct KvWrite {             // optional store of K/V columns (features [D, 3D)) into KV pages
+    void* pool = nullptr;    // [page][n_layer][2][NH][PAGE][HD] elements
+    int kv_f32 = 0;
+    int n_layer = 0, layer = 0;
+    const int32_t* block_table = nullptr;   // [slot][max_pages]
+    int max_pages = 0;
+    const int32_t* tok_slot = nullptr;      // prefill: slot of each row
+    const int32_t* tok_pos = nullptr;       // prefill: position of each row (nullptr = decode)
+    const SlotState* st = nullptr;          // decode: row = slot, pos = st.kvpos, only if decode_now
+};
+
+struct GemmQ8Params {
+    const int8_t* xq = nullptr;
+    const uint16_t* xd = nullptr;
+    int M = 0;
+    const uint4* wq = nullptr;
+    const uint16_t* wd = nullptr;
+    int N = 0, K = 0;
+    const float* bias = nullptr;
+    const float* resid = nullptr;   // [M][N]
+    float* y = nullptr;             // [M][N]
+    int8_t* yq = nullptr;           // [M][N]   (EPI_RELU_Q8)
+    uint16_t* yd = nullptr;         // [M][N/32]
+    KvWrite kv;
+};
+
+void launch_gemm_q8(const GemmQ8Params& p, int epi, cudaStream_t s);
+// Raise the dynamic shared-memory limit of every GEMM instantiation on the current device.
+cudaError_t gemm_q8_init_device();
+
+// Host-side repack of raw GGUF Q8_0 blocks [N][K/32] x 34 B into the two planes.
+void pack_q8_0_host(const uint8_t* raw, int N, int K, uint8_t* wq_out, uint16_t* wd_out);
+
+// ------------------------------------------------------------ F32 GEMM, double accumulation
+// y[m][n] = (float) sum_k (double)(w[n][k] * x(m, k))  (+ add[m][n]); x(m,k) = x[m*ldx + k], or,
+// for the BERT projection, gathered from per-sequence [1024][T] feature blocks with an implicit
+// trailing 1 (see F32Gather).
+struct F32Gather {          // x(m, k): k < bert_dim -> feat[row_off + k*T], k == bert_dim -> 1; row_T < 0 -> 0
+    const float* feat = nullptr;      // concatenated per-sequence [bert_dim][T_s] blocks
+    const int64_t* row_off = nullptr; // [M] offset of feat[0*T + t] for row m
+    const int32_t* row_T = nullptr;   // [M] T of the row's sequence, -1 for rows without features
+    int bert_dim = 0;
+};
+void launch_gemm_f32d(const float* x, int ldx, const F32Gather* gather, int M, const float* w, int N, int K,
+                      const float* add, int ldadd, float* y, int ldy, cudaStream_t s);
+
+// ------------------------------------------------------------ LayerNorm + Q8_0, quantize
+void launch_layernorm_q8(const float* v, int rows, const float* w, const float* b, float* y, int8_t* yq,
+                         uint16_t* yd, cudaStream_t s);
+void launch_quantize_q8(const float* x, int rows, int K, int8_t* q, uint16_t* d, cudaStream_t s);
+
+// ------------------------------------------------------------ attention
+struct DecAttnParams {
+    const float* q = nullptr;
+    int q_stride = 0;
+    const void* pool = nullptr;
+    int kv_f32 = 0;
+    int n_layer = 0, layer = 0;
+    const int32_t* block_table = nullptr;
+    int max_pages = 0;
+    const int32_t* kvpos = nullptr;      // op entry: plain arrays
+    const int32_t* active = nullptr;
+    const SlotState* st = nullptr;       // engine: slot state (kvpos, decode_now)
+    int B = 0;
+    int max_chunks = 0;
+    float scale = 0.f;
+    int8_t* out_q = nullptr;
+    uint16_t* out_d = nullptr;
+    float* out_f32 = nullptr;
+    float* part = nullptr;               // scratch [B][NH][max_chunks][2 + HD]
+    int32_t* counter = nullptr;          // scratch [B][NH], zero between launches
+};
+void launch_decode_attention(const DecAttnParams& p, cudaStream_t s);
+
+struct PrefillTile { int32_t seq, q0; };
+struct PrefAttnParams {
+    const float* qkv = nullptr;          // [M][3D]
+    const int32_t* seq_start = nullptr;  // device
+    const int32_t* seq_len = nullptr;
+    const int32_t* text_len = nullptr;
+    const PrefillTile* tiles = nullptr;  // device, n_tiles
+    int n_tiles = 0;
+    float scale = 0.f;
+    int8_t* out_q = nullptr;
+    uint16_t* out_d = nullptr;
+    float* out_f32 = nullptr;
+};
+constexpr int PREF_QTILE = 64;
+void launch_prefill_attention(const PrefAttnParams& p, cudaStream_t s);
+
+// ------------------------------------------------------------ embeddings
+// Prefill: row m -> text (phone id, PE t) or prompt (code, PE t); x = emb + alpha * pe (FMA).
+struct PrefEmbedParams {
+    const int32_t* ids = nullptr;        // [M]
+    const int32_t* pe_pos = nullptr;     // [M]
+    const int32_t* is_text = nullptr;    // [M]
+    const float* text_emb = nullptr;
+    const float* audio_emb = nullptr;
+    const float* pe = nullptr;
+    float text_alpha = 1.f, audio_alpha = 1.f;
+    int M = 0;
+    float* x = nullptr;                  // [M][D]
+};
+void launch_prefill_embed(const PrefEmbedParams& p, cudaStream_t s);
+
+// ------------------------------------------------------------ sampler and step control
+struct SamplerParams {
+    const float* logits = nullptr;       // [nslots][V]
+    int V = 0, eos = 0, nslots = 0;
+    int top_k = 15;
+    float top_p = 1.f, temperature = 1.f, rep = 1.35f;
+    SlotState* st = nullptr;
+    uint16_t* counts = nullptr;          // [nslots][V]
+    int32_t* hist = nullptr;             // [nslots][HIST] ring of the repetition window
+    int32_t* out_tokens = nullptr;       // [nslots][tok_cap]
+    int tok_cap = 0;
+    const int32_t* forced = nullptr;     // [nslots][forced_cap] teacher-forced tokens
+    int forced_cap = 0;
+    const uint64_t* jump = nullptr;      // [32][64] xorshift jump matrices (columns)
+    int draws_per_lane = 0;
+};
+void launch_sampler(const SamplerParams& p, cudaStream_t s);
+
+// Group stop rules + next-token embedding (+ Q8_0) + KV position bump.
+struct StepPrepParams {
+    SlotState* st = nullptr;
+    int nslots = 0;
+    int eos = 0;
+    const int32_t* out_tokens = nullptr;
+    int tok_cap = 0;
+    const float* audio_emb = nullptr;
+    const float* pe = nullptr;
+    float audio_alpha = 1.f;
+    float* x = nullptr;                  // [nslots][D]
+    int8_t* xq = nullptr;
+    uint16_t* xd = nullptr;
+};
+void launch_step_prep(const StepPrepParams& p, cudaStream_t s);
+
+// dst[didx[r]] = src[sidx[r]] for rows of `width` floats (index arrays may be null = identity).
+void launch_copy_rows(float* dst, const int32_t* didx, const float* src, const int32_t* sidx, int nrows, int width,
+                      cudaStream_t s);
+
+}  // namespace gsvcu

@@ -1,0 +1,215 @@
+/* gsvcu.h -- C ABI of the B200 (sm_100a) library for gsv.cpp's AR semantic-token hot path.
+ *
+ * The reference path lives in gsv.cpp's src/gsv_ar.{h,cpp} (class gsv_ar) on top of ggml graphs.
+ * This library replaces its internals: a C++ host shim (gsv.cpp_b200/csrc/gsv_ar.cpp) implements
+ * the unchanged `class gsv_ar` API on these entry points, and any FFI (ctypes, cgo, JNI) can bind
+ * them directly. Plain C types only: pointers, sizes, status codes.
+ *
+ * Conventions
+ *   - Every function returns GSVCU_OK (0) or a negative GSVCU_ERR_* code; the message of the last
+ *     failure of a context is gsvcu_last_error(ctx). Nothing calls exit().
+ *   - A context owns one CUDA device and one stream; use it from one host thread at a time
+ *     (the reference serialises gsv_ar calls the same way, tools/svc_core.h:628,1312).
+ *   - "host" pointers are CPU memory; "dev" pointers are device memory on the context's device.
+ */
+#ifndef GSVCU_H
+#define GSVCU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    GSVCU_OK = 0,
+    GSVCU_ERR_ARG = -1,      /* invalid argument (null pointer, size or id out of range) */
+    GSVCU_ERR_CUDA = -2,     /* a CUDA call failed */
+    GSVCU_ERR_OOM = -3,      /* device memory or KV page pool exhausted */
+    GSVCU_ERR_IO = -4,       /* file could not be opened or read */
+    GSVCU_ERR_FORMAT = -5,   /* GGUF content is not a supported AR model */
+    GSVCU_ERR_STATE = -6,    /* call made in the wrong state (e.g. no model loaded) */
+    GSVCU_ERR_DEVICE = -7    /* device is not an sm_100 GPU or does not exist */
+};
+
+enum { GSVCU_KV_F16 = 0, GSVCU_KV_F32 = 1 };
+
+typedef struct gsvcu_ctx gsvcu_ctx;
+
+/* Model dimensions, as read from the GGUF KV pairs (reference src/gsv_ar.cpp:571-582). */
+typedef struct {
+    int32_t hidden_dim, n_head, head_dim, n_layer, vocab_size, phoneme_vocab_size, eos, bert_dim, ffn_dim;
+    float text_pe_alpha, audio_pe_alpha;
+} gsvcu_hparams;
+
+/* Sampler settings; same fields and defaults as gsv_sampler_cfg (reference src/gsv_sampler.h:18-23):
+ * top_k 15 (<=0 off), top_p 1.0 (>=1 off), temperature 1.0, repetition_penalty 1.35. */
+typedef struct {
+    int32_t top_k;
+    float top_p, temperature, repetition_penalty;
+} gsvcu_sampler_cfg;
+
+/* One sequence (gsv_ar_request, reference src/gsv_ar.h:13-17): phone ids, BERT features laid out
+ * [bert_dim][n_phones] (bert[k * n_phones + t]), reference prompt semantic codes. */
+typedef struct {
+    const int32_t* phones;
+    int32_t n_phones;
+    const float* bert;
+    const int32_t* prompt;
+    int32_t n_prompt;
+} gsvcu_request;
+
+/* Called after each block of decode steps with the number of steps completed so far; the C++ shim
+ * forwards it to gsvprog::tick() (reference src/gsv_ar.cpp:761-763). May be NULL. */
+typedef void (*gsvcu_progress_fn)(void* user, int32_t steps_done);
+
+/* ---------------------------------------------------------------- context and model */
+
+/* Open a context on CUDA device `device` (what gsv_device_parse selects, reference src/gsv_device.h:19-37). */
+int gsvcu_create(int device, gsvcu_ctx** out);
+void gsvcu_destroy(gsvcu_ctx* ctx);
+const char* gsvcu_last_error(const gsvcu_ctx* ctx);
+
+/* Load an AR GGUF file (replaces gsv_ar::load, reference src/gsv_ar.cpp:490-705): tensor names of
+ * tools/export_gguf/convert_ar.py:106-130; attention/FFN matrices must be Q8_0, embeddings,
+ * bert_proj, predict, norms and biases F32 (src/gsv_ar.cpp:632-637). Weights are repacked into
+ * tensor-core fragment order on the device. */
+int gsvcu_load_gguf(gsvcu_ctx* ctx, const char* path);
+int gsvcu_get_hparams(const gsvcu_ctx* ctx, gsvcu_hparams* out);
+
+/* Size the paged KV pool and the per-step buffers: up to `max_slots` sequences in flight, each
+ * with at most `max_ctx` tokens of context (prefix + generated), KV element type GSVCU_KV_F16 or
+ * GSVCU_KV_F32. Replaces alloc_cache (reference src/gsv_ar.cpp:94-118). Called implicitly with
+ * defaults by the calls below when needed. */
+int gsvcu_kv_reserve(gsvcu_ctx* ctx, int32_t max_slots, int32_t max_ctx, int32_t kv_dtype);
+/* Free the KV pool and per-step buffers (gsv_ar::release_cache, reference src/gsv_ar.cpp:826). */
+int gsvcu_release_cache(gsvcu_ctx* ctx);
+
+/* Parse and validate an AR GGUF file on the host only (no device): KV hyper-parameters and every
+ * tensor's name, shape and type, as gsvcu_load_gguf requires (reference src/gsv_ar.cpp:545-662).
+ * err (may be NULL) receives the reason of a failure. */
+int gsvcu_inspect_gguf(const char* path, gsvcu_hparams* out, char* err, int32_t err_cap);
+
+/* ---------------------------------------------------------------- reference-facing path */
+
+/* Prefill only; host logits_out [B][vocab] of each sequence's last position
+ * (gsv_ar::first_logits, reference src/gsv_ar.cpp:707-717). */
+int gsvcu_first_logits(gsvcu_ctx* ctx, const gsvcu_request* reqs, int32_t B, float* logits_out);
+
+/* Prefill + KV-cached decode + on-device sampling with the stop rules of gsv_ar::generate
+ * (reference src/gsv_ar.cpp:719-824): per-sequence seeds (seeds[b], or seed_base + 0x9E3779B9*b),
+ * EOS masked while step < 11, repetition window of the last 4096 tokens, optional teacher forcing
+ * (oracle_tokens, same token for every sequence), EOS finish, early stop keyed on sequence 0,
+ * max_steps. Outputs (host):
+ *   tokens_out [B][cap]   prompt + generated tokens, without the token that stopped the sequence
+ *   n_tokens_out [B]      number of valid entries per row (may exceed cap: then rows are truncated)
+ *   lens_out [B]          generated counts in the order the sequences finished (gsv_ar_result::lens) */
+int gsvcu_generate(gsvcu_ctx* ctx, const gsvcu_request* reqs, int32_t B, const gsvcu_sampler_cfg* sampler,
+                   uint64_t seed_base, int32_t early_stop_num, int32_t max_steps, const int32_t* oracle_tokens,
+                   int32_t n_oracle, const uint64_t* seeds, int32_t n_seeds, int32_t* tokens_out,
+                   int32_t* n_tokens_out, int32_t* lens_out, int32_t cap, gsvcu_progress_fn progress, void* user);
+
+/* Teacher-forced trace for parity checks (the reference's GSV_AR_PROB_DUMP / oracle_tokens
+ * diagnostics, src/gsv_ar.cpp:775-778): prefill, then decode `n_steps` forced tokens per sequence
+ * (forced [B][n_steps], host). logits_out [n_steps + 1][B][vocab] (row 0 = prefill). dump (may be
+ * NULL) [n_steps + 1][B][n_layer][4][hidden]: per layer, for the last position of the step, the
+ * attention output, LN1 output, (n1 + W2 h) + b2 and the layer output. */
+int gsvcu_debug_trace(gsvcu_ctx* ctx, const gsvcu_request* reqs, int32_t B, const int32_t* forced, int32_t n_steps,
+                      float* logits_out, float* dump);
+
+/* ---------------------------------------------------------------- continuous batching
+ * The batched entry behind gsv_engine::ar_generate_batch / svc::ArBatcher (reference
+ * tools/svc_core.h:1244-1340) generalised to refill: sequences are admitted into free slots while
+ * others decode. */
+
+typedef struct {
+    int32_t slot;          /* slot that ran the sequence */
+    int32_t tag;           /* caller tag given at admission */
+    int32_t finish_kind;   /* 0 EOS, 1 early stop, 2 max_steps */
+    int32_t n_generated;   /* generated tokens (gsv_ar_result::lens value) */
+    int32_t n_tokens;      /* tokens copied to the caller buffer (prompt excluded) */
+} gsvcu_finished;
+
+/* Admit sequences into free slots (prefill runs immediately). seeds[i] seeds sequence i; tags are
+ * returned with its completion. Fails with GSVCU_ERR_OOM if slots or KV pages are short. */
+int gsvcu_serve_admit(gsvcu_ctx* ctx, const gsvcu_request* reqs, int32_t n, const gsvcu_sampler_cfg* sampler,
+                      const uint64_t* seeds, const int32_t* tags, int32_t max_steps, int32_t early_stop_num);
+/* Run `n_steps` decode steps for every slot in flight, then report the sequences that finished:
+ * up to max_done records in done[], their generated tokens concatenated in tokens (host, capacity
+ * tok_cap; may be NULL). Returns the number of records (>= 0) or an error. */
+int gsvcu_serve_step(gsvcu_ctx* ctx, int32_t n_steps, gsvcu_finished* done, int32_t max_done, int32_t* tokens,
+                     int32_t tok_cap);
+/* Slots currently in flight. */
+int gsvcu_serve_active(const gsvcu_ctx* ctx);
+/* Generated tokens produced so far: finished sequences plus the tokens sampled so far by the
+ * sequences in flight (as of the last gsvcu_serve_step). */
+int64_t gsvcu_serve_tokens_total(const gsvcu_ctx* ctx);
+
+/* ---------------------------------------------------------------- kernel-level entry points
+ * Device pointers, the context's stream. Used by the parity tests and microbenchmarks. */
+
+/* Activation quantization to Q8_0 planes: x [rows][K] f32 -> q int8 [rows][K], d fp16 bits [rows][K/32]
+ * (ggml quantize_row_q8_0 semantics, the src1 conversion of the Q8_0 mul_mat at src/gsv_ar.cpp:244). */
+int gsvcu_op_quantize_q8_0(gsvcu_ctx* ctx, const float* x_dev, int32_t rows, int32_t K, int8_t* q_dev,
+                           uint16_t* d_dev);
+
+/* Repack raw GGUF Q8_0 blocks (host, [N][K/32] x 34 bytes) into device fragment planes. wq_dev needs
+ * N*K bytes, wd_dev N*K/32 fp16. N % 32 == 0, K % 32 == 0. (Weight upload of src/gsv_ar.cpp:549-570.) */
+int gsvcu_op_pack_q8_0(gsvcu_ctx* ctx, const uint8_t* raw_host, int32_t N, int32_t K, void* wq_dev, void* wd_dev);
+
+/* Y = W . X^T over Q8_0 planes (ggml Q8_0 mul_mat semantics, src/gsv_ar.cpp:244,260,262,263) with an epilogue:
+ *   epi 0: y = acc + bias                        (bias may be NULL)
+ *   epi 1: y = (resid + acc) + bias              (pre-LayerNorm sum, src/gsv_ar.cpp:261,264)
+ *   epi 2: y = relu(acc + bias) quantized to Q8_0 into yq_dev / yd_dev (src/gsv_ar.cpp:262)
+ * xq/xd: activation planes with M rows (row stride K). y_dev [M][N] f32 for epi 0/1. */
+int gsvcu_op_q8_gemm(gsvcu_ctx* ctx, const int8_t* xq_dev, const uint16_t* xd_dev, int32_t M, const void* wq_dev,
+                     const void* wd_dev, int32_t N, int32_t K, const float* bias_dev, const float* resid_dev,
+                     int32_t epi, float* y_dev, int8_t* yq_dev, uint16_t* yd_dev);
+
+/* Fused LayerNorm (layernorm_affine, P:1535-1585; ln_affine src/gsv_ar.cpp:157-165) over rows of 512
+ * already summed as (x + r) + bias, writing f32 and Q8_0 planes. */
+int gsvcu_op_layernorm_q8(gsvcu_ctx* ctx, const float* v_dev, int32_t rows, const float* w_dev, const float* b_dev,
+                          float* y_dev, int8_t* yq_dev, uint16_t* yd_dev);
+
+/* Y[M][N] = W[N][K] . X[M][K]^T in f32 with double accumulation (ggml F32 mul_mat, src/gsv_ar.cpp:241,266),
+ * optional add. */
+int gsvcu_op_f32_gemm(gsvcu_ctx* ctx, const float* x_dev, int32_t M, const float* w_dev, int32_t N, int32_t K,
+                      const float* add_dev, float* y_dev);
+
+/* Split-KV decode attention over a paged KV pool, 16 heads x 32 dims (flash_attn_ext over the cache,
+ * src/gsv_ar.cpp:402-405).
+ *   q_dev [B][q_stride] f32 (head h at h*32), pool_dev KV pages, block_table_dev [B][max_pages] int32,
+ *   kvpos_dev [B]: index of the newest key (keys 0..kvpos attend), active_dev [B] (0 = skip).
+ *   Page layout: [page][n_layer][K,V][16 heads][64 tokens][32] of kv_dtype elements.
+ *   Output: Q8_0 planes out_q [B][512], out_d [B][16]; out_f32 [B][512] optional (may be NULL).
+ * Partial results of the key chunks live in scratch memory owned by the context (grown on demand). */
+int gsvcu_op_decode_attention(gsvcu_ctx* ctx, const float* q_dev, int32_t q_stride, const void* pool_dev,
+                              int32_t kv_dtype, int32_t n_layer, int32_t layer, const int32_t* block_table_dev,
+                              int32_t max_pages, const int32_t* kvpos_dev, const int32_t* active_dev, int32_t B,
+                              int8_t* out_q_dev, uint16_t* out_d_dev, float* out_f32_dev);
+
+/* Prefix-masked prefill attention over packed sequences (src/gsv_ar.cpp:215-223, 257): qkv_dev
+ * [M][1536] rows (q|k|v), sequence s = rows [start_s, start_s + len_s) whose first text_len_s rows are
+ * text (bidirectional among text), the rest semantic (causal, full view of the text).
+ * seq_start/seq_len/text_len are host arrays of n_seq entries. */
+int gsvcu_op_prefill_attention(gsvcu_ctx* ctx, const float* qkv_dev, int32_t n_seq, const int32_t* seq_start,
+                               const int32_t* seq_len, const int32_t* text_len, int8_t* out_q_dev,
+                               uint16_t* out_d_dev, float* out_f32_dev);
+
+/* One sampling step per row (gsv_logits_to_probs + gsv_sample, reference src/gsv_sampler.cpp:8-89,
+ * with the step < 11 EOS mask of src/gsv_ar.cpp:768): logits_dev [B][V] f32; prev_host [B][prev_stride]
+ * repetition windows of n_prev_host[b] tokens (NULL = none); step_host [B] step index; rng_host [B]
+ * xorshift64* states, advanced in place; tokens_host [B] out. */
+int gsvcu_op_sample(gsvcu_ctx* ctx, const float* logits_dev, int32_t B, int32_t V, int32_t eos,
+                    const gsvcu_sampler_cfg* cfg, const int32_t* prev_host, const int32_t* n_prev_host,
+                    int32_t prev_stride, const int32_t* step_host, uint64_t* rng_host, int32_t* tokens_host);
+
+/* Synchronise the context's stream. */
+int gsvcu_sync(gsvcu_ctx* ctx);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GSVCU_H */

@@ -1,0 +1,87 @@
+"""The C ABI surface on the CPU: the library loads, exports every entry point the header declares,
+validates GGUF files on the host (corrupt files, wrong dtypes, missing tensors -> error codes, no
+crash), and refuses cleanly without an sm_100 GPU. No GPU work is launched here."""
+import ctypes as C
+import os
+import shutil
+
+import numpy as np
+import pytest
+
+import gsvcu
+
+HAVE_GPU = False
+try:
+    import torch
+    HAVE_GPU = torch.cuda.is_available()
+except Exception:
+    pass
+
+
+def test_every_declared_symbol_is_exported():
+    lib = gsvcu.load_library()
+    declared = gsvcu.declared_symbols()
+    assert len(declared) >= 20
+    for name in declared:
+        assert hasattr(lib, name), name
+        assert name in gsvcu.SIGNATURES, f"{name} has no ctypes signature"
+
+
+def test_inspect_valid_model(model_small):
+    rc, hp, msg = gsvcu.inspect_gguf(model_small)
+    assert rc == gsvcu.OK, msg
+    assert (hp.hidden_dim, hp.n_head, hp.n_layer, hp.vocab_size, hp.eos, hp.bert_dim) == (512, 16, 2, 1025, 1024, 1024)
+    assert hp.text_pe_alpha == 1.0 and hp.audio_pe_alpha == 1.0
+
+
+def test_inspect_rejects_bad_files(model_small, model_f32_small, tmp_path):
+    rc, _, msg = gsvcu.inspect_gguf(str(tmp_path / "missing.gguf"))
+    assert rc == -4 and "cannot open" in msg
+    data = open(model_small, "rb").read()
+    bad = tmp_path / "bad_magic.gguf"
+    bad.write_bytes(b"XXXX" + data[4:])
+    assert gsvcu.inspect_gguf(str(bad))[0] == -4
+    trunc = tmp_path / "trunc.gguf"
+    trunc.write_bytes(data[: len(data) // 2])
+    rc, _, msg = gsvcu.inspect_gguf(str(trunc))
+    assert rc == -4 and "out of file bounds" in msg
+    hdr = tmp_path / "hdr.gguf"
+    hdr.write_bytes(data[:40])
+    assert gsvcu.inspect_gguf(str(hdr))[0] == -4
+    # attention/FFN matrices must be Q8_0 (F32 matrices are a ggml option this build does not run)
+    rc, _, msg = gsvcu.inspect_gguf(model_f32_small)
+    assert rc == -5 and "expected 8" in msg
+
+
+def test_inspect_missing_tensor(tmp_path):
+    import gguf
+    w = gguf.GGUFWriter(str(tmp_path / "partial.gguf"), "gsv.ar")
+    w.add_uint32("ar.n_layer", 1)
+    w.add_tensor("ar.text_emb", np.zeros((732, 512), np.float32))
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    rc, _, msg = gsvcu.inspect_gguf(str(tmp_path / "partial.gguf"))
+    assert rc == -5 and "missing tensor" in msg
+
+
+@pytest.mark.skipif(HAVE_GPU, reason="checks the no-GPU refusal")
+def test_create_without_gpu_is_a_clean_error():
+    lib = gsvcu.load_library()
+    h = C.c_void_p()
+    assert lib.gsvcu_create(0, C.byref(h)) == -7
+    assert not h.value
+    with pytest.raises(gsvcu.GsvcuError):
+        gsvcu.Context(0)
+
+
+def test_null_arguments_are_rejected():
+    lib = gsvcu.load_library()
+    assert lib.gsvcu_create(0, None) == -1
+    assert lib.gsvcu_first_logits(None, None, 1, None) == -1
+    assert lib.gsvcu_generate(None, None, 1, None, 0, -1, 10, None, 0, None, 0, None, None, None, 0,
+                              gsvcu.PROGRESS_FN(), None) == -1
+    assert lib.gsvcu_serve_step(None, 1, None, 0, None, 0) == -1
+    assert lib.gsvcu_inspect_gguf(None, None, None, 0) == -1
+    assert lib.gsvcu_last_error(None) == b"null context"

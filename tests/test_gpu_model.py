@@ -1,0 +1,227 @@
+"""Model-level parity of the B200 path against the CPU oracle on identical GGUF weights and inputs.
+
+Bars: attention and layer outputs within 2e-3 relative L2, logits cosine
+>= 0.9999, greedy token streams identical for >= 95% of sequences over the first 200 steps (first
+divergence reported). The F16 KV cache of the B200 path is compared both with the oracle's F16-KV
+emulation (same rounding of stored K/V) and with the reference's F32 cache.
+"""
+import json
+import os
+import struct
+import subprocess
+
+import numpy as np
+import pytest
+
+import gsv_synth as S
+import oracle as O
+from conftest import cosine, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+REL_L2 = 2e-3
+COS = 0.9999
+
+
+@pytest.fixture(scope="module")
+def orc(model_full):
+    return O.OracleModel(model_full)
+
+
+@pytest.fixture(scope="module")
+def gctx(model_full):
+    import gsvcu
+    c = gsvcu.Context(0)
+    c.load(model_full)
+    yield c
+    c.close()
+
+
+def _reserve(gctx, kv, slots=16, ctx=1024):
+    gctx.release_cache()
+    gctx.kv_reserve(slots, ctx, kv)
+
+
+def test_hparams(gctx):
+    hp = gctx.hp
+    assert (hp.hidden_dim, hp.n_head, hp.n_layer, hp.vocab_size, hp.eos) == (512, 16, 24, 1025, 1024)
+
+
+def test_first_logits_parity(gctx, orc):
+    rng = np.random.default_rng(100)
+    reqs = [S.make_request(rng, 120, 40)] + S.ragged_requests(101, 3)   # config 0 prefix + ragged ones
+    _reserve(gctx, 1)
+    got = gctx.first_logits(reqs)
+    ref = orc.first_logits(reqs)
+    for b in range(len(reqs)):
+        c, r = cosine(got[b], ref[b]), rel_l2(got[b], ref[b])
+        print(f"seq {b}: cosine {c:.9f} rel-L2 {r:.3e}")
+        assert c >= COS and r <= REL_L2
+
+
+@pytest.mark.parametrize("kv", [1, 0])
+def test_layer_outputs_teacher_forced(gctx, orc, kv):
+    """Per-layer attention / LN1 / pre-LN2 / layer outputs, prefill + 6 forced decode steps."""
+    rng = np.random.default_rng(7)
+    reqs = S.ragged_requests(7, 2, lo=60, hi=120)
+    forced = rng.integers(0, 1024, (2, 6)).astype(np.int32)
+    _reserve(gctx, kv)
+    lg, dump = gctx.debug_trace(reqs, forced, dump=True)
+    rlg, rdump = orc.decode_trace(reqs, forced, kv_f16=(kv == 0), dump=True)
+    _, pdump = orc.first_logits(reqs, kv_f16=(kv == 0), dump=True)
+    ref_dump = np.concatenate([pdump[None], rdump], axis=0)   # [steps+1][B][NL][4][D]
+    worst = 0.0
+    for s in range(dump.shape[0]):
+        for b in range(dump.shape[1]):
+            for li in range(dump.shape[2]):
+                for it in range(4):
+                    e = rel_l2(dump[s, b, li, it], ref_dump[s, b, li, it])
+                    worst = max(worst, e)
+                    assert e <= REL_L2, (s, b, li, it, e)
+    print(f"kv={'f32' if kv else 'f16'} worst layer rel-L2 {worst:.3e}")
+    for s in range(lg.shape[0]):
+        for b in range(lg.shape[1]):
+            assert cosine(lg[s, b], rlg[s, b]) >= COS
+
+
+@pytest.mark.parametrize("kv", [1, 0])
+def test_decode_logits_trace(gctx, orc, kv):
+    rng = np.random.default_rng(8)
+    reqs = S.ragged_requests(8, 4)
+    forced = rng.integers(0, 1024, (4, 48)).astype(np.int32)
+    _reserve(gctx, kv)
+    lg = gctx.debug_trace(reqs, forced)
+    rlg = orc.decode_trace(reqs, forced, kv_f16=(kv == 0))
+    pairs = [(s, b) for s in range(lg.shape[0]) for b in range(lg.shape[1])]
+    cos = min(cosine(lg[s, b], rlg[s, b]) for s, b in pairs)
+    rl = max(rel_l2(lg[s, b], rlg[s, b]) for s, b in pairs)
+    print(f"kv={'f32' if kv else 'f16'} min cosine {cos:.9f} max rel-L2 {rl:.3e}")
+    assert cos >= COS and rl <= REL_L2
+    if kv == 0:   # the F16 cache against the reference's F32 cache
+        rlg32 = orc.decode_trace(reqs, forced, kv_f16=False)
+        cos32 = min(cosine(lg[s, b], rlg32[s, b]) for s, b in pairs)
+        rl32 = max(rel_l2(lg[s, b], rlg32[s, b]) for s, b in pairs)
+        print(f"f16 cache vs f32 reference: min cosine {cos32:.9f} max rel-L2 {rl32:.3e}")
+        assert cos32 >= COS
+
+
+def _first_divergence(a, b):
+    n = min(len(a), len(b))
+    for i in range(n):
+        if a[i] != b[i]:
+            return i
+    return None if len(a) == len(b) else n
+
+
+@pytest.mark.parametrize("kv", [1, 0])
+def test_greedy_streams_config1(gctx, orc, kv):
+    """BASELINE config 1 greedy variant: B=16, prefixes U[80,400] split 70/30, 200 steps."""
+    reqs = S.ragged_requests(1000, 16)
+    _reserve(gctx, kv)
+    steps = 200
+    got, glens = gctx.generate(reqs, top_k=1, seed_base=1000, max_steps=steps)
+    ref, rlens = orc.generate(reqs, top_k=1, seed_base=1000, max_steps=steps, kv_f16=(kv == 0))
+    same, report = 0, []
+    for b in range(len(reqs)):
+        P = len(reqs[b].prompt)
+        d = _first_divergence(got[b][P:], ref[b][P:])
+        same += d is None
+        if d is not None:
+            report.append((b, d))
+    print(f"kv={'f32' if kv else 'f16'} identical greedy streams: {same}/{len(reqs)}; "
+          f"first divergences (seq, step): {report}")
+    assert same / len(reqs) >= 0.95
+
+
+def test_sampled_generate_matches_oracle(gctx, orc):
+    """Default sampler (top_k 15, rep 1.35), per-sequence seeds, EOS and early-stop rules."""
+    rng = np.random.default_rng(3)
+    reqs = [S.make_request(rng, 40 + 10 * i, 30) for i in range(3)]
+    _reserve(gctx, 1)
+    seeds = [1000, 1001, 1002]
+    got, glens = gctx.generate(reqs, seeds=seeds, max_steps=60, early_stop=45)
+    ref, rlens = orc.generate(reqs, seeds=seeds, max_steps=60, early_stop=45)
+    assert glens == rlens
+    for b in range(3):
+        assert np.array_equal(got[b], ref[b]), b
+
+
+def test_oracle_tokens_teacher_forcing(gctx, orc):
+    rng = np.random.default_rng(4)
+    reqs = [S.make_request(rng, 30, 20), S.make_request(rng, 30, 20)]
+    forced = rng.integers(0, 1024, 25).astype(np.int32)
+    _reserve(gctx, 1)
+    got, glens = gctx.generate(reqs, seed_base=9, max_steps=25, oracle_tokens=forced)
+    ref, rlens = orc.generate(reqs, seed_base=9, max_steps=25, oracle_tokens=forced)
+    assert glens == rlens == [25, 25]
+    for b in range(2):
+        assert np.array_equal(got[b], ref[b])
+        assert np.array_equal(got[b][20:], forced)
+
+
+def test_eos_finish_and_lens_order(gctx, orc):
+    """EOS (forced at step 14) finishes every sequence; tokens exclude it."""
+    rng = np.random.default_rng(5)
+    reqs = [S.make_request(rng, 20, 10) for _ in range(3)]
+    forced = rng.integers(0, 1024, 30).astype(np.int32)
+    forced[14] = 1024
+    _reserve(gctx, 1)
+    got, glens = gctx.generate(reqs, seed_base=3, max_steps=30, oracle_tokens=forced)
+    ref, rlens = orc.generate(reqs, seed_base=3, max_steps=30, oracle_tokens=forced)
+    assert glens == rlens == [14, 14, 14]
+    for b in range(3):
+        assert np.array_equal(got[b], ref[b])
+        assert len(got[b]) == 10 + 14
+
+
+def test_serving_refill_equals_generate(gctx):
+    """Continuous batching: a sequence admitted into a refilled slot decodes exactly as alone."""
+    reqs = S.ragged_requests(55, 6, lo=40, hi=120)
+    seeds = [500 + i for i in range(6)]
+    steps = [40, 40, 40, 40, 68, 75]
+    _reserve(gctx, 0, slots=4, ctx=512)
+    alone = []
+    for i in range(6):
+        t, _ = gctx.generate([reqs[i]], seeds=[seeds[i]], max_steps=steps[i])
+        alone.append(t[0][len(reqs[i].prompt):])
+    gctx.serve_admit(reqs[:4], seeds[:4], list(range(4)), max_steps=40)
+    served, pending = {}, 4
+    for _ in range(200):
+        if len(served) == 6:
+            break
+        for f in gctx.serve_step(8, tok_cap=100000):
+            served[f["tag"]] = f["tokens"]
+            if pending < 6:
+                gctx.serve_admit([reqs[pending]], [seeds[pending]], [pending], max_steps=steps[pending])
+                pending += 1
+    assert len(served) == 6
+    for i in range(6):
+        assert np.array_equal(served[i], alone[i]), i
+
+
+def test_cpp_dropin_class(gctx, model_full, tmp_path):
+    """The C++ `class gsv_ar` shim (csrc/gsv_ar.cpp) gives the C ABI's results."""
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    exe = os.path.join(root, "gsv.cpp_b200", "lib", "gsv_ar_smoke")
+    assert os.path.exists(exe), "build with `make -C gsv.cpp_b200`"
+    rng = np.random.default_rng(77)
+    reqs = [S.make_request(rng, 33, 12), S.make_request(rng, 21, 12)]
+    f = tmp_path / "reqs.bin"
+    with open(f, "wb") as fh:
+        fh.write(struct.pack("<i", len(reqs)))
+        for r in reqs:
+            fh.write(struct.pack("<ii", len(r.phones), len(r.prompt)))
+            fh.write(np.asarray(r.phones, np.int32).tobytes())
+            fh.write(np.ascontiguousarray(r.bert, np.float32).tobytes())
+            fh.write(np.asarray(r.prompt, np.int32).tobytes())
+    out = subprocess.run([exe, model_full, str(f), "50", "-1", "7"], capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stderr
+    lines = [json.loads(x) for x in out.stdout.strip().splitlines()]
+    _reserve(gctx, 0)
+    got, glens = gctx.generate(reqs, seed_base=7, max_steps=50)
+    fl = gctx.first_logits(reqs)
+    np.testing.assert_allclose(np.array(lines[0]["first_logits"], np.float32), fl[0, :8], rtol=1e-7)
+    for b in range(2):
+        assert lines[1 + b]["tokens"] == got[b].tolist()
+    assert lines[3]["lens"] == glens
+    assert (lines[3]["hidden"], lines[3]["vocab"], lines[3]["eos"]) == (512, 1025, 1024)
