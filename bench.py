@@ -1,0 +1,330 @@
+"""bench.py -- AR semantic tokens/s of the B200 hot path on BASELINE config 4 (box-wide serving).
+
+One bench step = one serving job per GPU: 64 sequence slots, prefixes U[80,400] split 70/30
+phones/prompt codes, 1500 decode iterations with top_k 15 / rep 1.35 sampling and EOS (1024) on;
+finished slots are refilled from a seeded request queue every 16 iterations. Weak scaling: every
+rank runs its own 64-slot shard with its own request stream (no data-path collective).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl gsvcu|reference]
+
+value: job throughput with the requests' BERT features already in HBM (device pointers to the C ABI);
+e2e:   the same jobs through the same C ABI with every input in host memory (H2D inside the timed
+       region) and every finished sequence's tokens read back to the host.
+Timing: CUDA events on the library's stream, barrier + synchronize on both sides, max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for sub in ("gsv.cpp_b200", "oracle"):
+    sys.path.insert(0, os.path.join(ROOT, sub))
+
+METRIC = "AR semantic tokens/s (batched decode, box)"
+MODEL_CACHE = os.environ.get("GSVCU_MODEL_CACHE", "/tmp/gsvcu_models")
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="gsvcu", choices=["gsvcu", "reference"])
+    ap.add_argument("--slots", type=int, default=64)
+    ap.add_argument("--iters", type=int, default=1500)
+    ap.add_argument("--refill-every", type=int, default=16)
+    ap.add_argument("--kv", default="f16", choices=["f16", "f32"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+class RequestStream:
+    """Seeded queue of BASELINE config-4 requests for one (rank, job)."""
+
+    def __init__(self, rank, job, device=None):
+        import gsv_synth as S
+        self.S = S
+        self.rng = np.random.default_rng([20261201, rank, job])
+        self.device = device
+        self.n = 0
+        self.rank, self.job = rank, job
+
+    def next(self):
+        P = int(self.rng.integers(80, 401))
+        T = int(round(0.7 * P))
+        r = self.S.make_request(self.rng, T, P - T)
+        seed = (self.rank << 40) | (self.job << 20) | self.n
+        self.n += 1
+        return r, seed
+
+
+def stage(stream, count, device):
+    """Pre-generate `count` requests; with device, their BERT features are moved into HBM."""
+    import torch
+    out = []
+    for _ in range(count):
+        r, seed = stream.next()
+        if device is not None:
+            r = type(r)(phones=r.phones, bert=torch.from_numpy(np.ascontiguousarray(r.bert)).to(device), prompt=r.prompt)
+        out.append((r, seed))
+    return out
+
+
+def run_job(ctx, queue, args, counters):
+    """One serving job: returns generated tokens."""
+    ctx.serve_reset()
+    t0 = ctx.serve_tokens_total()
+    at = 0
+
+    def admit(k):
+        nonlocal at
+        if at + k > len(queue):
+            raise RuntimeError("request queue exhausted; enlarge the staged queue")
+        items = queue[at:at + k]
+        at += k
+        reqs = [r for r, _ in items]
+        ctx.serve_admit(reqs, [s for _, s in items], list(range(at - k, at)), max_steps=args.iters)
+        for r in reqs:
+            T, P = len(r.phones), len(r.prompt)
+            counters["h2d"] += 4 * T + 4 * P + (0 if hasattr(r.bert, "data_ptr") else 4 * 1024 * T)
+        counters["seqs"] += k
+
+    admit(args.slots)
+    it = 0
+    while it < args.iters:
+        n = min(args.refill_every, args.iters - it)
+        done = ctx.serve_step(n, max_done=args.slots, tok_cap=args.slots * args.iters)
+        it += n
+        counters["d2h"] += 64 * ctx.lib.gsvcu_serve_active(ctx.h) + sum(4 * len(d["tokens"]) for d in done)
+        if done and it < args.iters:
+            admit(len(done))
+    tokens = ctx.serve_tokens_total() - t0
+    ctx.serve_reset()
+    return tokens
+
+
+def sample_clocks(local_rank):
+    try:
+        return subprocess.Popen(
+            ["nvidia-smi", "-i", str(local_rank),
+             "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+             "--format=csv,noheader,nounits", "-lms", "200"],
+            stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+    except Exception:
+        return None
+
+
+def clock_summary(proc):
+    if proc is None:
+        return None
+    proc.terminate()
+    try:
+        out = proc.communicate(timeout=5)[0]
+    except Exception:
+        return None
+    rows = [[c.strip() for c in l.split(",")] for l in out.strip().splitlines() if l.count(",") >= 8]
+    if not rows:
+        return None
+    sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+    mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+    return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+            "reasons": reasons, "samples": len(rows)}
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def traffic_per_key():
+    """DRAM bytes per attended key of one decode-attention launch, from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "decode_attention_cfg3_b64.md")
+    try:
+        for line in open(p):
+            if line.startswith("dram_bytes_per_key:"):
+                return float(line.split(":")[1])
+    except OSError:
+        pass
+    return None
+
+
+def cpu_baseline(args, job_tokens, job_seqs):
+    """The oracle (CPU restatement of the reference's ggml CPU path) on a bounded sample of the job:
+    16 config-4 sequences, prefill timed, then 8 decode steps timed; the job's time is extrapolated
+    from the measured per-sequence prefill cost and per-token decode cost."""
+    import gsv_synth as S
+    import oracle as O
+    model = S.cached_model(MODEL_CACHE, seed=0, n_layer=24)
+    cores = os.cpu_count() or 1
+    O.set_threads(cores)
+    orc = O.OracleModel(model)
+    stream = RequestStream(99, 0)
+    reqs = [stream.next()[0] for _ in range(16)]
+    t0 = time.perf_counter()
+    orc.first_logits(reqs)
+    t_prefill = time.perf_counter() - t0
+    steps = 8
+    t0 = time.perf_counter()
+    orc.generate(reqs, seeds=list(range(16)), max_steps=steps + 1)
+    t_gen = time.perf_counter() - t0
+    per_seq_prefill = t_prefill / len(reqs)
+    per_token_decode = max(t_gen - t_prefill, 1e-9) / (len(reqs) * steps)
+    est = job_seqs * per_seq_prefill + job_tokens * per_token_decode
+    return {"value": job_tokens / est, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"16 config-4 sequences (prefill {t_prefill:.1f} s) + {steps} decode steps at B=16 "
+                      f"({t_gen - t_prefill:.1f} s) on {cores} threads; job time extrapolated for "
+                      f"{job_seqs} prefills + {job_tokens} tokens",
+            "sample_seconds": round(t_prefill + t_gen, 2)}
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    n_gpus = max(args.gpus, world)
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        cb = cpu_baseline(args, job_tokens=args.slots * args.iters, job_seqs=args.slots)
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tokens/s", "n_gpus": n_gpus,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "q8_0 int8 dot / f32", "data": "synthetic",
+            "config": {"workload": "cfg4 shard extrapolated from a bounded CPU sample",
+                       "slots_per_gpu": args.slots, "iters": args.iters},
+            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+        return
+
+    import torch
+    import torch.distributed as dist
+    import gsv_synth as S
+    import gsvcu
+
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    if rank == 0:
+        model = S.cached_model(MODEL_CACHE, seed=0, n_layer=24)
+    if world > 1:
+        dist.barrier()
+    model = S.cached_model(MODEL_CACHE, seed=0, n_layer=24)
+
+    ctx = gsvcu.Context(local_rank)
+    ctx.load(model)
+    max_ctx = 400 + args.iters + 8
+    ctx.kv_reserve(args.slots, max_ctx, gsvcu.KV_F16 if args.kv == "f16" else gsvcu.KV_F32)
+    ext = torch.cuda.ExternalStream(ctx.stream_handle())
+    queue_len = args.slots * 5
+    counters = {"h2d": 0, "d2h": 0, "seqs": 0}
+
+    for w in range(args.warmup):
+        run_job(ctx, stage(RequestStream(rank, 1000 + w), queue_len, None), args, counters)
+
+    def timed(device_inputs, job0):
+        queues = [stage(RequestStream(rank, job0 + k), queue_len, local_rank if device_inputs else None)
+                  for k in range(args.steps)]
+        counters.update(h2d=0, d2h=0, seqs=0)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        l0 = ctx.kernel_launches()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(ext)
+        tokens = 0
+        for q in queues:
+            tokens += run_job(ctx, q, args, counters)
+        ev1.record(ext)
+        torch.cuda.synchronize()
+        ms = ev0.elapsed_time(ev1)
+        if world > 1:
+            dist.barrier()
+        launches = ctx.kernel_launches() - l0
+        t = torch.tensor([ms, float(tokens), float(counters["seqs"])], dtype=torch.float64, device="cuda")
+        if world > 1:
+            mx = t.clone()
+            dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+            dist.all_reduce(t, op=dist.ReduceOp.SUM)
+            t[0] = mx[0]
+        return float(t[0]), float(t[1]), float(t[2]), launches, dict(counters)
+
+    clk = sample_clocks(local_rank)
+    ms_v, tok_v, seqs_v, launches_v, _ = timed(True, 2000)
+    clocks = clock_summary(clk)
+    ms_e, tok_e, seqs_e, _, cnt_e = timed(False, 2000)
+
+    # roofline of the dominant kernel (decode attention) on a mid-job state of the same workload
+    prof_q = stage(RequestStream(rank, 3000), queue_len, None)
+    ctx.serve_reset()
+    ctx.serve_admit([r for r, _ in prof_q[:args.slots]], [s for _, s in prof_q[:args.slots]],
+                    list(range(args.slots)), max_steps=args.iters)
+    ctx.serve_step(args.iters // 2)
+    prof_steps = 8
+    ms_cls, attn_bytes = ctx.step_profile(prof_steps)
+    ctx.serve_reset()
+    n_launch = prof_steps * ctx.hp.n_layer
+    attn_ms = ms_cls["decode_attn"] / n_launch
+    bytes_launch = attn_bytes / n_launch
+    peak, peak_kind = measured_peaks()
+    achieved = bytes_launch / (attn_ms * 1e-3) / 1e9
+    tpk = traffic_per_key()
+    keys_launch = bytes_launch / (2 * 512 * (2 if args.kv == "f16" else 4))
+
+    value = tok_v / (ms_v * 1e-3)
+    e2e = tok_e / (ms_e * 1e-3)
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": n_gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_v / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "q8_0 int8 MMA / f32 softmax / f16 KV" if args.kv == "f16" else
+        "q8_0 int8 MMA / f32 softmax / f32 KV", "data": "synthetic (seeded GGUF weights N(0,0.02), requests U[80,400])",
+        "config": {"workload": "cfg4: box-wide serving shard per GPU (BASELINE configs[4])",
+                   "model": "gsv AR 24 x 512, 16 heads x 32, FFN 2048, vocab 1025, Q8_0 attn/FFN",
+                   "slots_per_gpu": args.slots, "iters_per_job": args.iters, "refill_every": args.refill_every,
+                   "sampler": "top_k 15, top_p 1.0, temperature 1.0, rep 1.35, EOS 1024",
+                   "kv_cache": f"paged {args.kv}, 64-token pages", "parallelism": f"dp{n_gpus} (replicas, batch-sharded)",
+                   "l2": "no flush; KV working set per step (>1 GB) exceeds the 126 MB L2",
+                   "tokens_per_step": tok_v / args.steps, "sequences_per_step": seqs_v / args.steps},
+        "gpu_launches": launches_v,
+        "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": cnt_e["h2d"] // args.steps,
+                "d2h_bytes_per_step": cnt_e["d2h"] // args.steps},
+        "roofline": {"kernel": "k_decode_attn<__half>", "bound": "hbm", "achieved": achieved, "peak": peak,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": (tpk * keys_launch) if tpk else None, "algorithmic_bytes_per_launch": bytes_launch,
+                     "avg_launch_ms": attn_ms},
+        "step_profile_ms": {k: round(v / prof_steps, 4) for k, v in ms_cls.items()},
+        "clocks": clocks,
+    }
+    if n_gpus == 1 and not args.no_cpu_baseline:
+        cb = cpu_baseline(args, job_tokens=int(tok_v / args.steps), job_seqs=int(seqs_v / args.steps))
+        line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    print(json.dumps(line))
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

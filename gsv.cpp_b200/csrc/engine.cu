@@ -226,6 +226,11 @@ struct gsvcu_ctx {
     gsvcu_sampler_cfg graph_cfg{};
     gsvcu_sampler_cfg cfg{15, 1.0f, 1.0f, 1.35f};
     int64_t tokens_done = 0;   // generated tokens of finished sequences (serving)
+    int64_t launches = 0;      // kernels launched by this context (graph replays count their kernels)
+    int graph_kernels = 0;     // kernels in one captured decode step
+    // step profiler: events between kernel classes of an instrumented step
+    cudaEvent_t prof_ev[2] = {nullptr, nullptr};
+    float* prof_ms = nullptr;  // accumulators [GSVCU_PROF_CLASSES] while profiling, else null
 
     // op-entry scratch
     float* op_part = nullptr;
@@ -282,6 +287,8 @@ gsvcu_ctx::~gsvcu_ctx() {
     for (void* p : wallocs) cudaFree(p);
     if (op_part) cudaFree(op_part);
     if (op_counter) cudaFree(op_counter);
+    for (cudaEvent_t e : prof_ev)
+        if (e) cudaEventDestroy(e);
     if (stream) cudaStreamDestroy(stream);
 }
 
@@ -482,7 +489,7 @@ int gsvcu_ctx::prefill_pass(const int* slots, const gsvcu_request* reqs, int n, 
     std::vector<PrefillTile> tiles;
     size_t feat_n = 0;
     for (int i = 0; i < n; i++) feat_n += (size_t)BD * reqs[i].n_phones;
-    std::vector<float> feat(feat_n);
+    std::vector<size_t> feat_off(n);
     int m = 0;
     size_t fo = 0;
     for (int i = 0; i < n; i++) {
@@ -493,7 +500,7 @@ int gsvcu_ctx::prefill_pass(const int* slots, const gsvcu_request* reqs, int n, 
         tlen[i] = T;
         last[i] = m + T + P - 1;
         sl[i] = slots[i];
-        std::memcpy(feat.data() + fo, r.bert, (size_t)BD * T * 4);
+        feat_off[i] = fo;
         for (int t = 0; t < T; t++, m++) {
             ids[m] = r.phones[t];
             pepos[m] = t;
@@ -542,7 +549,11 @@ int gsvcu_ctx::prefill_pass(const int* slots, const gsvcu_request* reqs, int n, 
     CK(h2d(p_last, last.data(), (size_t)n * 4));
     CK(h2d(p_slots, sl.data(), (size_t)n * 4));
     CK(h2d(p_tiles, tiles.data(), tiles.size() * sizeof(PrefillTile)));
-    if (feat_n) CK(h2d(p_feat, feat.data(), feat_n * 4));
+    // BERT features: host or device memory (unified addressing picks the copy direction)
+    for (int i = 0; i < n; i++)
+        if (reqs[i].n_phones)
+            CK(cudaMemcpyAsync(p_feat + feat_off[i], reqs[i].bert, (size_t)BD * reqs[i].n_phones * 4, cudaMemcpyDefault,
+                               s));
 
     PrefEmbedParams ep;
     ep.ids = p_ids; ep.pe_pos = p_pepos; ep.is_text = p_istext; ep.text_emb = text_emb; ep.audio_emb = audio_emb;
@@ -597,6 +608,7 @@ int gsvcu_ctx::prefill_pass(const int* slots, const gsvcu_request* reqs, int n, 
     launch_copy_rows(p_xl, nullptr, x, p_last, n, D, s);
     launch_gemm_f32d(p_xl, D, nullptr, n, predict, V, D, nullptr, 0, p_lg, V, s);
     launch_copy_rows(logits, p_slots, p_lg, nullptr, n, V, s);
+    launches += 3 + (int64_t)NL * 7 + 3;
     CK(cudaGetLastError());
     // host staging vectors die at return: finish the pass before they go
     CK(cudaStreamSynchronize(s));
@@ -716,17 +728,34 @@ int gsvcu_ctx::admit(const gsvcu_request* reqs, int n, const uint64_t* seeds, co
 // With `dump` (host), every layer's rows of the slots in dump_slots are copied out (no capture).
 int gsvcu_ctx::launch_step(cudaStream_t s, float* dump, int dump_row, const int* dump_slots, int dump_B) {
     const int NL = hp.n_layer, V = hp.vocab_size, M = max_slots;
+    int nk = 0;
+    // class timing (profiler only): mark(c) closes the interval since the previous mark into class c
+    auto mark = [&](int c) -> int {
+        if (!prof_ms) return GSVCU_OK;
+        CK(cudaEventRecord(prof_ev[1], s));
+        CK(cudaEventSynchronize(prof_ev[1]));
+        float ms = 0.f;
+        CK(cudaEventElapsedTime(&ms, prof_ev[0], prof_ev[1]));
+        prof_ms[c] += ms;
+        CK(cudaEventRecord(prof_ev[0], s));
+        return GSVCU_OK;
+    };
+    if (prof_ms) CK(cudaEventRecord(prof_ev[0], s));
     SamplerParams sp;
     sp.logits = logits; sp.V = V; sp.eos = hp.eos; sp.nslots = M;
     sp.top_k = cfg.top_k; sp.top_p = cfg.top_p; sp.temperature = cfg.temperature; sp.rep = cfg.repetition_penalty;
     sp.st = st; sp.counts = counts; sp.hist = hist; sp.out_tokens = out_tokens; sp.tok_cap = tok_cap;
     sp.forced = forced; sp.forced_cap = forced_cap; sp.jump = jump; sp.draws_per_lane = dpl;
     launch_sampler(sp, s);
+    nk++;
+    TRY(mark(0));
     StepPrepParams pp;
     pp.st = st; pp.nslots = M; pp.eos = hp.eos; pp.out_tokens = out_tokens; pp.tok_cap = tok_cap;
     pp.audio_emb = audio_emb; pp.pe = pe; pp.audio_alpha = hp.audio_pe_alpha;
     pp.x = x; pp.xq = xq; pp.xd = xd;
     launch_step_prep(pp, s);
+    nk++;
+    TRY(mark(1));
     const float scale = 1.0f / std::sqrt((float)HD);
     for (int li = 0; li < NL; li++) {
         const LayerW& w = L[li];
@@ -735,24 +764,31 @@ int gsvcu_ctx::launch_step(cudaStream_t s, float* dump, int dump_row, const int*
         g.kv.pool = pool; g.kv.kv_f32 = kv_f32; g.kv.n_layer = NL; g.kv.layer = li; g.kv.block_table = block_table;
         g.kv.max_pages = max_pages; g.kv.st = st;
         launch_gemm_q8(g, EPI_BIAS, s);
+        TRY(mark(2));
         DecAttnParams a;
         a.q = qkv; a.q_stride = 3 * D; a.pool = pool; a.kv_f32 = kv_f32; a.n_layer = NL; a.layer = li;
         a.block_table = block_table; a.max_pages = max_pages; a.st = st; a.B = M; a.max_chunks = max_chunks;
         a.scale = scale; a.out_q = aq; a.out_d = ad; a.out_f32 = dump ? attn_f32 : nullptr;
         a.part = part; a.counter = counter;
         launch_decode_attention(a, s);
+        TRY(mark(3));
         GemmQ8Params o;
         o.xq = aq; o.xd = ad; o.M = M; o.wq = w.wq[1]; o.wd = w.wd[1]; o.N = D; o.K = D; o.bias = w.b_out; o.resid = x; o.y = pre;
         launch_gemm_q8(o, EPI_RESID, s);
+        TRY(mark(4));
         launch_layernorm_q8(pre, M, w.n1w, w.n1b, n1, n1q, n1d, s);
+        TRY(mark(5));
         GemmQ8Params f1;
         f1.xq = n1q; f1.xd = n1d; f1.M = M; f1.wq = w.wq[2]; f1.wd = w.wd[2]; f1.N = FF; f1.K = D; f1.bias = w.b_f1;
         f1.yq = hq; f1.yd = hd;
         launch_gemm_q8(f1, EPI_RELU_Q8, s);
+        TRY(mark(6));
         GemmQ8Params f2;
         f2.xq = hq; f2.xd = hd; f2.M = M; f2.wq = w.wq[3]; f2.wd = w.wd[3]; f2.N = D; f2.K = FF; f2.bias = w.b_f2;
         f2.resid = n1; f2.y = pre;
         launch_gemm_q8(f2, EPI_RESID, s);
+        TRY(mark(7));
+        nk += 7;
         if (dump) {
             const float* items[3] = {attn_f32, n1, pre};
             for (int it = 0; it < 3; it++)
@@ -761,12 +797,16 @@ int gsvcu_ctx::launch_step(cudaStream_t s, float* dump, int dump_row, const int*
                                        items[it] + (size_t)dump_slots[b] * D, D * 4, cudaMemcpyDeviceToHost, s));
         }
         launch_layernorm_q8(pre, M, w.n2w, w.n2b, x, xq, xd, s);
+        TRY(mark(5));
         if (dump)
             for (int b = 0; b < dump_B; b++)
                 CK(cudaMemcpyAsync(dump + ((((size_t)dump_row * dump_B + b) * NL + li) * 4 + 3) * D,
                                    x + (size_t)dump_slots[b] * D, D * 4, cudaMemcpyDeviceToHost, s));
     }
     launch_gemm_f32d(x, D, nullptr, M, predict, V, D, nullptr, 0, logits, V, s);
+    nk++;
+    TRY(mark(8));
+    graph_kernels = nk;
     return GSVCU_OK;
 }
 
@@ -794,6 +834,7 @@ int gsvcu_ctx::run_steps(int nsteps) {
         graph_cfg = cfg;
     }
     for (int i = 0; i < nsteps; i++) CK(cudaGraphLaunch(graph, stream));
+    launches += (int64_t)nsteps * graph_kernels;
     return GSVCU_OK;
 }
 
@@ -1283,6 +1324,56 @@ int gsvcu_op_sample(gsvcu_ctx* ctx, const float* logits_dev, int32_t B, int32_t 
         tokens_host[b] = toks[(size_t)b * cap + step_host[b]];
         rng_host[b] = hs[b].rng;
     }
+    return GSVCU_OK;
+}
+
+void* gsvcu_stream(const gsvcu_ctx* ctx) { return ctx ? (void*)ctx->stream : nullptr; }
+
+int64_t gsvcu_kernel_launches(const gsvcu_ctx* ctx) { return ctx ? ctx->launches : (int64_t)GSVCU_ERR_ARG; }
+
+int gsvcu_serve_reset(gsvcu_ctx* ctx) {
+    if (!ctx) return GSVCU_ERR_ARG;
+    if (!ctx->reserved) return GSVCU_OK;
+    DeviceGuard g(ctx->device);
+    CKC(ctx, cudaStreamSynchronize(ctx->stream));
+    for (int sl = 0; sl < ctx->max_slots; sl++)
+        if (ctx->slot_used[sl]) ctx->release_slot(sl);
+    CKC(ctx, cudaMemsetAsync(ctx->st, 0, sizeof(SlotState) * ctx->max_slots, ctx->stream));
+    for (auto& s : ctx->h_st) s = SlotState{};
+    CKC(ctx, cudaStreamSynchronize(ctx->stream));
+    return GSVCU_OK;
+}
+
+int gsvcu_step_profile(gsvcu_ctx* ctx, int32_t n_steps, float* ms_by_class, int64_t* attn_bytes) {
+    if (!ctx || n_steps <= 0 || !ms_by_class) return GSVCU_ERR_ARG;
+    if (!ctx->reserved) return ctx->fail(GSVCU_ERR_STATE, "no KV pool reserved");
+    DeviceGuard g(ctx->device);
+    for (int c = 0; c < GSVCU_PROF_CLASSES; c++) ms_by_class[c] = 0.f;
+    int64_t bytes = 0;
+    if (!ctx->prof_ev[0]) {
+        CKC(ctx, cudaEventCreate(&ctx->prof_ev[0]));
+        CKC(ctx, cudaEventCreate(&ctx->prof_ev[1]));
+    }
+    const size_t elem = ctx->kv_f32 ? 4 : 2;
+    for (int i = 0; i < n_steps; i++) {
+        TRY(ctx->read_status());
+        // keys each decoding slot will read in this step: kvlen + 1 (the token appended by the step)
+        for (int sl = 0; sl < ctx->max_slots; sl++) {
+            const SlotState& s = ctx->h_st[sl];
+            // (a slot that samples EOS this step is counted too; it skips attention, a negligible over-count)
+            const bool will_decode = ctx->slot_used[sl] && s.active && s.n_samp + 1 < s.max_steps;
+            // per layer: K and V rows of every key, q in (f32), Q8_0 output (512 B + 16 fp16 scales)
+            if (will_decode)
+                bytes += ((int64_t)(s.kvlen + 1) * 2 * D * elem + (int64_t)D * 4 + D + (D / QK) * 2) * ctx->hp.n_layer;
+        }
+        ctx->prof_ms = ms_by_class;
+        const int rc = ctx->launch_step(ctx->stream);
+        ctx->prof_ms = nullptr;
+        if (rc != GSVCU_OK) return rc;
+        ctx->launches += ctx->graph_kernels;
+    }
+    CKC(ctx, cudaStreamSynchronize(ctx->stream));
+    if (attn_bytes) *attn_bytes = bytes;
     return GSVCU_OK;
 }
 

@@ -79,7 +79,14 @@ SIGNATURES = {
     "gsvcu_op_prefill_attention": ([_P, _P, _I, _P, _P, _P, _P, _P, _P], C.c_int),
     "gsvcu_op_sample": ([_P, _P, _I, _I, _I, C.POINTER(SamplerCfg), _P, _P, _I, _P, _P, _P], C.c_int),
     "gsvcu_sync": ([_P], C.c_int),
+    "gsvcu_serve_reset": ([_P], C.c_int),
+    "gsvcu_step_profile": ([_P, _I, _P, _P], C.c_int),
+    "gsvcu_kernel_launches": ([_P], C.c_int64),
+    "gsvcu_stream": ([_P], C.c_void_p),
 }
+
+PROF_CLASSES = ["sampler", "step_prep", "qkv_gemm", "decode_attn", "out_gemm", "layernorm", "ffn1_gemm", "ffn2_gemm",
+                "predict"]
 
 _LIB = None
 
@@ -132,14 +139,21 @@ class _Reqs:
         arr = (Request * len(reqs))()
         for i, r in enumerate(reqs):
             ph = np.ascontiguousarray(r.phones, np.int32)
-            be = np.ascontiguousarray(r.bert, np.float32).reshape(-1)
             pr = np.ascontiguousarray(r.prompt, np.int32)
-            if be.size != bert_dim * ph.size:
-                raise ValueError("bert must hold bert_dim x n_phones values")
+            if hasattr(r.bert, "data_ptr"):      # device tensor (float32, contiguous, on the context's GPU)
+                be = r.bert
+                if be.numel() != bert_dim * ph.size or not be.is_contiguous():
+                    raise ValueError("bert must hold bert_dim x n_phones contiguous values")
+                bptr = C.cast(C.c_void_p(be.data_ptr()), C.POINTER(C.c_float))
+            else:
+                be = np.ascontiguousarray(r.bert, np.float32).reshape(-1)
+                if be.size != bert_dim * ph.size:
+                    raise ValueError("bert must hold bert_dim x n_phones values")
+                bptr = be.ctypes.data_as(C.POINTER(C.c_float))
             self.keep += [ph, be, pr]
             arr[i].phones = ph.ctypes.data_as(C.POINTER(C.c_int32))
             arr[i].n_phones = ph.size
-            arr[i].bert = be.ctypes.data_as(C.POINTER(C.c_float))
+            arr[i].bert = bptr
             arr[i].prompt = pr.ctypes.data_as(C.POINTER(C.c_int32)) if pr.size else None
             arr[i].n_prompt = pr.size
         self.arr = arr
@@ -246,6 +260,21 @@ class Context:
                             tokens=toks[at:at + f.n_tokens].copy()))
             at += f.n_tokens
         return out
+
+    def serve_reset(self):
+        self._check(self.lib.gsvcu_serve_reset(self.h))
+
+    def step_profile(self, n_steps):
+        ms = np.zeros(len(PROF_CLASSES), np.float32)
+        by = C.c_int64(0)
+        self._check(self.lib.gsvcu_step_profile(self.h, n_steps, _ptr(ms), C.byref(by)))
+        return dict(zip(PROF_CLASSES, ms.tolist())), int(by.value)
+
+    def kernel_launches(self):
+        return int(self.lib.gsvcu_kernel_launches(self.h))
+
+    def stream_handle(self):
+        return int(self.lib.gsvcu_stream(self.h) or 0)
 
     def serve_active(self):
         return self.lib.gsvcu_serve_active(self.h)

@@ -51,7 +51,8 @@ typedef struct {
 } gsvcu_sampler_cfg;
 
 /* One sequence (gsv_ar_request, reference src/gsv_ar.h:13-17): phone ids, BERT features laid out
- * [bert_dim][n_phones] (bert[k * n_phones + t]), reference prompt semantic codes. */
+ * [bert_dim][n_phones] (bert[k * n_phones + t]), reference prompt semantic codes. phones and prompt
+ * are host memory; bert may be host or device memory of the context's device. */
 typedef struct {
     const int32_t* phones;
     int32_t n_phones;
@@ -140,6 +141,9 @@ int gsvcu_serve_admit(gsvcu_ctx* ctx, const gsvcu_request* reqs, int32_t n, cons
  * tok_cap; may be NULL). Returns the number of records (>= 0) or an error. */
 int gsvcu_serve_step(gsvcu_ctx* ctx, int32_t n_steps, gsvcu_finished* done, int32_t max_done, int32_t* tokens,
                      int32_t tok_cap);
+/* Drop every sequence in flight (cancellation): slots and KV pages return to the pool, nothing is
+ * reported. */
+int gsvcu_serve_reset(gsvcu_ctx* ctx);
 /* Slots currently in flight. */
 int gsvcu_serve_active(const gsvcu_ctx* ctx);
 /* Generated tokens produced so far: finished sequences plus the tokens sampled so far by the
@@ -204,6 +208,24 @@ int gsvcu_op_prefill_attention(gsvcu_ctx* ctx, const float* qkv_dev, int32_t n_s
 int gsvcu_op_sample(gsvcu_ctx* ctx, const float* logits_dev, int32_t B, int32_t V, int32_t eos,
                     const gsvcu_sampler_cfg* cfg, const int32_t* prev_host, const int32_t* n_prev_host,
                     int32_t prev_stride, const int32_t* step_host, uint64_t* rng_host, int32_t* tokens_host);
+
+/* ---------------------------------------------------------------- profiling (GSV_AR_PROFILE buckets,
+ * reference src/gsv_ar.cpp:18-42) */
+
+/* Kernel classes of one decode step, indices of ms_by_class. */
+enum {
+    GSVCU_PROF_SAMPLER = 0, GSVCU_PROF_STEP_PREP, GSVCU_PROF_QKV_GEMM, GSVCU_PROF_DECODE_ATTN, GSVCU_PROF_OUT_GEMM,
+    GSVCU_PROF_LAYERNORM, GSVCU_PROF_FFN1_GEMM, GSVCU_PROF_FFN2_GEMM, GSVCU_PROF_PREDICT, GSVCU_PROF_CLASSES
+};
+/* Run n_steps decode steps of the slots in flight without the graph, timing every kernel class with
+ * CUDA events on the context's stream; ms_by_class [GSVCU_PROF_CLASSES] gets the summed milliseconds,
+ * attn_bytes (may be NULL) the algorithmic K/V + q/out bytes the attention launches read and wrote. */
+int gsvcu_step_profile(gsvcu_ctx* ctx, int32_t n_steps, float* ms_by_class, int64_t* attn_bytes);
+/* Number of kernels this context has launched (graph replays count their kernels). */
+int64_t gsvcu_kernel_launches(const gsvcu_ctx* ctx);
+/* The context's CUDA stream (cudaStream_t), for callers that order their own work after it or time
+ * it with events. */
+void* gsvcu_stream(const gsvcu_ctx* ctx);
 
 /* Synchronise the context's stream. */
 int gsvcu_sync(gsvcu_ctx* ctx);
