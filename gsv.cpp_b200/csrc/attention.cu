@@ -1,8 +1,8 @@
 // attention.cu -- decode (split-KV flash decoding over paged KV) and prefix-masked prefill attention.
 //
-// Both follow ggml flash_attn_ext's arithmetic as the reference uses it (src/gsv_ar.cpp:257,331,404):
-// score = (float)(sum_d (double)(q_d * k_d)) * (1/sqrt(32)), masked keys skipped, online softmax with
-// expf, S = S*ms + vs and VKQ = VKQ*ms + v*vs, output VKQ * (1/S), then Q8_0-quantized (one head
+// Both evaluate ggml flash_attn_ext as the reference uses it (src/gsv_ar.cpp:257,331,404):
+// score = (float)(sum_d (double)(q_d * k_d)) * (1/sqrt(32)), masked keys skipped, softmax(score) V
+// with the weights and sums in double, one final rounding to float; then Q8_0-quantized (one head
 // = one 32-value block) for the out-projection GEMM.
 #include <cfloat>
 
@@ -13,7 +13,15 @@ namespace gsvcu {
 // ------------------------------------------------------------------ decode
 // Work item = (slot, head, chunk of ATT_CHUNK keys), one warp each, 4 heads per CTA.
 // K/V rows of one head are 32 contiguous elements inside a 64-token page, so a warp reads
-// 8 tokens x 64 B (F16) per 128-bit load instruction; 4 loads of K and 4 of V are in flight per lane.
+// TPI tokens x 64 B (F16) per 128-bit load instruction; U loads of K and U of V are in flight per
+// lane, a block of TPI*U (32 for F16) tokens per iteration.
+//
+// Arithmetic: scores s = (float)(double sum of float products) * scale, as ggml's vec_dot_f32; the
+// softmax-weighted sum is carried in double: per block of tokens the warp-uniform running max m is
+// raised to the block max (rescaling l and o by exp(m_old - m_new)), lane j computes the weight
+// p_j = exp(s_j - m) of token j once, and each lane accumulates o += p * v for its dims. The result
+// (float)(o / l) is exact to ~1e-16 before the final rounding, so it does not depend on the
+// reduction order (token groups, split-KV chunks) and equals the oracle's evaluation bit for bit.
 // Chunks of one (slot, head) are merged by the last warp to finish (atomic ticket, no waiting).
 template <typename KT>
 __global__ void __launch_bounds__(128) k_decode_attn(const DecAttnParams p) {
@@ -21,6 +29,7 @@ __global__ void __launch_bounds__(128) k_decode_attn(const DecAttnParams p) {
     constexpr int LPT = HD / EPL;            // lanes per token
     constexpr int TPI = 32 / LPT;            // tokens per warp-load
     constexpr int U = 4;                     // loads in flight per lane (per K and per V)
+    constexpr int BLK = TPI * U;             // tokens per block (<= 32)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int slot = blockIdx.z, chunk = blockIdx.y, h = blockIdx.x * 4 + warp;
     int kvpos;
@@ -51,11 +60,12 @@ __global__ void __launch_bounds__(128) k_decode_attn(const DecAttnParams p) {
     const KT* pool = (const KT*)p.pool;
     const int32_t* bt = p.block_table + (size_t)slot * p.max_pages;
 
-    float m = -INFINITY, l = 0.0f, o[EPL];
+    float m = -INFINITY;      // warp-uniform running max
+    double l = 0.0, o[EPL];   // l: this lane's tokens; o: this lane's dims over its tokens
 #pragma unroll
-    for (int e = 0; e < EPL; e++) o[e] = 0.0f;
+    for (int e = 0; e < EPL; e++) o[e] = 0.0;
 
-    for (int base = k0; base < k1; base += TPI * U) {
+    for (int base = k0; base < k1; base += BLK) {
         const size_t pbase = (size_t)bt[base / PAGE] * page_elems;
         uint4 kr[U], vr[U];
 #pragma unroll
@@ -69,71 +79,83 @@ __global__ void __launch_bounds__(128) k_decode_attn(const DecAttnParams p) {
                 vr[u] = ldg_stream(pool + r + voff);
             }
         }
+        float sc[U];
 #pragma unroll
         for (int u = 0; u < U; u++) {
-            const int kk = base + u * TPI + tk;
-            float kf[EPL], vf[EPL];
+            float kf[EPL];
             if (sizeof(KT) == 2) {
                 const __half2* k2 = (const __half2*)&kr[u];
-                const __half2* v2 = (const __half2*)&vr[u];
 #pragma unroll
                 for (int e = 0; e < EPL / 2; e++) {
-                    const float2 a = __half22float2(k2[e]), b = __half22float2(v2[e]);
+                    const float2 a = __half22float2(k2[e]);
                     kf[2 * e] = a.x; kf[2 * e + 1] = a.y;
-                    vf[2 * e] = b.x; vf[2 * e + 1] = b.y;
                 }
             } else {
                 const float* k4 = (const float*)&kr[u];
-                const float* v4 = (const float*)&vr[u];
 #pragma unroll
-                for (int e = 0; e < EPL; e++) { kf[e] = k4[e]; vf[e] = v4[e]; }
+                for (int e = 0; e < EPL; e++) kf[e] = k4[e];
             }
             double dot = 0.0;
 #pragma unroll
             for (int e = 0; e < EPL; e++) dot += (double)__fmul_rn(q[e], kf[e]);
 #pragma unroll
             for (int off = 1; off < LPT; off <<= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
-            if (kk < k1) {
-                const float s = __fmul_rn((float)dot, p.scale);
-                if (s > m) {
-                    const float ms = expf(__fsub_rn(m, s));
-                    m = s;
+            const int kk = base + u * TPI + tk;
+            sc[u] = kk < k1 ? __fmul_rn((float)dot, p.scale) : -INFINITY;
+        }
+        // lane j (< BLK) takes the score of block token j = u*TPI + t, held by lane t*LPT
+        float mys = -INFINITY;
 #pragma unroll
-                    for (int e = 0; e < EPL; e++) o[e] = __fadd_rn(__fmul_rn(o[e], ms), vf[e]);
-                    l = fmaf(l, ms, 1.0f);
-                } else {
-                    const float vs = expf(__fsub_rn(s, m));
+        for (int u = 0; u < U; u++) {
+            const float t = __shfl_sync(0xffffffffu, sc[u], (lane % TPI) * LPT);
+            if (lane < BLK && lane / TPI == u) mys = t;
+        }
+        float bm = mys;
 #pragma unroll
-                    for (int e = 0; e < EPL; e++) o[e] = fmaf(vf[e], vs, o[e]);
-                    l = __fadd_rn(l, vs);
+        for (int off = 16; off > 0; off >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, off));
+        if (bm > m) {   // warp-uniform
+            const double r = m == -INFINITY ? 0.0 : exp((double)m - (double)bm);
+            l *= r;
+#pragma unroll
+            for (int e = 0; e < EPL; e++) o[e] *= r;
+            m = bm;
+        }
+        const double pj = mys == -INFINITY ? 0.0 : exp((double)mys - (double)m);
+        l += pj;
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const double pu = __shfl_sync(0xffffffffu, pj, u * TPI + tk);
+            if (sizeof(KT) == 2) {
+                const __half2* v2 = (const __half2*)&vr[u];
+#pragma unroll
+                for (int e = 0; e < EPL / 2; e++) {
+                    const float2 b = __half22float2(v2[e]);
+                    o[2 * e] = fma(pu, (double)b.x, o[2 * e]);
+                    o[2 * e + 1] = fma(pu, (double)b.y, o[2 * e + 1]);
                 }
+            } else {
+                const float* v4 = (const float*)&vr[u];
+#pragma unroll
+                for (int e = 0; e < EPL; e++) o[e] = fma(pu, (double)v4[e], o[e]);
             }
         }
     }
-    // merge the TPI token groups of the warp
+    // sum the token groups (same m everywhere): o over lanes with the same dims, l over the warp
 #pragma unroll
     for (int off = LPT; off < 32; off <<= 1) {
-        const float m2 = __shfl_xor_sync(0xffffffffu, m, off);
-        const float l2 = __shfl_xor_sync(0xffffffffu, l, off);
-        const float mn = fmaxf(m, m2);
-        const float a = m == -INFINITY ? 0.0f : expf(__fsub_rn(m, mn));
-        const float b = m2 == -INFINITY ? 0.0f : expf(__fsub_rn(m2, mn));
 #pragma unroll
-        for (int e = 0; e < EPL; e++) {
-            const float o2 = __shfl_xor_sync(0xffffffffu, o[e], off);
-            o[e] = fmaf(o2, b, __fmul_rn(o[e], a));
-        }
-        l = fmaf(l2, b, __fmul_rn(l, a));
-        m = mn;
+        for (int e = 0; e < EPL; e++) o[e] += __shfl_xor_sync(0xffffffffu, o[e], off);
     }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
 
     if (nch > 1) {
-        float* part = p.part + (((size_t)slot * NH + h) * p.max_chunks) * (2 + HD);
+        double* part = p.part + (((size_t)slot * NH + h) * p.max_chunks) * (2 + HD);
         if (tk == 0) {
 #pragma unroll
             for (int e = 0; e < EPL; e++) part[(size_t)chunk * (2 + HD) + 2 + sub * EPL + e] = o[e];
             if (sub == 0) {
-                part[(size_t)chunk * (2 + HD) + 0] = m;
+                part[(size_t)chunk * (2 + HD) + 0] = (double)m;
                 part[(size_t)chunk * (2 + HD) + 1] = l;
             }
         }
@@ -144,28 +166,26 @@ __global__ void __launch_bounds__(128) k_decode_attn(const DecAttnParams p) {
         ticket = __shfl_sync(0xffffffffu, ticket, 0);
         if (ticket != nch - 1) return;
         __threadfence();
-        float M = -INFINITY;
-        for (int c = 0; c < nch; c++) M = fmaxf(M, __ldcg(part + (size_t)c * (2 + HD)));
-        l = 0.0f;
+        double M = -INFINITY;
+        for (int c = 0; c < nch; c++) M = fmax(M, __ldcg(part + (size_t)c * (2 + HD)));
+        l = 0.0;
 #pragma unroll
-        for (int e = 0; e < EPL; e++) o[e] = 0.0f;
+        for (int e = 0; e < EPL; e++) o[e] = 0.0;
         for (int c = 0; c < nch; c++) {
-            const float mc = __ldcg(part + (size_t)c * (2 + HD));
-            const float lc = __ldcg(part + (size_t)c * (2 + HD) + 1);
-            const float w = mc == -INFINITY ? 0.0f : expf(__fsub_rn(mc, M));
-            l = fmaf(lc, w, l);
+            const double mc = __ldcg(part + (size_t)c * (2 + HD));
+            const double w = mc == -INFINITY ? 0.0 : exp(mc - M);
+            l = fma(__ldcg(part + (size_t)c * (2 + HD) + 1), w, l);
 #pragma unroll
-            for (int e = 0; e < EPL; e++) o[e] = fmaf(__ldcg(part + (size_t)c * (2 + HD) + 2 + sub * EPL + e), w, o[e]);
+            for (int e = 0; e < EPL; e++) o[e] = fma(__ldcg(part + (size_t)c * (2 + HD) + 2 + sub * EPL + e), w, o[e]);
         }
         if (lane == 0) p.counter[(size_t)slot * NH + h] = 0;   // ready for the next launch
     }
 
     // finalize and quantize the head's 32 values (one Q8_0 block)
-    const float inv = l == 0.0f ? 0.0f : __fdiv_rn(1.0f, l);
     float out[EPL], amax = 0.0f;
 #pragma unroll
     for (int e = 0; e < EPL; e++) {
-        out[e] = __fmul_rn(o[e], inv);
+        out[e] = l > 0.0 ? (float)(o[e] / l) : 0.0f;
         amax = fmaxf(amax, fabsf(out[e]));
     }
 #pragma unroll
@@ -191,8 +211,8 @@ void launch_decode_attention(const DecAttnParams& p, cudaStream_t s) {
 }
 
 // ------------------------------------------------------------------ prefill
-// One thread per query row of one head; keys visited in order, so the online-softmax sequence is
-// the same as the reference's per-row loop. Key/value tiles of 64 rows are staged in shared memory
+// One thread per query row of one head; keys visited in order, softmax-weighted sum carried in
+// double and rounded once (see the decode kernel). Key/value tiles of 64 rows are staged in shared memory
 // and read as broadcasts. Mask (src/gsv_ar.cpp:215-223) in-tile: text query (qi < T) sees text keys
 // [0, T); semantic query sees keys [0, qi].
 __global__ void __launch_bounds__(PREF_QTILE) k_prefill_attn(const PrefAttnParams p) {
@@ -206,11 +226,11 @@ __global__ void __launch_bounds__(PREF_QTILE) k_prefill_attn(const PrefAttnParam
     const bool valid = qi < S;
     float q[HD], o[HD];
 #pragma unroll
-    for (int d = 0; d < HD; d++) {
-        q[d] = valid ? p.qkv[(size_t)(start + qi) * 3 * D + h * HD + d] : 0.0f;
-        o[d] = 0.0f;
-    }
-    float m = -INFINITY, l = 0.0f;
+    for (int d = 0; d < HD; d++) q[d] = valid ? p.qkv[(size_t)(start + qi) * 3 * D + h * HD + d] : 0.0f;
+    float m = -INFINITY;
+    double l = 0.0, od[HD];
+#pragma unroll
+    for (int d = 0; d < HD; d++) od[d] = 0.0;
     const int kend = (q0 + PREF_QTILE <= T) ? T : max(T, min(S, q0 + PREF_QTILE));
     for (int kt = 0; kt < kend; kt += PREF_QTILE) {
         __syncthreads();
@@ -239,25 +259,23 @@ __global__ void __launch_bounds__(PREF_QTILE) k_prefill_attn(const PrefAttnParam
             for (int d = 0; d < HD; d++) dot += (double)__fmul_rn(q[d], Ks[j][d]);
             const float s = __fmul_rn((float)dot, p.scale);
             if (s > m) {
-                const float ms = expf(__fsub_rn(m, s));
+                const double r = m == -INFINITY ? 0.0 : exp((double)m - (double)s);
+                l *= r;
+#pragma unroll
+                for (int d = 0; d < HD; d++) od[d] *= r;
                 m = s;
-#pragma unroll
-                for (int d = 0; d < HD; d++) o[d] = __fadd_rn(__fmul_rn(o[d], ms), Vs[j][d]);
-                l = fmaf(l, ms, 1.0f);
-            } else {
-                const float vs = expf(__fsub_rn(s, m));
-#pragma unroll
-                for (int d = 0; d < HD; d++) o[d] = fmaf(Vs[j][d], vs, o[d]);
-                l = __fadd_rn(l, vs);
             }
+            const double pj = exp((double)s - (double)m);
+            l += pj;
+#pragma unroll
+            for (int d = 0; d < HD; d++) od[d] = fma(pj, (double)Vs[j][d], od[d]);
         }
     }
     if (!valid) return;
-    const float inv = l == 0.0f ? 0.0f : __fdiv_rn(1.0f, l);
     float amax = 0.0f;
 #pragma unroll
     for (int d = 0; d < HD; d++) {
-        o[d] = __fmul_rn(o[d], inv);
+        o[d] = l > 0.0 ? (float)(od[d] / l) : 0.0f;
         amax = fmaxf(amax, fabsf(o[d]));
     }
     float dsc, id;

@@ -209,7 +209,7 @@ struct gsvcu_ctx {
     float *x = nullptr, *qkv = nullptr, *pre = nullptr, *n1 = nullptr, *attn_f32 = nullptr;
     int8_t *xq = nullptr, *aq = nullptr, *n1q = nullptr, *hq = nullptr;
     uint16_t *xd = nullptr, *ad = nullptr, *n1d = nullptr, *hd = nullptr;
-    float* part = nullptr;
+    double* part = nullptr;
     int32_t* counter = nullptr;
     int max_chunks = 0;
     // prefill staging
@@ -233,7 +233,7 @@ struct gsvcu_ctx {
     float* prof_ms = nullptr;  // accumulators [GSVCU_PROF_CLASSES] while profiling, else null
 
     // op-entry scratch
-    float* op_part = nullptr;
+    double* op_part = nullptr;
     int32_t* op_counter = nullptr;
     size_t op_part_n = 0, op_counter_n = 0;
 
@@ -415,7 +415,7 @@ int gsvcu_ctx::reserve(int slots, int ctx, int kvd) {
         {(void**)&xq, M * D}, {(void**)&aq, M * D}, {(void**)&n1q, M * D}, {(void**)&hq, M * FF},
         {(void**)&xd, M * D / QK * 2}, {(void**)&ad, M * D / QK * 2}, {(void**)&n1d, M * D / QK * 2},
         {(void**)&hd, M * FF / QK * 2},
-        {(void**)&part, (size_t)max_slots * NH * max_chunks * (2 + HD) * 4},
+        {(void**)&part, (size_t)max_slots * NH * max_chunks * (2 + HD) * 8},
         {(void**)&counter, (size_t)max_slots * NH * 4},
         {(void**)&p_ids, M * 4}, {(void**)&p_pepos, M * 4}, {(void**)&p_istext, M * 4},
         {(void**)&p_tslot, M * 4}, {(void**)&p_tpos, M * 4}, {(void**)&p_rowT, M * 4}, {(void**)&p_rowoff, M * 8},
@@ -1198,7 +1198,7 @@ int gsvcu_op_decode_attention(gsvcu_ctx* ctx, const float* q_dev, int32_t q_stri
         }
         ctx->op_part = nullptr;
         ctx->op_part_n = 0;
-        CKC(ctx, cudaMalloc((void**)&ctx->op_part, need_part * 4));
+        CKC(ctx, cudaMalloc((void**)&ctx->op_part, need_part * 8));
         ctx->op_part_n = need_part;
     }
     if (need_cnt > ctx->op_counter_n) {

@@ -83,7 +83,7 @@ struct DecAttnParams {
     int8_t* out_q = nullptr;
     uint16_t* out_d = nullptr;
     float* out_f32 = nullptr;
-    float* part = nullptr;               // scratch [B][NH][max_chunks][2 + HD]
+    double* part = nullptr;              // scratch [B][NH][max_chunks][2 + HD]: m, l, o[HD]
     int32_t* counter = nullptr;          // scratch [B][NH], zero between launches
 };
 void launch_decode_attention(const DecAttnParams& p, cudaStream_t s);

@@ -29,6 +29,11 @@ __device__ __forceinline__ float key2f(uint32_t k) {
     return __uint_as_float(u);
 }
 
+// expf / logf of the reference sampler (glibc, near correctly rounded) evaluated through double and
+// rounded once: equal to glibc's results except in the rare inputs where those are not correctly rounded.
+__device__ __forceinline__ float exp_f(float x) { return (float)exp((double)x); }
+__device__ __forceinline__ float log_f(float x) { return (float)log((double)x); }
+
 __device__ __forceinline__ uint64_t xs_step(uint64_t s) {
     s ^= s >> 12;
     s ^= s << 25;
@@ -97,7 +102,7 @@ __global__ void __launch_bounds__(SAMP_T) k_sampler(const SamplerParams p) {
         }
         __syncthreads();
         const float mx = sv[0];
-        for (int k = tid; k < V; k += SAMP_T) pr[k] = expf(__fsub_rn(sv[k], mx));
+        for (int k = tid; k < V; k += SAMP_T) pr[k] = exp_f(__fsub_rn(sv[k], mx));
         __syncthreads();
         if (tid == 0) {
             float sum = 0.0f;
@@ -178,7 +183,7 @@ __global__ void __launch_bounds__(SAMP_T) k_sampler(const SamplerParams p) {
     mx = red[0];
 #pragma unroll
     for (int w = 1; w < SAMP_T / 32; w++) mx = fmaxf(mx, red[w]);
-    for (int i = tid; i < VMAX; i += SAMP_T) pr[i] = (i < V && lg[i] != -INFINITY) ? expf(__fsub_rn(lg[i], mx)) : 0.0f;
+    for (int i = tid; i < VMAX; i += SAMP_T) pr[i] = (i < V && lg[i] != -INFINITY) ? exp_f(__fsub_rn(lg[i], mx)) : 0.0f;
     __syncthreads();
 
     if (warp == 0) {
@@ -214,7 +219,7 @@ __global__ void __launch_bounds__(SAMP_T) k_sampler(const SamplerParams p) {
             const float pi = __fmul_rn(pr[i], inv);
             float v = 0.0f;
             if (pi > 0.0f) {
-                const float q = -logf(__fsub_rn(1.0f, U));
+                const float q = -log_f(__fsub_rn(1.0f, U));
                 v = __fdiv_rn(pi, q);
             }
             if (best_i == 0x7fffffff || v > best_v) {   // first element of the range, then strict >

@@ -17,8 +17,9 @@
 //     accumulated in float block by block as sumf = fma((float)sumi, d_w*d_x, sumf).
 //   * F32 mul_mat / F32 vec_dot: float products accumulated in double, rounded once
 //     (ggml_vec_dot_f32 scalar path).
-//   * flash_attn_ext (F32 K/V): per query, keys in order, online softmax with expf, masked keys
-//     skipped, S = S*ms + vs and VKQ = VKQ*ms + v*vs as fused multiply-adds, out = VKQ * (1/S).
+//   * flash_attn_ext (F32 K/V): scores s = (float)(double-accumulated q.k) * scale, masked keys
+//     skipped; softmax(s) V evaluated in double (double exp, double sums) and rounded once (an
+//     order-independent evaluation of ggml's float online softmax, see attn_row).
 //   * layernorm_affine (P:1535-1585): v = (x + r) + bias, mean / E[v^2] in double,
 //     var = E[v^2] - mean^2, inv = 1/sqrtf(var + eps), y = ((v - mean)*inv)*w + b.
 //   * add_act ReLU (P:1587-1620): y = max(a + b, 0).
@@ -216,32 +217,33 @@ void add_act(const float* a, const float* b, int64_t rows, int64_t n, int act, f
         }
 }
 
-// flash_attn_ext for one query row of one head (F32 K/V): keys in order, skip masked keys.
-// keep(k) decides visibility (the -inf/0 mask of src/gsv_ar.cpp:215-223, 450).
+// flash_attn_ext for one query row of one head (F32 K/V), masked keys skipped
+// (the -inf/0 mask of src/gsv_ar.cpp:215-223, 450; keep(k) decides visibility).
+// Scores follow ggml exactly: s = (float)(double-accumulated q.k) * scale. The softmax-weighted sum
+// softmax(s) V is then evaluated in double (weights exp(s - max) with the double exp, sums in double)
+// and rounded to float once. ggml's float online softmax is one float evaluation of the same
+// expression; this order-independent evaluation is what any other reduction order (split-KV chunks,
+// per-warp token groups) reproduces bit for bit after the final rounding.
 template <class Keep>
 void attn_row(const float* q, const float* K, const float* Vv, int64_t kstride, int64_t nk, int hd, float scale,
               Keep keep, float* out) {
-    float M = -INFINITY, S = 0.0f;
-    float acc[256];
-    for (int d = 0; d < hd; d++) acc[d] = 0.0f;
+    std::vector<float> sc((size_t)nk);
+    float M = -INFINITY;
     for (int64_t ic = 0; ic < nk; ic++) {
         if (!keep(ic)) continue;
-        const float s = vec_dot_f32(hd, q, K + ic * kstride) * scale;
-        const float Mold = M;
-        float ms = 1.0f, vs = 1.0f;
-        if (s > M) {
-            M = s;
-            ms = std::exp(Mold - M);
-            for (int d = 0; d < hd; d++) acc[d] *= ms;
-        } else {
-            vs = std::exp(s - M);
-        }
-        const float* v = Vv + ic * kstride;
-        for (int d = 0; d < hd; d++) acc[d] = std::fmaf(v[d], vs, acc[d]);
-        S = std::fmaf(S, ms, vs);
+        sc[ic] = vec_dot_f32(hd, q, K + ic * kstride) * scale;
+        M = std::max(M, sc[ic]);
     }
-    const float S_inv = S == 0.0f ? 0.0f : 1.0f / S;
-    for (int d = 0; d < hd; d++) out[d] = acc[d] * S_inv;
+    double l = 0.0, acc[256];
+    for (int d = 0; d < hd; d++) acc[d] = 0.0;
+    for (int64_t ic = 0; ic < nk; ic++) {
+        if (!keep(ic)) continue;
+        const double p = std::exp((double)sc[ic] - (double)M);
+        l += p;
+        const float* v = Vv + ic * kstride;
+        for (int d = 0; d < hd; d++) acc[d] += p * (double)v[d];
+    }
+    for (int d = 0; d < hd; d++) out[d] = l > 0.0 ? (float)(acc[d] / l) : 0.0f;
 }
 
 // ------------------------------------------------------------------ sampler (src/gsv_sampler.cpp)

@@ -178,9 +178,10 @@ def test_decode_attention_paged(ctx, kv_dtype):
     kk, vv = gather_kv(pool, bt, lens, layer)
     ref = O.decode_attention(q[:, :512].reshape(B, 16, 32), kk, vv, np.array(lens, np.int32),
                              1.0 / np.sqrt(np.float32(32))).reshape(B, 512)
-    for b in range(B - 1):
-        err = np.abs(got[b] - ref[b]).max()
-        assert err <= 2e-6 * max(1.0, np.abs(ref[b]).max()), (b, lens[b], err)
+    # order-independent evaluation on both sides: equal bit for bit (a double rounding tie could flip
+    # one last bit, vanishingly rarely)
+    mism = np.count_nonzero(got[:-1].view(np.uint32) != ref[:-1].view(np.uint32))
+    assert mism <= 2, (mism, np.abs(got[:-1] - ref[:-1]).max())
     assert np.all(got[-1] == -5.0) and np.all(out_q.cpu().numpy()[-1] == 77)
     rq, rd = split_blocks(O.quantize_q8_0(got[:-1]), B - 1, 512)
     assert np.array_equal(out_q.cpu().numpy()[:-1], rq)
@@ -201,8 +202,8 @@ def test_prefill_attention_prefix_mask(ctx):
     ctx.op_prefill_attention(dev(qkv), start, seq_len, text_len, out_q, out_d, out_f)
     got = out_f.cpu().numpy()
     ref = O.prefill_attention(qkv, seq_len, text_len, 16, 32, 1.0 / np.sqrt(np.float32(32)))
-    # same key order and double-accumulated scores as the oracle; only expf ulps can differ
-    np.testing.assert_allclose(got, ref, rtol=2e-6, atol=2e-6)
+    mism = np.count_nonzero(got.view(np.uint32) != ref.view(np.uint32))
+    assert mism <= 2, (mism, np.abs(got - ref).max())
     rq, rd = split_blocks(O.quantize_q8_0(got), M, 512)
     assert np.array_equal(out_q.cpu().numpy(), rq)
 
