@@ -969,10 +969,11 @@ int gsvcu_first_logits(gsvcu_ctx* ctx, const gsvcu_request* reqs, int32_t B, flo
     int rc = rc0;
     const int V = ctx->hp.vocab_size;
     for (int b = 0; b < B && rc == GSVCU_OK; b++) {
-        cudaError_t e = cudaMemcpy(logits_out + (size_t)b * V, ctx->logits + (size_t)slots[b] * V, (size_t)V * 4,
-                                   cudaMemcpyDeviceToHost);
+        cudaError_t e = cudaMemcpyAsync(logits_out + (size_t)b * V, ctx->logits + (size_t)slots[b] * V, (size_t)V * 4,
+                                        cudaMemcpyDeviceToHost, ctx->stream);
         if (e != cudaSuccess) rc = ctx->fail(GSVCU_ERR_CUDA, cudaGetErrorString(e));
     }
+    if (rc == GSVCU_OK && cudaStreamSynchronize(ctx->stream) != cudaSuccess) rc = ctx->fail(GSVCU_ERR_CUDA, "sync");
     for (int sl : slots) ctx->release_slot(sl);
     return rc;
 }
@@ -1004,8 +1005,9 @@ int gsvcu_generate(gsvcu_ctx* ctx, const gsvcu_request* reqs, int32_t B, const g
             const SlotState& s = ctx->h_st[slots[b]];
             const int ns = s.n_samp;
             if (ns > 0) {
-                cudaError_t e = cudaMemcpy(gen.data(), ctx->out_tokens + (size_t)slots[b] * ctx->tok_cap,
-                                           (size_t)ns * 4, cudaMemcpyDeviceToHost);
+                cudaError_t e = cudaMemcpyAsync(gen.data(), ctx->out_tokens + (size_t)slots[b] * ctx->tok_cap,
+                                                (size_t)ns * 4, cudaMemcpyDeviceToHost, ctx->stream);
+                if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
                 if (e != cudaSuccess) { rc = ctx->fail(GSVCU_ERR_CUDA, cudaGetErrorString(e)); break; }
             }
             const int kind = s.finish_kind < 0 ? 2 : s.finish_kind;
@@ -1044,10 +1046,11 @@ int gsvcu_debug_trace(gsvcu_ctx* ctx, const gsvcu_request* reqs, int32_t B, cons
     std::vector<int> slots;
     TRY(ctx->admit(reqs, B, sd.data(), nullptr, n_steps + 1, -1, true, forced, n_steps, true, slots, dump));
     const int V = ctx->hp.vocab_size;
-    auto fetch_logits = [&](int row) -> int {
+    auto fetch_logits = [&](int row) -> int {   // ordered after the step on the context's stream
         for (int b = 0; b < B; b++)
-            CKC(ctx, cudaMemcpy(logits_out + ((size_t)row * B + b) * V, ctx->logits + (size_t)slots[b] * V,
-                                (size_t)V * 4, cudaMemcpyDeviceToHost));
+            CKC(ctx, cudaMemcpyAsync(logits_out + ((size_t)row * B + b) * V, ctx->logits + (size_t)slots[b] * V,
+                                     (size_t)V * 4, cudaMemcpyDeviceToHost, ctx->stream));
+        CKC(ctx, cudaStreamSynchronize(ctx->stream));
         return GSVCU_OK;
     };
     int rc = fetch_logits(0);
@@ -1099,8 +1102,9 @@ int gsvcu_serve_step(gsvcu_ctx* ctx, int32_t n_steps, gsvcu_finished* done, int3
         f.n_generated = s.finish_kind == 2 ? s.max_steps : s.finish_idx;
         f.n_tokens = 0;
         if (tokens && keep > 0 && used + keep <= tok_cap) {
-            CKC(ctx, cudaMemcpy(tokens + used, ctx->out_tokens + (size_t)sl * ctx->tok_cap, (size_t)keep * 4,
-                                cudaMemcpyDeviceToHost));
+            CKC(ctx, cudaMemcpyAsync(tokens + used, ctx->out_tokens + (size_t)sl * ctx->tok_cap, (size_t)keep * 4,
+                                     cudaMemcpyDeviceToHost, ctx->stream));
+            CKC(ctx, cudaStreamSynchronize(ctx->stream));
             f.n_tokens = keep;
             used += keep;
         }
