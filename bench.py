@@ -42,7 +42,68 @@ def parse():
     ap.add_argument("--refill-every", type=int, default=16)
     ap.add_argument("--kv", default="f16", choices=["f16", "f32"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="serve", choices=["serve", "attn"],
+                    help="serve: config-4 serving shard (the bench line); attn: config-3 decode-attention sweep")
+    ap.add_argument("--attn-batches", default="1,8,32,64,128")
     return ap.parse_args()
+
+
+def attn_sweep(args):
+    """decode attention alone, B in {1,8,32,64,128}, per-sequence lengths U[256,2048],
+    one layer of a paged F16 (or F32) pool, q ~ N(0,1). Prints one JSON line per B with the achieved
+    algorithmic GB/s (K+V rows of every key + q in + Q8_0 out) against the measured HBM peak."""
+    import torch
+    import gsvcu
+    ctx = gsvcu.Context(0)
+    kv = gsvcu.KV_F16 if args.kv == "f16" else gsvcu.KV_F32
+    elem = 2 if kv == gsvcu.KV_F16 else 4
+    peak, peak_kind = measured_peaks()
+    for B in [int(b) for b in args.attn_batches.split(",")]:
+        rng = np.random.default_rng(B)
+        lens = rng.integers(256, 2049, B)
+        pages = [(int(l) + 63) // 64 for l in lens]
+        maxp = max(pages) + 1
+        npages = sum(pages) + 1
+        dt = torch.float16 if kv == gsvcu.KV_F16 else torch.float32
+        pool = torch.randn((npages, 1, 2, 16, 64, 32), device="cuda", dtype=torch.float32).to(dt)
+        perm = torch.randperm(npages, device="cpu").numpy().astype(np.int32)
+        bt = np.zeros((B, maxp), np.int32)
+        at = 0
+        for b, n in enumerate(pages):
+            bt[b, :n] = perm[at:at + n]
+            at += n
+        q = torch.randn((B, 512), device="cuda")
+        kvpos = torch.tensor(lens - 1, dtype=torch.int32, device="cuda")
+        active = torch.ones(B, dtype=torch.int32, device="cuda")
+        btd = torch.from_numpy(bt).cuda()
+        oq = torch.empty((B, 512), dtype=torch.int8, device="cuda")
+        od = torch.empty((B, 16), dtype=torch.int16, device="cuda")
+        ext = torch.cuda.ExternalStream(ctx.stream_handle())
+        call = lambda: ctx.op_decode_attention(q, 512, pool, kv, 1, 0, btd, maxp, kvpos, active, B, oq, od)
+        for _ in range(args.warmup):
+            call()
+        ctx.sync()
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")   # > L2 between timed launches
+        times = []
+        for _ in range(max(args.steps, 5)):
+            flush.zero_()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(ext)
+            call()
+            e1.record(ext)
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1))
+        ms = float(np.median(times))
+        keys = int(lens.sum())
+        nbytes = keys * 2 * 512 * elem + B * (512 * 4 + 512 + 32)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        print(json.dumps({"workload": "cfg3 decode attention", "B": B, "kv": args.kv, "keys": keys,
+                          "algorithmic_bytes": nbytes, "ms": ms, "GBps": gbs, "peak": peak, "peak_kind": peak_kind,
+                          "frac": gbs / peak, "l2": "256 MiB flush between launches"}))
+        del pool, flush
+        torch.cuda.empty_cache()
+    ctx.close()
 
 
 class RequestStream:
@@ -165,8 +226,10 @@ def traffic_per_key():
 
 def cpu_baseline(args, job_tokens, job_seqs):
     """The oracle (CPU restatement of the reference's ggml CPU path) on a bounded sample of the job:
-    16 config-4 sequences, prefill timed, then 8 decode steps timed; the job's time is extrapolated
-    from the measured per-sequence prefill cost and per-token decode cost."""
+    16 config-4 sequences; generate with 1 and with 9 decode steps (both include the same prefill),
+    so per-token decode = (t9 - t1) / (16 * 8) and per-sequence prefill = t1 / 16 (its single decode
+    step is charged to prefill, slightly against the CPU). The job's time is extrapolated from these
+    measured costs for the job's sequence and token counts."""
     import gsv_synth as S
     import oracle as O
     model = S.cached_model(MODEL_CACHE, seed=0, n_layer=24)
@@ -175,21 +238,22 @@ def cpu_baseline(args, job_tokens, job_seqs):
     orc = O.OracleModel(model)
     stream = RequestStream(99, 0)
     reqs = [stream.next()[0] for _ in range(16)]
+    seeds = list(range(16))
+    orc.generate(reqs[:2], seeds=seeds[:2], max_steps=2)   # warm caches / thread pool
     t0 = time.perf_counter()
-    orc.first_logits(reqs)
-    t_prefill = time.perf_counter() - t0
+    orc.generate(reqs, seeds=seeds, max_steps=1)
+    t1 = time.perf_counter() - t0
     steps = 8
     t0 = time.perf_counter()
-    orc.generate(reqs, seeds=list(range(16)), max_steps=steps + 1)
-    t_gen = time.perf_counter() - t0
-    per_seq_prefill = t_prefill / len(reqs)
-    per_token_decode = max(t_gen - t_prefill, 1e-9) / (len(reqs) * steps)
+    orc.generate(reqs, seeds=seeds, max_steps=1 + steps)
+    t9 = time.perf_counter() - t0
+    per_seq_prefill = t1 / len(reqs)
+    per_token_decode = max(t9 - t1, 1e-6) / (len(reqs) * steps)
     est = job_seqs * per_seq_prefill + job_tokens * per_token_decode
     return {"value": job_tokens / est, "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"16 config-4 sequences (prefill {t_prefill:.1f} s) + {steps} decode steps at B=16 "
-                      f"({t_gen - t_prefill:.1f} s) on {cores} threads; job time extrapolated for "
-                      f"{job_seqs} prefills + {job_tokens} tokens",
-            "sample_seconds": round(t_prefill + t_gen, 2)}
+            "sample": f"16 config-4 sequences at B=16 on {cores} threads: prefill+1 step {t1:.1f} s, "
+                      f"+{steps} decode steps {t9 - t1:.1f} s; job time extrapolated for {job_seqs} prefills "
+                      f"+ {job_tokens} tokens"}
 
 
 def main():
@@ -198,6 +262,11 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     n_gpus = max(args.gpus, world)
+
+    if args.workload == "attn":
+        if rank == 0:
+            attn_sweep(args)
+        return
 
     if args.impl == "reference":
         if rank != 0:
