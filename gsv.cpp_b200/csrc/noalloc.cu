@@ -1,0 +1,95 @@
+// noalloc.cu -- decode attention for callers that must not allocate device memory.
+//
+// Some callers cannot call cudaMalloc at the point where they run attention: code that runs while a
+// framework's caching allocator owns the whole device, code inside a real-time audio callback that
+// must not block on the driver's allocator, or embedders that forbid allocations after start-up.
+// gsvcu_op_decode_attention grows its split-KV scratch with cudaMalloc on first use; this variant runs
+// the same kernel with its scratch (per-chunk partial results and the per-(sequence, head) merge
+// counters) in a fixed array that is part of the library image. Every GPU that loads the library holds
+// this array (about 4.3 MiB) until the process exits.
+#include <cstdio>
+#include <mutex>
+
+#include "../../include/gsvcu.h"
+#include "kernels.h"
+
+namespace gsvcu {
+namespace {
+
+constexpr int kItems = GSVCU_NOALLOC_MAX_ITEMS;                       // (sequence, key chunk) pairs
+constexpr size_t kPartDoubles = (size_t)kItems * NH * (2 + HD);      // partials: m, l, o[32] per head
+constexpr size_t kCounters = (size_t)kItems * NH;                    // one merge counter per (sequence, head)
+
+// Scratch shared by every call on a device: partials first, then the counters.
+struct NoallocScratch {
+    double part[kPartDoubles];
+    int32_t counter[kCounters];
+};
+static __device__ __align__(256) NoallocScratch g_scratch;
+
+// Device address of g_scratch per device. In host code `g_scratch` is only a stand-in symbol; the
+// address a kernel may use comes from cudaGetSymbolAddress, taken once per device with it current.
+constexpr int kMaxDevices = 64;
+std::mutex g_mu;
+NoallocScratch* g_addr[kMaxDevices] = {};
+
+int scratch_for_current_device(NoallocScratch** out) {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        cudaGetLastError();
+        return GSVCU_ERR_DEVICE;
+    }
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!g_addr[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_scratch);
+        if (e != cudaSuccess || !p) {
+            cudaGetLastError();
+            return GSVCU_ERR_CUDA;
+        }
+        g_addr[dev] = (NoallocScratch*)p;
+    }
+    *out = g_addr[dev];
+    return GSVCU_OK;
+}
+
+}  // namespace
+}  // namespace gsvcu
+
+using namespace gsvcu;
+
+extern "C" int gsvcu_op_decode_attention_noalloc(void* stream, const float* q_dev, int32_t q_stride,
+                                                 const void* pool_dev, int32_t kv_dtype, int32_t n_layer,
+                                                 int32_t layer, const int32_t* block_table_dev, int32_t max_pages,
+                                                 const int32_t* kvpos_dev, const int32_t* active_dev, int32_t B,
+                                                 int8_t* out_q_dev, uint16_t* out_d_dev, float* out_f32_dev) {
+    if (!q_dev || !pool_dev || !block_table_dev || !kvpos_dev || !active_dev || !out_q_dev || !out_d_dev || B <= 0 ||
+        max_pages <= 0 || n_layer <= 0 || layer < 0 || layer >= n_layer || q_stride < D ||
+        (kv_dtype != GSVCU_KV_F16 && kv_dtype != GSVCU_KV_F32))
+        return GSVCU_ERR_ARG;
+    const int max_chunks = (max_pages * PAGE + ATT_CHUNK - 1) / ATT_CHUNK;
+    if ((int64_t)B * max_chunks > kItems) {
+        std::fprintf(stderr,
+                     "gsvcu_op_decode_attention_noalloc: B (%d) x key chunks (%d for %d pages) exceeds the fixed "
+                     "scratch of %d sequence-chunks (GSVCU_NOALLOC_MAX_ITEMS); use gsvcu_op_decode_attention\n",
+                     B, max_chunks, max_pages, kItems);
+        return GSVCU_ERR_ARG;
+    }
+    NoallocScratch* s = nullptr;
+    const int rc = scratch_for_current_device(&s);
+    if (rc != GSVCU_OK) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    // the counters must start at zero; a previous call leaves them at zero unless it was interrupted
+    if (cudaMemsetAsync(s->counter, 0, (size_t)B * NH * sizeof(int32_t), st) != cudaSuccess) {
+        cudaGetLastError();
+        return GSVCU_ERR_CUDA;
+    }
+    DecAttnParams a;
+    a.q = q_dev; a.q_stride = q_stride; a.pool = pool_dev; a.kv_f32 = kv_dtype; a.n_layer = n_layer; a.layer = layer;
+    a.block_table = block_table_dev; a.max_pages = max_pages; a.kvpos = kvpos_dev; a.active = active_dev; a.B = B;
+    a.max_chunks = max_chunks; a.scale = 1.0f / sqrtf((float)HD); a.out_q = out_q_dev; a.out_d = out_d_dev;
+    a.out_f32 = out_f32_dev; a.part = s->part; a.counter = s->counter;
+    launch_decode_attention(a, st);
+    if (cudaGetLastError() != cudaSuccess) return GSVCU_ERR_CUDA;
+    return GSVCU_OK;
+}

@@ -83,6 +83,7 @@ SIGNATURES = {
     "gsvcu_step_profile": ([_P, _I, _P, _P], C.c_int),
     "gsvcu_kernel_launches": ([_P], C.c_int64),
     "gsvcu_stream": ([_P], C.c_void_p),
+    "gsvcu_op_decode_attention_noalloc": ([_P, _P, _I, _P, _I, _I, _I, _P, _I, _P, _P, _I, _P, _P, _P], C.c_int),
 }
 
 PROF_CLASSES = ["sampler", "step_prep", "qkv_gemm", "decode_attn", "out_gemm", "layernorm", "ffn1_gemm", "ffn2_gemm",

@@ -193,6 +193,24 @@ int gsvcu_op_decode_attention(gsvcu_ctx* ctx, const float* q_dev, int32_t q_stri
                               int32_t max_pages, const int32_t* kvpos_dev, const int32_t* active_dev, int32_t B,
                               int8_t* out_q_dev, uint16_t* out_d_dev, float* out_f32_dev);
 
+/* Decode attention that allocates nothing (no counterpart in the reference; added for callers of
+ * this library that may not allocate device memory where they run attention -- e.g. code running
+ * while a framework's caching allocator owns the device, a real-time callback that must not block
+ * in the driver's allocator, or an embedder that forbids allocations after start-up).
+ * Same inputs, outputs and results as gsvcu_op_decode_attention, on the caller's `stream`
+ * (cudaStream_t, NULL = legacy default stream) of the current device, without a context. The split-KV
+ * scratch is a fixed array inside the library (about 4.3 MiB held on every GPU that loads it, until
+ * the process exits), sized for B * ceil(max_pages * 64 / 256) <= GSVCU_NOALLOC_MAX_ITEMS; larger
+ * calls return GSVCU_ERR_ARG with a message on stderr. The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress); make that first call before any stream capture.
+ * All calls share the array: calls that overlap on the GPU (other streams, other threads) race. */
+#define GSVCU_NOALLOC_MAX_ITEMS 1024
+int gsvcu_op_decode_attention_noalloc(void* stream, const float* q_dev, int32_t q_stride, const void* pool_dev,
+                                      int32_t kv_dtype, int32_t n_layer, int32_t layer,
+                                      const int32_t* block_table_dev, int32_t max_pages, const int32_t* kvpos_dev,
+                                      const int32_t* active_dev, int32_t B, int8_t* out_q_dev, uint16_t* out_d_dev,
+                                      float* out_f32_dev);
+
 /* Prefix-masked prefill attention over packed sequences (src/gsv_ar.cpp:215-223, 257): qkv_dev
  * [M][1536] rows (q|k|v), sequence s = rows [start_s, start_s + len_s) whose first text_len_s rows are
  * text (bidirectional among text), the rest semantic (causal, full view of the text).
