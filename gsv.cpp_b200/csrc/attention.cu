@@ -11,203 +11,303 @@
 namespace gsvcu {
 
 // ------------------------------------------------------------------ decode
-// Work item = (slot, head, chunk of ATT_CHUNK keys), one warp each, 4 heads per CTA.
-// K/V rows of one head are 32 contiguous elements inside a 64-token page, so a warp reads
-// TPI tokens x 64 B (F16) per 128-bit load instruction; U loads of K and U of V are in flight per
-// lane, a block of TPI*U (32 for F16) tokens per iteration.
+// Work item = (slot, head, 64-key page), one warp each, 4 heads (warps) per CTA. Lane 0 stages the
+// head's K and V rows of the page into shared memory with two TMA bulk copies (cp.async.bulk, no
+// multicast) completing on one mbarrier; the warp then reads them from shared memory.
 //
-// Arithmetic: scores s = (float)(double sum of float products) * scale, as ggml's vec_dot_f32; the
-// softmax-weighted sum is carried in double: per block of tokens the warp-uniform running max m is
-// raised to the block max (rescaling l and o by exp(m_old - m_new)), lane j computes the weight
-// p_j = exp(s_j - m) of token j once, and each lane accumulates o += p * v for its dims. The result
-// (float)(o / l) is exact to ~1e-16 before the final rounding, so it does not depend on the
-// reduction order (token groups, split-KV chunks) and equals the oracle's evaluation bit for bit.
-// Chunks of one (slot, head) are merged by the last warp to finish (atomic ticket, no waiting).
+// Arithmetic: a fixed float evaluation order, restated operation for operation by the CPU oracle
+// (decode_attention_canonical), so the two agree bit for bit. Lane l = 4*g + s owns dims 8s..8s+7 and
+// the keys t = 8u + g (u = 0..7) of its page ("token group" g):
+//   score    D_s = fma chain over the lane's 8 dims from 0; dot = (D0 + D1) + (D2 + D3); s_t = dot*scale
+//   page max m = max_t s_t;  p_t = exp_c(s_t - m)   (exp_c below: own float exp, same on the CPU)
+//   sums     L_g = sum over u of p_t (ascending u), O_g[d] = fma chain p_t * v_t[d] (ascending u), then
+//            l = ((L0+L1)+(L2+L3))+((L4+L5)+(L6+L7)), o[d] likewise
+//   merge    over the pages c = 0..n-1 in order: M = max m_c, w = exp_c(m_c - M),
+//            L = fma(w, l_c, L), O[d] = fma(w, o_c[d], O[d]); out = O / L.
+// Pages of one (slot, head) are merged by the last warp to finish (atomic ticket, no waiting).
+
+// exp(x) for x <= 0 in float: Cody-Waite reduction x = n*ln2 + r (ln2 split into a 15-bit head and a
+// float tail, so n*head is exact) and the degree-7 Taylor polynomial of exp(r), |r| <= ln2/2, by Horner
+// with fma; result p * 2^n. Max error ~1.2 ulp. x < -87 (or -inf) gives 0.
+__device__ __forceinline__ float exp_c(float x) {
+    if (!(x >= -87.0f)) return 0.0f;
+    const float n = rintf(__fmul_rn(x, 0x1.715476p+0f));   // x / ln2, to nearest even
+    float r = fmaf(-n, 0x1.62e4p-1f, x);
+    r = fmaf(-n, 0x1.7f7d1cp-20f, r);
+    float p = 0x1.a01a02p-13f;                              // 1/7!
+    p = fmaf(p, r, 0x1.6c16c2p-10f);                        // 1/6!
+    p = fmaf(p, r, 0x1.111112p-7f);                         // 1/5!
+    p = fmaf(p, r, 0x1.555556p-5f);                         // 1/4!
+    p = fmaf(p, r, 0x1.555556p-3f);                         // 1/3!
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    return __fmul_rn(p, __int_as_float(((int)n + 127) << 23));
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+// Bulk global -> shared copy completing on an mbarrier (no multicast).
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait for phase 0 of an mbarrier; warp-uniform result (false: the limit was reached).
+constexpr uint32_t MBAR_POLL_LIMIT = 1u << 22;
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar) {
+    uint32_t it = 0;
+    while (!mbar_try_wait(bar, 0)) {
+        if (++it == MBAR_POLL_LIMIT) break;
+    }
+    return __all_sync(0xffffffffu, it < MBAR_POLL_LIMIT);
+}
+
+// 8 consecutive values of a K/V row slice from shared memory, as floats.
 template <typename KT>
-__global__ void __launch_bounds__(128) k_decode_attn(const DecAttnParams p) {
-    constexpr int EPL = 16 / sizeof(KT);     // elements per lane per load
-    constexpr int LPT = HD / EPL;            // lanes per token
-    constexpr int TPI = 32 / LPT;            // tokens per warp-load
-    constexpr int U = 4;                     // loads in flight per lane (per K and per V)
-    constexpr int BLK = TPI * U;             // tokens per block (<= 32)
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int slot = blockIdx.z, chunk = blockIdx.y, h = blockIdx.x * 4 + warp;
-    int kvpos;
-    bool act;
-    if (p.st) {
-        act = p.st[slot].decode_now != 0;
-        kvpos = p.st[slot].kvpos;
+__device__ __forceinline__ void load8(const uint8_t* p, float (&f)[8]) {
+    if (sizeof(KT) == 2) {
+        const uint4 r = *(const uint4*)p;
+        const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            f[2 * i] = __half2float(__ushort_as_half((unsigned short)(w[i] & 0xffffu)));
+            f[2 * i + 1] = __half2float(__ushort_as_half((unsigned short)(w[i] >> 16)));
+        }
     } else {
-        act = p.active[slot] != 0;
-        kvpos = p.kvpos[slot];
+        const float4 a = *(const float4*)p, b = *(const float4*)(p + 16);
+        f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+        f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
     }
-    if (!act) return;
-    const int nkeys = kvpos + 1, k0 = chunk * ATT_CHUNK;
-    if (k0 >= nkeys) return;
-    const int k1 = min(k0 + ATT_CHUNK, nkeys);
-    const int nch = (nkeys + ATT_CHUNK - 1) / ATT_CHUNK;
-    const int sub = lane % LPT, tk = lane / LPT;
+}
 
-    float q[EPL];
-    {
-        const float* qp = p.q + (size_t)slot * p.q_stride + h * HD + sub * EPL;
+// Out = o / l for the head, quantized to one Q8_0 block (the head's 32 values); lane (g, s) holds dims
+// 8s..8s+7, group g = 0 writes.
+__device__ __forceinline__ void decode_write_out(const DecAttnParams& p, int slot, int h, int g, int sub,
+                                                 const float (&o)[8], float l) {
+    float out[8], amax = 0.0f;
 #pragma unroll
-        for (int e = 0; e < EPL; e++) q[e] = qp[e];
-    }
-    const size_t page_elems = (size_t)p.n_layer * 2 * NH * PAGE * HD;
-    const size_t koff = ((size_t)p.layer * 2 + 0) * NH * PAGE * HD + (size_t)h * PAGE * HD + sub * EPL;
-    const size_t voff = koff + (size_t)NH * PAGE * HD;
-    const KT* pool = (const KT*)p.pool;
-    const int32_t* bt = p.block_table + (size_t)slot * p.max_pages;
-
-    float m = -INFINITY;      // warp-uniform running max
-    double l = 0.0, o[EPL];   // l: this lane's tokens; o: this lane's dims over its tokens
-#pragma unroll
-    for (int e = 0; e < EPL; e++) o[e] = 0.0;
-
-    for (int base = k0; base < k1; base += BLK) {
-        const size_t pbase = (size_t)bt[base / PAGE] * page_elems;
-        uint4 kr[U], vr[U];
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-            const int kk = base + u * TPI + tk;
-            kr[u] = make_uint4(0u, 0u, 0u, 0u);
-            vr[u] = kr[u];
-            if (kk < k1) {
-                const size_t r = pbase + (size_t)(kk % PAGE) * HD;
-                kr[u] = ldg_stream(pool + r + koff);
-                vr[u] = ldg_stream(pool + r + voff);
-            }
-        }
-        float sc[U];
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-            float kf[EPL];
-            if (sizeof(KT) == 2) {
-                const __half2* k2 = (const __half2*)&kr[u];
-#pragma unroll
-                for (int e = 0; e < EPL / 2; e++) {
-                    const float2 a = __half22float2(k2[e]);
-                    kf[2 * e] = a.x; kf[2 * e + 1] = a.y;
-                }
-            } else {
-                const float* k4 = (const float*)&kr[u];
-#pragma unroll
-                for (int e = 0; e < EPL; e++) kf[e] = k4[e];
-            }
-            double dot = 0.0;
-#pragma unroll
-            for (int e = 0; e < EPL; e++) dot += (double)__fmul_rn(q[e], kf[e]);
-#pragma unroll
-            for (int off = 1; off < LPT; off <<= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
-            const int kk = base + u * TPI + tk;
-            sc[u] = kk < k1 ? __fmul_rn((float)dot, p.scale) : -INFINITY;
-        }
-        // lane j (< BLK) takes the score of block token j = u*TPI + t, held by lane t*LPT
-        float mys = -INFINITY;
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-            const float t = __shfl_sync(0xffffffffu, sc[u], (lane % TPI) * LPT);
-            if (lane < BLK && lane / TPI == u) mys = t;
-        }
-        float bm = mys;
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, off));
-        if (bm > m) {   // warp-uniform
-            const double r = m == -INFINITY ? 0.0 : exp((double)m - (double)bm);
-            l *= r;
-#pragma unroll
-            for (int e = 0; e < EPL; e++) o[e] *= r;
-            m = bm;
-        }
-        const double pj = mys == -INFINITY ? 0.0 : exp((double)mys - (double)m);
-        l += pj;
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-            const double pu = __shfl_sync(0xffffffffu, pj, u * TPI + tk);
-            if (sizeof(KT) == 2) {
-                const __half2* v2 = (const __half2*)&vr[u];
-#pragma unroll
-                for (int e = 0; e < EPL / 2; e++) {
-                    const float2 b = __half22float2(v2[e]);
-                    o[2 * e] = fma(pu, (double)b.x, o[2 * e]);
-                    o[2 * e + 1] = fma(pu, (double)b.y, o[2 * e + 1]);
-                }
-            } else {
-                const float* v4 = (const float*)&vr[u];
-#pragma unroll
-                for (int e = 0; e < EPL; e++) o[e] = fma(pu, (double)v4[e], o[e]);
-            }
-        }
-    }
-    // sum the token groups (same m everywhere): o over lanes with the same dims, l over the warp
-#pragma unroll
-    for (int off = LPT; off < 32; off <<= 1) {
-#pragma unroll
-        for (int e = 0; e < EPL; e++) o[e] += __shfl_xor_sync(0xffffffffu, o[e], off);
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
-
-    if (nch > 1) {
-        double* part = p.part + (((size_t)slot * NH + h) * p.max_chunks) * (2 + HD);
-        if (tk == 0) {
-#pragma unroll
-            for (int e = 0; e < EPL; e++) part[(size_t)chunk * (2 + HD) + 2 + sub * EPL + e] = o[e];
-            if (sub == 0) {
-                part[(size_t)chunk * (2 + HD) + 0] = (double)m;
-                part[(size_t)chunk * (2 + HD) + 1] = l;
-            }
-        }
-        __threadfence();
-        __syncwarp();
-        int ticket = 0;
-        if (lane == 0) ticket = atomicAdd(p.counter + (size_t)slot * NH + h, 1);
-        ticket = __shfl_sync(0xffffffffu, ticket, 0);
-        if (ticket != nch - 1) return;
-        __threadfence();
-        double M = -INFINITY;
-        for (int c = 0; c < nch; c++) M = fmax(M, __ldcg(part + (size_t)c * (2 + HD)));
-        l = 0.0;
-#pragma unroll
-        for (int e = 0; e < EPL; e++) o[e] = 0.0;
-        for (int c = 0; c < nch; c++) {
-            const double mc = __ldcg(part + (size_t)c * (2 + HD));
-            const double w = mc == -INFINITY ? 0.0 : exp(mc - M);
-            l = fma(__ldcg(part + (size_t)c * (2 + HD) + 1), w, l);
-#pragma unroll
-            for (int e = 0; e < EPL; e++) o[e] = fma(__ldcg(part + (size_t)c * (2 + HD) + 2 + sub * EPL + e), w, o[e]);
-        }
-        if (lane == 0) p.counter[(size_t)slot * NH + h] = 0;   // ready for the next launch
-    }
-
-    // finalize and quantize the head's 32 values (one Q8_0 block)
-    float out[EPL], amax = 0.0f;
-#pragma unroll
-    for (int e = 0; e < EPL; e++) {
-        out[e] = l > 0.0 ? (float)(o[e] / l) : 0.0f;
+    for (int e = 0; e < 8; e++) {
+        out[e] = __fdiv_rn(o[e], l);
         amax = fmaxf(amax, fabsf(out[e]));
     }
-#pragma unroll
-    for (int off = 1; off < LPT; off <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
     float dsc, id;
     q8_scale(amax, dsc, id);
-    if (tk == 0) {
-        int8_t* qo = p.out_q + (size_t)slot * D + h * HD + sub * EPL;
+    if (g == 0) {
+        int8_t* qo = p.out_q + (size_t)slot * D + h * HD + sub * 8;
+        uint32_t w0 = 0, w1 = 0;
 #pragma unroll
-        for (int e = 0; e < EPL; e++) qo[e] = q8_val(out[e], id);
-        if (sub == 0) p.out_d[(size_t)slot * (D / QK) + h] = f2h(dsc);
+        for (int e = 0; e < 4; e++) {
+            w0 |= (uint32_t)(uint8_t)q8_val(out[e], id) << (8 * e);
+            w1 |= (uint32_t)(uint8_t)q8_val(out[e + 4], id) << (8 * e);
+        }
+        *(uint2*)qo = make_uint2(w0, w1);
+        if (sub == 0) p.out_d[(size_t)slot * (D / QK) + h] = l == l ? f2h(dsc) : (uint16_t)0x7e00u;
         if (p.out_f32) {
-#pragma unroll
-            for (int e = 0; e < EPL; e++) p.out_f32[(size_t)slot * D + h * HD + sub * EPL + e] = out[e];
+            float4* of = (float4*)(p.out_f32 + (size_t)slot * D + h * HD + sub * 8);
+            of[0] = make_float4(out[0], out[1], out[2], out[3]);
+            of[1] = make_float4(out[4], out[5], out[6], out[7]);
         }
     }
 }
 
-void launch_decode_attention(const DecAttnParams& p, cudaStream_t s) {
+__device__ __forceinline__ bool decode_slot(const DecAttnParams& p, int slot, int& kvpos) {
+    if (p.st) {
+        kvpos = p.st[slot].kvpos;
+        return p.st[slot].decode_now != 0;
+    }
+    kvpos = p.kvpos[slot];
+    return p.active[slot] != 0;
+}
+
+template <typename KT> struct DecShape {
+    static constexpr int ROWB = HD * (int)sizeof(KT);   // bytes per token row of one head
+    static constexpr int PGB = PAGE * ROWB;             // K (or V) bytes of one head in one page
+    static constexpr int WARPB = 2 * PGB;               // K + V rows of one warp
+    static constexpr size_t SMEM = (size_t)4 * WARPB + 4 * 8;   // 4 warps + 4 mbarriers
+};
+
+// One CTA per (4-head group, page, slot); warp = head. Pages of sequences longer than one page leave a
+// partial {m, l, -, -, o[32]} for k_decode_merge; one-page sequences are finished here.
+template <typename KT>
+__global__ void __launch_bounds__(128) k_decode_attn(const DecAttnParams p) {
+    using S = DecShape<KT>;
+    extern __shared__ __align__(128) uint8_t sm[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int slot = blockIdx.z, chunk = blockIdx.y, h = blockIdx.x * 4 + warp;
+    int kvpos;
+    if (!decode_slot(p, slot, kvpos)) return;
+    const int nkeys = kvpos + 1, k0 = chunk * PAGE;
+    if (k0 >= nkeys) return;
+    const int n = min(PAGE, nkeys - k0);
+    const int sub = lane & 3, g = lane >> 2;
+
+    uint8_t* ks = sm + (size_t)warp * S::WARPB;
+    uint8_t* vs = ks + S::PGB;
+    const uint32_t bar = smem_u32((uint64_t*)(sm + 4 * S::WARPB) + warp);
+    if (lane == 0) {
+        const int page = p.block_table[(size_t)slot * p.max_pages + chunk];
+        const KT* kp = (const KT*)p.pool + (size_t)page * p.n_layer * 2 * NH * PAGE * HD +
+                       ((size_t)p.layer * 2 * NH + h) * PAGE * HD;
+        const uint32_t bytes = (uint32_t)n * S::ROWB;
+        mbar_init(bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        mbar_expect_tx(bar, 2 * bytes);
+        bulk_g2s(smem_u32(ks), kp, bytes, bar);
+        bulk_g2s(smem_u32(vs), kp + (size_t)NH * PAGE * HD, bytes, bar);
+    }
+    float q[8];
+    {
+        const float4* qp = (const float4*)(p.q + (size_t)slot * p.q_stride + h * HD + sub * 8);
+        const float4 a = qp[0], b = qp[1];
+        q[0] = a.x; q[1] = a.y; q[2] = a.z; q[3] = a.w;
+        q[4] = b.x; q[5] = b.y; q[6] = b.z; q[7] = b.w;
+    }
+    __syncwarp();
+    if (!mbar_wait_bounded(bar)) {   // the page never arrived: flag it, drain (bounded), poison
+        if (lane == 0 && p.err) atomicExch(p.err, 1);
+        (void)mbar_wait_bounded(bar);
+    }
+
+    // scores of the lane's 8 keys t = 8u + g
+    float sc[8], m = -INFINITY;
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+        const int t = 8 * u + g;
+        float d = 0.0f;
+        if (t < n) {
+            float kf[8];
+            load8<KT>(ks + (size_t)t * S::ROWB + sub * 8 * sizeof(KT), kf);
+#pragma unroll
+            for (int e = 0; e < 8; e++) d = fmaf(q[e], kf[e], d);
+        }
+        d = __fadd_rn(d, __shfl_xor_sync(0xffffffffu, d, 1));
+        d = __fadd_rn(d, __shfl_xor_sync(0xffffffffu, d, 2));
+        sc[u] = t < n ? __fmul_rn(d, p.scale) : -INFINITY;
+        m = fmaxf(m, sc[u]);
+    }
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    // weights: lane (g, s) evaluates keys u = s and u = s + 4 of its group, then they are shared
+    float sa = sc[0], sb = sc[4];
+#pragma unroll
+    for (int u = 1; u < 4; u++)
+        if (sub == u) { sa = sc[u]; sb = sc[u + 4]; }
+    const float pa = exp_c(sa - m), pb = exp_c(sb - m);   // exp_c(-inf) = 0 for keys past the end
+    float l = 0.0f, o[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) o[e] = 0.0f;
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+        const float pu = __shfl_sync(0xffffffffu, u < 4 ? pa : pb, 4 * g + (u & 3));
+        const int t = 8 * u + g;
+        if (t < n) {
+            float vf[8];
+            load8<KT>(vs + (size_t)t * S::ROWB + sub * 8 * sizeof(KT), vf);
+            l = __fadd_rn(l, pu);
+#pragma unroll
+            for (int e = 0; e < 8; e++) o[e] = fmaf(pu, vf[e], o[e]);
+        }
+    }
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+        l = __fadd_rn(l, __shfl_xor_sync(0xffffffffu, l, off));
+#pragma unroll
+        for (int e = 0; e < 8; e++) o[e] = __fadd_rn(o[e], __shfl_xor_sync(0xffffffffu, o[e], off));
+    }
+    if (nkeys <= PAGE) {
+        decode_write_out(p, slot, h, g, sub, o, l);
+        return;
+    }
+    if (g == 0) {
+        float* part = p.part + (((size_t)slot * NH + h) * p.max_chunks + chunk) * PART_STRIDE;
+        __stcg((float4*)(part + 4 + sub * 8), make_float4(o[0], o[1], o[2], o[3]));
+        __stcg((float4*)(part + 8 + sub * 8), make_float4(o[4], o[5], o[6], o[7]));
+        if (sub == 0) __stcg((float2*)part, make_float2(m, l));
+    }
+}
+
+// Merge of the page partials of sequences longer than one page: warp per (slot, head), pages in
+// order (M = max m, w = exp_c(m - M), L = fma(w, l, L), O = fma(w, o, O)), 32 pages per batch staged
+// in shared memory by lane-parallel loads.
+__global__ void __launch_bounds__(128) k_decode_merge(const DecAttnParams p) {
+    __shared__ __align__(16) float sbuf[4][64 + 32 * 32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int item = blockIdx.x * 4 + warp;
+    if (item >= p.B * NH) return;
+    const int slot = item / NH, h = item % NH;
+    int kvpos;
+    if (!decode_slot(p, slot, kvpos)) return;
+    const int nch = (kvpos + PAGE) / PAGE;
+    if (nch <= 1) return;
+    const int sub = lane & 3, g = lane >> 2;
+    const float* part = p.part + (((size_t)slot * NH + h) * p.max_chunks) * PART_STRIDE;
+    float M = -INFINITY;
+    for (int c = lane; c < nch; c += 32) M = fmaxf(M, __ldcg(part + (size_t)c * PART_STRIDE));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    float* sw = sbuf[warp];          // [32] page weights
+    float* sl = sbuf[warp] + 32;     // [32] page sums
+    float* so = sbuf[warp] + 64;     // [32][32] page outputs
+    float L = 0.0f, O[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) O[e] = 0.0f;
+    for (int c0 = 0; c0 < nch; c0 += 32) {
+        const int cnt = min(32, nch - c0);
+        if (lane < cnt) {
+            const float2 ml = __ldcg((const float2*)(part + (size_t)(c0 + lane) * PART_STRIDE));
+            sw[lane] = exp_c(ml.x - M);
+            sl[lane] = ml.y;
+        }
+        for (int i = lane; i < cnt * 8; i += 32) {
+            const int c = i >> 3, j = i & 7;
+            *(float4*)(so + c * 32 + j * 4) = __ldcg((const float4*)(part + (size_t)(c0 + c) * PART_STRIDE + 4 + j * 4));
+        }
+        __syncwarp();
+        for (int c = 0; c < cnt; c++) {
+            const float w = sw[c];
+            L = fmaf(w, sl[c], L);
+            const float4 a = *(const float4*)(so + c * 32 + sub * 8), b = *(const float4*)(so + c * 32 + sub * 8 + 4);
+            O[0] = fmaf(w, a.x, O[0]); O[1] = fmaf(w, a.y, O[1]); O[2] = fmaf(w, a.z, O[2]); O[3] = fmaf(w, a.w, O[3]);
+            O[4] = fmaf(w, b.x, O[4]); O[5] = fmaf(w, b.y, O[5]); O[6] = fmaf(w, b.z, O[6]); O[7] = fmaf(w, b.w, O[7]);
+        }
+        __syncwarp();
+    }
+    decode_write_out(p, slot, h, g, sub, O, L);
+}
+
+cudaError_t attention_init_device() {
+    cudaError_t e = cudaFuncSetAttribute(k_decode_attn<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)DecShape<__half>::SMEM);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(k_decode_attn<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)DecShape<float>::SMEM);
+}
+
+int launch_decode_attention(const DecAttnParams& p, cudaStream_t s) {
     dim3 grid(NH / 4, p.max_chunks, p.B);
-    if (p.kv_f32) k_decode_attn<float><<<grid, 128, 0, s>>>(p);
-    else k_decode_attn<__half><<<grid, 128, 0, s>>>(p);
+    if (p.kv_f32) k_decode_attn<float><<<grid, 128, DecShape<float>::SMEM, s>>>(p);
+    else k_decode_attn<__half><<<grid, 128, DecShape<__half>::SMEM, s>>>(p);
+    if (p.max_chunks <= 1) return 1;
+    k_decode_merge<<<(p.B * NH + 3) / 4, 128, 0, s>>>(p);
+    return 2;
 }
 
 // ------------------------------------------------------------------ prefill
@@ -256,7 +356,7 @@ __global__ void __launch_bounds__(PREF_QTILE) k_prefill_attn(const PrefAttnParam
             if (!vis) continue;
             double dot = 0.0;
 #pragma unroll
-            for (int d = 0; d < HD; d++) dot += (double)__fmul_rn(q[d], Ks[j][d]);
+            for (int d = 0; d < HD; d++) dot = fma((double)q[d], (double)Ks[j][d], dot);
             const float s = __fmul_rn((float)dot, p.scale);
             if (s > m) {
                 const double r = m == -INFINITY ? 0.0 : exp((double)m - (double)s);

@@ -17,7 +17,6 @@ constexpr int HD = 32;        // head dim = one Q8_0 block
 constexpr int FF = 2048;      // FFN width (4 D)
 constexpr int QK = 32;        // Q8_0 block
 constexpr int PAGE = 64;      // tokens per KV page
-constexpr int ATT_CHUNK = 256;  // keys per split-KV work item of decode attention
 constexpr int HIST = 4096;    // repetition-penalty window (src/gsv_ar.cpp:769-771)
 
 __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }

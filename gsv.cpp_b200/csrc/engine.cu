@@ -209,8 +209,7 @@ struct gsvcu_ctx {
     float *x = nullptr, *qkv = nullptr, *pre = nullptr, *n1 = nullptr, *attn_f32 = nullptr;
     int8_t *xq = nullptr, *aq = nullptr, *n1q = nullptr, *hq = nullptr;
     uint16_t *xd = nullptr, *ad = nullptr, *n1d = nullptr, *hd = nullptr;
-    double* part = nullptr;
-    int32_t* counter = nullptr;
+    float* part = nullptr;
     int max_chunks = 0;
     // prefill staging
     int32_t *p_ids = nullptr, *p_pepos = nullptr, *p_istext = nullptr, *p_tslot = nullptr, *p_tpos = nullptr,
@@ -233,9 +232,10 @@ struct gsvcu_ctx {
     float* prof_ms = nullptr;  // accumulators [GSVCU_PROF_CLASSES] while profiling, else null
 
     // op-entry scratch
-    double* op_part = nullptr;
-    int32_t* op_counter = nullptr;
-    size_t op_part_n = 0, op_counter_n = 0;
+    float* op_part = nullptr;
+    size_t op_part_n = 0;
+    // set by decode attention when a bounded wait for its staged K/V gave up (checked on status reads)
+    int32_t* att_err = nullptr;
 
     ~gsvcu_ctx();
     int load(const char* path);
@@ -286,7 +286,7 @@ gsvcu_ctx::~gsvcu_ctx() {
     free_cache();
     for (void* p : wallocs) cudaFree(p);
     if (op_part) cudaFree(op_part);
-    if (op_counter) cudaFree(op_counter);
+    if (att_err) cudaFree(att_err);
     for (cudaEvent_t e : prof_ev)
         if (e) cudaEventDestroy(e);
     if (stream) cudaStreamDestroy(stream);
@@ -394,7 +394,7 @@ int gsvcu_ctx::reserve(int slots, int ctx, int kvd) {
     kv_f32 = kvd;
     max_pages = (ctx + PAGE - 1) / PAGE;
     n_pages = max_slots * max_pages;
-    max_chunks = (ctx + ATT_CHUNK - 1) / ATT_CHUNK;
+    max_chunks = decode_chunks(ctx);
     tok_cap = ctx;
     forced_cap = ctx;
     Mmax = std::max(PREFILL_ROWS, max_slots);
@@ -415,8 +415,7 @@ int gsvcu_ctx::reserve(int slots, int ctx, int kvd) {
         {(void**)&xq, M * D}, {(void**)&aq, M * D}, {(void**)&n1q, M * D}, {(void**)&hq, M * FF},
         {(void**)&xd, M * D / QK * 2}, {(void**)&ad, M * D / QK * 2}, {(void**)&n1d, M * D / QK * 2},
         {(void**)&hd, M * FF / QK * 2},
-        {(void**)&part, (size_t)max_slots * NH * max_chunks * (2 + HD) * 8},
-        {(void**)&counter, (size_t)max_slots * NH * 4},
+        {(void**)&part, (size_t)max_slots * NH * max_chunks * PART_STRIDE * 4},
         {(void**)&p_ids, M * 4}, {(void**)&p_pepos, M * 4}, {(void**)&p_istext, M * 4},
         {(void**)&p_tslot, M * 4}, {(void**)&p_tpos, M * 4}, {(void**)&p_rowT, M * 4}, {(void**)&p_rowoff, M * 8},
         {(void**)&p_sstart, (size_t)max_slots * 4}, {(void**)&p_slen, (size_t)max_slots * 4},
@@ -432,7 +431,6 @@ int gsvcu_ctx::reserve(int slots, int ctx, int kvd) {
             return r;
         }
     }
-    CK(cudaMemsetAsync(counter, 0, (size_t)max_slots * NH * 4, stream));
     CK(cudaMemsetAsync(st, 0, sizeof(SlotState) * max_slots, stream));
     CK(cudaMemsetAsync(xq, 0, M * D, stream));
     CK(cudaMemsetAsync(xd, 0, M * D / QK * 2, stream));
@@ -769,8 +767,8 @@ int gsvcu_ctx::launch_step(cudaStream_t s, float* dump, int dump_row, const int*
         a.q = qkv; a.q_stride = 3 * D; a.pool = pool; a.kv_f32 = kv_f32; a.n_layer = NL; a.layer = li;
         a.block_table = block_table; a.max_pages = max_pages; a.st = st; a.B = M; a.max_chunks = max_chunks;
         a.scale = scale; a.out_q = aq; a.out_d = ad; a.out_f32 = dump ? attn_f32 : nullptr;
-        a.part = part; a.counter = counter;
-        launch_decode_attention(a, s);
+        a.part = part; a.err = att_err;
+        nk += launch_decode_attention(a, s);
         TRY(mark(3));
         GemmQ8Params o;
         o.xq = aq; o.xd = ad; o.M = M; o.wq = w.wq[1]; o.wd = w.wd[1]; o.N = D; o.K = D; o.bias = w.b_out; o.resid = x; o.y = pre;
@@ -788,7 +786,7 @@ int gsvcu_ctx::launch_step(cudaStream_t s, float* dump, int dump_row, const int*
         f2.resid = n1; f2.y = pre;
         launch_gemm_q8(f2, EPI_RESID, s);
         TRY(mark(7));
-        nk += 7;
+        nk += 6;
         if (dump) {
             const float* items[3] = {attn_f32, n1, pre};
             for (int it = 0; it < 3; it++)
@@ -839,8 +837,11 @@ int gsvcu_ctx::run_steps(int nsteps) {
 }
 
 int gsvcu_ctx::read_status() {
+    int32_t aerr = 0;
     CK(cudaMemcpyAsync(h_st.data(), st, sizeof(SlotState) * max_slots, cudaMemcpyDeviceToHost, stream));
+    CK(cudaMemcpyAsync(&aerr, att_err, sizeof(aerr), cudaMemcpyDeviceToHost, stream));
     CK(cudaStreamSynchronize(stream));
+    if (aerr) return fail(GSVCU_ERR_CUDA, "decode attention: staged K/V never arrived (bounded wait gave up)");
     return GSVCU_OK;
 }
 
@@ -892,13 +893,16 @@ int gsvcu_create(int device, gsvcu_ctx** out) {
     cudaDeviceProp prop;
     if (cudaGetDeviceProperties(&prop, device) != cudaSuccess || prop.major != 10) return GSVCU_ERR_DEVICE;
     DeviceGuard g(device);
-    if (gemm_q8_init_device() != cudaSuccess) {
+    if (gemm_q8_init_device() != cudaSuccess || attention_init_device() != cudaSuccess) {
         cudaGetLastError();
         return GSVCU_ERR_CUDA;
     }
     gsvcu_ctx* c = new gsvcu_ctx();
     c->device = device;
-    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
+    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaMalloc((void**)&c->att_err, sizeof(int32_t)) != cudaSuccess ||
+        cudaMemset(c->att_err, 0, sizeof(int32_t)) != cudaSuccess) {
+        cudaGetLastError();
         delete c;
         return GSVCU_ERR_CUDA;
     }
@@ -1189,12 +1193,12 @@ int gsvcu_op_decode_attention(gsvcu_ctx* ctx, const float* q_dev, int32_t q_stri
                               int8_t* out_q_dev, uint16_t* out_d_dev, float* out_f32_dev) {
     if (!ctx || !q_dev || !pool_dev || !block_table_dev || !kvpos_dev || !active_dev || !out_q_dev || !out_d_dev ||
         B <= 0 || max_pages <= 0 || n_layer <= 0 || layer < 0 || layer >= n_layer || q_stride < D ||
-        (kv_dtype != GSVCU_KV_F16 && kv_dtype != GSVCU_KV_F32))
+        (kv_dtype != GSVCU_KV_F16 && kv_dtype != GSVCU_KV_F32) || !decode_attention_aligned(q_dev, q_stride, pool_dev,
+                                                                                            out_q_dev, out_f32_dev))
         return GSVCU_ERR_ARG;
     DeviceGuard g(ctx->device);
-    const int max_chunks = (max_pages * PAGE + ATT_CHUNK - 1) / ATT_CHUNK;
-    const size_t need_part = (size_t)B * NH * max_chunks * (2 + HD);
-    const size_t need_cnt = (size_t)B * NH;
+    const int max_chunks = decode_chunks(max_pages * PAGE);
+    const size_t need_part = (size_t)B * NH * max_chunks * PART_STRIDE;
     if (need_part > ctx->op_part_n) {
         if (ctx->op_part) {
             cudaStreamSynchronize(ctx->stream);
@@ -1202,25 +1206,14 @@ int gsvcu_op_decode_attention(gsvcu_ctx* ctx, const float* q_dev, int32_t q_stri
         }
         ctx->op_part = nullptr;
         ctx->op_part_n = 0;
-        CKC(ctx, cudaMalloc((void**)&ctx->op_part, need_part * 8));
+        CKC(ctx, cudaMalloc((void**)&ctx->op_part, need_part * 4));
         ctx->op_part_n = need_part;
-    }
-    if (need_cnt > ctx->op_counter_n) {
-        if (ctx->op_counter) {
-            cudaStreamSynchronize(ctx->stream);
-            cudaFree(ctx->op_counter);
-        }
-        ctx->op_counter = nullptr;
-        ctx->op_counter_n = 0;
-        CKC(ctx, cudaMalloc((void**)&ctx->op_counter, need_cnt * 4));
-        CKC(ctx, cudaMemsetAsync(ctx->op_counter, 0, need_cnt * 4, ctx->stream));
-        ctx->op_counter_n = need_cnt;
     }
     DecAttnParams a;
     a.q = q_dev; a.q_stride = q_stride; a.pool = pool_dev; a.kv_f32 = kv_dtype; a.n_layer = n_layer; a.layer = layer;
     a.block_table = block_table_dev; a.max_pages = max_pages; a.kvpos = kvpos_dev; a.active = active_dev; a.B = B;
     a.max_chunks = max_chunks; a.scale = 1.0f / std::sqrt((float)HD); a.out_q = out_q_dev; a.out_d = out_d_dev;
-    a.out_f32 = out_f32_dev; a.part = ctx->op_part; a.counter = ctx->op_counter;
+    a.out_f32 = out_f32_dev; a.part = ctx->op_part; a.err = ctx->att_err;
     launch_decode_attention(a, ctx->stream);
     CKC(ctx, cudaGetLastError());
     return GSVCU_OK;

@@ -83,10 +83,24 @@ struct DecAttnParams {
     int8_t* out_q = nullptr;
     uint16_t* out_d = nullptr;
     float* out_f32 = nullptr;
-    double* part = nullptr;              // scratch [B][NH][max_chunks][2 + HD]: m, l, o[HD]
-    int32_t* counter = nullptr;          // scratch [B][NH], zero between launches
+    float* part = nullptr;               // scratch [B][NH][max_chunks][PART_STRIDE]: m, l, -, -, o[HD]
+    int32_t* err = nullptr;              // set to 1 if a bounded wait gave up (may be null)
 };
-void launch_decode_attention(const DecAttnParams& p, cudaStream_t s);
+// Split-KV work items of decode attention: one per 64-key page. A page's partial result is
+// {m, l, pad, pad, o[32]} floats (o 16-byte aligned).
+inline int decode_chunks(int max_tokens) { return (max_tokens + PAGE - 1) / PAGE; }
+constexpr int PART_STRIDE = 4 + HD;
+// Alignment the decode-attention kernel relies on: 16-byte q rows (float4 loads), pool (TMA bulk
+// copies) and f32 output (float4 stores), 8-byte Q8_0 output rows (8-byte stores).
+inline bool decode_attention_aligned(const float* q, int q_stride, const void* pool, const int8_t* out_q,
+                                     const float* out_f32) {
+    return ((uintptr_t)q & 15) == 0 && (q_stride & 3) == 0 && ((uintptr_t)pool & 15) == 0 &&
+           ((uintptr_t)out_q & 7) == 0 && ((uintptr_t)out_f32 & 15) == 0;
+}
+// Returns the number of kernels launched (2 when sequences may span several pages: pages + merge).
+int launch_decode_attention(const DecAttnParams& p, cudaStream_t s);
+// Raise the dynamic shared-memory limit of the decode-attention kernels on the current device.
+cudaError_t attention_init_device();
 
 struct PrefillTile { int32_t seq, q0; };
 struct PrefAttnParams {

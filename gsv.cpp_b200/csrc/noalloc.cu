@@ -4,9 +4,9 @@
 // framework's caching allocator owns the whole device, code inside a real-time audio callback that
 // must not block on the driver's allocator, or embedders that forbid allocations after start-up.
 // gsvcu_op_decode_attention grows its split-KV scratch with cudaMalloc on first use; this variant runs
-// the same kernel with its scratch (per-chunk partial results and the per-(sequence, head) merge
-// counters) in a fixed array that is part of the library image. Every GPU that loads the library holds
-// this array (about 4.3 MiB) until the process exits.
+// the same kernels with their scratch (the per-page partial results) in a fixed array that is part of
+// the library image. Every GPU that loads the library holds this array (about 2.3 MiB) until the
+// process exits.
 #include <cstdio>
 #include <mutex>
 
@@ -16,14 +16,13 @@
 namespace gsvcu {
 namespace {
 
-constexpr int kItems = GSVCU_NOALLOC_MAX_ITEMS;                       // (sequence, key chunk) pairs
-constexpr size_t kPartDoubles = (size_t)kItems * NH * (2 + HD);      // partials: m, l, o[32] per head
-constexpr size_t kCounters = (size_t)kItems * NH;                    // one merge counter per (sequence, head)
+constexpr int kItems = GSVCU_NOALLOC_MAX_ITEMS;                       // (sequence, KV page) pairs
+constexpr size_t kPartFloats = (size_t)kItems * NH * PART_STRIDE;    // partials: m, l, o[32] per head
 
-// Scratch shared by every call on a device: partials first, then the counters.
+// Scratch shared by every call on a device.
 struct NoallocScratch {
-    double part[kPartDoubles];
-    int32_t counter[kCounters];
+    float part[kPartFloats];
+    int32_t err;   // set by the kernel when a bounded wait for staged K/V gave up (outputs are NaN then)
 };
 static __device__ __align__(256) NoallocScratch g_scratch;
 
@@ -47,6 +46,10 @@ int scratch_for_current_device(NoallocScratch** out) {
             cudaGetLastError();
             return GSVCU_ERR_CUDA;
         }
+        if (attention_init_device() != cudaSuccess) {
+            cudaGetLastError();
+            return GSVCU_ERR_CUDA;
+        }
         g_addr[dev] = (NoallocScratch*)p;
     }
     *out = g_addr[dev];
@@ -65,30 +68,26 @@ extern "C" int gsvcu_op_decode_attention_noalloc(void* stream, const float* q_de
                                                  int8_t* out_q_dev, uint16_t* out_d_dev, float* out_f32_dev) {
     if (!q_dev || !pool_dev || !block_table_dev || !kvpos_dev || !active_dev || !out_q_dev || !out_d_dev || B <= 0 ||
         max_pages <= 0 || n_layer <= 0 || layer < 0 || layer >= n_layer || q_stride < D ||
-        (kv_dtype != GSVCU_KV_F16 && kv_dtype != GSVCU_KV_F32))
+        (kv_dtype != GSVCU_KV_F16 && kv_dtype != GSVCU_KV_F32) ||
+        !decode_attention_aligned(q_dev, q_stride, pool_dev, out_q_dev, out_f32_dev))
         return GSVCU_ERR_ARG;
-    const int max_chunks = (max_pages * PAGE + ATT_CHUNK - 1) / ATT_CHUNK;
+    const int max_chunks = decode_chunks(max_pages * PAGE);
     if ((int64_t)B * max_chunks > kItems) {
         std::fprintf(stderr,
-                     "gsvcu_op_decode_attention_noalloc: B (%d) x key chunks (%d for %d pages) exceeds the fixed "
-                     "scratch of %d sequence-chunks (GSVCU_NOALLOC_MAX_ITEMS); use gsvcu_op_decode_attention\n",
-                     B, max_chunks, max_pages, kItems);
+                     "gsvcu_op_decode_attention_noalloc: B (%d) x max_pages (%d) exceeds the fixed scratch of %d "
+                     "sequence-pages (GSVCU_NOALLOC_MAX_ITEMS); use gsvcu_op_decode_attention\n",
+                     B, max_pages, kItems);
         return GSVCU_ERR_ARG;
     }
     NoallocScratch* s = nullptr;
     const int rc = scratch_for_current_device(&s);
     if (rc != GSVCU_OK) return rc;
     cudaStream_t st = (cudaStream_t)stream;
-    // the counters must start at zero; a previous call leaves them at zero unless it was interrupted
-    if (cudaMemsetAsync(s->counter, 0, (size_t)B * NH * sizeof(int32_t), st) != cudaSuccess) {
-        cudaGetLastError();
-        return GSVCU_ERR_CUDA;
-    }
     DecAttnParams a;
     a.q = q_dev; a.q_stride = q_stride; a.pool = pool_dev; a.kv_f32 = kv_dtype; a.n_layer = n_layer; a.layer = layer;
     a.block_table = block_table_dev; a.max_pages = max_pages; a.kvpos = kvpos_dev; a.active = active_dev; a.B = B;
     a.max_chunks = max_chunks; a.scale = 1.0f / sqrtf((float)HD); a.out_q = out_q_dev; a.out_d = out_d_dev;
-    a.out_f32 = out_f32_dev; a.part = s->part; a.counter = s->counter;
+    a.out_f32 = out_f32_dev; a.part = s->part; a.err = &s->err;
     launch_decode_attention(a, st);
     if (cudaGetLastError() != cudaSuccess) return GSVCU_ERR_CUDA;
     return GSVCU_OK;

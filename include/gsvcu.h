@@ -187,7 +187,10 @@ int gsvcu_op_f32_gemm(gsvcu_ctx* ctx, const float* x_dev, int32_t M, const float
  *   kvpos_dev [B]: index of the newest key (keys 0..kvpos attend), active_dev [B] (0 = skip).
  *   Page layout: [page][n_layer][K,V][16 heads][64 tokens][32] of kv_dtype elements.
  *   Output: Q8_0 planes out_q [B][512], out_d [B][16]; out_f32 [B][512] optional (may be NULL).
- * Partial results of the key chunks live in scratch memory owned by the context (grown on demand). */
+ *   Alignment: q_dev, pool_dev and out_f32_dev 16-byte aligned, q_stride a multiple of 4, out_q_dev
+ *   8-byte aligned (else GSVCU_ERR_ARG); kvpos < max_pages * 64.
+ * One split-KV work item per 64-key page; the pages' partial results live in scratch memory owned by
+ * the context (grown on demand). */
 int gsvcu_op_decode_attention(gsvcu_ctx* ctx, const float* q_dev, int32_t q_stride, const void* pool_dev,
                               int32_t kv_dtype, int32_t n_layer, int32_t layer, const int32_t* block_table_dev,
                               int32_t max_pages, const int32_t* kvpos_dev, const int32_t* active_dev, int32_t B,
@@ -199,9 +202,9 @@ int gsvcu_op_decode_attention(gsvcu_ctx* ctx, const float* q_dev, int32_t q_stri
  * in the driver's allocator, or an embedder that forbids allocations after start-up).
  * Same inputs, outputs and results as gsvcu_op_decode_attention, on the caller's `stream`
  * (cudaStream_t, NULL = legacy default stream) of the current device, without a context. The split-KV
- * scratch is a fixed array inside the library (about 4.3 MiB held on every GPU that loads it, until
- * the process exits), sized for B * ceil(max_pages * 64 / 256) <= GSVCU_NOALLOC_MAX_ITEMS; larger
- * calls return GSVCU_ERR_ARG with a message on stderr. The first call on a device looks up the
+ * scratch is a fixed array inside the library (about 2.3 MiB held on every GPU that loads it, until
+ * the process exits), sized for B * max_pages <= GSVCU_NOALLOC_MAX_ITEMS (one split-KV work item per
+ * 64-key page); larger calls return GSVCU_ERR_ARG with a message on stderr. The first call on a device looks up the
  * array's device address (cudaGetSymbolAddress); make that first call before any stream capture.
  * All calls share the array: calls that overlap on the GPU (other streams, other threads) race. */
 #define GSVCU_NOALLOC_MAX_ITEMS 1024

@@ -17,9 +17,13 @@
 //     accumulated in float block by block as sumf = fma((float)sumi, d_w*d_x, sumf).
 //   * F32 mul_mat / F32 vec_dot: float products accumulated in double, rounded once
 //     (ggml_vec_dot_f32 scalar path).
-//   * flash_attn_ext (F32 K/V): scores s = (float)(double-accumulated q.k) * scale, masked keys
-//     skipped; softmax(s) V evaluated in double (double exp, double sums) and rounded once (an
-//     order-independent evaluation of ggml's float online softmax, see attn_row).
+//   * flash_attn_ext (F32 K/V), prefill rows: scores s = (float)(double sum of the exact products
+//     q_e*k_e) * scale (the products are exact as in the FMA-vectorised ggml_vec_dot_f32 of the
+//     -mavx2 -mfma build), masked keys skipped; softmax(s) V evaluated in double (double exp, double
+//     sums) and rounded once (an order-independent evaluation of ggml's float online softmax, see
+//     attn_row).
+//   * flash_attn_ext, decode rows: float arithmetic in a fixed page-split order with an own float exp
+//     (decode_attention_canonical), the evaluation order of the library's decode kernel.
 //   * layernorm_affine (P:1535-1585): v = (x + r) + bias, mean / E[v^2] in double,
 //     var = E[v^2] - mean^2, inv = 1/sqrtf(var + eps), y = ((v - mean)*inv)*w + b.
 //   * add_act ReLU (P:1587-1620): y = max(a + b, 0).
@@ -31,6 +35,7 @@
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <numeric>
 #include <string>
@@ -219,7 +224,9 @@ void add_act(const float* a, const float* b, int64_t rows, int64_t n, int act, f
 
 // flash_attn_ext for one query row of one head (F32 K/V), masked keys skipped
 // (the -inf/0 mask of src/gsv_ar.cpp:215-223, 450; keep(k) decides visibility).
-// Scores follow ggml exactly: s = (float)(double-accumulated q.k) * scale. The softmax-weighted sum
+// Scores: s = (float)(sum of the exact products q_e*k_e, accumulated in double) * scale. A float
+// product of two floats is exact in double, so the sum carries ~1e-16 relative error and its rounding
+// to float does not depend on the summation order. The softmax-weighted sum
 // softmax(s) V is then evaluated in double (weights exp(s - max) with the double exp, sums in double)
 // and rounded to float once. ggml's float online softmax is one float evaluation of the same
 // expression; this order-independent evaluation is what any other reduction order (split-KV chunks,
@@ -231,7 +238,10 @@ void attn_row(const float* q, const float* K, const float* Vv, int64_t kstride, 
     float M = -INFINITY;
     for (int64_t ic = 0; ic < nk; ic++) {
         if (!keep(ic)) continue;
-        sc[ic] = vec_dot_f32(hd, q, K + ic * kstride) * scale;
+        const float* k = K + ic * kstride;
+        double dot = 0.0;
+        for (int d = 0; d < hd; d++) dot += (double)q[d] * (double)k[d];
+        sc[ic] = (float)dot * scale;
         M = std::max(M, sc[ic]);
     }
     double l = 0.0, acc[256];
@@ -244,6 +254,84 @@ void attn_row(const float* q, const float* K, const float* Vv, int64_t kstride, 
         for (int d = 0; d < hd; d++) acc[d] += p * (double)v[d];
     }
     for (int d = 0; d < hd; d++) out[d] = l > 0.0 ? (float)(acc[d] / l) : 0.0f;
+}
+
+// exp(x) for x <= 0 in float: Cody-Waite reduction x = n*ln2 + r (ln2 split into a 15-bit head and a
+// float tail, so n*head is exact), degree-7 Taylor polynomial of exp(r) by Horner with fma, times 2^n.
+// x < -87 (or -inf) gives 0. Max error ~1.2 ulp.
+inline float exp_c(float x) {
+    if (!(x >= -87.0f)) return 0.0f;
+    const float n = rintf(x * 0x1.715476p+0f);
+    float r = std::fma(-n, 0x1.62e4p-1f, x);
+    r = std::fma(-n, 0x1.7f7d1cp-20f, r);
+    float p = 0x1.a01a02p-13f;
+    p = std::fma(p, r, 0x1.6c16c2p-10f);
+    p = std::fma(p, r, 0x1.111112p-7f);
+    p = std::fma(p, r, 0x1.555556p-5f);
+    p = std::fma(p, r, 0x1.555556p-3f);
+    p = std::fma(p, r, 0.5f);
+    p = std::fma(p, r, 1.0f);
+    p = std::fma(p, r, 1.0f);
+    uint32_t bits = (uint32_t)((int)n + 127) << 23;
+    float sc;
+    std::memcpy(&sc, &bits, 4);
+    return p * sc;
+}
+
+// Decode attention of one query row of one head (HD = 32) over nk cached keys, in the library's
+// fixed evaluation order (flash_attn_ext of src/gsv_ar.cpp:450-456 for a decode row, with ggml's
+// float online softmax replaced by a page-split evaluation whose every operation is pinned):
+// keys are split into 64-key pages; in a page, key t belongs to group g = t % 8, dims are split into
+// 4 slices of 8.
+//   score: D_s = fma chain over slice s from 0; dot = (D0 + D1) + (D2 + D3); s_t = dot * scale
+//   page:  m = max s_t; p_t = exp_c(s_t - m); per group: L_g = sum of p_t, O_g[d] = fma chain of
+//          p_t * v_t[d], both in ascending t; l = ((L0+L1)+(L2+L3))+((L4+L5)+(L6+L7)), o[d] likewise
+//   merge: M = max over pages of m; per page in order: w = exp_c(m - M), L = fma(w, l, L),
+//          O[d] = fma(w, o[d], O[d]); out[d] = O[d] / L.
+void decode_attention_canonical(const float* q, const float* K, const float* Vv, int64_t kstride, int64_t nk,
+                                float scale, float* out) {
+    constexpr int HD = 32, PG = 64;
+    float L = 0.0f, O[HD] = {}, M = -INFINITY;
+    const int64_t npg = (nk + PG - 1) / PG;
+    std::vector<float> pm((size_t)npg), pl((size_t)npg), po((size_t)npg * HD);
+    for (int64_t c = 0; c < npg; c++) {
+        const int64_t n = std::min<int64_t>(PG, nk - c * PG);
+        float sc[PG], m = -INFINITY;
+        for (int64_t t = 0; t < n; t++) {
+            const float* k = K + (c * PG + t) * kstride;
+            float Ds[4];
+            for (int sl = 0; sl < 4; sl++) {
+                float d = 0.0f;
+                for (int e = 0; e < 8; e++) d = std::fma(q[sl * 8 + e], k[sl * 8 + e], d);
+                Ds[sl] = d;
+            }
+            sc[t] = ((Ds[0] + Ds[1]) + (Ds[2] + Ds[3])) * scale;
+            m = std::max(m, sc[t]);
+        }
+        float Lg[8] = {}, Og[8][HD] = {};
+        for (int64_t t = 0; t < n; t++) {
+            const float pt = exp_c(sc[t] - m);
+            const float* v = Vv + (c * PG + t) * kstride;
+            const int g = (int)(t % 8);
+            Lg[g] = Lg[g] + pt;
+            for (int d = 0; d < HD; d++) Og[g][d] = std::fma(pt, v[d], Og[g][d]);
+        }
+        auto tree = [](const float* x) { return ((x[0] + x[1]) + (x[2] + x[3])) + ((x[4] + x[5]) + (x[6] + x[7])); };
+        pm[c] = m;
+        pl[c] = tree(Lg);
+        for (int d = 0; d < HD; d++) {
+            float col[8];
+            for (int g = 0; g < 8; g++) col[g] = Og[g][d];
+            po[(size_t)c * HD + d] = tree(col);
+        }
+        M = std::max(M, m);
+    }
+    for (int64_t c = 0; c < npg; c++) {
+        const float w = exp_c(pm[c] - M);
+        L = std::fma(w, pl[c], L);
+        for (int d = 0; d < HD; d++) O[d] = std::fma(w, po[(size_t)c * HD + d], O[d]);
+    }
+    for (int d = 0; d < HD; d++) out[d] = O[d] / L;
 }
 
 // ------------------------------------------------------------------ sampler (src/gsv_sampler.cpp)
@@ -507,8 +595,7 @@ void decode_step(const orc_model& m, std::vector<SeqCache*>& caches, const float
                 const float* q = qkv.data() + (size_t)b * 3 * D + hh * HD;
                 const float* K = c.k.data() + (size_t)li * c.cap * D + hh * HD;
                 const float* Vv = c.v.data() + (size_t)li * c.cap * D + hh * HD;
-                auto keep = [](int64_t) { return true; };
-                attn_row(q, K, Vv, D, c.len + 1, HD, scale, keep, att.data() + (size_t)b * D + hh * HD);
+                decode_attention_canonical(q, K, Vv, D, c.len + 1, scale, att.data() + (size_t)b * D + hh * HD);
             }
         mul_mat(w.out_w, att.data(), B, o.data());
         ln_affine(cur.data(), o.data(), w.out_b.data(), w.n1w.data(), w.n1b.data(), B, D, 1e-5f, n1.data());
@@ -598,13 +685,16 @@ void orc_add_act(const float* a, const float* b, int64_t rows, int64_t n, int ac
 // lens [B] keys visible per sequence; out [B][NH][HD].
 void orc_decode_attention(const float* q, const float* k, const float* v, const int32_t* lens, int B, int Lmax, int NH,
                           int HD, float scale, float* out) {
+    if (HD != 32) {
+        std::fprintf(stderr, "orc_decode_attention: head dim must be 32\n");
+        std::abort();
+    }
     #pragma omp parallel for collapse(2) num_threads(nthreads()) schedule(dynamic)
     for (int b = 0; b < B; b++)
         for (int h = 0; h < NH; h++) {
             const size_t base = (size_t)b * Lmax * NH * HD + (size_t)h * HD;
-            auto keep = [](int64_t) { return true; };
-            attn_row(q + ((size_t)b * NH + h) * HD, k + base, v + base, (int64_t)NH * HD, lens[b], HD, scale, keep,
-                     out + ((size_t)b * NH + h) * HD);
+            decode_attention_canonical(q + ((size_t)b * NH + h) * HD, k + base, v + base, (int64_t)NH * HD, lens[b],
+                                       scale, out + ((size_t)b * NH + h) * HD);
         }
 }
 

@@ -86,6 +86,25 @@ def test_layernorm_vs_float64():
     assert np.abs(y - ref).max() < 1e-5
 
 
+def test_decode_attention_canonical_vs_float64():
+    """The page-split float evaluation (own exp, fixed order) is softmax(q.K) V to float accuracy,
+    including single-key, partial-page and many-page rows and large score ranges."""
+    rng = np.random.default_rng(12)
+    lens = np.array([1, 2, 63, 64, 65, 130, 700, 2049], np.int32)
+    B, L = len(lens), int(lens.max())
+    q = (rng.standard_normal((B, 16, 32)) * 2).astype(np.float32)
+    k = rng.standard_normal((B, L, 16, 32)).astype(np.float32)
+    v = rng.standard_normal((B, L, 16, 32)).astype(np.float32)
+    scale = np.float32(1.0 / np.sqrt(32.0))
+    got = O.decode_attention(q, k, v, lens, scale)
+    for b in range(B):
+        n = lens[b]
+        s = np.einsum("hd,thd->ht", q[b].astype(np.float64), k[b, :n].astype(np.float64)) * float(scale)
+        w = np.exp(s - s.max(1, keepdims=True))
+        ref = np.einsum("ht,thd->hd", w / w.sum(1, keepdims=True), v[b, :n].astype(np.float64))
+        assert np.abs(got[b] - ref).max() < 2e-5 * max(1.0, np.abs(ref).max()), b
+
+
 def test_q8_mul_mat_vs_dequantized_float64():
     """Q8_0 mul_mat equals the float64 product of the dequantized operands up to float rounding."""
     rng = np.random.default_rng(3)

@@ -80,6 +80,9 @@ def test_noalloc_rejects_sizes_beyond_its_scratch():
     lib = gsvcu.load_library()
     dummy = torch.zeros(16, dtype=torch.int32, device="cuda")
     p = C.c_void_p(dummy.data_ptr())
-    # 64 sequences x 32 pages (8 key chunks each) = 512 sequence-chunks fits; 64 x 80 pages = 1280 does not
+    # B x max_pages must stay within 1024 sequence-pages: 64 x 80 does not fit
     rc = lib.gsvcu_op_decode_attention_noalloc(None, p, 1536, p, 0, 1, 0, p, 80, p, p, 64, p, p, None)
+    assert rc == -1
+    # nor does 64 x 17 = 1088 (F32 pool)
+    rc = lib.gsvcu_op_decode_attention_noalloc(None, p, 1536, p, 1, 1, 0, p, 17, p, p, 64, p, p, None)
     assert rc == -1
