@@ -152,26 +152,46 @@ __global__ void __launch_bounds__(128) k_decode_attn(const DecAttnParams p) {
     extern __shared__ __align__(128) uint8_t sm[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int slot = blockIdx.z, chunk = blockIdx.y, h = blockIdx.x * 4 + warp;
+    // In the decode step (p.st set) the slot state and every KV row but this step's are at least two
+    // kernels old, so they are read before griddep_wait; op-entry inputs may come from the previous
+    // kernel and are read after it.
+    const bool early = p.st != nullptr;
+    if (!early) {
+        griddep_wait();
+        griddep_launch();
+    }
     int kvpos;
-    if (!decode_slot(p, slot, kvpos)) return;
+    const bool act = decode_slot(p, slot, kvpos);
     const int nkeys = kvpos + 1, k0 = chunk * PAGE;
-    if (k0 >= nkeys) return;
+    if (!act || k0 >= nkeys) {
+        if (early) griddep_wait();
+        return;
+    }
     const int n = min(PAGE, nkeys - k0);
     const int sub = lane & 3, g = lane >> 2;
 
     uint8_t* ks = sm + (size_t)warp * S::WARPB;
     uint8_t* vs = ks + S::PGB;
     const uint32_t bar = smem_u32((uint64_t*)(sm + 4 * S::WARPB) + warp);
-    if (lane == 0) {
+    const bool fresh = chunk == kvpos / PAGE;   // holds the key the previous kernel wrote this step
+    auto stage = [&]() {
         const int page = p.block_table[(size_t)slot * p.max_pages + chunk];
         const KT* kp = (const KT*)p.pool + (size_t)page * p.n_layer * 2 * NH * PAGE * HD +
                        ((size_t)p.layer * 2 * NH + h) * PAGE * HD;
         const uint32_t bytes = (uint32_t)n * S::ROWB;
-        mbar_init(bar, 1);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         mbar_expect_tx(bar, 2 * bytes);
         bulk_g2s(smem_u32(ks), kp, bytes, bar);
         bulk_g2s(smem_u32(vs), kp + (size_t)NH * PAGE * HD, bytes, bar);
+    };
+    if (lane == 0) {
+        mbar_init(bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        if (!(early && fresh)) stage();
+    }
+    if (early) {
+        griddep_wait();
+        griddep_launch();
+        if (fresh && lane == 0) stage();
     }
     float q[8];
     {
@@ -251,6 +271,8 @@ __global__ void __launch_bounds__(128) k_decode_merge(const DecAttnParams p) {
     __shared__ __align__(16) float sbuf[4][64 + 32 * 32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int item = blockIdx.x * 4 + warp;
+    griddep_wait();
+    griddep_launch();
     if (item >= p.B * NH) return;
     const int slot = item / NH, h = item % NH;
     int kvpos;
@@ -303,10 +325,10 @@ cudaError_t attention_init_device() {
 
 int launch_decode_attention(const DecAttnParams& p, cudaStream_t s) {
     dim3 grid(NH / 4, p.max_chunks, p.B);
-    if (p.kv_f32) k_decode_attn<float><<<grid, 128, DecShape<float>::SMEM, s>>>(p);
-    else k_decode_attn<__half><<<grid, 128, DecShape<__half>::SMEM, s>>>(p);
+    if (p.kv_f32) launch_pdl(k_decode_attn<float>, grid, dim3(128), DecShape<float>::SMEM, s, p);
+    else launch_pdl(k_decode_attn<__half>, grid, dim3(128), DecShape<__half>::SMEM, s, p);
     if (p.max_chunks <= 1) return 1;
-    k_decode_merge<<<(p.B * NH + 3) / 4, 128, 0, s>>>(p);
+    launch_pdl(k_decode_merge, dim3((p.B * NH + 3) / 4), dim3(128), 0, s, p);
     return 2;
 }
 
@@ -319,6 +341,8 @@ __global__ void __launch_bounds__(PREF_QTILE) k_prefill_attn(const PrefAttnParam
     __shared__ float Ks[PREF_QTILE][HD];
     __shared__ float Vs[PREF_QTILE][HD];
     const int h = blockIdx.x;
+    griddep_wait();
+    griddep_launch();
     const PrefillTile tile = p.tiles[blockIdx.y];
     const int sq = tile.seq, q0 = tile.q0;
     const int start = p.seq_start[sq], S = p.seq_len[sq], T = p.text_len[sq];
@@ -394,7 +418,7 @@ __global__ void __launch_bounds__(PREF_QTILE) k_prefill_attn(const PrefAttnParam
 void launch_prefill_attention(const PrefAttnParams& p, cudaStream_t s) {
     if (p.n_tiles == 0) return;
     dim3 grid(NH, p.n_tiles);
-    k_prefill_attn<<<grid, PREF_QTILE, 0, s>>>(p);
+    launch_pdl(k_prefill_attn, grid, dim3(PREF_QTILE), 0, s, p);
 }
 
 }  // namespace gsvcu

@@ -36,6 +36,15 @@ __device__ __forceinline__ double warp_sum_d(double v) {
     return v;
 }
 
+// Programmatic dependent launch. Every kernel of the library calls griddep_wait() before it reads
+// anything the previous kernel in the stream may have written (and before it exits), then
+// griddep_launch() to let the next kernel start its own prologue. Because no kernel triggers its
+// dependents before its own wait returned, a kernel's prologue (the code before griddep_wait) may read
+// data written two or more kernels earlier, never the immediately preceding kernel's output. Without a
+// programmatic predecessor both are no-ops.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Read-only 128-bit load that does not allocate in L1 (streamed weights / KV).
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {
     uint4 r;

@@ -64,7 +64,14 @@ __global__ void __launch_bounds__(32 * KS) k_gemm_q8(const GemmQ8Params p) {
         fb[i] = ldg_stream(w1 + (size_t)kb * 32);
     }
 
-    // stage activations, their scales and the weight scales
+    for (int i = tid; i < 32 * KB; i += NT) {
+        const int kb = i >> 5, f = i & 31;
+        Wds[i] = p.wd[(size_t)(f0 + f) * KB + kb];
+    }
+    // weights above are constant; the activations below come from the previous kernel
+    griddep_wait();
+    griddep_launch();
+    // stage activations and their scales
     const int vpr = K / 16;
     for (int i = tid; i < TOK * vpr; i += NT) {
         const int r = i / vpr, c = i - r * vpr;
@@ -75,10 +82,6 @@ __global__ void __launch_bounds__(32 * KS) k_gemm_q8(const GemmQ8Params p) {
     for (int i = tid; i < TOK * KB; i += NT) {
         const int r = i / KB;
         Xds[i] = tok0 + r < p.M ? p.xd[(size_t)(tok0 + r) * KB + (i - r * KB)] : (uint16_t)0;
-    }
-    for (int i = tid; i < 32 * KB; i += NT) {
-        const int kb = i >> 5, f = i & 31;
-        Wds[i] = p.wd[(size_t)(f0 + f) * KB + kb];
     }
     __syncthreads();
 
@@ -203,9 +206,9 @@ static void launch_t(const GemmQ8Params& p, int epi, cudaStream_t s) {
     dim3 grid(p.N / 32, (p.M + 8 * T - 1) / (8 * T));
     dim3 block(32 * KS);
     switch (epi) {
-        case EPI_BIAS: k_gemm_q8<T, KS, EPI_BIAS><<<grid, block, smem, s>>>(p); break;
-        case EPI_RESID: k_gemm_q8<T, KS, EPI_RESID><<<grid, block, smem, s>>>(p); break;
-        default: k_gemm_q8<T, KS, EPI_RELU_Q8><<<grid, block, smem, s>>>(p); break;
+        case EPI_BIAS: launch_pdl(k_gemm_q8<T, KS, EPI_BIAS>, grid, block, smem, s, p); break;
+        case EPI_RESID: launch_pdl(k_gemm_q8<T, KS, EPI_RESID>, grid, block, smem, s, p); break;
+        default: launch_pdl(k_gemm_q8<T, KS, EPI_RELU_Q8>, grid, block, smem, s, p); break;
     }
 }
 

@@ -1,5 +1,6 @@
 // kernels.h -- host-side launchers of the gsvcu kernels (internal to the library).
 #pragma once
+#include <utility>
 
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -7,6 +8,23 @@
 #include "common.cuh"
 
 namespace gsvcu {
+
+// Launch with programmatic stream serialization allowed (see griddep_wait in common.cuh): the kernel
+// may become resident while its predecessor finishes, and waits for it in griddep_wait().
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // ------------------------------------------------------------ Q8_0 GEMM
 // Activation planes: xq int8 [M][K] row-major, xd fp16 [M][K/32].

@@ -13,6 +13,8 @@ __global__ void __launch_bounds__(128) k_layernorm_q8(const float* __restrict__ 
                                                       const float* __restrict__ b, float* __restrict__ y,
                                                       int8_t* __restrict__ yq, uint16_t* __restrict__ yd) {
     const int row = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    griddep_wait();
+    griddep_launch();
     if (row >= rows) return;
     float x[16];
     const float4* src = (const float4*)(v + (size_t)row * D + lane * 16);
@@ -60,13 +62,15 @@ __global__ void __launch_bounds__(128) k_layernorm_q8(const float* __restrict__ 
 void launch_layernorm_q8(const float* v, int rows, const float* w, const float* b, float* y, int8_t* yq, uint16_t* yd,
                          cudaStream_t s) {
     if (rows <= 0) return;
-    k_layernorm_q8<<<(rows + 3) / 4, 128, 0, s>>>(v, rows, w, b, y, yq, yd);
+    launch_pdl(k_layernorm_q8, dim3((rows + 3) / 4), dim3(128), 0, s, v, rows, w, b, y, yq, yd);
 }
 
 // ------------------------------------------------------------------ quantize
 // quantize_row_q8_0 on rows of K floats: one thread per 32-value block.
 __global__ void k_quantize_q8(const float* __restrict__ x, int nblocks, int8_t* __restrict__ q, uint16_t* __restrict__ d) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    griddep_wait();
+    griddep_launch();
     if (i >= nblocks) return;
     float v[32], amax = 0.0f;
     const float4* src = (const float4*)(x + (size_t)i * 32);
@@ -96,7 +100,7 @@ __global__ void k_quantize_q8(const float* __restrict__ x, int nblocks, int8_t* 
 void launch_quantize_q8(const float* x, int rows, int K, int8_t* q, uint16_t* d, cudaStream_t s) {
     const int nb = rows * (K / QK);
     if (nb <= 0) return;
-    k_quantize_q8<<<(nb + 127) / 128, 128, 0, s>>>(x, nb, q, d);
+    launch_pdl(k_quantize_q8, dim3((nb + 127) / 128), dim3(128), 0, s, x, nb, q, d);
 }
 
 // ------------------------------------------------------------------ F32 GEMM, double accumulation
@@ -112,6 +116,8 @@ __global__ void __launch_bounds__(256) k_gemm_f32d(const float* __restrict__ x, 
     __shared__ float Xs[32][33];
     const int tid = threadIdx.x, tn = tid & 31, tm = tid >> 5;
     const int n0 = blockIdx.x * 32, m0 = blockIdx.y * 32;
+    griddep_wait();
+    griddep_launch();
     double acc[4][2];
 #pragma unroll
     for (int i = 0; i < 4; i++) acc[i][0] = acc[i][1] = 0.0;
@@ -166,7 +172,7 @@ void launch_gemm_f32d(const float* x, int ldx, const F32Gather* gather, int M, c
     dim3 grid((N + 31) / 32, (M + 31) / 32);
     F32Gather g;
     if (gather) g = *gather;
-    k_gemm_f32d<<<grid, 256, 0, s>>>(x, ldx, g, gather ? 1 : 0, M, w, N, K, add, ldadd, y, ldy);
+    launch_pdl(k_gemm_f32d, grid, dim3(256), 0, s, x, ldx, g, gather ? 1 : 0, M, w, N, K, add, ldadd, y, ldy);
 }
 
 // ------------------------------------------------------------------ embeddings
@@ -174,6 +180,8 @@ void launch_gemm_f32d(const float* x, int ldx, const F32Gather* gather, int M, c
 // prompt row = audio_emb[code] + alpha_a * pe[t] (FMA, as the reference compiles with -mfma).
 __global__ void k_prefill_embed(const PrefEmbedParams p) {
     const int m = blockIdx.x, d = threadIdx.x;
+    griddep_wait();
+    griddep_launch();
     if (m >= p.M) return;
     const int id = p.ids[m], pos = p.pe_pos[m];
     const bool text = p.is_text[m] != 0;
@@ -184,7 +192,7 @@ __global__ void k_prefill_embed(const PrefEmbedParams p) {
 
 void launch_prefill_embed(const PrefEmbedParams& p, cudaStream_t s) {
     if (p.M <= 0) return;
-    k_prefill_embed<<<p.M, D, 0, s>>>(p);
+    launch_pdl(k_prefill_embed, dim3(p.M), dim3(D), 0, s, p);
 }
 
 // ------------------------------------------------------------------ step control
@@ -194,6 +202,8 @@ void launch_prefill_embed(const PrefEmbedParams& p, cudaStream_t s) {
 // (:798-806), its Q8_0 planes, and their KV write position. One warp per slot.
 __global__ void __launch_bounds__(128) k_step_prep(const StepPrepParams p) {
     const int slot = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    griddep_wait();
+    griddep_launch();
     if (slot >= p.nslots) return;
     SlotState* st = p.st + slot;
     if (!st->active) {
@@ -250,13 +260,15 @@ __global__ void __launch_bounds__(128) k_step_prep(const StepPrepParams p) {
 }
 
 void launch_step_prep(const StepPrepParams& p, cudaStream_t s) {
-    k_step_prep<<<(p.nslots + 3) / 4, 128, 0, s>>>(p);
+    launch_pdl(k_step_prep, dim3((p.nslots + 3) / 4), dim3(128), 0, s, p);
 }
 
 // ------------------------------------------------------------------ row gather / scatter
 __global__ void k_copy_rows(float* __restrict__ dst, const int32_t* __restrict__ didx, const float* __restrict__ src,
                             const int32_t* __restrict__ sidx, int width) {
     const int r = blockIdx.x;
+    griddep_wait();
+    griddep_launch();
     const size_t so = (size_t)(sidx ? sidx[r] : r) * width, dof = (size_t)(didx ? didx[r] : r) * width;
     for (int c = threadIdx.x; c < width; c += blockDim.x) dst[dof + c] = src[so + c];
 }
@@ -264,7 +276,7 @@ __global__ void k_copy_rows(float* __restrict__ dst, const int32_t* __restrict__
 void launch_copy_rows(float* dst, const int32_t* didx, const float* src, const int32_t* sidx, int nrows, int width,
                       cudaStream_t s) {
     if (nrows <= 0) return;
-    k_copy_rows<<<nrows, 256, 0, s>>>(dst, didx, src, sidx, width);
+    launch_pdl(k_copy_rows, dim3(nrows), dim3(256), 0, s, dst, didx, src, sidx, width);
 }
 
 }  // namespace gsvcu

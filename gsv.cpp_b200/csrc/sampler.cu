@@ -43,6 +43,8 @@ __device__ __forceinline__ uint64_t xs_step(uint64_t s) {
 
 __global__ void __launch_bounds__(SAMP_T) k_sampler(const SamplerParams p) {
     const int slot = blockIdx.x;
+    griddep_wait();
+    griddep_launch();
     SlotState* st = p.st + slot;
     if (!st->active) return;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -268,7 +270,7 @@ __global__ void __launch_bounds__(SAMP_T) k_sampler(const SamplerParams p) {
 
 void launch_sampler(const SamplerParams& p, cudaStream_t s) {
     if (p.nslots <= 0) return;
-    k_sampler<<<p.nslots, SAMP_T, 0, s>>>(p);
+    launch_pdl(k_sampler, dim3(p.nslots), dim3(SAMP_T), 0, s, p);
 }
 
 }  // namespace gsvcu
