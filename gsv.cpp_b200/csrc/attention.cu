@@ -19,31 +19,12 @@ namespace gsvcu {
 // (decode_attention_canonical), so the two agree bit for bit. Lane l = 4*g + s owns dims 8s..8s+7 and
 // the keys t = 8u + g (u = 0..7) of its page ("token group" g):
 //   score    D_s = fma chain over the lane's 8 dims from 0; dot = (D0 + D1) + (D2 + D3); s_t = dot*scale
-//   page max m = max_t s_t;  p_t = exp_c(s_t - m)   (exp_c below: own float exp, same on the CPU)
+//   page max m = max_t s_t;  p_t = exp_canon(s_t - m)   (own float exp, common.cuh; same on the CPU)
 //   sums     L_g = sum over u of p_t (ascending u), O_g[d] = fma chain p_t * v_t[d] (ascending u), then
 //            l = ((L0+L1)+(L2+L3))+((L4+L5)+(L6+L7)), o[d] likewise
-//   merge    over the pages c = 0..n-1 in order: M = max m_c, w = exp_c(m_c - M),
+//   merge    over the pages c = 0..n-1 in order: M = max m_c, w = exp_canon(m_c - M),
 //            L = fma(w, l_c, L), O[d] = fma(w, o_c[d], O[d]); out = O / L.
 // Pages of one (slot, head) are merged by the last warp to finish (atomic ticket, no waiting).
-
-// exp(x) for x <= 0 in float: Cody-Waite reduction x = n*ln2 + r (ln2 split into a 15-bit head and a
-// float tail, so n*head is exact) and the degree-7 Taylor polynomial of exp(r), |r| <= ln2/2, by Horner
-// with fma; result p * 2^n. Max error ~1.2 ulp. x < -87 (or -inf) gives 0.
-__device__ __forceinline__ float exp_c(float x) {
-    if (!(x >= -87.0f)) return 0.0f;
-    const float n = rintf(__fmul_rn(x, 0x1.715476p+0f));   // x / ln2, to nearest even
-    float r = fmaf(-n, 0x1.62e4p-1f, x);
-    r = fmaf(-n, 0x1.7f7d1cp-20f, r);
-    float p = 0x1.a01a02p-13f;                              // 1/7!
-    p = fmaf(p, r, 0x1.6c16c2p-10f);                        // 1/6!
-    p = fmaf(p, r, 0x1.111112p-7f);                         // 1/5!
-    p = fmaf(p, r, 0x1.555556p-5f);                         // 1/4!
-    p = fmaf(p, r, 0x1.555556p-3f);                         // 1/3!
-    p = fmaf(p, r, 0.5f);
-    p = fmaf(p, r, 1.0f);
-    p = fmaf(p, r, 1.0f);
-    return __fmul_rn(p, __int_as_float(((int)n + 127) << 23));
-}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -230,7 +211,7 @@ __global__ void __launch_bounds__(128) k_decode_attn(const DecAttnParams p) {
 #pragma unroll
     for (int u = 1; u < 4; u++)
         if (sub == u) { sa = sc[u]; sb = sc[u + 4]; }
-    const float pa = exp_c(sa - m), pb = exp_c(sb - m);   // exp_c(-inf) = 0 for keys past the end
+    const float pa = exp_canon(sa - m), pb = exp_canon(sb - m);   // exp_canon(-inf) = 0 for keys past the end
     float l = 0.0f, o[8];
 #pragma unroll
     for (int e = 0; e < 8; e++) o[e] = 0.0f;
@@ -252,7 +233,7 @@ __global__ void __launch_bounds__(128) k_decode_attn(const DecAttnParams p) {
 #pragma unroll
         for (int e = 0; e < 8; e++) o[e] = __fadd_rn(o[e], __shfl_xor_sync(0xffffffffu, o[e], off));
     }
-    if (nkeys <= PAGE) {
+    if (nkeys <= PAGE && !p.partials_only) {
         decode_write_out(p, slot, h, g, sub, o, l);
         return;
     }
@@ -265,7 +246,7 @@ __global__ void __launch_bounds__(128) k_decode_attn(const DecAttnParams p) {
 }
 
 // Merge of the page partials of sequences longer than one page: warp per (slot, head), pages in
-// order (M = max m, w = exp_c(m - M), L = fma(w, l, L), O = fma(w, o, O)), 32 pages per batch staged
+// order (M = max m, w = exp_canon(m - M), L = fma(w, l, L), O = fma(w, o, O)), 32 pages per batch staged
 // in shared memory by lane-parallel loads.
 __global__ void __launch_bounds__(128) k_decode_merge(const DecAttnParams p) {
     __shared__ __align__(16) float sbuf[4][64 + 32 * 32];
@@ -295,7 +276,7 @@ __global__ void __launch_bounds__(128) k_decode_merge(const DecAttnParams p) {
         const int cnt = min(32, nch - c0);
         if (lane < cnt) {
             const float2 ml = __ldcg((const float2*)(part + (size_t)(c0 + lane) * PART_STRIDE));
-            sw[lane] = exp_c(ml.x - M);
+            sw[lane] = exp_canon(ml.x - M);
             sl[lane] = ml.y;
         }
         for (int i = lane; i < cnt * 8; i += 32) {
@@ -327,7 +308,7 @@ int launch_decode_attention(const DecAttnParams& p, cudaStream_t s) {
     dim3 grid(NH / 4, p.max_chunks, p.B);
     if (p.kv_f32) launch_pdl(k_decode_attn<float>, grid, dim3(128), DecShape<float>::SMEM, s, p);
     else launch_pdl(k_decode_attn<__half>, grid, dim3(128), DecShape<__half>::SMEM, s, p);
-    if (p.max_chunks <= 1) return 1;
+    if (p.max_chunks <= 1 || p.partials_only) return 1;
     launch_pdl(k_decode_merge, dim3((p.B * NH + 3) / 4), dim3(128), 0, s, p);
     return 2;
 }

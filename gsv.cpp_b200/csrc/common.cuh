@@ -54,6 +54,25 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {
     return r;
 }
 
+// exp(x) for x <= 0 in float, the decode-attention softmax and page-merge exponential: Cody-Waite reduction x = n*ln2 + r (ln2 split into a 15-bit head and a
+// float tail, so n*head is exact) and the degree-7 Taylor polynomial of exp(r), |r| <= ln2/2, by Horner
+// with fma; result p * 2^n. Max error ~1.2 ulp. x < -87 (or -inf) gives 0.
+__device__ __forceinline__ float exp_canon(float x) {
+    if (!(x >= -87.0f)) return 0.0f;
+    const float n = rintf(__fmul_rn(x, 0x1.715476p+0f));   // x / ln2, to nearest even
+    float r = fmaf(-n, 0x1.62e4p-1f, x);
+    r = fmaf(-n, 0x1.7f7d1cp-20f, r);
+    float p = 0x1.a01a02p-13f;                              // 1/7!
+    p = fmaf(p, r, 0x1.6c16c2p-10f);                        // 1/6!
+    p = fmaf(p, r, 0x1.111112p-7f);                         // 1/5!
+    p = fmaf(p, r, 0x1.555556p-5f);                         // 1/4!
+    p = fmaf(p, r, 0x1.555556p-3f);                         // 1/3!
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    return __fmul_rn(p, __int_as_float(((int)n + 127) << 23));
+}
+
 // Per-slot decode state (device), one entry per sequence slot.
 struct SlotState {
     int32_t active;       // 1 while the sequence is in flight

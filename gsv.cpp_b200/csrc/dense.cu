@@ -1,0 +1,570 @@
+// dense.cu -- the decode step's per-layer tail fused on a 16-CTA thread-block cluster.
+//
+// After the decode-attention kernel has left one partial result per (slot, head, KV page), one
+// cluster of 16 CTAs carries 8 slots through the rest of the layer and the next layer's QKV
+// projection (the reference's per-layer graph, src/gsv_ar.cpp:402-467):
+//   0  merge of the attention pages, head j = cluster rank j        -> Q8_0 block j of each row
+//   1  out-projection, output columns [32j, 32j+32), + residual x + bias, LayerNorm row statistics
+//   2  LayerNorm 1 on the CTA's 32 columns                           -> Q8_0 block j of n1
+//   3  FFN1, columns [128j, 128j+128), bias + ReLU                   -> Q8_0 blocks 4j..4j+3 of h
+//   4  FFN2, columns [32j, 32j+32), + residual n1 + bias, LayerNorm row statistics
+//   5  LayerNorm 2                                                   -> x (global) and its Q8_0 block j
+//   6  next layer's QKV: q, k, v columns of head j                   -> q (global), K/V page rows
+// Every CTA keeps full copies of the Q8_0 rows a GEMM reads; each CTA computes one 32-column block of
+// a row and pushes it into all 16 CTAs' shared memory (distributed shared memory), then the cluster
+// barrier publishes it. LayerNorm's double row sums are exchanged the same way.
+//
+// Arithmetic is that of the unfused kernels (gemm_q8.cu, misc.cu, attention.cu), operation for
+// operation: each Q8_0 output is one warp's sequential float chain over the K blocks in order,
+// acc = fma((float)isum_b, d_w * d_x, acc), from exact int32 block sums (mma.m16n8k32 s8 with a zero
+// accumulator); LayerNorm sums are double; the page merge follows the same page order.
+//
+// Weights: each CTA's slices of the four matrices (~200 KB per layer) are copied into shared memory by
+// TMA bulk copies issued before griddep_wait, so they load while the attention kernel runs.
+#include <cooperative_groups.h>
+
+#include "kernels.h"
+
+namespace cg = cooperative_groups;
+
+namespace gsvcu {
+
+namespace {
+
+constexpr int DR = 16;       // slots (rows) per cluster: two n = 8 tiles of mma.m16n8k32
+constexpr int DC = 16;       // CTAs per cluster
+constexpr int DT = 512;      // threads per CTA: one warp per row in the row-wise phases
+constexpr int NW = DT / 32;  // warps
+constexpr int KB1 = D / QK;  // K blocks of a 512-wide input (16)
+constexpr int KB2 = FF / QK; // K blocks of a 2048-wide input (64)
+constexpr int RS1 = D + 16;  // padded stride of a 512-wide int8 row in shared memory
+constexpr int RS2 = FF + 16;
+
+// shared-memory layout (bytes); activation rows are int8 [DR][RS] followed by f32 scales [DR][KB]
+constexpr int SM_W_OUT = 0;                        // out rows [32j, 32j+32): 2 row groups x 16 K blocks
+constexpr int SM_D_OUT = SM_W_OUT + 2 * KB1 * 512; // [32][16] fp16
+constexpr int SM_W_F1 = SM_D_OUT + 32 * KB1 * 2;   // ffn1 rows [128j, +128): 8 row groups
+constexpr int SM_D_F1 = SM_W_F1 + 8 * KB1 * 512;   // [128][16]
+constexpr int SM_W_F2 = SM_D_F1 + 128 * KB1 * 2;   // ffn2 rows [32j, +32): 2 row groups x 64 K blocks
+constexpr int SM_D_F2 = SM_W_F2 + 2 * KB2 * 512;   // [32][64]
+constexpr int SM_W_QKV = 0;                        // next layer's q|k|v rows of head j (reuses out + ffn1)
+constexpr int SM_D_QKV = SM_W_QKV + 6 * KB1 * 512; // [96][16]
+constexpr int ROWS1_BYTES = DR * RS1 + DR * KB1 * 4;
+constexpr int HROWS_BYTES = DR * RS2 + DR * KB2 * 4;
+constexpr int SM_AROWS = SM_D_F2 + 32 * KB2 * 2;   // attention output rows (Q8_0), all 16 blocks
+constexpr int SM_N1ROWS = SM_AROWS + ROWS1_BYTES;  // n1 rows (Q8_0); later the x rows of the next QKV
+constexpr int SM_XROWS = SM_N1ROWS;
+constexpr int SM_HROWS = SM_N1ROWS + ROWS1_BYTES;  // h rows (Q8_0), 2048 wide
+constexpr int SM_LNP1 = SM_HROWS + HROWS_BYTES;    // [16 src][DR rows] {sum, sum of squares} doubles
+constexpr int SM_LNP2 = SM_LNP1 + DC * DR * 16;
+constexpr int SM_XOWN = SM_LNP2 + DC * DR * 16;    // [DR][32] f32: this CTA's columns of x (phases 0-1)
+constexpr int SM_N1OWN = SM_XOWN;                  // [DR][32] f32: this CTA's columns of n1 (phases 2-4)
+constexpr int SM_PRE = SM_N1OWN + DR * 32 * 4;     // [DR][32] f32: pre-LayerNorm sums
+constexpr int SM_STG = SM_PRE + DR * 32 * 4;       // per warp: one staging slot per exchange (never reused)
+constexpr int STG_ATT = 0, STG_N1 = 32, STG_X = 64, STG_H = 96, STG_HD = 224, STG_WARP = 240;
+constexpr int SM_PAR = SM_STG + NW * STG_WARP;     // this CTA's bias / LayerNorm parameters (f32)
+constexpr int P_BOUT = 0, P_BF1 = 32, P_BF2 = 160, P_N1W = 192, P_N1B = 224, P_N2W = 256, P_N2B = 288, P_BQKV = 320,
+              P_COUNT = 416;
+constexpr int SM_ROWMETA = SM_PAR + P_COUNT * 4;   // per row: pages to merge (0: not decoding), KV page, KV pos
+constexpr int SM_BARS = SM_ROWMETA + DR * 3 * 4;   // 4 weight barriers + 6 exchange barriers
+constexpr int SMEM_DENSE = SM_BARS + 10 * 8;
+// aliases: phase-0 page-merge scratch in the h rows; FFN1's f32 outputs in the attention rows
+constexpr int MERGE_ROW_BYTES = (16 + 16 + 16 * 32) * 4;   // one row: 16 pages' w, l, o
+static_assert(NW == DR && NW * MERGE_ROW_BYTES <= HROWS_BYTES, "merge scratch");
+static_assert(DR * 128 * 4 <= ROWS1_BYTES, "ffn1 staging");
+static_assert(SM_D_QKV + 96 * KB1 * 2 <= SM_W_F2, "qkv weights reuse out + ffn1");
+static_assert(SMEM_DENSE <= 232448, "shared memory");
+static_assert(SM_AROWS % 16 == 0 && SM_N1ROWS % 16 == 0 && SM_HROWS % 16 == 0 && SM_D_F1 % 16 == 0 &&
+                  SM_D_F2 % 16 == 0 && SM_D_QKV % 16 == 0 && SM_LNP1 % 16 == 0 && SM_LNP2 % 16 == 0 &&
+                  SM_STG % 16 == 0 && STG_WARP % 16 == 0 && SM_BARS % 8 == 0 && (DR * RS1) % 16 == 0 &&
+                  (DR * RS2) % 16 == 0,
+              "alignment");
+// bytes each CTA receives per exchange (every CTA sends to all 16, itself included)
+constexpr uint32_t EX_BLOCK = DC * DR * (32 + 4);  // one Q8_0 block (32 B + f32 scale) per (sender, row)
+constexpr uint32_t EX_STATS = DC * DR * 16;        // one {sum, sum of squares} per (sender, row)
+enum { BW_OUT = 0, BW_F1, BW_F2, BW_QKV, BX_ATT, BX_LN1, BX_N1, BX_H, BX_LN2, BX_X };
+
+__device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void d_mbar_init(uint32_t bar) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void d_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void d_bulk(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+// Bounded wait on phase 0 of an mbarrier by a whole warp; false if the limit was reached.
+__device__ __forceinline__ bool d_wait(uint32_t bar) {
+    uint32_t it = 0, ok = 0;
+    for (;;) {
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(ok)
+            : "r"(bar)
+            : "memory");
+        if (ok || ++it == (1u << 22)) break;
+    }
+    return __all_sync(0xffffffffu, ok != 0);
+}
+// Address of a local shared-memory location in the shared window of cluster CTA `rank`.
+__device__ __forceinline__ uint32_t d_mapa(uint32_t local, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+    return r;
+}
+// Remote stores into a peer's shared memory that count their bytes on the peer's mbarrier.
+__device__ __forceinline__ void d_st_async16(uint32_t addr, uint4 v, uint32_t bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(addr),
+                 "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(bar)
+                 : "memory");
+}
+__device__ __forceinline__ void d_st_async4(uint32_t addr, uint32_t v, uint32_t bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(addr), "r"(v),
+                 "r"(bar)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mma_s8(int (&c)[4], const uint4& a, uint32_t b0, uint32_t b1) {
+    asm(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%11,%12,%13};\n"
+        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+        : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+// One warp: row group lr (16 features) of a weight slice in shared memory against row tile rt (rows
+// 8rt..8rt+7) of X, all KB blocks in order. Thread (g, t) ends with features 16lr+g, 16lr+g+8 x rows
+// 8rt+2t, 8rt+2t+1 in acc[0..3].
+template <int KB>
+__device__ __forceinline__ void rg_gemm(const uint8_t* W, const uint16_t* DW, int lr, const int8_t* X, int rs,
+                                        const float* DX, int rt, float (&acc)[4]) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int fa = lr * 16 + g, fb = fa + 8, ra = rt * 8 + 2 * t, rb = ra + 1;
+    acc[0] = acc[1] = acc[2] = acc[3] = 0.0f;
+    const uint4* wp = (const uint4*)W + (size_t)lr * KB * 32 + lane;
+    const int8_t* xr = X + (rt * 8 + g) * rs + t * 4;
+    constexpr int KC = 8;   // K blocks whose MMAs are issued back to back before their chain steps
+#pragma unroll 1
+    for (int k0 = 0; k0 < KB; k0 += KC) {
+        int c[KC][4];
+#pragma unroll
+        for (int j = 0; j < KC; j++) {
+            const int kb = k0 + j;
+            const uint4 a = wp[kb * 32];
+            const uint32_t b0 = *(const uint32_t*)(xr + kb * 32), b1 = *(const uint32_t*)(xr + kb * 32 + 16);
+            mma_s8(c[j], a, b0, b1);
+        }
+#pragma unroll
+        for (int j = 0; j < KC; j++) {
+            const int kb = k0 + j;
+            const float dwa = h2f(DW[fa * KB + kb]), dwb = h2f(DW[fb * KB + kb]);
+            const float dxa = DX[ra * KB + kb], dxb = DX[rb * KB + kb];
+            acc[0] = fmaf((float)c[j][0], __fmul_rn(dwa, dxa), acc[0]);
+            acc[1] = fmaf((float)c[j][1], __fmul_rn(dwa, dxb), acc[1]);
+            acc[2] = fmaf((float)c[j][2], __fmul_rn(dwb, dxa), acc[2]);
+            acc[3] = fmaf((float)c[j][3], __fmul_rn(dwb, dxb), acc[3]);
+        }
+    }
+}
+
+// Quantize the 32 values v (lane l holds column l of the block) into q (32 B of shared memory); returns
+// the block's scale, rounded through fp16 (what a reader of the fp16 scale sees), in every lane.
+__device__ __forceinline__ float q8_block_stage(float v, int8_t* q) {
+    const int lane = threadIdx.x & 31;
+    float amax = fabsf(v);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    float dsc, id;
+    q8_scale(amax, dsc, id);
+    q[lane] = q8_val(v, id);
+    return h2f(f2h(dsc));
+}
+
+__device__ __forceinline__ void d_bulk_s2c(uint32_t dst_cluster, uint32_t src, uint32_t bytes, uint32_t bar_cluster) {
+    asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     dst_cluster),
+                 "r"(src), "r"(bytes), "r"(bar_cluster)
+                 : "memory");
+}
+
+// Send one staged Q8_0 block (32 B at sq) with scale d as block b of row r of the rows region `rows`
+// (int8 stride rs, f32 scales [DR][kb] after the rows) of every CTA; bytes counted on `bar`. One warp:
+// lanes 0..15 copy the quants to CTA lane, lanes 16..31 store the scale to CTA lane - 16.
+__device__ __forceinline__ void send_block(const int8_t* sq, float d, int r, uint32_t rows, int rs, int kb, int b,
+                                           uint32_t bar) {
+    const int lane = threadIdx.x & 31, dst = lane & 15;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // staged quants -> async proxy
+    __syncwarp();
+    const uint32_t rrows = d_mapa(rows, dst), rbar = d_mapa(bar, dst);
+    if (lane < 16) d_bulk_s2c(rrows + r * rs + b * 32, su32(sq), 32, rbar);
+    else d_st_async4(rrows + DR * rs + (r * kb + b) * 4, __float_as_uint(d), rbar);
+}
+// Send 4 consecutive staged blocks (128 B at sq) with their 4 scales (16 B at sd) as blocks b0..b0+3.
+__device__ __forceinline__ void send_blocks4(const int8_t* sq, const float* sd, int r, uint32_t rows, int rs, int kb,
+                                             int b0, uint32_t bar) {
+    const int lane = threadIdx.x & 31, dst = lane & 15;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+    const uint32_t rrows = d_mapa(rows, dst), rbar = d_mapa(bar, dst);
+    if (lane < 16) d_bulk_s2c(rrows + r * rs + b0 * 32, su32(sq), 128, rbar);
+    else d_bulk_s2c(rrows + DR * rs + (r * kb + b0) * 4, su32(sd), 16, rbar);
+}
+
+// LayerNorm row statistics of row r (lane = column, 32 values) in double, sent as slot [rank][r] of
+// every CTA's table.
+__device__ __forceinline__ void send_row_stats(float v, int r, int rank, uint32_t table, uint32_t bar) {
+    const int lane = threadIdx.x & 31;
+    double s = (double)v, s2 = (double)v * (double)v;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        s += __shfl_xor_sync(0xffffffffu, s, off);
+        s2 += __shfl_xor_sync(0xffffffffu, s2, off);
+    }
+    if (lane < DC) {
+        const uint4 w = make_uint4(__double2loint(s), __double2hiint(s), __double2loint(s2), __double2hiint(s2));
+        d_st_async16(d_mapa(table, lane) + (rank * DR + r) * 16, w, d_mapa(bar, lane));
+    }
+}
+
+// LayerNorm (misc.cu k_layernorm_q8 arithmetic) of one column of row r from the table; w, b: the column's
+// weight and bias.
+__device__ __forceinline__ float ln_apply(const double* lnp, int r, float v, float w, float b) {
+    double s = 0.0, s2 = 0.0;
+#pragma unroll
+    for (int src = 0; src < DC; src++) {
+        s += lnp[(src * DR + r) * 2];
+        s2 += lnp[(src * DR + r) * 2 + 1];
+    }
+    const float mean = (float)(s * (1.0 / D));   // D = 512: exact, equals s / D
+    const float var = fmaf(-mean, mean, (float)(s2 * (1.0 / D)));
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f)));
+    return fmaf(__fmul_rn(__fsub_rn(v, mean), inv), w, b);
+}
+
+}  // namespace
+
+template <bool HAS_QKV>
+__global__ void __launch_bounds__(DT, 1) k_dense_layer(const DenseParams p) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    cg::cluster_group cl = cg::this_cluster();
+    const int rank = (int)cl.block_rank();
+    const int r0 = (blockIdx.x / DC) * DR;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int sub = lane & 3;
+    const uint32_t bars = su32(sm + SM_BARS);
+    auto bar = [&](int i) { return bars + 8 * i; };
+    bool ok = true;
+
+    if (tid == 0) {
+        for (int i = 0; i < 10; i++) d_mbar_init(bar(i));
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        // exchanges: the bytes the 16 CTAs will send here
+        d_expect_tx(bar(BX_ATT), EX_BLOCK);
+        d_expect_tx(bar(BX_LN1), EX_STATS);
+        d_expect_tx(bar(BX_N1), EX_BLOCK);
+        d_expect_tx(bar(BX_H), 4 * EX_BLOCK);
+        d_expect_tx(bar(BX_LN2), EX_STATS);
+        if (HAS_QKV) d_expect_tx(bar(BX_X), EX_BLOCK);
+    }
+    // announce this CTA's armed barriers now; wait for the peers' only before the first send
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    if (tid == 0) {   // weights of this CTA's slices (constant), before the wait for the attention kernel
+        d_expect_tx(bar(BW_OUT), 2 * KB1 * 512 + 32 * KB1 * 2);
+        d_bulk(su32(sm + SM_W_OUT), p.w_out + (size_t)(2 * rank) * KB1 * 32, 2 * KB1 * 512, bar(BW_OUT));
+        d_bulk(su32(sm + SM_D_OUT), p.d_out + (size_t)(32 * rank) * KB1, 32 * KB1 * 2, bar(BW_OUT));
+        d_expect_tx(bar(BW_F1), 8 * KB1 * 512 + 128 * KB1 * 2);
+        d_bulk(su32(sm + SM_W_F1), p.w_f1 + (size_t)(8 * rank) * KB1 * 32, 8 * KB1 * 512, bar(BW_F1));
+        d_bulk(su32(sm + SM_D_F1), p.d_f1 + (size_t)(128 * rank) * KB1, 128 * KB1 * 2, bar(BW_F1));
+        d_expect_tx(bar(BW_F2), 2 * KB2 * 512 + 32 * KB2 * 2);
+        d_bulk(su32(sm + SM_W_F2), p.w_f2 + (size_t)(2 * rank) * KB2 * 32, 2 * KB2 * 512, bar(BW_F2));
+        d_bulk(su32(sm + SM_D_F2), p.d_f2 + (size_t)(32 * rank) * KB2, 32 * KB2 * 2, bar(BW_F2));
+    }
+    // slot state, block table, x and this CTA's parameters were written two or more kernels ago (or by
+    // the host): read them while the attention kernel finishes
+    float* par = (float*)(sm + SM_PAR);
+    int* meta = (int*)(sm + SM_ROWMETA);
+    float* xown = (float*)(sm + SM_XOWN);
+    for (int i = tid; i < P_COUNT; i += DT) {
+        float v;
+        if (i < P_BF1) v = p.b_out[32 * rank + i - P_BOUT];
+        else if (i < P_BF2) v = p.b_f1[128 * rank + i - P_BF1];
+        else if (i < P_N1W) v = p.b_f2[32 * rank + i - P_BF2];
+        else if (i < P_N1B) v = p.n1w[32 * rank + i - P_N1W];
+        else if (i < P_N2W) v = p.n1b[32 * rank + i - P_N1B];
+        else if (i < P_N2B) v = p.n2w[32 * rank + i - P_N2W];
+        else if (i < P_BQKV) v = p.n2b[32 * rank + i - P_N2B];
+        else v = HAS_QKV ? p.b_qkv[((i - P_BQKV) >> 5) * D + 32 * rank + ((i - P_BQKV) & 31)] : 0.0f;
+        par[i] = v;
+    }
+    if (tid < DR) {
+        const int slot = r0 + tid;
+        int nch = 0, page = 0, pos = 0;
+        if (slot < p.M && p.st[slot].decode_now) {
+            pos = p.st[slot].kvpos;
+            nch = pos / PAGE + 1;
+            if (HAS_QKV) page = p.kv.block_table[(size_t)slot * p.kv.max_pages + pos / PAGE];
+        }
+        meta[tid * 3] = nch;
+        meta[tid * 3 + 1] = page;
+        meta[tid * 3 + 2] = pos;
+    }
+    for (int i = tid; i < DR * 32; i += DT) {
+        const int slot = r0 + (i >> 5);
+        xown[i] = slot < p.M ? p.x[(size_t)slot * D + 32 * rank + (i & 31)] : 0.0f;
+    }
+    griddep_wait();
+    griddep_launch();
+    __syncthreads();
+
+    uint8_t* stg = sm + SM_STG + warp * STG_WARP;
+    float* n1own = (float*)(sm + SM_N1OWN);
+    float* pre = (float*)(sm + SM_PRE);
+    const int r = warp;   // the row of this warp in the row-wise phases
+
+    float att_d = 0.0f;
+    // ---- phase 0: merge the pages of head `rank` for row r. One round of loads brings every page's m and
+    // the first 16 pages' l and o; longer rows load 16 more pages per batch.
+    {
+        const int nch = meta[r * 3];
+        const float* part = p.part + (((size_t)(r0 + r) * NH + rank) * p.max_chunks) * PART_STRIDE;
+        float* scr = (float*)(sm + SM_HROWS + warp * MERGE_ROW_BYTES);
+        auto stage_batch = [&](int c0) {
+            const int cnt = max(0, min(16, nch - c0));
+            if (lane < cnt) {
+                const float2 ml = __ldcg((const float2*)(part + (size_t)(c0 + lane) * PART_STRIDE));
+                scr[lane] = ml.x;   // m, replaced by the page weight once M is known
+                scr[16 + lane] = ml.y;
+            }
+            for (int i = lane; i < cnt * 8; i += 32) {
+                const int c = i >> 3, jj = i & 7;
+                *(float4*)(scr + 32 + c * 32 + jj * 4) =
+                    __ldcg((const float4*)(part + (size_t)(c0 + c) * PART_STRIDE + 4 + jj * 4));
+            }
+        };
+        stage_batch(0);
+        float M = -INFINITY;
+        for (int c = lane; c < nch; c += 32) M = fmaxf(M, __ldcg(part + (size_t)c * PART_STRIDE));
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+        float L = 0.0f, O[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) O[e] = 0.0f;
+        for (int c0 = 0; c0 < nch; c0 += 16) {
+            if (c0 > 0) stage_batch(c0);
+            __syncwarp();
+            const int cnt = min(16, nch - c0);
+            if (lane < cnt) scr[lane] = exp_canon(scr[lane] - M);
+            __syncwarp();
+            for (int c = 0; c < cnt; c++) {
+                const float w = scr[c];
+                L = fmaf(w, scr[16 + c], L);
+                const float4 a = *(const float4*)(scr + 32 + c * 32 + sub * 8);
+                const float4 b = *(const float4*)(scr + 32 + c * 32 + sub * 8 + 4);
+                O[0] = fmaf(w, a.x, O[0]); O[1] = fmaf(w, a.y, O[1]); O[2] = fmaf(w, a.z, O[2]);
+                O[3] = fmaf(w, a.w, O[3]); O[4] = fmaf(w, b.x, O[4]); O[5] = fmaf(w, b.y, O[5]);
+                O[6] = fmaf(w, b.z, O[6]); O[7] = fmaf(w, b.w, O[7]);
+            }
+            __syncwarp();
+        }
+        if (nch) {
+            // lane (g, s) holds dims 8s..8s+7; column `lane` of the block comes from lane lane/8
+            float mine[8], v = 0.0f;
+#pragma unroll
+            for (int e = 0; e < 8; e++) mine[e] = __fdiv_rn(O[e], L);
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                const float t = __shfl_sync(0xffffffffu, mine[e], lane >> 3);
+                if ((lane & 7) == e) v = t;
+            }
+            att_d = q8_block_stage(v, (int8_t*)(stg + STG_ATT));
+        } else {
+            ((int8_t*)(stg + STG_ATT))[lane] = 0;
+        }
+    }
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");   // every peer's barriers are armed
+    send_block((const int8_t*)(stg + STG_ATT), att_d, r, su32(sm + SM_AROWS), RS1, KB1, rank, bar(BX_ATT));
+
+    // ---- phase 1: out-projection + residual + bias (columns 32*rank + 0..31)
+    if (warp < 4) {
+        ok &= d_wait(bar(BX_ATT));
+        ok &= d_wait(bar(BW_OUT));
+        float acc[4];
+        const int lr = warp & 1, rt = warp >> 1;
+        rg_gemm<KB1>(sm + SM_W_OUT, (const uint16_t*)(sm + SM_D_OUT), lr, (const int8_t*)(sm + SM_AROWS), RS1,
+                     (const float*)(sm + SM_AROWS + DR * RS1), rt, acc);
+        const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int f = lr * 16 + g + (i >= 2 ? 8 : 0), rr = rt * 8 + 2 * t + (i & 1);
+            pre[rr * 32 + f] = __fadd_rn(__fadd_rn(xown[rr * 32 + f], acc[i]), par[P_BOUT + f]);
+        }
+    }
+    __syncthreads();
+    send_row_stats(pre[r * 32 + lane], r, rank, su32(sm + SM_LNP1), bar(BX_LN1));
+
+    // ---- phase 2: LayerNorm 1 of the CTA's columns -> n1 (kept) and its Q8_0 block (sent)
+    ok &= d_wait(bar(BX_LN1));
+    {
+        const float n1 = ln_apply((const double*)(sm + SM_LNP1), r, pre[r * 32 + lane], par[P_N1W + lane],
+                                  par[P_N1B + lane]);
+        n1own[r * 32 + lane] = n1;
+        const float d = q8_block_stage(n1, (int8_t*)(stg + STG_N1));
+        send_block((const int8_t*)(stg + STG_N1), d, r, su32(sm + SM_N1ROWS), RS1, KB1, rank, bar(BX_N1));
+    }
+
+    // ---- phase 3: FFN1 (columns 128*rank + 0..127), bias + ReLU: warp = (row group, row tile)
+    float* hown = (float*)(sm + SM_AROWS);   // [DR][128] f32 (the attention rows are consumed)
+    ok &= d_wait(bar(BX_N1));
+    ok &= d_wait(bar(BW_F1));
+    {
+        const int lr = warp & 7, rt = warp >> 3;
+        float acc[4];
+        rg_gemm<KB1>(sm + SM_W_F1, (const uint16_t*)(sm + SM_D_F1), lr, (const int8_t*)(sm + SM_N1ROWS), RS1,
+                     (const float*)(sm + SM_N1ROWS + DR * RS1), rt, acc);
+        const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int f = lr * 16 + g + (i >= 2 ? 8 : 0), rr = rt * 8 + 2 * t + (i & 1);
+            const float h = __fadd_rn(acc[i], par[P_BF1 + f]);
+            hown[rr * 128 + f] = h > 0.0f ? h : 0.0f;
+        }
+    }
+    __syncthreads();
+    if (HAS_QKV && tid == 0) {   // out + ffn1 slices are consumed: the next layer's q|k|v rows go there
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        d_expect_tx(bar(BW_QKV), 6 * KB1 * 512 + 96 * KB1 * 2);
+        for (int part = 0; part < 3; part++) {
+            d_bulk(su32(sm + SM_W_QKV + part * 2 * KB1 * 512),
+                   p.w_qkv + (size_t)(part * (D / 16) + 2 * rank) * KB1 * 32, 2 * KB1 * 512, bar(BW_QKV));
+            d_bulk(su32(sm + SM_D_QKV + part * 32 * KB1 * 2), p.d_qkv + (size_t)(part * D + 32 * rank) * KB1,
+                   32 * KB1 * 2, bar(BW_QKV));
+        }
+    }
+    {
+        float* hd = (float*)(stg + STG_HD);
+#pragma unroll
+        for (int b = 0; b < 4; b++) {
+            const float d = q8_block_stage(hown[r * 128 + b * 32 + lane], (int8_t*)(stg + STG_H) + b * 32);
+            if (lane == 0) hd[b] = d;
+        }
+        send_blocks4((const int8_t*)(stg + STG_H), hd, r, su32(sm + SM_HROWS), RS2, KB2, 4 * rank, bar(BX_H));
+    }
+
+    // ---- phase 4: FFN2 + residual n1 + bias (columns 32*rank + 0..31)
+    if (warp < 4) {
+        ok &= d_wait(bar(BX_H));
+        ok &= d_wait(bar(BW_F2));
+        float acc[4];
+        const int lr = warp & 1, rt = warp >> 1;
+        rg_gemm<KB2>(sm + SM_W_F2, (const uint16_t*)(sm + SM_D_F2), lr, (const int8_t*)(sm + SM_HROWS), RS2,
+                     (const float*)(sm + SM_HROWS + DR * RS2), rt, acc);
+        const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int f = lr * 16 + g + (i >= 2 ? 8 : 0), rr = rt * 8 + 2 * t + (i & 1);
+            pre[rr * 32 + f] = __fadd_rn(__fadd_rn(n1own[rr * 32 + f], acc[i]), par[P_BF2 + f]);
+        }
+    }
+    __syncthreads();
+    send_row_stats(pre[r * 32 + lane], r, rank, su32(sm + SM_LNP2), bar(BX_LN2));
+
+    // ---- phase 5: LayerNorm 2 -> x (global, next layer's residual) and its Q8_0 block
+    ok &= d_wait(bar(BX_LN2));
+    {
+        const float xv = ln_apply((const double*)(sm + SM_LNP2), r, pre[r * 32 + lane], par[P_N2W + lane],
+                                  par[P_N2B + lane]);
+        if (r0 + r < p.M) p.x[(size_t)(r0 + r) * D + 32 * rank + lane] = xv;
+        if (HAS_QKV) {
+            const float d = q8_block_stage(xv, (int8_t*)(stg + STG_X));
+            send_block((const int8_t*)(stg + STG_X), d, r, su32(sm + SM_XROWS), RS1, KB1, rank, bar(BX_X));
+        }
+    }
+
+    // ---- phase 6: next layer's q, k, v of head `rank` (+ bias); K/V into the pages. warp = (row group, tile)
+    if (HAS_QKV && warp < 12) {
+        ok &= d_wait(bar(BX_X));
+        ok &= d_wait(bar(BW_QKV));
+        const int lr = warp % 6, rt = warp / 6, part = lr >> 1, g = lane >> 2, t = lane & 3;
+        float acc[4];
+        rg_gemm<KB1>(sm + SM_W_QKV, (const uint16_t*)(sm + SM_D_QKV), lr, (const int8_t*)(sm + SM_XROWS), RS1,
+                     (const float*)(sm + SM_XROWS + DR * RS1), rt, acc);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int f = (lr & 1) * 16 + g + (i >= 2 ? 8 : 0), rr = rt * 8 + 2 * t + (i & 1), slot = r0 + rr;
+            if (slot >= p.M) continue;
+            const float y = __fadd_rn(acc[i], par[P_BQKV + part * 32 + f]);
+            if (part == 0) {
+                p.q[(size_t)slot * p.q_stride + 32 * rank + f] = y;
+            } else if (meta[rr * 3]) {
+                const int page = meta[rr * 3 + 1], pos = meta[rr * 3 + 2];
+                const size_t e = ((((size_t)page * p.kv.n_layer + p.kv.layer) * 2 + (part - 1)) * NH + rank) *
+                                     (PAGE * HD) +
+                                 (size_t)(pos % PAGE) * HD + f;
+                if (p.kv.kv_f32) ((float*)p.kv.pool)[e] = y;
+                else ((__half*)p.kv.pool)[e] = __float2half_rn(y);
+            }
+        }
+    }
+    if (!__all_sync(0xffffffffu, ok)) {
+        // a copy or an exchange never completed: flag it and wait (bounded) for what may still arrive
+        if (lane == 0 && p.err) atomicExch(p.err, 1);
+        for (int i = 0; i < 10; i++)
+            if (HAS_QKV || (i != BW_QKV && i != BX_X)) (void)d_wait(bar(i));
+    }
+    // no CTA leaves while a peer may still be sending to it
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;\nbarrier.cluster.wait.aligned;" ::: "memory");
+}
+
+cudaError_t dense_init_device(bool* usable) {
+    *usable = false;
+    cudaError_t e;
+    void (*ks[2])(const DenseParams) = {k_dense_layer<true>, k_dense_layer<false>};
+    for (auto k : ks) {
+        if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_DENSE))) return e;
+        if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1))) return e;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(DC);
+    cfg.blockDim = dim3(DT);
+    cfg.dynamicSmemBytes = SMEM_DENSE;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = DC;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, k_dense_layer<true>, &cfg);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return cudaSuccess;   // not usable: the unfused kernels run instead
+    }
+    *usable = n >= 1;
+    return cudaSuccess;
+}
+
+void launch_dense_layer(const DenseParams& p, cudaStream_t s) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((p.M + DR - 1) / DR * DC));
+    cfg.blockDim = dim3(DT);
+    cfg.dynamicSmemBytes = SMEM_DENSE;
+    cfg.stream = s;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = DC;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 2;
+    if (p.w_qkv) cudaLaunchKernelEx(&cfg, k_dense_layer<true>, p);
+    else cudaLaunchKernelEx(&cfg, k_dense_layer<false>, p);
+}
+
+}  // namespace gsvcu

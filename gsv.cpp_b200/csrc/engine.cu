@@ -236,6 +236,8 @@ struct gsvcu_ctx {
     size_t op_part_n = 0;
     // set by decode attention when a bounded wait for its staged K/V gave up (checked on status reads)
     int32_t* att_err = nullptr;
+    // decode steps run the fused layer tail (dense.cu) when the device can hold its cluster
+    bool dense_ok = false, fused = true;
 
     ~gsvcu_ctx();
     int load(const char* path);
@@ -755,6 +757,49 @@ int gsvcu_ctx::launch_step(cudaStream_t s, float* dump, int dump_row, const int*
     nk++;
     TRY(mark(1));
     const float scale = 1.0f / std::sqrt((float)HD);
+    if (fused && dense_ok && !dump) {
+        // fused layers: QKV of layer 0, then per layer the page attention and the cluster layer tail
+        // (merge, out, LN1, FFN1, FFN2, LN2, next layer's QKV); 2 + 1 + 2 NL + 1 kernels
+        {
+            const LayerW& w = L[0];
+            GemmQ8Params g;
+            g.xq = xq; g.xd = xd; g.M = M; g.wq = w.wq[0]; g.wd = w.wd[0]; g.N = 3 * D; g.K = D; g.bias = w.b_qkv;
+            g.y = qkv;
+            g.kv.pool = pool; g.kv.kv_f32 = kv_f32; g.kv.n_layer = NL; g.kv.layer = 0; g.kv.block_table = block_table;
+            g.kv.max_pages = max_pages; g.kv.st = st;
+            launch_gemm_q8(g, EPI_BIAS, s);
+            nk++;
+            TRY(mark(GSVCU_PROF_QKV_GEMM));
+        }
+        for (int li = 0; li < NL; li++) {
+            const LayerW& w = L[li];
+            DecAttnParams a;
+            a.q = qkv; a.q_stride = 3 * D; a.pool = pool; a.kv_f32 = kv_f32; a.n_layer = NL; a.layer = li;
+            a.block_table = block_table; a.max_pages = max_pages; a.st = st; a.B = M; a.max_chunks = max_chunks;
+            a.scale = scale; a.out_q = aq; a.out_d = ad; a.part = part; a.partials_only = 1; a.err = att_err;
+            nk += launch_decode_attention(a, s);
+            TRY(mark(GSVCU_PROF_DECODE_ATTN));
+            DenseParams d;
+            d.M = M; d.st = st; d.part = part; d.max_chunks = max_chunks;
+            d.w_out = w.wq[1]; d.d_out = w.wd[1]; d.b_out = w.b_out; d.n1w = w.n1w; d.n1b = w.n1b;
+            d.w_f1 = w.wq[2]; d.d_f1 = w.wd[2]; d.b_f1 = w.b_f1; d.w_f2 = w.wq[3]; d.d_f2 = w.wd[3]; d.b_f2 = w.b_f2;
+            d.n2w = w.n2w; d.n2b = w.n2b; d.x = x; d.err = att_err;
+            if (li + 1 < NL) {
+                const LayerW& wn = L[li + 1];
+                d.w_qkv = wn.wq[0]; d.d_qkv = wn.wd[0]; d.b_qkv = wn.b_qkv; d.q = qkv; d.q_stride = 3 * D;
+                d.kv.pool = pool; d.kv.kv_f32 = kv_f32; d.kv.n_layer = NL; d.kv.layer = li + 1;
+                d.kv.block_table = block_table; d.kv.max_pages = max_pages; d.kv.st = st;
+            }
+            launch_dense_layer(d, s);
+            nk++;
+            TRY(mark(GSVCU_PROF_DENSE));
+        }
+        launch_gemm_f32d(x, D, nullptr, M, predict, V, D, nullptr, 0, logits, V, s);
+        nk++;
+        TRY(mark(GSVCU_PROF_PREDICT));
+        graph_kernels = nk;
+        return GSVCU_OK;
+    }
     for (int li = 0; li < NL; li++) {
         const LayerW& w = L[li];
         GemmQ8Params g;
@@ -893,12 +938,15 @@ int gsvcu_create(int device, gsvcu_ctx** out) {
     cudaDeviceProp prop;
     if (cudaGetDeviceProperties(&prop, device) != cudaSuccess || prop.major != 10) return GSVCU_ERR_DEVICE;
     DeviceGuard g(device);
-    if (gemm_q8_init_device() != cudaSuccess || attention_init_device() != cudaSuccess) {
+    bool dense_usable = false;
+    if (gemm_q8_init_device() != cudaSuccess || attention_init_device() != cudaSuccess ||
+        dense_init_device(&dense_usable) != cudaSuccess) {
         cudaGetLastError();
         return GSVCU_ERR_CUDA;
     }
     gsvcu_ctx* c = new gsvcu_ctx();
     c->device = device;
+    c->dense_ok = dense_usable;
     if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
         cudaMalloc((void**)&c->att_err, sizeof(int32_t)) != cudaSuccess ||
         cudaMemset(c->att_err, 0, sizeof(int32_t)) != cudaSuccess) {
@@ -1373,6 +1421,20 @@ int gsvcu_step_profile(gsvcu_ctx* ctx, int32_t n_steps, float* ms_by_class, int6
     if (attn_bytes) *attn_bytes = bytes;
     return GSVCU_OK;
 }
+
+int gsvcu_set_fused_decode(gsvcu_ctx* ctx, int32_t on) {
+    if (!ctx) return GSVCU_ERR_ARG;
+    DeviceGuard g(ctx->device);
+    if (ctx->fused != (on != 0) && ctx->graph) {   // the captured step belongs to the other variant
+        cudaStreamSynchronize(ctx->stream);
+        cudaGraphExecDestroy(ctx->graph);
+        ctx->graph = nullptr;
+    }
+    ctx->fused = on != 0;
+    return GSVCU_OK;
+}
+
+int gsvcu_fused_decode(const gsvcu_ctx* ctx) { return ctx && ctx->fused && ctx->dense_ok ? 1 : 0; }
 
 int gsvcu_sync(gsvcu_ctx* ctx) {
     if (!ctx) return GSVCU_ERR_ARG;

@@ -102,6 +102,7 @@ struct DecAttnParams {
     uint16_t* out_d = nullptr;
     float* out_f32 = nullptr;
     float* part = nullptr;               // scratch [B][NH][max_chunks][PART_STRIDE]: m, l, -, -, o[HD]
+    int partials_only = 0;               // 1: every page leaves its partial (the fused layer tail merges)
     int32_t* err = nullptr;              // set to 1 if a bounded wait gave up (may be null)
 };
 // Split-KV work items of decode attention: one per 64-key page. A page's partial result is
@@ -115,10 +116,36 @@ inline bool decode_attention_aligned(const float* q, int q_stride, const void* p
     return ((uintptr_t)q & 15) == 0 && (q_stride & 3) == 0 && ((uintptr_t)pool & 15) == 0 &&
            ((uintptr_t)out_q & 7) == 0 && ((uintptr_t)out_f32 & 15) == 0;
 }
-// Returns the number of kernels launched (2 when sequences may span several pages: pages + merge).
+// Returns the number of kernels launched (2 when sequences may span several pages: pages + merge;
+// 1 with partials_only, where the caller merges).
 int launch_decode_attention(const DecAttnParams& p, cudaStream_t s);
 // Raise the dynamic shared-memory limit of the decode-attention kernels on the current device.
 cudaError_t attention_init_device();
+
+// ------------------------------------------------------------ fused decode layer tail (dense.cu)
+// Page merge -> out-projection + residual -> LayerNorm 1 -> FFN1 (ReLU) -> FFN2 + residual ->
+// LayerNorm 2 [-> next layer's QKV with the K/V page store], one 16-CTA cluster per 8 slots.
+struct DenseParams {
+    int M = 0;                          // slots (rows); a multiple of 8 is not required
+    const SlotState* st = nullptr;
+    const float* part = nullptr;        // attention partials of this layer (partials_only launch)
+    int max_chunks = 0;
+    const uint4* w_out = nullptr; const uint16_t* d_out = nullptr; const float* b_out = nullptr;
+    const float* n1w = nullptr; const float* n1b = nullptr;
+    const uint4* w_f1 = nullptr; const uint16_t* d_f1 = nullptr; const float* b_f1 = nullptr;
+    const uint4* w_f2 = nullptr; const uint16_t* d_f2 = nullptr; const float* b_f2 = nullptr;
+    const float* n2w = nullptr; const float* n2b = nullptr;
+    float* x = nullptr;                 // [M][D] residual stream: this layer's input in, its output out
+    const uint4* w_qkv = nullptr;       // next layer's QKV (nullptr: last layer)
+    const uint16_t* d_qkv = nullptr; const float* b_qkv = nullptr;
+    float* q = nullptr;                 // next layer's q, row stride q_stride
+    int q_stride = 0;
+    KvWrite kv;                         // next layer's K/V page store (decode: st)
+    int32_t* err = nullptr;             // set to 1 if a bounded wait gave up
+};
+// Set the kernel attributes on the current device; *usable = a 16-CTA cluster of it can be resident.
+cudaError_t dense_init_device(bool* usable);
+void launch_dense_layer(const DenseParams& p, cudaStream_t s);
 
 struct PrefillTile { int32_t seq, q0; };
 struct PrefAttnParams {

@@ -84,10 +84,12 @@ SIGNATURES = {
     "gsvcu_kernel_launches": ([_P], C.c_int64),
     "gsvcu_stream": ([_P], C.c_void_p),
     "gsvcu_op_decode_attention_noalloc": ([_P, _P, _I, _P, _I, _I, _I, _P, _I, _P, _P, _I, _P, _P, _P], C.c_int),
+    "gsvcu_set_fused_decode": ([_P, _I], C.c_int),
+    "gsvcu_fused_decode": ([_P], C.c_int),
 }
 
 PROF_CLASSES = ["sampler", "step_prep", "qkv_gemm", "decode_attn", "out_gemm", "layernorm", "ffn1_gemm", "ffn2_gemm",
-                "predict"]
+                "predict", "dense_fused"]
 
 _LIB = None
 
@@ -273,6 +275,12 @@ class Context:
 
     def kernel_launches(self):
         return int(self.lib.gsvcu_kernel_launches(self.h))
+
+    def set_fused_decode(self, on):
+        self._check(self.lib.gsvcu_set_fused_decode(self.h, 1 if on else 0))
+
+    def fused_decode(self):
+        return bool(self.lib.gsvcu_fused_decode(self.h))
 
     def stream_handle(self):
         return int(self.lib.gsvcu_stream(self.h) or 0)

@@ -236,12 +236,23 @@ int gsvcu_op_sample(gsvcu_ctx* ctx, const float* logits_dev, int32_t B, int32_t 
 /* Kernel classes of one decode step, indices of ms_by_class. */
 enum {
     GSVCU_PROF_SAMPLER = 0, GSVCU_PROF_STEP_PREP, GSVCU_PROF_QKV_GEMM, GSVCU_PROF_DECODE_ATTN, GSVCU_PROF_OUT_GEMM,
-    GSVCU_PROF_LAYERNORM, GSVCU_PROF_FFN1_GEMM, GSVCU_PROF_FFN2_GEMM, GSVCU_PROF_PREDICT, GSVCU_PROF_CLASSES
+    GSVCU_PROF_LAYERNORM, GSVCU_PROF_FFN1_GEMM, GSVCU_PROF_FFN2_GEMM, GSVCU_PROF_PREDICT,
+    GSVCU_PROF_DENSE,   /* fused layer tail: page merge, out, LN1, FFN1, FFN2, LN2, next QKV */
+    GSVCU_PROF_CLASSES
 };
 /* Run n_steps decode steps of the slots in flight without the graph, timing every kernel class with
- * CUDA events on the context's stream; ms_by_class [GSVCU_PROF_CLASSES] gets the summed milliseconds,
+ * CUDA events on the context's stream; ms_by_class [GSVCU_PROF_CLASSES] gets the summed milliseconds
+ * (with the fused decode step: sampler, step prep, layer 0's QKV, decode attention, fused layer tail
+ * and predict; otherwise one class per unfused kernel),
  * attn_bytes (may be NULL) the algorithmic K/V + q/out bytes the attention launches read and wrote. */
 int gsvcu_step_profile(gsvcu_ctx* ctx, int32_t n_steps, float* ms_by_class, int64_t* attn_bytes);
+/* Decode-step variant (no counterpart in the reference; an implementation switch of this library).
+ * on = 1 (default): each layer after attention runs as one 16-CTA cluster kernel (page merge,
+ * out-projection, LayerNorm, FFN, LayerNorm, next layer's QKV), when the device can hold such a
+ * cluster; on = 0: one kernel per operation. Results are identical. Returns GSVCU_OK;
+ * gsvcu_fused_decode tells whether the fused variant is in use. */
+int gsvcu_set_fused_decode(gsvcu_ctx* ctx, int32_t on);
+int gsvcu_fused_decode(const gsvcu_ctx* ctx);
 /* Number of kernels this context has launched (graph replays count their kernels). */
 int64_t gsvcu_kernel_launches(const gsvcu_ctx* ctx);
 /* The context's CUDA stream (cudaStream_t), for callers that order their own work after it or time

@@ -110,6 +110,27 @@ def test_decode_logits_trace(gctx, orc, kv):
         assert cos32 >= 0.999 and rl32 <= 0.05
 
 
+def test_fused_and_unfused_decode_steps_agree(gctx, orc):
+    """The cluster-fused layer tail and the one-kernel-per-op decode step give the same logits, bit
+    for bit, and both equal the oracle (F16 and F32 KV)."""
+    assert gctx.fused_decode(), "the 16-CTA cluster layer tail should be resident on B200"
+    rng = np.random.default_rng(21)
+    reqs = S.ragged_requests(21, 9, lo=30, hi=200)   # 9 slots: two 8-slot clusters, one partly empty
+    forced = rng.integers(0, 1024, (9, 70)).astype(np.int32)   # crosses page boundaries
+    for kv in (0, 1):
+        _reserve(gctx, kv)
+        got = gctx.debug_trace(reqs, forced)
+        gctx.set_fused_decode(False)
+        try:
+            _reserve(gctx, kv)
+            unf = gctx.debug_trace(reqs, forced)
+        finally:
+            gctx.set_fused_decode(True)
+        assert np.array_equal(got.view(np.uint32), unf.view(np.uint32)), kv
+        ref = orc.decode_trace(reqs, forced, kv_f16=(kv == 0))
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), kv
+
+
 def _first_divergence(a, b):
     n = min(len(a), len(b))
     for i in range(n):
