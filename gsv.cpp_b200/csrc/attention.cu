@@ -132,17 +132,33 @@ __global__ void __launch_bounds__(128) k_decode_attn(const DecAttnParams p) {
     using S = DecShape<KT>;
     extern __shared__ __align__(128) uint8_t sm[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int slot = blockIdx.z, chunk = blockIdx.y, h = blockIdx.x * 4 + warp;
-    // In the decode step (p.st set) the slot state and every KV row but this step's are at least two
-    // kernels old, so they are read before griddep_wait; op-entry inputs may come from the previous
-    // kernel and are read after it.
+    // In the decode step (p.st set) the slot state, the page list and every KV row but this step's are
+    // at least two kernels old, so they are read before griddep_wait; op-entry inputs may come from the
+    // previous kernel and are read after it.
     const bool early = p.st != nullptr;
     if (!early) {
         griddep_wait();
         griddep_launch();
     }
-    int kvpos;
-    const bool act = decode_slot(p, slot, kvpos);
+    int slot, chunk, h, kvpos;
+    bool act;
+    if (p.work) {   // compacted list: CTA = (item, head group), trailing CTAs past the list exit
+        const int item = p.work_base[p.group] + (int)(blockIdx.x >> 2);
+        h = (int)(blockIdx.x & 3) * 4 + warp;
+        act = item < p.work_base[p.group + 1];
+        slot = 0; chunk = 0; kvpos = 0;
+        if (act) {
+            const int2 w = p.work[item];
+            slot = w.x;
+            chunk = w.y & 0xff;
+            kvpos = w.y >> 8;
+        }
+    } else {
+        slot = p.slot0 + blockIdx.z;
+        chunk = blockIdx.y;
+        h = blockIdx.x * 4 + warp;
+        act = decode_slot(p, slot, kvpos);
+    }
     const int nkeys = kvpos + 1, k0 = chunk * PAGE;
     if (!act || k0 >= nkeys) {
         if (early) griddep_wait();
@@ -255,7 +271,7 @@ __global__ void __launch_bounds__(128) k_decode_merge(const DecAttnParams p) {
     griddep_wait();
     griddep_launch();
     if (item >= p.B * NH) return;
-    const int slot = item / NH, h = item % NH;
+    const int slot = p.slot0 + item / NH, h = item % NH;
     int kvpos;
     if (!decode_slot(p, slot, kvpos)) return;
     const int nch = (kvpos + PAGE) / PAGE;
@@ -304,8 +320,65 @@ cudaError_t attention_init_device() {
                                 (int)DecShape<float>::SMEM);
 }
 
+// One CTA of 1024 threads: slot-major exclusive prefix of the slots' page counts, then the items.
+__global__ void __launch_bounds__(1024) k_page_list(const SlotState* st, int M, int split, int2* work, int32_t* base) {
+    griddep_wait();
+    griddep_launch();
+    __shared__ int wsum[32];
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const int C = (M + 1023) / 1024;   // slots per thread (<= 4)
+    int np[4], kp[4], cnt = 0;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int slot = t * C + i;
+        np[i] = 0;
+        kp[i] = 0;
+        if (i < C && slot < M && st[slot].decode_now) {
+            kp[i] = st[slot].kvpos;
+            np[i] = kp[i] / PAGE + 1;
+        }
+        cnt += np[i];
+    }
+    int x = cnt;   // inclusive scan over the block
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, off);
+        if (lane >= off) x += y;
+    }
+    if (lane == 31) wsum[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        int w = wsum[lane];
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, w, off);
+            if (lane >= off) w += y;
+        }
+        wsum[lane] = w;
+    }
+    __syncthreads();
+    int off = x - cnt + (warp ? wsum[warp - 1] : 0);   // exclusive prefix of this thread's first slot
+    if (t == 0) base[0] = 0;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int slot = t * C + i;
+        if (i < C && slot == split) base[1] = off;
+        for (int pg = 0; pg < np[i]; pg++) work[off + pg] = make_int2(slot, pg | (kp[i] << 8));
+        off += np[i];
+    }
+    if (t == 1023) {
+        base[2] = off;
+        if (split >= M) base[1] = off;
+    }
+}
+
+void launch_page_list(const SlotState* st, int M, int split, int2* work, int32_t* base, cudaStream_t s) {
+    launch_pdl(k_page_list, dim3(1), dim3(1024), 0, s, st, M, split, work, base);
+}
+
 int launch_decode_attention(const DecAttnParams& p, cudaStream_t s) {
     dim3 grid(NH / 4, p.max_chunks, p.B);
+    if (p.work) grid = dim3(4 * p.B * p.max_chunks);
     if (p.kv_f32) launch_pdl(k_decode_attn<float>, grid, dim3(128), DecShape<float>::SMEM, s, p);
     else launch_pdl(k_decode_attn<__half>, grid, dim3(128), DecShape<__half>::SMEM, s, p);
     if (p.max_chunks <= 1 || p.partials_only) return 1;

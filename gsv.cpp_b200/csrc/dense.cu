@@ -67,13 +67,14 @@ constexpr int P_BOUT = 0, P_BF1 = 32, P_BF2 = 160, P_N1W = 192, P_N1B = 224, P_N
               P_COUNT = 416;
 constexpr int SM_ROWMETA = SM_PAR + P_COUNT * 4;   // per row: pages to merge (0: not decoding), KV page, KV pos
 constexpr int SM_BARS = SM_ROWMETA + DR * 3 * 4;   // 4 weight barriers + 6 exchange barriers
-constexpr int SMEM_DENSE = SM_BARS + 10 * 8;
+constexpr int SMEM_DENSE = SM_BARS + 11 * 8;
 // aliases: phase-0 page-merge scratch in the h rows; FFN1's f32 outputs in the attention rows
 constexpr int MERGE_ROW_BYTES = (16 + 16 + 16 * 32) * 4;   // one row: 16 pages' w, l, o
 static_assert(NW == DR && NW * MERGE_ROW_BYTES <= HROWS_BYTES, "merge scratch");
 static_assert(DR * 128 * 4 <= ROWS1_BYTES, "ffn1 staging");
 static_assert(SM_D_QKV + 96 * KB1 * 2 <= SM_W_F2, "qkv weights reuse out + ffn1");
 static_assert(SMEM_DENSE <= 232448, "shared memory");
+static_assert(SM_PAR % 16 == 0 && SM_XOWN % 16 == 0 && SM_ROWMETA % 4 == 0, "alignment of TMA destinations");
 static_assert(SM_AROWS % 16 == 0 && SM_N1ROWS % 16 == 0 && SM_HROWS % 16 == 0 && SM_D_F1 % 16 == 0 &&
                   SM_D_F2 % 16 == 0 && SM_D_QKV % 16 == 0 && SM_LNP1 % 16 == 0 && SM_LNP2 % 16 == 0 &&
                   SM_STG % 16 == 0 && STG_WARP % 16 == 0 && SM_BARS % 8 == 0 && (DR * RS1) % 16 == 0 &&
@@ -82,7 +83,7 @@ static_assert(SM_AROWS % 16 == 0 && SM_N1ROWS % 16 == 0 && SM_HROWS % 16 == 0 &&
 // bytes each CTA receives per exchange (every CTA sends to all 16, itself included)
 constexpr uint32_t EX_BLOCK = DC * DR * (32 + 4);  // one Q8_0 block (32 B + f32 scale) per (sender, row)
 constexpr uint32_t EX_STATS = DC * DR * 16;        // one {sum, sum of squares} per (sender, row)
-enum { BW_OUT = 0, BW_F1, BW_F2, BW_QKV, BX_ATT, BX_LN1, BX_N1, BX_H, BX_LN2, BX_X };
+enum { BW_OUT = 0, BW_F1, BW_F2, BW_QKV, BX_ATT, BX_LN1, BX_N1, BX_H, BX_LN2, BX_X, BW_PAR };
 
 __device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -171,6 +172,49 @@ __device__ __forceinline__ void rg_gemm(const uint8_t* W, const uint16_t* DW, in
     }
 }
 
+// FFN2-shaped row group (KB2 = 64 blocks) split over 4 warps by K quarter q: each warp issues its 16
+// MMAs at once, then the warps continue one float chain in block order, handing the running sums
+// over through shared memory `hand` ([4 lanes x ... ]) with named barriers bar_base + q.
+__device__ __forceinline__ void rg_gemm_ksplit4(const uint8_t* W, const uint16_t* DW, int lr, const int8_t* X, int rs,
+                                                const float* DX, int rt, int q, float* hand, int bar_base,
+                                                float (&acc)[4]) {
+    constexpr int KB = KB2, KQ = KB2 / 4;
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int fa = lr * 16 + g, fb = fa + 8, ra = rt * 8 + 2 * t, rb = ra + 1;
+    const uint4* wp = (const uint4*)W + (size_t)lr * KB * 32 + lane;
+    const int8_t* xr = X + (rt * 8 + g) * rs + t * 4;
+    int c[KQ][4];
+#pragma unroll
+    for (int j = 0; j < KQ; j++) {
+        const int kb = q * KQ + j;
+        const uint4 a = wp[kb * 32];
+        const uint32_t b0 = *(const uint32_t*)(xr + kb * 32), b1 = *(const uint32_t*)(xr + kb * 32 + 16);
+        mma_s8(c[j], a, b0, b1);
+    }
+    if (q > 0) {   // the previous quarter's warp has stored the running sums
+        asm volatile("bar.sync %0, 64;" ::"r"(bar_base + q) : "memory");
+        const float4 v = *(const float4*)(hand + lane * 4);
+        acc[0] = v.x; acc[1] = v.y; acc[2] = v.z; acc[3] = v.w;
+    } else {
+        acc[0] = acc[1] = acc[2] = acc[3] = 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < KQ; j++) {
+        const int kb = q * KQ + j;
+        const float dwa = h2f(DW[fa * KB + kb]), dwb = h2f(DW[fb * KB + kb]);
+        const float dxa = DX[ra * KB + kb], dxb = DX[rb * KB + kb];
+        acc[0] = fmaf((float)c[j][0], __fmul_rn(dwa, dxa), acc[0]);
+        acc[1] = fmaf((float)c[j][1], __fmul_rn(dwa, dxb), acc[1]);
+        acc[2] = fmaf((float)c[j][2], __fmul_rn(dwb, dxa), acc[2]);
+        acc[3] = fmaf((float)c[j][3], __fmul_rn(dwb, dxb), acc[3]);
+    }
+    if (q < 3) {
+        if (q > 0) __syncwarp();   // this warp's read of `hand` is done before it is overwritten
+        *(float4*)(hand + lane * 4) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        asm volatile("bar.arrive %0, 64;" ::"r"(bar_base + q + 1) : "memory");
+    }
+}
+
 // Quantize the 32 values v (lane l holds column l of the block) into q (32 B of shared memory); returns
 // the block's scale, rounded through fp16 (what a reader of the fp16 scale sees), in every lane.
 __device__ __forceinline__ float q8_block_stage(float v, int8_t* q) {
@@ -252,7 +296,8 @@ __global__ void __launch_bounds__(DT, 1) k_dense_layer(const DenseParams p) {
     extern __shared__ __align__(128) uint8_t sm[];
     cg::cluster_group cl = cg::this_cluster();
     const int rank = (int)cl.block_rank();
-    const int r0 = (blockIdx.x / DC) * DR;
+    const int r0 = p.slot0 + (blockIdx.x / DC) * DR;   // first slot of this cluster
+    const int rend = p.slot0 + p.M;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int sub = lane & 3;
     const uint32_t bars = su32(sm + SM_BARS);
@@ -260,7 +305,7 @@ __global__ void __launch_bounds__(DT, 1) k_dense_layer(const DenseParams p) {
     bool ok = true;
 
     if (tid == 0) {
-        for (int i = 0; i < 10; i++) d_mbar_init(bar(i));
+        for (int i = 0; i < 11; i++) d_mbar_init(bar(i));
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         // exchanges: the bytes the 16 CTAs will send here
         d_expect_tx(bar(BX_ATT), EX_BLOCK);
@@ -270,51 +315,58 @@ __global__ void __launch_bounds__(DT, 1) k_dense_layer(const DenseParams p) {
         d_expect_tx(bar(BX_LN2), EX_STATS);
         if (HAS_QKV) d_expect_tx(bar(BX_X), EX_BLOCK);
     }
+    __syncthreads();   // the barriers are initialised for every warp of the CTA
     // announce this CTA's armed barriers now; wait for the peers' only before the first send
     asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-    if (tid == 0) {   // weights of this CTA's slices (constant), before the wait for the attention kernel
-        d_expect_tx(bar(BW_OUT), 2 * KB1 * 512 + 32 * KB1 * 2);
-        d_bulk(su32(sm + SM_W_OUT), p.w_out + (size_t)(2 * rank) * KB1 * 32, 2 * KB1 * 512, bar(BW_OUT));
-        d_bulk(su32(sm + SM_D_OUT), p.d_out + (size_t)(32 * rank) * KB1, 32 * KB1 * 2, bar(BW_OUT));
-        d_expect_tx(bar(BW_F1), 8 * KB1 * 512 + 128 * KB1 * 2);
-        d_bulk(su32(sm + SM_W_F1), p.w_f1 + (size_t)(8 * rank) * KB1 * 32, 8 * KB1 * 512, bar(BW_F1));
-        d_bulk(su32(sm + SM_D_F1), p.d_f1 + (size_t)(128 * rank) * KB1, 128 * KB1 * 2, bar(BW_F1));
-        d_expect_tx(bar(BW_F2), 2 * KB2 * 512 + 32 * KB2 * 2);
-        d_bulk(su32(sm + SM_W_F2), p.w_f2 + (size_t)(2 * rank) * KB2 * 32, 2 * KB2 * 512, bar(BW_F2));
-        d_bulk(su32(sm + SM_D_F2), p.d_f2 + (size_t)(32 * rank) * KB2, 32 * KB2 * 2, bar(BW_F2));
+    if (warp == 0) {   // weights of this CTA's slices (constant), before the wait for the attention kernel
+        if (lane == 0) {
+            d_expect_tx(bar(BW_OUT), 2 * KB1 * 512 + 32 * KB1 * 2);
+            d_expect_tx(bar(BW_F1), 8 * KB1 * 512 + 128 * KB1 * 2);
+            d_expect_tx(bar(BW_F2), 2 * KB2 * 512 + 32 * KB2 * 2);
+        }
+        __syncwarp();
+        if (lane == 0) d_bulk(su32(sm + SM_W_OUT), p.w_out + (size_t)(2 * rank) * KB1 * 32, 2 * KB1 * 512, bar(BW_OUT));
+        if (lane == 1) d_bulk(su32(sm + SM_D_OUT), p.d_out + (size_t)(32 * rank) * KB1, 32 * KB1 * 2, bar(BW_OUT));
+        if (lane == 2) d_bulk(su32(sm + SM_W_F1), p.w_f1 + (size_t)(8 * rank) * KB1 * 32, 8 * KB1 * 512, bar(BW_F1));
+        if (lane == 3) d_bulk(su32(sm + SM_D_F1), p.d_f1 + (size_t)(128 * rank) * KB1, 128 * KB1 * 2, bar(BW_F1));
+        if (lane == 4) d_bulk(su32(sm + SM_W_F2), p.w_f2 + (size_t)(2 * rank) * KB2 * 32, 2 * KB2 * 512, bar(BW_F2));
+        if (lane == 5) d_bulk(su32(sm + SM_D_F2), p.d_f2 + (size_t)(32 * rank) * KB2, 32 * KB2 * 2, bar(BW_F2));
     }
-    // slot state, block table, x and this CTA's parameters were written two or more kernels ago (or by
-    // the host): read them while the attention kernel finishes
+    // slot state, x and this CTA's parameters were written two or more kernels ago (or by the host):
+    // parameters and x columns are copied in by TMA, the slot state read, while the attention finishes
     float* par = (float*)(sm + SM_PAR);
     int* meta = (int*)(sm + SM_ROWMETA);
     float* xown = (float*)(sm + SM_XOWN);
-    for (int i = tid; i < P_COUNT; i += DT) {
-        float v;
-        if (i < P_BF1) v = p.b_out[32 * rank + i - P_BOUT];
-        else if (i < P_BF2) v = p.b_f1[128 * rank + i - P_BF1];
-        else if (i < P_N1W) v = p.b_f2[32 * rank + i - P_BF2];
-        else if (i < P_N1B) v = p.n1w[32 * rank + i - P_N1W];
-        else if (i < P_N2W) v = p.n1b[32 * rank + i - P_N1B];
-        else if (i < P_N2B) v = p.n2w[32 * rank + i - P_N2W];
-        else if (i < P_BQKV) v = p.n2b[32 * rank + i - P_N2B];
-        else v = HAS_QKV ? p.b_qkv[((i - P_BQKV) >> 5) * D + 32 * rank + ((i - P_BQKV) & 31)] : 0.0f;
-        par[i] = v;
+    if (warp == 1) {   // one copy per lane (the barrier's bytes are armed by lane 0 first)
+        const int nrows = max(0, min(DR, rend - r0));
+        const uint32_t bp = bar(BW_PAR);
+        if (lane == 0) d_expect_tx(bp, (HAS_QKV ? P_COUNT : P_BQKV) * 4 + nrows * 128);
+        __syncwarp();
+        if (lane < 6) {
+            const float* src = lane == 0 ? p.b_out : lane == 1 ? p.b_f2 : lane == 2 ? p.n1w
+                             : lane == 3 ? p.n1b : lane == 4 ? p.n2w : p.n2b;
+            const int dst = lane == 0 ? P_BOUT : lane == 1 ? P_BF2 : lane == 2 ? P_N1W
+                          : lane == 3 ? P_N1B : lane == 4 ? P_N2W : P_N2B;
+            d_bulk(su32(par + dst), src + 32 * rank, 128, bp);
+        } else if (lane == 6) {
+            d_bulk(su32(par + P_BF1), p.b_f1 + 128 * rank, 512, bp);
+        } else if (lane < 10) {
+            const int part = lane - 7;
+            if (HAS_QKV) d_bulk(su32(par + P_BQKV + part * 32), p.b_qkv + part * D + 32 * rank, 128, bp);
+        } else if (lane - 10 < nrows) {
+            const int r = lane - 10;
+            d_bulk(su32(xown + r * 32), p.x + (size_t)(r0 + r) * D + 32 * rank, 128, bp);
+        }
     }
     if (tid < DR) {
         const int slot = r0 + tid;
-        int nch = 0, page = 0, pos = 0;
-        if (slot < p.M && p.st[slot].decode_now) {
+        int nch = 0, pos = 0;
+        if (slot < rend && p.st[slot].decode_now) {
             pos = p.st[slot].kvpos;
             nch = pos / PAGE + 1;
-            if (HAS_QKV) page = p.kv.block_table[(size_t)slot * p.kv.max_pages + pos / PAGE];
         }
         meta[tid * 3] = nch;
-        meta[tid * 3 + 1] = page;
         meta[tid * 3 + 2] = pos;
-    }
-    for (int i = tid; i < DR * 32; i += DT) {
-        const int slot = r0 + (i >> 5);
-        xown[i] = slot < p.M ? p.x[(size_t)slot * D + 32 * rank + (i & 31)] : 0.0f;
     }
     griddep_wait();
     griddep_launch();
@@ -385,10 +437,16 @@ __global__ void __launch_bounds__(DT, 1) k_dense_layer(const DenseParams p) {
             ((int8_t*)(stg + STG_ATT))[lane] = 0;
         }
     }
+    ok &= d_wait(bar(BW_PAR));   // parameters and x columns
     asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");   // every peer's barriers are armed
     send_block((const int8_t*)(stg + STG_ATT), att_d, r, su32(sm + SM_AROWS), RS1, KB1, rank, bar(BX_ATT));
 
-    // ---- phase 1: out-projection + residual + bias (columns 32*rank + 0..31)
+    // ---- phase 1: out-projection + residual + bias (columns 32*rank + 0..31); an idle warp looks up
+    // the KV page of this step's key for phase 6
+    if (HAS_QKV && warp == NW - 1 && lane < DR) {
+        const int rr = lane;
+        meta[rr * 3 + 1] = meta[rr * 3] ? p.kv.block_table[(size_t)(r0 + rr) * p.kv.max_pages + meta[rr * 3 + 2] / PAGE] : 0;
+    }
     if (warp < 4) {
         ok &= d_wait(bar(BX_ATT));
         ok &= d_wait(bar(BW_OUT));
@@ -454,19 +512,23 @@ __global__ void __launch_bounds__(DT, 1) k_dense_layer(const DenseParams p) {
         send_blocks4((const int8_t*)(stg + STG_H), hd, r, su32(sm + SM_HROWS), RS2, KB2, 4 * rank, bar(BX_H));
     }
 
-    // ---- phase 4: FFN2 + residual n1 + bias (columns 32*rank + 0..31)
-    if (warp < 4) {
+    // ---- phase 4: FFN2 + residual n1 + bias (columns 32*rank + 0..31): task = (row group, row tile) on
+    // warps 4 task .. 4 task + 3, one K quarter each, chained in block order
+    {
         ok &= d_wait(bar(BX_H));
         ok &= d_wait(bar(BW_F2));
+        const int task = warp >> 2, q = warp & 3, lr = task & 1, rt = task >> 1;
+        float* hand = (float*)(sm + SM_LNP1) + task * 128;   // LN1 sums are consumed by now
         float acc[4];
-        const int lr = warp & 1, rt = warp >> 1;
-        rg_gemm<KB2>(sm + SM_W_F2, (const uint16_t*)(sm + SM_D_F2), lr, (const int8_t*)(sm + SM_HROWS), RS2,
-                     (const float*)(sm + SM_HROWS + DR * RS2), rt, acc);
-        const int g = lane >> 2, t = lane & 3;
+        rg_gemm_ksplit4(sm + SM_W_F2, (const uint16_t*)(sm + SM_D_F2), lr, (const int8_t*)(sm + SM_HROWS), RS2,
+                        (const float*)(sm + SM_HROWS + DR * RS2), rt, q, hand, 1 + task * 3, acc);
+        if (q == 3) {
+            const int g = lane >> 2, t = lane & 3;
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int f = lr * 16 + g + (i >= 2 ? 8 : 0), rr = rt * 8 + 2 * t + (i & 1);
-            pre[rr * 32 + f] = __fadd_rn(__fadd_rn(n1own[rr * 32 + f], acc[i]), par[P_BF2 + f]);
+            for (int i = 0; i < 4; i++) {
+                const int f = lr * 16 + g + (i >= 2 ? 8 : 0), rr = rt * 8 + 2 * t + (i & 1);
+                pre[rr * 32 + f] = __fadd_rn(__fadd_rn(n1own[rr * 32 + f], acc[i]), par[P_BF2 + f]);
+            }
         }
     }
     __syncthreads();
@@ -477,7 +539,7 @@ __global__ void __launch_bounds__(DT, 1) k_dense_layer(const DenseParams p) {
     {
         const float xv = ln_apply((const double*)(sm + SM_LNP2), r, pre[r * 32 + lane], par[P_N2W + lane],
                                   par[P_N2B + lane]);
-        if (r0 + r < p.M) p.x[(size_t)(r0 + r) * D + 32 * rank + lane] = xv;
+        if (r0 + r < rend) p.x[(size_t)(r0 + r) * D + 32 * rank + lane] = xv;
         if (HAS_QKV) {
             const float d = q8_block_stage(xv, (int8_t*)(stg + STG_X));
             send_block((const int8_t*)(stg + STG_X), d, r, su32(sm + SM_XROWS), RS1, KB1, rank, bar(BX_X));
@@ -495,7 +557,7 @@ __global__ void __launch_bounds__(DT, 1) k_dense_layer(const DenseParams p) {
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             const int f = (lr & 1) * 16 + g + (i >= 2 ? 8 : 0), rr = rt * 8 + 2 * t + (i & 1), slot = r0 + rr;
-            if (slot >= p.M) continue;
+            if (slot >= rend) continue;
             const float y = __fadd_rn(acc[i], par[P_BQKV + part * 32 + f]);
             if (part == 0) {
                 p.q[(size_t)slot * p.q_stride + 32 * rank + f] = y;
@@ -512,16 +574,21 @@ __global__ void __launch_bounds__(DT, 1) k_dense_layer(const DenseParams p) {
     if (!__all_sync(0xffffffffu, ok)) {
         // a copy or an exchange never completed: flag it and wait (bounded) for what may still arrive
         if (lane == 0 && p.err) atomicExch(p.err, 1);
-        for (int i = 0; i < 10; i++)
+        for (int i = 0; i < 11; i++)
             if (HAS_QKV || (i != BW_QKV && i != BX_X)) (void)d_wait(bar(i));
     }
     // no CTA leaves while a peer may still be sending to it
     asm volatile("barrier.cluster.arrive.relaxed.aligned;\nbarrier.cluster.wait.aligned;" ::: "memory");
 }
 
+static int g_dense_priority = 0;   // the device's highest stream priority
+
 cudaError_t dense_init_device(bool* usable) {
     *usable = false;
     cudaError_t e;
+    int least = 0, greatest = 0;
+    if ((e = cudaDeviceGetStreamPriorityRange(&least, &greatest))) return e;
+    g_dense_priority = greatest;
     void (*ks[2])(const DenseParams) = {k_dense_layer<true>, k_dense_layer<false>};
     for (auto k : ks) {
         if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_DENSE))) return e;
@@ -554,15 +621,18 @@ void launch_dense_layer(const DenseParams& p, cudaStream_t s) {
     cfg.blockDim = dim3(DT);
     cfg.dynamicSmemBytes = SMEM_DENSE;
     cfg.stream = s;
-    cudaLaunchAttribute at[2];
+    cudaLaunchAttribute at[3];
     at[0].id = cudaLaunchAttributeClusterDimension;
     at[0].val.clusterDim.x = DC;
     at[0].val.clusterDim.y = 1;
     at[0].val.clusterDim.z = 1;
     at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     at[1].val.programmaticStreamSerializationAllowed = 1;
+    // latency-bound clusters go first when attention CTAs of the other slot group free SMs
+    at[2].id = cudaLaunchAttributePriority;
+    at[2].val.priority = g_dense_priority;
     cfg.attrs = at;
-    cfg.numAttrs = 2;
+    cfg.numAttrs = 3;
     if (p.w_qkv) cudaLaunchKernelEx(&cfg, k_dense_layer<true>, p);
     else cudaLaunchKernelEx(&cfg, k_dense_layer<false>, p);
 }

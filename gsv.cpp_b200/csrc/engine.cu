@@ -211,6 +211,8 @@ struct gsvcu_ctx {
     uint16_t *xd = nullptr, *ad = nullptr, *n1d = nullptr, *hd = nullptr;
     float* part = nullptr;
     int max_chunks = 0;
+    int2* work = nullptr;          // the decode step's (slot, page) list and its group offsets
+    int32_t* work_base = nullptr;
     // prefill staging
     int32_t *p_ids = nullptr, *p_pepos = nullptr, *p_istext = nullptr, *p_tslot = nullptr, *p_tpos = nullptr,
             *p_rowT = nullptr, *p_sstart = nullptr, *p_slen = nullptr, *p_tlen = nullptr, *p_last = nullptr,
@@ -238,6 +240,10 @@ struct gsvcu_ctx {
     int32_t* att_err = nullptr;
     // decode steps run the fused layer tail (dense.cu) when the device can hold its cluster
     bool dense_ok = false, fused = true;
+    // two slot groups run their layer chains on these streams, so one group's layer tail overlaps the
+    // other group's attention (fork/join events inside the captured step)
+    cudaStream_t gstream[2] = {nullptr, nullptr};
+    cudaEvent_t gevent[3] = {nullptr, nullptr, nullptr};
 
     ~gsvcu_ctx();
     int load(const char* path);
@@ -289,6 +295,10 @@ gsvcu_ctx::~gsvcu_ctx() {
     for (void* p : wallocs) cudaFree(p);
     if (op_part) cudaFree(op_part);
     if (att_err) cudaFree(att_err);
+    for (cudaStream_t gs : gstream)
+        if (gs) cudaStreamDestroy(gs);
+    for (cudaEvent_t ge : gevent)
+        if (ge) cudaEventDestroy(ge);
     for (cudaEvent_t e : prof_ev)
         if (e) cudaEventDestroy(e);
     if (stream) cudaStreamDestroy(stream);
@@ -418,6 +428,7 @@ int gsvcu_ctx::reserve(int slots, int ctx, int kvd) {
         {(void**)&xd, M * D / QK * 2}, {(void**)&ad, M * D / QK * 2}, {(void**)&n1d, M * D / QK * 2},
         {(void**)&hd, M * FF / QK * 2},
         {(void**)&part, (size_t)max_slots * NH * max_chunks * PART_STRIDE * 4},
+        {(void**)&work, (size_t)max_slots * max_chunks * sizeof(int2)}, {(void**)&work_base, 4 * 4},
         {(void**)&p_ids, M * 4}, {(void**)&p_pepos, M * 4}, {(void**)&p_istext, M * 4},
         {(void**)&p_tslot, M * 4}, {(void**)&p_tpos, M * 4}, {(void**)&p_rowT, M * 4}, {(void**)&p_rowoff, M * 8},
         {(void**)&p_sstart, (size_t)max_slots * 4}, {(void**)&p_slen, (size_t)max_slots * 4},
@@ -758,45 +769,69 @@ int gsvcu_ctx::launch_step(cudaStream_t s, float* dump, int dump_row, const int*
     TRY(mark(1));
     const float scale = 1.0f / std::sqrt((float)HD);
     if (fused && dense_ok && !dump) {
-        // fused layers: QKV of layer 0, then per layer the page attention and the cluster layer tail
-        // (merge, out, LN1, FFN1, FFN2, LN2, next layer's QKV); 2 + 1 + 2 NL + 1 kernels
-        {
-            const LayerW& w = L[0];
-            GemmQ8Params g;
-            g.xq = xq; g.xd = xd; g.M = M; g.wq = w.wq[0]; g.wd = w.wd[0]; g.N = 3 * D; g.K = D; g.bias = w.b_qkv;
-            g.y = qkv;
-            g.kv.pool = pool; g.kv.kv_f32 = kv_f32; g.kv.n_layer = NL; g.kv.layer = 0; g.kv.block_table = block_table;
-            g.kv.max_pages = max_pages; g.kv.st = st;
-            launch_gemm_q8(g, EPI_BIAS, s);
-            nk++;
-            TRY(mark(GSVCU_PROF_QKV_GEMM));
-        }
-        for (int li = 0; li < NL; li++) {
-            const LayerW& w = L[li];
-            DecAttnParams a;
-            a.q = qkv; a.q_stride = 3 * D; a.pool = pool; a.kv_f32 = kv_f32; a.n_layer = NL; a.layer = li;
-            a.block_table = block_table; a.max_pages = max_pages; a.st = st; a.B = M; a.max_chunks = max_chunks;
-            a.scale = scale; a.out_q = aq; a.out_d = ad; a.part = part; a.partials_only = 1; a.err = att_err;
-            nk += launch_decode_attention(a, s);
-            TRY(mark(GSVCU_PROF_DECODE_ATTN));
-            DenseParams d;
-            d.M = M; d.st = st; d.part = part; d.max_chunks = max_chunks;
-            d.w_out = w.wq[1]; d.d_out = w.wd[1]; d.b_out = w.b_out; d.n1w = w.n1w; d.n1b = w.n1b;
-            d.w_f1 = w.wq[2]; d.d_f1 = w.wd[2]; d.b_f1 = w.b_f1; d.w_f2 = w.wq[3]; d.d_f2 = w.wd[3]; d.b_f2 = w.b_f2;
-            d.n2w = w.n2w; d.n2b = w.n2b; d.x = x; d.err = att_err;
-            if (li + 1 < NL) {
-                const LayerW& wn = L[li + 1];
-                d.w_qkv = wn.wq[0]; d.d_qkv = wn.wd[0]; d.b_qkv = wn.b_qkv; d.q = qkv; d.q_stride = 3 * D;
-                d.kv.pool = pool; d.kv.kv_f32 = kv_f32; d.kv.n_layer = NL; d.kv.layer = li + 1;
-                d.kv.block_table = block_table; d.kv.max_pages = max_pages; d.kv.st = st;
+        // fused layers for slots [s0, s0 + rows): QKV of layer 0, then per layer the page attention and
+        // the cluster layer tail (merge, out, LN1, FFN1, FFN2, LN2, next layer's QKV), then the logits
+        auto chain = [&](cudaStream_t cs, int s0, int rows) -> int {
+            {
+                const LayerW& w = L[0];
+                GemmQ8Params g;
+                g.xq = xq + (size_t)s0 * D; g.xd = xd + (size_t)s0 * (D / QK); g.M = rows; g.wq = w.wq[0];
+                g.wd = w.wd[0]; g.N = 3 * D; g.K = D; g.bias = w.b_qkv; g.y = qkv + (size_t)s0 * 3 * D;
+                g.kv.pool = pool; g.kv.kv_f32 = kv_f32; g.kv.n_layer = NL; g.kv.layer = 0;
+                g.kv.block_table = block_table + (size_t)s0 * max_pages; g.kv.max_pages = max_pages;
+                g.kv.st = st + s0;
+                launch_gemm_q8(g, EPI_BIAS, cs);
+                nk++;
+                TRY(mark(GSVCU_PROF_QKV_GEMM));
             }
-            launch_dense_layer(d, s);
+            for (int li = 0; li < NL; li++) {
+                const LayerW& w = L[li];
+                DecAttnParams a;
+                a.q = qkv; a.q_stride = 3 * D; a.pool = pool; a.kv_f32 = kv_f32; a.n_layer = NL; a.layer = li;
+                a.block_table = block_table; a.max_pages = max_pages; a.st = st; a.slot0 = s0; a.B = rows;
+                a.max_chunks = max_chunks; a.scale = scale; a.out_q = aq; a.out_d = ad; a.part = part;
+                a.partials_only = 1; a.err = att_err;
+                a.work = work; a.work_base = work_base; a.group = s0 ? 1 : 0;
+                nk += launch_decode_attention(a, cs);
+                TRY(mark(GSVCU_PROF_DECODE_ATTN));
+                DenseParams d;
+                d.slot0 = s0; d.M = rows; d.st = st; d.part = part; d.max_chunks = max_chunks;
+                d.w_out = w.wq[1]; d.d_out = w.wd[1]; d.b_out = w.b_out; d.n1w = w.n1w; d.n1b = w.n1b;
+                d.w_f1 = w.wq[2]; d.d_f1 = w.wd[2]; d.b_f1 = w.b_f1; d.w_f2 = w.wq[3]; d.d_f2 = w.wd[3];
+                d.b_f2 = w.b_f2; d.n2w = w.n2w; d.n2b = w.n2b; d.x = x; d.err = att_err;
+                if (li + 1 < NL) {
+                    const LayerW& wn = L[li + 1];
+                    d.w_qkv = wn.wq[0]; d.d_qkv = wn.wd[0]; d.b_qkv = wn.b_qkv; d.q = qkv; d.q_stride = 3 * D;
+                    d.kv.pool = pool; d.kv.kv_f32 = kv_f32; d.kv.n_layer = NL; d.kv.layer = li + 1;
+                    d.kv.block_table = block_table; d.kv.max_pages = max_pages; d.kv.st = st;
+                }
+                launch_dense_layer(d, cs);
+                nk++;
+                TRY(mark(GSVCU_PROF_DENSE));
+            }
+            launch_gemm_f32d(x + (size_t)s0 * D, D, nullptr, rows, predict, V, D, nullptr, 0,
+                             logits + (size_t)s0 * V, V, cs);
             nk++;
-            TRY(mark(GSVCU_PROF_DENSE));
-        }
-        launch_gemm_f32d(x, D, nullptr, M, predict, V, D, nullptr, 0, logits, V, s);
+            TRY(mark(GSVCU_PROF_PREDICT));
+            return GSVCU_OK;
+        };
+        const bool two = !prof_ms && M >= 32 && M % 32 == 0;
+        launch_page_list(st, M, two ? M / 2 : M, work, work_base, s);
         nk++;
-        TRY(mark(GSVCU_PROF_PREDICT));
+        if (!two) {
+            TRY(chain(s, 0, M));
+        } else {
+            // two slot groups on their own streams; the step's tail joins them back into s
+            const int half = M / 2;
+            CK(cudaEventRecord(gevent[2], s));
+            for (int gi = 0; gi < 2; gi++) {
+                CK(cudaStreamWaitEvent(gstream[gi], gevent[2], 0));
+                TRY(chain(gstream[gi], gi * half, half));
+                CK(cudaEventRecord(gevent[gi], gstream[gi]));
+            }
+            CK(cudaStreamWaitEvent(s, gevent[0], 0));
+            CK(cudaStreamWaitEvent(s, gevent[1], 0));
+        }
         graph_kernels = nk;
         return GSVCU_OK;
     }
@@ -949,7 +984,12 @@ int gsvcu_create(int device, gsvcu_ctx** out) {
     c->dense_ok = dense_usable;
     if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
         cudaMalloc((void**)&c->att_err, sizeof(int32_t)) != cudaSuccess ||
-        cudaMemset(c->att_err, 0, sizeof(int32_t)) != cudaSuccess) {
+        cudaMemset(c->att_err, 0, sizeof(int32_t)) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&c->gstream[0], cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&c->gstream[1], cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&c->gevent[0], cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&c->gevent[1], cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&c->gevent[2], cudaEventDisableTiming) != cudaSuccess) {
         cudaGetLastError();
         delete c;
         return GSVCU_ERR_CUDA;

@@ -200,6 +200,166 @@ __global__ void __launch_bounds__(32 * KS) k_gemm_q8(const GemmQ8Params p) {
     }
 }
 
+// ------------------------------------------------------------------ large-M tiles (prefill)
+// CTA tile: 64 output features x 64 tokens, 8 warps; warp w owns row group w&3 (16 features) and
+// tokens 32*(w>>2) .. +31 (four n = 8 tiles). K advances in chunks of 8 blocks, double-buffered with
+// cp.async; every Q8_0 block is one mma.m16n8k32 with a zero accumulator and each output's float chain
+// acc = fma((float)isum_b, d_w*d_x, acc) runs in registers in block order (the same chain as above).
+// The epilogue goes through shared memory, one token row per warp-iteration, for coalesced stores.
+namespace {
+constexpr int TF = 64, TT = 64, TKC = 8;        // features, tokens, K blocks per chunk
+constexpr int TB_STRIDE = TKC * 32 + 16;        // padded int8 row stride of a token's chunk
+constexpr int TS_A = 4 * TKC * 512;             // weight fragments of one chunk
+constexpr int TS_B = TT * TB_STRIDE;            // activation rows of one chunk
+constexpr int TS_DW = TF * TKC * 2, TS_DX = TT * TKC * 2;
+constexpr int TSTAGE = TS_A + TS_B + TS_DW + TS_DX;
+constexpr int TSMEM = 2 * TSTAGE;
+static_assert(TT * (TF + 1) * 4 <= TSMEM, "epilogue staging fits in the chunk buffers");
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+                 "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+}  // namespace
+
+template <int EPI>
+__global__ void __launch_bounds__(256) k_gemm_q8_tile(const GemmQ8Params p) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int K = p.K, KB = K / QK;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int f0 = blockIdx.x * TF, t0 = blockIdx.y * TT;
+    const int rg = warp & 3, th = warp >> 2;
+
+    // chunk c -> stage st
+    auto load_chunk = [&](int c, int st) {
+        uint8_t* base = smem + (size_t)st * TSTAGE;
+        const int k0 = c * TKC;
+        for (int i = tid; i < 4 * TKC * 32; i += 256) {   // 4 row groups x TKC blocks x 32 lanes of 16 B
+            const int r = i / (TKC * 32), rest = i - r * (TKC * 32);
+            cp_async16(base + (size_t)i * 16, p.wq + ((size_t)(f0 / 16 + r) * KB + k0) * 32 + rest, 16);
+        }
+        for (int i = tid; i < TT * TKC * 2; i += 256) {   // TT rows x (TKC*32 B = TKC*2 x 16 B)
+            const int n = i / (TKC * 2), j = i - n * (TKC * 2);
+            const bool ok = t0 + n < p.M;
+            const int8_t* src = p.xq + (size_t)(ok ? t0 + n : 0) * K + k0 * 32 + j * 16;
+            cp_async16(base + TS_A + n * TB_STRIDE + j * 16, src, ok ? 16 : 0);
+        }
+        if (tid < TF) cp_async16(base + TS_A + TS_B + tid * 16, p.wd + (size_t)(f0 + tid) * KB + k0, 16);
+        else if (tid < TF + TT) {
+            const int n = tid - TF;
+            const bool ok = t0 + n < p.M;
+            cp_async16(base + TS_A + TS_B + TS_DW + n * 16, p.xd + (size_t)(ok ? t0 + n : 0) * KB + k0, ok ? 16 : 0);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+
+    griddep_wait();
+    griddep_launch();
+    float acc[4][4];
+#pragma unroll
+    for (int nt = 0; nt < 4; nt++) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
+    const int nchunks = KB / TKC;
+    load_chunk(0, 0);
+    for (int c = 0; c < nchunks; c++) {
+        if (c + 1 < nchunks) {
+            load_chunk(c + 1, (c + 1) & 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncthreads();
+        const uint8_t* base = smem + (size_t)(c & 1) * TSTAGE;
+        const uint4* A = (const uint4*)base + (size_t)rg * TKC * 32 + lane;
+        const int8_t* B = (const int8_t*)(base + TS_A) + (th * 32 + g) * TB_STRIDE + t * 4;
+        const uint16_t* DW = (const uint16_t*)(base + TS_A + TS_B);
+        const uint16_t* DX = (const uint16_t*)(base + TS_A + TS_B + TS_DW);
+        const int fa = rg * 16 + g, fb = fa + 8;
+#pragma unroll 2
+        for (int kb = 0; kb < TKC; kb++) {
+            const uint4 a = A[kb * 32];
+            int cc[4][4];
+#pragma unroll
+            for (int nt = 0; nt < 4; nt++) {
+                const int8_t* br = B + nt * 8 * TB_STRIDE + kb * 32;
+                mma_s8(cc[nt], a, *(const uint32_t*)br, *(const uint32_t*)(br + 16));
+            }
+            const float dwa = h2f(DW[fa * TKC + kb]), dwb = h2f(DW[fb * TKC + kb]);
+#pragma unroll
+            for (int nt = 0; nt < 4; nt++) {
+                const int ra = th * 32 + nt * 8 + 2 * t;
+                const float dxa = h2f(DX[ra * TKC + kb]), dxb = h2f(DX[(ra + 1) * TKC + kb]);
+                acc[nt][0] = fmaf((float)cc[nt][0], __fmul_rn(dwa, dxa), acc[nt][0]);
+                acc[nt][1] = fmaf((float)cc[nt][1], __fmul_rn(dwa, dxb), acc[nt][1]);
+                acc[nt][2] = fmaf((float)cc[nt][2], __fmul_rn(dwb, dxa), acc[nt][2]);
+                acc[nt][3] = fmaf((float)cc[nt][3], __fmul_rn(dwb, dxb), acc[nt][3]);
+            }
+        }
+        __syncthreads();   // this stage is refilled by the next iteration's prefetch
+    }
+
+    // epilogue: ys[token][feature] (stride TF + 1) then one token row per warp iteration
+    float* ys = (float*)smem;
+#pragma unroll
+    for (int nt = 0; nt < 4; nt++) {
+        const int ra = th * 32 + nt * 8 + 2 * t, fa = rg * 16 + g;
+        ys[ra * (TF + 1) + fa] = acc[nt][0];
+        ys[(ra + 1) * (TF + 1) + fa] = acc[nt][1];
+        ys[ra * (TF + 1) + fa + 8] = acc[nt][2];
+        ys[(ra + 1) * (TF + 1) + fa + 8] = acc[nt][3];
+    }
+    __syncthreads();
+    for (int nl = warp; nl < TT; nl += 8) {
+        const int n = t0 + nl;
+        if (n >= p.M) break;   // warp-uniform
+#pragma unroll
+        for (int half = 0; half < 2; half++) {
+            const int fl = half * 32 + lane, f = f0 + fl;
+            const float a = ys[nl * (TF + 1) + fl];
+            const float bias = p.bias ? p.bias[f] : 0.0f;
+            if (EPI == EPI_BIAS) {
+                const float y = __fadd_rn(a, bias);
+                p.y[(size_t)n * p.N + f] = y;
+                bool ok = p.kv.pool && f >= D;
+                int slot = 0, pos = 0;
+                if (ok) {
+                    if (p.kv.tok_pos) {   // prefill: row n is token tok_pos[n] of slot tok_slot[n]
+                        slot = p.kv.tok_slot[n];
+                        pos = p.kv.tok_pos[n];
+                    } else {              // decode: row n is slot n, at its step position
+                        slot = n;
+                        ok = p.kv.st[n].decode_now != 0;
+                        pos = p.kv.st[n].kvpos;
+                    }
+                }
+                if (ok) {
+                    const int kvsel = (f - D) >> 9, fh = (f - D) & (D - 1);
+                    const int h = fh >> 5, dd = fh & 31;
+                    const int page = p.kv.block_table[(size_t)slot * p.kv.max_pages + pos / PAGE];
+                    const size_t e = ((((size_t)page * p.kv.n_layer + p.kv.layer) * 2 + kvsel) * NH + h) * (PAGE * HD) +
+                                     (size_t)(pos % PAGE) * HD + dd;
+                    if (p.kv.kv_f32) ((float*)p.kv.pool)[e] = y;
+                    else ((__half*)p.kv.pool)[e] = __float2half_rn(y);
+                }
+            } else if (EPI == EPI_RESID) {
+                const float r = p.resid[(size_t)n * p.N + f];
+                p.y[(size_t)n * p.N + f] = __fadd_rn(__fadd_rn(r, a), bias);
+            } else {   // relu(acc + bias), one Q8_0 block per 32 features across the warp
+                float h = __fadd_rn(a, bias);
+                h = h > 0.0f ? h : 0.0f;
+                float amax = fabsf(h);
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+                float dsc, id;
+                q8_scale(amax, dsc, id);
+                p.yq[(size_t)n * p.N + f] = q8_val(h, id);
+                if (lane == 0) p.yd[(size_t)n * (p.N / QK) + f / QK] = f2h(dsc);
+            }
+        }
+    }
+}
+
 template <int T, int KS>
 static void launch_t(const GemmQ8Params& p, int epi, cudaStream_t s) {
     const size_t smem = gemm_smem_bytes(T, KS, p.K);
@@ -225,7 +385,10 @@ cudaError_t gemm_q8_init_device() {
     cudaError_t e;
     if ((e = init_t<1, 4>(512))) return e;
     if ((e = init_t<1, 8>(2048))) return e;
-    return init_t<4, 4>(2048);
+    if ((e = init_t<4, 4>(2048))) return e;
+    if ((e = cudaFuncSetAttribute(k_gemm_q8_tile<EPI_BIAS>, cudaFuncAttributeMaxDynamicSharedMemorySize, TSMEM))) return e;
+    if ((e = cudaFuncSetAttribute(k_gemm_q8_tile<EPI_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, TSMEM))) return e;
+    return cudaFuncSetAttribute(k_gemm_q8_tile<EPI_RELU_Q8>, cudaFuncAttributeMaxDynamicSharedMemorySize, TSMEM);
 }
 
 void launch_gemm_q8(const GemmQ8Params& p, int epi, cudaStream_t s) {
@@ -234,6 +397,13 @@ void launch_gemm_q8(const GemmQ8Params& p, int epi, cudaStream_t s) {
     if (p.M <= 64) {
         if (KB % 32 == 0) launch_t<1, 8>(p, epi, s);
         else launch_t<1, 4>(p, epi, s);
+    } else if (p.N % TF == 0 && KB % TKC == 0) {
+        dim3 grid(p.N / TF, (p.M + TT - 1) / TT);
+        switch (epi) {
+            case EPI_BIAS: launch_pdl(k_gemm_q8_tile<EPI_BIAS>, grid, dim3(256), TSMEM, s, p); break;
+            case EPI_RESID: launch_pdl(k_gemm_q8_tile<EPI_RESID>, grid, dim3(256), TSMEM, s, p); break;
+            default: launch_pdl(k_gemm_q8_tile<EPI_RELU_Q8>, grid, dim3(256), TSMEM, s, p); break;
+        }
     } else {
         launch_t<4, 4>(p, epi, s);
     }

@@ -103,6 +103,12 @@ struct DecAttnParams {
     float* out_f32 = nullptr;
     float* part = nullptr;               // scratch [B][NH][max_chunks][PART_STRIDE]: m, l, -, -, o[HD]
     int partials_only = 0;               // 1: every page leaves its partial (the fused layer tail merges)
+    int slot0 = 0;                       // first slot of this launch: slots slot0 .. slot0 + B - 1
+    // compacted work list of the decode step (k_page_list): item i = {slot, page | kvpos << 8}; this
+    // launch serves items work_base[group] .. work_base[group + 1] - 1 (null: rectangular grid)
+    const int2* work = nullptr;
+    const int32_t* work_base = nullptr;
+    int group = 0;
     int32_t* err = nullptr;              // set to 1 if a bounded wait gave up (may be null)
 };
 // Split-KV work items of decode attention: one per 64-key page. A page's partial result is
@@ -121,12 +127,16 @@ inline bool decode_attention_aligned(const float* q, int q_stride, const void* p
 int launch_decode_attention(const DecAttnParams& p, cudaStream_t s);
 // Raise the dynamic shared-memory limit of the decode-attention kernels on the current device.
 cudaError_t attention_init_device();
+// Build the decode step's (slot, page) list of the M slots (slots decoding this step), slot-major;
+// base[0] = 0, base[1] = items of slots < split, base[2] = all items. M <= 4096.
+void launch_page_list(const SlotState* st, int M, int split, int2* work, int32_t* base, cudaStream_t s);
 
 // ------------------------------------------------------------ fused decode layer tail (dense.cu)
 // Page merge -> out-projection + residual -> LayerNorm 1 -> FFN1 (ReLU) -> FFN2 + residual ->
 // LayerNorm 2 [-> next layer's QKV with the K/V page store], one 16-CTA cluster per 8 slots.
 struct DenseParams {
-    int M = 0;                          // slots (rows); a multiple of 8 is not required
+    int slot0 = 0;                      // first slot (row) of this launch
+    int M = 0;                          // slots (rows) of this launch: slot0 .. slot0 + M - 1
     const SlotState* st = nullptr;
     const float* part = nullptr;        // attention partials of this layer (partials_only launch)
     int max_chunks = 0;

@@ -58,7 +58,7 @@ def test_quantize_bitexact(ctx):
     assert np.array_equal(d.cpu().numpy().view(np.uint16), rd)
 
 
-@pytest.mark.parametrize("M", [1, 8, 13, 64, 100, 257])
+@pytest.mark.parametrize("M", [1, 8, 13, 64, 100, 257, 1000])
 @pytest.mark.parametrize("NK", [(1536, 512), (512, 512), (2048, 512), (512, 2048)])
 def test_q8_gemm_bitexact(ctx, M, NK):
     import gsvcu
