@@ -502,13 +502,19 @@ __global__ void __launch_bounds__(DT, 1) k_dense_layer(const DenseParams p) {
                    32 * KB1 * 2, bar(BW_QKV));
         }
     }
-    {
+    {   // the row's 4 Q8_0 blocks at once: lane (b, c) quantizes columns 4c..4c+3 of block b = lane / 8
         float* hd = (float*)(stg + STG_HD);
+        const int b = lane >> 3, c = lane & 7;
+        const float4 v = *(const float4*)(hown + r * 128 + b * 32 + c * 4);
+        float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 #pragma unroll
-        for (int b = 0; b < 4; b++) {
-            const float d = q8_block_stage(hown[r * 128 + b * 32 + lane], (int8_t*)(stg + STG_H) + b * 32);
-            if (lane == 0) hd[b] = d;
-        }
+        for (int off = 4; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+        float dsc, id;
+        q8_scale(amax, dsc, id);
+        const uint32_t qw = (uint32_t)(uint8_t)q8_val(v.x, id) | (uint32_t)(uint8_t)q8_val(v.y, id) << 8 |
+                            (uint32_t)(uint8_t)q8_val(v.z, id) << 16 | (uint32_t)(uint8_t)q8_val(v.w, id) << 24;
+        *(uint32_t*)(stg + STG_H + b * 32 + c * 4) = qw;
+        if (c == 0) hd[b] = h2f(f2h(dsc));
         send_blocks4((const int8_t*)(stg + STG_H), hd, r, su32(sm + SM_HROWS), RS2, KB2, 4 * rank, bar(BX_H));
     }
 

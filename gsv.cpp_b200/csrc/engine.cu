@@ -240,6 +240,7 @@ struct gsvcu_ctx {
     int32_t* att_err = nullptr;
     // decode steps run the fused layer tail (dense.cu) when the device can hold its cluster
     bool dense_ok = false, fused = true;
+    bool two_groups = false;   // fused step: split the slots into two groups on forked streams (mode 2)
     // two slot groups run their layer chains on these streams, so one group's layer tail overlaps the
     // other group's attention (fork/join events inside the captured step)
     cudaStream_t gstream[2] = {nullptr, nullptr};
@@ -815,7 +816,7 @@ int gsvcu_ctx::launch_step(cudaStream_t s, float* dump, int dump_row, const int*
             TRY(mark(GSVCU_PROF_PREDICT));
             return GSVCU_OK;
         };
-        const bool two = !prof_ms && M >= 32 && M % 32 == 0;
+        const bool two = two_groups && !prof_ms && M >= 32 && M % 32 == 0;
         launch_page_list(st, M, two ? M / 2 : M, work, work_base, s);
         nk++;
         if (!two) {
@@ -1462,19 +1463,24 @@ int gsvcu_step_profile(gsvcu_ctx* ctx, int32_t n_steps, float* ms_by_class, int6
     return GSVCU_OK;
 }
 
-int gsvcu_set_fused_decode(gsvcu_ctx* ctx, int32_t on) {
-    if (!ctx) return GSVCU_ERR_ARG;
+int gsvcu_set_fused_decode(gsvcu_ctx* ctx, int32_t mode) {
+    if (!ctx || mode < 0 || mode > 2) return GSVCU_ERR_ARG;
     DeviceGuard g(ctx->device);
-    if (ctx->fused != (on != 0) && ctx->graph) {   // the captured step belongs to the other variant
+    const bool fused = mode != 0, two = mode == 2;
+    if ((ctx->fused != fused || ctx->two_groups != two) && ctx->graph) {   // the captured step is the other variant
         cudaStreamSynchronize(ctx->stream);
         cudaGraphExecDestroy(ctx->graph);
         ctx->graph = nullptr;
     }
-    ctx->fused = on != 0;
+    ctx->fused = fused;
+    ctx->two_groups = two;
     return GSVCU_OK;
 }
 
-int gsvcu_fused_decode(const gsvcu_ctx* ctx) { return ctx && ctx->fused && ctx->dense_ok ? 1 : 0; }
+int gsvcu_fused_decode(const gsvcu_ctx* ctx) {
+    if (!ctx || !ctx->fused || !ctx->dense_ok) return 0;
+    return ctx->two_groups ? 2 : 1;
+}
 
 int gsvcu_sync(gsvcu_ctx* ctx) {
     if (!ctx) return GSVCU_ERR_ARG;

@@ -276,11 +276,13 @@ class Context:
     def kernel_launches(self):
         return int(self.lib.gsvcu_kernel_launches(self.h))
 
-    def set_fused_decode(self, on):
-        self._check(self.lib.gsvcu_set_fused_decode(self.h, 1 if on else 0))
+    def set_fused_decode(self, mode):
+        """mode: 0 unfused, 1 fused one group, 2 fused two slot groups (True -> 2, False -> 0)."""
+        mode = 2 if mode is True else 0 if mode is False else int(mode)
+        self._check(self.lib.gsvcu_set_fused_decode(self.h, mode))
 
     def fused_decode(self):
-        return bool(self.lib.gsvcu_fused_decode(self.h))
+        return int(self.lib.gsvcu_fused_decode(self.h))
 
     def stream_handle(self):
         return int(self.lib.gsvcu_stream(self.h) or 0)

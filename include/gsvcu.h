@@ -247,11 +247,13 @@ enum {
  * attn_bytes (may be NULL) the algorithmic K/V + q/out bytes the attention launches read and wrote. */
 int gsvcu_step_profile(gsvcu_ctx* ctx, int32_t n_steps, float* ms_by_class, int64_t* attn_bytes);
 /* Decode-step variant (no counterpart in the reference; an implementation switch of this library).
- * on = 1 (default): each layer after attention runs as one 16-CTA cluster kernel (page merge,
+ * mode 1 (default): each layer after attention runs as one 16-CTA cluster kernel (page merge,
  * out-projection, LayerNorm, FFN, LayerNorm, next layer's QKV), when the device can hold such a
- * cluster; on = 0: one kernel per operation. Results are identical. Returns GSVCU_OK;
- * gsvcu_fused_decode tells whether the fused variant is in use. */
-int gsvcu_set_fused_decode(gsvcu_ctx* ctx, int32_t on);
+ * cluster; mode 2: the same with >= 32 slots (a multiple of 32) split into two groups on forked
+ * streams, so one group's layer tail may overlap the other's attention (measured on B200: no gain,
+ * the clusters wait for whole SMs); mode 0: one kernel per operation. Results are identical. Returns GSVCU_OK (GSVCU_ERR_ARG for
+ * another mode); gsvcu_fused_decode returns the mode in use (0 when the cluster does not fit). */
+int gsvcu_set_fused_decode(gsvcu_ctx* ctx, int32_t mode);
 int gsvcu_fused_decode(const gsvcu_ctx* ctx);
 /* Number of kernels this context has launched (graph replays count their kernels). */
 int64_t gsvcu_kernel_launches(const gsvcu_ctx* ctx);

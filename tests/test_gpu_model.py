@@ -120,25 +120,29 @@ def test_fused_and_unfused_decode_steps_agree(gctx, orc):
     for kv in (0, 1):
         _reserve(gctx, kv)
         got = gctx.debug_trace(reqs, forced)
-        gctx.set_fused_decode(False)
+        gctx.set_fused_decode(0)
         try:
             _reserve(gctx, kv)
             unf = gctx.debug_trace(reqs, forced)
         finally:
-            gctx.set_fused_decode(True)
+            gctx.set_fused_decode(1)
         assert np.array_equal(got.view(np.uint32), unf.view(np.uint32)), kv
         ref = orc.decode_trace(reqs, forced, kv_f16=(kv == 0))
         assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), kv
 
 
 def test_fused_two_slot_groups_match_oracle(gctx, orc):
-    """With 64 reserved slots the fused step runs two slot groups on forked streams; sequences in both
-    groups (slots 0..39) decode bit for bit as the oracle."""
+    """Mode 2: with 64 reserved slots the fused step runs two slot groups on forked streams; sequences in
+    both groups (slots 0..39) decode bit for bit as the oracle."""
     rng = np.random.default_rng(23)
     reqs = S.ragged_requests(23, 40, lo=30, hi=120)
     forced = rng.integers(0, 1024, (40, 12)).astype(np.int32)
-    _reserve(gctx, 0, slots=64, ctx=256)
-    got = gctx.debug_trace(reqs, forced)
+    gctx.set_fused_decode(2)
+    try:
+        _reserve(gctx, 0, slots=64, ctx=256)
+        got = gctx.debug_trace(reqs, forced)
+    finally:
+        gctx.set_fused_decode(1)
     ref = orc.decode_trace(reqs, forced, kv_f16=True)
     assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
 
