@@ -166,9 +166,76 @@ __global__ void __launch_bounds__(256) k_gemm_f32d(const float* __restrict__ x, 
     }
 }
 
+// Rows x of width K = 512 times F32 weights w [N][512] (the logits, src/gsv_ar.cpp:266), for few rows:
+// warp per output column n with the column's 512 weights in registers (16 per lane); per row the lane
+// forms its 16 float products, sums them in double, and the warp adds the 32 lane sums in double,
+// rounded once -- the double sum of float products of k_gemm_f32d. A float converts to double by
+// moving its bits into the double's fields, which encodes value * 2^-896 exactly (normal and subnormal
+// floats); the sums are scaled back by 2^896 before the rounding. The scaling is exact as long as no
+// partial sum falls below 2^-126 in magnitude (then its last bits are those of a subnormal double).
+__device__ __forceinline__ double f32_to_f64_scaled(float v) {
+    const uint32_t u = __float_as_uint(v);
+    return __hiloint2double((int)((u & 0x80000000u) | ((u & 0x7fffffffu) >> 3)), (int)(u << 29));
+}
+
+constexpr int LG_ROWS = 4;   // rows per pass (independent sums in flight)
+__global__ void __launch_bounds__(256) k_logits512(const float* __restrict__ x, int ldx, int M,
+                                                   const float* __restrict__ w, int N, const float* __restrict__ add,
+                                                   int ldadd, float* __restrict__ y, int ldy) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n = blockIdx.x * 8 + warp;
+    griddep_wait();
+    griddep_launch();
+    if (n >= N) return;
+    float wr[16];
+    {
+        const float4* wp = (const float4*)(w + (size_t)n * D + lane * 16);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float4 t = wp[i];
+            wr[4 * i] = t.x; wr[4 * i + 1] = t.y; wr[4 * i + 2] = t.z; wr[4 * i + 3] = t.w;
+        }
+    }
+    for (int m0 = 0; m0 < M; m0 += LG_ROWS) {
+        double acc[LG_ROWS];
+#pragma unroll
+        for (int r = 0; r < LG_ROWS; r++) {
+            acc[r] = 0.0;
+            const int m = min(m0 + r, M - 1);
+            const float4* xp = (const float4*)(x + (size_t)m * ldx + lane * 16);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const float4 t = xp[i];
+                acc[r] += f32_to_f64_scaled(__fmul_rn(wr[4 * i], t.x));
+                acc[r] += f32_to_f64_scaled(__fmul_rn(wr[4 * i + 1], t.y));
+                acc[r] += f32_to_f64_scaled(__fmul_rn(wr[4 * i + 2], t.z));
+                acc[r] += f32_to_f64_scaled(__fmul_rn(wr[4 * i + 3], t.w));
+            }
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+            for (int r = 0; r < LG_ROWS; r++) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], off);
+        if (lane < LG_ROWS && m0 + lane < M) {
+            double a = acc[0];
+#pragma unroll
+            for (int r = 1; r < LG_ROWS; r++)
+                if (lane == r) a = acc[r];
+            const int m = m0 + lane;
+            float v = (float)(a * 0x1p896);
+            if (add) v = __fadd_rn(add[(size_t)m * ldadd + n], v);
+            y[(size_t)m * ldy + n] = v;
+        }
+    }
+}
+
 void launch_gemm_f32d(const float* x, int ldx, const F32Gather* gather, int M, const float* w, int N, int K,
                       const float* add, int ldadd, float* y, int ldy, cudaStream_t s) {
     if (M <= 0) return;
+    if (!gather && K == D && M <= 256 && (ldx & 3) == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)w & 15) == 0) {
+        launch_pdl(k_logits512, dim3((N + 7) / 8), dim3(256), 0, s, x, ldx, M, w, N, add, ldadd, y, ldy);
+        return;
+    }
     dim3 grid((N + 31) / 32, (M + 31) / 32);
     F32Gather g;
     if (gather) g = *gather;
