@@ -42,8 +42,10 @@ def parse():
     ap.add_argument("--refill-every", type=int, default=16)
     ap.add_argument("--kv", default="f16", choices=["f16", "f32"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="serve", choices=["serve", "attn"],
-                    help="serve: config-4 serving shard (the bench line); attn: config-3 decode-attention sweep")
+    ap.add_argument("--workload", default="serve", choices=["serve", "attn", "gemv", "prefill", "single"],
+                    help="serve: config-4 serving shard (the bench line); attn: config-3 decode-attention sweep; "
+                         "gemv: config-3 Q8_0 GEMV sweep; prefill: config-2 prefill attention + GEMMs; "
+                         "single: config-0 single-sequence decode latency")
     ap.add_argument("--attn-batches", default="1,8,32,64,128")
     return ap.parse_args()
 
@@ -106,6 +108,180 @@ def attn_sweep(args):
                           "frac": gbs / peak, "l2": "256 MiB flush between launches"}))
         del pool, flush
         torch.cuda.empty_cache()
+    ctx.close()
+
+
+def _flush_and_time(ext, flush, call, reps):
+    """Median CUDA-event time (ms) of call() on the library stream, L2 flushed before each launch."""
+    import torch
+    times = []
+    for _ in range(reps):
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(ext):
+            flush.zero_()
+        e0.record(ext)
+        call()
+        e1.record(ext)
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    return float(np.median(times))
+
+
+def _rand_q8(rng, rows, K):
+    """Random Q8_0 blocks in GGUF layout [rows][K/32][34]: fp16 scale + 32 int8 (no quantizer needed)."""
+    raw = np.zeros((rows, K // 32, 34), np.uint8)
+    raw[..., :2] = (rng.uniform(0.0005, 0.002, (rows, K // 32)).astype(np.float16)).view(np.uint8).reshape(rows, K // 32, 2)
+    raw[..., 2:] = rng.integers(-127, 128, (rows, K // 32, 32)).astype(np.int8).view(np.uint8)
+    return raw
+
+
+def gemv_sweep(args):
+    """BASELINE config 3, GEMV half: Q8_0 GEMM/GEMV shapes 512x1536, 512x512, 512x2048, 2048x512 (the unfused
+    decode kernels, one launch each) and the 512x1025 F32 logits projection, at B in {1,8,32,64,128}, with a
+    256 MiB L2 flush before each launch. Algorithmic bytes: weights (34/32 B per Q8_0 weight, 4 B per F32
+    weight) + activations in + outputs."""
+    import torch
+    import gsvcu
+    ctx = gsvcu.Context(0)
+    ext = torch.cuda.ExternalStream(ctx.stream_handle())
+    peak, peak_kind = measured_peaks()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    rng = np.random.default_rng(3)
+    for (N, K) in [(1536, 512), (512, 512), (2048, 512), (512, 2048)]:
+        raw = _rand_q8(rng, N, K)
+        wq = torch.empty(N * K, dtype=torch.uint8, device="cuda")
+        wd = torch.empty(N * K // 32, dtype=torch.int16, device="cuda")
+        ctx.op_pack_q8_0(raw, N, K, wq, wd)
+        bias = torch.randn(N, device="cuda")
+        for B in [int(b) for b in args.attn_batches.split(",")]:
+            xraw = _rand_q8(rng, B, K)
+            xq = torch.from_numpy(np.ascontiguousarray(xraw[..., 2:]).reshape(B, K).view(np.int8)).cuda()
+            xd = torch.from_numpy(np.ascontiguousarray(xraw[..., :2]).reshape(B, K // 32, 2).view(np.int16)
+                                  .reshape(B, K // 32)).cuda()
+            y = torch.empty((B, N), device="cuda")
+            call = lambda: ctx.op_q8_gemm(xq, xd, B, wq, wd, N, K, bias, None, gsvcu.EPI_BIAS, y=y)
+            for _ in range(max(args.warmup, 50)):
+                call()
+            ms = _flush_and_time(ext, flush, call, max(args.steps, 5))
+            nbytes = N * K * 34 // 32 + B * (K + K // 16) + B * N * 4 + N * 4
+            gbs = nbytes / (ms * 1e-3) / 1e9
+            print(json.dumps({"workload": "cfg3 Q8_0 GEMV", "shape": f"{K}x{N}", "B": B, "algorithmic_bytes": nbytes,
+                              "ms": ms, "GBps": gbs, "peak": peak, "peak_kind": peak_kind, "frac": gbs / peak,
+                              "kernel": "k_gemm_q8 (unfused decode path, one launch)",
+                              "l2": "256 MiB flush before each launch"}))
+    N, K = 1025, 512
+    w = torch.randn((N, K), device="cuda") * 0.02
+    for B in [int(b) for b in args.attn_batches.split(",")]:
+        x = torch.randn((B, K), device="cuda")
+        y = torch.empty((B, N), device="cuda")
+        call = lambda: ctx.op_f32_gemm(x, B, w, N, K, None, y)
+        for _ in range(max(args.warmup, 50)):
+            call()
+        ms = _flush_and_time(ext, flush, call, max(args.steps, 5))
+        nbytes = N * K * 4 + B * K * 4 + B * N * 4
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        print(json.dumps({"workload": "cfg3 logits GEMV (F32 predict)", "shape": f"{K}x{N}", "B": B,
+                          "algorithmic_bytes": nbytes, "ms": ms, "GBps": gbs, "peak": peak, "peak_kind": peak_kind,
+                          "frac": gbs / peak, "kernel": "k_logits512", "l2": "256 MiB flush before each launch"}))
+    ctx.close()
+
+
+def prefill_bench(args):
+    """B=8 sequences of 512 positions, the first 256 bidirectional text positions, the last
+    256 semantic positions causal with full access to the text; 16 heads x 32, Q/K/V ~ N(0,1). Times the
+    prefix-masked prefill attention (one layer) and the four Q8_0 GEMMs at M = 8*512 = 4096, and measures
+    the int8 tensor peak in this run (torch._int_mm, cuBLASLt, 8192^3) as the GEMMs' denominator."""
+    import torch
+    import gsvcu
+    ctx = gsvcu.Context(0)
+    ext = torch.cuda.ExternalStream(ctx.stream_handle())
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    B, S, T = 8, 512, 256
+    M = B * S
+    qkv = torch.randn((M, 1536), device="cuda")
+    out_q = torch.empty((M, 512), dtype=torch.int8, device="cuda")
+    out_d = torch.empty((M, 16), dtype=torch.int16, device="cuda")
+    starts = np.arange(B, dtype=np.int32) * S
+    call = lambda: ctx.op_prefill_attention(qkv, starts, [S] * B, [T] * B, out_q, out_d)
+    for _ in range(max(args.warmup, 10)):
+        call()
+    ms = _flush_and_time(ext, flush, call, max(args.steps, 5))
+    pairs = T * T + T * T + T * (T + 1) // 2          # visible (query, key) pairs per sequence
+    flops = 4 * 512 * pairs * B
+    print(json.dumps({"workload": "cfg2 prefill attention (one layer)", "B": B, "S": S, "text": T,
+                      "visible_pairs_per_seq": pairs, "mask_density": pairs / (S * S), "algorithmic_flops": flops,
+                      "ms": ms, "TFLOPs": flops / (ms * 1e-3) / 1e12,
+                      "bound": "FP64 CUDA cores (pinned double-precision softmax, thread per query)"}))
+    # int8 tensor-core peak measured here (the GEMMs' denominator)
+    a = torch.randint(-127, 128, (8192, 8192), dtype=torch.int8, device="cuda")
+    b = torch.randint(-127, 128, (8192, 8192), dtype=torch.int8, device="cuda")
+    for _ in range(3):
+        torch._int_mm(a, b)
+    torch.cuda.synchronize()
+    best = 1e9
+    for _ in range(10):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch._int_mm(a, b)
+        e1.record()
+        torch.cuda.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    int8_tops = 2 * 8192 ** 3 / (best * 1e-3) / 1e12
+    del a, b
+    rng = np.random.default_rng(4)
+    for (N, K) in [(1536, 512), (512, 512), (2048, 512), (512, 2048)]:
+        raw = _rand_q8(rng, N, K)
+        wq = torch.empty(N * K, dtype=torch.uint8, device="cuda")
+        wd = torch.empty(N * K // 32, dtype=torch.int16, device="cuda")
+        ctx.op_pack_q8_0(raw, N, K, wq, wd)
+        xraw = _rand_q8(rng, M, K)
+        xq = torch.from_numpy(np.ascontiguousarray(xraw[..., 2:]).reshape(M, K).view(np.int8)).cuda()
+        xd = torch.from_numpy(np.ascontiguousarray(xraw[..., :2]).reshape(M, K // 32, 2).view(np.int16)
+                              .reshape(M, K // 32)).cuda()
+        y = torch.empty((M, N), device="cuda")
+        bias = torch.randn(N, device="cuda")
+        call = lambda: ctx.op_q8_gemm(xq, xd, M, wq, wd, N, K, bias, None, gsvcu.EPI_BIAS, y=y)
+        for _ in range(max(args.warmup, 10)):
+            call()
+        ms = _flush_and_time(ext, flush, call, max(args.steps, 5))
+        tops = 2 * M * N * K / (ms * 1e-3) / 1e12
+        print(json.dumps({"workload": "cfg2 prefill Q8_0 GEMM", "M": M, "shape": f"{K}x{N}", "ms": ms,
+                          "TOPs": tops, "peak_int8_TOPs_measured_here": int8_tops, "frac": tops / int8_tops,
+                          "kernel": "k_gemm_q8_tile (mma.m16n8k32 s8 per Q8_0 block + pinned float chain)"}))
+    ctx.close()
+
+
+def single_bench(args):
+    """one sequence, 120 phones with BERT features + 40 prompt codes, greedy decode
+    (top_k 1), early stop off, up to 500 steps; reports per-token decode latency (the reference's published
+    CPU figure is 12.55 ms/token on 4 threads)."""
+    import torch
+    import gsv_synth as S
+    import gsvcu
+    model = S.cached_model(MODEL_CACHE, seed=0, n_layer=24)
+    ctx = gsvcu.Context(0)
+    ctx.load(model)
+    ctx.kv_reserve(1, 700, gsvcu.KV_F16 if args.kv == "f16" else gsvcu.KV_F32)
+    rng = np.random.default_rng(120)
+    req = S.make_request(rng, 120, 40)
+    ext = torch.cuda.ExternalStream(ctx.stream_handle())
+    for _ in range(max(args.warmup, 3)):
+        ctx.generate([req], top_k=1, seed_base=1, max_steps=500)
+    res = []
+    for _ in range(max(args.steps, 3)):
+        ctx.sync()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(ext)
+        toks, lens = ctx.generate([req], top_k=1, seed_base=1, max_steps=500)
+        e1.record(ext)
+        torch.cuda.synchronize()
+        res.append((e0.elapsed_time(e1), int(lens[0])))
+    ms, n = min(res)
+    print(json.dumps({"workload": "cfg0 single sequence, greedy", "prefix": "120 phones + 40 prompt",
+                      "tokens": n, "ms_total": ms, "ms_per_token": ms / max(n, 1),
+                      "note": "wall time on the library stream incl. prefill and the 16-step status reads",
+                      "reference_cpu_ms_per_token": 12.55}))
     ctx.close()
 
 
@@ -266,9 +442,9 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     n_gpus = max(args.gpus, world)
 
-    if args.workload == "attn":
+    if args.workload != "serve":
         if rank == 0:
-            attn_sweep(args)
+            {"attn": attn_sweep, "gemv": gemv_sweep, "prefill": prefill_bench, "single": single_bench}[args.workload](args)
         return
 
     if args.impl == "reference":
@@ -351,6 +527,14 @@ def main():
     ctx.serve_admit([r for r, _ in prof_q[:args.slots]], [s for _, s in prof_q[:args.slots]],
                     list(range(args.slots)), max_steps=args.iters)
     ctx.serve_step(args.iters // 2)
+    # whole decode step (graph replay) at this state: weights + every decoding slot's K/V
+    ctx.sync()
+    se0, se1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    se0.record(ext)
+    ctx.serve_step(16)
+    se1.record(ext)
+    torch.cuda.synchronize()
+    step_ms = se0.elapsed_time(se1) / 16
     prof_steps = 8
     ms_cls, attn_bytes = ctx.step_profile(prof_steps)
     ctx.serve_reset()
@@ -387,6 +571,12 @@ def main():
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": (tpk * keys_launch) if tpk else None, "algorithmic_bytes_per_launch": bytes_launch,
                      "avg_launch_ms": attn_ms},
+        "decode_step_roofline": {"bytes_per_step": 82954240 + attn_bytes / prof_steps, "ms_per_step": step_ms,
+                                 "achieved": (82954240 + attn_bytes / prof_steps) / (step_ms * 1e-3) / 1e9,
+                                 "peak": peak, "unit": "GB/s",
+                                 "frac": (82954240 + attn_bytes / prof_steps) / (step_ms * 1e-3) / 1e9 / peak,
+                                 "state": "mid-job (iteration ~iters/2), 16 graph-replayed steps; bytes = Q8_0 + "
+                                          "F32 weights (82.95 MB) + K/V and q/out of every decoding slot"},
         "step_profile_ms": {k: round(v / prof_steps, 4) for k, v in ms_cls.items()},
         "clocks": clocks,
     }
