@@ -10,6 +10,7 @@
 
 namespace gsvcu {
 
+
 // ------------------------------------------------------------------ decode
 // Work item = (slot, head, 64-key page), one warp each, 4 heads (warps) per CTA. Lane 0 stages the
 // head's K and V rows of the page into shared memory with two TMA bulk copies (cp.async.bulk, no
@@ -125,6 +126,63 @@ template <typename KT> struct DecShape {
     static constexpr size_t SMEM = (size_t)4 * WARPB + 4 * 8;   // 4 warps + 4 mbarriers
 };
 
+// One warp: the pinned-order softmax of one head over one staged page (n keys of K rows ks, V rows vs)
+// for query q (lane (g, s) holds dims 8s..8s+7); returns the page max m, sum l and o (lane's 8 dims).
+template <typename KT>
+__device__ __forceinline__ void page_softmax(const uint8_t* ks, const uint8_t* vs, int n, const float (&q)[8],
+                                             float scale, float& m_out, float& l_out, float (&o)[8]) {
+    using S = DecShape<KT>;
+    const int lane = threadIdx.x & 31, sub = lane & 3, g = lane >> 2;
+    // scores of the lane's 8 keys t = 8u + g
+    float sc[8], m = -INFINITY;
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+        const int t = 8 * u + g;
+        float d = 0.0f;
+        if (t < n) {
+            float kf[8];
+            load8<KT>(ks + (size_t)t * S::ROWB + sub * 8 * sizeof(KT), kf);
+#pragma unroll
+            for (int e = 0; e < 8; e++) d = fmaf(q[e], kf[e], d);
+        }
+        d = __fadd_rn(d, __shfl_xor_sync(0xffffffffu, d, 1));
+        d = __fadd_rn(d, __shfl_xor_sync(0xffffffffu, d, 2));
+        sc[u] = t < n ? __fmul_rn(d, scale) : -INFINITY;
+        m = fmaxf(m, sc[u]);
+    }
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    // weights: lane (g, s) evaluates keys u = s and u = s + 4 of its group, then they are shared
+    float sa = sc[0], sb = sc[4];
+#pragma unroll
+    for (int u = 1; u < 4; u++)
+        if (sub == u) { sa = sc[u]; sb = sc[u + 4]; }
+    const float pa = exp_canon(sa - m), pb = exp_canon(sb - m);   // exp_canon(-inf) = 0 for keys past the end
+    float l = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 8; e++) o[e] = 0.0f;
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+        const float pu = __shfl_sync(0xffffffffu, u < 4 ? pa : pb, 4 * g + (u & 3));
+        const int t = 8 * u + g;
+        if (t < n) {
+            float vf[8];
+            load8<KT>(vs + (size_t)t * S::ROWB + sub * 8 * sizeof(KT), vf);
+            l = __fadd_rn(l, pu);
+#pragma unroll
+            for (int e = 0; e < 8; e++) o[e] = fmaf(pu, vf[e], o[e]);
+        }
+    }
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+        l = __fadd_rn(l, __shfl_xor_sync(0xffffffffu, l, off));
+#pragma unroll
+        for (int e = 0; e < 8; e++) o[e] = __fadd_rn(o[e], __shfl_xor_sync(0xffffffffu, o[e], off));
+    }
+    m_out = m;
+    l_out = l;
+}
+
 // One CTA per (4-head group, page, slot); warp = head. Pages of sequences longer than one page leave a
 // partial {m, l, -, -, o[32]} for k_decode_merge; one-page sequences are finished here.
 template <typename KT>
@@ -203,52 +261,8 @@ __global__ void __launch_bounds__(128) k_decode_attn(const DecAttnParams p) {
         (void)mbar_wait_bounded(bar);
     }
 
-    // scores of the lane's 8 keys t = 8u + g
-    float sc[8], m = -INFINITY;
-#pragma unroll
-    for (int u = 0; u < 8; u++) {
-        const int t = 8 * u + g;
-        float d = 0.0f;
-        if (t < n) {
-            float kf[8];
-            load8<KT>(ks + (size_t)t * S::ROWB + sub * 8 * sizeof(KT), kf);
-#pragma unroll
-            for (int e = 0; e < 8; e++) d = fmaf(q[e], kf[e], d);
-        }
-        d = __fadd_rn(d, __shfl_xor_sync(0xffffffffu, d, 1));
-        d = __fadd_rn(d, __shfl_xor_sync(0xffffffffu, d, 2));
-        sc[u] = t < n ? __fmul_rn(d, p.scale) : -INFINITY;
-        m = fmaxf(m, sc[u]);
-    }
-#pragma unroll
-    for (int off = 4; off < 32; off <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-    // weights: lane (g, s) evaluates keys u = s and u = s + 4 of its group, then they are shared
-    float sa = sc[0], sb = sc[4];
-#pragma unroll
-    for (int u = 1; u < 4; u++)
-        if (sub == u) { sa = sc[u]; sb = sc[u + 4]; }
-    const float pa = exp_canon(sa - m), pb = exp_canon(sb - m);   // exp_canon(-inf) = 0 for keys past the end
-    float l = 0.0f, o[8];
-#pragma unroll
-    for (int e = 0; e < 8; e++) o[e] = 0.0f;
-#pragma unroll
-    for (int u = 0; u < 8; u++) {
-        const float pu = __shfl_sync(0xffffffffu, u < 4 ? pa : pb, 4 * g + (u & 3));
-        const int t = 8 * u + g;
-        if (t < n) {
-            float vf[8];
-            load8<KT>(vs + (size_t)t * S::ROWB + sub * 8 * sizeof(KT), vf);
-            l = __fadd_rn(l, pu);
-#pragma unroll
-            for (int e = 0; e < 8; e++) o[e] = fmaf(pu, vf[e], o[e]);
-        }
-    }
-#pragma unroll
-    for (int off = 4; off < 32; off <<= 1) {
-        l = __fadd_rn(l, __shfl_xor_sync(0xffffffffu, l, off));
-#pragma unroll
-        for (int e = 0; e < 8; e++) o[e] = __fadd_rn(o[e], __shfl_xor_sync(0xffffffffu, o[e], off));
-    }
+    float m, l, o[8];
+    page_softmax<KT>(ks, vs, n, q, p.scale, m, l, o);
     if (nkeys <= PAGE && !p.partials_only) {
         decode_write_out(p, slot, h, g, sub, o, l);
         return;
@@ -314,7 +328,7 @@ __global__ void __launch_bounds__(128) k_decode_merge(const DecAttnParams p) {
 
 cudaError_t attention_init_device() {
     cudaError_t e = cudaFuncSetAttribute(k_decode_attn<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)DecShape<__half>::SMEM);
+                             (int)DecShape<__half>::SMEM);
     if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(k_decode_attn<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)DecShape<float>::SMEM);

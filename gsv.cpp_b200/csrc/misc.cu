@@ -178,7 +178,8 @@ __device__ __forceinline__ double f32_to_f64_scaled(float v) {
     return __hiloint2double((int)((u & 0x80000000u) | ((u & 0x7fffffffu) >> 3)), (int)(u << 29));
 }
 
-constexpr int LG_ROWS = 4;   // rows per pass (independent sums in flight)
+// 32 rows per pass: each lane forms its 16-product double sums for all 32 rows, then a butterfly
+// reduce-scatter over the warp (31 double shuffles) leaves row r's total in lane r.
 __global__ void __launch_bounds__(256) k_logits512(const float* __restrict__ x, int ldx, int M,
                                                    const float* __restrict__ w, int N, const float* __restrict__ add,
                                                    int ldadd, float* __restrict__ y, int ldy) {
@@ -196,33 +197,37 @@ __global__ void __launch_bounds__(256) k_logits512(const float* __restrict__ x, 
             wr[4 * i] = t.x; wr[4 * i + 1] = t.y; wr[4 * i + 2] = t.z; wr[4 * i + 3] = t.w;
         }
     }
-    for (int m0 = 0; m0 < M; m0 += LG_ROWS) {
-        double acc[LG_ROWS];
+    for (int m0 = 0; m0 < M; m0 += 32) {
+        double acc[32];
 #pragma unroll
-        for (int r = 0; r < LG_ROWS; r++) {
-            acc[r] = 0.0;
+        for (int r = 0; r < 32; r++) {
             const int m = min(m0 + r, M - 1);
             const float4* xp = (const float4*)(x + (size_t)m * ldx + lane * 16);
+            double a = 0.0;
 #pragma unroll
             for (int i = 0; i < 4; i++) {
                 const float4 t = xp[i];
-                acc[r] += f32_to_f64_scaled(__fmul_rn(wr[4 * i], t.x));
-                acc[r] += f32_to_f64_scaled(__fmul_rn(wr[4 * i + 1], t.y));
-                acc[r] += f32_to_f64_scaled(__fmul_rn(wr[4 * i + 2], t.z));
-                acc[r] += f32_to_f64_scaled(__fmul_rn(wr[4 * i + 3], t.w));
+                a += f32_to_f64_scaled(__fmul_rn(wr[4 * i], t.x));
+                a += f32_to_f64_scaled(__fmul_rn(wr[4 * i + 1], t.y));
+                a += f32_to_f64_scaled(__fmul_rn(wr[4 * i + 2], t.z));
+                a += f32_to_f64_scaled(__fmul_rn(wr[4 * i + 3], t.w));
+            }
+            acc[r] = a;
+        }
+        // reduce-scatter: after the step with bit s, a lane keeps the half of its rows selected by its bit s
+#pragma unroll
+        for (int s = 16; s >= 1; s >>= 1) {
+#pragma unroll
+            for (int j = 0; j < s; j++) {
+                const bool hi = (lane & s) != 0;
+                const double send = hi ? acc[j] : acc[j + s];
+                const double keep = hi ? acc[j + s] : acc[j];
+                acc[j] = keep + __shfl_xor_sync(0xffffffffu, send, s);
             }
         }
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1)
-#pragma unroll
-            for (int r = 0; r < LG_ROWS; r++) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], off);
-        if (lane < LG_ROWS && m0 + lane < M) {
-            double a = acc[0];
-#pragma unroll
-            for (int r = 1; r < LG_ROWS; r++)
-                if (lane == r) a = acc[r];
-            const int m = m0 + lane;
-            float v = (float)(a * 0x1p896);
+        const int m = m0 + lane;
+        if (m < M) {
+            float v = (float)(acc[0] * 0x1p896);
             if (add) v = __fadd_rn(add[(size_t)m * ldadd + n], v);
             y[(size_t)m * ldy + n] = v;
         }
