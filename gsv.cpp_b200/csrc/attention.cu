@@ -198,7 +198,7 @@ __global__ void __launch_bounds__(128) k_decode_attn(const DecAttnParams p) {
         griddep_wait();
         griddep_launch();
     }
-    int slot, chunk, h, kvpos;
+    int slot, chunk, h, kvpos, ppage = -1;   // ppage: physical page when the list carries it
     bool act;
     if (p.work) {   // compacted list: CTA = (item, head group), trailing CTAs past the list exit
         const int item = p.work_base[p.group] + (int)(blockIdx.x >> 2);
@@ -206,10 +206,11 @@ __global__ void __launch_bounds__(128) k_decode_attn(const DecAttnParams p) {
         act = item < p.work_base[p.group + 1];
         slot = 0; chunk = 0; kvpos = 0;
         if (act) {
-            const int2 w = p.work[item];
+            const int4 w = p.work[item];
             slot = w.x;
             chunk = w.y & 0xff;
             kvpos = w.y >> 8;
+            ppage = w.z;
         }
     } else {
         slot = p.slot0 + blockIdx.z;
@@ -230,7 +231,7 @@ __global__ void __launch_bounds__(128) k_decode_attn(const DecAttnParams p) {
     const uint32_t bar = smem_u32((uint64_t*)(sm + 4 * S::WARPB) + warp);
     const bool fresh = chunk == kvpos / PAGE;   // holds the key the previous kernel wrote this step
     auto stage = [&]() {
-        const int page = p.block_table[(size_t)slot * p.max_pages + chunk];
+        const int page = ppage >= 0 ? ppage : p.block_table[(size_t)slot * p.max_pages + chunk];
         const KT* kp = (const KT*)p.pool + (size_t)page * p.n_layer * 2 * NH * PAGE * HD +
                        ((size_t)p.layer * 2 * NH + h) * PAGE * HD;
         const uint32_t bytes = (uint32_t)n * S::ROWB;
@@ -335,7 +336,8 @@ cudaError_t attention_init_device() {
 }
 
 // One CTA of 1024 threads: slot-major exclusive prefix of the slots' page counts, then the items.
-__global__ void __launch_bounds__(1024) k_page_list(const SlotState* st, int M, int split, int2* work, int32_t* base) {
+__global__ void __launch_bounds__(1024) k_page_list(const SlotState* st, int M, int split, const int32_t* block_table,
+                                                   int max_pages, int4* work, int32_t* base) {
     griddep_wait();
     griddep_launch();
     __shared__ int wsum[32];
@@ -377,7 +379,8 @@ __global__ void __launch_bounds__(1024) k_page_list(const SlotState* st, int M, 
     for (int i = 0; i < 4; i++) {
         const int slot = t * C + i;
         if (i < C && slot == split) base[1] = off;
-        for (int pg = 0; pg < np[i]; pg++) work[off + pg] = make_int2(slot, pg | (kp[i] << 8));
+        for (int pg = 0; pg < np[i]; pg++)
+            work[off + pg] = make_int4(slot, pg | (kp[i] << 8), block_table[(size_t)slot * max_pages + pg], 0);
         off += np[i];
     }
     if (t == 1023) {
@@ -386,8 +389,9 @@ __global__ void __launch_bounds__(1024) k_page_list(const SlotState* st, int M, 
     }
 }
 
-void launch_page_list(const SlotState* st, int M, int split, int2* work, int32_t* base, cudaStream_t s) {
-    launch_pdl(k_page_list, dim3(1), dim3(1024), 0, s, st, M, split, work, base);
+void launch_page_list(const SlotState* st, int M, int split, const int32_t* block_table, int max_pages, int4* work,
+                      int32_t* base, cudaStream_t s) {
+    launch_pdl(k_page_list, dim3(1), dim3(1024), 0, s, st, M, split, block_table, max_pages, work, base);
 }
 
 int launch_decode_attention(const DecAttnParams& p, cudaStream_t s) {

@@ -211,7 +211,7 @@ struct gsvcu_ctx {
     uint16_t *xd = nullptr, *ad = nullptr, *n1d = nullptr, *hd = nullptr;
     float* part = nullptr;
     int max_chunks = 0;
-    int2* work = nullptr;          // the decode step's (slot, page) list and its group offsets
+    int4* work = nullptr;          // the decode step's (slot, page) list and its group offsets
     int32_t* work_base = nullptr;
     // prefill staging
     int32_t *p_ids = nullptr, *p_pepos = nullptr, *p_istext = nullptr, *p_tslot = nullptr, *p_tpos = nullptr,
@@ -429,7 +429,7 @@ int gsvcu_ctx::reserve(int slots, int ctx, int kvd) {
         {(void**)&xd, M * D / QK * 2}, {(void**)&ad, M * D / QK * 2}, {(void**)&n1d, M * D / QK * 2},
         {(void**)&hd, M * FF / QK * 2},
         {(void**)&part, (size_t)max_slots * NH * max_chunks * PART_STRIDE * 4},
-        {(void**)&work, (size_t)max_slots * max_chunks * sizeof(int2)}, {(void**)&work_base, 4 * 4},
+        {(void**)&work, (size_t)max_slots * max_chunks * sizeof(int4)}, {(void**)&work_base, 4 * 4},
         {(void**)&p_ids, M * 4}, {(void**)&p_pepos, M * 4}, {(void**)&p_istext, M * 4},
         {(void**)&p_tslot, M * 4}, {(void**)&p_tpos, M * 4}, {(void**)&p_rowT, M * 4}, {(void**)&p_rowoff, M * 8},
         {(void**)&p_sstart, (size_t)max_slots * 4}, {(void**)&p_slen, (size_t)max_slots * 4},
@@ -817,7 +817,7 @@ int gsvcu_ctx::launch_step(cudaStream_t s, float* dump, int dump_row, const int*
             return GSVCU_OK;
         };
         const bool two = two_groups && !prof_ms && M >= 32 && M % 32 == 0;
-        launch_page_list(st, M, two ? M / 2 : M, work, work_base, s);
+        launch_page_list(st, M, two ? M / 2 : M, block_table, max_pages, work, work_base, s);
         nk++;
         if (!two) {
             TRY(chain(s, 0, M));

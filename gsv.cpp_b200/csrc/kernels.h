@@ -104,9 +104,9 @@ struct DecAttnParams {
     float* part = nullptr;               // scratch [B][NH][max_chunks][PART_STRIDE]: m, l, -, -, o[HD]
     int partials_only = 0;               // 1: every page leaves its partial (the fused layer tail merges)
     int slot0 = 0;                       // first slot of this launch: slots slot0 .. slot0 + B - 1
-    // compacted work list of the decode step (k_page_list): item i = {slot, page | kvpos << 8}; this
-    // launch serves items work_base[group] .. work_base[group + 1] - 1 (null: rectangular grid)
-    const int2* work = nullptr;
+    // compacted work list of the decode step (k_page_list): item i = {slot, chunk | kvpos << 8, physical
+    // page, 0}; this launch serves items work_base[group] .. work_base[group + 1] - 1 (null: rectangular grid)
+    const int4* work = nullptr;
     const int32_t* work_base = nullptr;
     int group = 0;
     int32_t* err = nullptr;              // set to 1 if a bounded wait gave up (may be null)
@@ -129,7 +129,8 @@ int launch_decode_attention(const DecAttnParams& p, cudaStream_t s);
 cudaError_t attention_init_device();
 // Build the decode step's (slot, page) list of the M slots (slots decoding this step), slot-major;
 // base[0] = 0, base[1] = items of slots < split, base[2] = all items. M <= 4096.
-void launch_page_list(const SlotState* st, int M, int split, int2* work, int32_t* base, cudaStream_t s);
+void launch_page_list(const SlotState* st, int M, int split, const int32_t* block_table, int max_pages, int4* work,
+                      int32_t* base, cudaStream_t s);
 
 // ------------------------------------------------------------ fused decode layer tail (dense.cu)
 // Page merge -> out-projection + residual -> LayerNorm 1 -> FFN1 (ReLU) -> FFN2 + residual ->
