@@ -42,6 +42,8 @@ def parse():
     ap.add_argument("--refill-every", type=int, default=16)
     ap.add_argument("--kv", default="f16", choices=["f16", "f32"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--lookahead", action="store_true",
+                    help="serve with gsvcu_set_serve_lookahead (the next chunk runs while the host handles results)")
     ap.add_argument("--workload", default="serve", choices=["serve", "attn", "gemv", "prefill", "single"],
                     help="serve: config-4 serving shard (the bench line); attn: config-3 decode-attention sweep; "
                          "gemv: config-3 Q8_0 GEMV sweep; prefill: config-2 prefill attention + GEMMs; "
@@ -337,16 +339,26 @@ def run_job(ctx, queue, args, counters):
         counters["seqs"] += k
 
     admit(args.slots)
+    lookahead = args.lookahead
+    ctx.set_serve_lookahead(lookahead)
     it = 0
-    while it < args.iters:
+    if lookahead:   # the first call only starts a chunk; each later call reports the previous one
+        it = min(args.refill_every, args.iters)
+        ctx.serve_step(it, max_done=args.slots, tok_cap=args.slots * args.iters)
+    while True:
         n = min(args.refill_every, args.iters - it)
+        if not lookahead and n == 0:
+            break
         done = ctx.serve_step(n, max_done=args.slots, tok_cap=args.slots * args.iters)
-        it += n
         counters["d2h"] += 64 * ctx.lib.gsvcu_serve_active(ctx.h) + sum(4 * len(d["tokens"]) for d in done)
+        if lookahead and n == 0:
+            break
+        it += n
         if done and it < args.iters:
             admit(len(done))
     tokens = ctx.serve_tokens_total() - t0
     ctx.serve_reset()
+    ctx.set_serve_lookahead(False)
     return tokens
 
 
@@ -562,6 +574,7 @@ def main():
                    "slots_per_gpu": args.slots, "iters_per_job": args.iters, "refill_every": args.refill_every,
                    "sampler": "top_k 15, top_p 1.0, temperature 1.0, rep 1.35, EOS 1024",
                    "kv_cache": f"paged {args.kv}, 64-token pages", "parallelism": f"dp{n_gpus} (replicas, batch-sharded)",
+                   "serve_lookahead": args.lookahead,
                    "l2": "no flush; KV working set per step (>1 GB) exceeds the 126 MB L2",
                    "tokens_per_step": tok_v / args.steps, "sequences_per_step": seqs_v / args.steps},
         "gpu_launches": launches_v,

@@ -241,6 +241,8 @@ struct gsvcu_ctx {
     // decode steps run the fused layer tail (dense.cu) when the device can hold its cluster
     bool dense_ok = false, fused = true;
     bool two_groups = false;   // fused step: split the slots into two groups on forked streams (mode 2)
+    // serving lookahead: gsvcu_serve_step leaves the next chunk of steps running when it returns
+    bool lookahead = false, inflight = false;
     // two slot groups run their layer chains on these streams, so one group's layer tail overlaps the
     // other group's attention (fork/join events inside the captured step)
     cudaStream_t gstream[2] = {nullptr, nullptr};
@@ -1026,12 +1028,17 @@ int gsvcu_get_hparams(const gsvcu_ctx* ctx, gsvcu_hparams* out) {
 int gsvcu_kv_reserve(gsvcu_ctx* ctx, int32_t max_slots, int32_t max_ctx, int32_t kv_dtype) {
     if (!ctx) return GSVCU_ERR_ARG;
     DeviceGuard g(ctx->device);
+    if (ctx->inflight) return ctx->fail(GSVCU_ERR_STATE, "kv_reserve while a serving chunk is running");
     return ctx->reserve(max_slots, max_ctx, kv_dtype);
 }
 
 int gsvcu_release_cache(gsvcu_ctx* ctx) {
     if (!ctx) return GSVCU_ERR_ARG;
     DeviceGuard g(ctx->device);
+    if (ctx->inflight) {
+        CKC(ctx, cudaStreamSynchronize(ctx->stream));
+        ctx->inflight = false;
+    }
     ctx->free_cache();
     return GSVCU_OK;
 }
@@ -1178,9 +1185,18 @@ int gsvcu_serve_step(gsvcu_ctx* ctx, int32_t n_steps, gsvcu_finished* done, int3
     DeviceGuard g(ctx->device);
     bool any = false;
     for (char u : ctx->slot_used) any |= u != 0;
-    if (!any) return 0;
-    if (n_steps > 0) TRY(ctx->run_steps(n_steps));
-    TRY(ctx->read_status());
+    if (!any && !ctx->inflight) return 0;
+    if (ctx->lookahead && !ctx->inflight) {
+        // nothing running yet: start the first chunk and report nothing
+        if (n_steps > 0) {
+            TRY(ctx->run_steps(n_steps));
+            ctx->inflight = true;
+        }
+        return 0;
+    }
+    if (!ctx->lookahead && n_steps > 0) TRY(ctx->run_steps(n_steps));
+    TRY(ctx->read_status());   // with lookahead: the chunk started by the previous call
+    ctx->inflight = false;
     int nd = 0, used = 0;
     for (int sl = 0; sl < ctx->max_slots; sl++) {
         if (!ctx->slot_used[sl]) continue;
@@ -1194,17 +1210,36 @@ int gsvcu_serve_step(gsvcu_ctx* ctx, int32_t n_steps, gsvcu_finished* done, int3
         f.finish_kind = s.finish_kind;
         f.n_generated = s.finish_kind == 2 ? s.max_steps : s.finish_idx;
         f.n_tokens = 0;
-        if (tokens && keep > 0 && used + keep <= tok_cap) {
+        if (tokens && keep > 0 && used + keep <= tok_cap) {   // copied below, one synchronisation for all
             CKC(ctx, cudaMemcpyAsync(tokens + used, ctx->out_tokens + (size_t)sl * ctx->tok_cap, (size_t)keep * 4,
                                      cudaMemcpyDeviceToHost, ctx->stream));
-            CKC(ctx, cudaStreamSynchronize(ctx->stream));
             f.n_tokens = keep;
             used += keep;
         }
         ctx->tokens_done += keep;
-        ctx->release_slot(sl);
+    }
+    if (used) CKC(ctx, cudaStreamSynchronize(ctx->stream));
+    for (int i = 0; i < nd; i++) ctx->release_slot(done[i].slot);
+    if (ctx->lookahead && n_steps > 0) {
+        bool active = false;
+        for (int sl = 0; sl < ctx->max_slots; sl++) active |= ctx->slot_used[sl] && ctx->h_st[sl].active;
+        if (active) {   // the next chunk runs while the caller handles these results and admits
+            TRY(ctx->run_steps(n_steps));
+            ctx->inflight = true;
+        }
     }
     return nd;
+}
+
+int gsvcu_set_serve_lookahead(gsvcu_ctx* ctx, int32_t on) {
+    if (!ctx) return GSVCU_ERR_ARG;
+    DeviceGuard g(ctx->device);
+    if (ctx->inflight) {   // finish the running chunk under the old rule; its results are reported next call
+        CKC(ctx, cudaStreamSynchronize(ctx->stream));
+    }
+    ctx->lookahead = on != 0;
+    if (!ctx->lookahead) ctx->inflight = false;
+    return GSVCU_OK;
 }
 
 int gsvcu_serve_active(const gsvcu_ctx* ctx) {
@@ -1422,6 +1457,7 @@ int gsvcu_serve_reset(gsvcu_ctx* ctx) {
     if (!ctx->reserved) return GSVCU_OK;
     DeviceGuard g(ctx->device);
     CKC(ctx, cudaStreamSynchronize(ctx->stream));
+    ctx->inflight = false;
     for (int sl = 0; sl < ctx->max_slots; sl++)
         if (ctx->slot_used[sl]) ctx->release_slot(sl);
     CKC(ctx, cudaMemsetAsync(ctx->st, 0, sizeof(SlotState) * ctx->max_slots, ctx->stream));

@@ -85,6 +85,7 @@ SIGNATURES = {
     "gsvcu_stream": ([_P], C.c_void_p),
     "gsvcu_op_decode_attention_noalloc": ([_P, _P, _I, _P, _I, _I, _I, _P, _I, _P, _P, _I, _P, _P, _P], C.c_int),
     "gsvcu_set_fused_decode": ([_P, _I], C.c_int),
+    "gsvcu_set_serve_lookahead": ([_P, _I], C.c_int),
     "gsvcu_fused_decode": ([_P], C.c_int),
 }
 
@@ -275,6 +276,9 @@ class Context:
 
     def kernel_launches(self):
         return int(self.lib.gsvcu_kernel_launches(self.h))
+
+    def set_serve_lookahead(self, on):
+        self._check(self.lib.gsvcu_set_serve_lookahead(self.h, 1 if on else 0))
 
     def set_fused_decode(self, mode):
         """mode: 0 unfused, 1 fused one group, 2 fused two slot groups (True -> 2, False -> 0)."""

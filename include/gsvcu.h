@@ -141,6 +141,13 @@ int gsvcu_serve_admit(gsvcu_ctx* ctx, const gsvcu_request* reqs, int32_t n, cons
  * tok_cap; may be NULL). Returns the number of records (>= 0) or an error. */
 int gsvcu_serve_step(gsvcu_ctx* ctx, int32_t n_steps, gsvcu_finished* done, int32_t max_done, int32_t* tokens,
                      int32_t tok_cap);
+/* Serving lookahead (no counterpart in the reference; an extension of this library's serving API).
+ * on = 1: gsvcu_serve_step(n) first reports the chunk of steps started by the previous call, then
+ * starts the next n steps before it returns, so the GPU keeps decoding while the caller handles the
+ * results and admits new sequences (they join from the chunk started by the following call). The
+ * first call only starts a chunk (returns 0); a final call with n = 0 collects the last chunk.
+ * Tokens of every sequence are the same as without lookahead. Default 0. */
+int gsvcu_set_serve_lookahead(gsvcu_ctx* ctx, int32_t on);
 /* Drop every sequence in flight (cancellation): slots and KV pages return to the pool, nothing is
  * reported. */
 int gsvcu_serve_reset(gsvcu_ctx* ctx);

@@ -241,6 +241,40 @@ def test_serving_refill_equals_generate(gctx):
         assert np.array_equal(served[i], alone[i]), i
 
 
+def test_serving_lookahead_refill_equals_generate(gctx):
+    """With the serving lookahead the next chunk runs while results are collected; refilled sequences
+    join one chunk later and every sequence still decodes exactly as alone."""
+    reqs = S.ragged_requests(56, 6, lo=40, hi=120)
+    seeds = [600 + i for i in range(6)]
+    steps = [40, 40, 40, 40, 68, 75]
+    _reserve(gctx, 0, slots=4, ctx=512)
+    alone = []
+    for i in range(6):
+        t, _ = gctx.generate([reqs[i]], seeds=[seeds[i]], max_steps=steps[i])
+        alone.append(t[0][len(reqs[i].prompt):])
+    gctx.serve_admit(reqs[:4], seeds[:4], list(range(4)), max_steps=40)
+    gctx.set_serve_lookahead(True)
+    try:
+        assert gctx.serve_step(8, tok_cap=100000) == []   # starts the first chunk
+        served, pending = {}, 4
+        for _ in range(200):
+            if len(served) == 6:
+                break
+            for f in gctx.serve_step(8, tok_cap=100000):
+                served[f["tag"]] = f["tokens"]
+                if pending < 6:
+                    gctx.serve_admit([reqs[pending]], [seeds[pending]], [pending], max_steps=steps[pending])
+                    pending += 1
+        for f in gctx.serve_step(0, tok_cap=100000):
+            served[f["tag"]] = f["tokens"]
+    finally:
+        gctx.serve_reset()
+        gctx.set_serve_lookahead(False)
+    assert len(served) == 6
+    for i in range(6):
+        assert np.array_equal(served[i], alone[i]), i
+
+
 def test_cpp_dropin_class(gctx, model_full, tmp_path):
     """The C++ `class gsv_ar` shim (csrc/gsv_ar.cpp) gives the C ABI's results."""
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
