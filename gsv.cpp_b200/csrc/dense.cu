@@ -93,10 +93,15 @@ __device__ __forceinline__ void d_mbar_init(uint32_t bar) {
 __device__ __forceinline__ void d_expect_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
+// Bulk global -> shared copy; weights and parameters are reused every step: kept in L2 (evict-last).
 __device__ __forceinline__ void d_bulk(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-                 "l"(src), "r"(bytes), "r"(bar)
-                 : "memory");
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            dst),
+        "l"(src), "r"(bytes), "r"(bar), "l"(pol)
+        : "memory");
 }
 // Bounded wait on phase 0 of an mbarrier by a whole warp; false if the limit was reached.
 __device__ __forceinline__ bool d_wait(uint32_t bar) {
