@@ -68,9 +68,8 @@ constexpr int P_BOUT = 0, P_BF1 = 32, P_BF2 = 160, P_N1W = 192, P_N1B = 224, P_N
 constexpr int SM_ROWMETA = SM_PAR + P_COUNT * 4;   // per row: pages to merge (0: not decoding), KV page, KV pos
 constexpr int SM_BARS = SM_ROWMETA + DR * 3 * 4;   // 4 weight barriers + 6 exchange barriers
 constexpr int SMEM_DENSE = SM_BARS + 11 * 8;
-// aliases: phase-0 page-merge scratch in the h rows; FFN1's f32 outputs in the attention rows
-constexpr int MERGE_ROW_BYTES = (16 + 16 + 16 * 32) * 4;   // one row: 16 pages' w, l, o
-static_assert(NW == DR && NW * MERGE_ROW_BYTES <= HROWS_BYTES, "merge scratch");
+// alias: FFN1's f32 outputs in the attention rows
+static_assert(NW == DR, "one warp per row");
 static_assert(DR * 128 * 4 <= ROWS1_BYTES, "ffn1 staging");
 static_assert(SM_D_QKV + 96 * KB1 * 2 <= SM_W_F2, "qkv weights reuse out + ffn1");
 static_assert(SMEM_DENSE <= 232448, "shared memory");
@@ -304,7 +303,6 @@ __global__ void __launch_bounds__(DT, 1) k_dense_layer(const DenseParams p) {
     const int r0 = p.slot0 + (blockIdx.x / DC) * DR;   // first slot of this cluster
     const int rend = p.slot0 + p.M;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int sub = lane & 3;
     const uint32_t bars = su32(sm + SM_BARS);
     auto bar = [&](int i) { return bars + 8 * i; };
     bool ok = true;
@@ -383,61 +381,42 @@ __global__ void __launch_bounds__(DT, 1) k_dense_layer(const DenseParams p) {
     const int r = warp;   // the row of this warp in the row-wise phases
 
     float att_d = 0.0f;
-    // ---- phase 0: merge the pages of head `rank` for row r. One round of loads brings every page's m and
-    // the first 16 pages' l and o; longer rows load 16 more pages per batch.
+    // ---- phase 0: merge the pages of head `rank` for row r; lane l holds dim l. One round of loads
+    // brings m, l and o[l] of up to 32 pages (rows longer than 2048 keys take one more round per 32
+    // pages); the pages are then merged in order from registers.
     {
         const int nch = meta[r * 3];
         const float* part = p.part + (((size_t)(r0 + r) * NH + rank) * p.max_chunks) * PART_STRIDE;
-        float* scr = (float*)(sm + SM_HROWS + warp * MERGE_ROW_BYTES);
-        auto stage_batch = [&](int c0) {
-            const int cnt = max(0, min(16, nch - c0));
-            if (lane < cnt) {
-                const float2 ml = __ldcg((const float2*)(part + (size_t)(c0 + lane) * PART_STRIDE));
-                scr[lane] = ml.x;   // m, replaced by the page weight once M is known
-                scr[16 + lane] = ml.y;
-            }
-            for (int i = lane; i < cnt * 8; i += 32) {
-                const int c = i >> 3, jj = i & 7;
-                *(float4*)(scr + 32 + c * 32 + jj * 4) =
-                    __ldcg((const float4*)(part + (size_t)(c0 + c) * PART_STRIDE + 4 + jj * 4));
-            }
+        float o[32];
+        float2 ml;
+        auto load_round = [&](int c0) {
+            const int cnt = min(32, nch - c0);
+            ml = lane < cnt ? __ldcg((const float2*)(part + (size_t)(c0 + lane) * PART_STRIDE))
+                            : make_float2(-INFINITY, 0.0f);
+#pragma unroll
+            for (int j = 0; j < 32; j++) o[j] = j < cnt ? __ldcg(part + (size_t)(c0 + j) * PART_STRIDE + 4 + lane) : 0.0f;
         };
-        stage_batch(0);
-        float M = -INFINITY;
-        for (int c = lane; c < nch; c += 32) M = fmaxf(M, __ldcg(part + (size_t)c * PART_STRIDE));
+        load_round(0);
+        float M = ml.x;
+        for (int c = 32 + lane; c < nch; c += 32) M = fmaxf(M, __ldcg(part + (size_t)c * PART_STRIDE));
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-        float L = 0.0f, O[8];
+        float L = 0.0f, O = 0.0f;
+        for (int c0 = 0; c0 < nch; c0 += 32) {
+            if (c0 > 0) load_round(c0);
+            const int cnt = min(32, nch - c0);
+            const float w = lane < cnt ? exp_canon(ml.x - M) : 0.0f;
 #pragma unroll
-        for (int e = 0; e < 8; e++) O[e] = 0.0f;
-        for (int c0 = 0; c0 < nch; c0 += 16) {
-            if (c0 > 0) stage_batch(c0);
-            __syncwarp();
-            const int cnt = min(16, nch - c0);
-            if (lane < cnt) scr[lane] = exp_canon(scr[lane] - M);
-            __syncwarp();
-            for (int c = 0; c < cnt; c++) {
-                const float w = scr[c];
-                L = fmaf(w, scr[16 + c], L);
-                const float4 a = *(const float4*)(scr + 32 + c * 32 + sub * 8);
-                const float4 b = *(const float4*)(scr + 32 + c * 32 + sub * 8 + 4);
-                O[0] = fmaf(w, a.x, O[0]); O[1] = fmaf(w, a.y, O[1]); O[2] = fmaf(w, a.z, O[2]);
-                O[3] = fmaf(w, a.w, O[3]); O[4] = fmaf(w, b.x, O[4]); O[5] = fmaf(w, b.y, O[5]);
-                O[6] = fmaf(w, b.z, O[6]); O[7] = fmaf(w, b.w, O[7]);
+            for (int j = 0; j < 32; j++) {
+                if (j < cnt) {
+                    const float wj = __shfl_sync(0xffffffffu, w, j), lj = __shfl_sync(0xffffffffu, ml.y, j);
+                    L = fmaf(wj, lj, L);
+                    O = fmaf(wj, o[j], O);
+                }
             }
-            __syncwarp();
         }
         if (nch) {
-            // lane (g, s) holds dims 8s..8s+7; column `lane` of the block comes from lane lane/8
-            float mine[8], v = 0.0f;
-#pragma unroll
-            for (int e = 0; e < 8; e++) mine[e] = __fdiv_rn(O[e], L);
-#pragma unroll
-            for (int e = 0; e < 8; e++) {
-                const float t = __shfl_sync(0xffffffffu, mine[e], lane >> 3);
-                if ((lane & 7) == e) v = t;
-            }
-            att_d = q8_block_stage(v, (int8_t*)(stg + STG_ATT));
+            att_d = q8_block_stage(__fdiv_rn(O, L), (int8_t*)(stg + STG_ATT));
         } else {
             ((int8_t*)(stg + STG_ATT))[lane] = 0;
         }
