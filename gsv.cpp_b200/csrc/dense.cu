@@ -1,7 +1,7 @@
 // dense.cu -- the decode step's per-layer tail fused on a 16-CTA thread-block cluster.
 //
 // After the decode-attention kernel has left one partial result per (slot, head, KV page), one
-// cluster of 16 CTAs carries 8 slots through the rest of the layer and the next layer's QKV
+// cluster of 16 CTAs carries 16 slots through the rest of the layer and the next layer's QKV
 // projection (the reference's per-layer graph, src/gsv_ar.cpp:402-467):
 //   0  merge of the attention pages, head j = cluster rank j        -> Q8_0 block j of each row
 //   1  out-projection, output columns [32j, 32j+32), + residual x + bias, LayerNorm row statistics
@@ -10,9 +10,10 @@
 //   4  FFN2, columns [32j, 32j+32), + residual n1 + bias, LayerNorm row statistics
 //   5  LayerNorm 2                                                   -> x (global) and its Q8_0 block j
 //   6  next layer's QKV: q, k, v columns of head j                   -> q (global), K/V page rows
-// Every CTA keeps full copies of the Q8_0 rows a GEMM reads; each CTA computes one 32-column block of
-// a row and pushes it into all 16 CTAs' shared memory (distributed shared memory), then the cluster
-// barrier publishes it. LayerNorm's double row sums are exchanged the same way.
+// Every CTA keeps full copies of the Q8_0 rows a GEMM reads, block-major; each CTA computes one
+// 32-column block of all 16 rows, stages it, and copies it into all 16 CTAs' shared memory
+// (distributed shared memory) with one bulk copy per CTA, counted on the receivers' mbarriers.
+// LayerNorm's double row sums go to every CTA as 16-byte remote stores counted the same way.
 //
 // Arithmetic is that of the unfused kernels (gemm_q8.cu, misc.cu, attention.cu), operation for
 // operation: each Q8_0 output is one warp's sequential float chain over the K blocks in order,
@@ -37,10 +38,12 @@ constexpr int DT = 512;      // threads per CTA: one warp per row in the row-wis
 constexpr int NW = DT / 32;  // warps
 constexpr int KB1 = D / QK;  // K blocks of a 512-wide input (16)
 constexpr int KB2 = FF / QK; // K blocks of a 2048-wide input (64)
-constexpr int RS1 = D + 16;  // padded stride of a 512-wide int8 row in shared memory
-constexpr int RS2 = FF + 16;
+// One exchanged Q8_0 block of all DR rows: quants [DR][32], then f32 scales [DR]. Within a row,
+// column c sits at byte qpos(c), which places the 8 quants lane (g, t) of mma.m16n8k32 reads as its
+// B fragment (columns 4t..4t+3 and 16+4t..16+4t+3) side by side.
+constexpr int BLK = DR * 32 + DR * 4;
 
-// shared-memory layout (bytes); activation rows are int8 [DR][RS] followed by f32 scales [DR][KB]
+// shared-memory layout (bytes); activation rows are block-major: [KB][BLK]
 constexpr int SM_W_OUT = 0;                        // out rows [32j, 32j+32): 2 row groups x 16 K blocks
 constexpr int SM_D_OUT = SM_W_OUT + 2 * KB1 * 512; // [32][16] fp16
 constexpr int SM_W_F1 = SM_D_OUT + 32 * KB1 * 2;   // ffn1 rows [128j, +128): 8 row groups
@@ -49,8 +52,8 @@ constexpr int SM_W_F2 = SM_D_F1 + 128 * KB1 * 2;   // ffn2 rows [32j, +32): 2 ro
 constexpr int SM_D_F2 = SM_W_F2 + 2 * KB2 * 512;   // [32][64]
 constexpr int SM_W_QKV = 0;                        // next layer's q|k|v rows of head j (reuses out + ffn1)
 constexpr int SM_D_QKV = SM_W_QKV + 6 * KB1 * 512; // [96][16]
-constexpr int ROWS1_BYTES = DR * RS1 + DR * KB1 * 4;
-constexpr int HROWS_BYTES = DR * RS2 + DR * KB2 * 4;
+constexpr int ROWS1_BYTES = KB1 * BLK;
+constexpr int HROWS_BYTES = KB2 * BLK;
 constexpr int SM_AROWS = SM_D_F2 + 32 * KB2 * 2;   // attention output rows (Q8_0), all 16 blocks
 constexpr int SM_N1ROWS = SM_AROWS + ROWS1_BYTES;  // n1 rows (Q8_0); later the x rows of the next QKV
 constexpr int SM_XROWS = SM_N1ROWS;
@@ -60,9 +63,9 @@ constexpr int SM_LNP2 = SM_LNP1 + DC * DR * 16;
 constexpr int SM_XOWN = SM_LNP2 + DC * DR * 16;    // [DR][32] f32: this CTA's columns of x (phases 0-1)
 constexpr int SM_N1OWN = SM_XOWN;                  // [DR][32] f32: this CTA's columns of n1 (phases 2-4)
 constexpr int SM_PRE = SM_N1OWN + DR * 32 * 4;     // [DR][32] f32: pre-LayerNorm sums
-constexpr int SM_STG = SM_PRE + DR * 32 * 4;       // per warp: one staging slot per exchange (never reused)
-constexpr int STG_ATT = 0, STG_N1 = 32, STG_X = 64, STG_H = 96, STG_HD = 224, STG_WARP = 240;
-constexpr int SM_PAR = SM_STG + NW * STG_WARP;     // this CTA's bias / LayerNorm parameters (f32)
+constexpr int SM_STG = SM_PRE + DR * 32 * 4;       // staged blocks, one region per exchange (never reused)
+constexpr int STG_ATT = 0, STG_N1 = BLK, STG_X = 2 * BLK, STG_H = 3 * BLK, STG_BYTES = 7 * BLK;
+constexpr int SM_PAR = SM_STG + STG_BYTES;         // this CTA's bias / LayerNorm parameters (f32)
 constexpr int P_BOUT = 0, P_BF1 = 32, P_BF2 = 160, P_N1W = 192, P_N1B = 224, P_N2W = 256, P_N2B = 288, P_BQKV = 320,
               P_COUNT = 416;
 constexpr int SM_ROWMETA = SM_PAR + P_COUNT * 4;   // per row: pages to merge (0: not decoding), KV page, KV pos
@@ -76,11 +79,10 @@ static_assert(SMEM_DENSE <= 232448, "shared memory");
 static_assert(SM_PAR % 16 == 0 && SM_XOWN % 16 == 0 && SM_ROWMETA % 4 == 0, "alignment of TMA destinations");
 static_assert(SM_AROWS % 16 == 0 && SM_N1ROWS % 16 == 0 && SM_HROWS % 16 == 0 && SM_D_F1 % 16 == 0 &&
                   SM_D_F2 % 16 == 0 && SM_D_QKV % 16 == 0 && SM_LNP1 % 16 == 0 && SM_LNP2 % 16 == 0 &&
-                  SM_STG % 16 == 0 && STG_WARP % 16 == 0 && SM_BARS % 8 == 0 && (DR * RS1) % 16 == 0 &&
-                  (DR * RS2) % 16 == 0,
+                  SM_STG % 16 == 0 && BLK % 16 == 0 && SM_BARS % 8 == 0,
               "alignment");
 // bytes each CTA receives per exchange (every CTA sends to all 16, itself included)
-constexpr uint32_t EX_BLOCK = DC * DR * (32 + 4);  // one Q8_0 block (32 B + f32 scale) per (sender, row)
+constexpr uint32_t EX_BLOCK = DC * BLK;            // one block of all rows per sender
 constexpr uint32_t EX_STATS = DC * DR * 16;        // one {sum, sum of squares} per (sender, row)
 enum { BW_OUT = 0, BW_F1, BW_F2, BW_QKV, BX_ATT, BX_LN1, BX_N1, BX_H, BX_LN2, BX_X, BW_PAR };
 
@@ -127,11 +129,6 @@ __device__ __forceinline__ void d_st_async16(uint32_t addr, uint4 v, uint32_t ba
                  "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(bar)
                  : "memory");
 }
-__device__ __forceinline__ void d_st_async4(uint32_t addr, uint32_t v, uint32_t bar) {
-    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(addr), "r"(v),
-                 "r"(bar)
-                 : "memory");
-}
 
 __device__ __forceinline__ void mma_s8(int (&c)[4], const uint4& a, uint32_t b0, uint32_t b1) {
     asm(
@@ -141,60 +138,73 @@ __device__ __forceinline__ void mma_s8(int (&c)[4], const uint4& a, uint32_t b0,
         : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
 }
 
+// fp16 scale j (0..7) of 8 consecutive ones loaded as a uint4
+__device__ __forceinline__ float h2f_pick(const uint4& s, int j) {
+    const uint32_t w = (j >> 1) == 0 ? s.x : (j >> 1) == 1 ? s.y : (j >> 1) == 2 ? s.z : s.w;
+    return h2f((uint16_t)((j & 1) ? (w >> 16) : (w & 0xffffu)));
+}
+
 // One warp: row group lr (16 features) of a weight slice in shared memory against row tile rt (rows
-// 8rt..8rt+7) of X, all KB blocks in order. Thread (g, t) ends with features 16lr+g, 16lr+g+8 x rows
-// 8rt+2t, 8rt+2t+1 in acc[0..3].
-template <int KB>
-__device__ __forceinline__ void rg_gemm(const uint8_t* W, const uint16_t* DW, int lr, const int8_t* X, int rs,
-                                        const float* DX, int rt, float (&acc)[4]) {
+// 8rt..8rt+7) of the block-major rows X, K blocks [kb0, kb0 + NK) in order, continuing acc. Thread
+// (g, t) holds features 16lr+g, 16lr+g+8 x rows 8rt+2t, 8rt+2t+1 in acc[0..3].
+template <int KB, int NK>
+__device__ __forceinline__ void rg_chain(const uint8_t* W, const uint16_t* DW, int lr, const uint8_t* X, int rt,
+                                         int kb0, float (&acc)[4]) {
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int fa = lr * 16 + g, fb = fa + 8, ra = rt * 8 + 2 * t, rb = ra + 1;
-    acc[0] = acc[1] = acc[2] = acc[3] = 0.0f;
+    const int fa = lr * 16 + g, fb = fa + 8;
     const uint4* wp = (const uint4*)W + (size_t)lr * KB * 32 + lane;
-    const int8_t* xr = X + (rt * 8 + g) * rs + t * 4;
+    const uint8_t* xq = X + (rt * 8 + g) * 32 + t * 8;        // B fragment of block kb at xq + kb * BLK
+    const uint8_t* xd = X + DR * 32 + (rt * 8 + 2 * t) * 4;   // scales of rows 8rt+2t, +1 at xd + kb * BLK
     constexpr int KC = 8;   // K blocks whose MMAs are issued back to back before their chain steps
+    static_assert(NK % KC == 0, "K blocks in batches of 8");
 #pragma unroll 1
-    for (int k0 = 0; k0 < KB; k0 += KC) {
+    for (int k0 = kb0; k0 < kb0 + NK; k0 += KC) {
         int c[KC][4];
 #pragma unroll
         for (int j = 0; j < KC; j++) {
             const int kb = k0 + j;
-            const uint4 a = wp[kb * 32];
-            const uint32_t b0 = *(const uint32_t*)(xr + kb * 32), b1 = *(const uint32_t*)(xr + kb * 32 + 16);
-            mma_s8(c[j], a, b0, b1);
+            const uint2 bq = *(const uint2*)(xq + kb * BLK);
+            mma_s8(c[j], wp[kb * 32], bq.x, bq.y);
         }
+        const uint4 sa = *(const uint4*)(DW + fa * KB + k0), sb = *(const uint4*)(DW + fb * KB + k0);
 #pragma unroll
         for (int j = 0; j < KC; j++) {
-            const int kb = k0 + j;
-            const float dwa = h2f(DW[fa * KB + kb]), dwb = h2f(DW[fb * KB + kb]);
-            const float dxa = DX[ra * KB + kb], dxb = DX[rb * KB + kb];
-            acc[0] = fmaf((float)c[j][0], __fmul_rn(dwa, dxa), acc[0]);
-            acc[1] = fmaf((float)c[j][1], __fmul_rn(dwa, dxb), acc[1]);
-            acc[2] = fmaf((float)c[j][2], __fmul_rn(dwb, dxa), acc[2]);
-            acc[3] = fmaf((float)c[j][3], __fmul_rn(dwb, dxb), acc[3]);
+            const float dwa = h2f_pick(sa, j), dwb = h2f_pick(sb, j);
+            const float2 dx = *(const float2*)(xd + (k0 + j) * BLK);
+            acc[0] = fmaf((float)c[j][0], __fmul_rn(dwa, dx.x), acc[0]);
+            acc[1] = fmaf((float)c[j][1], __fmul_rn(dwa, dx.y), acc[1]);
+            acc[2] = fmaf((float)c[j][2], __fmul_rn(dwb, dx.x), acc[2]);
+            acc[3] = fmaf((float)c[j][3], __fmul_rn(dwb, dx.y), acc[3]);
         }
     }
+}
+template <int KB>
+__device__ __forceinline__ void rg_gemm(const uint8_t* W, const uint16_t* DW, int lr, const uint8_t* X, int rt,
+                                        float (&acc)[4]) {
+    acc[0] = acc[1] = acc[2] = acc[3] = 0.0f;
+    rg_chain<KB, KB>(W, DW, lr, X, rt, 0, acc);
 }
 
 // FFN2-shaped row group (KB2 = 64 blocks) split over 4 warps by K quarter q: each warp issues its 16
 // MMAs at once, then the warps continue one float chain in block order, handing the running sums
 // over through shared memory `hand` ([4 lanes x ... ]) with named barriers bar_base + q.
-__device__ __forceinline__ void rg_gemm_ksplit4(const uint8_t* W, const uint16_t* DW, int lr, const int8_t* X, int rs,
-                                                const float* DX, int rt, int q, float* hand, int bar_base,
-                                                float (&acc)[4]) {
+__device__ __forceinline__ void rg_gemm_ksplit4(const uint8_t* W, const uint16_t* DW, int lr, const uint8_t* X,
+                                                int rt, int q, float* hand, int bar_base, float (&acc)[4]) {
     constexpr int KB = KB2, KQ = KB2 / 4;
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int fa = lr * 16 + g, fb = fa + 8, ra = rt * 8 + 2 * t, rb = ra + 1;
+    const int fa = lr * 16 + g, fb = fa + 8;
     const uint4* wp = (const uint4*)W + (size_t)lr * KB * 32 + lane;
-    const int8_t* xr = X + (rt * 8 + g) * rs + t * 4;
+    const uint8_t* xq = X + (rt * 8 + g) * 32 + t * 8;
+    const uint8_t* xd = X + DR * 32 + (rt * 8 + 2 * t) * 4;
     int c[KQ][4];
 #pragma unroll
     for (int j = 0; j < KQ; j++) {
         const int kb = q * KQ + j;
-        const uint4 a = wp[kb * 32];
-        const uint32_t b0 = *(const uint32_t*)(xr + kb * 32), b1 = *(const uint32_t*)(xr + kb * 32 + 16);
-        mma_s8(c[j], a, b0, b1);
+        const uint2 bq = *(const uint2*)(xq + kb * BLK);
+        mma_s8(c[j], wp[kb * 32], bq.x, bq.y);
     }
+    const uint4 sa0 = *(const uint4*)(DW + fa * KB + q * KQ), sa1 = *(const uint4*)(DW + fa * KB + q * KQ + 8);
+    const uint4 sb0 = *(const uint4*)(DW + fb * KB + q * KQ), sb1 = *(const uint4*)(DW + fb * KB + q * KQ + 8);
     if (q > 0) {   // the previous quarter's warp has stored the running sums
         asm volatile("bar.sync %0, 64;" ::"r"(bar_base + q) : "memory");
         const float4 v = *(const float4*)(hand + lane * 4);
@@ -204,13 +214,12 @@ __device__ __forceinline__ void rg_gemm_ksplit4(const uint8_t* W, const uint16_t
     }
 #pragma unroll
     for (int j = 0; j < KQ; j++) {
-        const int kb = q * KQ + j;
-        const float dwa = h2f(DW[fa * KB + kb]), dwb = h2f(DW[fb * KB + kb]);
-        const float dxa = DX[ra * KB + kb], dxb = DX[rb * KB + kb];
-        acc[0] = fmaf((float)c[j][0], __fmul_rn(dwa, dxa), acc[0]);
-        acc[1] = fmaf((float)c[j][1], __fmul_rn(dwa, dxb), acc[1]);
-        acc[2] = fmaf((float)c[j][2], __fmul_rn(dwb, dxa), acc[2]);
-        acc[3] = fmaf((float)c[j][3], __fmul_rn(dwb, dxb), acc[3]);
+        const float dwa = h2f_pick(j < 8 ? sa0 : sa1, j & 7), dwb = h2f_pick(j < 8 ? sb0 : sb1, j & 7);
+        const float2 dx = *(const float2*)(xd + (q * KQ + j) * BLK);
+        acc[0] = fmaf((float)c[j][0], __fmul_rn(dwa, dx.x), acc[0]);
+        acc[1] = fmaf((float)c[j][1], __fmul_rn(dwa, dx.y), acc[1]);
+        acc[2] = fmaf((float)c[j][2], __fmul_rn(dwb, dx.x), acc[2]);
+        acc[3] = fmaf((float)c[j][3], __fmul_rn(dwb, dx.y), acc[3]);
     }
     if (q < 3) {
         if (q > 0) __syncwarp();   // this warp's read of `hand` is done before it is overwritten
@@ -219,17 +228,20 @@ __device__ __forceinline__ void rg_gemm_ksplit4(const uint8_t* W, const uint16_t
     }
 }
 
-// Quantize the 32 values v (lane l holds column l of the block) into q (32 B of shared memory); returns
-// the block's scale, rounded through fp16 (what a reader of the fp16 scale sees), in every lane.
-__device__ __forceinline__ float q8_block_stage(float v, int8_t* q) {
+// Byte of column c within a row's 32 quants of an exchanged block.
+__device__ __forceinline__ int qpos(int c) { return ((c & 15) >> 2) * 8 + ((c >> 4) << 2) + (c & 3); }
+
+// Quantize the 32 values v (lane l holds column l) as row r of the staged block `blk`; the scale is
+// stored rounded through fp16 (what a reader of the fp16 scale sees).
+__device__ __forceinline__ void stage_row_block(float v, uint8_t* blk, int r) {
     const int lane = threadIdx.x & 31;
     float amax = fabsf(v);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
     float dsc, id;
     q8_scale(amax, dsc, id);
-    q[lane] = q8_val(v, id);
-    return h2f(f2h(dsc));
+    blk[r * 32 + qpos(lane)] = (uint8_t)q8_val(v, id);
+    if (lane == 0) *(float*)(blk + DR * 32 + r * 4) = h2f(f2h(dsc));
 }
 
 __device__ __forceinline__ void d_bulk_s2c(uint32_t dst_cluster, uint32_t src, uint32_t bytes, uint32_t bar_cluster) {
@@ -239,27 +251,13 @@ __device__ __forceinline__ void d_bulk_s2c(uint32_t dst_cluster, uint32_t src, u
                  : "memory");
 }
 
-// Send one staged Q8_0 block (32 B at sq) with scale d as block b of row r of the rows region `rows`
-// (int8 stride rs, f32 scales [DR][kb] after the rows) of every CTA; bytes counted on `bar`. One warp:
-// lanes 0..15 copy the quants to CTA lane, lanes 16..31 store the scale to CTA lane - 16.
-__device__ __forceinline__ void send_block(const int8_t* sq, float d, int r, uint32_t rows, int rs, int kb, int b,
-                                           uint32_t bar) {
-    const int lane = threadIdx.x & 31, dst = lane & 15;
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // staged quants -> async proxy
-    __syncwarp();
-    const uint32_t rrows = d_mapa(rows, dst), rbar = d_mapa(bar, dst);
-    if (lane < 16) d_bulk_s2c(rrows + r * rs + b * 32, su32(sq), 32, rbar);
-    else d_st_async4(rrows + DR * rs + (r * kb + b) * 4, __float_as_uint(d), rbar);
-}
-// Send 4 consecutive staged blocks (128 B at sq) with their 4 scales (16 B at sd) as blocks b0..b0+3.
-__device__ __forceinline__ void send_blocks4(const int8_t* sq, const float* sd, int r, uint32_t rows, int rs, int kb,
-                                             int b0, uint32_t bar) {
-    const int lane = threadIdx.x & 31, dst = lane & 15;
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    __syncwarp();
-    const uint32_t rrows = d_mapa(rows, dst), rbar = d_mapa(bar, dst);
-    if (lane < 16) d_bulk_s2c(rrows + r * rs + b0 * 32, su32(sq), 128, rbar);
-    else d_bulk_s2c(rrows + DR * rs + (r * kb + b0) * 4, su32(sd), 16, rbar);
+// Every thread of the CTA, after staging: copy the staged bytes into bytes [off, off + bytes) of the
+// rows region `rows` of every CTA of the cluster, counted on their `bar`; one bulk copy per CTA.
+__device__ __forceinline__ void send_staged(const uint8_t* stg, uint32_t rows, uint32_t off, uint32_t bytes,
+                                            uint32_t bar) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // staged bytes -> async proxy
+    __syncthreads();
+    if (threadIdx.x < DC) d_bulk_s2c(d_mapa(rows + off, threadIdx.x), su32(stg), bytes, d_mapa(bar, threadIdx.x));
 }
 
 // LayerNorm row statistics of row r (lane = column, 32 values) in double, sent as slot [rank][r] of
@@ -375,12 +373,11 @@ __global__ void __launch_bounds__(DT, 1) k_dense_layer(const DenseParams p) {
     griddep_launch();
     __syncthreads();
 
-    uint8_t* stg = sm + SM_STG + warp * STG_WARP;
+    uint8_t* stg = sm + SM_STG;
     float* n1own = (float*)(sm + SM_N1OWN);
     float* pre = (float*)(sm + SM_PRE);
     const int r = warp;   // the row of this warp in the row-wise phases
 
-    float att_d = 0.0f;
     // ---- phase 0: merge the pages of head `rank` for row r; lane l holds dim l. One round of loads
     // brings m, l and o[l] of up to 32 pages (rows longer than 2048 keys take one more round per 32
     // pages); the pages are then merged in order from registers.
@@ -416,14 +413,15 @@ __global__ void __launch_bounds__(DT, 1) k_dense_layer(const DenseParams p) {
             }
         }
         if (nch) {
-            att_d = q8_block_stage(__fdiv_rn(O, L), (int8_t*)(stg + STG_ATT));
-        } else {
-            ((int8_t*)(stg + STG_ATT))[lane] = 0;
+            stage_row_block(__fdiv_rn(O, L), stg + STG_ATT, r);
+        } else {   // not decoding: zero quants, scale 0
+            stg[STG_ATT + r * 32 + lane] = 0;
+            if (lane == 0) *(float*)(stg + STG_ATT + DR * 32 + r * 4) = 0.0f;
         }
     }
     ok &= d_wait(bar(BW_PAR));   // parameters and x columns
     asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");   // every peer's barriers are armed
-    send_block((const int8_t*)(stg + STG_ATT), att_d, r, su32(sm + SM_AROWS), RS1, KB1, rank, bar(BX_ATT));
+    send_staged(stg + STG_ATT, su32(sm + SM_AROWS), rank * BLK, BLK, bar(BX_ATT));
 
     // ---- phase 1: out-projection + residual + bias (columns 32*rank + 0..31); an idle warp looks up
     // the KV page of this step's key for phase 6
@@ -436,8 +434,7 @@ __global__ void __launch_bounds__(DT, 1) k_dense_layer(const DenseParams p) {
         ok &= d_wait(bar(BW_OUT));
         float acc[4];
         const int lr = warp & 1, rt = warp >> 1;
-        rg_gemm<KB1>(sm + SM_W_OUT, (const uint16_t*)(sm + SM_D_OUT), lr, (const int8_t*)(sm + SM_AROWS), RS1,
-                     (const float*)(sm + SM_AROWS + DR * RS1), rt, acc);
+        rg_gemm<KB1>(sm + SM_W_OUT, (const uint16_t*)(sm + SM_D_OUT), lr, sm + SM_AROWS, rt, acc);
         const int g = lane >> 2, t = lane & 3;
 #pragma unroll
         for (int i = 0; i < 4; i++) {
@@ -454,9 +451,9 @@ __global__ void __launch_bounds__(DT, 1) k_dense_layer(const DenseParams p) {
         const float n1 = ln_apply((const double*)(sm + SM_LNP1), r, pre[r * 32 + lane], par[P_N1W + lane],
                                   par[P_N1B + lane]);
         n1own[r * 32 + lane] = n1;
-        const float d = q8_block_stage(n1, (int8_t*)(stg + STG_N1));
-        send_block((const int8_t*)(stg + STG_N1), d, r, su32(sm + SM_N1ROWS), RS1, KB1, rank, bar(BX_N1));
+        stage_row_block(n1, stg + STG_N1, r);
     }
+    send_staged(stg + STG_N1, su32(sm + SM_N1ROWS), rank * BLK, BLK, bar(BX_N1));
 
     // ---- phase 3: FFN1 (columns 128*rank + 0..127), bias + ReLU: warp = (row group, row tile)
     float* hown = (float*)(sm + SM_AROWS);   // [DR][128] f32 (the attention rows are consumed)
@@ -465,8 +462,7 @@ __global__ void __launch_bounds__(DT, 1) k_dense_layer(const DenseParams p) {
     {
         const int lr = warp & 7, rt = warp >> 3;
         float acc[4];
-        rg_gemm<KB1>(sm + SM_W_F1, (const uint16_t*)(sm + SM_D_F1), lr, (const int8_t*)(sm + SM_N1ROWS), RS1,
-                     (const float*)(sm + SM_N1ROWS + DR * RS1), rt, acc);
+        rg_gemm<KB1>(sm + SM_W_F1, (const uint16_t*)(sm + SM_D_F1), lr, sm + SM_N1ROWS, rt, acc);
         const int g = lane >> 2, t = lane & 3;
 #pragma unroll
         for (int i = 0; i < 4; i++) {
@@ -487,7 +483,6 @@ __global__ void __launch_bounds__(DT, 1) k_dense_layer(const DenseParams p) {
         }
     }
     {   // the row's 4 Q8_0 blocks at once: lane (b, c) quantizes columns 4c..4c+3 of block b = lane / 8
-        float* hd = (float*)(stg + STG_HD);
         const int b = lane >> 3, c = lane & 7;
         const float4 v = *(const float4*)(hown + r * 128 + b * 32 + c * 4);
         float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
@@ -497,10 +492,11 @@ __global__ void __launch_bounds__(DT, 1) k_dense_layer(const DenseParams p) {
         q8_scale(amax, dsc, id);
         const uint32_t qw = (uint32_t)(uint8_t)q8_val(v.x, id) | (uint32_t)(uint8_t)q8_val(v.y, id) << 8 |
                             (uint32_t)(uint8_t)q8_val(v.z, id) << 16 | (uint32_t)(uint8_t)q8_val(v.w, id) << 24;
-        *(uint32_t*)(stg + STG_H + b * 32 + c * 4) = qw;
-        if (c == 0) hd[b] = h2f(f2h(dsc));
-        send_blocks4((const int8_t*)(stg + STG_H), hd, r, su32(sm + SM_HROWS), RS2, KB2, 4 * rank, bar(BX_H));
+        uint8_t* blk = stg + STG_H + b * BLK;
+        *(uint32_t*)(blk + r * 32 + qpos(4 * c)) = qw;   // columns 4c..4c+3 are adjacent under qpos
+        if (c == 0) *(float*)(blk + DR * 32 + r * 4) = h2f(f2h(dsc));
     }
+    send_staged(stg + STG_H, su32(sm + SM_HROWS), 4 * rank * BLK, 4 * BLK, bar(BX_H));
 
     // ---- phase 4: FFN2 + residual n1 + bias (columns 32*rank + 0..31): task = (row group, row tile) on
     // warps 4 task .. 4 task + 3, one K quarter each, chained in block order
@@ -510,8 +506,8 @@ __global__ void __launch_bounds__(DT, 1) k_dense_layer(const DenseParams p) {
         const int task = warp >> 2, q = warp & 3, lr = task & 1, rt = task >> 1;
         float* hand = (float*)(sm + SM_LNP1) + task * 128;   // LN1 sums are consumed by now
         float acc[4];
-        rg_gemm_ksplit4(sm + SM_W_F2, (const uint16_t*)(sm + SM_D_F2), lr, (const int8_t*)(sm + SM_HROWS), RS2,
-                        (const float*)(sm + SM_HROWS + DR * RS2), rt, q, hand, 1 + task * 3, acc);
+        rg_gemm_ksplit4(sm + SM_W_F2, (const uint16_t*)(sm + SM_D_F2), lr, sm + SM_HROWS, rt, q, hand, 1 + task * 3,
+                        acc);
         if (q == 3) {
             const int g = lane >> 2, t = lane & 3;
 #pragma unroll
@@ -530,11 +526,9 @@ __global__ void __launch_bounds__(DT, 1) k_dense_layer(const DenseParams p) {
         const float xv = ln_apply((const double*)(sm + SM_LNP2), r, pre[r * 32 + lane], par[P_N2W + lane],
                                   par[P_N2B + lane]);
         if (r0 + r < rend) p.x[(size_t)(r0 + r) * D + 32 * rank + lane] = xv;
-        if (HAS_QKV) {
-            const float d = q8_block_stage(xv, (int8_t*)(stg + STG_X));
-            send_block((const int8_t*)(stg + STG_X), d, r, su32(sm + SM_XROWS), RS1, KB1, rank, bar(BX_X));
-        }
+        if (HAS_QKV) stage_row_block(xv, stg + STG_X, r);
     }
+    if (HAS_QKV) send_staged(stg + STG_X, su32(sm + SM_XROWS), rank * BLK, BLK, bar(BX_X));
 
     // ---- phase 6: next layer's q, k, v of head `rank` (+ bias); K/V into the pages. warp = (row group, tile)
     if (HAS_QKV && warp < 12) {
@@ -542,8 +536,7 @@ __global__ void __launch_bounds__(DT, 1) k_dense_layer(const DenseParams p) {
         ok &= d_wait(bar(BW_QKV));
         const int lr = warp % 6, rt = warp / 6, part = lr >> 1, g = lane >> 2, t = lane & 3;
         float acc[4];
-        rg_gemm<KB1>(sm + SM_W_QKV, (const uint16_t*)(sm + SM_D_QKV), lr, (const int8_t*)(sm + SM_XROWS), RS1,
-                     (const float*)(sm + SM_XROWS + DR * RS1), rt, acc);
+        rg_gemm<KB1>(sm + SM_W_QKV, (const uint16_t*)(sm + SM_D_QKV), lr, sm + SM_XROWS, rt, acc);
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             const int f = (lr & 1) * 16 + g + (i >= 2 ? 8 : 0), rr = rt * 8 + 2 * t + (i & 1), slot = r0 + rr;
