@@ -279,10 +279,11 @@ __global__ void __launch_bounds__(128) k_decode_attn(const DecAttnParams p) {
         return;
     }
     if (g == 0) {
-        float* part = p.part + (((size_t)slot * NH + h) * p.max_chunks + chunk) * PART_STRIDE;
-        __stcg((float4*)(part + 4 + sub * 8), make_float4(o[0], o[1], o[2], o[3]));
-        __stcg((float4*)(part + 8 + sub * 8), make_float4(o[4], o[5], o[6], o[7]));
-        if (sub == 0) __stcg((float2*)part, make_float2(m, l));
+        const size_t item = ((size_t)slot * NH + h) * p.max_chunks + chunk;
+        float* po = p.part + item * HD + sub * 8;
+        __stcg((float4*)po, make_float4(o[0], o[1], o[2], o[3]));
+        __stcg((float4*)(po + 4), make_float4(o[4], o[5], o[6], o[7]));
+        if (sub == 0) __stcg((float2*)p.part_ml + item, make_float2(m, l));
     }
 }
 
@@ -302,9 +303,11 @@ __global__ void __launch_bounds__(128) k_decode_merge(const DecAttnParams p) {
     const int nch = (kvpos + PAGE) / PAGE;
     if (nch <= 1) return;
     const int sub = lane & 3, g = lane >> 2;
-    const float* part = p.part + (((size_t)slot * NH + h) * p.max_chunks) * PART_STRIDE;
+    const size_t item0 = ((size_t)slot * NH + h) * p.max_chunks;
+    const float* po = p.part + item0 * HD;
+    const float2* pml = (const float2*)p.part_ml + item0;
     float M = -INFINITY;
-    for (int c = lane; c < nch; c += 32) M = fmaxf(M, __ldcg(part + (size_t)c * PART_STRIDE));
+    for (int c = lane; c < nch; c += 32) M = fmaxf(M, __ldcg((const float*)(pml + c)));
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
     float* sw = sbuf[warp];          // [32] page weights
@@ -316,13 +319,13 @@ __global__ void __launch_bounds__(128) k_decode_merge(const DecAttnParams p) {
     for (int c0 = 0; c0 < nch; c0 += 32) {
         const int cnt = min(32, nch - c0);
         if (lane < cnt) {
-            const float2 ml = __ldcg((const float2*)(part + (size_t)(c0 + lane) * PART_STRIDE));
+            const float2 ml = __ldcg(pml + c0 + lane);
             sw[lane] = exp_canon(ml.x - M);
             sl[lane] = ml.y;
         }
         for (int i = lane; i < cnt * 8; i += 32) {
             const int c = i >> 3, j = i & 7;
-            *(float4*)(so + c * 32 + j * 4) = __ldcg((const float4*)(part + (size_t)(c0 + c) * PART_STRIDE + 4 + j * 4));
+            *(float4*)(so + c * 32 + j * 4) = __ldcg((const float4*)(po + (size_t)(c0 + c) * HD + j * 4));
         }
         __syncwarp();
         for (int c = 0; c < cnt; c++) {

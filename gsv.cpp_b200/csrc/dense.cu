@@ -304,6 +304,13 @@ __global__ void __launch_bounds__(DT, 1) k_dense_layer(const DenseParams p) {
     const uint32_t bars = su32(sm + SM_BARS);
     auto bar = [&](int i) { return bars + 8 * i; };
     bool ok = true;
+    // slot state of row tid (written two or more kernels ago): both fields in one round trip, issued
+    // first so the latency overlaps the set-up below
+    int st_now = 0, st_pos = 0;
+    if (tid < DR && r0 + tid < rend) {
+        st_now = p.st[r0 + tid].decode_now;
+        st_pos = p.st[r0 + tid].kvpos;
+    }
 
     if (tid == 0) {
         for (int i = 0; i < 11; i++) d_mbar_init(bar(i));
@@ -317,8 +324,9 @@ __global__ void __launch_bounds__(DT, 1) k_dense_layer(const DenseParams p) {
         if (HAS_QKV) d_expect_tx(bar(BX_X), EX_BLOCK);
     }
     __syncthreads();   // the barriers are initialised for every warp of the CTA
-    // announce this CTA's armed barriers now; wait for the peers' only before the first send
-    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    // announce this CTA's armed barriers now (fence.mbarrier_init above publishes the initialisation);
+    // wait for the peers' only before the first send
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
     if (warp == 0) {   // weights of this CTA's slices (constant), before the wait for the attention kernel
         if (lane == 0) {
             d_expect_tx(bar(BW_OUT), 2 * KB1 * 512 + 32 * KB1 * 2);
@@ -333,8 +341,8 @@ __global__ void __launch_bounds__(DT, 1) k_dense_layer(const DenseParams p) {
         if (lane == 4) d_bulk(su32(sm + SM_W_F2), p.w_f2 + (size_t)(2 * rank) * KB2 * 32, 2 * KB2 * 512, bar(BW_F2));
         if (lane == 5) d_bulk(su32(sm + SM_D_F2), p.d_f2 + (size_t)(32 * rank) * KB2, 32 * KB2 * 2, bar(BW_F2));
     }
-    // slot state, x and this CTA's parameters were written two or more kernels ago (or by the host):
-    // parameters and x columns are copied in by TMA, the slot state read, while the attention finishes
+    // x and this CTA's parameters were written two or more kernels ago (or by the host): copied in by
+    // TMA while the attention finishes
     float* par = (float*)(sm + SM_PAR);
     int* meta = (int*)(sm + SM_ROWMETA);
     float* xown = (float*)(sm + SM_XOWN);
@@ -360,14 +368,8 @@ __global__ void __launch_bounds__(DT, 1) k_dense_layer(const DenseParams p) {
         }
     }
     if (tid < DR) {
-        const int slot = r0 + tid;
-        int nch = 0, pos = 0;
-        if (slot < rend && p.st[slot].decode_now) {
-            pos = p.st[slot].kvpos;
-            nch = pos / PAGE + 1;
-        }
-        meta[tid * 3] = nch;
-        meta[tid * 3 + 2] = pos;
+        meta[tid * 3] = st_now ? st_pos / PAGE + 1 : 0;
+        meta[tid * 3 + 2] = st_now ? st_pos : 0;
     }
     griddep_wait();
     griddep_launch();
@@ -383,19 +385,20 @@ __global__ void __launch_bounds__(DT, 1) k_dense_layer(const DenseParams p) {
     // pages); the pages are then merged in order from registers.
     {
         const int nch = meta[r * 3];
-        const float* part = p.part + (((size_t)(r0 + r) * NH + rank) * p.max_chunks) * PART_STRIDE;
+        const size_t item0 = ((size_t)(r0 + r) * NH + rank) * p.max_chunks;
+        const float* po = p.part + item0 * HD;
+        const float2* pml = (const float2*)p.part_ml + item0;
         float o[32];
         float2 ml;
         auto load_round = [&](int c0) {
             const int cnt = min(32, nch - c0);
-            ml = lane < cnt ? __ldcg((const float2*)(part + (size_t)(c0 + lane) * PART_STRIDE))
-                            : make_float2(-INFINITY, 0.0f);
+            ml = lane < cnt ? __ldcg(pml + c0 + lane) : make_float2(-INFINITY, 0.0f);
 #pragma unroll
-            for (int j = 0; j < 32; j++) o[j] = j < cnt ? __ldcg(part + (size_t)(c0 + j) * PART_STRIDE + 4 + lane) : 0.0f;
+            for (int j = 0; j < 32; j++) o[j] = j < cnt ? __ldcg(po + (size_t)(c0 + j) * HD + lane) : 0.0f;
         };
         load_round(0);
         float M = ml.x;
-        for (int c = 32 + lane; c < nch; c += 32) M = fmaxf(M, __ldcg(part + (size_t)c * PART_STRIDE));
+        for (int c = 32 + lane; c < nch; c += 32) M = fmaxf(M, __ldcg((const float*)(pml + c)));
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
         float L = 0.0f, O = 0.0f;

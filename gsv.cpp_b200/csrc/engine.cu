@@ -793,12 +793,14 @@ int gsvcu_ctx::launch_step(cudaStream_t s, float* dump, int dump_row, const int*
                 a.q = qkv; a.q_stride = 3 * D; a.pool = pool; a.kv_f32 = kv_f32; a.n_layer = NL; a.layer = li;
                 a.block_table = block_table; a.max_pages = max_pages; a.st = st; a.slot0 = s0; a.B = rows;
                 a.max_chunks = max_chunks; a.scale = scale; a.out_q = aq; a.out_d = ad; a.part = part;
+                a.part_ml = part_ml_of(part, (size_t)max_slots * NH * max_chunks);
                 a.partials_only = 1; a.err = att_err;
                 a.work = work; a.work_base = work_base; a.group = s0 ? 1 : 0;
                 nk += launch_decode_attention(a, cs);
                 TRY(mark(GSVCU_PROF_DECODE_ATTN));
                 DenseParams d;
                 d.slot0 = s0; d.M = rows; d.st = st; d.part = part; d.max_chunks = max_chunks;
+                d.part_ml = part_ml_of(part, (size_t)max_slots * NH * max_chunks);
                 d.w_out = w.wq[1]; d.d_out = w.wd[1]; d.b_out = w.b_out; d.n1w = w.n1w; d.n1b = w.n1b;
                 d.w_f1 = w.wq[2]; d.d_f1 = w.wd[2]; d.b_f1 = w.b_f1; d.w_f2 = w.wq[3]; d.d_f2 = w.wd[3];
                 d.b_f2 = w.b_f2; d.n2w = w.n2w; d.n2b = w.n2b; d.x = x; d.err = att_err;
@@ -850,7 +852,7 @@ int gsvcu_ctx::launch_step(cudaStream_t s, float* dump, int dump_row, const int*
         a.q = qkv; a.q_stride = 3 * D; a.pool = pool; a.kv_f32 = kv_f32; a.n_layer = NL; a.layer = li;
         a.block_table = block_table; a.max_pages = max_pages; a.st = st; a.B = M; a.max_chunks = max_chunks;
         a.scale = scale; a.out_q = aq; a.out_d = ad; a.out_f32 = dump ? attn_f32 : nullptr;
-        a.part = part; a.err = att_err;
+        a.part = part; a.part_ml = part_ml_of(part, (size_t)max_slots * NH * max_chunks); a.err = att_err;
         nk += launch_decode_attention(a, s);
         TRY(mark(3));
         GemmQ8Params o;
@@ -1338,6 +1340,7 @@ int gsvcu_op_decode_attention(gsvcu_ctx* ctx, const float* q_dev, int32_t q_stri
     a.block_table = block_table_dev; a.max_pages = max_pages; a.kvpos = kvpos_dev; a.active = active_dev; a.B = B;
     a.max_chunks = max_chunks; a.scale = 1.0f / std::sqrt((float)HD); a.out_q = out_q_dev; a.out_d = out_d_dev;
     a.out_f32 = out_f32_dev; a.part = ctx->op_part; a.err = ctx->att_err;
+    a.part_ml = part_ml_of(ctx->op_part, (size_t)B * NH * max_chunks);
     launch_decode_attention(a, ctx->stream);
     CKC(ctx, cudaGetLastError());
     return GSVCU_OK;

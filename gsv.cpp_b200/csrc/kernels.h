@@ -101,7 +101,8 @@ struct DecAttnParams {
     int8_t* out_q = nullptr;
     uint16_t* out_d = nullptr;
     float* out_f32 = nullptr;
-    float* part = nullptr;               // scratch [B][NH][max_chunks][PART_STRIDE]: m, l, -, -, o[HD]
+    float* part = nullptr;               // scratch: page outputs o [items][HD], see part_ml_of
+    float* part_ml = nullptr;            // scratch: page {max, sum} [items] f32x2
     int partials_only = 0;               // 1: every page leaves its partial (the fused layer tail merges)
     int slot0 = 0;                       // first slot of this launch: slots slot0 .. slot0 + B - 1
     // compacted work list of the decode step (k_page_list): item i = {slot, chunk | kvpos << 8, physical
@@ -111,10 +112,12 @@ struct DecAttnParams {
     int group = 0;
     int32_t* err = nullptr;              // set to 1 if a bounded wait gave up (may be null)
 };
-// Split-KV work items of decode attention: one per 64-key page. A page's partial result is
-// {m, l, pad, pad, o[32]} floats (o 16-byte aligned).
+// Split-KV work items of decode attention: one per 64-key page. Page partials of item
+// (slot * NH + head) * max_chunks + page: o, HD floats (a 128-byte row), in one array, and {m, l} in a
+// second one that follows it; PART_STRIDE floats per item are allocated for both.
 inline int decode_chunks(int max_tokens) { return (max_tokens + PAGE - 1) / PAGE; }
 constexpr int PART_STRIDE = 4 + HD;
+inline float* part_ml_of(float* part, size_t items) { return part + items * HD; }
 // Alignment the decode-attention kernel relies on: 16-byte q rows (float4 loads), pool (TMA bulk
 // copies) and f32 output (float4 stores), 8-byte Q8_0 output rows (8-byte stores).
 inline bool decode_attention_aligned(const float* q, int q_stride, const void* pool, const int8_t* out_q,
@@ -140,6 +143,7 @@ struct DenseParams {
     int M = 0;                          // slots (rows) of this launch: slot0 .. slot0 + M - 1
     const SlotState* st = nullptr;
     const float* part = nullptr;        // attention partials of this layer (partials_only launch)
+    const float* part_ml = nullptr;
     int max_chunks = 0;
     const uint4* w_out = nullptr; const uint16_t* d_out = nullptr; const float* b_out = nullptr;
     const float* n1w = nullptr; const float* n1b = nullptr;

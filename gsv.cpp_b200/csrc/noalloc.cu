@@ -17,7 +17,7 @@ namespace gsvcu {
 namespace {
 
 constexpr int kItems = GSVCU_NOALLOC_MAX_ITEMS;                       // (sequence, KV page) pairs
-constexpr size_t kPartFloats = (size_t)kItems * NH * PART_STRIDE;    // partials: m, l, o[32] per head
+constexpr size_t kPartFloats = (size_t)kItems * NH * PART_STRIDE;    // partials: o[32], {m, l} per head
 
 // Scratch shared by every call on a device.
 struct NoallocScratch {
@@ -88,6 +88,7 @@ extern "C" int gsvcu_op_decode_attention_noalloc(void* stream, const float* q_de
     a.block_table = block_table_dev; a.max_pages = max_pages; a.kvpos = kvpos_dev; a.active = active_dev; a.B = B;
     a.max_chunks = max_chunks; a.scale = 1.0f / sqrtf((float)HD); a.out_q = out_q_dev; a.out_d = out_d_dev;
     a.out_f32 = out_f32_dev; a.part = s->part; a.err = &s->err;
+    a.part_ml = part_ml_of(s->part, (size_t)B * NH * max_chunks);
     launch_decode_attention(a, st);
     if (cudaGetLastError() != cudaSuccess) return GSVCU_ERR_CUDA;
     return GSVCU_OK;
