@@ -185,49 +185,6 @@ __device__ __forceinline__ void rg_gemm(const uint8_t* W, const uint16_t* DW, in
     rg_chain<KB, KB>(W, DW, lr, X, rt, 0, acc);
 }
 
-// FFN2-shaped row group (KB2 = 64 blocks) split over 4 warps by K quarter q: each warp issues its 16
-// MMAs at once, then the warps continue one float chain in block order, handing the running sums
-// over through shared memory `hand` ([4 lanes x ... ]) with named barriers bar_base + q.
-__device__ __forceinline__ void rg_gemm_ksplit4(const uint8_t* W, const uint16_t* DW, int lr, const uint8_t* X,
-                                                int rt, int q, float* hand, int bar_base, float (&acc)[4]) {
-    constexpr int KB = KB2, KQ = KB2 / 4;
-    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int fa = lr * 16 + g, fb = fa + 8;
-    const uint4* wp = (const uint4*)W + (size_t)lr * KB * 32 + lane;
-    const uint8_t* xq = X + (rt * 8 + g) * 32 + t * 8;
-    const uint8_t* xd = X + DR * 32 + (rt * 8 + 2 * t) * 4;
-    int c[KQ][4];
-#pragma unroll
-    for (int j = 0; j < KQ; j++) {
-        const int kb = q * KQ + j;
-        const uint2 bq = *(const uint2*)(xq + kb * BLK);
-        mma_s8(c[j], wp[kb * 32], bq.x, bq.y);
-    }
-    const uint4 sa0 = *(const uint4*)(DW + fa * KB + q * KQ), sa1 = *(const uint4*)(DW + fa * KB + q * KQ + 8);
-    const uint4 sb0 = *(const uint4*)(DW + fb * KB + q * KQ), sb1 = *(const uint4*)(DW + fb * KB + q * KQ + 8);
-    if (q > 0) {   // the previous quarter's warp has stored the running sums
-        asm volatile("bar.sync %0, 64;" ::"r"(bar_base + q) : "memory");
-        const float4 v = *(const float4*)(hand + lane * 4);
-        acc[0] = v.x; acc[1] = v.y; acc[2] = v.z; acc[3] = v.w;
-    } else {
-        acc[0] = acc[1] = acc[2] = acc[3] = 0.0f;
-    }
-#pragma unroll
-    for (int j = 0; j < KQ; j++) {
-        const float dwa = h2f_pick(j < 8 ? sa0 : sa1, j & 7), dwb = h2f_pick(j < 8 ? sb0 : sb1, j & 7);
-        const float2 dx = *(const float2*)(xd + (q * KQ + j) * BLK);
-        acc[0] = fmaf((float)c[j][0], __fmul_rn(dwa, dx.x), acc[0]);
-        acc[1] = fmaf((float)c[j][1], __fmul_rn(dwa, dx.y), acc[1]);
-        acc[2] = fmaf((float)c[j][2], __fmul_rn(dwb, dx.x), acc[2]);
-        acc[3] = fmaf((float)c[j][3], __fmul_rn(dwb, dx.y), acc[3]);
-    }
-    if (q < 3) {
-        if (q > 0) __syncwarp();   // this warp's read of `hand` is done before it is overwritten
-        *(float4*)(hand + lane * 4) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-        asm volatile("bar.arrive %0, 64;" ::"r"(bar_base + q + 1) : "memory");
-    }
-}
-
 // Byte of column c within a row's 32 quants of an exchanged block.
 __device__ __forceinline__ int qpos(int c) { return ((c & 15) >> 2) * 8 + ((c >> 4) << 2) + (c & 3); }
 
@@ -501,17 +458,15 @@ __global__ void __launch_bounds__(DT, 1) k_dense_layer(const DenseParams p) {
     }
     send_staged(stg + STG_H, su32(sm + SM_HROWS), 4 * rank * BLK, 4 * BLK, bar(BX_H));
 
-    // ---- phase 4: FFN2 + residual n1 + bias (columns 32*rank + 0..31): task = (row group, row tile) on
-    // warps 4 task .. 4 task + 3, one K quarter each, chained in block order
+    // ---- phase 4: FFN2 + residual n1 + bias (columns 32*rank + 0..31): warp = (row group, row tile), each
+    // the whole 64-block chain (splitting K over warps with hand-offs of the running sums measured slower)
     {
         ok &= d_wait(bar(BX_H));
         ok &= d_wait(bar(BW_F2));
-        const int task = warp >> 2, q = warp & 3, lr = task & 1, rt = task >> 1;
-        float* hand = (float*)(sm + SM_LNP1) + task * 128;   // LN1 sums are consumed by now
-        float acc[4];
-        rg_gemm_ksplit4(sm + SM_W_F2, (const uint16_t*)(sm + SM_D_F2), lr, sm + SM_HROWS, rt, q, hand, 1 + task * 3,
-                        acc);
-        if (q == 3) {
+        if (warp < 4) {
+            const int lr = warp & 1, rt = warp >> 1;
+            float acc[4];
+            rg_gemm<KB2>(sm + SM_W_F2, (const uint16_t*)(sm + SM_D_F2), lr, sm + SM_HROWS, rt, acc);
             const int g = lane >> 2, t = lane & 3;
 #pragma unroll
             for (int i = 0; i < 4; i++) {
