@@ -417,10 +417,10 @@ def traffic_per_key():
 
 def cpu_baseline(args, job_tokens, job_seqs):
     """The oracle (CPU restatement of the reference's ggml CPU path) on a bounded sample of the job:
-    16 config-4 sequences; generate with 1 and with 9 decode steps (both include the same prefill),
-    so per-token decode = (t9 - t1) / (16 * 8) and per-sequence prefill = t1 / 16 (its single decode
-    step is charged to prefill, slightly against the CPU). The job's time is extrapolated from these
-    measured costs for the job's sequence and token counts."""
+    16 config-4 sequences generated for 1 + 24 steps at B=16. The oracle times its prefills and its
+    batched decode steps separately, so per-sequence prefill = prefill time / 16 and per-token decode =
+    decode time / (16 x decode steps); the job's time is extrapolated from these measured costs for the
+    job's sequence and token counts."""
     import gsv_synth as S
     import oracle as O
     model = S.cached_model(MODEL_CACHE, seed=0, n_layer=24)
@@ -431,20 +431,16 @@ def cpu_baseline(args, job_tokens, job_seqs):
     reqs = [stream.next()[0] for _ in range(16)]
     seeds = list(range(16))
     orc.generate(reqs[:2], seeds=seeds[:2], max_steps=2)   # warm caches / thread pool
-    t0 = time.perf_counter()
-    orc.generate(reqs, seeds=seeds, max_steps=1)
-    t1 = time.perf_counter() - t0
-    steps = 8
-    t0 = time.perf_counter()
+    steps = 24
     orc.generate(reqs, seeds=seeds, max_steps=1 + steps)
-    t9 = time.perf_counter() - t0
-    per_seq_prefill = t1 / len(reqs)
-    per_token_decode = max(t9 - t1, 1e-6) / (len(reqs) * steps)
+    t_pre, t_dec, n_dec = O.last_generate_seconds()
+    per_seq_prefill = t_pre / len(reqs)
+    per_token_decode = t_dec / (len(reqs) * max(n_dec, 1))
     est = job_seqs * per_seq_prefill + job_tokens * per_token_decode
     return {"value": job_tokens / est, "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"16 config-4 sequences at B=16 on {cores} threads: prefill+1 step {t1:.1f} s, "
-                      f"+{steps} decode steps {t9 - t1:.1f} s; job time extrapolated for {job_seqs} prefills "
-                      f"+ {job_tokens} tokens"}
+            "sample": f"16 config-4 sequences at B=16 on {cores} threads: prefill {t_pre:.2f} s, {n_dec} batched "
+                      f"decode steps {t_dec:.2f} s; job time extrapolated for {job_seqs} prefills + {job_tokens} "
+                      f"tokens"}
 
 
 def main():

@@ -32,6 +32,7 @@
 // with -ffp-contract=off so nothing else is fused.
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
@@ -865,6 +866,16 @@ int orc_decode_trace(orc_model* m, int B, const int32_t* phones, const int32_t* 
 // Sequences are computed independently (equal to the reference's left-padded batch, whose pad keys
 // are always masked); PE of generated token idx is prompt_len_b + idx with prompt_len_b the
 // sequence's own prompt length (the reference requires equal prompt lengths, :730-733).
+// Wall time of the last orc_generate call on this thread, split into the prefills and the decode
+// steps (a timing aid for the CPU baseline: the two parts differ by orders of magnitude per token).
+static thread_local double g_gen_prefill_s = 0.0, g_gen_decode_s = 0.0;
+static thread_local int g_gen_decode_steps = 0;
+void orc_last_generate_seconds(double* prefill_s, double* decode_s, int* decode_steps) {
+    *prefill_s = g_gen_prefill_s;
+    *decode_s = g_gen_decode_s;
+    *decode_steps = g_gen_decode_steps;
+}
+
 int orc_generate(orc_model* m, int B, const int32_t* phones, const int32_t* n_phones, const float* bert,
                  const int32_t* prompts, const int32_t* n_prompt, int top_k, float top_p, float temperature, float rep,
                  uint64_t seed_base, int early_stop_num, int max_steps, const int32_t* oracle_tokens, int n_oracle,
@@ -877,10 +888,15 @@ int orc_generate(orc_model* m, int B, const int32_t* phones, const int32_t* n_ph
     sc.top_k = top_k; sc.top_p = top_p; sc.temperature = temperature; sc.rep = rep;
     std::vector<SeqCache> caches(B);
     std::vector<float> lg((size_t)B * V);
+    using clk = std::chrono::steady_clock;
+    const auto t_start = clk::now();
     for (int b = 0; b < B; b++) {
         init_cache(*m, caches[b], reqs[b].T + reqs[b].P + max_steps + 8);
         prefill_one(*m, reqs[b], kv_f16 != 0, caches[b], lg.data() + (size_t)b * V, nullptr);
     }
+    g_gen_prefill_s = std::chrono::duration<double>(clk::now() - t_start).count();
+    g_gen_decode_s = 0.0;
+    g_gen_decode_steps = 0;
     if (first_logits_out) std::memcpy(first_logits_out, lg.data(), lg.size() * 4);
     std::vector<std::vector<int32_t>> y(B);
     for (int b = 0; b < B; b++) y[b].assign(reqs[b].prompt, reqs[b].prompt + reqs[b].P);
@@ -938,7 +954,10 @@ int orc_generate(orc_model* m, int B, const int32_t* phones, const int32_t* n_ph
                 x[j * D + d] = std::fmaf(m->audio_alpha, m->pe[(size_t)pos * D + d], m->audio_emb[(size_t)tok * D + d]);
         }
         std::vector<float> lg2(which.size() * V);
+        const auto t_step = clk::now();
         decode_step(*m, ptrs, x.data(), kv_f16 != 0, lg2.data(), nullptr);
+        g_gen_decode_s += std::chrono::duration<double>(clk::now() - t_step).count();
+        g_gen_decode_steps++;
         for (size_t j = 0; j < which.size(); j++)
             std::memcpy(lg.data() + (size_t)which[j] * V, lg2.data() + j * V, V * 4);
     }

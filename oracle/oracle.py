@@ -65,6 +65,8 @@ def _load():
                                        C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, _i32p, _i32p, _i32p,
                                        C.c_int, C.c_void_p]
     lib.orc_generate.restype = C.c_int
+    lib.orc_last_generate_seconds.argtypes = [C.POINTER(C.c_double), C.POINTER(C.c_double), C.POINTER(C.c_int)]
+    lib.orc_last_generate_seconds.restype = None
     return lib
 
 
@@ -280,6 +282,13 @@ class OracleModel:
         if with_first_logits:
             return out, lens.tolist(), fl
         return out, lens.tolist()
+
+
+def last_generate_seconds():
+    """(prefill seconds, decode seconds, decode steps) of the last OracleModel.generate on this thread."""
+    p, d, n = C.c_double(), C.c_double(), C.c_int()
+    lib().orc_last_generate_seconds(C.byref(p), C.byref(d), C.byref(n))
+    return p.value, d.value, n.value
 
 
 # ------------------------------------------------------------------ the reference's own sampler
