@@ -980,7 +980,7 @@ int gsvcu_create(int device, gsvcu_ctx** out) {
     DeviceGuard g(device);
     bool dense_usable = false;
     if (gemm_q8_init_device() != cudaSuccess || attention_init_device() != cudaSuccess ||
-        dense_init_device(&dense_usable) != cudaSuccess) {
+        logits_init_device() != cudaSuccess || dense_init_device(&dense_usable) != cudaSuccess) {
         cudaGetLastError();
         return GSVCU_ERR_CUDA;
     }

@@ -75,6 +75,7 @@ struct F32Gather {          // x(m, k): k < bert_dim -> feat[row_off + k*T], k =
     const int32_t* row_T = nullptr;   // [M] T of the row's sequence, -1 for rows without features
     int bert_dim = 0;
 };
+cudaError_t logits_init_device();   // shared-memory attribute of the K = 512 logits kernel
 void launch_gemm_f32d(const float* x, int ldx, const F32Gather* gather, int M, const float* w, int N, int K,
                       const float* add, int ldadd, float* y, int ldy, cudaStream_t s);
 

@@ -105,9 +105,10 @@ void launch_quantize_q8(const float* x, int rows, int K, int8_t* q, uint16_t* d,
 
 // ------------------------------------------------------------------ F32 GEMM, double accumulation
 // ggml F32 mul_mat (src/gsv_ar.cpp:241 BERT projection with the [W|b] augmented weight, :266 logits):
-// float products accumulated in double and rounded once. The double sum of float products is exact
-// or within a few double ulps of the serial sum, so its rounding to float matches the reference's
-// serial order except in vanishingly rare ties. Tile: 32 outputs x 32 rows, K in steps of 32.
+// products exact in double (fma of the widened operands), accumulated in double and rounded once.
+// The double sum is exact or within a few double ulps of the serial sum, so its rounding to float
+// matches the serial order except in vanishingly rare ties. Tile: 32 outputs x 32 rows, K in steps
+// of 32.
 __global__ void __launch_bounds__(256) k_gemm_f32d(const float* __restrict__ x, int ldx, F32Gather gth, int use_gather,
                                                    int M, const float* __restrict__ w, int N, int K,
                                                    const float* __restrict__ add, int ldadd, float* __restrict__ y,
@@ -150,7 +151,7 @@ __global__ void __launch_bounds__(256) k_gemm_f32d(const float* __restrict__ x, 
         for (int kk = 0; kk < 32; kk++) {
             const float wv = Ws[tn][kk];
 #pragma unroll
-            for (int i = 0; i < 4; i++) acc[i][kk & 1] += (double)__fmul_rn(wv, Xs[tm * 4 + i][kk]);
+            for (int i = 0; i < 4; i++) acc[i][kk & 1] = fma((double)wv, (double)Xs[tm * 4 + i][kk], acc[i][kk & 1]);
         }
         __syncthreads();
     }
@@ -166,79 +167,74 @@ __global__ void __launch_bounds__(256) k_gemm_f32d(const float* __restrict__ x, 
     }
 }
 
-// Rows x of width K = 512 times F32 weights w [N][512] (the logits, src/gsv_ar.cpp:266), for few rows:
-// warp per output column n with the column's 512 weights in registers (16 per lane); per row the lane
-// forms its 16 float products, sums them in double, and the warp adds the 32 lane sums in double,
-// rounded once -- the double sum of float products of k_gemm_f32d. A float converts to double by
-// moving its bits into the double's fields, which encodes value * 2^-896 exactly (normal and subnormal
-// floats); the sums are scaled back by 2^896 before the rounding. The scaling is exact as long as no
-// partial sum falls below 2^-126 in magnitude (then its last bits are those of a subnormal double).
-__device__ __forceinline__ double f32_to_f64_scaled(float v) {
-    const uint32_t u = __float_as_uint(v);
-    return __hiloint2double((int)((u & 0x80000000u) | ((u & 0x7fffffffu) >> 3)), (int)(u << 29));
-}
-
-// 32 rows per pass: each lane forms its 16-product double sums for all 32 rows, then a butterfly
-// reduce-scatter over the warp (31 double shuffles) leaves row r's total in lane r.
+// Rows x of width K = 512 (M <= 256) times F32 weights w [N][512] (the logits, src/gsv_ar.cpp:266),
+// the arithmetic of k_gemm_f32d: products exact in double, accumulated in double, rounded once. A CTA
+// owns 8 output columns x 32 rows; its weights (constant) are widened into shared memory before the
+// wait for the rows. The 8 warps split K into 64-wide ranges with lane = row, 8 independent double
+// chains per lane (one per column, each x value reused 8 times); the 8 range sums are added in range
+// order.
+constexpr int LG_COLS = 8, LG_ROWS = 32, LG_XSTR = D + 1;   // odd row stride: lane = row reads conflict-free
+constexpr size_t LG_SMEM = (size_t)D * LG_COLS * 8 + (size_t)LG_ROWS * LG_XSTR * 4;
 __global__ void __launch_bounds__(256) k_logits512(const float* __restrict__ x, int ldx, int M,
                                                    const float* __restrict__ w, int N, const float* __restrict__ add,
                                                    int ldadd, float* __restrict__ y, int ldy) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n = blockIdx.x * 8 + warp;
+    extern __shared__ __align__(16) uint8_t lg_sm[];
+    double* sw = (double*)lg_sm;                                    // [D][LG_COLS], later [8][32][LG_COLS] sums
+    float* sx = (float*)(lg_sm + (size_t)D * LG_COLS * 8);          // [LG_ROWS][LG_XSTR]
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n0 = blockIdx.x * LG_COLS, m0 = blockIdx.y * LG_ROWS;
+    for (int i = tid; i < D * LG_COLS; i += 256) {
+        const int c = i / D, k = i - c * D, n = n0 + c;
+        sw[k * LG_COLS + c] = n < N ? (double)w[(size_t)n * D + k] : 0.0;
+    }
     griddep_wait();
     griddep_launch();
-    if (n >= N) return;
-    float wr[16];
-    {
-        const float4* wp = (const float4*)(w + (size_t)n * D + lane * 16);
+    for (int i = tid; i < LG_ROWS * D; i += 256) {
+        const int r = i / D, k = i - r * D, m = m0 + r;
+        sx[r * LG_XSTR + k] = m < M ? x[(size_t)m * ldx + k] : 0.0f;
+    }
+    __syncthreads();
+    double acc[LG_COLS];
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const float4 t = wp[i];
-            wr[4 * i] = t.x; wr[4 * i + 1] = t.y; wr[4 * i + 2] = t.z; wr[4 * i + 3] = t.w;
+    for (int j = 0; j < LG_COLS; j++) acc[j] = 0.0;
+    const float* xr = sx + lane * LG_XSTR;
+#pragma unroll 4
+    for (int k = warp * 64; k < warp * 64 + 64; k++) {
+        const double xv = (double)xr[k];
+        const double2* wp = (const double2*)(sw + k * LG_COLS);
+#pragma unroll
+        for (int j = 0; j < LG_COLS / 2; j++) {
+            const double2 ww = wp[j];
+            acc[2 * j] = fma(xv, ww.x, acc[2 * j]);
+            acc[2 * j + 1] = fma(xv, ww.y, acc[2 * j + 1]);
         }
     }
-    for (int m0 = 0; m0 < M; m0 += 32) {
-        double acc[32];
+    __syncthreads();   // every warp is done with the weights: their space takes the range sums
+    double* sred = sw;
 #pragma unroll
-        for (int r = 0; r < 32; r++) {
-            const int m = min(m0 + r, M - 1);
-            const float4* xp = (const float4*)(x + (size_t)m * ldx + lane * 16);
-            double a = 0.0;
+    for (int j = 0; j < LG_COLS; j++) sred[(warp * LG_ROWS + lane) * LG_COLS + j] = acc[j];
+    __syncthreads();
+    const int r = tid / LG_COLS, c = tid % LG_COLS, m = m0 + r, n = n0 + c;
+    double sum = 0.0;
 #pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const float4 t = xp[i];
-                a += f32_to_f64_scaled(__fmul_rn(wr[4 * i], t.x));
-                a += f32_to_f64_scaled(__fmul_rn(wr[4 * i + 1], t.y));
-                a += f32_to_f64_scaled(__fmul_rn(wr[4 * i + 2], t.z));
-                a += f32_to_f64_scaled(__fmul_rn(wr[4 * i + 3], t.w));
-            }
-            acc[r] = a;
-        }
-        // reduce-scatter: after the step with bit s, a lane keeps the half of its rows selected by its bit s
-#pragma unroll
-        for (int s = 16; s >= 1; s >>= 1) {
-#pragma unroll
-            for (int j = 0; j < s; j++) {
-                const bool hi = (lane & s) != 0;
-                const double send = hi ? acc[j] : acc[j + s];
-                const double keep = hi ? acc[j + s] : acc[j];
-                acc[j] = keep + __shfl_xor_sync(0xffffffffu, send, s);
-            }
-        }
-        const int m = m0 + lane;
-        if (m < M) {
-            float v = (float)(acc[0] * 0x1p896);
-            if (add) v = __fadd_rn(add[(size_t)m * ldadd + n], v);
-            y[(size_t)m * ldy + n] = v;
-        }
+    for (int q = 0; q < 8; q++) sum += sred[(q * LG_ROWS + r) * LG_COLS + c];
+    if (m < M && n < N) {
+        float v = (float)sum;
+        if (add) v = __fadd_rn(add[(size_t)m * ldadd + n], v);
+        y[(size_t)m * ldy + n] = v;
     }
+}
+
+cudaError_t logits_init_device() {
+    return cudaFuncSetAttribute(k_logits512, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)LG_SMEM);
 }
 
 void launch_gemm_f32d(const float* x, int ldx, const F32Gather* gather, int M, const float* w, int N, int K,
                       const float* add, int ldadd, float* y, int ldy, cudaStream_t s) {
     if (M <= 0) return;
     if (!gather && K == D && M <= 256 && (ldx & 3) == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)w & 15) == 0) {
-        launch_pdl(k_logits512, dim3((N + 7) / 8), dim3(256), 0, s, x, ldx, M, w, N, add, ldadd, y, ldy);
+        launch_pdl(k_logits512, dim3((N + LG_COLS - 1) / LG_COLS, (M + LG_ROWS - 1) / LG_ROWS), dim3(256), LG_SMEM, s,
+                   x, ldx, M, w, N, add, ldadd, y, ldy);
         return;
     }
     dim3 grid((N + 31) / 32, (M + 31) / 32);

@@ -43,11 +43,15 @@ __device__ __forceinline__ uint64_t xs_step(uint64_t s) {
 
 __global__ void __launch_bounds__(SAMP_T) k_sampler(const SamplerParams p) {
     const int slot = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // the jump matrices (constant since initialisation) are staged before the wait for the logits,
+    // transposed to [bit][lane] so that the 32 lanes read 32 consecutive words
+    __shared__ uint64_t jmp[64 * 32];
+    for (int e = tid; e < 64 * 32; e += SAMP_T) jmp[(e & 63) * 32 + (e >> 6)] = p.jump[e];
     griddep_wait();
     griddep_launch();
     SlotState* st = p.st + slot;
     if (!st->active) return;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int V = p.V;
     __shared__ float lg[VMAX];
     __shared__ float pr[VMAX];
@@ -206,11 +210,8 @@ __global__ void __launch_bounds__(SAMP_T) k_sampler(const SamplerParams p) {
         const int dpl = p.draws_per_lane;
         const uint64_t s0 = st->rng;
         uint64_t s = 0;
-        {
-            const uint64_t* J = p.jump + (size_t)lane * 64;
-            for (int b = 0; b < 64; b++)
-                if ((s0 >> b) & 1ull) s ^= J[b];
-        }
+#pragma unroll
+        for (int b = 0; b < 64; b++) s ^= ((s0 >> b) & 1ull) ? jmp[b * 32 + lane] : 0ull;
         float best_v = -INFINITY;
         int best_i = 0x7fffffff;
         const int i0 = lane * dpl, i1 = min(V, i0 + dpl);

@@ -15,8 +15,9 @@
 //     id = 1/d, roundf, d stored as fp16) -- pinned bit-exactly against gguf-py's Q8_0
 //     quantizer, which documents bit-exactness with ggml-quants.c; then per 32-block integer dot,
 //     accumulated in float block by block as sumf = fma((float)sumi, d_w*d_x, sumf).
-//   * F32 mul_mat / F32 vec_dot: float products accumulated in double, rounded once
-//     (ggml_vec_dot_f32 scalar path).
+//   * F32 mul_mat / F32 vec_dot: products exact in double, accumulated in double, rounded once
+//     (ggml_vec_dot_f32; its scalar path rounds each product to float, its FMA-vectorised path
+//     accumulates in float: both within roundings of this).
 //   * flash_attn_ext (F32 K/V), prefill rows: scores s = (float)(double sum of the exact products
 //     q_e*k_e) * scale (the products are exact as in the FMA-vectorised ggml_vec_dot_f32 of the
 //     -mavx2 -mfma build), masked keys skipped; softmax(s) V evaluated in double (double exp, double
@@ -143,10 +144,12 @@ inline float vec_dot_q8_0(int64_t K, const uint8_t* w, const uint8_t* x) {
     return sumf;
 }
 
-// ggml_vec_dot_f32 scalar semantics: float products, double accumulation, one final rounding.
+// ggml_vec_dot_f32 (the F32 matrices: BERT projection, logits) with products exact in double,
+// accumulated in double, rounded once. ggml's scalar path rounds each product to float first and its
+// FMA-vectorised path accumulates in float lanes; both differ from this by roundings only.
 inline float vec_dot_f32(int64_t n, const float* x, const float* y) {
     double s = 0.0;
-    for (int64_t i = 0; i < n; i++) s += (double)(x[i] * y[i]);
+    for (int64_t i = 0; i < n; i++) s = std::fma((double)x[i], (double)y[i], s);
     return (float)s;
 }
 
