@@ -423,8 +423,9 @@ int launch_decode_attention(const DecAttnParams& p, cudaStream_t s) {
 // and read as broadcasts. Mask (src/gsv_ar.cpp:215-223) in-tile: text query (qi < T) sees text keys
 // [0, T); semantic query sees keys [0, qi].
 __global__ void __launch_bounds__(PREF_QTILE) k_prefill_attn(const PrefAttnParams p) {
-    __shared__ float Ks[PREF_QTILE][HD];
-    __shared__ float Vs[PREF_QTILE][HD];
+    // the tile's K and V rows, widened to double once when loaded (the values every product uses)
+    __shared__ __align__(16) double Ks[PREF_QTILE][HD];
+    __shared__ __align__(16) double Vs[PREF_QTILE][HD];
     const int h = blockIdx.x;
     griddep_wait();
     griddep_launch();
@@ -433,9 +434,10 @@ __global__ void __launch_bounds__(PREF_QTILE) k_prefill_attn(const PrefAttnParam
     const int start = p.seq_start[sq], S = p.seq_len[sq], T = p.text_len[sq];
     const int qi = q0 + threadIdx.x;
     const bool valid = qi < S;
-    float q[HD], o[HD];
+    double qd[HD];
+    float o[HD];
 #pragma unroll
-    for (int d = 0; d < HD; d++) q[d] = valid ? p.qkv[(size_t)(start + qi) * 3 * D + h * HD + d] : 0.0f;
+    for (int d = 0; d < HD; d++) qd[d] = valid ? (double)p.qkv[(size_t)(start + qi) * 3 * D + h * HD + d] : 0.0;
     float m = -INFINITY;
     double l = 0.0, od[HD];
 #pragma unroll
@@ -453,31 +455,41 @@ __global__ void __launch_bounds__(PREF_QTILE) k_prefill_attn(const PrefAttnParam
                     kv = *(const float4*)(kr + d4 * 4);
                     vv = *(const float4*)(kr + D + d4 * 4);
                 }
-                *(float4*)&Ks[threadIdx.x][d4 * 4] = kv;
-                *(float4*)&Vs[threadIdx.x][d4 * 4] = vv;
+                *(double2*)&Ks[threadIdx.x][d4 * 4] = make_double2(kv.x, kv.y);
+                *(double2*)&Ks[threadIdx.x][d4 * 4 + 2] = make_double2(kv.z, kv.w);
+                *(double2*)&Vs[threadIdx.x][d4 * 4] = make_double2(vv.x, vv.y);
+                *(double2*)&Vs[threadIdx.x][d4 * 4 + 2] = make_double2(vv.z, vv.w);
             }
         }
         __syncthreads();
         const int nk = min(PREF_QTILE, kend - kt);
-        for (int j = 0; j < nk; j++) {
-            const int key = kt + j;
-            const bool vis = valid && (qi < T ? key < T : key <= qi);
-            if (!vis) continue;
-            double dot = 0.0;
+        // four keys per step: four independent dot chains (each sequential over the dims), then the
+        // softmax updates in key order
+        for (int j0 = 0; j0 < nk; j0 += 4) {
+            double dot[4] = {0.0, 0.0, 0.0, 0.0};
 #pragma unroll
-            for (int d = 0; d < HD; d++) dot = fma((double)q[d], (double)Ks[j][d], dot);
-            const float s = __fmul_rn((float)dot, p.scale);
-            if (s > m) {
-                const double r = m == -INFINITY ? 0.0 : exp((double)m - (double)s);
-                l *= r;
+            for (int d = 0; d < HD; d++) {
 #pragma unroll
-                for (int d = 0; d < HD; d++) od[d] *= r;
-                m = s;
+                for (int u = 0; u < 4; u++) dot[u] = fma(qd[d], Ks[j0 + u][d], dot[u]);
             }
-            const double pj = exp((double)s - (double)m);
-            l += pj;
 #pragma unroll
-            for (int d = 0; d < HD; d++) od[d] = fma(pj, (double)Vs[j][d], od[d]);
+            for (int u = 0; u < 4; u++) {
+                const int j = j0 + u, key = kt + j;
+                const bool vis = valid && j < nk && (qi < T ? key < T : key <= qi);
+                if (!vis) continue;
+                const float s = __fmul_rn((float)dot[u], p.scale);
+                if (s > m) {
+                    const double r = m == -INFINITY ? 0.0 : exp((double)m - (double)s);
+                    l *= r;
+#pragma unroll
+                    for (int d = 0; d < HD; d++) od[d] *= r;
+                    m = s;
+                }
+                const double pj = exp((double)s - (double)m);
+                l += pj;
+#pragma unroll
+                for (int d = 0; d < HD; d++) od[d] = fma(pj, Vs[j][d], od[d]);
+            }
         }
     }
     if (!valid) return;
