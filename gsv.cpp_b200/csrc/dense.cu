@@ -20,8 +20,10 @@
 // acc = fma((float)isum_b, d_w * d_x, acc), from exact int32 block sums (mma.m16n8k32 s8 with a zero
 // accumulator); LayerNorm sums are double; the page merge follows the same page order.
 //
-// Weights: each CTA's slices of the four matrices (~200 KB per layer) are copied into shared memory by
-// TMA bulk copies issued before griddep_wait, so they load while the attention kernel runs.
+// Weights: each CTA's slices of the out, FFN1 and FFN2 matrices (~150 KB per layer) are copied into
+// shared memory by TMA bulk copies issued first thing, before griddep_wait (a 230 KB CTA becomes
+// resident only once its SM has no attention CTA left, so the copies overlap the prologue and the page
+// merge); the next layer's QKV slices follow once FFN1 has consumed the out and FFN1 slices.
 #include <cooperative_groups.h>
 
 #include "kernels.h"

@@ -138,7 +138,7 @@ void launch_page_list(const SlotState* st, int M, int split, const int32_t* bloc
 
 // ------------------------------------------------------------ fused decode layer tail (dense.cu)
 // Page merge -> out-projection + residual -> LayerNorm 1 -> FFN1 (ReLU) -> FFN2 + residual ->
-// LayerNorm 2 [-> next layer's QKV with the K/V page store], one 16-CTA cluster per 8 slots.
+// LayerNorm 2 [-> next layer's QKV with the K/V page store], one 16-CTA cluster per 16 slots.
 struct DenseParams {
     int slot0 = 0;                      // first slot (row) of this launch
     int M = 0;                          // slots (rows) of this launch: slot0 .. slot0 + M - 1
