@@ -125,10 +125,12 @@ int validate_model(const GgufFile& f, ModelView& mv, std::string& err) {
         return GSVCU_ERR_FORMAT;
     }
     const int NL = hp.n_layer, V = hp.vocab_size, PV = hp.phoneme_vocab_size, BD = hp.bert_dim;
-    auto need = [&](const std::string& name, uint32_t type, std::vector<int64_t> dims, const GgufTensor** out) -> int {
+    // type 0 = F32, 8 = Q8_0; alt_type: a second accepted type (-1: none)
+    auto need = [&](const std::string& name, uint32_t type, std::vector<int64_t> dims, const GgufTensor** out,
+                    int alt_type = -1) -> int {
         const GgufTensor* t = f.tensor(name);
         if (!t) { err = "missing tensor " + name; return GSVCU_ERR_FORMAT; }
-        if (t->type != type) {
+        if (t->type != type && (alt_type < 0 || t->type != (uint32_t)alt_type)) {
             err = "tensor " + name + " has ggml type " + std::to_string(t->type) + ", expected " + std::to_string(type);
             return GSVCU_ERR_FORMAT;
         }
@@ -146,7 +148,7 @@ int validate_model(const GgufFile& f, ModelView& mv, std::string& err) {
     if ((r = need("ar.text_emb", 0, {D, PV}, &mv.te)) || (r = need("ar.audio_emb", 0, {D, V}, &mv.ae)) ||
         (r = need("ar.bert_proj", 0, {BD, D}, &mv.bp)) || (r = need("ar.bert_proj_b", 0, {D}, &mv.bb)) ||
         (r = need("ar.text_pe_alpha", 0, {1}, &mv.ta)) || (r = need("ar.audio_pe_alpha", 0, {1}, &mv.aa)) ||
-        (r = need("ar.predict", 0, {D, V}, &mv.pr)))
+        (r = need("ar.predict", 0, {D, V}, &mv.pr, 8)))   // F32 or Q8_0 (exporter --spec predict=q8_0)
         return r;
     std::memcpy(&hp.text_pe_alpha, mv.ta->data, 4);
     std::memcpy(&hp.audio_pe_alpha, mv.aa->data, 4);
@@ -182,6 +184,12 @@ struct gsvcu_ctx {
     gsvcu_hparams hp{};
     std::vector<LayerW> L;
     float *predict = nullptr, *bert_aug = nullptr, *text_emb = nullptr, *audio_emb = nullptr, *pe = nullptr;
+    // Q8_0 predict: packed like the layer matrices, rows padded with zero blocks to V_pad (multiple of 32)
+    bool predict_q8 = false;
+    int V_pad = 0;
+    uint4* predict_wq = nullptr;
+    uint16_t* predict_wd = nullptr;
+    int launch_logits(const float* xr, int M, int8_t* xq_s, uint16_t* xd_s, float* out, cudaStream_t s);
     uint64_t* jump = nullptr;
     int dpl = 0;
 
@@ -324,7 +332,20 @@ int gsvcu_ctx::load(const char* path) {
     };
     TRY(upload(mv.te->data, mv.te->nbytes, (void**)&text_emb));
     TRY(upload(mv.ae->data, mv.ae->nbytes, (void**)&audio_emb));
-    TRY(upload(mv.pr->data, mv.pr->nbytes, (void**)&predict));
+    if (mv.pr->type == 8) {   // Q8_0 predict
+        predict_q8 = true;
+        V_pad = (V + 31) / 32 * 32;
+        std::vector<uint8_t> raw((size_t)V_pad * (D / QK) * 34, 0);   // zero blocks: scale 0, quants 0
+        std::memcpy(raw.data(), mv.pr->data, (size_t)V * (D / QK) * 34);
+        std::vector<uint8_t> pq((size_t)V_pad * D);
+        std::vector<uint16_t> pd((size_t)V_pad * D / QK);
+        pack_q8_0_host(raw.data(), V_pad, D, pq.data(), pd.data());
+        TRY(upload(pq.data(), pq.size(), (void**)&predict_wq));
+        TRY(upload(pd.data(), pd.size() * 2, (void**)&predict_wd));
+    } else {
+        predict_q8 = false;
+        TRY(upload(mv.pr->data, mv.pr->nbytes, (void**)&predict));
+    }
     {   // [W | b] augmented BERT projection (src/gsv_ar.cpp:648-656)
         std::vector<float> aug((size_t)D * (BD + 1));
         const float* w = (const float*)mv.bp->data;
@@ -492,6 +513,23 @@ void gsvcu_ctx::release_slot(int slot) {
 // ------------------------------------------------------------------ prefill
 // Packs the sequences' rows back to back (no padding; the reference's left-pad keys are always
 // masked, src/gsv_ar.cpp:219, so they contribute nothing) and runs the layers over all rows.
+// logits of M rows xr [M][D] f32 into out [M][V] (src/gsv_ar.cpp:266, ggml mul_mat with `predict`): the F32
+// path of k_gemm_f32d, or for a Q8_0 predict the rows quantized to Q8_0 (into xq_s, xd_s) and the Q8_0
+// GEMM, as for the layer matrices. Returns the kernels launched.
+int gsvcu_ctx::launch_logits(const float* xr, int M, int8_t* xq_s, uint16_t* xd_s, float* out, cudaStream_t s) {
+    const int V = hp.vocab_size;
+    if (!predict_q8) {
+        launch_gemm_f32d(xr, D, nullptr, M, predict, V, D, nullptr, 0, out, V, s);
+        return 1;
+    }
+    launch_quantize_q8(xr, M, D, xq_s, xd_s, s);
+    GemmQ8Params g;
+    g.xq = xq_s; g.xd = xd_s; g.M = M; g.wq = predict_wq; g.wd = predict_wd; g.N = V_pad; g.K = D;
+    g.y = out; g.ldy = V; g.n_store = V;
+    launch_gemm_q8(g, EPI_BIAS, s);
+    return 2;
+}
+
 int gsvcu_ctx::prefill_pass(const int* slots, const gsvcu_request* reqs, int n, float* dump, int dump_b0,
                             int dump_B) {
     const int NL = hp.n_layer, V = hp.vocab_size, BD = hp.bert_dim;
@@ -620,9 +658,9 @@ int gsvcu_ctx::prefill_pass(const int* slots, const gsvcu_request* reqs, int n, 
     }
     // logits of each sequence's last position (src/gsv_ar.cpp:266-269) into its slot's row
     launch_copy_rows(p_xl, nullptr, x, p_last, n, D, s);
-    launch_gemm_f32d(p_xl, D, nullptr, n, predict, V, D, nullptr, 0, p_lg, V, s);
+    const int nlg = launch_logits(p_xl, n, xq, xd, p_lg, s);   // the pass's Q8_0 rows are consumed
     launch_copy_rows(logits, p_slots, p_lg, nullptr, n, V, s);
-    launches += 3 + (int64_t)NL * 7 + 3;
+    launches += 3 + (int64_t)NL * 7 + 2 + nlg;
     CK(cudaGetLastError());
     // host staging vectors die at return: finish the pass before they go
     CK(cudaStreamSynchronize(s));
@@ -814,9 +852,8 @@ int gsvcu_ctx::launch_step(cudaStream_t s, float* dump, int dump_row, const int*
                 nk++;
                 TRY(mark(GSVCU_PROF_DENSE));
             }
-            launch_gemm_f32d(x + (size_t)s0 * D, D, nullptr, rows, predict, V, D, nullptr, 0,
-                             logits + (size_t)s0 * V, V, cs);
-            nk++;
+            nk += launch_logits(x + (size_t)s0 * D, rows, xq + (size_t)s0 * D, xd + (size_t)s0 * (D / QK),
+                                logits + (size_t)s0 * V, cs);
             TRY(mark(GSVCU_PROF_PREDICT));
             return GSVCU_OK;
         };
@@ -886,8 +923,7 @@ int gsvcu_ctx::launch_step(cudaStream_t s, float* dump, int dump_row, const int*
                 CK(cudaMemcpyAsync(dump + ((((size_t)dump_row * dump_B + b) * NL + li) * 4 + 3) * D,
                                    x + (size_t)dump_slots[b] * D, D * 4, cudaMemcpyDeviceToHost, s));
     }
-    launch_gemm_f32d(x, D, nullptr, M, predict, V, D, nullptr, 0, logits, V, s);
-    nk++;
+    nk += launch_logits(x, M, xq, xd, logits, s);
     TRY(mark(8));
     graph_kernels = nk;
     return GSVCU_OK;

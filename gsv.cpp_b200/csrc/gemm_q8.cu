@@ -157,7 +157,7 @@ __global__ void __launch_bounds__(32 * KS) k_gemm_q8(const GemmQ8Params p) {
         const float bias = p.bias ? p.bias[f] : 0.0f;
         if (EPI == EPI_BIAS) {
             const float y = __fadd_rn(acc[q], bias);
-            if (valid) p.y[(size_t)n * p.N + f] = y;
+            if (valid && f < (p.n_store ? p.n_store : p.N)) p.y[(size_t)n * (p.ldy ? p.ldy : p.N) + f] = y;
             if (valid && p.kv.pool && f >= D) {
                 int slot, pos;
                 bool ok = true;
@@ -320,7 +320,7 @@ __global__ void __launch_bounds__(256) k_gemm_q8_tile(const GemmQ8Params p) {
             const float bias = p.bias ? p.bias[f] : 0.0f;
             if (EPI == EPI_BIAS) {
                 const float y = __fadd_rn(a, bias);
-                p.y[(size_t)n * p.N + f] = y;
+                if (f < (p.n_store ? p.n_store : p.N)) p.y[(size_t)n * (p.ldy ? p.ldy : p.N) + f] = y;
                 bool ok = p.kv.pool && f >= D;
                 int slot = 0, pos = 0;
                 if (ok) {

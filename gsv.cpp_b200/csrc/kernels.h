@@ -53,6 +53,8 @@ struct GemmQ8Params {
     const float* bias = nullptr;
     const float* resid = nullptr;   // [M][N]
     float* y = nullptr;             // [M][N]
+    int ldy = 0;                    // EPI_BIAS: row stride of y (0: N)
+    int n_store = 0;                // EPI_BIAS: columns of y stored (0: N); N may carry zero padding rows
     int8_t* yq = nullptr;           // [M][N]   (EPI_RELU_Q8)
     uint16_t* yd = nullptr;         // [M][N/32]
     KvWrite kv;
@@ -66,7 +68,7 @@ cudaError_t gemm_q8_init_device();
 void pack_q8_0_host(const uint8_t* raw, int N, int K, uint8_t* wq_out, uint16_t* wd_out);
 
 // ------------------------------------------------------------ F32 GEMM, double accumulation
-// y[m][n] = (float) sum_k (double)(w[n][k] * x(m, k))  (+ add[m][n]); x(m,k) = x[m*ldx + k], or,
+// y[m][n] = (float) sum_k (double)w[n][k] * (double)x(m, k)  (+ add[m][n]); x(m,k) = x[m*ldx + k], or,
 // for the BERT projection, gathered from per-sequence [1024][T] feature blocks with an implicit
 // trailing 1 (see F32Gather).
 struct F32Gather {          // x(m, k): k < bert_dim -> feat[row_off + k*T], k == bert_dim -> 1; row_T < 0 -> 0

@@ -27,13 +27,15 @@ class Dims:
 
 
 def write_model(path: str, seed: int = 0, dims: Dims | None = None, mat_type: str = "q8_0",
-                ln_noise: float = 0.02) -> str:
+                ln_noise: float = 0.02, predict_type: str = "f32") -> str:
+    """predict_type "q8_0" stores ar.predict as Q8_0 (the exporter's --spec predict=q8_0)."""
     import gguf
 
     d = dims or Dims()
     rng = np.random.default_rng(seed)
     D, FF = d.D, 4 * d.D
-    qt = {"q8_0": gguf.GGMLQuantizationType.Q8_0, "f32": gguf.GGMLQuantizationType.F32}[mat_type]
+    types = {"q8_0": gguf.GGMLQuantizationType.Q8_0, "f32": gguf.GGMLQuantizationType.F32}
+    qt = types[mat_type]
 
     def n(*shape, s=0.02):
         return (rng.standard_normal(shape, dtype=np.float32) * np.float32(s)).astype(np.float32)
@@ -60,7 +62,7 @@ def write_model(path: str, seed: int = 0, dims: Dims | None = None, mat_type: st
     add("ar.bert_proj_b", n(D))
     add("ar.text_pe_alpha", np.ones(1, np.float32))
     add("ar.audio_pe_alpha", np.ones(1, np.float32))
-    add("ar.predict", n(d.V, D))
+    add("ar.predict", n(d.V, D), types[predict_type])
     for li in range(d.NL):
         p = f"transformer.block{li}"
         add(f"{p}.qkv_w", n(3 * D, D), qt)
@@ -82,13 +84,15 @@ def write_model(path: str, seed: int = 0, dims: Dims | None = None, mat_type: st
     return path
 
 
-def cached_model(cache_dir: str, seed: int = 0, n_layer: int = 24, mat_type: str = "q8_0") -> str:
+def cached_model(cache_dir: str, seed: int = 0, n_layer: int = 24, mat_type: str = "q8_0",
+                 predict_type: str = "f32") -> str:
     """Write (once) and return the path of a synthetic model in cache_dir."""
     os.makedirs(cache_dir, exist_ok=True)
-    path = os.path.join(cache_dir, f"gsv_ar_synth_s{seed}_l{n_layer}_{mat_type}.gguf")
+    suffix = "" if predict_type == "f32" else f"_p{predict_type}"
+    path = os.path.join(cache_dir, f"gsv_ar_synth_s{seed}_l{n_layer}_{mat_type}{suffix}.gguf")
     if not os.path.exists(path):
         tmp = path + f".tmp{os.getpid()}"
-        write_model(tmp, seed=seed, dims=Dims(NL=n_layer), mat_type=mat_type)
+        write_model(tmp, seed=seed, dims=Dims(NL=n_layer), mat_type=mat_type, predict_type=predict_type)
         os.replace(tmp, path)
     return path
 

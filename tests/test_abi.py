@@ -53,6 +53,16 @@ def test_inspect_rejects_bad_files(model_small, model_f32_small, tmp_path):
     assert rc == -5 and "expected 8" in msg
 
 
+def test_inspect_q8_0_predict():
+    """A Q8_0 predict matrix (exporter --spec predict=q8_0) is accepted; the logits then run on the Q8_0
+    GEMM (GPU parity: tests/test_gpu_model.py::test_q8_0_predict_matches_oracle)."""
+    import gsv_synth as S
+    from conftest import MODEL_CACHE
+    rc, hp, msg = gsvcu.inspect_gguf(S.cached_model(MODEL_CACHE, seed=9, n_layer=2, predict_type="q8_0"))
+    assert rc == gsvcu.OK, msg
+    assert hp.vocab_size == 1025
+
+
 def test_inspect_missing_tensor(tmp_path):
     import gguf
     w = gguf.GGUFWriter(str(tmp_path / "partial.gguf"), "gsv.ar")

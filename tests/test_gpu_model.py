@@ -15,7 +15,7 @@ import pytest
 
 import gsv_synth as S
 import oracle as O
-from conftest import cosine, rel_l2
+from conftest import MODEL_CACHE, cosine, rel_l2
 
 pytestmark = pytest.mark.gpu
 
@@ -301,3 +301,27 @@ def test_cpp_dropin_class(gctx, model_full, tmp_path):
         assert lines[1 + b]["tokens"] == got[b].tolist()
     assert lines[3]["lens"] == glens
     assert (lines[3]["hidden"], lines[3]["vocab"], lines[3]["eos"]) == (512, 1025, 1024)
+
+
+def test_q8_0_predict_matches_oracle():
+    """A model whose predict matrix is Q8_0 (exporter --spec predict=q8_0): logits by the Q8_0 GEMM over
+    the Q8_0-quantized rows, as ggml's Q8_0 mul_mat; first logits and a teacher-forced decode trace
+    (fused and unfused steps) equal the oracle bit for bit."""
+    import gsvcu
+    model = S.cached_model(MODEL_CACHE, seed=9, n_layer=2, predict_type="q8_0")
+    orc9 = O.OracleModel(model)
+    c = gsvcu.Context(0)
+    try:
+        c.load(model)
+        reqs = S.ragged_requests(29, 5, lo=30, hi=150)
+        forced = np.random.default_rng(29).integers(0, 1024, (5, 20)).astype(np.int32)
+        c.kv_reserve(8, 512, 0)
+        ref = orc9.decode_trace(reqs, forced, kv_f16=True)
+        got = c.debug_trace(reqs, forced)
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+        c.set_fused_decode(0)
+        unf = c.debug_trace(reqs, forced)
+        c.set_fused_decode(1)
+        assert np.array_equal(unf.view(np.uint32), ref.view(np.uint32))
+    finally:
+        c.close()
