@@ -145,7 +145,8 @@ int validate_model(const GgufFile& f, ModelView& mv, std::string& err) {
         return GSVCU_OK;
     };
     int r;
-    if ((r = need("ar.text_emb", 0, {D, PV}, &mv.te)) || (r = need("ar.audio_emb", 0, {D, V}, &mv.ae)) ||
+    // embeddings: F32, or F16 (exporter --spec emb=f16) widened to F32 on load
+    if ((r = need("ar.text_emb", 0, {D, PV}, &mv.te, 1)) || (r = need("ar.audio_emb", 0, {D, V}, &mv.ae, 1)) ||
         (r = need("ar.bert_proj", 0, {BD, D}, &mv.bp)) || (r = need("ar.bert_proj_b", 0, {D}, &mv.bb)) ||
         (r = need("ar.text_pe_alpha", 0, {1}, &mv.ta)) || (r = need("ar.audio_pe_alpha", 0, {1}, &mv.aa)) ||
         (r = need("ar.predict", 0, {D, V}, &mv.pr, 8)))   // F32 or Q8_0 (exporter --spec predict=q8_0)
@@ -330,8 +331,16 @@ int gsvcu_ctx::load(const char* path) {
         CK(cudaMemcpy(*dst, src, bytes, cudaMemcpyHostToDevice));
         return GSVCU_OK;
     };
-    TRY(upload(mv.te->data, mv.te->nbytes, (void**)&text_emb));
-    TRY(upload(mv.ae->data, mv.ae->nbytes, (void**)&audio_emb));
+    auto upload_emb = [&](const GgufTensor* t, float** dst) -> int {   // F16 tables widened exactly
+        if (t->type == 0) return upload(t->data, t->nbytes, (void**)dst);
+        const size_t n = t->nbytes / 2;
+        std::vector<float> f32(n);
+        const __half* h = (const __half*)t->data;
+        for (size_t i = 0; i < n; i++) f32[i] = __half2float(h[i]);
+        return upload(f32.data(), n * 4, (void**)dst);
+    };
+    TRY(upload_emb(mv.te, &text_emb));
+    TRY(upload_emb(mv.ae, &audio_emb));
     if (mv.pr->type == 8) {   // Q8_0 predict
         predict_q8 = true;
         V_pad = (V + 31) / 32 * 32;

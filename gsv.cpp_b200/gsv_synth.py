@@ -27,8 +27,9 @@ class Dims:
 
 
 def write_model(path: str, seed: int = 0, dims: Dims | None = None, mat_type: str = "q8_0",
-                ln_noise: float = 0.02, predict_type: str = "f32") -> str:
-    """predict_type "q8_0" stores ar.predict as Q8_0 (the exporter's --spec predict=q8_0)."""
+                ln_noise: float = 0.02, predict_type: str = "f32", emb_type: str = "f32") -> str:
+    """predict_type "q8_0" stores ar.predict as Q8_0 (the exporter's --spec predict=q8_0); emb_type
+    "f16" stores the text / audio embeddings as F16 (--spec emb=f16)."""
     import gguf
 
     d = dims or Dims()
@@ -53,11 +54,14 @@ def write_model(path: str, seed: int = 0, dims: Dims | None = None, mat_type: st
         arr = np.ascontiguousarray(arr, dtype=np.float32)
         if dtype == gguf.GGMLQuantizationType.F32:
             w.add_tensor(name, arr, raw_dtype=dtype)
+        elif dtype == gguf.GGMLQuantizationType.F16:
+            w.add_tensor(name, arr.astype(np.float16), raw_dtype=dtype)
         else:
             w.add_tensor(name, gguf.quants.quantize(arr, dtype), raw_dtype=dtype)
 
-    add("ar.text_emb", n(d.PV, D))
-    add("ar.audio_emb", n(d.V, D))
+    et = {"f32": gguf.GGMLQuantizationType.F32, "f16": gguf.GGMLQuantizationType.F16}[emb_type]
+    add("ar.text_emb", n(d.PV, D), et)
+    add("ar.audio_emb", n(d.V, D), et)
     add("ar.bert_proj", n(D, d.BERT))
     add("ar.bert_proj_b", n(D))
     add("ar.text_pe_alpha", np.ones(1, np.float32))
@@ -85,14 +89,15 @@ def write_model(path: str, seed: int = 0, dims: Dims | None = None, mat_type: st
 
 
 def cached_model(cache_dir: str, seed: int = 0, n_layer: int = 24, mat_type: str = "q8_0",
-                 predict_type: str = "f32") -> str:
+                 predict_type: str = "f32", emb_type: str = "f32") -> str:
     """Write (once) and return the path of a synthetic model in cache_dir."""
     os.makedirs(cache_dir, exist_ok=True)
-    suffix = "" if predict_type == "f32" else f"_p{predict_type}"
+    suffix = ("" if predict_type == "f32" else f"_p{predict_type}") + ("" if emb_type == "f32" else f"_e{emb_type}")
     path = os.path.join(cache_dir, f"gsv_ar_synth_s{seed}_l{n_layer}_{mat_type}{suffix}.gguf")
     if not os.path.exists(path):
         tmp = path + f".tmp{os.getpid()}"
-        write_model(tmp, seed=seed, dims=Dims(NL=n_layer), mat_type=mat_type, predict_type=predict_type)
+        write_model(tmp, seed=seed, dims=Dims(NL=n_layer), mat_type=mat_type, predict_type=predict_type,
+                    emb_type=emb_type)
         os.replace(tmp, path)
     return path
 

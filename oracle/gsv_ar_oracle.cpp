@@ -465,6 +465,37 @@ bool set_vec(std::vector<float>& v, int type, const void* data, int64_t nbytes, 
     return true;
 }
 
+// IEEE binary16 -> binary32, exact (normal, subnormal, zero, inf, NaN).
+float half_bits_to_float(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h & 0x8000u) << 16, e = (h >> 10) & 0x1fu, m = h & 0x3ffu;
+    uint32_t bits;
+    if (e == 0x1fu) bits = sign | 0x7f800000u | (m << 13);
+    else if (e != 0) bits = sign | ((e + 112u) << 23) | (m << 13);
+    else if (m == 0) bits = sign;
+    else {   // subnormal: normalise
+        int shift = 0;
+        uint32_t mm = m;
+        while (!(mm & 0x400u)) { mm <<= 1; shift++; }
+        bits = sign | ((uint32_t)(113 - shift) << 23) | ((mm & 0x3ffu) << 13);
+    }
+    float f;
+    std::memcpy(&f, &bits, 4);
+    return f;
+}
+
+// Embedding table: F32, or F16 widened to F32 on load (ggml get_rows of an F16 table yields the same
+// values). The reference loader accepts F32 only (src/gsv_ar.cpp:633-637); F16 is what the exporter
+// writes for --spec emb=f16.
+bool set_emb(std::vector<float>& v, int type, const void* data, int64_t nbytes, int64_t n, std::string& err, const char* name) {
+    if (type == T_F16 && nbytes == n * 2) {
+        v.resize((size_t)n);
+        const uint16_t* h = (const uint16_t*)data;
+        for (int64_t i = 0; i < n; i++) v[(size_t)i] = half_bits_to_float(h[i]);
+        return true;
+    }
+    return set_vec(v, type, data, nbytes, n, err, name);
+}
+
 // mk_pe (src/gsv_ar.cpp:173-181)
 void make_pe(orc_model& m, int pe_max) {
     m.pe_max = pe_max;
@@ -757,8 +788,8 @@ const char* orc_model_error(orc_model* m) { return m ? m->err.c_str() : "null mo
 int orc_model_set(orc_model* m, const char* name, int type, const void* data, int64_t nbytes) {
     const int D = m->D, FF = 4 * D;
     std::string n(name);
-    if (n == "ar.text_emb") return set_vec(m->text_emb, type, data, nbytes, (int64_t)m->PV * D, m->err, name) ? 0 : -1;
-    if (n == "ar.audio_emb") return set_vec(m->audio_emb, type, data, nbytes, (int64_t)m->V * D, m->err, name) ? 0 : -1;
+    if (n == "ar.text_emb") return set_emb(m->text_emb, type, data, nbytes, (int64_t)m->PV * D, m->err, name) ? 0 : -1;
+    if (n == "ar.audio_emb") return set_emb(m->audio_emb, type, data, nbytes, (int64_t)m->V * D, m->err, name) ? 0 : -1;
     if (n == "ar.bert_proj") return set_vec(m->bert_proj, type, data, nbytes, (int64_t)D * m->BERT, m->err, name) ? 0 : -1;
     if (n == "ar.bert_proj_b") return set_vec(m->bert_proj_b, type, data, nbytes, D, m->err, name) ? 0 : -1;
     if (n == "ar.text_pe_alpha" || n == "ar.audio_pe_alpha") {

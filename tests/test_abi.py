@@ -53,12 +53,14 @@ def test_inspect_rejects_bad_files(model_small, model_f32_small, tmp_path):
     assert rc == -5 and "expected 8" in msg
 
 
-def test_inspect_q8_0_predict():
-    """A Q8_0 predict matrix (exporter --spec predict=q8_0) is accepted; the logits then run on the Q8_0
-    GEMM (GPU parity: tests/test_gpu_model.py::test_q8_0_predict_matches_oracle)."""
+@pytest.mark.parametrize("predict_type,emb_type", [("q8_0", "f32"), ("f32", "f16")])
+def test_inspect_export_formats(predict_type, emb_type):
+    """A Q8_0 predict matrix (exporter --spec predict=q8_0) and F16 embeddings (--spec emb=f16) are
+    accepted (GPU parity: tests/test_gpu_model.py::test_export_formats_match_oracle)."""
     import gsv_synth as S
     from conftest import MODEL_CACHE
-    rc, hp, msg = gsvcu.inspect_gguf(S.cached_model(MODEL_CACHE, seed=9, n_layer=2, predict_type="q8_0"))
+    rc, hp, msg = gsvcu.inspect_gguf(S.cached_model(MODEL_CACHE, seed=9, n_layer=2, predict_type=predict_type,
+                                                    emb_type=emb_type))
     assert rc == gsvcu.OK, msg
     assert hp.vocab_size == 1025
 

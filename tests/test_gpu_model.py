@@ -303,12 +303,14 @@ def test_cpp_dropin_class(gctx, model_full, tmp_path):
     assert (lines[3]["hidden"], lines[3]["vocab"], lines[3]["eos"]) == (512, 1025, 1024)
 
 
-def test_q8_0_predict_matches_oracle():
-    """A model whose predict matrix is Q8_0 (exporter --spec predict=q8_0): logits by the Q8_0 GEMM over
-    the Q8_0-quantized rows, as ggml's Q8_0 mul_mat; first logits and a teacher-forced decode trace
-    (fused and unfused steps) equal the oracle bit for bit."""
+@pytest.mark.parametrize("predict_type,emb_type", [("q8_0", "f32"), ("f32", "f16")])
+def test_export_formats_match_oracle(predict_type, emb_type):
+    """Exporter formats beyond the default: a Q8_0 predict matrix (--spec predict=q8_0: logits by the Q8_0
+    GEMM over the Q8_0-quantized rows, as ggml's Q8_0 mul_mat) and F16 embeddings (--spec emb=f16,
+    widened to F32 on load). A teacher-forced decode trace (fused and unfused steps) equals the oracle
+    bit for bit."""
     import gsvcu
-    model = S.cached_model(MODEL_CACHE, seed=9, n_layer=2, predict_type="q8_0")
+    model = S.cached_model(MODEL_CACHE, seed=9, n_layer=2, predict_type=predict_type, emb_type=emb_type)
     orc9 = O.OracleModel(model)
     c = gsvcu.Context(0)
     try:
