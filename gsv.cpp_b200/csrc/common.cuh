@@ -89,6 +89,10 @@ struct SlotState {
     int32_t hist_head;    // ring position of the oldest token
     int32_t n_forced;     // teacher-forced tokens available
     int32_t decode_now;   // 1 when this step decodes the slot
+    // the sequence's sampler settings (gsv_sampler_cfg, src/gsv_sampler.h:18-23): sequences with
+    // different settings share one running batch
+    int32_t top_k;
+    float top_p, temperature, rep;
     uint64_t rng;         // xorshift64* state (src/gsv_sampler.h:33-42)
 };
 

@@ -233,7 +233,6 @@ struct gsvcu_ctx {
 
     // ------------------------------------------------------------ decode graph
     cudaGraphExec_t graph = nullptr;
-    gsvcu_sampler_cfg graph_cfg{};
     gsvcu_sampler_cfg cfg{15, 1.0f, 1.0f, 1.35f};
     int64_t tokens_done = 0;   // generated tokens of finished sequences (serving)
     int64_t launches = 0;      // kernels launched by this context (graph replays count their kernels)
@@ -503,12 +502,9 @@ int gsvcu_ctx::ensure(int need_slots, int need_ctx, int kvd) {
     return reserve(slots, ctx, kvd);
 }
 
+// Sampler settings of the next admissions; every slot keeps those it was admitted with, so sequences
+// with different settings share the running batch.
 int gsvcu_ctx::set_cfg(const gsvcu_sampler_cfg& c) {
-    const bool same = c.top_k == cfg.top_k && c.top_p == cfg.top_p && c.temperature == cfg.temperature &&
-                      c.repetition_penalty == cfg.repetition_penalty;
-    if (same) return GSVCU_OK;
-    for (char u : slot_used)
-        if (u) return fail(GSVCU_ERR_STATE, "sampler settings differ from the sequences in flight");
     cfg = c;
     return GSVCU_OK;
 }
@@ -756,6 +752,10 @@ int gsvcu_ctx::admit(const gsvcu_request* reqs, int n, const uint64_t* seeds, co
         ss.hist_len = nh;
         ss.hist_head = 0;
         ss.decode_now = 0;
+        ss.top_k = cfg.top_k;
+        ss.top_p = cfg.top_p;
+        ss.temperature = cfg.temperature;
+        ss.rep = cfg.repetition_penalty;
         const uint64_t seed = seeds ? seeds[i] : (uint64_t)i;
         ss.rng = seed ? seed : 1;   // gsv_rng(seed) (src/gsv_sampler.h:35)
         ss.n_forced = 0;
@@ -804,7 +804,6 @@ int gsvcu_ctx::launch_step(cudaStream_t s, float* dump, int dump_row, const int*
     if (prof_ms) CK(cudaEventRecord(prof_ev[0], s));
     SamplerParams sp;
     sp.logits = logits; sp.V = V; sp.eos = hp.eos; sp.nslots = M;
-    sp.top_k = cfg.top_k; sp.top_p = cfg.top_p; sp.temperature = cfg.temperature; sp.rep = cfg.repetition_penalty;
     sp.st = st; sp.counts = counts; sp.hist = hist; sp.out_tokens = out_tokens; sp.tok_cap = tok_cap;
     sp.forced = forced; sp.forced_cap = forced_cap; sp.jump = jump; sp.draws_per_lane = dpl;
     launch_sampler(sp, s);
@@ -939,14 +938,7 @@ int gsvcu_ctx::launch_step(cudaStream_t s, float* dump, int dump_row, const int*
 }
 
 int gsvcu_ctx::run_steps(int nsteps) {
-    const bool cfg_same = graph && graph_cfg.top_k == cfg.top_k && graph_cfg.top_p == cfg.top_p &&
-                          graph_cfg.temperature == cfg.temperature &&
-                          graph_cfg.repetition_penalty == cfg.repetition_penalty;
-    if (!cfg_same) {
-        if (graph) {
-            cudaGraphExecDestroy(graph);
-            graph = nullptr;
-        }
+    if (!graph) {   // the step reads every per-slot setting from device memory: one capture serves all
         cudaGraph_t gr;
         CK(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
         const int lr = launch_step(stream);
@@ -959,7 +951,6 @@ int gsvcu_ctx::run_steps(int nsteps) {
             graph = nullptr;
             return fail(GSVCU_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
         }
-        graph_cfg = cfg;
     }
     for (int i = 0; i < nsteps; i++) CK(cudaGraphLaunch(graph, stream));
     launches += (int64_t)nsteps * graph_kernels;
@@ -1455,6 +1446,10 @@ int gsvcu_op_sample(gsvcu_ctx* ctx, const float* logits_dev, int32_t B, int32_t 
         ss.group_first = b;
         ss.finish_kind = -1;
         ss.rng = rng_host[b];
+        ss.top_k = cfg->top_k;
+        ss.top_p = cfg->top_p;
+        ss.temperature = cfg->temperature;
+        ss.rep = cfg->repetition_penalty;
         const int np = prev_host ? n_prev_host[b] : 0;
         if (np < 0 || np > prev_stride * (prev_host != nullptr)) return GSVCU_ERR_ARG;
         const int nh = std::min(np, HIST);
@@ -1478,7 +1473,6 @@ int gsvcu_op_sample(gsvcu_ctx* ctx, const float* logits_dev, int32_t B, int32_t 
     cudaMemcpyAsync(blk + o_jump, jm.data(), jm.size() * 8, cudaMemcpyHostToDevice, s);
     SamplerParams sp;
     sp.logits = logits_dev; sp.V = V; sp.eos = eos; sp.nslots = B;
-    sp.top_k = cfg->top_k; sp.top_p = cfg->top_p; sp.temperature = cfg->temperature; sp.rep = cfg->repetition_penalty;
     sp.st = (SlotState*)(blk + o_st); sp.counts = (uint16_t*)(blk + o_cnt); sp.hist = (int32_t*)(blk + o_ring);
     sp.out_tokens = (int32_t*)(blk + o_tok); sp.tok_cap = cap; sp.jump = (const uint64_t*)(blk + o_jump);
     sp.draws_per_lane = dpl;

@@ -200,9 +200,7 @@ void launch_prefill_embed(const PrefEmbedParams& p, cudaStream_t s);
 struct SamplerParams {
     const float* logits = nullptr;       // [nslots][V]
     int V = 0, eos = 0, nslots = 0;
-    int top_k = 15;
-    float top_p = 1.f, temperature = 1.f, rep = 1.35f;
-    SlotState* st = nullptr;
+    SlotState* st = nullptr;             // per slot: sampler settings, RNG, step, repetition window size
     uint16_t* counts = nullptr;          // [nslots][V]
     int32_t* hist = nullptr;             // [nslots][HIST] ring of the repetition window
     int32_t* out_tokens = nullptr;       // [nslots][tok_cap]

@@ -53,6 +53,8 @@ __global__ void __launch_bounds__(SAMP_T) k_sampler(const SamplerParams p) {
     SlotState* st = p.st + slot;
     if (!st->active) return;
     const int V = p.V;
+    const int top_k = st->top_k;
+    const float top_p = st->top_p, temperature = st->temperature, rep = st->rep;
     __shared__ float lg[VMAX];
     __shared__ float pr[VMAX];
     __shared__ float sv[SORT_N];
@@ -69,13 +71,13 @@ __global__ void __launch_bounds__(SAMP_T) k_sampler(const SamplerParams p) {
     __syncthreads();
 
     // 1) repetition penalty
-    if (p.rep != 1.0f) {
+    if (rep != 1.0f) {
         const uint16_t* cnt = p.counts + (size_t)slot * V;
         for (int i = tid; i < V; i += SAMP_T) {
             const int c = cnt[i];
             if (c) {
                 float l = lg[i];
-                for (int r = 0; r < c; r++) l = l < 0.0f ? __fmul_rn(l, p.rep) : __fdiv_rn(l, p.rep);
+                for (int r = 0; r < c; r++) l = l < 0.0f ? __fmul_rn(l, rep) : __fdiv_rn(l, rep);
                 lg[i] = l;
             }
         }
@@ -83,7 +85,7 @@ __global__ void __launch_bounds__(SAMP_T) k_sampler(const SamplerParams p) {
     }
 
     // 2) top-p (nucleus) over a stable descending order
-    if (p.top_p < 1.0f) {
+    if (top_p < 1.0f) {
         for (int i = tid; i < SORT_N; i += SAMP_T) {
             sv[i] = i < V ? lg[i] : -INFINITY;
             si[i] = (int16_t)i;
@@ -117,7 +119,7 @@ __global__ void __launch_bounds__(SAMP_T) k_sampler(const SamplerParams p) {
             float cum = 0.0f;
             for (int k = 0; k < V; k++) {
                 cum = fmaf(pr[k], inv_sum, cum);
-                if (k > 0 && cum > p.top_p) lg[si[k]] = -INFINITY;
+                if (k > 0 && cum > top_p) lg[si[k]] = -INFINITY;
             }
         }
         __syncthreads();
@@ -125,14 +127,14 @@ __global__ void __launch_bounds__(SAMP_T) k_sampler(const SamplerParams p) {
 
     // 3) temperature
     {
-        const float t = fmaxf(p.temperature, 1e-5f);
+        const float t = fmaxf(temperature, 1e-5f);
         for (int i = tid; i < V; i += SAMP_T) lg[i] = __fdiv_rn(lg[i], t);
         __syncthreads();
     }
 
     // 4) top-k: exact k-th largest value by 4-pass radix select on order-preserving keys
-    if (p.top_k > 0 && p.top_k < V) {
-        if (tid == 0) { sel_prefix = 0u; sel_krem = (uint32_t)p.top_k; }
+    if (top_k > 0 && top_k < V) {
+        if (tid == 0) { sel_prefix = 0u; sel_krem = (uint32_t)top_k; }
         for (int pass = 0; pass < 4; pass++) {
             const int shift = 24 - 8 * pass;
             const uint32_t mask = pass == 0 ? 0u : (0xffffffffu << (shift + 8));

@@ -133,7 +133,9 @@ typedef struct {
 } gsvcu_finished;
 
 /* Admit sequences into free slots (prefill runs immediately). seeds[i] seeds sequence i; tags are
- * returned with its completion. Fails with GSVCU_ERR_OOM if slots or KV pages are short. */
+ * returned with its completion. Every admitted sequence keeps `sampler` (NULL: the reference defaults)
+ * for its whole life, so sequences with different sampler settings share the running batch. Fails
+ * with GSVCU_ERR_OOM if slots or KV pages are short. */
 int gsvcu_serve_admit(gsvcu_ctx* ctx, const gsvcu_request* reqs, int32_t n, const gsvcu_sampler_cfg* sampler,
                       const uint64_t* seeds, const int32_t* tags, int32_t max_steps, int32_t early_stop_num);
 /* Run `n_steps` decode steps for every slot in flight, then report the sequences that finished:

@@ -275,6 +275,31 @@ def test_serving_lookahead_refill_equals_generate(gctx):
         assert np.array_equal(served[i], alone[i]), i
 
 
+def test_serving_mixed_sampler_settings(gctx):
+    """Sequences admitted with different sampler settings share the running batch (every slot keeps the
+    settings it was admitted with) and each decodes exactly as alone."""
+    reqs = S.ragged_requests(57, 4, lo=40, hi=120)
+    seeds = [700 + i for i in range(4)]
+    cfgs = [dict(top_k=15, top_p=1.0, temperature=1.0, rep=1.35), dict(top_k=5, top_p=0.8, temperature=0.7, rep=1.1),
+            dict(top_k=1, top_p=1.0, temperature=1.0, rep=1.0), dict(top_k=30, top_p=0.95, temperature=1.3, rep=1.35)]
+    _reserve(gctx, 0, slots=4, ctx=512)
+    alone = []
+    for i in range(4):
+        t, _ = gctx.generate([reqs[i]], seeds=[seeds[i]], max_steps=48, **cfgs[i])
+        alone.append(t[0][len(reqs[i].prompt):])
+    for i in range(4):
+        gctx.serve_admit([reqs[i]], [seeds[i]], [i], max_steps=48, **cfgs[i])
+    served = {}
+    for _ in range(100):
+        if len(served) == 4:
+            break
+        for f in gctx.serve_step(8, tok_cap=100000):
+            served[f["tag"]] = f["tokens"]
+    assert len(served) == 4
+    for i in range(4):
+        assert np.array_equal(served[i], alone[i]), i
+
+
 def test_cpp_dropin_class(gctx, model_full, tmp_path):
     """The C++ `class gsv_ar` shim (csrc/gsv_ar.cpp) gives the C ABI's results."""
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
