@@ -300,6 +300,59 @@ def test_serving_mixed_sampler_settings(gctx):
         assert np.array_equal(served[i], alone[i]), i
 
 
+def test_cpp_ar_server_matches_generate(gctx, model_full, tmp_path):
+    """The C++ continuous-batching front end (include/gsv_ar_server.h, the role of svc::ArBatcher): tasks
+    submitted from 3 threads into 4 slots, with different sampler settings, early-stop limits, lengths
+    and empty BERT sides, each return exactly the tokens of gsv_ar::generate of that one sequence
+    (prompt_phones ++ phones, prompt_bert ++ bert, prompt codes; as gsv_engine::ar_generate_batch)."""
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    exe = os.path.join(root, "gsv.cpp_b200", "lib", "gsv_ar_server_test")
+    assert os.path.exists(exe), "build with `make -C gsv.cpp_b200`"
+    rng = np.random.default_rng(91)
+    cfgs = [(15, 1.0, 1.0, 1.35), (5, 0.8, 0.7, 1.1), (1, 1.0, 1.0, 1.0), (30, 0.95, 1.3, 1.35)]
+    pp = rng.integers(0, 732, 11).astype(np.int32)            # one reference text for most tasks
+    pbert = rng.standard_normal((1024, 11), dtype=np.float32)
+    codes = rng.integers(0, 1024, 9).astype(np.int32)
+    tasks = []
+    for i in range(10):
+        Pt = int(rng.integers(10, 60))
+        t = dict(phones=rng.integers(0, 732, Pt).astype(np.int32),
+                 bert=rng.standard_normal((1024, Pt), dtype=np.float32) if i % 3 else np.zeros((1024, 0), np.float32),
+                 pp=pp if i % 4 else rng.integers(0, 732, 7).astype(np.int32), codes=codes,
+                 max_steps=int(rng.integers(20, 70)), early_stop=[-1, 30][i % 2], cfg=cfgs[i % 4], seed=900 + i)
+        t["pbert"] = pbert if i % 4 else np.zeros((1024, 0), np.float32)
+        tasks.append(t)
+    f = tmp_path / "tasks.bin"
+    with open(f, "wb") as fh:
+        fh.write(struct.pack("<i", len(tasks)))
+        for t in tasks:
+            k, tp, temp, rp = t["cfg"]
+            fh.write(struct.pack("<iiiiiifffQ", len(t["phones"]), len(t["pp"]), len(t["codes"]), t["max_steps"],
+                                 t["early_stop"], k, tp, temp, rp, t["seed"]))
+            for arr, dt, n in ((t["phones"], np.int32, None), (t["bert"], np.float32, len(t["phones"])),
+                               (t["pp"], np.int32, None), (t["pbert"], np.float32, len(t["pp"])),
+                               (t["codes"], np.int32, None)):
+                a = np.ascontiguousarray(arr, dt)
+                if n is not None and a.size == 0:   # an empty BERT side is written as zeros
+                    a = np.zeros((1024, n), np.float32)
+                fh.write(a.tobytes())
+    out = subprocess.run([exe, model_full, str(f), "3", "4"], capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0, out.stderr
+    lines = [json.loads(x) for x in out.stdout.strip().splitlines()]
+    assert lines[-1]["done"] == len(tasks)
+    _reserve(gctx, 0)
+    for i, t in enumerate(tasks):
+        bert = np.concatenate([t["pbert"] if t["pbert"].size else np.zeros((1024, len(t["pp"])), np.float32),
+                               t["bert"] if t["bert"].size else np.zeros((1024, len(t["phones"])), np.float32)], 1)
+        req = S.Request(phones=np.concatenate([t["pp"], t["phones"]]), bert=np.ascontiguousarray(bert),
+                        prompt=t["codes"])
+        k, tp, temp, rp = t["cfg"]
+        toks, _ = gctx.generate([req], top_k=k, top_p=tp, temperature=temp, rep=rp, early_stop=t["early_stop"],
+                                max_steps=t["max_steps"], seeds=[t["seed"]])
+        assert lines[i]["task"] == i
+        assert lines[i]["tokens"] == toks[0][len(t["codes"]):].tolist(), i
+
+
 def test_cpp_dropin_class(gctx, model_full, tmp_path):
     """The C++ `class gsv_ar` shim (csrc/gsv_ar.cpp) gives the C ABI's results."""
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
