@@ -25,6 +25,7 @@ struct LayerW {
 constexpr int PE_MAX = 8192;          // positional table rows (reference: 4096, src/gsv_ar.cpp:44)
 constexpr int PREFILL_ROWS = 16384;   // rows of one prefill pass
 constexpr int STEP_CHUNK = 16;        // decode steps between host status reads in generate
+constexpr int GRAPH_CHUNK = 16;       // decode steps captured in one graph (no launch gap between them)
 
 struct DeviceGuard {
     int prev = -1;
@@ -232,7 +233,14 @@ struct gsvcu_ctx {
     size_t feat_cap = 0;
 
     // ------------------------------------------------------------ decode graph
-    cudaGraphExec_t graph = nullptr;
+    cudaGraphExec_t graph = nullptr;         // one decode step
+    cudaGraphExec_t graph_chunk = nullptr;   // GRAPH_CHUNK decode steps in one graph
+    void drop_graphs() {
+        if (graph) cudaGraphExecDestroy(graph);
+        if (graph_chunk) cudaGraphExecDestroy(graph_chunk);
+        graph = graph_chunk = nullptr;
+    }
+    int capture_steps(int n, cudaGraphExec_t* out);
     gsvcu_sampler_cfg cfg{15, 1.0f, 1.0f, 1.35f};
     int64_t tokens_done = 0;   // generated tokens of finished sequences (serving)
     int64_t launches = 0;      // kernels launched by this context (graph replays count their kernels)
@@ -406,11 +414,8 @@ int gsvcu_ctx::load(const char* path) {
 
 // ------------------------------------------------------------------ KV pool and buffers
 void gsvcu_ctx::free_cache() {
-    if (graph) {
-        cudaGraphExecDestroy(graph);
-        graph = nullptr;
-    }
     if (stream) cudaStreamSynchronize(stream);
+    drop_graphs();
     for (void* p : callocs) cudaFree(p);
     callocs.clear();
     p_feat = nullptr;
@@ -937,22 +942,36 @@ int gsvcu_ctx::launch_step(cudaStream_t s, float* dump, int dump_row, const int*
     return GSVCU_OK;
 }
 
-int gsvcu_ctx::run_steps(int nsteps) {
-    if (!graph) {   // the step reads every per-slot setting from device memory: one capture serves all
-        cudaGraph_t gr;
-        CK(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
-        const int lr = launch_step(stream);
-        cudaError_t e = cudaStreamEndCapture(stream, &gr);
-        if (lr != GSVCU_OK) return lr;
-        if (e != cudaSuccess) return fail(GSVCU_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
-        e = cudaGraphInstantiate(&graph, gr, 0);
-        cudaGraphDestroy(gr);
-        if (e != cudaSuccess) {
-            graph = nullptr;
-            return fail(GSVCU_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
-        }
+// Capture n consecutive decode steps into one executable graph. Every per-slot value lives in device
+// memory, so one capture serves every later launch; inside the graph the programmatic edges also join
+// the last kernel of a step to the first of the next.
+int gsvcu_ctx::capture_steps(int n, cudaGraphExec_t* out) {
+    cudaGraph_t gr;
+    CK(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+    int lr = GSVCU_OK;
+    for (int k = 0; k < n && lr == GSVCU_OK; k++) lr = launch_step(stream);
+    cudaError_t e = cudaStreamEndCapture(stream, &gr);
+    if (lr != GSVCU_OK) return lr;
+    if (e != cudaSuccess) return fail(GSVCU_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+    e = cudaGraphInstantiate(out, gr, 0);
+    cudaGraphDestroy(gr);
+    if (e != cudaSuccess) {
+        *out = nullptr;
+        return fail(GSVCU_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
     }
-    for (int i = 0; i < nsteps; i++) CK(cudaGraphLaunch(graph, stream));
+    return GSVCU_OK;
+}
+
+int gsvcu_ctx::run_steps(int nsteps) {
+    int left = nsteps;
+    if (left >= GRAPH_CHUNK) {
+        if (!graph_chunk) TRY(capture_steps(GRAPH_CHUNK, &graph_chunk));
+        for (; left >= GRAPH_CHUNK; left -= GRAPH_CHUNK) CK(cudaGraphLaunch(graph_chunk, stream));
+    }
+    if (left > 0) {
+        if (!graph) TRY(capture_steps(1, &graph));
+        for (int i = 0; i < left; i++) CK(cudaGraphLaunch(graph, stream));
+    }
     launches += (int64_t)nsteps * graph_kernels;
     return GSVCU_OK;
 }
@@ -1545,10 +1564,9 @@ int gsvcu_set_fused_decode(gsvcu_ctx* ctx, int32_t mode) {
     if (!ctx || mode < 0 || mode > 2) return GSVCU_ERR_ARG;
     DeviceGuard g(ctx->device);
     const bool fused = mode != 0, two = mode == 2;
-    if ((ctx->fused != fused || ctx->two_groups != two) && ctx->graph) {   // the captured step is the other variant
-        cudaStreamSynchronize(ctx->stream);
-        cudaGraphExecDestroy(ctx->graph);
-        ctx->graph = nullptr;
+    if ((ctx->fused != fused || ctx->two_groups != two) && (ctx->graph || ctx->graph_chunk)) {
+        cudaStreamSynchronize(ctx->stream);   // the captured steps are the other variant
+        ctx->drop_graphs();
     }
     ctx->fused = fused;
     ctx->two_groups = two;
