@@ -319,6 +319,20 @@ def stage(stream, count, device):
     return out
 
 
+def reduce_over_ranks(ms, tokens, seqs, world, device):
+    """Whole-job numbers over the ranks: the slowest rank's time (max) and the tokens and sequences of
+    all ranks (sum); the identity on one rank. Every rank takes the same two collectives."""
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([ms, float(tokens), float(seqs)], dtype=torch.float64, device=device)
+    if world > 1:
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        t[0] = mx[0]
+    return float(t[0]), float(t[1]), float(t[2])
+
+
 def run_job(ctx, queue, args, counters):
     """One serving job: returns generated tokens."""
     ctx.serve_reset()
@@ -516,13 +530,7 @@ def main():
         if world > 1:
             dist.barrier()
         launches = ctx.kernel_launches() - l0
-        t = torch.tensor([ms, float(tokens), float(counters["seqs"])], dtype=torch.float64, device="cuda")
-        if world > 1:
-            mx = t.clone()
-            dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-            dist.all_reduce(t, op=dist.ReduceOp.SUM)
-            t[0] = mx[0]
-        return float(t[0]), float(t[1]), float(t[2]), launches, dict(counters)
+        return (*reduce_over_ranks(ms, tokens, counters["seqs"], world, "cuda"), launches, dict(counters))
 
     clk = sample_clocks(local_rank)
     ms_v, tok_v, seqs_v, launches_v, _ = timed(True, 2000)
