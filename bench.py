@@ -42,6 +42,8 @@ def parse():
     ap.add_argument("--refill-every", type=int, default=16)
     ap.add_argument("--kv", default="f16", choices=["f16", "f32"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-sample-seqs", type=int, default=16,
+                    help="sequences of the bounded CPU sample the baseline / reference arm extrapolates from")
     ap.add_argument("--lookahead", action="store_true",
                     help="serve with gsvcu_set_serve_lookahead (the next chunk runs while the host handles results)")
     ap.add_argument("--workload", default="serve", choices=["serve", "attn", "gemv", "prefill", "single"],
@@ -431,10 +433,10 @@ def traffic_per_key():
 
 def cpu_baseline(args, job_tokens, job_seqs):
     """The oracle (CPU restatement of the reference's ggml CPU path) on a bounded sample of the job:
-    16 config-4 sequences generated for 1 + 24 steps at B=16. The oracle times its prefills and its
-    batched decode steps separately, so per-sequence prefill = prefill time / 16 and per-token decode =
-    decode time / (16 x decode steps); the job's time is extrapolated from these measured costs for the
-    job's sequence and token counts."""
+    n = --cpu-sample-seqs (16) config-4 sequences generated for 1 + 24 steps at B=n. The oracle times its
+    prefills and its batched decode steps separately, so per-sequence prefill = prefill time / n and
+    per-token decode = decode time / (n x decode steps); the job's time is extrapolated from these
+    measured costs for the job's sequence and token counts."""
     import gsv_synth as S
     import oracle as O
     model = S.cached_model(MODEL_CACHE, seed=0, n_layer=24)
@@ -442,8 +444,9 @@ def cpu_baseline(args, job_tokens, job_seqs):
     O.set_threads(cores)
     orc = O.OracleModel(model)
     stream = RequestStream(99, 0)
-    reqs = [stream.next()[0] for _ in range(16)]
-    seeds = list(range(16))
+    n = max(1, getattr(args, "cpu_sample_seqs", 16))
+    reqs = [stream.next()[0] for _ in range(n)]
+    seeds = list(range(n))
     orc.generate(reqs[:2], seeds=seeds[:2], max_steps=2)   # warm caches / thread pool
     steps = 24
     orc.generate(reqs, seeds=seeds, max_steps=1 + steps)
@@ -452,7 +455,8 @@ def cpu_baseline(args, job_tokens, job_seqs):
     per_token_decode = t_dec / (len(reqs) * max(n_dec, 1))
     est = job_seqs * per_seq_prefill + job_tokens * per_token_decode
     return {"value": job_tokens / est, "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"16 config-4 sequences at B=16 on {cores} threads: prefill {t_pre:.2f} s, {n_dec} batched "
+            "job_ms": est * 1e3,
+            "sample": f"{n} config-4 sequences at B={n} on {cores} threads: prefill {t_pre:.2f} s, {n_dec} batched "
                       f"decode steps {t_dec:.2f} s; job time extrapolated for {job_seqs} prefills + {job_tokens} "
                       f"tokens"}
 
@@ -475,8 +479,8 @@ def main():
         cb = cpu_baseline(args, job_tokens=args.slots * args.iters, job_seqs=args.slots)
         print(json.dumps({
             "impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tokens/s", "n_gpus": n_gpus,
-            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "q8_0 int8 dot / f32", "data": "synthetic",
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": cb["job_ms"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "q8_0 int8 dot / f32", "data": "synthetic",
             "config": {"workload": "cfg4 shard extrapolated from a bounded CPU sample",
                        "slots_per_gpu": args.slots, "iters": args.iters},
             "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},

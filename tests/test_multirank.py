@@ -73,3 +73,20 @@ def test_request_stream_is_reproducible():
     for _ in range(3):
         (ra, sa), (rb, sb) = a.next(), b.next()
         assert sa == sb and ra.phones.tolist() == rb.phones.tolist() and ra.prompt.tolist() == rb.prompt.tolist()
+
+
+def test_reference_arm_line():
+    """`bench.py --impl reference` (the CPU reference arm the driver runs beside this library's arm) prints
+    one JSON line with the bench contract's keys, on a 2-sequence CPU sample."""
+    import json
+    import subprocess
+    out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "1",
+                          "--warmup", "3", "--cpu-sample-seqs", "2"], capture_output=True, text=True, timeout=600,
+                         cwd=ROOT)
+    assert out.returncode == 0, out.stderr
+    line = json.loads(out.stdout.strip().splitlines()[-1])
+    for k in ("impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+              "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
+        assert k in line, k
+    assert line["impl"] == "reference" and line["value"] > 0 and line["ms_per_step"] > 0
+    assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["cpu_baseline"]["kind"] == "port"
