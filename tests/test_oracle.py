@@ -6,7 +6,9 @@
   ggml's reference quantize_row_q8_0);
 * add_act: the reference's own test inputs and tolerance (tests/test_add_act.cpp:64-65, 86-98);
 * transformer semantics (prefix mask, post-LN layers, PE, BERT projection, KV-cached decode):
-  against a float64 numpy restatement on a model with F32 matrices (no activation quantization).
+  against a float64 numpy restatement on a model with F32 matrices (no activation quantization);
+* export formats: F16 embeddings widen exactly; Q8_0 logits bit-exact against a numpy restatement
+  of ggml's Q8_0 dot with a correctly rounded fmaf.
 """
 import os
 
@@ -239,3 +241,86 @@ def test_oracle_batch_equals_single(model_small):
     for b in range(3):
         ts, _ = orc.generate([reqs[b]], seeds=[seeds[b]], max_steps=25)
         assert np.array_equal(tb[b], ts[0])
+
+
+def _gguf_widened_copy(src, dst, names):
+    """Rewrite a GGUF file with the tensors in `names` stored as F32 holding their exact values."""
+    import gguf
+    rd = gguf.GGUFReader(src)
+    w = gguf.GGUFWriter(dst, str(rd.fields["general.architecture"].contents()))
+    for f in rd.fields.values():
+        if f.name.startswith("ar."):
+            if f.types[0] == gguf.GGUFValueType.UINT32:
+                w.add_uint32(f.name, int(f.contents()))
+            else:
+                w.add_float32(f.name, float(f.contents()))
+    for t in rd.tensors:
+        data = np.array(t.data)
+        if t.name in names:
+            w.add_tensor(t.name, gguf.quants.dequantize(data, t.tensor_type).astype(np.float32),
+                         raw_dtype=gguf.GGMLQuantizationType.F32)
+        else:
+            w.add_tensor(t.name, data, raw_dtype=t.tensor_type)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    return dst
+
+
+def test_oracle_f16_embeddings_widen_exactly(tmp_path):
+    """F16 text/audio embeddings (exporter --spec emb=f16) are widened exactly: the oracle gives the
+    same logits, bit for bit, as for a twin file storing those values as F32."""
+    e16 = S.write_model(str(tmp_path / "e16.gguf"), seed=21, dims=S.Dims(NL=2), emb_type="f16")
+    e32 = _gguf_widened_copy(e16, str(tmp_path / "e32.gguf"), {"ar.text_emb", "ar.audio_emb"})
+    rng = np.random.default_rng(21)
+    reqs = [S.make_request(rng, 23, 9), S.make_request(rng, 14, 0)]
+    forced = rng.integers(0, 1024, (2, 4)).astype(np.int32)
+    a = O.OracleModel(e16).decode_trace(reqs, forced)
+    b = O.OracleModel(e32).decode_trace(reqs, forced)
+    assert np.array_equal(a, b)
+
+
+def _fmaf(a, b, c):
+    """Correctly rounded float32 fma of float32 arrays whose product a*b is exact in float64.
+
+    The float64 sum s = a*b + c is rounded once; TwoSum gives its exact residual e. Rounding s to
+    float32 is then wrong only when s lies exactly halfway between two float32 values and e != 0:
+    the exact value lies on e's side of that midpoint."""
+    p = np.asarray(a, np.float64) * np.asarray(b, np.float64)
+    c = np.asarray(c, np.float64)
+    s = p + c
+    bv = s - p
+    e = (p - (s - bv)) + (c - bv)
+    f = s.astype(np.float32)
+    g = np.nextafter(f, np.where(s > f, np.inf, -np.inf).astype(np.float32))
+    mid = (f.astype(np.float64) + g.astype(np.float64)) * 0.5 == s
+    up, dn = np.maximum(f, g), np.minimum(f, g)
+    return np.where(mid & (e > 0), up, np.where(mid & (e < 0), dn, f))
+
+
+def test_oracle_q8_0_logits_restated(tmp_path):
+    """Q8_0 ar.predict (exporter --spec predict=q8_0): the logits equal, bit for bit, a numpy
+    restatement of ggml's Q8_0 mul_mat -- the hidden state quantized by gguf-py's Q8_0 quantizer,
+    exact integer block dots, float accumulation acc = fmaf(isum, d_w * d_x, acc) in block order."""
+    import gguf
+    path = S.write_model(str(tmp_path / "p8.gguf"), seed=22, dims=S.Dims(NL=2), predict_type="q8_0")
+    orc = O.OracleModel(path)
+    rng = np.random.default_rng(22)
+    reqs = [S.make_request(rng, 31, 7), S.make_request(rng, 12, 20)]
+    logits, dump = orc.first_logits(reqs, dump=True)
+    W = next(t for t in gguf.GGUFReader(path).tensors if t.name == "ar.predict")
+    wb = np.array(W.data).reshape(orc.V, orc.D // 32, 34)
+    dw = wb[..., :2].copy().view(np.float16)[..., 0].astype(np.float32)
+    qw = wb[..., 2:].copy().view(np.int8).astype(np.int32)
+    for b in range(len(reqs)):
+        x = dump[b, orc.NL - 1, 3]          # last layer's output at the last position
+        xb = gguf.quants.quantize(x.reshape(1, orc.D), gguf.GGMLQuantizationType.Q8_0).reshape(-1, 34)
+        dx = xb[:, :2].copy().view(np.float16)[:, 0].astype(np.float32)
+        qx = xb[:, 2:].copy().view(np.int8).astype(np.int32)
+        isum = (qw * qx[None]).sum(-1).astype(np.float32)
+        d = dw * dx[None]                    # exact: two 11-bit significands
+        acc = np.zeros(orc.V, np.float32)
+        for ib in range(orc.D // 32):
+            acc = _fmaf(isum[:, ib], d[:, ib], acc)
+        assert np.array_equal(acc, logits[b]), b
