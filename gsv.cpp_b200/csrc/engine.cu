@@ -16,8 +16,10 @@ using namespace gsvcu;
 namespace {
 
 struct LayerW {
-    uint4* wq[4] = {nullptr, nullptr, nullptr, nullptr};     // qkv, out, ffn1, ffn2 fragment planes
-    uint16_t* wd[4] = {nullptr, nullptr, nullptr, nullptr};  // matching fp16 scale planes
+    int mt[4] = {8, 8, 8, 8};                                // ggml type of qkv, out, ffn1, ffn2: 8 Q8_0, 0 F32, 1 F16
+    uint4* wq[4] = {nullptr, nullptr, nullptr, nullptr};     // Q8_0: fragment planes
+    uint16_t* wd[4] = {nullptr, nullptr, nullptr, nullptr};  //       matching fp16 scale planes
+    const void* wf[4] = {nullptr, nullptr, nullptr, nullptr};  // F32 / F16: the GGUF rows [N][K] as stored
     float *b_qkv = nullptr, *b_out = nullptr, *n1w = nullptr, *n1b = nullptr;
     float *b_f1 = nullptr, *b_f2 = nullptr, *n2w = nullptr, *n2b = nullptr;
 };
@@ -126,13 +128,16 @@ int validate_model(const GgufFile& f, ModelView& mv, std::string& err) {
         return GSVCU_ERR_FORMAT;
     }
     const int NL = hp.n_layer, V = hp.vocab_size, PV = hp.phoneme_vocab_size, BD = hp.bert_dim;
-    // type 0 = F32, 8 = Q8_0; alt_type: a second accepted type (-1: none)
-    auto need = [&](const std::string& name, uint32_t type, std::vector<int64_t> dims, const GgufTensor** out,
-                    int alt_type = -1) -> int {
+    // accepted ggml types: 0 = F32, 1 = F16, 8 = Q8_0
+    auto need = [&](const std::string& name, std::vector<uint32_t> types, std::vector<int64_t> dims,
+                    const GgufTensor** out) -> int {
         const GgufTensor* t = f.tensor(name);
         if (!t) { err = "missing tensor " + name; return GSVCU_ERR_FORMAT; }
-        if (t->type != type && (alt_type < 0 || t->type != (uint32_t)alt_type)) {
-            err = "tensor " + name + " has ggml type " + std::to_string(t->type) + ", expected " + std::to_string(type);
+        if (std::find(types.begin(), types.end(), t->type) == types.end()) {
+            std::string want;
+            for (uint32_t ty : types) want += (want.empty() ? "" : " or ") + std::to_string(ty);
+            err = "tensor " + name + " has ggml type " + std::to_string(t->type) + ", expected " + want +
+                  " (0 F32, 1 F16, 8 Q8_0)";
             return GSVCU_ERR_FORMAT;
         }
         int64_t ne = 1, ne_want = 1;
@@ -146,11 +151,12 @@ int validate_model(const GgufFile& f, ModelView& mv, std::string& err) {
         return GSVCU_OK;
     };
     int r;
-    // embeddings: F32, or F16 (exporter --spec emb=f16) widened to F32 on load
-    if ((r = need("ar.text_emb", 0, {D, PV}, &mv.te, 1)) || (r = need("ar.audio_emb", 0, {D, V}, &mv.ae, 1)) ||
-        (r = need("ar.bert_proj", 0, {BD, D}, &mv.bp)) || (r = need("ar.bert_proj_b", 0, {D}, &mv.bb)) ||
-        (r = need("ar.text_pe_alpha", 0, {1}, &mv.ta)) || (r = need("ar.audio_pe_alpha", 0, {1}, &mv.aa)) ||
-        (r = need("ar.predict", 0, {D, V}, &mv.pr, 8)))   // F32 or Q8_0 (exporter --spec predict=q8_0)
+    // embeddings: F32, or F16 (exporter --spec emb=f16) widened to F32 on load; predict: F32, Q8_0 or
+    // F16 (--spec predict=q8_0 / f16); layer matrices: Q8_0, F32 or F16 (--spec attn=.., ffn=..)
+    if ((r = need("ar.text_emb", {0, 1}, {D, PV}, &mv.te)) || (r = need("ar.audio_emb", {0, 1}, {D, V}, &mv.ae)) ||
+        (r = need("ar.bert_proj", {0}, {BD, D}, &mv.bp)) || (r = need("ar.bert_proj_b", {0}, {D}, &mv.bb)) ||
+        (r = need("ar.text_pe_alpha", {0}, {1}, &mv.ta)) || (r = need("ar.audio_pe_alpha", {0}, {1}, &mv.aa)) ||
+        (r = need("ar.predict", {0, 8, 1}, {D, V}, &mv.pr)))
         return r;
     std::memcpy(&hp.text_pe_alpha, mv.ta->data, 4);
     std::memcpy(&hp.audio_pe_alpha, mv.aa->data, 4);
@@ -161,9 +167,14 @@ int validate_model(const GgufFile& f, ModelView& mv, std::string& err) {
     for (int li = 0; li < NL; li++) {
         const std::string pfx = "transformer.block" + std::to_string(li) + ".";
         for (int m = 0; m < 4; m++)
-            if ((r = need(pfx + kMatNames[m], 8, {NK[m][1], NK[m][0]}, &mv.mats[(size_t)li * 4 + m]))) return r;
+            if ((r = need(pfx + kMatNames[m], {8, 0, 1}, {NK[m][1], NK[m][0]}, &mv.mats[(size_t)li * 4 + m]))) return r;
+        // FFN1's epilogue produces what FFN2 reads: Q8_0 blocks for a Q8_0 ffn2_w, floats otherwise
+        if ((mv.mats[(size_t)li * 4 + 2]->type == 8) != (mv.mats[(size_t)li * 4 + 3]->type == 8)) {
+            err = pfx + "ffn1_w / ffn2_w: both Q8_0 or both F32 / F16 (the exporter's ffn group) expected";
+            return GSVCU_ERR_FORMAT;
+        }
         for (int k = 0; k < 8; k++)
-            if ((r = need(pfx + kVecNames[k], 0, {VL[k]}, &mv.vecs[(size_t)li * 8 + k]))) return r;
+            if ((r = need(pfx + kVecNames[k], {0}, {VL[k]}, &mv.vecs[(size_t)li * 8 + k]))) return r;
     }
     return GSVCU_OK;
 }
@@ -191,7 +202,19 @@ struct gsvcu_ctx {
     int V_pad = 0;
     uint4* predict_wq = nullptr;
     uint16_t* predict_wd = nullptr;
+    const void* predict_f16 = nullptr;   // F16 predict [V][D] (gemm_fx)
+    // layer matrices: all Q8_0 (the fused decode step needs that), any F32 / F16 FFN (needs hf)
+    bool all_q8 = true, ffn_float = false;
+    float* hf = nullptr;                 // F32 / F16 FFN: relu(W1 n1 + b1) rows [Mmax][FF]
     int launch_logits(const float* xr, int M, int8_t* xq_s, uint16_t* xd_s, float* out, cudaStream_t s);
+    // the four GEMMs of layer li over rows [r0, r0 + M) (Q8_0 or F32 / F16 per matrix); kv: K/V store of QKV
+    struct LayerIO {
+        const float *x, *attn, *n1;        // F32 inputs (x also the out-proj residual)
+        const int8_t *xq, *aq, *n1q;       // Q8_0 inputs and their scales
+        const uint16_t *xd, *ad, *n1d;
+        float *qkv, *pre;
+    };
+    void layer_gemm(int li, int m, const LayerIO& io, int M, const KvWrite& kv, cudaStream_t s);
     uint64_t* jump = nullptr;
     int dpl = 0;
 
@@ -348,7 +371,10 @@ int gsvcu_ctx::load(const char* path) {
     };
     TRY(upload_emb(mv.te, &text_emb));
     TRY(upload_emb(mv.ae, &audio_emb));
-    if (mv.pr->type == 8) {   // Q8_0 predict
+    if (mv.pr->type == 1) {   // F16 predict, evaluated by gemm_fx
+        predict_q8 = false;
+        TRY(upload(mv.pr->data, mv.pr->nbytes, (void**)&predict_f16));
+    } else if (mv.pr->type == 8) {   // Q8_0 predict
         predict_q8 = true;
         V_pad = (V + 31) / 32 * 32;
         std::vector<uint8_t> raw((size_t)V_pad * (D / QK) * 34, 0);   // zero blocks: scale 0, quants 0
@@ -376,10 +402,21 @@ int gsvcu_ctx::load(const char* path) {
     std::vector<uint8_t> wq_tmp;
     std::vector<uint16_t> wd_tmp;
     const int NK[4][2] = {{3 * D, D}, {D, D}, {FF, D}, {D, FF}};
+    all_q8 = true;
+    ffn_float = false;
     for (int li = 0; li < NL; li++) {
         for (int m = 0; m < 4; m++) {
             const GgufTensor* t = mv.mats[(size_t)li * 4 + m];
             const int N = NK[m][0], K = NK[m][1];
+            L[li].mt[m] = (int)t->type;
+            if (t->type != 8) {   // F32 / F16: kept as stored, row-major [N][K]
+                all_q8 = false;
+                ffn_float |= m >= 2;
+                void* dst = nullptr;
+                TRY(upload(t->data, t->nbytes, &dst));
+                L[li].wf[m] = dst;
+                continue;
+            }
             wq_tmp.resize((size_t)N * K);
             wd_tmp.resize((size_t)N * K / QK);
             pack_q8_0_host(t->data, N, K, wq_tmp.data(), wd_tmp.data());
@@ -473,8 +510,13 @@ int gsvcu_ctx::reserve(int slots, int ctx, int kvd) {
         {(void**)&p_slots, (size_t)max_slots * 4},
         {(void**)&p_tiles, (M / PREF_QTILE + max_slots) * sizeof(PrefillTile)},
         {(void**)&p_xl, (size_t)max_slots * D * 4}, {(void**)&p_lg, (size_t)max_slots * V * 4},
+        {(void**)&hf, ffn_float ? M * FF * 4 : 0},
     };
     for (const A& a : list) {
+        if (!a.bytes) {
+            *a.p = nullptr;
+            continue;
+        }
         const int r = alloc_dev(a.p, a.bytes, callocs);
         if (r != GSVCU_OK) {
             free_cache();
@@ -528,6 +570,12 @@ void gsvcu_ctx::release_slot(int slot) {
 // GEMM, as for the layer matrices. Returns the kernels launched.
 int gsvcu_ctx::launch_logits(const float* xr, int M, int8_t* xq_s, uint16_t* xd_s, float* out, cudaStream_t s) {
     const int V = hp.vocab_size;
+    if (predict_f16) {
+        GemmFxParams g;
+        g.x = xr; g.ldx = D; g.M = M; g.w = predict_f16; g.wtype = FX_F16; g.N = V; g.K = D; g.y = out; g.ldy = V;
+        launch_gemm_fx(g, FXE_BIAS, s);
+        return 1;
+    }
     if (!predict_q8) {
         launch_gemm_f32d(xr, D, nullptr, M, predict, V, D, nullptr, 0, out, V, s);
         return 1;
@@ -635,29 +683,22 @@ int gsvcu_ctx::prefill_pass(const int* slots, const gsvcu_request* reqs, int n, 
         }
         return GSVCU_OK;
     };
+    const LayerIO io{x, attn_f32, n1, xq, aq, n1q, xd, ad, n1d, qkv, pre};
     for (int li = 0; li < NL; li++) {
         const LayerW& w = L[li];
-        GemmQ8Params g;
-        g.xq = xq; g.xd = xd; g.M = M; g.wq = w.wq[0]; g.wd = w.wd[0]; g.N = 3 * D; g.K = D; g.bias = w.b_qkv; g.y = qkv;
-        g.kv.pool = pool; g.kv.kv_f32 = kv_f32; g.kv.n_layer = NL; g.kv.layer = li; g.kv.block_table = block_table;
-        g.kv.max_pages = max_pages; g.kv.tok_slot = p_tslot; g.kv.tok_pos = p_tpos;
-        launch_gemm_q8(g, EPI_BIAS, s);
+        KvWrite kv;
+        kv.pool = pool; kv.kv_f32 = kv_f32; kv.n_layer = NL; kv.layer = li; kv.block_table = block_table;
+        kv.max_pages = max_pages; kv.tok_slot = p_tslot; kv.tok_pos = p_tpos;
+        layer_gemm(li, 0, io, M, kv, s);
         PrefAttnParams a;
         a.qkv = qkv; a.seq_start = p_sstart; a.seq_len = p_slen; a.text_len = p_tlen; a.tiles = p_tiles;
-        a.n_tiles = (int)tiles.size(); a.scale = scale; a.out_q = aq; a.out_d = ad; a.out_f32 = dump ? attn_f32 : nullptr;
+        a.n_tiles = (int)tiles.size(); a.scale = scale; a.out_q = aq; a.out_d = ad;
+        a.out_f32 = dump || w.mt[1] != 8 ? attn_f32 : nullptr;
         launch_prefill_attention(a, s);
-        GemmQ8Params o;
-        o.xq = aq; o.xd = ad; o.M = M; o.wq = w.wq[1]; o.wd = w.wd[1]; o.N = D; o.K = D; o.bias = w.b_out; o.resid = x; o.y = pre;
-        launch_gemm_q8(o, EPI_RESID, s);
+        layer_gemm(li, 1, io, M, KvWrite(), s);
         launch_layernorm_q8(pre, M, w.n1w, w.n1b, n1, n1q, n1d, s);
-        GemmQ8Params f1;
-        f1.xq = n1q; f1.xd = n1d; f1.M = M; f1.wq = w.wq[2]; f1.wd = w.wd[2]; f1.N = FF; f1.K = D; f1.bias = w.b_f1;
-        f1.yq = hq; f1.yd = hd;
-        launch_gemm_q8(f1, EPI_RELU_Q8, s);
-        GemmQ8Params f2;
-        f2.xq = hq; f2.xd = hd; f2.M = M; f2.wq = w.wq[3]; f2.wd = w.wd[3]; f2.N = D; f2.K = FF; f2.bias = w.b_f2;
-        f2.resid = n1; f2.y = pre;
-        launch_gemm_q8(f2, EPI_RESID, s);
+        layer_gemm(li, 2, io, M, KvWrite(), s);
+        layer_gemm(li, 3, io, M, KvWrite(), s);
         if (dump) {
             TRY(dump_rows(li, 0, attn_f32));
             TRY(dump_rows(li, 1, n1));
@@ -675,6 +716,31 @@ int gsvcu_ctx::prefill_pass(const int* slots, const gsvcu_request* reqs, int n, 
     // host staging vectors die at return: finish the pass before they go
     CK(cudaStreamSynchronize(s));
     return GSVCU_OK;
+}
+
+// Layer li's GEMM m (0 QKV, 1 out, 2 FFN1, 3 FFN2) over M rows: QKV = x W^T + b (+ K/V store),
+// pre = (x + attn W^T) + b, FFN1 -> relu(n1 W^T + b) (Q8_0 blocks hq/hd or floats hf, as FFN2 reads),
+// pre = (n1 + h W^T) + b.
+void gsvcu_ctx::layer_gemm(int li, int m, const LayerIO& io, int M, const KvWrite& kv, cudaStream_t s) {
+    const LayerW& w = L[li];
+    const float* bias[4] = {w.b_qkv, w.b_out, w.b_f1, w.b_f2};
+    const int N[4] = {3 * D, D, FF, D}, K[4] = {D, D, D, FF};
+    if (w.mt[m] == 8) {
+        GemmQ8Params g;
+        g.M = M; g.wq = w.wq[m]; g.wd = w.wd[m]; g.N = N[m]; g.K = K[m]; g.bias = bias[m];
+        if (m == 0) { g.xq = io.xq; g.xd = io.xd; g.y = io.qkv; g.kv = kv; launch_gemm_q8(g, EPI_BIAS, s); }
+        if (m == 1) { g.xq = io.aq; g.xd = io.ad; g.resid = io.x; g.y = io.pre; launch_gemm_q8(g, EPI_RESID, s); }
+        if (m == 2) { g.xq = io.n1q; g.xd = io.n1d; g.yq = hq; g.yd = hd; launch_gemm_q8(g, EPI_RELU_Q8, s); }
+        if (m == 3) { g.xq = hq; g.xd = hd; g.resid = io.n1; g.y = io.pre; launch_gemm_q8(g, EPI_RESID, s); }
+        return;
+    }
+    GemmFxParams g;
+    g.M = M; g.w = w.wf[m]; g.wtype = w.mt[m] == 1 ? FX_F16 : FX_F32; g.N = N[m]; g.K = K[m]; g.bias = bias[m];
+    g.ldx = K[m];
+    if (m == 0) { g.x = io.x; g.y = io.qkv; g.kv = kv; launch_gemm_fx(g, FXE_BIAS, s); }
+    if (m == 1) { g.x = io.attn; g.resid = io.x; g.y = io.pre; launch_gemm_fx(g, FXE_RESID, s); }
+    if (m == 2) { g.x = io.n1; g.y = hf; launch_gemm_fx(g, FXE_RELU, s); }
+    if (m == 3) { g.x = hf; g.resid = io.n1; g.y = io.pre; launch_gemm_fx(g, FXE_RESID, s); }
 }
 
 // Admit n sequences into free slots: pages, slot state, repetition window, prefill.
@@ -822,7 +888,7 @@ int gsvcu_ctx::launch_step(cudaStream_t s, float* dump, int dump_row, const int*
     nk++;
     TRY(mark(1));
     const float scale = 1.0f / std::sqrt((float)HD);
-    if (fused && dense_ok && !dump) {
+    if (fused && dense_ok && all_q8 && !dump) {
         // fused layers for slots [s0, s0 + rows): QKV of layer 0, then per layer the page attention and
         // the cluster layer tail (merge, out, LN1, FFN1, FFN2, LN2, next layer's QKV), then the logits
         auto chain = [&](cudaStream_t cs, int s0, int rows) -> int {
@@ -890,36 +956,28 @@ int gsvcu_ctx::launch_step(cudaStream_t s, float* dump, int dump_row, const int*
         graph_kernels = nk;
         return GSVCU_OK;
     }
+    const LayerIO io{x, attn_f32, n1, xq, aq, n1q, xd, ad, n1d, qkv, pre};
     for (int li = 0; li < NL; li++) {
         const LayerW& w = L[li];
-        GemmQ8Params g;
-        g.xq = xq; g.xd = xd; g.M = M; g.wq = w.wq[0]; g.wd = w.wd[0]; g.N = 3 * D; g.K = D; g.bias = w.b_qkv; g.y = qkv;
-        g.kv.pool = pool; g.kv.kv_f32 = kv_f32; g.kv.n_layer = NL; g.kv.layer = li; g.kv.block_table = block_table;
-        g.kv.max_pages = max_pages; g.kv.st = st;
-        launch_gemm_q8(g, EPI_BIAS, s);
+        KvWrite kv;
+        kv.pool = pool; kv.kv_f32 = kv_f32; kv.n_layer = NL; kv.layer = li; kv.block_table = block_table;
+        kv.max_pages = max_pages; kv.st = st;
+        layer_gemm(li, 0, io, M, kv, s);
         TRY(mark(2));
         DecAttnParams a;
         a.q = qkv; a.q_stride = 3 * D; a.pool = pool; a.kv_f32 = kv_f32; a.n_layer = NL; a.layer = li;
         a.block_table = block_table; a.max_pages = max_pages; a.st = st; a.B = M; a.max_chunks = max_chunks;
-        a.scale = scale; a.out_q = aq; a.out_d = ad; a.out_f32 = dump ? attn_f32 : nullptr;
+        a.scale = scale; a.out_q = aq; a.out_d = ad; a.out_f32 = dump || w.mt[1] != 8 ? attn_f32 : nullptr;
         a.part = part; a.part_ml = part_ml_of(part, (size_t)max_slots * NH * max_chunks); a.err = att_err;
         nk += launch_decode_attention(a, s);
         TRY(mark(3));
-        GemmQ8Params o;
-        o.xq = aq; o.xd = ad; o.M = M; o.wq = w.wq[1]; o.wd = w.wd[1]; o.N = D; o.K = D; o.bias = w.b_out; o.resid = x; o.y = pre;
-        launch_gemm_q8(o, EPI_RESID, s);
+        layer_gemm(li, 1, io, M, KvWrite(), s);
         TRY(mark(4));
         launch_layernorm_q8(pre, M, w.n1w, w.n1b, n1, n1q, n1d, s);
         TRY(mark(5));
-        GemmQ8Params f1;
-        f1.xq = n1q; f1.xd = n1d; f1.M = M; f1.wq = w.wq[2]; f1.wd = w.wd[2]; f1.N = FF; f1.K = D; f1.bias = w.b_f1;
-        f1.yq = hq; f1.yd = hd;
-        launch_gemm_q8(f1, EPI_RELU_Q8, s);
+        layer_gemm(li, 2, io, M, KvWrite(), s);
         TRY(mark(6));
-        GemmQ8Params f2;
-        f2.xq = hq; f2.xd = hd; f2.M = M; f2.wq = w.wq[3]; f2.wd = w.wd[3]; f2.N = D; f2.K = FF; f2.bias = w.b_f2;
-        f2.resid = n1; f2.y = pre;
-        launch_gemm_q8(f2, EPI_RESID, s);
+        layer_gemm(li, 3, io, M, KvWrite(), s);
         TRY(mark(7));
         nk += 6;
         if (dump) {
@@ -1368,6 +1426,19 @@ int gsvcu_op_f32_gemm(gsvcu_ctx* ctx, const float* x_dev, int32_t M, const float
     return GSVCU_OK;
 }
 
+int gsvcu_op_fx_gemm(gsvcu_ctx* ctx, const float* x_dev, int32_t M, const void* w_dev, int32_t wtype, int32_t N,
+                     int32_t K, const float* bias_dev, float* y_dev) {
+    if (!ctx || !x_dev || !w_dev || !y_dev || M < 0 || N <= 0 || K <= 0 || K % 32 || (wtype != 0 && wtype != 1))
+        return GSVCU_ERR_ARG;
+    DeviceGuard g(ctx->device);
+    GemmFxParams p;
+    p.x = x_dev; p.ldx = K; p.M = M; p.w = w_dev; p.wtype = wtype == 1 ? FX_F16 : FX_F32; p.N = N; p.K = K;
+    p.bias = bias_dev; p.y = y_dev;
+    launch_gemm_fx(p, FXE_BIAS, ctx->stream);
+    CKC(ctx, cudaGetLastError());
+    return GSVCU_OK;
+}
+
 int gsvcu_op_decode_attention(gsvcu_ctx* ctx, const float* q_dev, int32_t q_stride, const void* pool_dev,
                               int32_t kv_dtype, int32_t n_layer, int32_t layer, const int32_t* block_table_dev,
                               int32_t max_pages, const int32_t* kvpos_dev, const int32_t* active_dev, int32_t B,
@@ -1574,7 +1645,7 @@ int gsvcu_set_fused_decode(gsvcu_ctx* ctx, int32_t mode) {
 }
 
 int gsvcu_fused_decode(const gsvcu_ctx* ctx) {
-    if (!ctx || !ctx->fused || !ctx->dense_ok) return 0;
+    if (!ctx || !ctx->fused || !ctx->dense_ok || !ctx->all_q8) return 0;   // float layer matrices: unfused step
     return ctx->two_groups ? 2 : 1;
 }
 

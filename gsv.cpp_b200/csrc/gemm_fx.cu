@@ -1,0 +1,146 @@
+// gemm_fx.cu -- GEMM over F32 / F16 weight matrices: the layer matrices of the exporter's default
+// (F32) and --f16 files (tools/export_gguf/export.py:48-54) and an F16 ar.predict.
+//
+// Arithmetic: ggml's F32 / F16 mul_mat (src/gsv_ar.cpp:244,260,262,263,266) in the order of its
+// FMA-vectorised dot (ggml_vec_dot_f32 / ggml_vec_dot_f16 built with -mavx2 -mfma: four 8-lane
+// float accumulators over steps of 32 values). For an F16 matrix the activations are first rounded
+// to F16 (round-to-nearest-even), as ggml converts src1 to the matrix's vec_dot_type. Chain c
+// (c = 0..31) accumulates w[k] * x[k] for k = c, c + 32, ... with one FMA per term; the 32 chain sums
+// are then added pairwise: chain c with c^16 (accumulators 0+2, 1+3), ^8 (0+1), ^4 (the two 128-bit
+// halves), ^1 and ^2 (the two horizontal adds). K is a multiple of 32.
+//
+// Mapping: lane c of a warp runs chain c, so every load of a warp is one contiguous 32-value row
+// segment. A warp owns 8 rows x 8 columns (64 chains per lane: each x value feeds 8 FMAs, each weight
+// 8); the pairwise fold is a transposing butterfly that halves the values a lane holds at each level
+// (32 + 16 + 8 + 4 + 2 shuffles for 64 outputs), after which each lane holds two finished outputs.
+// A CTA of 4 warps covers 16 rows x 16 columns.
+#include "kernels.h"
+
+namespace gsvcu {
+namespace {
+
+constexpr int FX_RW = 8, FX_CW = 8;              // warp tile: rows x columns
+constexpr int FX_WM = 2, FX_WN = 2;              // warps per CTA along rows / columns
+constexpr int FX_TM = FX_RW * FX_WM, FX_TN = FX_CW * FX_WN;
+constexpr int FX_NV = FX_RW * FX_CW;             // outputs per warp
+
+template <int WT>
+__device__ __forceinline__ float ld_w(const void* w, int i) {
+    if (WT == FX_F32) return __ldg((const float*)w + i);
+    return __half2float(__ldg((const __half*)w + i));
+}
+
+// One level of the pairwise fold over the first N values of every lane: lanes l and l^OFF hold the
+// same outputs' sums of chain groups l and l^OFF; lane l keeps the lower half of the outputs when bit
+// OFF of l is clear, the upper half otherwise, and receives its partner's sums for them.
+template <int OFF, int N>
+__device__ __forceinline__ void fold(float (&v)[FX_NV], int lane) {
+    const bool up = (lane & OFF) != 0;
+#pragma unroll
+    for (int i = 0; i < N / 2; i++) {
+        const float send = up ? v[i] : v[i + N / 2];
+        const float keep = up ? v[i + N / 2] : v[i];
+        v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, OFF));
+    }
+}
+
+// K/V column f (in [D, 3D)) of row n into its KV page: the layout and conversion of the Q8_0 GEMM's
+// epilogue (prefill rows by tok_slot / tok_pos, decode rows by the slot state).
+__device__ __forceinline__ void kv_store(const KvWrite& kv, int n, int f, float y) {
+    int slot, pos;
+    if (kv.tok_pos) {
+        slot = kv.tok_slot[n];
+        pos = kv.tok_pos[n];
+    } else {
+        if (!kv.st[n].decode_now) return;
+        slot = n;
+        pos = kv.st[n].kvpos;
+    }
+    const int kvsel = (f - D) >> 9, fh = (f - D) & (D - 1);
+    const int h = fh >> 5, dd = fh & 31;
+    const int page = kv.block_table[(size_t)slot * kv.max_pages + pos / PAGE];
+    const size_t e = ((((size_t)page * kv.n_layer + kv.layer) * 2 + kvsel) * NH + h) * (PAGE * HD) +
+                     (size_t)(pos % PAGE) * HD + dd;
+    if (kv.kv_f32) ((float*)kv.pool)[e] = y;
+    else ((__half*)kv.pool)[e] = __float2half_rn(y);
+}
+
+template <int WT, int EPI>
+__global__ void __launch_bounds__(128) k_gemm_fx(const GemmFxParams p) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.y * FX_TM + (warp / FX_WN) * FX_RW;
+    const int n0 = blockIdx.x * FX_TN + (warp % FX_WN) * FX_CW;
+    // rows / columns past the edge read the last valid one; their sums are never stored
+    int xo[FX_RW], wo[FX_CW];
+#pragma unroll
+    for (int r = 0; r < FX_RW; r++) xo[r] = min(m0 + r, p.M - 1) * p.ldx + lane;
+#pragma unroll
+    for (int j = 0; j < FX_CW; j++) wo[j] = min(n0 + j, p.N - 1) * p.K + lane;
+    float acc[FX_NV];
+#pragma unroll
+    for (int i = 0; i < FX_NV; i++) acc[i] = 0.0f;
+    griddep_wait();
+    griddep_launch();
+#pragma unroll 2
+    for (int k0 = 0; k0 < p.K; k0 += 32) {
+        float xv[FX_RW], wv[FX_CW];
+#pragma unroll
+        for (int r = 0; r < FX_RW; r++) {
+            const float t = p.x[xo[r] + k0];
+            xv[r] = WT == FX_F16 ? __half2float(__float2half_rn(t)) : t;
+        }
+#pragma unroll
+        for (int j = 0; j < FX_CW; j++) wv[j] = ld_w<WT>(p.w, wo[j] + k0);
+#pragma unroll
+        for (int r = 0; r < FX_RW; r++)
+#pragma unroll
+            for (int j = 0; j < FX_CW; j++) acc[r * FX_CW + j] = fmaf(wv[j], xv[r], acc[r * FX_CW + j]);
+    }
+    fold<16, 64>(acc, lane);
+    fold<8, 32>(acc, lane);
+    fold<4, 16>(acc, lane);
+    fold<1, 8>(acc, lane);
+    fold<2, 4>(acc, lane);
+    // acc[e], e = 0, 1: output index 32 b4 + 16 b3 + 8 b2 + 4 b0 + 2 b1 + e (b = the lane's bits),
+    // i.e. row 4 b4 + 2 b3 + b2 and column 4 b0 + 2 b1 + e of the warp tile
+    const int m = m0 + ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+    const int nb = n0 + (lane & 1) * 4 + ((lane >> 1) & 1) * 2;
+    if (m >= p.M) return;
+#pragma unroll
+    for (int e = 0; e < 2; e++) {
+        const int n = nb + e;
+        if (n >= p.N) continue;
+        const float bias = p.bias ? p.bias[n] : 0.0f;
+        if (EPI == FXE_BIAS) {
+            const float y = __fadd_rn(acc[e], bias);
+            if (n < (p.n_store ? p.n_store : p.N)) p.y[(size_t)m * (p.ldy ? p.ldy : p.N) + n] = y;
+            if (p.kv.pool && n >= D) kv_store(p.kv, m, n, y);
+        } else if (EPI == FXE_RESID) {
+            const float r = p.resid[(size_t)m * p.N + n];
+            p.y[(size_t)m * p.N + n] = __fadd_rn(__fadd_rn(r, acc[e]), bias);
+        } else {   // FXE_RELU
+            const float h = __fadd_rn(acc[e], bias);
+            p.y[(size_t)m * p.N + n] = h > 0.0f ? h : 0.0f;
+        }
+    }
+}
+
+template <int WT>
+void launch_wt(const GemmFxParams& p, int epi, cudaStream_t s) {
+    const dim3 grid((p.N + FX_TN - 1) / FX_TN, (p.M + FX_TM - 1) / FX_TM), block(128);
+    switch (epi) {
+        case FXE_BIAS: launch_pdl(k_gemm_fx<WT, FXE_BIAS>, grid, block, 0, s, p); break;
+        case FXE_RESID: launch_pdl(k_gemm_fx<WT, FXE_RESID>, grid, block, 0, s, p); break;
+        default: launch_pdl(k_gemm_fx<WT, FXE_RELU>, grid, block, 0, s, p); break;
+    }
+}
+
+}  // namespace
+
+void launch_gemm_fx(const GemmFxParams& p, int epi, cudaStream_t s) {
+    if (p.M <= 0 || p.N <= 0) return;
+    if (p.wtype == FX_F16) launch_wt<FX_F16>(p, epi, s);
+    else launch_wt<FX_F32>(p, epi, s);
+}
+
+}  // namespace gsvcu

@@ -67,6 +67,28 @@ cudaError_t gemm_q8_init_device();
 // Host-side repack of raw GGUF Q8_0 blocks [N][K/32] x 34 B into the two planes.
 void pack_q8_0_host(const uint8_t* raw, int N, int K, uint8_t* wq_out, uint16_t* wd_out);
 
+// ------------------------------------------------------------ F32 / F16 weight GEMM (gemm_fx.cu)
+// y[m][n] = sum_k w[n][k] * x(m, k) for F32 / F16 layer matrices and an F16 predict, in the order of
+// ggml's FMA-vectorised dot: x rounded to F16 for an F16 w, 32 float FMA chains (chain c takes
+// k = c, c + 32, ...) added pairwise as chains c^16, ^8, ^4, ^1, ^2. K % 32 == 0; w row-major [N][K].
+enum { FX_F32 = 0, FX_F16 = 1 };
+enum { FXE_BIAS = 0, FXE_RESID = 1, FXE_RELU = 2 };   // y = acc + b (+ K/V store); (r + acc) + b; relu(acc + b)
+struct GemmFxParams {
+    const float* x = nullptr;
+    int ldx = 0;
+    int M = 0;
+    const void* w = nullptr;
+    int wtype = FX_F32;
+    int N = 0, K = 0;
+    const float* bias = nullptr;
+    const float* resid = nullptr;   // FXE_RESID: [M][N]
+    float* y = nullptr;             // [M][ldy] (FXE_BIAS) or [M][N]
+    int ldy = 0;                    // FXE_BIAS: row stride of y (0: N)
+    int n_store = 0;                // FXE_BIAS: columns of y stored (0: N)
+    KvWrite kv;                     // FXE_BIAS: optional K/V store of columns [D, 3D)
+};
+void launch_gemm_fx(const GemmFxParams& p, int epi, cudaStream_t s);
+
 // ------------------------------------------------------------ F32 GEMM, double accumulation
 // y[m][n] = (float) sum_k (double)w[n][k] * (double)x(m, k)  (+ add[m][n]); x(m,k) = x[m*ldx + k], or,
 // for the BERT projection, gathered from per-sequence [1024][T] feature blocks with an implicit

@@ -27,16 +27,22 @@ class Dims:
 
 
 def write_model(path: str, seed: int = 0, dims: Dims | None = None, mat_type: str = "q8_0",
-                ln_noise: float = 0.02, predict_type: str = "f32", emb_type: str = "f32") -> str:
-    """predict_type "q8_0" stores ar.predict as Q8_0 (the exporter's --spec predict=q8_0); emb_type
-    "f16" stores the text / audio embeddings as F16 (--spec emb=f16)."""
+                ln_noise: float = 0.02, predict_type: str = "f32", emb_type: str = "f32",
+                ffn_type: str | None = None) -> str:
+    """mat_type is the type of the attention matrices (the exporter's --spec attn=...) and, unless
+    ffn_type is given, of the FFN matrices (--spec ffn=...): "q8_0", "f16" or "f32". predict_type
+    "q8_0" / "f16" stores ar.predict as Q8_0 / F16 (--spec predict=...); emb_type "f16" stores the
+    text / audio embeddings as F16 (--spec emb=f16). The exporter's --f16 preset is
+    mat_type="f16", predict_type="f16", emb_type="f16"; its default (no flags) is mat_type="f32"."""
     import gguf
 
     d = dims or Dims()
     rng = np.random.default_rng(seed)
     D, FF = d.D, 4 * d.D
-    types = {"q8_0": gguf.GGMLQuantizationType.Q8_0, "f32": gguf.GGMLQuantizationType.F32}
+    types = {"q8_0": gguf.GGMLQuantizationType.Q8_0, "f32": gguf.GGMLQuantizationType.F32,
+             "f16": gguf.GGMLQuantizationType.F16}
     qt = types[mat_type]
+    ft = types[ffn_type or mat_type]
 
     def n(*shape, s=0.02):
         return (rng.standard_normal(shape, dtype=np.float32) * np.float32(s)).astype(np.float32)
@@ -75,9 +81,9 @@ def write_model(path: str, seed: int = 0, dims: Dims | None = None, mat_type: st
         add(f"{p}.out_b", n(D))
         add(f"{p}.norm1_w", 1.0 + n(D, s=ln_noise))
         add(f"{p}.norm1_b", n(D, s=ln_noise))
-        add(f"{p}.ffn1_w", n(FF, D), qt)
+        add(f"{p}.ffn1_w", n(FF, D), ft)
         add(f"{p}.ffn1_b", n(FF))
-        add(f"{p}.ffn2_w", n(D, FF), qt)
+        add(f"{p}.ffn2_w", n(D, FF), ft)
         add(f"{p}.ffn2_b", n(D))
         add(f"{p}.norm2_w", 1.0 + n(D, s=ln_noise))
         add(f"{p}.norm2_b", n(D, s=ln_noise))
@@ -89,15 +95,16 @@ def write_model(path: str, seed: int = 0, dims: Dims | None = None, mat_type: st
 
 
 def cached_model(cache_dir: str, seed: int = 0, n_layer: int = 24, mat_type: str = "q8_0",
-                 predict_type: str = "f32", emb_type: str = "f32") -> str:
+                 predict_type: str = "f32", emb_type: str = "f32", ffn_type: str | None = None) -> str:
     """Write (once) and return the path of a synthetic model in cache_dir."""
     os.makedirs(cache_dir, exist_ok=True)
     suffix = ("" if predict_type == "f32" else f"_p{predict_type}") + ("" if emb_type == "f32" else f"_e{emb_type}")
+    suffix += "" if ffn_type in (None, mat_type) else f"_f{ffn_type}"
     path = os.path.join(cache_dir, f"gsv_ar_synth_s{seed}_l{n_layer}_{mat_type}{suffix}.gguf")
     if not os.path.exists(path):
         tmp = path + f".tmp{os.getpid()}"
         write_model(tmp, seed=seed, dims=Dims(NL=n_layer), mat_type=mat_type, predict_type=predict_type,
-                    emb_type=emb_type)
+                    emb_type=emb_type, ffn_type=ffn_type)
         os.replace(tmp, path)
     return path
 

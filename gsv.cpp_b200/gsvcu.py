@@ -75,6 +75,7 @@ SIGNATURES = {
     "gsvcu_op_q8_gemm": ([_P, _P, _P, _I, _P, _P, _I, _I, _P, _P, _I, _P, _P, _P], C.c_int),
     "gsvcu_op_layernorm_q8": ([_P, _P, _I, _P, _P, _P, _P, _P], C.c_int),
     "gsvcu_op_f32_gemm": ([_P, _P, _I, _P, _I, _I, _P, _P], C.c_int),
+    "gsvcu_op_fx_gemm": ([_P, _P, _I, _P, _I, _I, _I, _P, _P], C.c_int),
     "gsvcu_op_decode_attention": ([_P, _P, _I, _P, _I, _I, _I, _P, _I, _P, _P, _I, _P, _P, _P], C.c_int),
     "gsvcu_op_prefill_attention": ([_P, _P, _I, _P, _P, _P, _P, _P, _P], C.c_int),
     "gsvcu_op_sample": ([_P, _P, _I, _I, _I, C.POINTER(SamplerCfg), _P, _P, _I, _P, _P, _P], C.c_int),
@@ -315,6 +316,9 @@ class Context:
 
     def op_f32_gemm(self, x, M, w, N, K, add, y):
         self._check(self.lib.gsvcu_op_f32_gemm(self.h, _ptr(x), M, _ptr(w), N, K, _ptr(add), _ptr(y)))
+
+    def op_fx_gemm(self, x, M, w, wtype, N, K, bias, y):
+        self._check(self.lib.gsvcu_op_fx_gemm(self.h, _ptr(x), M, _ptr(w), wtype, N, K, _ptr(bias), _ptr(y)))
 
     def op_decode_attention(self, q, q_stride, pool, kv_dtype, n_layer, layer, block_table, max_pages, kvpos, active,
                             B, out_q, out_d, out_f32=None):

@@ -73,9 +73,10 @@ void gsvcu_destroy(gsvcu_ctx* ctx);
 const char* gsvcu_last_error(const gsvcu_ctx* ctx);
 
 /* Load an AR GGUF file (replaces gsv_ar::load, reference src/gsv_ar.cpp:490-705): tensor names of
- * tools/export_gguf/convert_ar.py:106-130; attention/FFN matrices must be Q8_0, embeddings,
- * bert_proj, predict, norms and biases F32 (src/gsv_ar.cpp:632-637). Weights are repacked into
- * tensor-core fragment order on the device. */
+ * tools/export_gguf/convert_ar.py:106-130. Attention / FFN matrices Q8_0, F32 or F16 (the exporter's
+ * --spec attn=.., ffn=..; ffn1_w and ffn2_w of a layer both Q8_0 or both F32 / F16), predict F32, Q8_0
+ * or F16, embeddings F32 or F16 (widened on load), bert_proj, norms and biases F32. Q8_0 matrices are
+ * repacked into tensor-core fragment order on the device; F32 / F16 matrices are kept as stored. */
 int gsvcu_load_gguf(gsvcu_ctx* ctx, const char* path);
 int gsvcu_get_hparams(const gsvcu_ctx* ctx, gsvcu_hparams* out);
 
@@ -190,6 +191,13 @@ int gsvcu_op_layernorm_q8(gsvcu_ctx* ctx, const float* v_dev, int32_t rows, cons
 int gsvcu_op_f32_gemm(gsvcu_ctx* ctx, const float* x_dev, int32_t M, const float* w_dev, int32_t N, int32_t K,
                       const float* add_dev, float* y_dev);
 
+/* Y[M][N] = W[N][K] . X[M][K]^T (+ bias[N], may be NULL) for an F32 (wtype 0) or F16 (wtype 1) layer
+ * matrix (ggml F32 / F16 mul_mat, src/gsv_ar.cpp:244,260,262,263) in the order of ggml's FMA-vectorised
+ * dot: X rounded to F16 for an F16 W, 32 float FMA chains (chain c over k = c, c + 32, ...) added
+ * pairwise as chains c^16, ^8, ^4, ^1, ^2. K a multiple of 32. */
+int gsvcu_op_fx_gemm(gsvcu_ctx* ctx, const float* x_dev, int32_t M, const void* w_dev, int32_t wtype, int32_t N,
+                     int32_t K, const float* bias_dev, float* y_dev);
+
 /* Split-KV decode attention over a paged KV pool, 16 heads x 32 dims (flash_attn_ext over the cache,
  * src/gsv_ar.cpp:402-405).
  *   q_dev [B][q_stride] f32 (head h at h*32), pool_dev KV pages, block_table_dev [B][max_pages] int32,
@@ -261,7 +269,8 @@ int gsvcu_step_profile(gsvcu_ctx* ctx, int32_t n_steps, float* ms_by_class, int6
  * cluster; mode 2: the same with >= 32 slots (a multiple of 32) split into two groups on forked
  * streams, so one group's layer tail may overlap the other's attention (measured on B200: no gain,
  * the clusters wait for whole SMs); mode 0: one kernel per operation. Results are identical. Returns GSVCU_OK (GSVCU_ERR_ARG for
- * another mode); gsvcu_fused_decode returns the mode in use (0 when the cluster does not fit). */
+ * another mode); gsvcu_fused_decode returns the mode in use (0 when the cluster does not fit, or
+ * when the model has F32 / F16 layer matrices: the fused tail reads Q8_0 weights only). */
 int gsvcu_set_fused_decode(gsvcu_ctx* ctx, int32_t mode);
 int gsvcu_fused_decode(const gsvcu_ctx* ctx);
 /* Number of kernels this context has launched (graph replays count their kernels). */

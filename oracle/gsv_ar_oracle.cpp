@@ -15,9 +15,14 @@
 //     id = 1/d, roundf, d stored as fp16) -- pinned bit-exactly against gguf-py's Q8_0
 //     quantizer, which documents bit-exactness with ggml-quants.c; then per 32-block integer dot,
 //     accumulated in float block by block as sumf = fma((float)sumi, d_w*d_x, sumf).
-//   * F32 mul_mat / F32 vec_dot: products exact in double, accumulated in double, rounded once
-//     (ggml_vec_dot_f32; its scalar path rounds each product to float, its FMA-vectorised path
-//     accumulates in float: both within roundings of this).
+//   * F32 mul_mat of ar.predict and of the BERT projection: products exact in double, accumulated
+//     in double, rounded once (ggml_vec_dot_f32; its scalar path rounds each product to float, its
+//     FMA-vectorised path accumulates in float: both within roundings of this).
+//   * F32 / F16 layer matrices and an F16 ar.predict: ggml's FMA-vectorised dot (-mavx2 -mfma;
+//     ggml_vec_dot_f32 / ggml_vec_dot_f16 with 4 accumulators x 8 float lanes): src1 rounded to F16
+//     for an F16 matrix (ggml's vec_dot_type), 32 float FMA chains (chain c takes k = c, c+32, ...),
+//     folded as accumulators 0+2, 1+3, then 0+1, then the two 128-bit halves, then two horizontal
+//     adds -- i.e. chains c and c^16, ^8, ^4, ^1, ^2 added pairwise in that order (vec_dot_canon).
 //   * flash_attn_ext (F32 K/V), prefill rows: scores s = (float)(double sum of the exact products
 //     q_e*k_e) * scale (the products are exact as in the FMA-vectorised ggml_vec_dot_f32 of the
 //     -mavx2 -mfma build), masked keys skipped; softmax(s) V evaluated in double (double exp, double
@@ -164,17 +169,43 @@ inline int nthreads() {
 
 enum { T_F32 = 0, T_F16 = 1, T_Q8_0 = 8 };
 
-// A weight matrix [N][K] (torch [out,in] == ggml ne0=in), either F32 or Q8_0 raw GGUF blocks.
+// A weight matrix [N][K] (torch [out,in] == ggml ne0=in): F32 or F16 (widened to f), or Q8_0 raw
+// GGUF blocks. canon: evaluated by vec_dot_canon (xf16: with src1 rounded to F16 first).
 struct Mat {
     int type = T_F32;
     int64_t N = 0, K = 0;
+    bool canon = false, xf16 = false;
     std::vector<float> f;
     std::vector<uint8_t> q;
 };
 
+// ggml's AVX2 F32/F16 dot in float (K a multiple of 32): chain c accumulates w[k]*x[k] for
+// k = c, c+32, ... with FMA; the 32 chain sums are folded pairwise, c with c^16, then ^8, ^4, ^1, ^2
+// (the accumulator / lane reduction of the 4 x 8-lane vector sums).
+inline float vec_dot_canon(int64_t K, const float* w, const float* x) {
+    float s[32] = {};
+    for (int64_t k0 = 0; k0 < K; k0 += 32)
+        for (int c = 0; c < 32; c++) s[c] = std::fmaf(w[k0 + c], x[k0 + c], s[c]);
+    for (int off : {16, 8, 4, 1, 2})
+        for (int c = 0; c < 32; c++)
+            if (!(c & off)) s[c] = s[c] + s[c | off];
+    return s[0];
+}
+
 // Y[M][N] = mul_mat(W, X) for X [M][K]   (src/gsv_ar.cpp:244,260,262,263; ggml mul_mat)
 void mul_mat(const Mat& W, const float* X, int64_t M, float* Y) {
     const int64_t N = W.N, K = W.K;
+    if (W.canon) {   // F32 / F16 layer matrices, F16 predict
+        std::vector<float> xr(X, X + M * K);
+        if (W.xf16)
+            for (float& v : xr) v = round_f16(v);
+        #pragma omp parallel for num_threads(nthreads()) schedule(static)
+        for (int64_t n = 0; n < N; n++) {
+            const float* w = W.f.data() + n * K;
+            for (int64_t m = 0; m < M; m++) Y[m * N + n] = vec_dot_canon(K, w, xr.data() + m * K);
+        }
+        return;
+    }
     if (W.type == T_Q8_0) {
         std::vector<uint8_t> xq((size_t)M * (K / QK) * Q8_BYTES);
         #pragma omp parallel for num_threads(nthreads()) schedule(static)
@@ -442,13 +473,24 @@ struct orc_model {
 
 namespace {
 
-bool set_mat(Mat& m, int type, const void* data, int64_t nbytes, int64_t N, int64_t K, std::string& err, const char* name) {
+// canon_f32: an F32 matrix is a layer matrix (vec_dot_canon) rather than the predict / BERT
+// projection (vec_dot_f32). F16 matrices are always evaluated by vec_dot_canon.
+bool set_mat(Mat& m, int type, const void* data, int64_t nbytes, int64_t N, int64_t K, std::string& err, const char* name,
+             bool canon_f32 = false) {
     m.type = type;
     m.N = N;
     m.K = K;
+    m.canon = m.xf16 = false;
     if (type == T_F32) {
         if (nbytes != N * K * 4) { err = std::string("bad size for ") + name; return false; }
         m.f.assign((const float*)data, (const float*)data + N * K);
+        m.canon = canon_f32 && K % 32 == 0;
+    } else if (type == T_F16) {
+        if (K % 32 || nbytes != N * K * 2) { err = std::string("bad size for ") + name; return false; }
+        m.f.resize((size_t)(N * K));
+        const uint16_t* h = (const uint16_t*)data;
+        for (int64_t i = 0; i < N * K; i++) m.f[(size_t)i] = f16_to_f32(h[i]);
+        m.canon = m.xf16 = true;
     } else if (type == T_Q8_0) {
         if (K % QK || nbytes != N * (K / QK) * Q8_BYTES) { err = std::string("bad size for ") + name; return false; }
         m.q.assign((const uint8_t*)data, (const uint8_t*)data + nbytes);
@@ -699,12 +741,13 @@ void orc_fp32_to_fp16(const float* x, uint16_t* y, int64_t n) { for (int64_t i =
 void orc_fp16_to_fp32(const uint16_t* x, float* y, int64_t n) { for (int64_t i = 0; i < n; i++) y[i] = f16_to_f32(x[i]); }
 void orc_quantize_q8_0(const float* x, int64_t n, uint8_t* blocks) { quantize_q8_0(x, n, blocks); }
 
-// Y[M][N] = W[N][K] . X[M][K]^T with W raw Q8_0 blocks (type 8) or F32 (type 0).
-int orc_mul_mat(int type, const void* W, int64_t N, int64_t K, const float* X, int64_t M, float* Y) {
+// Y[M][N] = W[N][K] . X[M][K]^T with W raw Q8_0 blocks (type 8), F32 (type 0) or F16 (type 1);
+// layer != 0: W is a layer matrix (an F32 W is then evaluated like an F16 one, by vec_dot_canon).
+int orc_mul_mat(int type, const void* W, int64_t N, int64_t K, const float* X, int64_t M, float* Y, int layer) {
     Mat w;
     std::string err;
-    const int64_t nbytes = type == T_Q8_0 ? N * (K / QK) * Q8_BYTES : N * K * 4;
-    if (!set_mat(w, type, W, nbytes, N, K, err, "W")) return -1;
+    const int64_t nbytes = type == T_Q8_0 ? N * (K / QK) * Q8_BYTES : N * K * (type == T_F16 ? 2 : 4);
+    if (!set_mat(w, type, W, nbytes, N, K, err, "W", layer != 0)) return -1;
     mul_mat(w, X, M, Y);
     return 0;
 }
@@ -803,10 +846,10 @@ int orc_model_set(orc_model* m, const char* name, int type, const void* data, in
     if (std::sscanf(name, "transformer.block%d.%63s", &li, field) == 2 && li >= 0 && li < m->NL) {
         orc_layer& L = m->L[li];
         std::string f(field);
-        if (f == "qkv_w") return set_mat(L.qkv_w, type, data, nbytes, 3 * D, D, m->err, name) ? 0 : -1;
-        if (f == "out_w") return set_mat(L.out_w, type, data, nbytes, D, D, m->err, name) ? 0 : -1;
-        if (f == "ffn1_w") return set_mat(L.f1w, type, data, nbytes, FF, D, m->err, name) ? 0 : -1;
-        if (f == "ffn2_w") return set_mat(L.f2w, type, data, nbytes, D, FF, m->err, name) ? 0 : -1;
+        if (f == "qkv_w") return set_mat(L.qkv_w, type, data, nbytes, 3 * D, D, m->err, name, true) ? 0 : -1;
+        if (f == "out_w") return set_mat(L.out_w, type, data, nbytes, D, D, m->err, name, true) ? 0 : -1;
+        if (f == "ffn1_w") return set_mat(L.f1w, type, data, nbytes, FF, D, m->err, name, true) ? 0 : -1;
+        if (f == "ffn2_w") return set_mat(L.f2w, type, data, nbytes, D, FF, m->err, name, true) ? 0 : -1;
         if (f == "qkv_b") return set_vec(L.qkv_b, type, data, nbytes, 3 * D, m->err, name) ? 0 : -1;
         if (f == "out_b") return set_vec(L.out_b, type, data, nbytes, D, m->err, name) ? 0 : -1;
         if (f == "ffn1_b") return set_vec(L.f1b, type, data, nbytes, FF, m->err, name) ? 0 : -1;

@@ -34,7 +34,7 @@ def _load():
     lib.orc_fp32_to_fp16.argtypes = [_f32p, _u16p, C.c_int64]
     lib.orc_fp16_to_fp32.argtypes = [_u16p, _f32p, C.c_int64]
     lib.orc_quantize_q8_0.argtypes = [_f32p, C.c_int64, _u8p]
-    lib.orc_mul_mat.argtypes = [C.c_int, C.c_void_p, C.c_int64, C.c_int64, _f32p, C.c_int64, _f32p]
+    lib.orc_mul_mat.argtypes = [C.c_int, C.c_void_p, C.c_int64, C.c_int64, _f32p, C.c_int64, _f32p, C.c_int]
     lib.orc_mul_mat.restype = C.c_int
     lib.orc_ln_affine.argtypes = [_f32p, C.c_void_p, C.c_void_p, _f32p, _f32p, C.c_int64, C.c_int64, C.c_float, _f32p]
     lib.orc_add_act.argtypes = [_f32p, _f32p, C.c_int64, C.c_int64, C.c_int, _f32p]
@@ -104,13 +104,14 @@ def quantize_q8_0(x: np.ndarray) -> np.ndarray:
     return out
 
 
-def mul_mat(w: np.ndarray, wtype: int, N: int, K: int, x: np.ndarray) -> np.ndarray:
-    """Y[M][N] = W[N][K] . X[M][K]^T with ggml CPU semantics (wtype 8 = raw Q8_0 bytes, 0 = F32)."""
+def mul_mat(w: np.ndarray, wtype: int, N: int, K: int, x: np.ndarray, layer: bool = False) -> np.ndarray:
+    """Y[M][N] = W[N][K] . X[M][K]^T with ggml CPU semantics (wtype 8 = raw Q8_0 bytes, 0 = F32,
+    1 = F16). layer: W is a layer matrix, so an F32 W takes the FMA-vectorised order of an F16 one."""
     x = np.ascontiguousarray(x, dtype=np.float32)
     M = x.size // K
     y = np.empty((M, N), np.float32)
     w = np.ascontiguousarray(w)
-    if lib().orc_mul_mat(wtype, w.ctypes.data, N, K, x, M, y):
+    if lib().orc_mul_mat(wtype, w.ctypes.data, N, K, x, M, y, int(layer)):
         raise ValueError("orc_mul_mat failed")
     return y
 

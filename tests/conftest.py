@@ -53,3 +53,35 @@ def cosine(a, b):
     a = np.asarray(a, np.float64).ravel()
     b = np.asarray(b, np.float64).ravel()
     return float(a @ b / max(np.linalg.norm(a) * np.linalg.norm(b), 1e-30))
+
+
+def gguf_retyped_copy(src, dst, retype):
+    """Rewrite a GGUF file with tensor `name` stored as ggml type retype[name] (its values converted
+    through float32: exact when widening to F32)."""
+    import gguf
+    F32, F16 = gguf.GGMLQuantizationType.F32, gguf.GGMLQuantizationType.F16
+    rd = gguf.GGUFReader(src)
+    w = gguf.GGUFWriter(dst, str(rd.fields["general.architecture"].contents()))
+    for f in rd.fields.values():
+        if f.name.startswith("ar."):
+            if f.types[0] == gguf.GGUFValueType.UINT32:
+                w.add_uint32(f.name, int(f.contents()))
+            else:
+                w.add_float32(f.name, float(f.contents()))
+    for t in rd.tensors:
+        data = np.array(t.data)
+        if t.name in retype:
+            arr, ty = gguf.quants.dequantize(data, t.tensor_type).astype(np.float32), retype[t.name]
+            if ty == F32:
+                w.add_tensor(t.name, arr, raw_dtype=F32)
+            elif ty == F16:
+                w.add_tensor(t.name, arr.astype(np.float16), raw_dtype=F16)
+            else:
+                w.add_tensor(t.name, gguf.quants.quantize(arr, ty), raw_dtype=ty)
+        else:
+            w.add_tensor(t.name, data, raw_dtype=t.tensor_type)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    return dst

@@ -48,21 +48,39 @@ def test_inspect_rejects_bad_files(model_small, model_f32_small, tmp_path):
     hdr = tmp_path / "hdr.gguf"
     hdr.write_bytes(data[:40])
     assert gsvcu.inspect_gguf(str(hdr))[0] == -4
-    # attention/FFN matrices must be Q8_0 (F32 matrices are a ggml option this build does not run)
+    # layer matrices Q8_0, F32 or F16: F32 matrices load
     rc, _, msg = gsvcu.inspect_gguf(model_f32_small)
-    assert rc == -5 and "expected 8" in msg
+    assert rc == gsvcu.OK, msg
 
 
-@pytest.mark.parametrize("predict_type,emb_type", [("q8_0", "f32"), ("f32", "f16")])
-def test_inspect_export_formats(predict_type, emb_type):
-    """A Q8_0 predict matrix (exporter --spec predict=q8_0) and F16 embeddings (--spec emb=f16) are
-    accepted (GPU parity: tests/test_gpu_model.py::test_export_formats_match_oracle)."""
+@pytest.mark.parametrize("mat_type,ffn_type,predict_type,emb_type", [
+    ("q8_0", "q8_0", "q8_0", "f32"), ("q8_0", "q8_0", "f32", "f16"), ("f16", "f16", "f16", "f16"),
+    ("f32", "f32", "f32", "f32"), ("q8_0", "f16", "f32", "f32"), ("f16", "q8_0", "f32", "f32")])
+def test_inspect_export_formats(mat_type, ffn_type, predict_type, emb_type):
+    """The exporter's formats: Q8_0 / F16 predict, F16 embeddings, F32 / F16 attention and FFN matrices and
+    mixed attn / ffn groups are accepted (GPU parity: tests/test_gpu_model.py::
+    test_export_formats_match_oracle)."""
     import gsv_synth as S
     from conftest import MODEL_CACHE
-    rc, hp, msg = gsvcu.inspect_gguf(S.cached_model(MODEL_CACHE, seed=9, n_layer=2, predict_type=predict_type,
-                                                    emb_type=emb_type))
+    rc, hp, msg = gsvcu.inspect_gguf(S.cached_model(MODEL_CACHE, seed=9, n_layer=2, mat_type=mat_type,
+                                                    predict_type=predict_type, emb_type=emb_type,
+                                                    ffn_type=ffn_type))
     assert rc == gsvcu.OK, msg
     assert hp.vocab_size == 1025
+
+
+def test_inspect_rejects_unsupported_matrix_types(model_small, tmp_path):
+    """ffn1_w and ffn2_w of a layer are one group (Q8_0, or F32 / F16); other ggml types (K-quants,
+    Q4 / Q5, BF16) are refused with the tensor named."""
+    import gguf
+    from conftest import gguf_retyped_copy
+    T = gguf.GGMLQuantizationType
+    mixed = gguf_retyped_copy(model_small, str(tmp_path / "mixed.gguf"), {"transformer.block1.ffn2_w": T.F32})
+    rc, _, msg = gsvcu.inspect_gguf(mixed)
+    assert rc == -5 and "transformer.block1.ffn1_w / ffn2_w" in msg
+    q4 = gguf_retyped_copy(model_small, str(tmp_path / "q4.gguf"), {"transformer.block0.out_w": T.Q4_0})
+    rc, _, msg = gsvcu.inspect_gguf(q4)
+    assert rc == -5 and "transformer.block0.out_w has ggml type 2" in msg
 
 
 def test_inspect_missing_tensor(tmp_path):

@@ -381,14 +381,26 @@ def test_cpp_dropin_class(gctx, model_full, tmp_path):
     assert (lines[3]["hidden"], lines[3]["vocab"], lines[3]["eos"]) == (512, 1025, 1024)
 
 
-@pytest.mark.parametrize("predict_type,emb_type", [("q8_0", "f32"), ("f32", "f16")])
-def test_export_formats_match_oracle(predict_type, emb_type):
-    """Exporter formats beyond the default: a Q8_0 predict matrix (--spec predict=q8_0: logits by the Q8_0
-    GEMM over the Q8_0-quantized rows, as ggml's Q8_0 mul_mat) and F16 embeddings (--spec emb=f16,
-    widened to F32 on load). A teacher-forced decode trace (fused and unfused steps) equals the oracle
-    bit for bit."""
+EXPORT_FORMATS = [   # (attention matrices, FFN matrices, predict, embeddings)
+    ("q8_0", "q8_0", "q8_0", "f32"),   # --spec predict=q8_0
+    ("q8_0", "q8_0", "f32", "f16"),    # --spec emb=f16
+    ("f16", "f16", "f16", "f16"),      # --f16 (attn=f16,ffn=f16,predict=f16,emb=f16)
+    ("f32", "f32", "f32", "f32"),      # no flags: F32 matrices
+    ("q8_0", "f16", "f32", "f32"),     # --spec attn=q8_0,ffn=f16
+    ("f16", "q8_0", "f32", "f32"),     # --spec attn=f16,ffn=q8_0
+]
+
+
+@pytest.mark.parametrize("mat_type,ffn_type,predict_type,emb_type", EXPORT_FORMATS)
+def test_export_formats_match_oracle(mat_type, ffn_type, predict_type, emb_type):
+    """The exporter's formats besides --q8: Q8_0 / F16 predict (logits by the Q8_0 GEMM over Q8_0 rows, or
+    by the F16 dot), F16 embeddings (widened on load), F32 / F16 attention and FFN matrices (ggml's
+    FMA-vectorised F32 / F16 dot) and mixes of the attn / ffn groups. A teacher-forced decode trace
+    (fused and unfused steps; float matrices always run unfused) equals the oracle bit for bit, and so
+    does a sampled generate through the graph-captured decode step."""
     import gsvcu
-    model = S.cached_model(MODEL_CACHE, seed=9, n_layer=2, predict_type=predict_type, emb_type=emb_type)
+    model = S.cached_model(MODEL_CACHE, seed=9, n_layer=2, mat_type=mat_type, predict_type=predict_type,
+                           emb_type=emb_type, ffn_type=ffn_type)
     orc9 = O.OracleModel(model)
     c = gsvcu.Context(0)
     try:
@@ -403,5 +415,12 @@ def test_export_formats_match_oracle(predict_type, emb_type):
         unf = c.debug_trace(reqs, forced)
         c.set_fused_decode(1)
         assert np.array_equal(unf.view(np.uint32), ref.view(np.uint32))
+        assert c.fused_decode() == (1 if mat_type == ffn_type == "q8_0" else 0)
+        seeds = [31, 32, 33, 34, 35]
+        got, glens = c.generate(reqs, seeds=seeds, max_steps=40)
+        exp, elens = orc9.generate(reqs, seeds=seeds, max_steps=40, kv_f16=True)
+        assert glens == elens
+        for b in range(5):
+            assert np.array_equal(got[b], exp[b]), b
     finally:
         c.close()

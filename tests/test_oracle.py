@@ -17,7 +17,7 @@ import pytest
 
 import gsv_synth as S
 import oracle as O
-from conftest import rel_l2
+from conftest import gguf_retyped_copy, rel_l2
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
 
@@ -243,36 +243,13 @@ def test_oracle_batch_equals_single(model_small):
         assert np.array_equal(tb[b], ts[0])
 
 
-def _gguf_widened_copy(src, dst, names):
-    """Rewrite a GGUF file with the tensors in `names` stored as F32 holding their exact values."""
-    import gguf
-    rd = gguf.GGUFReader(src)
-    w = gguf.GGUFWriter(dst, str(rd.fields["general.architecture"].contents()))
-    for f in rd.fields.values():
-        if f.name.startswith("ar."):
-            if f.types[0] == gguf.GGUFValueType.UINT32:
-                w.add_uint32(f.name, int(f.contents()))
-            else:
-                w.add_float32(f.name, float(f.contents()))
-    for t in rd.tensors:
-        data = np.array(t.data)
-        if t.name in names:
-            w.add_tensor(t.name, gguf.quants.dequantize(data, t.tensor_type).astype(np.float32),
-                         raw_dtype=gguf.GGMLQuantizationType.F32)
-        else:
-            w.add_tensor(t.name, data, raw_dtype=t.tensor_type)
-    w.write_header_to_file()
-    w.write_kv_data_to_file()
-    w.write_tensors_to_file()
-    w.close()
-    return dst
-
-
 def test_oracle_f16_embeddings_widen_exactly(tmp_path):
     """F16 text/audio embeddings (exporter --spec emb=f16) are widened exactly: the oracle gives the
     same logits, bit for bit, as for a twin file storing those values as F32."""
     e16 = S.write_model(str(tmp_path / "e16.gguf"), seed=21, dims=S.Dims(NL=2), emb_type="f16")
-    e32 = _gguf_widened_copy(e16, str(tmp_path / "e32.gguf"), {"ar.text_emb", "ar.audio_emb"})
+    import gguf
+    F32 = gguf.GGMLQuantizationType.F32
+    e32 = gguf_retyped_copy(e16, str(tmp_path / "e32.gguf"), {"ar.text_emb": F32, "ar.audio_emb": F32})
     rng = np.random.default_rng(21)
     reqs = [S.make_request(rng, 23, 9), S.make_request(rng, 14, 0)]
     forced = rng.integers(0, 1024, (2, 4)).astype(np.int32)
@@ -324,3 +301,29 @@ def test_oracle_q8_0_logits_restated(tmp_path):
         for ib in range(orc.D // 32):
             acc = _fmaf(isum[:, ib], d[:, ib], acc)
         assert np.array_equal(acc, logits[b]), b
+
+
+@pytest.mark.parametrize("wtype,K", [(0, 512), (1, 512), (1, 2048)])
+def test_oracle_float_layer_mul_mat_restated(wtype, K):
+    """F32 / F16 layer matrices (exporter default / --f16): the oracle's mul_mat equals, bit for bit, a
+    numpy restatement of ggml's FMA-vectorised dot -- src1 rounded to F16 for an F16 matrix, 32 float
+    FMA chains (chain c takes k = c, c+32, ...), chains folded pairwise as c^16, ^8, ^4, ^1, ^2."""
+    rng = np.random.default_rng(31 + K + wtype)
+    N, M = 40, 5
+    W = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    X = rng.standard_normal((M, K)).astype(np.float32)
+    if wtype == 1:
+        wraw = W.astype(np.float16)
+        wf, xr = wraw.astype(np.float32), X.astype(np.float16).astype(np.float32)
+    else:
+        wraw, wf, xr = W, W, X
+    got = O.mul_mat(wraw, wtype, N, K, X, layer=True)
+    s = np.zeros((M, N, 32), np.float32)
+    for t in range(K // 32):
+        s = _fmaf(wf[None, :, 32 * t:32 * t + 32], xr[:, None, 32 * t:32 * t + 32], s)
+    for off in (16, 8, 4, 1, 2):
+        lo = [c for c in range(32) if not c & off]
+        s[..., lo] = s[..., lo] + s[..., [c | off for c in lo]]
+    assert np.array_equal(got, s[..., 0])
+    if wtype == 0:   # not the predict / BERT projection order (exact products, double sums)
+        assert not np.array_equal(got, O.mul_mat(wraw, 0, N, K, X))
