@@ -41,6 +41,9 @@ def parse():
     ap.add_argument("--iters", type=int, default=1500)
     ap.add_argument("--refill-every", type=int, default=16)
     ap.add_argument("--kv", default="f16", choices=["f16", "f32"])
+    ap.add_argument("--format", default="q8_0", choices=list(FORMATS),
+                    help="model file of the serve workload: q8_0 (the exporter's --q8, the headline), f16 (its --f16 "
+                         "preset: F16 matrices, predict and embeddings) or f32 (no flags)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-seqs", type=int, default=16,
                     help="sequences of the bounded CPU sample the baseline / reference arm extrapolates from")
@@ -461,6 +464,15 @@ def cpu_baseline(args, job_tokens, job_seqs):
                       f"tokens"}
 
 
+# serve-workload model formats: cached_model arguments and the weight bytes one decode step reads
+# (24 layers x 3,145,728 matrix weights + 26,624 B of F32 biases / LN per layer + the 1025 x 512 predict)
+FORMATS = {
+    "q8_0": (dict(mat_type="q8_0"), 82954240, "Q8_0 attn/FFN, F32 predict"),
+    "f16": (dict(mat_type="f16", predict_type="f16", emb_type="f16"), 152683520, "F16 attn/FFN/predict/embeddings"),
+    "f32": (dict(mat_type="f32"), 304728064, "F32 attn/FFN/predict"),
+}
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -497,11 +509,12 @@ def main():
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
+    fmt_kw, weight_bytes, fmt_desc = FORMATS[args.format]
     if rank == 0:
-        model = S.cached_model(MODEL_CACHE, seed=0, n_layer=24)
+        model = S.cached_model(MODEL_CACHE, seed=0, n_layer=24, **fmt_kw)
     if world > 1:
         dist.barrier()
-    model = S.cached_model(MODEL_CACHE, seed=0, n_layer=24)
+    model = S.cached_model(MODEL_CACHE, seed=0, n_layer=24, **fmt_kw)
 
     ctx = gsvcu.Context(local_rank)
     ctx.load(model)
@@ -575,10 +588,12 @@ def main():
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": n_gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_v / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "q8_0 int8 MMA / f32 softmax / f16 KV" if args.kv == "f16" else
-        "q8_0 int8 MMA / f32 softmax / f32 KV", "data": "synthetic (seeded GGUF weights N(0,0.02), requests U[80,400])",
+        "vs_baseline": None,
+        "dtype": ("q8_0 int8 MMA" if args.format == "q8_0" else f"{args.format} weights / f32 FMA") +
+                 f" / f32 softmax / {args.kv} KV",
+        "data": "synthetic (seeded GGUF weights N(0,0.02), requests U[80,400])",
         "config": {"workload": "cfg4: box-wide serving shard per GPU (BASELINE configs[4])",
-                   "model": "gsv AR 24 x 512, 16 heads x 32, FFN 2048, vocab 1025, Q8_0 attn/FFN",
+                   "model": f"gsv AR 24 x 512, 16 heads x 32, FFN 2048, vocab 1025, {fmt_desc}",
                    "slots_per_gpu": args.slots, "iters_per_job": args.iters, "refill_every": args.refill_every,
                    "sampler": "top_k 15, top_p 1.0, temperature 1.0, rep 1.35, EOS 1024",
                    "kv_cache": f"paged {args.kv}, 64-token pages", "parallelism": f"dp{n_gpus} (replicas, batch-sharded)",
@@ -592,12 +607,12 @@ def main():
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": (tpk * keys_launch) if tpk else None, "algorithmic_bytes_per_launch": bytes_launch,
                      "avg_launch_ms": attn_ms},
-        "decode_step_roofline": {"bytes_per_step": 82954240 + attn_bytes / prof_steps, "ms_per_step": step_ms,
-                                 "achieved": (82954240 + attn_bytes / prof_steps) / (step_ms * 1e-3) / 1e9,
+        "decode_step_roofline": {"bytes_per_step": weight_bytes + attn_bytes / prof_steps, "ms_per_step": step_ms,
+                                 "achieved": (weight_bytes + attn_bytes / prof_steps) / (step_ms * 1e-3) / 1e9,
                                  "peak": peak, "unit": "GB/s",
-                                 "frac": (82954240 + attn_bytes / prof_steps) / (step_ms * 1e-3) / 1e9 / peak,
-                                 "state": "mid-job (iteration ~iters/2), 16 graph-replayed steps; bytes = Q8_0 + "
-                                          "F32 weights (82.95 MB) + K/V and q/out of every decoding slot"},
+                                 "frac": (weight_bytes + attn_bytes / prof_steps) / (step_ms * 1e-3) / 1e9 / peak,
+                                 "state": f"mid-job (iteration ~iters/2), 16 graph-replayed steps; bytes = weights "
+                                          f"({weight_bytes / 1e6:.2f} MB) + K/V and q/out of every decoding slot"},
         "step_profile_ms": {k: round(v / prof_steps, 4) for k, v in ms_cls.items()},
         "clocks": clocks,
     }
