@@ -1428,7 +1428,8 @@ int gsvcu_op_f32_gemm(gsvcu_ctx* ctx, const float* x_dev, int32_t M, const float
 
 int gsvcu_op_fx_gemm(gsvcu_ctx* ctx, const float* x_dev, int32_t M, const void* w_dev, int32_t wtype, int32_t N,
                      int32_t K, const float* bias_dev, float* y_dev) {
-    if (!ctx || !x_dev || !w_dev || !y_dev || M < 0 || N <= 0 || K <= 0 || K % 32 || (wtype != 0 && wtype != 1))
+    if (!ctx || !x_dev || !w_dev || !y_dev || M < 0 || N <= 0 || K <= 0 || K % 64 || (wtype != 0 && wtype != 1) ||
+        ((uintptr_t)x_dev & 15) || ((uintptr_t)w_dev & 15))
         return GSVCU_ERR_ARG;
     DeviceGuard g(ctx->device);
     GemmFxParams p;

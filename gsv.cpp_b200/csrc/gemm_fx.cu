@@ -9,11 +9,15 @@
 // are then added pairwise: chain c with c^16 (accumulators 0+2, 1+3), ^8 (0+1), ^4 (the two 128-bit
 // halves), ^1 and ^2 (the two horizontal adds). K is a multiple of 32.
 //
-// Mapping: lane c of a warp runs chain c, so every load of a warp is one contiguous 32-value row
-// segment. A warp owns 8 rows x 8 columns (64 chains per lane: each x value feeds 8 FMAs, each weight
-// 8); the pairwise fold is a transposing butterfly that halves the values a lane holds at each level
-// (32 + 16 + 8 + 4 + 2 shuffles for 64 outputs), after which each lane holds two finished outputs.
-// A CTA of 4 warps covers 16 rows x 16 columns.
+// Mapping: lane c of a warp runs chain c. A warp owns 8 rows x 8 columns (64 chains per lane: each x
+// value feeds 8 FMAs, each weight 8); the pairwise fold is a transposing butterfly that halves the
+// values a lane holds at each level (32 + 16 + 8 + 4 + 2 shuffles for 64 outputs), after which each
+// lane holds two finished outputs. A CTA of 4 warps covers 16 rows x 16 columns and streams its x rows
+// and weight rows through a 4-stage cp.async pipeline of 64-value slices (a lane reads k = 32t + c of
+// a slice from shared memory, conflict-free); the weight slices of the first stages are requested
+// before the wait for the predecessor kernel. K is a multiple of 64 here.
+#include <type_traits>
+
 #include "kernels.h"
 
 namespace gsvcu {
@@ -23,12 +27,25 @@ constexpr int FX_RW = 8, FX_CW = 8;              // warp tile: rows x columns
 constexpr int FX_WM = 2, FX_WN = 2;              // warps per CTA along rows / columns
 constexpr int FX_TM = FX_RW * FX_WM, FX_TN = FX_CW * FX_WN;
 constexpr int FX_NV = FX_RW * FX_CW;             // outputs per warp
+constexpr int FX_KC = 64;                        // k values per pipeline stage (two chain steps)
+constexpr int FX_ST = 4;                         // pipeline stages
 
 template <int WT>
-__device__ __forceinline__ float ld_w(const void* w, int i) {
-    if (WT == FX_F32) return __ldg((const float*)w + i);
-    return __half2float(__ldg((const __half*)w + i));
+using fx_wt = typename std::conditional<WT == FX_F16, __half, float>::type;
+
+template <int WT>
+struct FxSmem {
+    float x[FX_ST][FX_TM][FX_KC];
+    fx_wt<WT> w[FX_ST][FX_TN][FX_KC];
+};
+
+__device__ __forceinline__ void fx_cp16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+                 : "memory");
 }
+
+__device__ __forceinline__ float widen(float v) { return v; }
+__device__ __forceinline__ float widen(__half v) { return __half2float(v); }
 
 // One level of the pairwise fold over the first N values of every lane: lanes l and l^OFF hold the
 // same outputs' sums of chain groups l and l^OFF; lane l keeps the lower half of the outputs when bit
@@ -67,35 +84,67 @@ __device__ __forceinline__ void kv_store(const KvWrite& kv, int n, int f, float 
 
 template <int WT, int EPI>
 __global__ void __launch_bounds__(128) k_gemm_fx(const GemmFxParams p) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.y * FX_TM + (warp / FX_WN) * FX_RW;
-    const int n0 = blockIdx.x * FX_TN + (warp % FX_WN) * FX_CW;
-    // rows / columns past the edge read the last valid one; their sums are never stored
-    int xo[FX_RW], wo[FX_CW];
-#pragma unroll
-    for (int r = 0; r < FX_RW; r++) xo[r] = min(m0 + r, p.M - 1) * p.ldx + lane;
-#pragma unroll
-    for (int j = 0; j < FX_CW; j++) wo[j] = min(n0 + j, p.N - 1) * p.K + lane;
+    __shared__ __align__(16) FxSmem<WT> sm;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int mt = blockIdx.y * FX_TM, nt = blockIdx.x * FX_TN;   // the CTA's first row / column
+    const int wr = (warp / FX_WN) * FX_RW, wc = (warp % FX_WN) * FX_CW;
+    const int m0 = mt + wr, n0 = nt + wc;
+    const int nch = p.K / FX_KC;
+    // one stage = the CTA's 16 x rows and 16 weight rows over 64 k values, in 16-byte copies; rows /
+    // columns past the edge copy the last valid one (their sums are never stored)
+    constexpr int XCH = FX_KC * 4 / 16, WCH = FX_KC * (int)sizeof(fx_wt<WT>) / 16;   // 16-byte chunks per row
+    auto load_w = [&](int st, int c) {
+        for (int q = tid; q < FX_TN * WCH; q += 128) {
+            const int j = q / WCH, part = q % WCH;
+            const fx_wt<WT>* src = (const fx_wt<WT>*)p.w + (size_t)min(nt + j, p.N - 1) * p.K + c * FX_KC +
+                                   part * (16 / (int)sizeof(fx_wt<WT>));
+            fx_cp16(&sm.w[st][j][part * (16 / (int)sizeof(fx_wt<WT>))], src);
+        }
+    };
+    auto load_x = [&](int st, int c) {
+        for (int q = tid; q < FX_TM * XCH; q += 128) {
+            const int r = q / XCH, part = q % XCH;
+            fx_cp16(&sm.x[st][r][part * 4], p.x + (size_t)min(mt + r, p.M - 1) * p.ldx + c * FX_KC + part * 4);
+        }
+    };
     float acc[FX_NV];
 #pragma unroll
     for (int i = 0; i < FX_NV; i++) acc[i] = 0.0f;
+    for (int s = 0; s < FX_ST - 1; s++)   // weights do not depend on the predecessor kernel
+        if (s < nch) load_w(s, s);
     griddep_wait();
     griddep_launch();
-#pragma unroll 2
-    for (int k0 = 0; k0 < p.K; k0 += 32) {
-        float xv[FX_RW], wv[FX_CW];
-#pragma unroll
-        for (int r = 0; r < FX_RW; r++) {
-            const float t = p.x[xo[r] + k0];
-            xv[r] = WT == FX_F16 ? __half2float(__float2half_rn(t)) : t;
-        }
-#pragma unroll
-        for (int j = 0; j < FX_CW; j++) wv[j] = ld_w<WT>(p.w, wo[j] + k0);
-#pragma unroll
-        for (int r = 0; r < FX_RW; r++)
-#pragma unroll
-            for (int j = 0; j < FX_CW; j++) acc[r * FX_CW + j] = fmaf(wv[j], xv[r], acc[r * FX_CW + j]);
+    for (int s = 0; s < FX_ST - 1; s++) {   // group s: stage s's x (group 0 also the weights above)
+        if (s < nch) load_x(s, s);
+        asm volatile("cp.async.commit_group;" ::: "memory");
     }
+    for (int c = 0; c < nch; c++) {
+        asm volatile("cp.async.wait_group %0;" ::"n"(FX_ST - 2) : "memory");   // stage c has landed
+        __syncthreads();   // ... for every thread, and stage c - 1 is free again
+        const int cn = c + FX_ST - 1;
+        if (cn < nch) {
+            load_w(cn % FX_ST, cn);
+            load_x(cn % FX_ST, cn);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        const int st = c % FX_ST;
+#pragma unroll
+        for (int t = 0; t < FX_KC / 32; t++) {   // chain step k = c*64 + 32t + lane
+            float xv[FX_RW], wv[FX_CW];
+#pragma unroll
+            for (int r = 0; r < FX_RW; r++) {
+                const float v = sm.x[st][wr + r][32 * t + lane];
+                xv[r] = WT == FX_F16 ? __half2float(__float2half_rn(v)) : v;
+            }
+#pragma unroll
+            for (int j = 0; j < FX_CW; j++) wv[j] = widen(sm.w[st][wc + j][32 * t + lane]);
+#pragma unroll
+            for (int r = 0; r < FX_RW; r++)
+#pragma unroll
+                for (int j = 0; j < FX_CW; j++) acc[r * FX_CW + j] = fmaf(wv[j], xv[r], acc[r * FX_CW + j]);
+        }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
     fold<16, 64>(acc, lane);
     fold<8, 32>(acc, lane);
     fold<4, 16>(acc, lane);
@@ -138,7 +187,7 @@ void launch_wt(const GemmFxParams& p, int epi, cudaStream_t s) {
 }  // namespace
 
 void launch_gemm_fx(const GemmFxParams& p, int epi, cudaStream_t s) {
-    if (p.M <= 0 || p.N <= 0) return;
+    if (p.M <= 0 || p.N <= 0 || p.K % FX_KC) return;
     if (p.wtype == FX_F16) launch_wt<FX_F16>(p, epi, s);
     else launch_wt<FX_F32>(p, epi, s);
 }

@@ -70,7 +70,8 @@ void pack_q8_0_host(const uint8_t* raw, int N, int K, uint8_t* wq_out, uint16_t*
 // ------------------------------------------------------------ F32 / F16 weight GEMM (gemm_fx.cu)
 // y[m][n] = sum_k w[n][k] * x(m, k) for F32 / F16 layer matrices and an F16 predict, in the order of
 // ggml's FMA-vectorised dot: x rounded to F16 for an F16 w, 32 float FMA chains (chain c takes
-// k = c, c + 32, ...) added pairwise as chains c^16, ^8, ^4, ^1, ^2. K % 32 == 0; w row-major [N][K].
+// k = c, c + 32, ...) added pairwise as chains c^16, ^8, ^4, ^1, ^2. K % 64 == 0; w row-major [N][K];
+// x, w and every row of both 16-byte aligned (ldx * 4 and K * element size multiples of 16).
 enum { FX_F32 = 0, FX_F16 = 1 };
 enum { FXE_BIAS = 0, FXE_RESID = 1, FXE_RELU = 2 };   // y = acc + b (+ K/V store); (r + acc) + b; relu(acc + b)
 struct GemmFxParams {

@@ -194,7 +194,7 @@ int gsvcu_op_f32_gemm(gsvcu_ctx* ctx, const float* x_dev, int32_t M, const float
 /* Y[M][N] = W[N][K] . X[M][K]^T (+ bias[N], may be NULL) for an F32 (wtype 0) or F16 (wtype 1) layer
  * matrix (ggml F32 / F16 mul_mat, src/gsv_ar.cpp:244,260,262,263) in the order of ggml's FMA-vectorised
  * dot: X rounded to F16 for an F16 W, 32 float FMA chains (chain c over k = c, c + 32, ...) added
- * pairwise as chains c^16, ^8, ^4, ^1, ^2. K a multiple of 32. */
+ * pairwise as chains c^16, ^8, ^4, ^1, ^2. K a multiple of 64; x_dev and w_dev 16-byte aligned. */
 int gsvcu_op_fx_gemm(gsvcu_ctx* ctx, const float* x_dev, int32_t M, const void* w_dev, int32_t wtype, int32_t N,
                      int32_t K, const float* bias_dev, float* y_dev);
 
