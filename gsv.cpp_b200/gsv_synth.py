@@ -30,8 +30,9 @@ def write_model(path: str, seed: int = 0, dims: Dims | None = None, mat_type: st
                 ln_noise: float = 0.02, predict_type: str = "f32", emb_type: str = "f32",
                 ffn_type: str | None = None) -> str:
     """mat_type is the type of the attention matrices (the exporter's --spec attn=...) and, unless
-    ffn_type is given, of the FFN matrices (--spec ffn=...): "q8_0", "f16" or "f32". predict_type
-    "q8_0" / "f16" stores ar.predict as Q8_0 / F16 (--spec predict=...); emb_type "f16" stores the
+    ffn_type is given, of the FFN matrices (--spec ffn=...): "q8_0", "q4_0", "q5_0", "f16" or "f32".
+    predict_type "q8_0" / "q4_0" / "q5_0" / "f16" stores ar.predict in that type (--spec predict=...);
+    emb_type "f16" stores the
     text / audio embeddings as F16 (--spec emb=f16). The exporter's --f16 preset is
     mat_type="f16", predict_type="f16", emb_type="f16"; its default (no flags) is mat_type="f32"."""
     import gguf
@@ -40,7 +41,8 @@ def write_model(path: str, seed: int = 0, dims: Dims | None = None, mat_type: st
     rng = np.random.default_rng(seed)
     D, FF = d.D, 4 * d.D
     types = {"q8_0": gguf.GGMLQuantizationType.Q8_0, "f32": gguf.GGMLQuantizationType.F32,
-             "f16": gguf.GGMLQuantizationType.F16}
+             "f16": gguf.GGMLQuantizationType.F16, "q4_0": gguf.GGMLQuantizationType.Q4_0,
+             "q5_0": gguf.GGMLQuantizationType.Q5_0}
     qt = types[mat_type]
     ft = types[ffn_type or mat_type]
 

@@ -105,8 +105,9 @@ def quantize_q8_0(x: np.ndarray) -> np.ndarray:
 
 
 def mul_mat(w: np.ndarray, wtype: int, N: int, K: int, x: np.ndarray, layer: bool = False) -> np.ndarray:
-    """Y[M][N] = W[N][K] . X[M][K]^T with ggml CPU semantics (wtype 8 = raw Q8_0 bytes, 0 = F32,
-    1 = F16). layer: W is a layer matrix, so an F32 W takes the FMA-vectorised order of an F16 one."""
+    """Y[M][N] = W[N][K] . X[M][K]^T with ggml CPU semantics (wtype 8 / 2 / 6 = raw Q8_0 / Q4_0 / Q5_0
+    bytes, 0 = F32, 1 = F16). layer: W is a layer matrix, so an F32 W takes the FMA-vectorised order of an
+    F16 one."""
     x = np.ascontiguousarray(x, dtype=np.float32)
     M = x.size // K
     y = np.empty((M, N), np.float32)

@@ -388,16 +388,19 @@ EXPORT_FORMATS = [   # (attention matrices, FFN matrices, predict, embeddings)
     ("f32", "f32", "f32", "f32"),      # no flags: F32 matrices
     ("q8_0", "f16", "f32", "f32"),     # --spec attn=q8_0,ffn=f16
     ("f16", "q8_0", "f32", "f32"),     # --spec attn=f16,ffn=q8_0
+    ("q4_0", "q4_0", "q4_0", "f32"),   # --spec attn=q4_0,ffn=q4_0,predict=q4_0
+    ("q8_0", "q5_0", "q5_0", "f16"),   # --spec attn=q8_0,ffn=q5_0,predict=q5_0,emb=f16
 ]
 
 
 @pytest.mark.parametrize("mat_type,ffn_type,predict_type,emb_type", EXPORT_FORMATS)
 def test_export_formats_match_oracle(mat_type, ffn_type, predict_type, emb_type):
-    """The exporter's formats besides --q8: Q8_0 / F16 predict (logits by the Q8_0 GEMM over Q8_0 rows, or
-    by the F16 dot), F16 embeddings (widened on load), F32 / F16 attention and FFN matrices (ggml's
-    FMA-vectorised F32 / F16 dot) and mixes of the attn / ffn groups. A teacher-forced decode trace
-    (fused and unfused steps; float matrices always run unfused) equals the oracle bit for bit, and so
-    does a sampled generate through the graph-captured decode step."""
+    """The exporter's formats besides --q8: Q8_0 / Q4_0 / Q5_0 / F16 predict (logits by the Q8_0 GEMM over
+    Q8_0 rows, or by the F16 dot), F16 embeddings (widened on load), F32 / F16 attention and FFN matrices
+    (ggml's FMA-vectorised F32 / F16 dot), Q4_0 / Q5_0 matrices (repacked into Q8_0 blocks on load) and
+    mixes of the attn / ffn groups. A teacher-forced decode trace (fused and unfused steps; float
+    matrices always run unfused) equals the oracle bit for bit, and so does a sampled generate through
+    the graph-captured decode step."""
     import gsvcu
     model = S.cached_model(MODEL_CACHE, seed=9, n_layer=2, mat_type=mat_type, predict_type=predict_type,
                            emb_type=emb_type, ffn_type=ffn_type)
@@ -415,7 +418,8 @@ def test_export_formats_match_oracle(mat_type, ffn_type, predict_type, emb_type)
         unf = c.debug_trace(reqs, forced)
         c.set_fused_decode(1)
         assert np.array_equal(unf.view(np.uint32), ref.view(np.uint32))
-        assert c.fused_decode() == (1 if mat_type == ffn_type == "q8_0" else 0)
+        blockq = ("q8_0", "q4_0", "q5_0")   # run by the Q8_0 kernels, fused decode step included
+        assert c.fused_decode() == (1 if mat_type in blockq and ffn_type in blockq else 0)
         seeds = [31, 32, 33, 34, 35]
         got, glens = c.generate(reqs, seeds=seeds, max_steps=40)
         exp, elens = orc9.generate(reqs, seeds=seeds, max_steps=40, kv_f16=True)
