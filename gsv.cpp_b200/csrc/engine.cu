@@ -16,7 +16,7 @@ using namespace gsvcu;
 namespace {
 
 struct LayerW {
-    int mt[4] = {8, 8, 8, 8};   // qkv, out, ffn1, ffn2: 8 Q8_0 kernels (Q8_0 / Q4_0 / Q5_0), 0 F32, 1 F16
+    int mt[4] = {8, 8, 8, 8};   // qkv, out, ffn1, ffn2: 8 Q8_0 kernels (Q8_0 / Q4_0 / Q5_0 / IQ4_NL), 0 F32, 1 F16
     uint4* wq[4] = {nullptr, nullptr, nullptr, nullptr};     // Q8_0: fragment planes
     uint16_t* wd[4] = {nullptr, nullptr, nullptr, nullptr};  //       matching fp16 scale planes
     const void* wf[4] = {nullptr, nullptr, nullptr, nullptr};  // F32 / F16: the GGUF rows [N][K] as stored
@@ -103,14 +103,17 @@ struct ModelView {
 
 const char* kMatNames[4] = {"qkv_w", "out_w", "ffn1_w", "ffn2_w"};
 
-// ggml types run by the Q8_0 kernels: Q8_0 itself, and Q4_0 / Q5_0 repacked into Q8_0 blocks
-bool q8_class(uint32_t type) { return type == 8 || type == 2 || type == 6; }
+// ggml types run by the Q8_0 kernels: Q8_0 itself, and Q4_0 / Q5_0 / IQ4_NL repacked into Q8_0 blocks
+bool q8_class(uint32_t type) { return type == 8 || type == 2 || type == 6 || type == 20; }
 
-// Q4_0 / Q5_0 blocks (ggml block_q4_0 / block_q5_0: fp16 d; Q5_0 then the 32 fifth bits as a
-// little-endian uint32; then 16 bytes whose low nibbles are values 0..15 and high nibbles values
-// 16..31) as Q8_0 blocks holding the same signed values (nibble - 8, five-bit value - 16) and the same
-// d. ggml's Q4_0 / Q5_0 dot against Q8_0 activations is an integer block dot scaled by d_w * d_x, so on
-// these blocks it is the Q8_0 block dot.
+// IQ4_NL's 16 values of a 4-bit code (ggml kvalues_iq4nl; part of the GGUF format)
+constexpr int8_t kIq4nl[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+
+// Q4_0 / Q5_0 / IQ4_NL blocks (ggml block_q4_0 / block_q5_0 / block_iq4_nl: fp16 d; Q5_0 then the 32
+// fifth bits as a little-endian uint32; then 16 bytes whose low nibbles are values 0..15 and high
+// nibbles values 16..31) as Q8_0 blocks holding the same signed values (nibble - 8, five-bit value - 16,
+// kIq4nl[nibble]) and the same d. ggml's dot of these types against Q8_0 activations is an integer
+// block dot scaled by d_w * d_x, so on these blocks it is the Q8_0 block dot.
 std::vector<uint8_t> to_q8_0_blocks(const GgufTensor* t) {
     const size_t bs = t->type == 6 ? 22 : 18, nb = t->nbytes / bs;
     std::vector<uint8_t> out(nb * 34);
@@ -124,6 +127,11 @@ std::vector<uint8_t> to_q8_0_blocks(const GgufTensor* t) {
             for (int j = 0; j < 16; j++) {
                 q[j] = (int8_t)((src[2 + j] & 15) - 8);
                 q[j + 16] = (int8_t)((src[2 + j] >> 4) - 8);
+            }
+        } else if (t->type == 20) {
+            for (int j = 0; j < 16; j++) {
+                q[j] = kIq4nl[src[2 + j] & 15];
+                q[j + 16] = kIq4nl[src[2 + j] >> 4];
             }
         } else {
             uint32_t qh;
@@ -162,7 +170,7 @@ int validate_model(const GgufFile& f, ModelView& mv, std::string& err) {
         return GSVCU_ERR_FORMAT;
     }
     const int NL = hp.n_layer, V = hp.vocab_size, PV = hp.phoneme_vocab_size, BD = hp.bert_dim;
-    // accepted ggml types: 0 = F32, 1 = F16, 2 = Q4_0, 6 = Q5_0, 8 = Q8_0
+    // accepted ggml types: 0 = F32, 1 = F16, 2 = Q4_0, 6 = Q5_0, 8 = Q8_0, 20 = IQ4_NL
     auto need = [&](const std::string& name, std::vector<uint32_t> types, std::vector<int64_t> dims,
                     const GgufTensor** out) -> int {
         const GgufTensor* t = f.tensor(name);
@@ -171,7 +179,7 @@ int validate_model(const GgufFile& f, ModelView& mv, std::string& err) {
             std::string want;
             for (uint32_t ty : types) want += (want.empty() ? "" : " or ") + std::to_string(ty);
             err = "tensor " + name + " has ggml type " + std::to_string(t->type) + ", expected " + want +
-                  " (0 F32, 1 F16, 2 Q4_0, 6 Q5_0, 8 Q8_0)";
+                  " (0 F32, 1 F16, 2 Q4_0, 6 Q5_0, 8 Q8_0, 20 IQ4_NL)";
             return GSVCU_ERR_FORMAT;
         }
         int64_t ne = 1, ne_want = 1;
@@ -186,11 +194,11 @@ int validate_model(const GgufFile& f, ModelView& mv, std::string& err) {
     };
     int r;
     // embeddings: F32, or F16 (exporter --spec emb=f16) widened to F32 on load; predict and layer
-    // matrices: F32, F16, Q8_0, Q4_0 or Q5_0 (--spec predict=.., attn=.., ffn=..)
+    // matrices: F32, F16, Q8_0, Q4_0, Q5_0 or IQ4_NL (--spec predict=.., attn=.., ffn=..)
     if ((r = need("ar.text_emb", {0, 1}, {D, PV}, &mv.te)) || (r = need("ar.audio_emb", {0, 1}, {D, V}, &mv.ae)) ||
         (r = need("ar.bert_proj", {0}, {BD, D}, &mv.bp)) || (r = need("ar.bert_proj_b", {0}, {D}, &mv.bb)) ||
         (r = need("ar.text_pe_alpha", {0}, {1}, &mv.ta)) || (r = need("ar.audio_pe_alpha", {0}, {1}, &mv.aa)) ||
-        (r = need("ar.predict", {0, 8, 1, 2, 6}, {D, V}, &mv.pr)))
+        (r = need("ar.predict", {0, 8, 1, 2, 6, 20}, {D, V}, &mv.pr)))
         return r;
     std::memcpy(&hp.text_pe_alpha, mv.ta->data, 4);
     std::memcpy(&hp.audio_pe_alpha, mv.aa->data, 4);
@@ -201,12 +209,12 @@ int validate_model(const GgufFile& f, ModelView& mv, std::string& err) {
     for (int li = 0; li < NL; li++) {
         const std::string pfx = "transformer.block" + std::to_string(li) + ".";
         for (int m = 0; m < 4; m++)
-            if ((r = need(pfx + kMatNames[m], {8, 0, 1, 2, 6}, {NK[m][1], NK[m][0]}, &mv.mats[(size_t)li * 4 + m])))
+            if ((r = need(pfx + kMatNames[m], {8, 0, 1, 2, 6, 20}, {NK[m][1], NK[m][0]}, &mv.mats[(size_t)li * 4 + m])))
                 return r;
         // FFN1's epilogue produces what FFN2 reads: Q8_0 blocks for a block-quantized ffn2_w, floats otherwise
         if (q8_class(mv.mats[(size_t)li * 4 + 2]->type) != q8_class(mv.mats[(size_t)li * 4 + 3]->type)) {
-            err = pfx + "ffn1_w / ffn2_w: both block-quantized (Q8_0 / Q4_0 / Q5_0) or both F32 / F16 (the exporter's "
-                        "ffn group) expected";
+            err = pfx + "ffn1_w / ffn2_w: both block-quantized (Q8_0 / Q4_0 / Q5_0 / IQ4_NL) or both F32 / F16 (the "
+                        "exporter's ffn group) expected";
             return GSVCU_ERR_FORMAT;
         }
         for (int k = 0; k < 8; k++)
@@ -410,7 +418,7 @@ int gsvcu_ctx::load(const char* path) {
     if (mv.pr->type == 1) {   // F16 predict, evaluated by gemm_fx
         predict_q8 = false;
         TRY(upload(mv.pr->data, mv.pr->nbytes, (void**)&predict_f16));
-    } else if (q8_class(mv.pr->type)) {   // Q8_0 predict (Q4_0 / Q5_0 as Q8_0 blocks)
+    } else if (q8_class(mv.pr->type)) {   // Q8_0 predict (Q4_0 / Q5_0 / IQ4_NL as Q8_0 blocks)
         predict_q8 = true;
         V_pad = (V + 31) / 32 * 32;
         std::vector<uint8_t> raw((size_t)V_pad * (D / QK) * 34, 0);   // zero blocks: scale 0, quants 0

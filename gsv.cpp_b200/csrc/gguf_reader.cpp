@@ -132,8 +132,9 @@ bool GgufFile::open(const std::string& path, std::string& err) {
         switch (T.type) {
             case 0: T.nbytes = (uint64_t)ne * 4; break;
             case 1: T.nbytes = (uint64_t)ne * 2; break;
-            case 2:   // Q4_0: fp16 d + 16 bytes of nibbles per 32 values
-            case 6:   // Q5_0: fp16 d + 4 bytes of high bits + 16 bytes of nibbles
+            case 2:    // Q4_0: fp16 d + 16 bytes of nibbles per 32 values
+            case 20:   // IQ4_NL: fp16 d + 16 bytes of nibbles (table indices)
+            case 6:    // Q5_0: fp16 d + 4 bytes of high bits + 16 bytes of nibbles
             case 8:   // Q8_0: fp16 d + 32 int8
                 if (T.dims[0] % 32) { err = "block-quantized row not a multiple of 32: " + T.name; return false; }
                 T.nbytes = (uint64_t)ne / 32 * (T.type == 8 ? 34 : T.type == 6 ? 22 : 18);

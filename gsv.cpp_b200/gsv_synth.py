@@ -26,12 +26,29 @@ class Dims:
     BERT: int = 1024
 
 
+def iq4_nl_blocks(arr: np.ndarray) -> np.ndarray:
+    """IQ4_NL blocks of a float [N][K] array from a plain quantizer (not ggml's scale search): per 32
+    values d = fp16(amax / 127) and each value the nearest entry of the IQ4_NL table, codes packed as
+    block_iq4_nl (fp16 d, then values 0..15 in the low nibbles and 16..31 in the high ones)."""
+    from gguf import quants
+    table = np.array(quants.IQ4_NL.kvalues, np.float32)
+    N, K = arr.shape
+    b = arr.reshape(N, K // 32, 32)
+    d = (np.abs(b).max(-1, keepdims=True) / 127).astype(np.float16)
+    df = d.astype(np.float32)
+    df[df == 0] = 1
+    idx = np.abs(b[..., None] / df[..., None] - table).argmin(-1).astype(np.uint8)
+    qs = idx[..., :16] | (idx[..., 16:] << 4)
+    return np.concatenate([d.view(np.uint8).reshape(N, K // 32, 2), qs], axis=-1).reshape(N, K // 32 * 18)
+
+
 def write_model(path: str, seed: int = 0, dims: Dims | None = None, mat_type: str = "q8_0",
                 ln_noise: float = 0.02, predict_type: str = "f32", emb_type: str = "f32",
                 ffn_type: str | None = None) -> str:
     """mat_type is the type of the attention matrices (the exporter's --spec attn=...) and, unless
-    ffn_type is given, of the FFN matrices (--spec ffn=...): "q8_0", "q4_0", "q5_0", "f16" or "f32".
-    predict_type "q8_0" / "q4_0" / "q5_0" / "f16" stores ar.predict in that type (--spec predict=...);
+    ffn_type is given, of the FFN matrices (--spec ffn=...): "q8_0", "q4_0", "q5_0", "iq4_nl", "f16" or
+    "f32" (iq4_nl: the reference's tools/quantize_gguf.cpp tier, quantized by iq4_nl_blocks). predict_type
+    "q8_0" / "q4_0" / "q5_0" / "iq4_nl" / "f16" stores ar.predict in that type (--spec predict=...);
     emb_type "f16" stores the
     text / audio embeddings as F16 (--spec emb=f16). The exporter's --f16 preset is
     mat_type="f16", predict_type="f16", emb_type="f16"; its default (no flags) is mat_type="f32"."""
@@ -42,7 +59,7 @@ def write_model(path: str, seed: int = 0, dims: Dims | None = None, mat_type: st
     D, FF = d.D, 4 * d.D
     types = {"q8_0": gguf.GGMLQuantizationType.Q8_0, "f32": gguf.GGMLQuantizationType.F32,
              "f16": gguf.GGMLQuantizationType.F16, "q4_0": gguf.GGMLQuantizationType.Q4_0,
-             "q5_0": gguf.GGMLQuantizationType.Q5_0}
+             "q5_0": gguf.GGMLQuantizationType.Q5_0, "iq4_nl": gguf.GGMLQuantizationType.IQ4_NL}
     qt = types[mat_type]
     ft = types[ffn_type or mat_type]
 
@@ -64,6 +81,8 @@ def write_model(path: str, seed: int = 0, dims: Dims | None = None, mat_type: st
             w.add_tensor(name, arr, raw_dtype=dtype)
         elif dtype == gguf.GGMLQuantizationType.F16:
             w.add_tensor(name, arr.astype(np.float16), raw_dtype=dtype)
+        elif dtype == gguf.GGMLQuantizationType.IQ4_NL:
+            w.add_tensor(name, iq4_nl_blocks(arr), raw_dtype=dtype)
         else:
             w.add_tensor(name, gguf.quants.quantize(arr, dtype), raw_dtype=dtype)
 

@@ -167,7 +167,7 @@ inline int nthreads() {
 #endif
 }
 
-enum { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q5_0 = 6, T_Q8_0 = 8 };
+enum { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q5_0 = 6, T_Q8_0 = 8, T_IQ4_NL = 20 };
 
 // A weight matrix [N][K] (torch [out,in] == ggml ne0=in): F32 or F16 (widened to f), or Q8_0 raw
 // GGUF blocks. canon: evaluated by vec_dot_canon (xf16: with src1 rounded to F16 first).
@@ -494,12 +494,14 @@ bool set_mat(Mat& m, int type, const void* data, int64_t nbytes, int64_t N, int6
     } else if (type == T_Q8_0) {
         if (K % QK || nbytes != N * (K / QK) * Q8_BYTES) { err = std::string("bad size for ") + name; return false; }
         m.q.assign((const uint8_t*)data, (const uint8_t*)data + nbytes);
-    } else if (type == T_Q4_0 || type == T_Q5_0) {
-        // ggml block_q4_0 {fp16 d; u8 qs[16]} / block_q5_0 {fp16 d; u8 qh[4]; u8 qs[16]}: value i (0..31) is
-        // d * (q_i - 8) / d * (q_i - 16), q_i = low (i < 16) or high (i >= 16) nibble of qs[i % 16], plus
-        // bit i of qh as bit 4 for Q5_0. ggml's Q4_0 / Q5_0 x Q8_0 dot is the integer dot of the q_i - 8 /
-        // q_i - 16 with the activation block, scaled by d_w * d_x: the Q8_0 dot of a block holding them.
-        const int64_t bs = type == T_Q4_0 ? 18 : 22, nb = N * (K / QK);
+    } else if (type == T_Q4_0 || type == T_Q5_0 || type == T_IQ4_NL) {
+        // ggml block_q4_0 / block_iq4_nl {fp16 d; u8 qs[16]} / block_q5_0 {fp16 d; u8 qh[4]; u8 qs[16]}:
+        // value i (0..31) is d * (q_i - 8) / d * kvalues_iq4nl[q_i] / d * (q_i - 16), q_i = low (i < 16) or
+        // high (i >= 16) nibble of qs[i % 16], plus bit i of qh as bit 4 for Q5_0. ggml's dot of these
+        // types against Q8_0 activations is the integer dot of those signed values with the activation
+        // block, scaled by d_w * d_x: the Q8_0 dot of a block holding them.
+        static const int kv_iq4nl[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+        const int64_t bs = type == T_Q5_0 ? 22 : 18, nb = N * (K / QK);
         if (K % QK || nbytes != nb * bs) { err = std::string("bad size for ") + name; return false; }
         m.type = T_Q8_0;
         m.q.assign((size_t)(nb * Q8_BYTES), 0);
@@ -507,13 +509,14 @@ bool set_mat(Mat& m, int type, const void* data, int64_t nbytes, int64_t N, int6
             const uint8_t* src = (const uint8_t*)data + b * bs;
             uint8_t* dst = m.q.data() + b * Q8_BYTES;
             std::memcpy(dst, src, 2);
-            const uint8_t* qs = src + (type == T_Q4_0 ? 2 : 6);
+            const uint8_t* qs = src + (type == T_Q5_0 ? 6 : 2);
             uint32_t qh = 0;
             if (type == T_Q5_0) std::memcpy(&qh, src + 2, 4);
             for (int i = 0; i < QK; i++) {
                 int q = i < 16 ? (qs[i] & 0x0f) : (qs[i - 16] >> 4);
                 if (type == T_Q5_0) q += (int)((qh >> i) & 1u) * 16;
-                dst[2 + i] = (uint8_t)(int8_t)(q - (type == T_Q4_0 ? 8 : 16));
+                const int v = type == T_IQ4_NL ? kv_iq4nl[q] : q - (type == T_Q4_0 ? 8 : 16);
+                dst[2 + i] = (uint8_t)(int8_t)v;
             }
         }
     } else {
@@ -763,14 +766,14 @@ void orc_fp32_to_fp16(const float* x, uint16_t* y, int64_t n) { for (int64_t i =
 void orc_fp16_to_fp32(const uint16_t* x, float* y, int64_t n) { for (int64_t i = 0; i < n; i++) y[i] = f16_to_f32(x[i]); }
 void orc_quantize_q8_0(const float* x, int64_t n, uint8_t* blocks) { quantize_q8_0(x, n, blocks); }
 
-// Y[M][N] = W[N][K] . X[M][K]^T with W raw Q8_0 / Q4_0 / Q5_0 blocks (type 8 / 2 / 6), F32 (type 0) or
-// F16 (type 1);
+// Y[M][N] = W[N][K] . X[M][K]^T with W raw Q8_0 / Q4_0 / Q5_0 / IQ4_NL blocks (type 8 / 2 / 6 / 20), F32
+// (type 0) or F16 (type 1);
 // layer != 0: W is a layer matrix (an F32 W is then evaluated like an F16 one, by vec_dot_canon).
 int orc_mul_mat(int type, const void* W, int64_t N, int64_t K, const float* X, int64_t M, float* Y, int layer) {
     Mat w;
     std::string err;
     const int64_t nbytes = type == T_Q8_0   ? N * (K / QK) * Q8_BYTES
-                           : type == T_Q4_0 ? N * (K / QK) * 18
+                           : type == T_Q4_0 || type == T_IQ4_NL ? N * (K / QK) * 18
                            : type == T_Q5_0 ? N * (K / QK) * 22
                                             : N * K * (type == T_F16 ? 2 : 4);
     if (!set_mat(w, type, W, nbytes, N, K, err, "W", layer != 0)) return -1;

@@ -56,7 +56,7 @@ def test_inspect_rejects_bad_files(model_small, model_f32_small, tmp_path):
 @pytest.mark.parametrize("mat_type,ffn_type,predict_type,emb_type", [
     ("q8_0", "q8_0", "q8_0", "f32"), ("q8_0", "q8_0", "f32", "f16"), ("f16", "f16", "f16", "f16"),
     ("f32", "f32", "f32", "f32"), ("q8_0", "f16", "f32", "f32"), ("f16", "q8_0", "f32", "f32"),
-    ("q4_0", "q4_0", "q4_0", "f32"), ("q8_0", "q5_0", "q5_0", "f16")])
+    ("q4_0", "q4_0", "q4_0", "f32"), ("q8_0", "q5_0", "q5_0", "f16"), ("q8_0", "iq4_nl", "iq4_nl", "f32")])
 def test_inspect_export_formats(mat_type, ffn_type, predict_type, emb_type):
     """The exporter's formats: Q8_0 / Q4_0 / Q5_0 / F16 predict, F16 embeddings, F32 / F16 / Q4_0 / Q5_0
     attention and FFN matrices and mixed attn / ffn groups are accepted (GPU parity:

@@ -390,6 +390,7 @@ EXPORT_FORMATS = [   # (attention matrices, FFN matrices, predict, embeddings)
     ("f16", "q8_0", "f32", "f32"),     # --spec attn=f16,ffn=q8_0
     ("q4_0", "q4_0", "q4_0", "f32"),   # --spec attn=q4_0,ffn=q4_0,predict=q4_0
     ("q8_0", "q5_0", "q5_0", "f16"),   # --spec attn=q8_0,ffn=q5_0,predict=q5_0,emb=f16
+    ("q8_0", "iq4_nl", "iq4_nl", "f32"),   # tools/quantize_gguf.cpp --spec attn=q8_0,ffn=iq4_nl,predict=iq4_nl
 ]
 
 
@@ -418,7 +419,7 @@ def test_export_formats_match_oracle(mat_type, ffn_type, predict_type, emb_type)
         unf = c.debug_trace(reqs, forced)
         c.set_fused_decode(1)
         assert np.array_equal(unf.view(np.uint32), ref.view(np.uint32))
-        blockq = ("q8_0", "q4_0", "q5_0")   # run by the Q8_0 kernels, fused decode step included
+        blockq = ("q8_0", "q4_0", "q5_0", "iq4_nl")   # run by the Q8_0 kernels, fused decode step included
         assert c.fused_decode() == (1 if mat_type in blockq and ffn_type in blockq else 0)
         seeds = [31, 32, 33, 34, 35]
         got, glens = c.generate(reqs, seeds=seeds, max_steps=40)

@@ -329,24 +329,25 @@ def test_oracle_float_layer_mul_mat_restated(wtype, K):
         assert not np.array_equal(got, O.mul_mat(wraw, 0, N, K, X))
 
 
-@pytest.mark.parametrize("wtype", [2, 6])
-def test_oracle_q4_0_q5_0_as_q8_0_blocks(wtype):
-    """Q4_0 / Q5_0 matrices (exporter --spec ...=q4_0 / q5_0): the oracle's mul_mat equals, bit for bit, the
-    Q8_0 mul_mat of blocks holding gguf-py's dequantized values divided by the block scale (ggml's
-    Q4_0 / Q5_0 x Q8_0 dot is the integer dot of those values scaled by d_w * d_x)."""
+@pytest.mark.parametrize("wtype", [2, 6, 20])
+def test_oracle_q4_0_q5_0_iq4_nl_as_q8_0_blocks(wtype):
+    """Q4_0 / Q5_0 / IQ4_NL matrices (--spec ...=q4_0 / q5_0, tools/quantize_gguf.cpp iq4_nl): the oracle's
+    mul_mat equals, bit for bit, the Q8_0 mul_mat of blocks holding gguf-py's dequantized values divided
+    by the block scale (ggml's dot of these types against Q8_0 activations is the integer dot of those
+    values scaled by d_w * d_x)."""
     import gguf
     ty = gguf.GGMLQuantizationType(wtype)
     rng = np.random.default_rng(40 + wtype)
     N, K, M = 48, 512, 6
     W = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
     X = rng.standard_normal((M, K)).astype(np.float32)
-    raw = gguf.quants.quantize(W, ty)
+    raw = S.iq4_nl_blocks(W) if wtype == 20 else gguf.quants.quantize(W, ty)
     deq = gguf.quants.dequantize(raw, ty).reshape(N, K // 32, 32)
-    bs = 18 if wtype == 2 else 22
+    bs = 22 if wtype == 6 else 18
     d = raw.reshape(N, K // 32, bs)[..., :2].copy().view(np.float16).astype(np.float32)
     assert (d != 0).all()
-    q = deq / d                                   # exact: deq is d * (an integer of 4 / 5 bits)
-    assert np.array_equal(q, np.round(q)) and np.abs(q).max() <= (8 if wtype == 2 else 16)
+    q = deq / d                                   # exact: deq is d * (an integer of at most 8 bits)
+    assert np.array_equal(q, np.round(q)) and np.abs(q).max() <= {2: 8, 6: 16, 20: 127}[wtype]
     q8 = np.zeros((N, K // 32, 34), np.uint8)
     q8[..., :2] = raw.reshape(N, K // 32, bs)[..., :2]
     q8[..., 2:] = q.astype(np.int8).view(np.uint8)
