@@ -16,7 +16,8 @@ using namespace gsvcu;
 namespace {
 
 struct LayerW {
-    int mt[4] = {8, 8, 8, 8};   // qkv, out, ffn1, ffn2: 8 Q8_0 kernels (Q8_0 / Q4_0 / Q5_0 / IQ4_NL), 0 F32, 1 F16
+    int mt[4] = {8, 8, 8, 8};   // qkv, out, ffn1, ffn2: 8 Q8_0 kernels (Q8_0 / Q4_0 / Q5_0 / IQ4_NL), 0 F32,
+                                //   1 F16, 30 BF16 (gemm_fx)
     uint4* wq[4] = {nullptr, nullptr, nullptr, nullptr};     // Q8_0: fragment planes
     uint16_t* wd[4] = {nullptr, nullptr, nullptr, nullptr};  //       matching fp16 scale planes
     const void* wf[4] = {nullptr, nullptr, nullptr, nullptr};  // F32 / F16: the GGUF rows [N][K] as stored
@@ -170,7 +171,7 @@ int validate_model(const GgufFile& f, ModelView& mv, std::string& err) {
         return GSVCU_ERR_FORMAT;
     }
     const int NL = hp.n_layer, V = hp.vocab_size, PV = hp.phoneme_vocab_size, BD = hp.bert_dim;
-    // accepted ggml types: 0 = F32, 1 = F16, 2 = Q4_0, 6 = Q5_0, 8 = Q8_0, 20 = IQ4_NL
+    // accepted ggml types: 0 = F32, 1 = F16, 2 = Q4_0, 6 = Q5_0, 8 = Q8_0, 20 = IQ4_NL, 30 = BF16
     auto need = [&](const std::string& name, std::vector<uint32_t> types, std::vector<int64_t> dims,
                     const GgufTensor** out) -> int {
         const GgufTensor* t = f.tensor(name);
@@ -179,7 +180,7 @@ int validate_model(const GgufFile& f, ModelView& mv, std::string& err) {
             std::string want;
             for (uint32_t ty : types) want += (want.empty() ? "" : " or ") + std::to_string(ty);
             err = "tensor " + name + " has ggml type " + std::to_string(t->type) + ", expected " + want +
-                  " (0 F32, 1 F16, 2 Q4_0, 6 Q5_0, 8 Q8_0, 20 IQ4_NL)";
+                  " (0 F32, 1 F16, 2 Q4_0, 6 Q5_0, 8 Q8_0, 20 IQ4_NL, 30 BF16)";
             return GSVCU_ERR_FORMAT;
         }
         int64_t ne = 1, ne_want = 1;
@@ -193,12 +194,13 @@ int validate_model(const GgufFile& f, ModelView& mv, std::string& err) {
         return GSVCU_OK;
     };
     int r;
-    // embeddings: F32, or F16 (exporter --spec emb=f16) widened to F32 on load; predict and layer
-    // matrices: F32, F16, Q8_0, Q4_0, Q5_0 or IQ4_NL (--spec predict=.., attn=.., ffn=..)
-    if ((r = need("ar.text_emb", {0, 1}, {D, PV}, &mv.te)) || (r = need("ar.audio_emb", {0, 1}, {D, V}, &mv.ae)) ||
+    // embeddings: F32, or F16 / BF16 (exporter --spec emb=f16 / bf16) widened to F32 on load; predict and
+    // layer matrices: F32, F16, BF16, Q8_0, Q4_0, Q5_0 or IQ4_NL (--spec predict=.., attn=.., ffn=..)
+    if ((r = need("ar.text_emb", {0, 1, 30}, {D, PV}, &mv.te)) ||
+        (r = need("ar.audio_emb", {0, 1, 30}, {D, V}, &mv.ae)) ||
         (r = need("ar.bert_proj", {0}, {BD, D}, &mv.bp)) || (r = need("ar.bert_proj_b", {0}, {D}, &mv.bb)) ||
         (r = need("ar.text_pe_alpha", {0}, {1}, &mv.ta)) || (r = need("ar.audio_pe_alpha", {0}, {1}, &mv.aa)) ||
-        (r = need("ar.predict", {0, 8, 1, 2, 6, 20}, {D, V}, &mv.pr)))
+        (r = need("ar.predict", {0, 8, 1, 2, 6, 20, 30}, {D, V}, &mv.pr)))
         return r;
     std::memcpy(&hp.text_pe_alpha, mv.ta->data, 4);
     std::memcpy(&hp.audio_pe_alpha, mv.aa->data, 4);
@@ -209,12 +211,13 @@ int validate_model(const GgufFile& f, ModelView& mv, std::string& err) {
     for (int li = 0; li < NL; li++) {
         const std::string pfx = "transformer.block" + std::to_string(li) + ".";
         for (int m = 0; m < 4; m++)
-            if ((r = need(pfx + kMatNames[m], {8, 0, 1, 2, 6, 20}, {NK[m][1], NK[m][0]}, &mv.mats[(size_t)li * 4 + m])))
+            if ((r = need(pfx + kMatNames[m], {8, 0, 1, 2, 6, 20, 30}, {NK[m][1], NK[m][0]},
+                          &mv.mats[(size_t)li * 4 + m])))
                 return r;
         // FFN1's epilogue produces what FFN2 reads: Q8_0 blocks for a block-quantized ffn2_w, floats otherwise
         if (q8_class(mv.mats[(size_t)li * 4 + 2]->type) != q8_class(mv.mats[(size_t)li * 4 + 3]->type)) {
-            err = pfx + "ffn1_w / ffn2_w: both block-quantized (Q8_0 / Q4_0 / Q5_0 / IQ4_NL) or both F32 / F16 (the "
-                        "exporter's ffn group) expected";
+            err = pfx + "ffn1_w / ffn2_w: both block-quantized (Q8_0 / Q4_0 / Q5_0 / IQ4_NL) or both F32 / F16 / BF16 "
+                        "(the exporter's ffn group) expected";
             return GSVCU_ERR_FORMAT;
         }
         for (int k = 0; k < 8; k++)
@@ -246,7 +249,8 @@ struct gsvcu_ctx {
     int V_pad = 0;
     uint4* predict_wq = nullptr;
     uint16_t* predict_wd = nullptr;
-    const void* predict_f16 = nullptr;   // F16 predict [V][D] (gemm_fx)
+    const void* predict_fx = nullptr;   // F16 / BF16 predict [V][D] (gemm_fx)
+    int predict_fx_type = FX_F16;
     // layer matrices: all Q8_0 (the fused decode step needs that), any F32 / F16 FFN (needs hf)
     bool all_q8 = true, ffn_float = false;
     float* hf = nullptr;                 // F32 / F16 FFN: relu(W1 n1 + b1) rows [Mmax][FF]
@@ -405,19 +409,28 @@ int gsvcu_ctx::load(const char* path) {
         CK(cudaMemcpy(*dst, src, bytes, cudaMemcpyHostToDevice));
         return GSVCU_OK;
     };
-    auto upload_emb = [&](const GgufTensor* t, float** dst) -> int {   // F16 tables widened exactly
+    auto upload_emb = [&](const GgufTensor* t, float** dst) -> int {   // F16 / BF16 tables widened exactly
         if (t->type == 0) return upload(t->data, t->nbytes, (void**)dst);
         const size_t n = t->nbytes / 2;
         std::vector<float> f32(n);
         const __half* h = (const __half*)t->data;
-        for (size_t i = 0; i < n; i++) f32[i] = __half2float(h[i]);
+        const uint16_t* b = (const uint16_t*)t->data;
+        for (size_t i = 0; i < n; i++) {
+            if (t->type == 1) {
+                f32[i] = __half2float(h[i]);
+            } else {   // BF16: the upper half of the F32 bits
+                const uint32_t bits = (uint32_t)b[i] << 16;
+                std::memcpy(&f32[i], &bits, 4);
+            }
+        }
         return upload(f32.data(), n * 4, (void**)dst);
     };
     TRY(upload_emb(mv.te, &text_emb));
     TRY(upload_emb(mv.ae, &audio_emb));
-    if (mv.pr->type == 1) {   // F16 predict, evaluated by gemm_fx
+    if (mv.pr->type == 1 || mv.pr->type == 30) {   // F16 / BF16 predict, evaluated by gemm_fx
         predict_q8 = false;
-        TRY(upload(mv.pr->data, mv.pr->nbytes, (void**)&predict_f16));
+        predict_fx_type = mv.pr->type == 1 ? FX_F16 : FX_BF16;
+        TRY(upload(mv.pr->data, mv.pr->nbytes, (void**)&predict_fx));
     } else if (q8_class(mv.pr->type)) {   // Q8_0 predict (Q4_0 / Q5_0 / IQ4_NL as Q8_0 blocks)
         predict_q8 = true;
         V_pad = (V + 31) / 32 * 32;
@@ -457,7 +470,7 @@ int gsvcu_ctx::load(const char* path) {
             const GgufTensor* t = mv.mats[(size_t)li * 4 + m];
             const int N = NK[m][0], K = NK[m][1];
             L[li].mt[m] = q8_class(t->type) ? 8 : (int)t->type;
-            if (!q8_class(t->type)) {   // F32 / F16: kept as stored, row-major [N][K]
+            if (!q8_class(t->type)) {   // F32 / F16 / BF16: kept as stored, row-major [N][K]
                 all_q8 = false;
                 ffn_float |= m >= 2;
                 void* dst = nullptr;
@@ -619,9 +632,10 @@ void gsvcu_ctx::release_slot(int slot) {
 // GEMM, as for the layer matrices. Returns the kernels launched.
 int gsvcu_ctx::launch_logits(const float* xr, int M, int8_t* xq_s, uint16_t* xd_s, float* out, cudaStream_t s) {
     const int V = hp.vocab_size;
-    if (predict_f16) {
+    if (predict_fx) {
         GemmFxParams g;
-        g.x = xr; g.ldx = D; g.M = M; g.w = predict_f16; g.wtype = FX_F16; g.N = V; g.K = D; g.y = out; g.ldy = V;
+        g.x = xr; g.ldx = D; g.M = M; g.w = predict_fx; g.wtype = predict_fx_type; g.N = V; g.K = D; g.y = out;
+        g.ldy = V;
         launch_gemm_fx(g, FXE_BIAS, s);
         return 1;
     }
@@ -784,7 +798,8 @@ void gsvcu_ctx::layer_gemm(int li, int m, const LayerIO& io, int M, const KvWrit
         return;
     }
     GemmFxParams g;
-    g.M = M; g.w = w.wf[m]; g.wtype = w.mt[m] == 1 ? FX_F16 : FX_F32; g.N = N[m]; g.K = K[m]; g.bias = bias[m];
+    g.M = M; g.w = w.wf[m]; g.wtype = w.mt[m] == 1 ? FX_F16 : w.mt[m] == 30 ? FX_BF16 : FX_F32;
+    g.N = N[m]; g.K = K[m]; g.bias = bias[m];
     g.ldx = K[m];
     if (m == 0) { g.x = io.x; g.y = io.qkv; g.kv = kv; launch_gemm_fx(g, FXE_BIAS, s); }
     if (m == 1) { g.x = io.attn; g.resid = io.x; g.y = io.pre; launch_gemm_fx(g, FXE_RESID, s); }
@@ -1477,12 +1492,12 @@ int gsvcu_op_f32_gemm(gsvcu_ctx* ctx, const float* x_dev, int32_t M, const float
 
 int gsvcu_op_fx_gemm(gsvcu_ctx* ctx, const float* x_dev, int32_t M, const void* w_dev, int32_t wtype, int32_t N,
                      int32_t K, const float* bias_dev, float* y_dev) {
-    if (!ctx || !x_dev || !w_dev || !y_dev || M < 0 || N <= 0 || K <= 0 || K % 64 || (wtype != 0 && wtype != 1) ||
+    if (!ctx || !x_dev || !w_dev || !y_dev || M < 0 || N <= 0 || K <= 0 || K % 64 || wtype < 0 || wtype > 2 ||
         ((uintptr_t)x_dev & 15) || ((uintptr_t)w_dev & 15))
         return GSVCU_ERR_ARG;
     DeviceGuard g(ctx->device);
     GemmFxParams p;
-    p.x = x_dev; p.ldx = K; p.M = M; p.w = w_dev; p.wtype = wtype == 1 ? FX_F16 : FX_F32; p.N = N; p.K = K;
+    p.x = x_dev; p.ldx = K; p.M = M; p.w = w_dev; p.wtype = wtype; p.N = N; p.K = K;
     p.bias = bias_dev; p.y = y_dev;
     launch_gemm_fx(p, FXE_BIAS, ctx->stream);
     CKC(ctx, cudaGetLastError());

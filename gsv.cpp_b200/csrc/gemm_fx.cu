@@ -1,10 +1,13 @@
-// gemm_fx.cu -- GEMM over F32 / F16 weight matrices: the layer matrices of the exporter's default
-// (F32) and --f16 files (tools/export_gguf/export.py:48-54) and an F16 ar.predict.
+// gemm_fx.cu -- GEMM over F32 / F16 / BF16 weight matrices: the layer matrices of the exporter's
+// default (F32) and --f16 files (tools/export_gguf/export.py:48-54) or of --spec ...=bf16, and an F16 /
+// BF16 ar.predict.
 //
 // Arithmetic: ggml's F32 / F16 mul_mat (src/gsv_ar.cpp:244,260,262,263,266) in the order of its
 // FMA-vectorised dot (ggml_vec_dot_f32 / ggml_vec_dot_f16 built with -mavx2 -mfma: four 8-lane
-// float accumulators over steps of 32 values). For an F16 matrix the activations are first rounded
-// to F16 (round-to-nearest-even), as ggml converts src1 to the matrix's vec_dot_type. Chain c
+// float accumulators over steps of 32 values). For an F16 / BF16 matrix the activations are first
+// rounded to F16 / BF16 (round-to-nearest-even), as ggml converts src1 to the matrix's vec_dot_type;
+// F16 and BF16 products are then exact in float. BF16 takes the same order (ggml's AVX2 BF16 dot may
+// pair the last two lane sums the other way round; this build defines it as the F16 order). Chain c
 // (c = 0..31) accumulates w[k] * x[k] for k = c, c + 32, ... with one FMA per term; the 32 chain sums
 // are then added pairwise: chain c with c^16 (accumulators 0+2, 1+3), ^8 (0+1), ^4 (the two 128-bit
 // halves), ^1 and ^2 (the two horizontal adds). K is a multiple of 32.
@@ -16,6 +19,8 @@
 // and weight rows through a 4-stage cp.async pipeline of 64-value slices (a lane reads k = 32t + c of
 // a slice from shared memory, conflict-free); the weight slices of the first stages are requested
 // before the wait for the predecessor kernel. K is a multiple of 64 here.
+#include <cuda_bf16.h>
+
 #include <type_traits>
 
 #include "kernels.h"
@@ -31,7 +36,8 @@ constexpr int FX_KC = 64;                        // k values per pipeline stage 
 constexpr int FX_ST = 4;                         // pipeline stages
 
 template <int WT>
-using fx_wt = typename std::conditional<WT == FX_F16, __half, float>::type;
+using fx_wt = typename std::conditional<WT == FX_F16, __half,
+                                        typename std::conditional<WT == FX_BF16, __nv_bfloat16, float>::type>::type;
 
 template <int WT>
 struct FxSmem {
@@ -46,6 +52,15 @@ __device__ __forceinline__ void fx_cp16(void* dst, const void* src) {
 
 __device__ __forceinline__ float widen(float v) { return v; }
 __device__ __forceinline__ float widen(__half v) { return __half2float(v); }
+__device__ __forceinline__ float widen(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+// the activation as ggml converts src1 for a matrix of type WT (vec_dot_type): F16 / BF16, RNE
+template <int WT>
+__device__ __forceinline__ float round_x(float v) {
+    if (WT == FX_F16) return __half2float(__float2half_rn(v));
+    if (WT == FX_BF16) return __bfloat162float(__float2bfloat16_rn(v));
+    return v;
+}
 
 // One level of the pairwise fold over the first N values of every lane: lanes l and l^OFF hold the
 // same outputs' sums of chain groups l and l^OFF; lane l keeps the lower half of the outputs when bit
@@ -133,8 +148,7 @@ __global__ void __launch_bounds__(128) k_gemm_fx(const GemmFxParams p) {
             float xv[FX_RW], wv[FX_CW];
 #pragma unroll
             for (int r = 0; r < FX_RW; r++) {
-                const float v = sm.x[st][wr + r][32 * t + lane];
-                xv[r] = WT == FX_F16 ? __half2float(__float2half_rn(v)) : v;
+                xv[r] = round_x<WT>(sm.x[st][wr + r][32 * t + lane]);
             }
 #pragma unroll
             for (int j = 0; j < FX_CW; j++) wv[j] = widen(sm.w[st][wc + j][32 * t + lane]);
@@ -189,6 +203,7 @@ void launch_wt(const GemmFxParams& p, int epi, cudaStream_t s) {
 void launch_gemm_fx(const GemmFxParams& p, int epi, cudaStream_t s) {
     if (p.M <= 0 || p.N <= 0 || p.K % FX_KC) return;
     if (p.wtype == FX_F16) launch_wt<FX_F16>(p, epi, s);
+    else if (p.wtype == FX_BF16) launch_wt<FX_BF16>(p, epi, s);
     else launch_wt<FX_F32>(p, epi, s);
 }
 

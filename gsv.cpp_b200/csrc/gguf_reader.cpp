@@ -131,7 +131,10 @@ bool GgufFile::open(const std::string& path, std::string& err) {
         if (!c.ok) { err = "corrupt GGUF tensor info"; return false; }
         switch (T.type) {
             case 0: T.nbytes = (uint64_t)ne * 4; break;
-            case 1: T.nbytes = (uint64_t)ne * 2; break;
+            case 1:    // F16
+            case 30:   // BF16
+                T.nbytes = (uint64_t)ne * 2;
+                break;
             case 2:    // Q4_0: fp16 d + 16 bytes of nibbles per 32 values
             case 20:   // IQ4_NL: fp16 d + 16 bytes of nibbles (table indices)
             case 6:    // Q5_0: fp16 d + 4 bytes of high bits + 16 bytes of nibbles

@@ -68,11 +68,12 @@ cudaError_t gemm_q8_init_device();
 void pack_q8_0_host(const uint8_t* raw, int N, int K, uint8_t* wq_out, uint16_t* wd_out);
 
 // ------------------------------------------------------------ F32 / F16 weight GEMM (gemm_fx.cu)
-// y[m][n] = sum_k w[n][k] * x(m, k) for F32 / F16 layer matrices and an F16 predict, in the order of
-// ggml's FMA-vectorised dot: x rounded to F16 for an F16 w, 32 float FMA chains (chain c takes
+// y[m][n] = sum_k w[n][k] * x(m, k) for F32 / F16 / BF16 layer matrices and an F16 / BF16 predict, in
+// the order of ggml's FMA-vectorised dot: x rounded to F16 / BF16 for an F16 / BF16 w (round to nearest
+// even), 32 float FMA chains (chain c takes
 // k = c, c + 32, ...) added pairwise as chains c^16, ^8, ^4, ^1, ^2. K % 64 == 0; w row-major [N][K];
 // x, w and every row of both 16-byte aligned (ldx * 4 and K * element size multiples of 16).
-enum { FX_F32 = 0, FX_F16 = 1 };
+enum { FX_F32 = 0, FX_F16 = 1, FX_BF16 = 2 };
 enum { FXE_BIAS = 0, FXE_RESID = 1, FXE_RELU = 2 };   // y = acc + b (+ K/V store); (r + acc) + b; relu(acc + b)
 struct GemmFxParams {
     const float* x = nullptr;

@@ -46,10 +46,10 @@ def write_model(path: str, seed: int = 0, dims: Dims | None = None, mat_type: st
                 ln_noise: float = 0.02, predict_type: str = "f32", emb_type: str = "f32",
                 ffn_type: str | None = None) -> str:
     """mat_type is the type of the attention matrices (the exporter's --spec attn=...) and, unless
-    ffn_type is given, of the FFN matrices (--spec ffn=...): "q8_0", "q4_0", "q5_0", "iq4_nl", "f16" or
-    "f32" (iq4_nl: the reference's tools/quantize_gguf.cpp tier, quantized by iq4_nl_blocks). predict_type
-    "q8_0" / "q4_0" / "q5_0" / "iq4_nl" / "f16" stores ar.predict in that type (--spec predict=...);
-    emb_type "f16" stores the
+    ffn_type is given, of the FFN matrices (--spec ffn=...): "q8_0", "q4_0", "q5_0", "iq4_nl", "f16",
+    "bf16" or "f32" (iq4_nl: the reference's tools/quantize_gguf.cpp tier, quantized by iq4_nl_blocks).
+    predict_type "q8_0" / "q4_0" / "q5_0" / "iq4_nl" / "f16" / "bf16" stores ar.predict in that type
+    (--spec predict=...); emb_type "f16" / "bf16" stores the
     text / audio embeddings as F16 (--spec emb=f16). The exporter's --f16 preset is
     mat_type="f16", predict_type="f16", emb_type="f16"; its default (no flags) is mat_type="f32"."""
     import gguf
@@ -59,7 +59,8 @@ def write_model(path: str, seed: int = 0, dims: Dims | None = None, mat_type: st
     D, FF = d.D, 4 * d.D
     types = {"q8_0": gguf.GGMLQuantizationType.Q8_0, "f32": gguf.GGMLQuantizationType.F32,
              "f16": gguf.GGMLQuantizationType.F16, "q4_0": gguf.GGMLQuantizationType.Q4_0,
-             "q5_0": gguf.GGMLQuantizationType.Q5_0, "iq4_nl": gguf.GGMLQuantizationType.IQ4_NL}
+             "q5_0": gguf.GGMLQuantizationType.Q5_0, "iq4_nl": gguf.GGMLQuantizationType.IQ4_NL,
+             "bf16": gguf.GGMLQuantizationType.BF16}
     qt = types[mat_type]
     ft = types[ffn_type or mat_type]
 
@@ -86,7 +87,8 @@ def write_model(path: str, seed: int = 0, dims: Dims | None = None, mat_type: st
         else:
             w.add_tensor(name, gguf.quants.quantize(arr, dtype), raw_dtype=dtype)
 
-    et = {"f32": gguf.GGMLQuantizationType.F32, "f16": gguf.GGMLQuantizationType.F16}[emb_type]
+    et = {"f32": gguf.GGMLQuantizationType.F32, "f16": gguf.GGMLQuantizationType.F16,
+          "bf16": gguf.GGMLQuantizationType.BF16}[emb_type]
     add("ar.text_emb", n(d.PV, D), et)
     add("ar.audio_emb", n(d.V, D), et)
     add("ar.bert_proj", n(D, d.BERT))

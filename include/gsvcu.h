@@ -74,11 +74,11 @@ const char* gsvcu_last_error(const gsvcu_ctx* ctx);
 
 /* Load an AR GGUF file (replaces gsv_ar::load, reference src/gsv_ar.cpp:490-705): tensor names of
  * tools/export_gguf/convert_ar.py:106-130. Attention / FFN matrices and predict Q8_0, Q4_0, Q5_0, IQ4_NL,
- * F32 or F16 (the exporter's --spec attn=.., ffn=.., predict=..; tools/quantize_gguf.cpp for IQ4_NL;
- * ffn1_w and ffn2_w of a layer both block-quantized or both F32 / F16), embeddings F32 or F16 (widened
- * on load), bert_proj, norms and biases F32. Q8_0 matrices, and Q4_0 / Q5_0 / IQ4_NL ones as the Q8_0
- * blocks of the same values, are repacked into tensor-core fragment order on the device; F32 / F16
- * matrices are kept as stored. */
+ * F32, F16 or BF16 (the exporter's --spec attn=.., ffn=.., predict=..; tools/quantize_gguf.cpp for
+ * IQ4_NL; ffn1_w and ffn2_w of a layer both block-quantized or both float), embeddings F32, F16 or
+ * BF16 (widened on load), bert_proj, norms and biases F32. Q8_0 matrices, and Q4_0 / Q5_0 / IQ4_NL ones
+ * as the Q8_0 blocks of the same values, are repacked into tensor-core fragment order on the device;
+ * F32 / F16 / BF16 matrices are kept as stored. */
 int gsvcu_load_gguf(gsvcu_ctx* ctx, const char* path);
 int gsvcu_get_hparams(const gsvcu_ctx* ctx, gsvcu_hparams* out);
 
@@ -193,9 +193,10 @@ int gsvcu_op_layernorm_q8(gsvcu_ctx* ctx, const float* v_dev, int32_t rows, cons
 int gsvcu_op_f32_gemm(gsvcu_ctx* ctx, const float* x_dev, int32_t M, const float* w_dev, int32_t N, int32_t K,
                       const float* add_dev, float* y_dev);
 
-/* Y[M][N] = W[N][K] . X[M][K]^T (+ bias[N], may be NULL) for an F32 (wtype 0) or F16 (wtype 1) layer
- * matrix (ggml F32 / F16 mul_mat, src/gsv_ar.cpp:244,260,262,263) in the order of ggml's FMA-vectorised
- * dot: X rounded to F16 for an F16 W, 32 float FMA chains (chain c over k = c, c + 32, ...) added
+/* Y[M][N] = W[N][K] . X[M][K]^T (+ bias[N], may be NULL) for an F32 (wtype 0), F16 (wtype 1) or BF16
+ * (wtype 2) layer matrix (ggml F32 / F16 / BF16 mul_mat, src/gsv_ar.cpp:244,260,262,263) in the order of
+ * ggml's FMA-vectorised dot: X rounded to F16 / BF16 for an F16 / BF16 W, 32 float FMA chains (chain c
+ * over k = c, c + 32, ...) added
  * pairwise as chains c^16, ^8, ^4, ^1, ^2. K a multiple of 64; x_dev and w_dev 16-byte aligned. */
 int gsvcu_op_fx_gemm(gsvcu_ctx* ctx, const float* x_dev, int32_t M, const void* w_dev, int32_t wtype, int32_t N,
                      int32_t K, const float* bias_dev, float* y_dev);

@@ -18,9 +18,10 @@
 //   * F32 mul_mat of ar.predict and of the BERT projection: products exact in double, accumulated
 //     in double, rounded once (ggml_vec_dot_f32; its scalar path rounds each product to float, its
 //     FMA-vectorised path accumulates in float: both within roundings of this).
-//   * F32 / F16 layer matrices and an F16 ar.predict: ggml's FMA-vectorised dot (-mavx2 -mfma;
-//     ggml_vec_dot_f32 / ggml_vec_dot_f16 with 4 accumulators x 8 float lanes): src1 rounded to F16
-//     for an F16 matrix (ggml's vec_dot_type), 32 float FMA chains (chain c takes k = c, c+32, ...),
+//   * F32 / F16 / BF16 layer matrices and an F16 / BF16 ar.predict: ggml's FMA-vectorised dot
+//     (-mavx2 -mfma; ggml_vec_dot_f32 / ggml_vec_dot_f16 with 4 accumulators x 8 float lanes): src1
+//     rounded to F16 / BF16 for an F16 / BF16 matrix (ggml's vec_dot_type; BF16 takes the F16 order),
+//     32 float FMA chains (chain c takes k = c, c+32, ...),
 //     folded as accumulators 0+2, 1+3, then 0+1, then the two 128-bit halves, then two horizontal
 //     adds -- i.e. chains c and c^16, ^8, ^4, ^1, ^2 added pairwise in that order (vec_dot_canon).
 //   * flash_attn_ext (F32 K/V), prefill rows: scores s = (float)(double sum of the exact products
@@ -167,14 +168,32 @@ inline int nthreads() {
 #endif
 }
 
-enum { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q5_0 = 6, T_Q8_0 = 8, T_IQ4_NL = 20 };
+enum { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q5_0 = 6, T_Q8_0 = 8, T_IQ4_NL = 20, T_BF16 = 30 };
 
-// A weight matrix [N][K] (torch [out,in] == ggml ne0=in): F32 or F16 (widened to f), or Q8_0 raw
-// GGUF blocks. canon: evaluated by vec_dot_canon (xf16: with src1 rounded to F16 first).
+// IEEE binary32 -> bfloat16 -> binary32, round-to-nearest-even (ggml's GGML_FP32_TO_BF16 for non-NaN)
+inline float round_bf16(float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return f;
+    u = ((u + 0x7fffu + ((u >> 16) & 1u)) >> 16) << 16;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
+inline float bf16_bits_to_float(uint16_t b) {
+    const uint32_t u = (uint32_t)b << 16;
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
+
+// A weight matrix [N][K] (torch [out,in] == ggml ne0=in): F32, F16 or BF16 (widened to f), or Q8_0
+// raw GGUF blocks. canon: evaluated by vec_dot_canon, with src1 rounded first to F16 (xround 1) or
+// BF16 (xround 2).
 struct Mat {
     int type = T_F32;
     int64_t N = 0, K = 0;
-    bool canon = false, xf16 = false;
+    bool canon = false;
+    int xround = 0;
     std::vector<float> f;
     std::vector<uint8_t> q;
 };
@@ -197,8 +216,10 @@ void mul_mat(const Mat& W, const float* X, int64_t M, float* Y) {
     const int64_t N = W.N, K = W.K;
     if (W.canon) {   // F32 / F16 layer matrices, F16 predict
         std::vector<float> xr(X, X + M * K);
-        if (W.xf16)
+        if (W.xround == 1)
             for (float& v : xr) v = round_f16(v);
+        if (W.xround == 2)
+            for (float& v : xr) v = round_bf16(v);
         #pragma omp parallel for num_threads(nthreads()) schedule(static)
         for (int64_t n = 0; n < N; n++) {
             const float* w = W.f.data() + n * K;
@@ -474,23 +495,25 @@ struct orc_model {
 namespace {
 
 // canon_f32: an F32 matrix is a layer matrix (vec_dot_canon) rather than the predict / BERT
-// projection (vec_dot_f32). F16 matrices are always evaluated by vec_dot_canon.
+// projection (vec_dot_f32). F16 / BF16 matrices are always evaluated by vec_dot_canon.
 bool set_mat(Mat& m, int type, const void* data, int64_t nbytes, int64_t N, int64_t K, std::string& err, const char* name,
              bool canon_f32 = false) {
     m.type = type;
     m.N = N;
     m.K = K;
-    m.canon = m.xf16 = false;
+    m.canon = false;
+    m.xround = 0;
     if (type == T_F32) {
         if (nbytes != N * K * 4) { err = std::string("bad size for ") + name; return false; }
         m.f.assign((const float*)data, (const float*)data + N * K);
         m.canon = canon_f32 && K % 32 == 0;
-    } else if (type == T_F16) {
+    } else if (type == T_F16 || type == T_BF16) {
         if (K % 32 || nbytes != N * K * 2) { err = std::string("bad size for ") + name; return false; }
         m.f.resize((size_t)(N * K));
         const uint16_t* h = (const uint16_t*)data;
-        for (int64_t i = 0; i < N * K; i++) m.f[(size_t)i] = f16_to_f32(h[i]);
-        m.canon = m.xf16 = true;
+        for (int64_t i = 0; i < N * K; i++) m.f[(size_t)i] = type == T_F16 ? f16_to_f32(h[i]) : bf16_bits_to_float(h[i]);
+        m.canon = true;
+        m.xround = type == T_F16 ? 1 : 2;
     } else if (type == T_Q8_0) {
         if (K % QK || nbytes != N * (K / QK) * Q8_BYTES) { err = std::string("bad size for ") + name; return false; }
         m.q.assign((const uint8_t*)data, (const uint8_t*)data + nbytes);
@@ -554,10 +577,10 @@ float half_bits_to_float(uint16_t h) {
 // values). The reference loader accepts F32 only (src/gsv_ar.cpp:633-637); F16 is what the exporter
 // writes for --spec emb=f16.
 bool set_emb(std::vector<float>& v, int type, const void* data, int64_t nbytes, int64_t n, std::string& err, const char* name) {
-    if (type == T_F16 && nbytes == n * 2) {
+    if ((type == T_F16 || type == T_BF16) && nbytes == n * 2) {
         v.resize((size_t)n);
         const uint16_t* h = (const uint16_t*)data;
-        for (int64_t i = 0; i < n; i++) v[(size_t)i] = half_bits_to_float(h[i]);
+        for (int64_t i = 0; i < n; i++) v[(size_t)i] = type == T_F16 ? half_bits_to_float(h[i]) : bf16_bits_to_float(h[i]);
         return true;
     }
     return set_vec(v, type, data, nbytes, n, err, name);
@@ -767,7 +790,7 @@ void orc_fp16_to_fp32(const uint16_t* x, float* y, int64_t n) { for (int64_t i =
 void orc_quantize_q8_0(const float* x, int64_t n, uint8_t* blocks) { quantize_q8_0(x, n, blocks); }
 
 // Y[M][N] = W[N][K] . X[M][K]^T with W raw Q8_0 / Q4_0 / Q5_0 / IQ4_NL blocks (type 8 / 2 / 6 / 20), F32
-// (type 0) or F16 (type 1);
+// (type 0), F16 (type 1) or BF16 (type 30);
 // layer != 0: W is a layer matrix (an F32 W is then evaluated like an F16 one, by vec_dot_canon).
 int orc_mul_mat(int type, const void* W, int64_t N, int64_t K, const float* X, int64_t M, float* Y, int layer) {
     Mat w;
@@ -775,7 +798,7 @@ int orc_mul_mat(int type, const void* W, int64_t N, int64_t K, const float* X, i
     const int64_t nbytes = type == T_Q8_0   ? N * (K / QK) * Q8_BYTES
                            : type == T_Q4_0 || type == T_IQ4_NL ? N * (K / QK) * 18
                            : type == T_Q5_0 ? N * (K / QK) * 22
-                                            : N * K * (type == T_F16 ? 2 : 4);
+                                            : N * K * (type == T_F16 || type == T_BF16 ? 2 : 4);
     if (!set_mat(w, type, W, nbytes, N, K, err, "W", layer != 0)) return -1;
     mul_mat(w, X, M, Y);
     return 0;

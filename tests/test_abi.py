@@ -56,7 +56,8 @@ def test_inspect_rejects_bad_files(model_small, model_f32_small, tmp_path):
 @pytest.mark.parametrize("mat_type,ffn_type,predict_type,emb_type", [
     ("q8_0", "q8_0", "q8_0", "f32"), ("q8_0", "q8_0", "f32", "f16"), ("f16", "f16", "f16", "f16"),
     ("f32", "f32", "f32", "f32"), ("q8_0", "f16", "f32", "f32"), ("f16", "q8_0", "f32", "f32"),
-    ("q4_0", "q4_0", "q4_0", "f32"), ("q8_0", "q5_0", "q5_0", "f16"), ("q8_0", "iq4_nl", "iq4_nl", "f32")])
+    ("q4_0", "q4_0", "q4_0", "f32"), ("q8_0", "q5_0", "q5_0", "f16"), ("q8_0", "iq4_nl", "iq4_nl", "f32"),
+    ("bf16", "bf16", "bf16", "bf16")])
 def test_inspect_export_formats(mat_type, ffn_type, predict_type, emb_type):
     """The exporter's formats: Q8_0 / Q4_0 / Q5_0 / F16 predict, F16 embeddings, F32 / F16 / Q4_0 / Q5_0
     attention and FFN matrices and mixed attn / ffn groups are accepted (GPU parity:
@@ -72,7 +73,7 @@ def test_inspect_export_formats(mat_type, ffn_type, predict_type, emb_type):
 
 def test_inspect_rejects_unsupported_matrix_types(model_small, tmp_path):
     """ffn1_w and ffn2_w of a layer are one group (block-quantized Q8_0 / Q4_0 / Q5_0, or F32 / F16); other
-    ggml types (K-quants, Q4_1 / Q5_1, BF16) are refused with the tensor named."""
+    ggml types (K-quants, Q4_1 / Q5_1) are refused with the tensor named."""
     import gguf
     from conftest import gguf_retyped_copy
     T = gguf.GGMLQuantizationType

@@ -391,6 +391,7 @@ EXPORT_FORMATS = [   # (attention matrices, FFN matrices, predict, embeddings)
     ("q4_0", "q4_0", "q4_0", "f32"),   # --spec attn=q4_0,ffn=q4_0,predict=q4_0
     ("q8_0", "q5_0", "q5_0", "f16"),   # --spec attn=q8_0,ffn=q5_0,predict=q5_0,emb=f16
     ("q8_0", "iq4_nl", "iq4_nl", "f32"),   # tools/quantize_gguf.cpp --spec attn=q8_0,ffn=iq4_nl,predict=iq4_nl
+    ("bf16", "bf16", "bf16", "bf16"),  # --spec attn=bf16,ffn=bf16,predict=bf16,emb=bf16
 ]
 
 

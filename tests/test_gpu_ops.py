@@ -127,20 +127,25 @@ def test_f32_gemm_double_accumulation(ctx, MNK):
     np.testing.assert_allclose(got, ref, rtol=1e-6, atol=1e-7)
 
 
-@pytest.mark.parametrize("wtype", [0, 1])
+@pytest.mark.parametrize("wtype", [0, 1, 2])
 @pytest.mark.parametrize("MNK", [(37, 1536, 512), (64, 512, 2048), (5, 1025, 512), (300, 2048, 512)])
 def test_fx_gemm_bitexact(ctx, wtype, MNK):
-    """F32 / F16 layer matrices (exporter default / --f16): equal, bit for bit, to the oracle's ggml
-    FMA-vectorised dot (X rounded to F16 for an F16 W; 32 float chains folded pairwise), ragged M / N."""
+    """F32 / F16 / BF16 layer matrices (exporter default / --f16 / --spec ...=bf16): equal, bit for bit, to
+    the oracle's ggml FMA-vectorised dot (X rounded to F16 / BF16 for an F16 / BF16 W; 32 float chains
+    folded pairwise), ragged M / N."""
+    import gguf
     M, N, K = MNK
     rng = np.random.default_rng(M + N + K + wtype)
     x = rng.standard_normal((M, K)).astype(np.float32)
     w = (0.02 * rng.standard_normal((N, K))).astype(np.float32)
-    wraw = w.astype(np.float16) if wtype == 1 else w
+    if wtype == 2:
+        wraw = gguf.quants.quantize(w, gguf.GGMLQuantizationType.BF16).view(np.int16)
+    else:
+        wraw = w.astype(np.float16) if wtype == 1 else w
     bias = (0.02 * rng.standard_normal(N)).astype(np.float32)
-    tw = torch.from_numpy(wraw.view(np.int16) if wtype == 1 else wraw).cuda()
+    tw = torch.from_numpy(wraw.view(np.int16) if wtype else wraw).cuda()
     y = torch.empty((M, N), dtype=torch.float32, device="cuda")
-    ref = O.mul_mat(wraw, wtype, N, K, x, layer=True)
+    ref = O.mul_mat(wraw, {0: 0, 1: 1, 2: 30}[wtype], N, K, x, layer=True)
     ctx.op_fx_gemm(dev(x), M, tw, wtype, N, K, None, y)
     ctx.sync()
     assert np.array_equal(y.cpu().numpy().view(np.uint32), ref.view(np.uint32))

@@ -243,10 +243,11 @@ def test_oracle_batch_equals_single(model_small):
         assert np.array_equal(tb[b], ts[0])
 
 
-def test_oracle_f16_embeddings_widen_exactly(tmp_path):
-    """F16 text/audio embeddings (exporter --spec emb=f16) are widened exactly: the oracle gives the
-    same logits, bit for bit, as for a twin file storing those values as F32."""
-    e16 = S.write_model(str(tmp_path / "e16.gguf"), seed=21, dims=S.Dims(NL=2), emb_type="f16")
+@pytest.mark.parametrize("emb_type", ["f16", "bf16"])
+def test_oracle_f16_embeddings_widen_exactly(tmp_path, emb_type):
+    """F16 / BF16 text/audio embeddings (exporter --spec emb=f16 / bf16) are widened exactly: the oracle
+    gives the same logits, bit for bit, as for a twin file storing those values as F32."""
+    e16 = S.write_model(str(tmp_path / "e16.gguf"), seed=21, dims=S.Dims(NL=2), emb_type=emb_type)
     import gguf
     F32 = gguf.GGMLQuantizationType.F32
     e32 = gguf_retyped_copy(e16, str(tmp_path / "e32.gguf"), {"ar.text_emb": F32, "ar.audio_emb": F32})
@@ -303,7 +304,13 @@ def test_oracle_q8_0_logits_restated(tmp_path):
         assert np.array_equal(acc, logits[b]), b
 
 
-@pytest.mark.parametrize("wtype,K", [(0, 512), (1, 512), (1, 2048)])
+def _round_bf16(x):
+    """float32 -> bfloat16 -> float32, round to nearest even (finite values)."""
+    u = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    return (((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16).astype(np.uint32).view(np.float32)
+
+
+@pytest.mark.parametrize("wtype,K", [(0, 512), (1, 512), (1, 2048), (30, 512)])
 def test_oracle_float_layer_mul_mat_restated(wtype, K):
     """F32 / F16 layer matrices (exporter default / --f16): the oracle's mul_mat equals, bit for bit, a
     numpy restatement of ggml's FMA-vectorised dot -- src1 rounded to F16 for an F16 matrix, 32 float
@@ -315,6 +322,11 @@ def test_oracle_float_layer_mul_mat_restated(wtype, K):
     if wtype == 1:
         wraw = W.astype(np.float16)
         wf, xr = wraw.astype(np.float32), X.astype(np.float16).astype(np.float32)
+    elif wtype == 30:   # BF16: gguf-py's converter (round to nearest even), src1 rounded the same way
+        import gguf
+        wraw = gguf.quants.quantize(W, gguf.GGMLQuantizationType.BF16)
+        wf, xr = _round_bf16(W), _round_bf16(X)
+        assert np.array_equal(wraw.view(np.uint16).astype(np.uint32) << 16, wf.view(np.uint32))
     else:
         wraw, wf, xr = W, W, X
     got = O.mul_mat(wraw, wtype, N, K, X, layer=True)
