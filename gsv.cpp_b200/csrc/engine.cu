@@ -17,7 +17,8 @@ namespace {
 
 struct LayerW {
     int mt[4] = {8, 8, 8, 8};   // qkv, out, ffn1, ffn2: 8 Q8_0 kernels (Q8_0 / Q4_0 / Q5_0 / IQ4_NL), 0 F32,
-                                //   1 F16, 30 BF16 (gemm_fx)
+                                //   1 F16, 30 BF16 (k_gemm_fx), 3 Q4_1 / Q5_1 (k_gemm_qm)
+    uint16_t* wm[4] = {nullptr, nullptr, nullptr, nullptr};  // Q4_1 / Q5_1: fp16 m planes (d in wd)
     uint4* wq[4] = {nullptr, nullptr, nullptr, nullptr};     // Q8_0: fragment planes
     uint16_t* wd[4] = {nullptr, nullptr, nullptr, nullptr};  //       matching fp16 scale planes
     const void* wf[4] = {nullptr, nullptr, nullptr, nullptr};  // F32 / F16: the GGUF rows [N][K] as stored
@@ -115,6 +116,28 @@ constexpr int8_t kIq4nl[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 
 // nibbles values 16..31) as Q8_0 blocks holding the same signed values (nibble - 8, five-bit value - 16,
 // kIq4nl[nibble]) and the same d. ggml's dot of these types against Q8_0 activations is an integer
 // block dot scaled by d_w * d_x, so on these blocks it is the Q8_0 block dot.
+// Q4_1 / Q5_1 blocks (ggml block_q4_1 / block_q5_1: fp16 d, m; Q5_1 then the fifth bits as a
+// little-endian uint32; then 16 bytes of nibbles, values 0..15 low, 16..31 high) as k_gemm_qm's planes:
+// the unsigned values as bytes [N][K], d and m as fp16 [N][K/32] each.
+void unpack_q_1(const GgufTensor* t, std::vector<uint8_t>& q, std::vector<uint16_t>& d, std::vector<uint16_t>& mn) {
+    const size_t bs = t->type == 7 ? 24 : 20, nb = t->nbytes / bs;
+    q.resize(nb * 32);
+    d.resize(nb);
+    mn.resize(nb);
+    for (size_t b = 0; b < nb; b++) {
+        const uint8_t* src = t->data + b * bs;
+        std::memcpy(&d[b], src, 2);
+        std::memcpy(&mn[b], src + 2, 2);
+        const uint8_t* qs = src + (t->type == 7 ? 8 : 4);
+        uint32_t qh = 0;
+        if (t->type == 7) std::memcpy(&qh, src + 4, 4);
+        for (int j = 0; j < 16; j++) {
+            q[b * 32 + j] = (uint8_t)((qs[j] & 15) | (((qh >> j) & 1u) << 4));
+            q[b * 32 + j + 16] = (uint8_t)((qs[j] >> 4) | (((qh >> (j + 16)) & 1u) << 4));
+        }
+    }
+}
+
 std::vector<uint8_t> to_q8_0_blocks(const GgufTensor* t) {
     const size_t bs = t->type == 6 ? 22 : 18, nb = t->nbytes / bs;
     std::vector<uint8_t> out(nb * 34);
@@ -171,7 +194,8 @@ int validate_model(const GgufFile& f, ModelView& mv, std::string& err) {
         return GSVCU_ERR_FORMAT;
     }
     const int NL = hp.n_layer, V = hp.vocab_size, PV = hp.phoneme_vocab_size, BD = hp.bert_dim;
-    // accepted ggml types: 0 = F32, 1 = F16, 2 = Q4_0, 6 = Q5_0, 8 = Q8_0, 20 = IQ4_NL, 30 = BF16
+    // accepted ggml types: 0 = F32, 1 = F16, 2 = Q4_0, 3 = Q4_1, 6 = Q5_0, 7 = Q5_1, 8 = Q8_0, 20 = IQ4_NL,
+    // 30 = BF16
     auto need = [&](const std::string& name, std::vector<uint32_t> types, std::vector<int64_t> dims,
                     const GgufTensor** out) -> int {
         const GgufTensor* t = f.tensor(name);
@@ -180,7 +204,7 @@ int validate_model(const GgufFile& f, ModelView& mv, std::string& err) {
             std::string want;
             for (uint32_t ty : types) want += (want.empty() ? "" : " or ") + std::to_string(ty);
             err = "tensor " + name + " has ggml type " + std::to_string(t->type) + ", expected " + want +
-                  " (0 F32, 1 F16, 2 Q4_0, 6 Q5_0, 8 Q8_0, 20 IQ4_NL, 30 BF16)";
+                  " (0 F32, 1 F16, 2 Q4_0, 3 Q4_1, 6 Q5_0, 7 Q5_1, 8 Q8_0, 20 IQ4_NL, 30 BF16)";
             return GSVCU_ERR_FORMAT;
         }
         int64_t ne = 1, ne_want = 1;
@@ -195,12 +219,13 @@ int validate_model(const GgufFile& f, ModelView& mv, std::string& err) {
     };
     int r;
     // embeddings: F32, or F16 / BF16 (exporter --spec emb=f16 / bf16) widened to F32 on load; predict and
-    // layer matrices: F32, F16, BF16, Q8_0, Q4_0, Q5_0 or IQ4_NL (--spec predict=.., attn=.., ffn=..)
+    // layer matrices: F32, F16, BF16, Q8_0, Q4_0, Q4_1, Q5_0, Q5_1 or IQ4_NL (--spec predict=.., attn=..,
+    // ffn=..)
     if ((r = need("ar.text_emb", {0, 1, 30}, {D, PV}, &mv.te)) ||
         (r = need("ar.audio_emb", {0, 1, 30}, {D, V}, &mv.ae)) ||
         (r = need("ar.bert_proj", {0}, {BD, D}, &mv.bp)) || (r = need("ar.bert_proj_b", {0}, {D}, &mv.bb)) ||
         (r = need("ar.text_pe_alpha", {0}, {1}, &mv.ta)) || (r = need("ar.audio_pe_alpha", {0}, {1}, &mv.aa)) ||
-        (r = need("ar.predict", {0, 8, 1, 2, 6, 20, 30}, {D, V}, &mv.pr)))
+        (r = need("ar.predict", {0, 8, 1, 2, 3, 6, 7, 20, 30}, {D, V}, &mv.pr)))
         return r;
     std::memcpy(&hp.text_pe_alpha, mv.ta->data, 4);
     std::memcpy(&hp.audio_pe_alpha, mv.aa->data, 4);
@@ -211,12 +236,13 @@ int validate_model(const GgufFile& f, ModelView& mv, std::string& err) {
     for (int li = 0; li < NL; li++) {
         const std::string pfx = "transformer.block" + std::to_string(li) + ".";
         for (int m = 0; m < 4; m++)
-            if ((r = need(pfx + kMatNames[m], {8, 0, 1, 2, 6, 20, 30}, {NK[m][1], NK[m][0]},
+            if ((r = need(pfx + kMatNames[m], {8, 0, 1, 2, 3, 6, 7, 20, 30}, {NK[m][1], NK[m][0]},
                           &mv.mats[(size_t)li * 4 + m])))
                 return r;
-        // FFN1's epilogue produces what FFN2 reads: Q8_0 blocks for a block-quantized ffn2_w, floats otherwise
+        // FFN1's epilogue produces what FFN2 reads: Q8_0 blocks for a Q8_0-class ffn2_w, floats otherwise
+        // (F32 / F16 / BF16, and Q4_1 / Q5_1, whose kernel quantizes its float rows to Q8_1 itself)
         if (q8_class(mv.mats[(size_t)li * 4 + 2]->type) != q8_class(mv.mats[(size_t)li * 4 + 3]->type)) {
-            err = pfx + "ffn1_w / ffn2_w: both block-quantized (Q8_0 / Q4_0 / Q5_0 / IQ4_NL) or both F32 / F16 / BF16 "
+            err = pfx + "ffn1_w / ffn2_w: both Q8_0 / Q4_0 / Q5_0 / IQ4_NL or both F32 / F16 / BF16 / Q4_1 / Q5_1 "
                         "(the exporter's ffn group) expected";
             return GSVCU_ERR_FORMAT;
         }
@@ -249,8 +275,9 @@ struct gsvcu_ctx {
     int V_pad = 0;
     uint4* predict_wq = nullptr;
     uint16_t* predict_wd = nullptr;
-    const void* predict_fx = nullptr;   // F16 / BF16 predict [V][D] (gemm_fx)
+    const void* predict_fx = nullptr;   // F16 / BF16 predict [V][D], or Q4_1 / Q5_1 values (gemm_fx.cu)
     int predict_fx_type = FX_F16;
+    uint16_t *predict_qd = nullptr, *predict_qm = nullptr;   // Q4_1 / Q5_1 predict: d, m planes
     // layer matrices: all Q8_0 (the fused decode step needs that), any F32 / F16 FFN (needs hf)
     bool all_q8 = true, ffn_float = false;
     float* hf = nullptr;                 // F32 / F16 FFN: relu(W1 n1 + b1) rows [Mmax][FF]
@@ -431,6 +458,15 @@ int gsvcu_ctx::load(const char* path) {
         predict_q8 = false;
         predict_fx_type = mv.pr->type == 1 ? FX_F16 : FX_BF16;
         TRY(upload(mv.pr->data, mv.pr->nbytes, (void**)&predict_fx));
+    } else if (mv.pr->type == 3 || mv.pr->type == 7) {   // Q4_1 / Q5_1 predict (k_gemm_qm)
+        predict_q8 = false;
+        predict_fx_type = FX_QM;
+        std::vector<uint8_t> q;
+        std::vector<uint16_t> qd, qm;
+        unpack_q_1(mv.pr, q, qd, qm);
+        TRY(upload(q.data(), q.size(), (void**)&predict_fx));
+        TRY(upload(qd.data(), qd.size() * 2, (void**)&predict_qd));
+        TRY(upload(qm.data(), qm.size() * 2, (void**)&predict_qm));
     } else if (q8_class(mv.pr->type)) {   // Q8_0 predict (Q4_0 / Q5_0 / IQ4_NL as Q8_0 blocks)
         predict_q8 = true;
         V_pad = (V + 31) / 32 * 32;
@@ -469,7 +505,20 @@ int gsvcu_ctx::load(const char* path) {
         for (int m = 0; m < 4; m++) {
             const GgufTensor* t = mv.mats[(size_t)li * 4 + m];
             const int N = NK[m][0], K = NK[m][1];
-            L[li].mt[m] = q8_class(t->type) ? 8 : (int)t->type;
+            L[li].mt[m] = q8_class(t->type) ? 8 : t->type == 7 ? 3 : (int)t->type;
+            if (t->type == 3 || t->type == 7) {   // Q4_1 / Q5_1: value bytes + d, m planes (k_gemm_qm)
+                all_q8 = false;
+                ffn_float |= m >= 2;
+                std::vector<uint8_t> q;
+                std::vector<uint16_t> qd, qm;
+                unpack_q_1(t, q, qd, qm);
+                void* dst = nullptr;
+                TRY(upload(q.data(), q.size(), &dst));
+                L[li].wf[m] = dst;
+                TRY(upload(qd.data(), qd.size() * 2, (void**)&L[li].wd[m]));
+                TRY(upload(qm.data(), qm.size() * 2, (void**)&L[li].wm[m]));
+                continue;
+            }
             if (!q8_class(t->type)) {   // F32 / F16 / BF16: kept as stored, row-major [N][K]
                 all_q8 = false;
                 ffn_float |= m >= 2;
@@ -635,7 +684,7 @@ int gsvcu_ctx::launch_logits(const float* xr, int M, int8_t* xq_s, uint16_t* xd_
     if (predict_fx) {
         GemmFxParams g;
         g.x = xr; g.ldx = D; g.M = M; g.w = predict_fx; g.wtype = predict_fx_type; g.N = V; g.K = D; g.y = out;
-        g.ldy = V;
+        g.ldy = V; g.wd = predict_qd; g.wm = predict_qm;
         launch_gemm_fx(g, FXE_BIAS, s);
         return 1;
     }
@@ -798,8 +847,8 @@ void gsvcu_ctx::layer_gemm(int li, int m, const LayerIO& io, int M, const KvWrit
         return;
     }
     GemmFxParams g;
-    g.M = M; g.w = w.wf[m]; g.wtype = w.mt[m] == 1 ? FX_F16 : w.mt[m] == 30 ? FX_BF16 : FX_F32;
-    g.N = N[m]; g.K = K[m]; g.bias = bias[m];
+    g.M = M; g.w = w.wf[m]; g.wtype = w.mt[m] == 1 ? FX_F16 : w.mt[m] == 30 ? FX_BF16 : w.mt[m] == 3 ? FX_QM : FX_F32;
+    g.wd = w.wd[m]; g.wm = w.wm[m]; g.N = N[m]; g.K = K[m]; g.bias = bias[m];
     g.ldx = K[m];
     if (m == 0) { g.x = io.x; g.y = io.qkv; g.kv = kv; launch_gemm_fx(g, FXE_BIAS, s); }
     if (m == 1) { g.x = io.attn; g.resid = io.x; g.y = io.pre; launch_gemm_fx(g, FXE_RESID, s); }

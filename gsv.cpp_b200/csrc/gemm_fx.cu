@@ -1,6 +1,7 @@
-// gemm_fx.cu -- GEMM over F32 / F16 / BF16 weight matrices: the layer matrices of the exporter's
-// default (F32) and --f16 files (tools/export_gguf/export.py:48-54) or of --spec ...=bf16, and an F16 /
-// BF16 ar.predict.
+// gemm_fx.cu -- GEMMs that read float activations: F32 / F16 / BF16 weight matrices (the layer
+// matrices of the exporter's default (F32) and --f16 files, tools/export_gguf/export.py:48-54, or of
+// --spec ...=bf16, and an F16 / BF16 ar.predict: k_gemm_fx) and Q4_1 / Q5_1 matrices (k_gemm_qm, which
+// quantizes its activation rows to Q8_1 itself).
 //
 // Arithmetic: ggml's F32 / F16 mul_mat (src/gsv_ar.cpp:244,260,262,263,266) in the order of its
 // FMA-vectorised dot (ggml_vec_dot_f32 / ggml_vec_dot_f16 built with -mavx2 -mfma: four 8-lane
@@ -97,6 +98,24 @@ __device__ __forceinline__ void kv_store(const KvWrite& kv, int n, int f, float 
     else ((__half*)kv.pool)[e] = __float2half_rn(y);
 }
 
+// One output's epilogue: bias (+ K/V page store), residual or bias + ReLU.
+template <int EPI>
+__device__ __forceinline__ void fx_store(const GemmFxParams& p, int m, int n, float a) {
+    if (m >= p.M || n >= p.N) return;
+    const float bias = p.bias ? p.bias[n] : 0.0f;
+    if (EPI == FXE_BIAS) {
+        const float y = __fadd_rn(a, bias);
+        if (n < (p.n_store ? p.n_store : p.N)) p.y[(size_t)m * (p.ldy ? p.ldy : p.N) + n] = y;
+        if (p.kv.pool && n >= D) kv_store(p.kv, m, n, y);
+    } else if (EPI == FXE_RESID) {
+        const float r = p.resid[(size_t)m * p.N + n];
+        p.y[(size_t)m * p.N + n] = __fadd_rn(__fadd_rn(r, a), bias);
+    } else {   // FXE_RELU
+        const float h = __fadd_rn(a, bias);
+        p.y[(size_t)m * p.N + n] = h > 0.0f ? h : 0.0f;
+    }
+}
+
 template <int WT, int EPI>
 __global__ void __launch_bounds__(128) k_gemm_fx(const GemmFxParams p) {
     __shared__ __align__(16) FxSmem<WT> sm;
@@ -168,24 +187,71 @@ __global__ void __launch_bounds__(128) k_gemm_fx(const GemmFxParams p) {
     // i.e. row 4 b4 + 2 b3 + b2 and column 4 b0 + 2 b1 + e of the warp tile
     const int m = m0 + ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
     const int nb = n0 + (lane & 1) * 4 + ((lane >> 1) & 1) * 2;
-    if (m >= p.M) return;
 #pragma unroll
-    for (int e = 0; e < 2; e++) {
-        const int n = nb + e;
-        if (n >= p.N) continue;
-        const float bias = p.bias ? p.bias[n] : 0.0f;
-        if (EPI == FXE_BIAS) {
-            const float y = __fadd_rn(acc[e], bias);
-            if (n < (p.n_store ? p.n_store : p.N)) p.y[(size_t)m * (p.ldy ? p.ldy : p.N) + n] = y;
-            if (p.kv.pool && n >= D) kv_store(p.kv, m, n, y);
-        } else if (EPI == FXE_RESID) {
-            const float r = p.resid[(size_t)m * p.N + n];
-            p.y[(size_t)m * p.N + n] = __fadd_rn(__fadd_rn(r, acc[e]), bias);
-        } else {   // FXE_RELU
-            const float h = __fadd_rn(acc[e], bias);
-            p.y[(size_t)m * p.N + n] = h > 0.0f ? h : 0.0f;
+    for (int e = 0; e < 2; e++) fx_store<EPI>(p, m, nb + e, acc[e]);
+}
+
+// Q4_1 / Q5_1 matrices: ggml's Q4_1 / Q5_1 x Q8_1 mul_mat in the order of its portable C dot. The CTA
+// first quantizes its 16 activation rows to Q8_1 in shared memory (quantize_row_q8_1_ref: the Q8_0
+// values and fp16 scale, plus s = fp16(sum of the values * d) with the unrounded d); thread (r, c) then
+// runs output (row r, column c) block by block: sumi = the exact integer dot of the weight's unsigned
+// 4- / 5-bit values (bytes since load) with the activation block, acc = acc + fma(d_w*d_x, sumi,
+// m_w*s_x). K is a multiple of 32, at most QM_KMAX.
+constexpr int QM_T = 16, QM_KMAX = 2048;
+
+template <int EPI>
+__global__ void __launch_bounds__(256) k_gemm_qm(const GemmFxParams p) {
+    __shared__ __align__(16) int8_t xq[QM_T][QM_KMAX];
+    __shared__ float xd[QM_T][QM_KMAX / 32], xs[QM_T][QM_KMAX / 32];
+    const int tid = threadIdx.x, nb = p.K / 32;
+    const int mt = blockIdx.y * QM_T, nt = blockIdx.x * QM_T;
+    griddep_wait();
+    griddep_launch();
+    for (int i = tid; i < QM_T * nb; i += 256) {
+        const int r = i / nb, b = i - r * nb;
+        const float* src = p.x + (size_t)min(mt + r, p.M - 1) * p.ldx + b * 32;
+        float v[32], amax = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            v[j] = src[j];
+            amax = fmaxf(amax, fabsf(v[j]));
         }
+        float d, id;
+        q8_scale(amax, d, id);
+        int sum = 0;
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            const int8_t q = q8_val(v[j], id);
+            xq[r][b * 32 + j] = q;
+            sum += q;
+        }
+        xd[r][b] = h2f(f2h(d));
+        xs[r][b] = h2f(f2h(__fmul_rn((float)sum, d)));
     }
+    __syncthreads();
+    const int r = tid / QM_T, c = tid % QM_T;
+    const int nc = min(nt + c, p.N - 1);
+    const int4* wrow = (const int4*)((const int8_t*)p.w + (size_t)nc * p.K);
+    const uint16_t* wdr = p.wd + (size_t)nc * nb;
+    const uint16_t* wmr = p.wm + (size_t)nc * nb;
+    float acc = 0.0f;
+    for (int b = 0; b < nb; b++) {
+        const int4 w0 = __ldg(wrow + 2 * b), w1 = __ldg(wrow + 2 * b + 1);
+        const int4* xr = (const int4*)&xq[r][b * 32];
+        const int4 x0 = xr[0], x1 = xr[1];
+        int sumi = __dp4a(w0.x, x0.x, 0);
+        sumi = __dp4a(w0.y, x0.y, sumi);
+        sumi = __dp4a(w0.z, x0.z, sumi);
+        sumi = __dp4a(w0.w, x0.w, sumi);
+        sumi = __dp4a(w1.x, x1.x, sumi);
+        sumi = __dp4a(w1.y, x1.y, sumi);
+        sumi = __dp4a(w1.z, x1.z, sumi);
+        sumi = __dp4a(w1.w, x1.w, sumi);
+        const float dd = __fmul_rn(h2f(wdr[b]), xd[r][b]);
+        const float ms = __fmul_rn(h2f(wmr[b]), xs[r][b]);
+        acc = __fadd_rn(acc, fmaf(dd, (float)sumi, ms));
+    }
+    fx_store<EPI>(p, mt + r, nt + c, acc);
 }
 
 template <int WT>
@@ -201,7 +267,18 @@ void launch_wt(const GemmFxParams& p, int epi, cudaStream_t s) {
 }  // namespace
 
 void launch_gemm_fx(const GemmFxParams& p, int epi, cudaStream_t s) {
-    if (p.M <= 0 || p.N <= 0 || p.K % FX_KC) return;
+    if (p.M <= 0 || p.N <= 0) return;
+    if (p.wtype == FX_QM) {
+        if (p.K % 32 || p.K > QM_KMAX) return;
+        const dim3 grid((p.N + QM_T - 1) / QM_T, (p.M + QM_T - 1) / QM_T), block(256);
+        switch (epi) {
+            case FXE_BIAS: launch_pdl(k_gemm_qm<FXE_BIAS>, grid, block, 0, s, p); break;
+            case FXE_RESID: launch_pdl(k_gemm_qm<FXE_RESID>, grid, block, 0, s, p); break;
+            default: launch_pdl(k_gemm_qm<FXE_RELU>, grid, block, 0, s, p); break;
+        }
+        return;
+    }
+    if (p.K % FX_KC) return;
     if (p.wtype == FX_F16) launch_wt<FX_F16>(p, epi, s);
     else if (p.wtype == FX_BF16) launch_wt<FX_BF16>(p, epi, s);
     else launch_wt<FX_F32>(p, epi, s);

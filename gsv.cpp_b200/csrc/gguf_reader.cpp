@@ -138,9 +138,12 @@ bool GgufFile::open(const std::string& path, std::string& err) {
             case 2:    // Q4_0: fp16 d + 16 bytes of nibbles per 32 values
             case 20:   // IQ4_NL: fp16 d + 16 bytes of nibbles (table indices)
             case 6:    // Q5_0: fp16 d + 4 bytes of high bits + 16 bytes of nibbles
-            case 8:   // Q8_0: fp16 d + 32 int8
+            case 8:    // Q8_0: fp16 d + 32 int8
+            case 3:    // Q4_1: fp16 d, m + 16 bytes of nibbles
+            case 7:    // Q5_1: fp16 d, m + 4 bytes of high bits + 16 bytes of nibbles
                 if (T.dims[0] % 32) { err = "block-quantized row not a multiple of 32: " + T.name; return false; }
-                T.nbytes = (uint64_t)ne / 32 * (T.type == 8 ? 34 : T.type == 6 ? 22 : 18);
+                T.nbytes = (uint64_t)ne / 32 *
+                           (T.type == 8 ? 34 : T.type == 7 ? 24 : T.type == 6 ? 22 : T.type == 3 ? 20 : 18);
                 break;
             default: T.nbytes = 0; break;   // unsupported types are rejected by the consumer
         }

@@ -46,9 +46,9 @@ def write_model(path: str, seed: int = 0, dims: Dims | None = None, mat_type: st
                 ln_noise: float = 0.02, predict_type: str = "f32", emb_type: str = "f32",
                 ffn_type: str | None = None) -> str:
     """mat_type is the type of the attention matrices (the exporter's --spec attn=...) and, unless
-    ffn_type is given, of the FFN matrices (--spec ffn=...): "q8_0", "q4_0", "q5_0", "iq4_nl", "f16",
-    "bf16" or "f32" (iq4_nl: the reference's tools/quantize_gguf.cpp tier, quantized by iq4_nl_blocks).
-    predict_type "q8_0" / "q4_0" / "q5_0" / "iq4_nl" / "f16" / "bf16" stores ar.predict in that type
+    ffn_type is given, of the FFN matrices (--spec ffn=...): "q8_0", "q4_0", "q4_1", "q5_0", "q5_1",
+    "iq4_nl", "f16", "bf16" or "f32" (iq4_nl: the reference's tools/quantize_gguf.cpp tier, quantized
+    by iq4_nl_blocks). predict_type "f32" or any of those stores ar.predict in that type
     (--spec predict=...); emb_type "f16" / "bf16" stores the
     text / audio embeddings as F16 (--spec emb=f16). The exporter's --f16 preset is
     mat_type="f16", predict_type="f16", emb_type="f16"; its default (no flags) is mat_type="f32"."""
@@ -60,7 +60,8 @@ def write_model(path: str, seed: int = 0, dims: Dims | None = None, mat_type: st
     types = {"q8_0": gguf.GGMLQuantizationType.Q8_0, "f32": gguf.GGMLQuantizationType.F32,
              "f16": gguf.GGMLQuantizationType.F16, "q4_0": gguf.GGMLQuantizationType.Q4_0,
              "q5_0": gguf.GGMLQuantizationType.Q5_0, "iq4_nl": gguf.GGMLQuantizationType.IQ4_NL,
-             "bf16": gguf.GGMLQuantizationType.BF16}
+             "bf16": gguf.GGMLQuantizationType.BF16, "q4_1": gguf.GGMLQuantizationType.Q4_1,
+             "q5_1": gguf.GGMLQuantizationType.Q5_1}
     qt = types[mat_type]
     ft = types[ffn_type or mat_type]
 

@@ -33,6 +33,9 @@
 //     (decode_attention_canonical), the evaluation order of the library's decode kernel.
 //   * layernorm_affine (P:1535-1585): v = (x + r) + bias, mean / E[v^2] in double,
 //     var = E[v^2] - mean^2, inv = 1/sqrtf(var + eps), y = ((v - mean)*inv)*w + b.
+//   * Q4_1 / Q5_1 mul_mat: src1 quantized to Q8_1 (the Q8_0 values and scale plus s = fp16(sum * d)),
+//     per block sumf = sumf + fma(d_w*d_x, sumi, m_w*s_x) (ggml's portable vec_dot_q4_1_q8_1 as GCC
+//     contracts it).
 //   * add_act ReLU (P:1587-1620): y = max(a + b, 0).
 // Where the reference's C++ is compiled with -mavx2 -mfma (CMakeLists.txt:88-92) GCC contracts
 // a*b+c into an FMA; the restatement writes those FMAs out with fmaf() and is itself compiled
@@ -129,6 +132,26 @@ void quantize_q8_0(const float* x, int64_t n, uint8_t* blocks) {
     }
 }
 
+// quantize_row_q8_1_ref (the src1 conversion of ggml's Q4_1 / Q5_1 mul_mat): the Q8_0 values and
+// scale, plus s = fp16(sum of the 32 values * d) with the unrounded d. Returns the values [n], the
+// fp16-rounded d and s of each block as floats.
+void quantize_q8_1(const float* x, int64_t n, int8_t* q, float* d_out, float* s_out) {
+    for (int64_t i = 0; i < n / QK; i++) {
+        float amax = 0.0f;
+        for (int j = 0; j < QK; j++) amax = std::max(amax, std::fabs(x[i * QK + j]));
+        const float d = amax / 127.0f;
+        const float id = d != 0.0f ? 1.0f / d : 0.0f;
+        int sum = 0;
+        for (int j = 0; j < QK; j++) {
+            const int v = (int)std::roundf(x[i * QK + j] * id);
+            q[i * QK + j] = (int8_t)v;
+            sum += v;
+        }
+        d_out[i] = f16_to_f32(f32_to_f16(d));
+        s_out[i] = f16_to_f32(f32_to_f16((float)sum * d));
+    }
+}
+
 inline float q8_d(const uint8_t* blk) {
     uint16_t h;
     std::memcpy(&h, blk, 2);
@@ -168,7 +191,7 @@ inline int nthreads() {
 #endif
 }
 
-enum { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q5_0 = 6, T_Q8_0 = 8, T_IQ4_NL = 20, T_BF16 = 30 };
+enum { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q4_1 = 3, T_Q5_0 = 6, T_Q5_1 = 7, T_Q8_0 = 8, T_IQ4_NL = 20, T_BF16 = 30 };
 
 // IEEE binary32 -> bfloat16 -> binary32, round-to-nearest-even (ggml's GGML_FP32_TO_BF16 for non-NaN)
 inline float round_bf16(float f) {
@@ -186,9 +209,9 @@ inline float bf16_bits_to_float(uint16_t b) {
     return f;
 }
 
-// A weight matrix [N][K] (torch [out,in] == ggml ne0=in): F32, F16 or BF16 (widened to f), or Q8_0
-// raw GGUF blocks. canon: evaluated by vec_dot_canon, with src1 rounded first to F16 (xround 1) or
-// BF16 (xround 2).
+// A weight matrix [N][K] (torch [out,in] == ggml ne0=in): F32, F16 or BF16 (widened to f), Q8_0 raw
+// GGUF blocks (q), or Q4_1 / Q5_1 as their unsigned values (qv, 0..31) and per-block d, m (dm).
+// canon: evaluated by vec_dot_canon, with src1 rounded first to F16 (xround 1) or BF16 (xround 2).
 struct Mat {
     int type = T_F32;
     int64_t N = 0, K = 0;
@@ -196,6 +219,8 @@ struct Mat {
     int xround = 0;
     std::vector<float> f;
     std::vector<uint8_t> q;
+    std::vector<int8_t> qv;
+    std::vector<float> dm;   // [N][K/32][2]: d, m
 };
 
 // ggml's AVX2 F32/F16 dot in float (K a multiple of 32): chain c accumulates w[k]*x[k] for
@@ -225,6 +250,30 @@ void mul_mat(const Mat& W, const float* X, int64_t M, float* Y) {
             const float* w = W.f.data() + n * K;
             for (int64_t m = 0; m < M; m++) Y[m * N + n] = vec_dot_canon(K, w, xr.data() + m * K);
         }
+        return;
+    }
+    if (W.type == T_Q4_1 || W.type == T_Q5_1) {
+        // ggml_vec_dot_q4_1_q8_1 / q5_1_q8_1 (portable C): per block the exact integer dot sumi of the
+        // unsigned values with the Q8_1 values, then sumf += (d_w*d_x)*sumi + m_w*s_x, which GCC
+        // contracts (-mfma) to sumf + fma(d_w*d_x, sumi, m_w*s_x); blocks in order.
+        const int64_t nb = K / QK;
+        std::vector<int8_t> xq((size_t)(M * K));
+        std::vector<float> xd((size_t)(M * nb)), xs((size_t)(M * nb));
+        for (int64_t m = 0; m < M; m++) quantize_q8_1(X + m * K, K, xq.data() + m * K, xd.data() + m * nb, xs.data() + m * nb);
+        #pragma omp parallel for num_threads(nthreads()) schedule(static)
+        for (int64_t n = 0; n < N; n++)
+            for (int64_t m = 0; m < M; m++) {
+                float acc = 0.0f;
+                for (int64_t b = 0; b < nb; b++) {
+                    int32_t sumi = 0;
+                    for (int j = 0; j < QK; j++)
+                        sumi += (int32_t)W.qv[(size_t)(n * K + b * QK + j)] * (int32_t)xq[(size_t)(m * K + b * QK + j)];
+                    const float dd = W.dm[(size_t)((n * nb + b) * 2)] * xd[(size_t)(m * nb + b)];
+                    const float ms = W.dm[(size_t)((n * nb + b) * 2 + 1)] * xs[(size_t)(m * nb + b)];
+                    acc = acc + std::fmaf(dd, (float)sumi, ms);
+                }
+                Y[m * N + n] = acc;
+            }
         return;
     }
     if (W.type == T_Q8_0) {
@@ -517,6 +566,28 @@ bool set_mat(Mat& m, int type, const void* data, int64_t nbytes, int64_t N, int6
     } else if (type == T_Q8_0) {
         if (K % QK || nbytes != N * (K / QK) * Q8_BYTES) { err = std::string("bad size for ") + name; return false; }
         m.q.assign((const uint8_t*)data, (const uint8_t*)data + nbytes);
+    } else if (type == T_Q4_1 || type == T_Q5_1) {
+        // ggml block_q4_1 {fp16 d, m; u8 qs[16]} / block_q5_1 {fp16 d, m; u8 qh[4]; u8 qs[16]}: value i is
+        // d * q_i + m, q_i the low (i < 16) or high (i >= 16) nibble of qs[i % 16] (+ bit i of qh as bit 4)
+        const int64_t bs = type == T_Q4_1 ? 20 : 24, nb = N * (K / QK);
+        if (K % QK || nbytes != nb * bs) { err = std::string("bad size for ") + name; return false; }
+        m.qv.assign((size_t)(N * K), 0);
+        m.dm.assign((size_t)(nb * 2), 0.0f);
+        for (int64_t b = 0; b < nb; b++) {
+            const uint8_t* src = (const uint8_t*)data + b * bs;
+            uint16_t h[2];
+            std::memcpy(h, src, 4);
+            m.dm[(size_t)(b * 2)] = f16_to_f32(h[0]);
+            m.dm[(size_t)(b * 2 + 1)] = f16_to_f32(h[1]);
+            const uint8_t* qs = src + (type == T_Q4_1 ? 4 : 8);
+            uint32_t qh = 0;
+            if (type == T_Q5_1) std::memcpy(&qh, src + 4, 4);
+            for (int i = 0; i < QK; i++) {
+                int q = i < 16 ? (qs[i] & 0x0f) : (qs[i - 16] >> 4);
+                if (type == T_Q5_1) q += (int)((qh >> i) & 1u) * 16;
+                m.qv[(size_t)(b * QK + i)] = (int8_t)q;
+            }
+        }
     } else if (type == T_Q4_0 || type == T_Q5_0 || type == T_IQ4_NL) {
         // ggml block_q4_0 / block_iq4_nl {fp16 d; u8 qs[16]} / block_q5_0 {fp16 d; u8 qh[4]; u8 qs[16]}:
         // value i (0..31) is d * (q_i - 8) / d * kvalues_iq4nl[q_i] / d * (q_i - 16), q_i = low (i < 16) or
@@ -789,13 +860,15 @@ void orc_fp32_to_fp16(const float* x, uint16_t* y, int64_t n) { for (int64_t i =
 void orc_fp16_to_fp32(const uint16_t* x, float* y, int64_t n) { for (int64_t i = 0; i < n; i++) y[i] = f16_to_f32(x[i]); }
 void orc_quantize_q8_0(const float* x, int64_t n, uint8_t* blocks) { quantize_q8_0(x, n, blocks); }
 
-// Y[M][N] = W[N][K] . X[M][K]^T with W raw Q8_0 / Q4_0 / Q5_0 / IQ4_NL blocks (type 8 / 2 / 6 / 20), F32
-// (type 0), F16 (type 1) or BF16 (type 30);
+// Y[M][N] = W[N][K] . X[M][K]^T with W raw Q8_0 / Q4_0 / Q5_0 / IQ4_NL / Q4_1 / Q5_1 blocks (type 8 / 2 /
+// 6 / 20 / 3 / 7), F32 (type 0), F16 (type 1) or BF16 (type 30);
 // layer != 0: W is a layer matrix (an F32 W is then evaluated like an F16 one, by vec_dot_canon).
 int orc_mul_mat(int type, const void* W, int64_t N, int64_t K, const float* X, int64_t M, float* Y, int layer) {
     Mat w;
     std::string err;
     const int64_t nbytes = type == T_Q8_0   ? N * (K / QK) * Q8_BYTES
+                           : type == T_Q4_1 ? N * (K / QK) * 20
+                           : type == T_Q5_1 ? N * (K / QK) * 24
                            : type == T_Q4_0 || type == T_IQ4_NL ? N * (K / QK) * 18
                            : type == T_Q5_0 ? N * (K / QK) * 22
                                             : N * K * (type == T_F16 || type == T_BF16 ? 2 : 4);

@@ -77,7 +77,11 @@ def gguf_retyped_copy(src, dst, retype):
             elif ty == F16:
                 w.add_tensor(t.name, arr.astype(np.float16), raw_dtype=F16)
             else:
-                w.add_tensor(t.name, gguf.quants.quantize(arr, ty), raw_dtype=ty)
+                try:
+                    w.add_tensor(t.name, gguf.quants.quantize(arr, ty), raw_dtype=ty)
+                except NotImplementedError:   # no gguf-py quantizer (K-quants): all-zero blocks
+                    bs, ts = gguf.GGML_QUANT_SIZES[ty]
+                    w.add_tensor(t.name, np.zeros((arr.shape[0], arr.shape[1] // bs * ts), np.uint8), raw_dtype=ty)
         else:
             w.add_tensor(t.name, data, raw_dtype=t.tensor_type)
     w.write_header_to_file()

@@ -392,15 +392,17 @@ EXPORT_FORMATS = [   # (attention matrices, FFN matrices, predict, embeddings)
     ("q8_0", "q5_0", "q5_0", "f16"),   # --spec attn=q8_0,ffn=q5_0,predict=q5_0,emb=f16
     ("q8_0", "iq4_nl", "iq4_nl", "f32"),   # tools/quantize_gguf.cpp --spec attn=q8_0,ffn=iq4_nl,predict=iq4_nl
     ("bf16", "bf16", "bf16", "bf16"),  # --spec attn=bf16,ffn=bf16,predict=bf16,emb=bf16
+    ("q4_1", "q4_1", "q4_1", "f32"),   # --spec attn=q4_1,ffn=q4_1,predict=q4_1
+    ("q8_0", "q5_1", "q5_1", "f16"),   # --spec attn=q8_0,ffn=q5_1,predict=q5_1,emb=f16
 ]
 
 
 @pytest.mark.parametrize("mat_type,ffn_type,predict_type,emb_type", EXPORT_FORMATS)
 def test_export_formats_match_oracle(mat_type, ffn_type, predict_type, emb_type):
-    """The exporter's formats besides --q8: Q8_0 / Q4_0 / Q5_0 / F16 predict (logits by the Q8_0 GEMM over
-    Q8_0 rows, or by the F16 dot), F16 embeddings (widened on load), F32 / F16 attention and FFN matrices
-    (ggml's FMA-vectorised F32 / F16 dot), Q4_0 / Q5_0 matrices (repacked into Q8_0 blocks on load) and
-    mixes of the attn / ffn groups. A teacher-forced decode trace (fused and unfused steps; float
+    """The exporter's formats besides --q8: Q8_0 / Q4_0 / Q5_0 / IQ4_NL / Q4_1 / Q5_1 / F16 / BF16 predict,
+    F16 / BF16 embeddings (widened on load), F32 / F16 / BF16 attention and FFN matrices (ggml's
+    FMA-vectorised dot), Q4_0 / Q5_0 / IQ4_NL matrices (repacked into Q8_0 blocks on load), Q4_1 / Q5_1
+    matrices (ggml's Q8_1 dot) and mixes of the attn / ffn groups. A teacher-forced decode trace (fused and unfused steps; float
     matrices always run unfused) equals the oracle bit for bit, and so does a sampled generate through
     the graph-captured decode step."""
     import gsvcu

@@ -367,3 +367,46 @@ def test_oracle_q4_0_q5_0_iq4_nl_as_q8_0_blocks(wtype):
     assert np.array_equal(got, O.mul_mat(q8, 8, N, K, X))
     ref = X.astype(np.float64) @ deq.reshape(N, K).astype(np.float64).T
     assert np.abs(got - ref).max() <= 2e-2 * np.abs(ref).max()   # Q8_0 activation rounding only
+
+
+@pytest.mark.parametrize("wtype", [3, 7])
+def test_oracle_q4_1_q5_1_restated(wtype):
+    """Q4_1 / Q5_1 matrices (exporter --spec ...=q4_1 / q5_1): the oracle's mul_mat equals, bit for bit, a
+    numpy restatement of ggml's portable Q4_1 / Q5_1 x Q8_1 dot -- src1 quantized to Q8_1 (Q8_0 values
+    and scale, s = fp16(sum * d)), per block the integer dot sumi of the unsigned weight values with
+    them, sumf = sumf + fma(d_w*d_x, sumi, m_w*s_x) in block order. The weight values are unpacked
+    independently and checked against gguf-py's dequantizer."""
+    import gguf
+    ty = gguf.GGMLQuantizationType(wtype)
+    rng = np.random.default_rng(50 + wtype)
+    N, K, M = 40, 512, 5
+    nb = K // 32
+    W = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    X = rng.standard_normal((M, K)).astype(np.float32)
+    raw = gguf.quants.quantize(W, ty)
+    blk = raw.reshape(N, nb, 20 if wtype == 3 else 24)
+    d = blk[..., 0:2].copy().view(np.float16)[..., 0].astype(np.float32)
+    mn = blk[..., 2:4].copy().view(np.float16)[..., 0].astype(np.float32)
+    qs = blk[..., 4:20] if wtype == 3 else blk[..., 8:24]
+    q = np.concatenate([qs & 15, qs >> 4], -1).astype(np.int64)
+    if wtype == 7:
+        qh = blk[..., 4:8].copy().view("<u4")[..., 0]
+        q += ((qh[..., None] >> np.arange(32, dtype=np.uint32)) & 1).astype(np.int64) * 16
+    deq = gguf.quants.dequantize(raw, ty).reshape(N, nb, 32)
+    assert np.array_equal(d[..., None] * q.astype(np.float32) + mn[..., None], deq)
+    xb = X.reshape(M, nb, 32)
+    dx = (np.abs(xb).max(-1) / np.float32(127)).astype(np.float32)
+    idx = np.where(dx != 0, np.float32(1) / np.where(dx != 0, dx, np.float32(1)), np.float32(0)).astype(np.float32)
+    v = (xb * idx[..., None]).astype(np.float32)
+    qx = (np.sign(v) * np.floor(np.abs(v).astype(np.float64) + 0.5)).astype(np.int64)     # roundf
+    assert np.array_equal(qx.astype(np.int8).view(np.uint8),
+                          O.quantize_q8_0(X).reshape(M, nb, 34)[..., 2:])
+    sx = (qx.sum(-1).astype(np.float32) * dx).astype(np.float16).astype(np.float32)
+    dxr = dx.astype(np.float16).astype(np.float32)
+    sumi = np.einsum("nbj,mbj->mnb", q, qx).astype(np.float32)
+    acc = np.zeros((M, N), np.float32)
+    for b in range(nb):
+        dd = (d[None, :, b] * dxr[:, None, b]).astype(np.float32)
+        ms = (mn[None, :, b] * sx[:, None, b]).astype(np.float32)
+        acc = (acc + _fmaf(dd, sumi[..., b], ms)).astype(np.float32)
+    assert np.array_equal(O.mul_mat(raw, wtype, N, K, X), acc)
