@@ -42,6 +42,66 @@ def iq4_nl_blocks(arr: np.ndarray) -> np.ndarray:
     return np.concatenate([d.view(np.uint8).reshape(N, K // 32, 2), qs], axis=-1).reshape(N, K // 32 * 18)
 
 
+def kquant_blocks(arr: np.ndarray, kind: str) -> np.ndarray:
+    """Q4_K / Q5_K / Q6_K blocks of a float [N][K] array (K % 256 == 0) from a plain quantizer (not ggml's
+    scale search), packed as block_q4_K {fp16 d, dmin; 12 bytes of 6-bit scales / mins; 128 bytes of
+    nibbles}, block_q5_K {d, dmin, scales, 32 bytes of fifth bits, nibbles}, block_q6_K {128 bytes of low
+    nibbles; 64 bytes of 2-bit highs; 16 int8 scales; fp16 d}."""
+    N, K = arr.shape
+    sb = arr.reshape(N * K // 256, 256).astype(np.float64)
+    nsb = sb.shape[0]
+    if kind == "q6_k":
+        sub = sb.reshape(nsb, 16, 16)
+        s = np.abs(sub).max(-1) / 31.0
+        d = (np.abs(s).max(-1) / 127.0).astype(np.float16)
+        df = np.where(d.astype(np.float64) == 0, 1.0, d.astype(np.float64))
+        sc = np.clip(np.round(s / df[:, None]), -128, 127).astype(np.int8)
+        step = df[:, None] * np.where(sc == 0, 1, sc)
+        q = (np.clip(np.round(sub / step[..., None]), -32, 31) + 32).astype(np.uint8).reshape(nsb, 256)
+        out = np.zeros((nsb, 210), np.uint8)
+        for hh in range(2):
+            for k in range(4):
+                v = q[:, 128 * hh + 32 * k: 128 * hh + 32 * k + 32]
+                lo = v & 15
+                col = 64 * hh + (k & 1) * 32
+                out[:, col:col + 32] |= lo if k < 2 else (lo << 4)
+                out[:, 128 + 32 * hh: 160 + 32 * hh] |= ((v >> 4) & 3) << (2 * k)
+        out[:, 192:208] = sc.view(np.uint8)
+        out[:, 208:210] = d.view(np.uint8).reshape(nsb, 2)
+        return out.reshape(N, K // 256 * 210)
+    top = 15 if kind == "q4_k" else 31
+    sub = sb.reshape(nsb, 8, 32)
+    mn = np.maximum(0.0, -sub.min(-1))
+    s = (sub.max(-1) + mn) / top
+    d = (s.max(-1) / 63.0).astype(np.float16)
+    dmin = (mn.max(-1) / 63.0).astype(np.float16)
+    df = np.where(d.astype(np.float64) == 0, 1.0, d.astype(np.float64))
+    dmf = np.where(dmin.astype(np.float64) == 0, 1.0, dmin.astype(np.float64))
+    sc = np.clip(np.round(s / df[:, None]), 1, 63).astype(np.uint8)
+    mq = np.clip(np.round(mn / dmf[:, None]), 0, 63).astype(np.uint8)
+    q = np.clip(np.round((sub + (dmf[:, None] * mq)[..., None]) / (df[:, None] * sc)[..., None]), 0, top)
+    q = q.astype(np.uint8).reshape(nsb, 256)
+    scales = np.zeros((nsb, 12), np.uint8)
+    for j in range(8):
+        if j < 4:
+            scales[:, j] |= sc[:, j]
+            scales[:, j + 4] |= mq[:, j]
+        else:
+            scales[:, j + 4] |= (sc[:, j] & 15) | ((mq[:, j] & 15) << 4)
+            scales[:, j - 4] |= (sc[:, j] >> 4) << 6
+            scales[:, j] |= (mq[:, j] >> 4) << 6
+    qs = np.zeros((nsb, 128), np.uint8)
+    qh = np.zeros((nsb, 32), np.uint8)
+    for g in range(4):
+        lo, hi = q[:, 64 * g: 64 * g + 32], q[:, 64 * g + 32: 64 * g + 64]
+        qs[:, 32 * g: 32 * g + 32] = (lo & 15) | ((hi & 15) << 4)
+        qh |= ((lo >> 4) & 1) << (2 * g)
+        qh |= ((hi >> 4) & 1) << (2 * g + 1)
+    hdr = np.concatenate([d.view(np.uint8).reshape(nsb, 2), dmin.view(np.uint8).reshape(nsb, 2), scales], -1)
+    out = np.concatenate([hdr, qs] if kind == "q4_k" else [hdr, qh, qs], -1)
+    return out.reshape(N, -1)
+
+
 def write_model(path: str, seed: int = 0, dims: Dims | None = None, mat_type: str = "q8_0",
                 ln_noise: float = 0.02, predict_type: str = "f32", emb_type: str = "f32",
                 ffn_type: str | None = None) -> str:

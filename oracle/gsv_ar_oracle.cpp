@@ -112,6 +112,7 @@ inline float round_f16(float f) { return f16_to_f32(f32_to_f16(f)); }
 
 // ------------------------------------------------------------------ Q8_0
 constexpr int QK = 32;
+constexpr int QKK = 256;   // K-quant super-block
 constexpr int Q8_BYTES = 34;   // fp16 d + 32 x int8
 
 // quantize_row_q8_0_ref semantics (ggml-quants.c; pinned via gguf-py's Q8_0 quantizer).
@@ -149,6 +150,34 @@ void quantize_q8_1(const float* x, int64_t n, int8_t* q, float* d_out, float* s_
         }
         d_out[i] = f16_to_f32(f32_to_f16(d));
         s_out[i] = f16_to_f32(f32_to_f16((float)sum * d));
+    }
+}
+
+// quantize_row_q8_K_ref (the src1 conversion of ggml's K-quant mul_mat), per 256 values: max = the
+// value of largest magnitude (first one wins), iscale = -127/max, q = min(127, nearest_int(iscale*x))
+// (round half to even), d = 1/iscale (0, q = 0 for an all-zero block), bsums = sums of 16 values.
+void quantize_q8_k(const float* x, int64_t n, int8_t* q, float* d_out, int32_t* bsums) {
+    for (int64_t i = 0; i < n / QKK; i++) {
+        const float* xb = x + i * QKK;
+        float amax = 0.0f, mx = 0.0f;
+        for (int j = 0; j < QKK; j++)
+            if (std::fabs(xb[j]) > amax) {
+                amax = std::fabs(xb[j]);
+                mx = xb[j];
+            }
+        if (amax == 0.0f) {
+            d_out[i] = 0.0f;
+            for (int j = 0; j < QKK; j++) q[i * QKK + j] = 0;
+        } else {
+            const float iscale = -127.0f / mx;
+            for (int j = 0; j < QKK; j++) q[i * QKK + j] = (int8_t)std::min(127, (int)std::nearbyint(iscale * xb[j]));
+            d_out[i] = 1.0f / iscale;
+        }
+        for (int g = 0; g < QKK / 16; g++) {
+            int s = 0;
+            for (int j = 0; j < 16; j++) s += q[i * QKK + g * 16 + j];
+            bsums[i * (QKK / 16) + g] = s;
+        }
     }
 }
 
@@ -191,7 +220,8 @@ inline int nthreads() {
 #endif
 }
 
-enum { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q4_1 = 3, T_Q5_0 = 6, T_Q5_1 = 7, T_Q8_0 = 8, T_IQ4_NL = 20, T_BF16 = 30 };
+enum { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q4_1 = 3, T_Q5_0 = 6, T_Q5_1 = 7, T_Q8_0 = 8, T_Q4_K = 12, T_Q5_K = 13,
+       T_Q6_K = 14, T_IQ4_NL = 20, T_BF16 = 30 };
 
 // IEEE binary32 -> bfloat16 -> binary32, round-to-nearest-even (ggml's GGML_FP32_TO_BF16 for non-NaN)
 inline float round_bf16(float f) {
@@ -220,7 +250,9 @@ struct Mat {
     std::vector<float> f;
     std::vector<uint8_t> q;
     std::vector<int8_t> qv;
-    std::vector<float> dm;   // [N][K/32][2]: d, m
+    std::vector<float> dm;   // [N][K/32][2]: d, m; K-quants: [N][K/256][2]: d, dmin
+    std::vector<int16_t> ksc;   // K-quants: sub-block scale of every value [N][K]
+    std::vector<uint8_t> kmin;  // Q4_K / Q5_K: the 8 sub-block mins of each super-block [N][K/256][8]
 };
 
 // ggml's AVX2 F32/F16 dot in float (K a multiple of 32): chain c accumulates w[k]*x[k] for
@@ -250,6 +282,43 @@ void mul_mat(const Mat& W, const float* X, int64_t M, float* Y) {
             const float* w = W.f.data() + n * K;
             for (int64_t m = 0; m < M; m++) Y[m * N + n] = vec_dot_canon(K, w, xr.data() + m * K);
         }
+        return;
+    }
+    if (W.type == T_Q4_K || W.type == T_Q5_K || W.type == T_Q6_K) {
+        // ggml_vec_dot_q{4,5,6}_K_q8_K (portable C): per super-block eight integer lane sums,
+        // aux32[l] = sum over the values e = l (mod 8) of scale(e) * a_e * q_e; the lanes accumulate
+        // sums[l] += (d_w*d_x) * aux32[l] (contracted to fma) over super-blocks; Q4_K / Q5_K also
+        // sumf -= (dmin_w*d_x) * sum_g bsums[g]*min[g/2] (contracted); at the end sumf += sums[l], l = 0..7.
+        const int64_t nsb = K / QKK;
+        std::vector<int8_t> xq((size_t)(M * K));
+        std::vector<float> xd((size_t)(M * nsb));
+        std::vector<int32_t> xb((size_t)(M * nsb * 16));
+        for (int64_t m = 0; m < M; m++)
+            quantize_q8_k(X + m * K, K, xq.data() + m * K, xd.data() + m * nsb, xb.data() + m * nsb * 16);
+        const bool has_min = W.type != T_Q6_K;
+        #pragma omp parallel for num_threads(nthreads()) schedule(static)
+        for (int64_t n = 0; n < N; n++)
+            for (int64_t m = 0; m < M; m++) {
+                float sums[8] = {}, sumf = 0.0f;
+                for (int64_t sb = 0; sb < nsb; sb++) {
+                    int32_t aux32[8] = {};
+                    for (int e = 0; e < QKK; e++) {
+                        const size_t wi = (size_t)(n * K + sb * QKK + e);
+                        aux32[e % 8] += (int32_t)W.ksc[wi] * ((int32_t)W.qv[wi] * (int32_t)xq[(size_t)(m * K + sb * QKK + e)]);
+                    }
+                    const float d = W.dm[(size_t)((n * nsb + sb) * 2)] * xd[(size_t)(m * nsb + sb)];
+                    for (int l = 0; l < 8; l++) sums[l] = std::fmaf(d, (float)aux32[l], sums[l]);
+                    if (has_min) {
+                        int32_t sumi = 0;
+                        for (int g = 0; g < 16; g++)
+                            sumi += xb[(size_t)((m * nsb + sb) * 16 + g)] * (int32_t)W.kmin[(size_t)((n * nsb + sb) * 8 + g / 2)];
+                        const float dmin = W.dm[(size_t)((n * nsb + sb) * 2 + 1)] * xd[(size_t)(m * nsb + sb)];
+                        sumf = std::fmaf(-dmin, (float)sumi, sumf);
+                    }
+                }
+                for (int l = 0; l < 8; l++) sumf = sumf + sums[l];
+                Y[m * N + n] = sumf;
+            }
         return;
     }
     if (W.type == T_Q4_1 || W.type == T_Q5_1) {
@@ -566,6 +635,66 @@ bool set_mat(Mat& m, int type, const void* data, int64_t nbytes, int64_t N, int6
     } else if (type == T_Q8_0) {
         if (K % QK || nbytes != N * (K / QK) * Q8_BYTES) { err = std::string("bad size for ") + name; return false; }
         m.q.assign((const uint8_t*)data, (const uint8_t*)data + nbytes);
+    } else if (type == T_Q4_K || type == T_Q5_K || type == T_Q6_K) {
+        // ggml block_q4_K {fp16 d, dmin; u8 scales[12]; u8 qs[128]}, block_q5_K {fp16 d, dmin;
+        // u8 scales[12]; u8 qh[32]; u8 qs[128]}, block_q6_K {u8 ql[128]; u8 qh[64]; i8 scales[16]; fp16 d}.
+        // Q4_K / Q5_K: 8 sub-blocks of 32 with 6-bit scale and min (get_scale_min_k4); value e of the
+        // 64-value group g: nibble (low for e < 32) of qs[32g + e % 32], + 16 * bit (2g + e/32) of
+        // qh[e % 32] for Q5_K; weight = d*scale*q - dmin*min. Q6_K: 16 sub-blocks of 16 with int8 scale;
+        // value e = 128h + 32k + l: low / high nibble (k = 0, 1 / 2, 3) of ql[64h + l + 32 (k odd)] | bits
+        // 2k..2k+1 of qh[32h + l] << 4, minus 32; weight = d*scale*q.
+        const int64_t bs = type == T_Q4_K ? 144 : type == T_Q5_K ? 176 : 210, nsb = N * (K / QKK);
+        if (K % QKK || nbytes != nsb * bs) { err = std::string("bad size for ") + name; return false; }
+        m.qv.assign((size_t)(N * K), 0);
+        m.ksc.assign((size_t)(N * K), 0);
+        m.dm.assign((size_t)(nsb * 2), 0.0f);
+        m.kmin.assign((size_t)(nsb * 8), 0);
+        for (int64_t b = 0; b < nsb; b++) {
+            const uint8_t* src = (const uint8_t*)data + b * bs;
+            int8_t* qv = m.qv.data() + b * QKK;
+            int16_t* sc = m.ksc.data() + b * QKK;
+            if (type == T_Q6_K) {
+                uint16_t h;
+                std::memcpy(&h, src + 208, 2);
+                m.dm[(size_t)(b * 2)] = f16_to_f32(h);
+                const uint8_t* ql = src;
+                const uint8_t* qh = src + 128;
+                const int8_t* s8 = (const int8_t*)(src + 192);
+                for (int e = 0; e < QKK; e++) {
+                    const int hh = e / 128, k = (e % 128) / 32, l = e % 32;
+                    const uint8_t lo = ql[64 * hh + l + (k & 1) * 32];
+                    const int nib = k < 2 ? (lo & 15) : (lo >> 4);
+                    qv[e] = (int8_t)((nib | (((qh[32 * hh + l] >> (2 * k)) & 3) << 4)) - 32);
+                    sc[e] = s8[e / 16];
+                }
+            } else {
+                uint16_t h[2];
+                std::memcpy(h, src, 4);
+                m.dm[(size_t)(b * 2)] = f16_to_f32(h[0]);
+                m.dm[(size_t)(b * 2 + 1)] = f16_to_f32(h[1]);
+                const uint8_t* s = src + 4;
+                int scl[8], mnv[8];
+                for (int j = 0; j < 8; j++) {
+                    if (j < 4) {
+                        scl[j] = s[j] & 63;
+                        mnv[j] = s[j + 4] & 63;
+                    } else {
+                        scl[j] = (s[j + 4] & 15) | ((s[j - 4] >> 6) << 4);
+                        mnv[j] = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+                    }
+                    m.kmin[(size_t)(b * 8 + j)] = (uint8_t)mnv[j];
+                }
+                const uint8_t* qh = src + 16;
+                const uint8_t* qs = src + (type == T_Q4_K ? 16 : 48);
+                for (int e = 0; e < QKK; e++) {
+                    const int g = e / 64, hi = (e % 64) / 32, l = e % 32;
+                    int q = hi ? (qs[32 * g + l] >> 4) : (qs[32 * g + l] & 15);
+                    if (type == T_Q5_K) q += ((qh[l] >> (2 * g + hi)) & 1) * 16;
+                    qv[e] = (int8_t)q;
+                    sc[e] = (int16_t)scl[e / 32];
+                }
+            }
+        }
     } else if (type == T_Q4_1 || type == T_Q5_1) {
         // ggml block_q4_1 {fp16 d, m; u8 qs[16]} / block_q5_1 {fp16 d, m; u8 qh[4]; u8 qs[16]}: value i is
         // d * q_i + m, q_i the low (i < 16) or high (i >= 16) nibble of qs[i % 16] (+ bit i of qh as bit 4)
@@ -867,6 +996,9 @@ int orc_mul_mat(int type, const void* W, int64_t N, int64_t K, const float* X, i
     Mat w;
     std::string err;
     const int64_t nbytes = type == T_Q8_0   ? N * (K / QK) * Q8_BYTES
+                           : type == T_Q4_K ? N * (K / QKK) * 144
+                           : type == T_Q5_K ? N * (K / QKK) * 176
+                           : type == T_Q6_K ? N * (K / QKK) * 210
                            : type == T_Q4_1 ? N * (K / QK) * 20
                            : type == T_Q5_1 ? N * (K / QK) * 24
                            : type == T_Q4_0 || type == T_IQ4_NL ? N * (K / QK) * 18

@@ -410,3 +410,89 @@ def test_oracle_q4_1_q5_1_restated(wtype):
         ms = (mn[None, :, b] * sx[:, None, b]).astype(np.float32)
         acc = (acc + _fmaf(dd, sumi[..., b], ms)).astype(np.float32)
     assert np.array_equal(O.mul_mat(raw, wtype, N, K, X), acc)
+
+
+def _kquant_unpack(raw, kind, nsb):
+    """(values, per-value scale, d, dmin, mins) of K-quant blocks, unpacked in numpy."""
+    if kind == "q6_k":
+        b = raw.reshape(nsb, 210)
+        ql, qh = b[:, :128].astype(np.int64), b[:, 128:192].astype(np.int64)
+        q = np.zeros((nsb, 256), np.int64)
+        for hh in range(2):
+            for k in range(4):
+                lo = ql[:, 64 * hh + (k & 1) * 32: 64 * hh + (k & 1) * 32 + 32]
+                nib = lo & 15 if k < 2 else lo >> 4
+                q[:, 128 * hh + 32 * k: 128 * hh + 32 * k + 32] = (nib | (((qh[:, 32 * hh: 32 * hh + 32] >> (2 * k)) & 3) << 4)) - 32
+        sc = np.repeat(b[:, 192:208].copy().view(np.int8).astype(np.int64), 16, axis=1)
+        d = b[:, 208:210].copy().view(np.float16)[:, 0].astype(np.float32)
+        return q, sc, d, None, None
+    b = raw.reshape(nsb, 144 if kind == "q4_k" else 176)
+    d = b[:, 0:2].copy().view(np.float16)[:, 0].astype(np.float32)
+    dmin = b[:, 2:4].copy().view(np.float16)[:, 0].astype(np.float32)
+    s = b[:, 4:16].astype(np.int64)
+    sc = np.zeros((nsb, 8), np.int64)
+    mn = np.zeros((nsb, 8), np.int64)
+    for j in range(8):
+        if j < 4:
+            sc[:, j], mn[:, j] = s[:, j] & 63, s[:, j + 4] & 63
+        else:
+            sc[:, j] = (s[:, j + 4] & 15) | ((s[:, j - 4] >> 6) << 4)
+            mn[:, j] = (s[:, j + 4] >> 4) | ((s[:, j] >> 6) << 4)
+    qs = b[:, 16:144] if kind == "q4_k" else b[:, 48:176]
+    q = np.zeros((nsb, 256), np.int64)
+    for g in range(4):
+        q[:, 64 * g: 64 * g + 32] = qs[:, 32 * g: 32 * g + 32] & 15
+        q[:, 64 * g + 32: 64 * g + 64] = qs[:, 32 * g: 32 * g + 32] >> 4
+        if kind == "q5_k":
+            qh = b[:, 16:48].astype(np.int64)
+            q[:, 64 * g: 64 * g + 32] += ((qh >> (2 * g)) & 1) * 16
+            q[:, 64 * g + 32: 64 * g + 64] += ((qh >> (2 * g + 1)) & 1) * 16
+    return q, np.repeat(sc, 32, axis=1), d, dmin, mn
+
+
+@pytest.mark.parametrize("kind,wtype", [("q4_k", 12), ("q5_k", 13), ("q6_k", 14)])
+def test_oracle_kquant_restated(kind, wtype):
+    """K-quant matrices (exporter --spec ...=q4_k / q5_k / q6_k): the oracle's mul_mat equals, bit for bit, a
+    numpy restatement of ggml's portable K-quant x Q8_K dot -- src1 quantized to Q8_K per 256 values
+    (iscale = -127/max, round half to even, d = 1/iscale, sums of 16), eight integer lane sums per
+    super-block (value e to lane e mod 8, times its sub-block scale), sums[l] = fma(d_w*d_x, lane, sums[l]),
+    for Q4_K / Q5_K sumf = fma(-dmin_w*d_x, sum of bsums*mins, sumf), then sumf + sums[0] + ... + sums[7].
+    The unpacked weights are checked against gguf-py's dequantizer."""
+    import gguf
+    ty = gguf.GGMLQuantizationType(wtype)
+    rng = np.random.default_rng(60 + wtype)
+    N, K, M = 24, 512, 5
+    nsb = K // 256
+    W = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    X = rng.standard_normal((M, K)).astype(np.float32)
+    X[1, :256] = 0.0                                  # an all-zero activation super-block
+    raw = S.kquant_blocks(W, kind)
+    q, sc, d, dmin, mn = _kquant_unpack(raw, kind, N * nsb)
+    deq = gguf.quants.dequantize(raw, ty).reshape(N * nsb, 256)
+    w = (d[:, None] * sc.astype(np.float32)).astype(np.float32) * q.astype(np.float32)
+    if dmin is not None:
+        w = w - np.repeat((dmin[:, None] * mn.astype(np.float32)).astype(np.float32), 32, axis=1)
+    np.testing.assert_allclose(w, deq, rtol=0, atol=1e-6 * np.abs(deq).max())
+    # Q8_K of the activations
+    xb = X.reshape(M * nsb, 256)
+    mx = xb[np.arange(M * nsb), np.abs(xb).argmax(-1)]
+    iscale = np.where(mx != 0, np.float32(-127) / np.where(mx != 0, mx, np.float32(1)), np.float32(0)).astype(np.float32)
+    qx = np.minimum(127, np.rint((iscale[:, None] * xb).astype(np.float32))).astype(np.int64)
+    dx = np.where(mx != 0, np.float32(1) / np.where(iscale != 0, iscale, np.float32(1)), np.float32(0)).astype(np.float32)
+    bs = qx.reshape(M * nsb, 16, 16).sum(-1)
+    q, sc = q.reshape(N, nsb, 256), sc.reshape(N, nsb, 256)
+    qx, dx, bs = qx.reshape(M, nsb, 256), dx.reshape(M, nsb), bs.reshape(M, nsb, 16)
+    sums = np.zeros((M, N, 8), np.float32)
+    sumf = np.zeros((M, N), np.float32)
+    for s_ in range(nsb):
+        prod = np.einsum("ne,me->mne", sc[:, s_] * q[:, s_], qx[:, s_])
+        lanes = prod.reshape(M, N, 32, 8).sum(2).astype(np.float32)      # value e -> lane e % 8
+        dd = (d.reshape(N, nsb)[None, :, s_] * dx[:, None, s_]).astype(np.float32)
+        sums = _fmaf(dd[..., None], lanes, sums).astype(np.float32)
+        if dmin is not None:
+            sumi = (bs[:, None, s_, :] * np.repeat(mn.reshape(N, nsb, 8)[None, :, s_, :], 2, axis=-1)).sum(-1)
+            dm = (dmin.reshape(N, nsb)[None, :, s_] * dx[:, None, s_]).astype(np.float32)
+            sumf = _fmaf(-dm, sumi.astype(np.float32), sumf).astype(np.float32)
+    for l in range(8):
+        sumf = (sumf + sums[..., l]).astype(np.float32)
+    assert np.array_equal(O.mul_mat(raw, wtype, N, K, X), sumf)
