@@ -17,8 +17,9 @@ namespace {
 
 struct LayerW {
     int mt[4] = {8, 8, 8, 8};   // qkv, out, ffn1, ffn2: 8 Q8_0 kernels (Q8_0 / Q4_0 / Q5_0 / IQ4_NL), 0 F32,
-                                //   1 F16, 30 BF16 (k_gemm_fx), 3 Q4_1 / Q5_1 (k_gemm_qm)
-    uint16_t* wm[4] = {nullptr, nullptr, nullptr, nullptr};  // Q4_1 / Q5_1: fp16 m planes (d in wd)
+                                //   1 F16, 30 BF16 (k_gemm_fx), 3 Q4_1 / Q5_1 (k_gemm_qm), 12 K-quants (k_gemm_qk)
+    uint16_t* wm[4] = {nullptr, nullptr, nullptr, nullptr};  // Q4_1 / Q5_1: fp16 m planes (d in wd); K-quants: dmin
+    uint8_t* wmins[4] = {nullptr, nullptr, nullptr, nullptr};  // Q4_K / Q5_K: sub-block mins
     uint4* wq[4] = {nullptr, nullptr, nullptr, nullptr};     // Q8_0: fragment planes
     uint16_t* wd[4] = {nullptr, nullptr, nullptr, nullptr};  //       matching fp16 scale planes
     const void* wf[4] = {nullptr, nullptr, nullptr, nullptr};  // F32 / F16: the GGUF rows [N][K] as stored
@@ -138,6 +139,61 @@ void unpack_q_1(const GgufTensor* t, std::vector<uint8_t>& q, std::vector<uint16
     }
 }
 
+// K-quant blocks as k_gemm_qk's planes: per 256-value super-block the values times their sub-block
+// scale as int16, lane-major (value e at (e % 8) * 32 + e / 8), d and dmin fp16, the 8 sub-block mins.
+// block_q4_K {fp16 d, dmin; u8 scales[12]; u8 qs[128]} / block_q5_K {d, dmin, scales[12], u8 qh[32],
+// qs[128]}: 8 sub-blocks of 32 with 6-bit scale and min (scale j < 4: scales[j] & 63, min scales[j+4] &
+// 63; j >= 4: scale (scales[j+4] & 15) | (scales[j-4] >> 6) << 4, min (scales[j+4] >> 4) | (scales[j] >> 6)
+// << 4); value 64g + 32h + l = nibble h of qs[32g + l] (+ 16 * bit 2g + h of qh[l] for Q5_K).
+// block_q6_K {u8 ql[128]; u8 qh[64]; i8 scales[16]; fp16 d}: value 128h + 32k + l = (nibble k / 2 of
+// ql[64h + 32(k & 1) + l] | bits 2k, 2k+1 of qh[32h + l] << 4) - 32, scale scales[value / 16].
+void unpack_kquant(const GgufTensor* t, std::vector<int16_t>& w, std::vector<uint16_t>& d, std::vector<uint16_t>& dmin,
+                   std::vector<uint8_t>& mins) {
+    const size_t bs = t->type == 12 ? 144 : t->type == 13 ? 176 : 210, nsb = t->nbytes / bs;
+    w.assign(nsb * 256, 0);
+    d.assign(nsb, 0);
+    dmin.assign(nsb, 0);
+    mins.assign(nsb * 8, 0);
+    for (size_t b = 0; b < nsb; b++) {
+        const uint8_t* src = t->data + b * bs;
+        int16_t* dst = w.data() + b * 256;
+        int val[256], scl[256];
+        if (t->type == 14) {
+            std::memcpy(&d[b], src + 208, 2);
+            for (int hh = 0; hh < 2; hh++)
+                for (int k = 0; k < 4; k++)
+                    for (int l = 0; l < 32; l++) {
+                        const int e = 128 * hh + 32 * k + l;
+                        const uint8_t lo = src[64 * hh + 32 * (k & 1) + l];
+                        const int nib = k < 2 ? (lo & 15) : (lo >> 4);
+                        val[e] = (nib | (((src[128 + 32 * hh + l] >> (2 * k)) & 3) << 4)) - 32;
+                        scl[e] = (int8_t)src[192 + e / 16];
+                    }
+        } else {
+            std::memcpy(&d[b], src, 2);
+            std::memcpy(&dmin[b], src + 2, 2);
+            const uint8_t* s = src + 4;
+            int sc[8];
+            for (int j = 0; j < 8; j++) {
+                sc[j] = j < 4 ? (s[j] & 63) : ((s[j + 4] & 15) | ((s[j - 4] >> 6) << 4));
+                mins[b * 8 + j] = (uint8_t)(j < 4 ? (s[j + 4] & 63) : ((s[j + 4] >> 4) | ((s[j] >> 6) << 4)));
+            }
+            const uint8_t* qh = src + 16;
+            const uint8_t* qs = src + (t->type == 12 ? 16 : 48);
+            for (int g = 0; g < 4; g++)
+                for (int h = 0; h < 2; h++)
+                    for (int l = 0; l < 32; l++) {
+                        const int e = 64 * g + 32 * h + l;
+                        int q = h ? (qs[32 * g + l] >> 4) : (qs[32 * g + l] & 15);
+                        if (t->type == 13) q += ((qh[l] >> (2 * g + h)) & 1) * 16;
+                        val[e] = q;
+                        scl[e] = sc[e / 32];
+                    }
+        }
+        for (int e = 0; e < 256; e++) dst[(e % 8) * 32 + e / 8] = (int16_t)(val[e] * scl[e]);
+    }
+}
+
 std::vector<uint8_t> to_q8_0_blocks(const GgufTensor* t) {
     const size_t bs = t->type == 6 ? 22 : 18, nb = t->nbytes / bs;
     std::vector<uint8_t> out(nb * 34);
@@ -194,8 +250,8 @@ int validate_model(const GgufFile& f, ModelView& mv, std::string& err) {
         return GSVCU_ERR_FORMAT;
     }
     const int NL = hp.n_layer, V = hp.vocab_size, PV = hp.phoneme_vocab_size, BD = hp.bert_dim;
-    // accepted ggml types: 0 = F32, 1 = F16, 2 = Q4_0, 3 = Q4_1, 6 = Q5_0, 7 = Q5_1, 8 = Q8_0, 20 = IQ4_NL,
-    // 30 = BF16
+    // accepted ggml types: 0 = F32, 1 = F16, 2 = Q4_0, 3 = Q4_1, 6 = Q5_0, 7 = Q5_1, 8 = Q8_0, 12 = Q4_K,
+    // 13 = Q5_K, 14 = Q6_K, 20 = IQ4_NL, 30 = BF16
     auto need = [&](const std::string& name, std::vector<uint32_t> types, std::vector<int64_t> dims,
                     const GgufTensor** out) -> int {
         const GgufTensor* t = f.tensor(name);
@@ -204,7 +260,7 @@ int validate_model(const GgufFile& f, ModelView& mv, std::string& err) {
             std::string want;
             for (uint32_t ty : types) want += (want.empty() ? "" : " or ") + std::to_string(ty);
             err = "tensor " + name + " has ggml type " + std::to_string(t->type) + ", expected " + want +
-                  " (0 F32, 1 F16, 2 Q4_0, 3 Q4_1, 6 Q5_0, 7 Q5_1, 8 Q8_0, 20 IQ4_NL, 30 BF16)";
+                  " (0 F32, 1 F16, 2 Q4_0, 3 Q4_1, 6 Q5_0, 7 Q5_1, 8 Q8_0, 12 Q4_K, 13 Q5_K, 14 Q6_K, 20 IQ4_NL, 30 BF16)";
             return GSVCU_ERR_FORMAT;
         }
         int64_t ne = 1, ne_want = 1;
@@ -219,13 +275,13 @@ int validate_model(const GgufFile& f, ModelView& mv, std::string& err) {
     };
     int r;
     // embeddings: F32, or F16 / BF16 (exporter --spec emb=f16 / bf16) widened to F32 on load; predict and
-    // layer matrices: F32, F16, BF16, Q8_0, Q4_0, Q4_1, Q5_0, Q5_1 or IQ4_NL (--spec predict=.., attn=..,
-    // ffn=..)
+    // layer matrices: F32, F16, BF16, Q8_0, Q4_0, Q4_1, Q5_0, Q5_1, IQ4_NL, Q4_K, Q5_K or Q6_K (--spec
+    // predict=.., attn=.., ffn=..)
     if ((r = need("ar.text_emb", {0, 1, 30}, {D, PV}, &mv.te)) ||
         (r = need("ar.audio_emb", {0, 1, 30}, {D, V}, &mv.ae)) ||
         (r = need("ar.bert_proj", {0}, {BD, D}, &mv.bp)) || (r = need("ar.bert_proj_b", {0}, {D}, &mv.bb)) ||
         (r = need("ar.text_pe_alpha", {0}, {1}, &mv.ta)) || (r = need("ar.audio_pe_alpha", {0}, {1}, &mv.aa)) ||
-        (r = need("ar.predict", {0, 8, 1, 2, 3, 6, 7, 20, 30}, {D, V}, &mv.pr)))
+        (r = need("ar.predict", {0, 8, 1, 2, 3, 6, 7, 12, 13, 14, 20, 30}, {D, V}, &mv.pr)))
         return r;
     std::memcpy(&hp.text_pe_alpha, mv.ta->data, 4);
     std::memcpy(&hp.audio_pe_alpha, mv.aa->data, 4);
@@ -236,14 +292,15 @@ int validate_model(const GgufFile& f, ModelView& mv, std::string& err) {
     for (int li = 0; li < NL; li++) {
         const std::string pfx = "transformer.block" + std::to_string(li) + ".";
         for (int m = 0; m < 4; m++)
-            if ((r = need(pfx + kMatNames[m], {8, 0, 1, 2, 3, 6, 7, 20, 30}, {NK[m][1], NK[m][0]},
+            if ((r = need(pfx + kMatNames[m], {8, 0, 1, 2, 3, 6, 7, 12, 13, 14, 20, 30}, {NK[m][1], NK[m][0]},
                           &mv.mats[(size_t)li * 4 + m])))
                 return r;
         // FFN1's epilogue produces what FFN2 reads: Q8_0 blocks for a Q8_0-class ffn2_w, floats otherwise
-        // (F32 / F16 / BF16, and Q4_1 / Q5_1, whose kernel quantizes its float rows to Q8_1 itself)
+        // (F32 / F16 / BF16, and Q4_1 / Q5_1 / K-quants, whose kernels quantize their float rows to Q8_1 /
+        // Q8_K themselves)
         if (q8_class(mv.mats[(size_t)li * 4 + 2]->type) != q8_class(mv.mats[(size_t)li * 4 + 3]->type)) {
-            err = pfx + "ffn1_w / ffn2_w: both Q8_0 / Q4_0 / Q5_0 / IQ4_NL or both F32 / F16 / BF16 / Q4_1 / Q5_1 "
-                        "(the exporter's ffn group) expected";
+            err = pfx + "ffn1_w / ffn2_w: both Q8_0 / Q4_0 / Q5_0 / IQ4_NL or both F32 / F16 / BF16 / Q4_1 / Q5_1 / "
+                        "K-quants (the exporter's ffn group) expected";
             return GSVCU_ERR_FORMAT;
         }
         for (int k = 0; k < 8; k++)
@@ -277,7 +334,8 @@ struct gsvcu_ctx {
     uint16_t* predict_wd = nullptr;
     const void* predict_fx = nullptr;   // F16 / BF16 predict [V][D], or Q4_1 / Q5_1 values (gemm_fx.cu)
     int predict_fx_type = FX_F16;
-    uint16_t *predict_qd = nullptr, *predict_qm = nullptr;   // Q4_1 / Q5_1 predict: d, m planes
+    uint16_t *predict_qd = nullptr, *predict_qm = nullptr;   // Q4_1 / Q5_1 predict: d, m (K-quants: d, dmin)
+    uint8_t* predict_mins = nullptr;                          // Q4_K / Q5_K predict: sub-block mins
     // layer matrices: all Q8_0 (the fused decode step needs that), any F32 / F16 FFN (needs hf)
     bool all_q8 = true, ffn_float = false;
     float* hf = nullptr;                 // F32 / F16 FFN: relu(W1 n1 + b1) rows [Mmax][FF]
@@ -458,6 +516,19 @@ int gsvcu_ctx::load(const char* path) {
         predict_q8 = false;
         predict_fx_type = mv.pr->type == 1 ? FX_F16 : FX_BF16;
         TRY(upload(mv.pr->data, mv.pr->nbytes, (void**)&predict_fx));
+    } else if (mv.pr->type == 12 || mv.pr->type == 13 || mv.pr->type == 14) {   // K-quant predict (k_gemm_qk)
+        predict_q8 = false;
+        predict_fx_type = FX_QK;
+        std::vector<int16_t> kw;
+        std::vector<uint16_t> kd, kdm;
+        std::vector<uint8_t> kmn;
+        unpack_kquant(mv.pr, kw, kd, kdm, kmn);
+        TRY(upload(kw.data(), kw.size() * 2, (void**)&predict_fx));
+        TRY(upload(kd.data(), kd.size() * 2, (void**)&predict_qd));
+        if (mv.pr->type != 14) {
+            TRY(upload(kdm.data(), kdm.size() * 2, (void**)&predict_qm));
+            TRY(upload(kmn.data(), kmn.size(), (void**)&predict_mins));
+        }
     } else if (mv.pr->type == 3 || mv.pr->type == 7) {   // Q4_1 / Q5_1 predict (k_gemm_qm)
         predict_q8 = false;
         predict_fx_type = FX_QM;
@@ -505,7 +576,24 @@ int gsvcu_ctx::load(const char* path) {
         for (int m = 0; m < 4; m++) {
             const GgufTensor* t = mv.mats[(size_t)li * 4 + m];
             const int N = NK[m][0], K = NK[m][1];
-            L[li].mt[m] = q8_class(t->type) ? 8 : t->type == 7 ? 3 : (int)t->type;
+            L[li].mt[m] = q8_class(t->type) ? 8 : t->type == 7 ? 3 : (t->type == 13 || t->type == 14) ? 12 : (int)t->type;
+            if (t->type == 12 || t->type == 13 || t->type == 14) {   // K-quants: k_gemm_qk planes
+                all_q8 = false;
+                ffn_float |= m >= 2;
+                std::vector<int16_t> kw;
+                std::vector<uint16_t> kd, kdm;
+                std::vector<uint8_t> kmn;
+                unpack_kquant(t, kw, kd, kdm, kmn);
+                void* dst = nullptr;
+                TRY(upload(kw.data(), kw.size() * 2, &dst));
+                L[li].wf[m] = dst;
+                TRY(upload(kd.data(), kd.size() * 2, (void**)&L[li].wd[m]));
+                if (t->type != 14) {
+                    TRY(upload(kdm.data(), kdm.size() * 2, (void**)&L[li].wm[m]));
+                    TRY(upload(kmn.data(), kmn.size(), (void**)&L[li].wmins[m]));
+                }
+                continue;
+            }
             if (t->type == 3 || t->type == 7) {   // Q4_1 / Q5_1: value bytes + d, m planes (k_gemm_qm)
                 all_q8 = false;
                 ffn_float |= m >= 2;
@@ -684,7 +772,7 @@ int gsvcu_ctx::launch_logits(const float* xr, int M, int8_t* xq_s, uint16_t* xd_
     if (predict_fx) {
         GemmFxParams g;
         g.x = xr; g.ldx = D; g.M = M; g.w = predict_fx; g.wtype = predict_fx_type; g.N = V; g.K = D; g.y = out;
-        g.ldy = V; g.wd = predict_qd; g.wm = predict_qm;
+        g.ldy = V; g.wd = predict_qd; g.wm = predict_qm; g.wmins = predict_mins;
         launch_gemm_fx(g, FXE_BIAS, s);
         return 1;
     }
@@ -847,8 +935,9 @@ void gsvcu_ctx::layer_gemm(int li, int m, const LayerIO& io, int M, const KvWrit
         return;
     }
     GemmFxParams g;
-    g.M = M; g.w = w.wf[m]; g.wtype = w.mt[m] == 1 ? FX_F16 : w.mt[m] == 30 ? FX_BF16 : w.mt[m] == 3 ? FX_QM : FX_F32;
-    g.wd = w.wd[m]; g.wm = w.wm[m]; g.N = N[m]; g.K = K[m]; g.bias = bias[m];
+    g.M = M; g.w = w.wf[m];
+    g.wtype = w.mt[m] == 1 ? FX_F16 : w.mt[m] == 30 ? FX_BF16 : w.mt[m] == 3 ? FX_QM : w.mt[m] == 12 ? FX_QK : FX_F32;
+    g.wd = w.wd[m]; g.wm = w.wm[m]; g.wmins = w.wmins[m]; g.N = N[m]; g.K = K[m]; g.bias = bias[m];
     g.ldx = K[m];
     if (m == 0) { g.x = io.x; g.y = io.qkv; g.kv = kv; launch_gemm_fx(g, FXE_BIAS, s); }
     if (m == 1) { g.x = io.attn; g.resid = io.x; g.y = io.pre; launch_gemm_fx(g, FXE_RESID, s); }

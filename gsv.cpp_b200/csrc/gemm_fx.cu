@@ -254,6 +254,91 @@ __global__ void __launch_bounds__(256) k_gemm_qm(const GemmFxParams p) {
     fx_store<EPI>(p, mt + r, nt + c, acc);
 }
 
+// K-quant matrices (Q4_K / Q5_K / Q6_K): ggml's K-quant x Q8_K mul_mat in the order of its portable C
+// dot. The CTA quantizes its 16 activation rows to Q8_K in shared memory (quantize_row_q8_K_ref, per 256
+// values: max = the value of largest magnitude, first one winning; iscale = -127/max; q = min(127,
+// round-half-even(iscale*x)); d = 1/iscale; sums of 16), storing each super-block lane-major like the
+// weights (value e at (e % 8) * 32 + e / 8). Thread (r, c) runs output (row r, column c): per
+// super-block eight exact lane sums (value e to lane e % 8) of the pre-scaled int16 weights times the
+// int8 activations (16 dp2a per lane), sums[l] = fma(d_w*d_x, lane, sums[l]); Q4_K / Q5_K also sumf =
+// fma(-dmin_w*d_x, sum_g bsums[g]*min[g/2], sumf); at the end sumf + sums[0] + ... + sums[7]. K is a
+// multiple of 256, at most QK_KMAX.
+constexpr int QK_T = 16, QK_KMAX = 2048;
+
+template <int EPI>
+__global__ void __launch_bounds__(256) k_gemm_qk(const GemmFxParams p) {
+    __shared__ __align__(16) int8_t xq[QK_T][QK_KMAX];
+    __shared__ float xd[QK_T][QK_KMAX / 256];
+    __shared__ int32_t xbs[QK_T][QK_KMAX / 16];
+    const int tid = threadIdx.x, nsb = p.K / 256;
+    const int mt = blockIdx.y * QK_T, nt = blockIdx.x * QK_T;
+    griddep_wait();
+    griddep_launch();
+    for (int i = tid; i < QK_T * nsb; i += 256) {
+        const int r = i / nsb, sb = i - r * nsb;
+        const float* src = p.x + (size_t)min(mt + r, p.M - 1) * p.ldx + sb * 256;
+        float amax = 0.0f, mx = 0.0f;
+        for (int j = 0; j < 256; j++) {
+            const float v = src[j];
+            if (fabsf(v) > amax) {
+                amax = fabsf(v);
+                mx = v;
+            }
+        }
+        const float iscale = amax != 0.0f ? __fdiv_rn(-127.0f, mx) : 0.0f;
+        int8_t* dst = &xq[r][sb * 256];
+        for (int g = 0; g < 16; g++) {
+            int s = 0;
+            for (int j = 0; j < 16; j++) {
+                const int e = g * 16 + j;
+                const int v = amax != 0.0f ? min(127, __float2int_rn(__fmul_rn(iscale, src[e]))) : 0;
+                dst[(e & 7) * 32 + (e >> 3)] = (int8_t)v;
+                s += v;
+            }
+            xbs[r][sb * 16 + g] = s;
+        }
+        xd[r][sb] = amax != 0.0f ? __fdiv_rn(1.0f, iscale) : 0.0f;
+    }
+    __syncthreads();
+    const int r = tid / QK_T, c = tid % QK_T;
+    const int nc = min(nt + c, p.N - 1);
+    const int4* wrow = (const int4*)((const int16_t*)p.w + (size_t)nc * p.K);
+    float sums[8], sumf = 0.0f;
+#pragma unroll
+    for (int l = 0; l < 8; l++) sums[l] = 0.0f;
+    for (int sb = 0; sb < nsb; sb++) {
+        const int4* xr = (const int4*)&xq[r][sb * 256];
+        const float xds = xd[r][sb];
+        const float dd = __fmul_rn(h2f(p.wd[(size_t)nc * nsb + sb]), xds);
+#pragma unroll
+        for (int l = 0; l < 8; l++) {   // lane l: 32 pre-scaled weights (4 x int4) and 32 activations (2 x int4)
+            const int4 x0 = xr[l * 2], x1 = xr[l * 2 + 1];
+            const int xw[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+            int acc = 0;
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const int4 w = __ldg(wrow + (size_t)sb * 32 + l * 4 + k);
+                acc = __dp2a_lo(w.x, xw[2 * k], acc);
+                acc = __dp2a_hi(w.y, xw[2 * k], acc);
+                acc = __dp2a_lo(w.z, xw[2 * k + 1], acc);
+                acc = __dp2a_hi(w.w, xw[2 * k + 1], acc);
+            }
+            sums[l] = fmaf(dd, (float)acc, sums[l]);
+        }
+        if (p.wmins) {
+            const uint8_t* mn = p.wmins + ((size_t)nc * nsb + sb) * 8;
+            int sumi = 0;
+#pragma unroll
+            for (int g = 0; g < 16; g++) sumi += xbs[r][sb * 16 + g] * (int)mn[g >> 1];
+            const float dmin = __fmul_rn(h2f(p.wm[(size_t)nc * nsb + sb]), xds);
+            sumf = fmaf(-dmin, (float)sumi, sumf);
+        }
+    }
+#pragma unroll
+    for (int l = 0; l < 8; l++) sumf = __fadd_rn(sumf, sums[l]);
+    fx_store<EPI>(p, mt + r, nt + c, sumf);
+}
+
 template <int WT>
 void launch_wt(const GemmFxParams& p, int epi, cudaStream_t s) {
     const dim3 grid((p.N + FX_TN - 1) / FX_TN, (p.M + FX_TM - 1) / FX_TM), block(128);
@@ -268,6 +353,16 @@ void launch_wt(const GemmFxParams& p, int epi, cudaStream_t s) {
 
 void launch_gemm_fx(const GemmFxParams& p, int epi, cudaStream_t s) {
     if (p.M <= 0 || p.N <= 0) return;
+    if (p.wtype == FX_QK) {
+        if (p.K % 256 || p.K > QK_KMAX) return;
+        const dim3 grid((p.N + QK_T - 1) / QK_T, (p.M + QK_T - 1) / QK_T), block(256);
+        switch (epi) {
+            case FXE_BIAS: launch_pdl(k_gemm_qk<FXE_BIAS>, grid, block, 0, s, p); break;
+            case FXE_RESID: launch_pdl(k_gemm_qk<FXE_RESID>, grid, block, 0, s, p); break;
+            default: launch_pdl(k_gemm_qk<FXE_RELU>, grid, block, 0, s, p); break;
+        }
+        return;
+    }
     if (p.wtype == FX_QM) {
         if (p.K % 32 || p.K > QM_KMAX) return;
         const dim3 grid((p.N + QM_T - 1) / QM_T, (p.M + QM_T - 1) / QM_T), block(256);

@@ -145,6 +145,12 @@ bool GgufFile::open(const std::string& path, std::string& err) {
                 T.nbytes = (uint64_t)ne / 32 *
                            (T.type == 8 ? 34 : T.type == 7 ? 24 : T.type == 6 ? 22 : T.type == 3 ? 20 : 18);
                 break;
+            case 12:   // Q4_K: 144 bytes per 256 values
+            case 13:   // Q5_K: 176 bytes
+            case 14:   // Q6_K: 210 bytes
+                if (T.dims[0] % 256) { err = "K-quant row not a multiple of 256: " + T.name; return false; }
+                T.nbytes = (uint64_t)ne / 256 * (T.type == 12 ? 144 : T.type == 13 ? 176 : 210);
+                break;
             default: T.nbytes = 0; break;   // unsupported types are rejected by the consumer
         }
         index_[T.name] = (size_t)i;

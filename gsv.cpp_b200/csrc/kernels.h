@@ -73,15 +73,18 @@ void pack_q8_0_host(const uint8_t* raw, int N, int K, uint8_t* wq_out, uint16_t*
 // even), 32 float FMA chains (chain c takes
 // k = c, c + 32, ...) added pairwise as chains c^16, ^8, ^4, ^1, ^2. K % 64 == 0; w row-major [N][K];
 // x, w and every row of both 16-byte aligned (ldx * 4 and K * element size multiples of 16).
-enum { FX_F32 = 0, FX_F16 = 1, FX_BF16 = 2, FX_QM = 3 };   // FX_QM: Q4_1 / Q5_1 (k_gemm_qm)
+enum { FX_F32 = 0, FX_F16 = 1, FX_BF16 = 2, FX_QM = 3, FX_QK = 4 };   // Q4_1 / Q5_1 (k_gemm_qm), K-quants (k_gemm_qk)
 enum { FXE_BIAS = 0, FXE_RESID = 1, FXE_RELU = 2 };   // y = acc + b (+ K/V store); (r + acc) + b; relu(acc + b)
 struct GemmFxParams {
     const float* x = nullptr;
     int ldx = 0;
     int M = 0;
-    const void* w = nullptr;        // FX_QM: the unsigned 4- / 5-bit values as bytes [N][K]
-    const uint16_t* wd = nullptr;   // FX_QM: fp16 d per 32-value block [N][K/32]
-    const uint16_t* wm = nullptr;   // FX_QM: fp16 m per block [N][K/32]
+    const void* w = nullptr;        // FX_QM: the unsigned 4- / 5-bit values as bytes [N][K]; FX_QK: int16
+                                    //   scale * value [N][K/256][lane 8][32] (value e of a super-block at
+                                    //   (e % 8) * 32 + e / 8)
+    const uint16_t* wd = nullptr;   // FX_QM: fp16 d per 32-value block [N][K/32]; FX_QK: d [N][K/256]
+    const uint16_t* wm = nullptr;   // FX_QM: fp16 m per block [N][K/32]; FX_QK: dmin [N][K/256] (Q4_K / Q5_K)
+    const uint8_t* wmins = nullptr; // FX_QK: the 8 sub-block mins of each super-block (Q4_K / Q5_K)
     int wtype = FX_F32;
     int N = 0, K = 0;
     const float* bias = nullptr;

@@ -107,8 +107,8 @@ def write_model(path: str, seed: int = 0, dims: Dims | None = None, mat_type: st
                 ffn_type: str | None = None) -> str:
     """mat_type is the type of the attention matrices (the exporter's --spec attn=...) and, unless
     ffn_type is given, of the FFN matrices (--spec ffn=...): "q8_0", "q4_0", "q4_1", "q5_0", "q5_1",
-    "iq4_nl", "f16", "bf16" or "f32" (iq4_nl: the reference's tools/quantize_gguf.cpp tier, quantized
-    by iq4_nl_blocks). predict_type "f32" or any of those stores ar.predict in that type
+    "q4_k", "q5_k", "q6_k", "iq4_nl", "f16", "bf16" or "f32" (iq4_nl: the reference's
+    tools/quantize_gguf.cpp tier, quantized by iq4_nl_blocks; K-quants by kquant_blocks). predict_type "f32" or any of those stores ar.predict in that type
     (--spec predict=...); emb_type "f16" / "bf16" stores the
     text / audio embeddings as F16 (--spec emb=f16). The exporter's --f16 preset is
     mat_type="f16", predict_type="f16", emb_type="f16"; its default (no flags) is mat_type="f32"."""
@@ -121,7 +121,8 @@ def write_model(path: str, seed: int = 0, dims: Dims | None = None, mat_type: st
              "f16": gguf.GGMLQuantizationType.F16, "q4_0": gguf.GGMLQuantizationType.Q4_0,
              "q5_0": gguf.GGMLQuantizationType.Q5_0, "iq4_nl": gguf.GGMLQuantizationType.IQ4_NL,
              "bf16": gguf.GGMLQuantizationType.BF16, "q4_1": gguf.GGMLQuantizationType.Q4_1,
-             "q5_1": gguf.GGMLQuantizationType.Q5_1}
+             "q5_1": gguf.GGMLQuantizationType.Q5_1, "q4_k": gguf.GGMLQuantizationType.Q4_K,
+             "q5_k": gguf.GGMLQuantizationType.Q5_K, "q6_k": gguf.GGMLQuantizationType.Q6_K}
     qt = types[mat_type]
     ft = types[ffn_type or mat_type]
 
@@ -145,6 +146,8 @@ def write_model(path: str, seed: int = 0, dims: Dims | None = None, mat_type: st
             w.add_tensor(name, arr.astype(np.float16), raw_dtype=dtype)
         elif dtype == gguf.GGMLQuantizationType.IQ4_NL:
             w.add_tensor(name, iq4_nl_blocks(arr), raw_dtype=dtype)
+        elif dtype in (gguf.GGMLQuantizationType.Q4_K, gguf.GGMLQuantizationType.Q5_K, gguf.GGMLQuantizationType.Q6_K):
+            w.add_tensor(name, kquant_blocks(arr, dtype.name.lower()), raw_dtype=dtype)
         else:
             w.add_tensor(name, gguf.quants.quantize(arr, dtype), raw_dtype=dtype)
 

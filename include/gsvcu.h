@@ -73,13 +73,14 @@ void gsvcu_destroy(gsvcu_ctx* ctx);
 const char* gsvcu_last_error(const gsvcu_ctx* ctx);
 
 /* Load an AR GGUF file (replaces gsv_ar::load, reference src/gsv_ar.cpp:490-705): tensor names of
- * tools/export_gguf/convert_ar.py:106-130. Attention / FFN matrices and predict Q8_0, Q4_0, Q4_1, Q5_0,
- * Q5_1, IQ4_NL, F32, F16 or BF16 (the exporter's --spec attn=.., ffn=.., predict=..;
- * tools/quantize_gguf.cpp for IQ4_NL; ffn1_w and ffn2_w of a layer both Q8_0 / Q4_0 / Q5_0 / IQ4_NL or
- * both of the others), embeddings F32, F16 or BF16 (widened on load), bert_proj, norms and biases F32.
- * Q8_0 matrices, and Q4_0 / Q5_0 / IQ4_NL ones as the Q8_0 blocks of the same values, are repacked into
- * tensor-core fragment order on the device; Q4_1 / Q5_1 are unpacked to value bytes and d / m planes;
- * F32 / F16 / BF16 matrices are kept as stored. K-quants are refused. */
+ * tools/export_gguf/convert_ar.py:106-130. Attention / FFN matrices and predict of any type the
+ * exporter (--spec attn=.., ffn=.., predict=..) or tools/quantize_gguf.cpp writes: Q8_0, Q4_0, Q4_1,
+ * Q5_0, Q5_1, Q4_K, Q5_K, Q6_K, IQ4_NL, F32, F16, BF16 (ffn1_w and ffn2_w of a layer both Q8_0 / Q4_0 /
+ * Q5_0 / IQ4_NL or both of the others); embeddings F32, F16 or BF16 (widened on load); bert_proj,
+ * norms and biases F32. Q8_0 matrices, and Q4_0 / Q5_0 / IQ4_NL ones as the Q8_0 blocks of the same
+ * values, are repacked into tensor-core fragment order on the device; Q4_1 / Q5_1 are unpacked to value
+ * bytes and d / m planes, K-quants to scaled int16 values and d / dmin / min planes; F32 / F16 / BF16
+ * matrices are kept as stored. Other ggml types are refused (GSVCU_ERR_FORMAT). */
 int gsvcu_load_gguf(gsvcu_ctx* ctx, const char* path);
 int gsvcu_get_hparams(const gsvcu_ctx* ctx, gsvcu_hparams* out);
 

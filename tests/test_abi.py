@@ -57,7 +57,8 @@ def test_inspect_rejects_bad_files(model_small, model_f32_small, tmp_path):
     ("q8_0", "q8_0", "q8_0", "f32"), ("q8_0", "q8_0", "f32", "f16"), ("f16", "f16", "f16", "f16"),
     ("f32", "f32", "f32", "f32"), ("q8_0", "f16", "f32", "f32"), ("f16", "q8_0", "f32", "f32"),
     ("q4_0", "q4_0", "q4_0", "f32"), ("q8_0", "q5_0", "q5_0", "f16"), ("q8_0", "iq4_nl", "iq4_nl", "f32"),
-    ("bf16", "bf16", "bf16", "bf16"), ("q4_1", "q4_1", "q4_1", "f32"), ("q8_0", "q5_1", "q5_1", "f16")])
+    ("bf16", "bf16", "bf16", "bf16"), ("q4_1", "q4_1", "q4_1", "f32"), ("q8_0", "q5_1", "q5_1", "f16"),
+    ("q8_0", "q6_k", "f16", "f16"), ("q4_k", "q5_k", "q6_k", "f32")])
 def test_inspect_export_formats(mat_type, ffn_type, predict_type, emb_type):
     """The exporter's formats: Q8_0 / Q4_0 / Q5_0 / F16 predict, F16 embeddings, F32 / F16 / Q4_0 / Q5_0
     attention and FFN matrices and mixed attn / ffn groups are accepted (GPU parity:
@@ -73,16 +74,17 @@ def test_inspect_export_formats(mat_type, ffn_type, predict_type, emb_type):
 
 def test_inspect_rejects_unsupported_matrix_types(model_small, tmp_path):
     """ffn1_w and ffn2_w of a layer are one group (Q8_0-class, or float-input: F32 / F16 / BF16 / Q4_1 /
-    Q5_1); other ggml types (the K-quants) are refused with the tensor named."""
+    Q5_1 / K-quants); ggml types no reference tool writes (Q2_K, Q3_K, the IQ2 / IQ3 family) are refused
+    with the tensor named."""
     import gguf
     from conftest import gguf_retyped_copy
     T = gguf.GGMLQuantizationType
     mixed = gguf_retyped_copy(model_small, str(tmp_path / "mixed.gguf"), {"transformer.block1.ffn2_w": T.F32})
     rc, _, msg = gsvcu.inspect_gguf(mixed)
     assert rc == -5 and "transformer.block1.ffn1_w / ffn2_w" in msg
-    q6k = gguf_retyped_copy(model_small, str(tmp_path / "q6k.gguf"), {"transformer.block0.out_w": T.Q6_K})
-    rc, _, msg = gsvcu.inspect_gguf(q6k)
-    assert rc == -5 and "transformer.block0.out_w has ggml type 14" in msg
+    q2k = gguf_retyped_copy(model_small, str(tmp_path / "q2k.gguf"), {"transformer.block0.out_w": T.Q2_K})
+    rc, _, msg = gsvcu.inspect_gguf(q2k)
+    assert rc == -5 and "transformer.block0.out_w has ggml type 10" in msg
 
 
 def test_inspect_missing_tensor(tmp_path):

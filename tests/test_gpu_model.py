@@ -394,6 +394,8 @@ EXPORT_FORMATS = [   # (attention matrices, FFN matrices, predict, embeddings)
     ("bf16", "bf16", "bf16", "bf16"),  # --spec attn=bf16,ffn=bf16,predict=bf16,emb=bf16
     ("q4_1", "q4_1", "q4_1", "f32"),   # --spec attn=q4_1,ffn=q4_1,predict=q4_1
     ("q8_0", "q5_1", "q5_1", "f16"),   # --spec attn=q8_0,ffn=q5_1,predict=q5_1,emb=f16
+    ("q8_0", "q6_k", "f16", "f16"),    # --spec attn=q8_0,ffn=q6_k,predict=f16,emb=f16 (the exporter's own example)
+    ("q4_k", "q5_k", "q6_k", "f32"),   # --spec attn=q4_k,ffn=q5_k,predict=q6_k
 ]
 
 
@@ -402,7 +404,7 @@ def test_export_formats_match_oracle(mat_type, ffn_type, predict_type, emb_type)
     """The exporter's formats besides --q8: Q8_0 / Q4_0 / Q5_0 / IQ4_NL / Q4_1 / Q5_1 / F16 / BF16 predict,
     F16 / BF16 embeddings (widened on load), F32 / F16 / BF16 attention and FFN matrices (ggml's
     FMA-vectorised dot), Q4_0 / Q5_0 / IQ4_NL matrices (repacked into Q8_0 blocks on load), Q4_1 / Q5_1
-    matrices (ggml's Q8_1 dot) and mixes of the attn / ffn groups. A teacher-forced decode trace (fused and unfused steps; float
+    matrices (ggml's Q8_1 dot), K-quant matrices (ggml's Q8_K dot) and mixes of the attn / ffn groups. A teacher-forced decode trace (fused and unfused steps; float
     matrices always run unfused) equals the oracle bit for bit, and so does a sampled generate through
     the graph-captured decode step."""
     import gsvcu
