@@ -43,7 +43,8 @@ def parse():
     ap.add_argument("--kv", default="f16", choices=["f16", "f32"])
     ap.add_argument("--format", default="q8_0", choices=list(FORMATS),
                     help="model file of the serve workload: q8_0 (the exporter's --q8, the headline), f16 (its --f16 "
-                         "preset: F16 matrices, predict and embeddings) or f32 (no flags)")
+                         "preset: F16 matrices, predict and embeddings), f32 (no flags) or q6_k (--spec "
+                         "attn=q8_0,ffn=q6_k,predict=f16,emb=f16)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-seqs", type=int, default=16,
                     help="sequences of the bounded CPU sample the baseline / reference arm extrapolates from")
@@ -470,6 +471,9 @@ FORMATS = {
     "q8_0": (dict(mat_type="q8_0"), 82954240, "Q8_0 attn/FFN, F32 predict"),
     "f16": (dict(mat_type="f16", predict_type="f16", emb_type="f16"), 152683520, "F16 attn/FFN/predict/embeddings"),
     "f32": (dict(mat_type="f32"), 304728064, "F32 attn/FFN/predict"),
+    # the exporter's own example: --spec attn=q8_0,ffn=q6_k,predict=f16,emb=f16 (file bytes of the matrices)
+    "q6_k": (dict(mat_type="q8_0", ffn_type="q6_k", predict_type="f16", emb_type="f16"), 69714944,
+             "Q8_0 attn, Q6_K FFN, F16 predict/embeddings"),
 }
 
 
@@ -589,7 +593,8 @@ def main():
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": n_gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_v / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None,
-        "dtype": ("q8_0 int8 MMA" if args.format == "q8_0" else f"{args.format} weights / f32 FMA") +
+        "dtype": ("q8_0 int8 MMA" if args.format == "q8_0" else
+                  "q8_0 int8 MMA + q6_k dp2a" if args.format == "q6_k" else f"{args.format} weights / f32 FMA") +
                  f" / f32 softmax / {args.kv} KV",
         "data": "synthetic (seeded GGUF weights N(0,0.02), requests U[80,400])",
         "config": {"workload": "cfg4: box-wide serving shard per GPU (BASELINE configs[4])",

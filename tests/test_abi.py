@@ -119,3 +119,19 @@ def test_null_arguments_are_rejected():
     assert lib.gsvcu_serve_step(None, 1, None, 0, None, 0) == -1
     assert lib.gsvcu_inspect_gguf(None, None, None, 0) == -1
     assert lib.gsvcu_last_error(None) == b"null context"
+
+
+def test_bench_weight_bytes_per_format(tmp_path):
+    """bench.py's per-format weight bytes per decode step equal the GGUF bytes of the matrices the step reads
+    (24 layers of attention / FFN matrices, their F32 biases and LayerNorms, the predict matrix)."""
+    import importlib.util
+    import gguf
+    import gsv_synth as S
+    spec = importlib.util.spec_from_file_location("bench_mod", os.path.join(os.path.dirname(__file__), "..", "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    for name, (kw, nbytes, _) in bench.FORMATS.items():
+        path = S.write_model(str(tmp_path / f"{name}.gguf"), seed=1, dims=S.Dims(NL=1), **kw)
+        t = {x.name: int(x.n_bytes) for x in gguf.GGUFReader(path).tensors}
+        layer = sum(v for k, v in t.items() if k.startswith("transformer.block0."))
+        assert 24 * layer + t["ar.predict"] == nbytes, name
