@@ -222,3 +222,74 @@ def ragged_requests(seed: int, B: int, lo: int = 80, hi: int = 400, text_frac: f
         T = int(round(text_frac * P))
         out.append(make_request(rng, T, P - T))
     return out
+
+
+@dataclass
+class BertDims:
+    """Dims of a synthetic gsv BERT (chinese-roberta-wwm-ext-large: 1024 / 16 / 4096 / 24 layers, 22 used)."""
+    D: int = 1024
+    NH: int = 16
+    FF: int = 4096
+    NL: int = 24
+    VOCAB: int = 21128
+    MAXPOS: int = 512
+
+
+def write_bert_model(path: str, seed: int = 0, dims: BertDims | None = None, mat_type: str = "f32") -> str:
+    """Seeded synthetic BERT GGUF with the names, shapes, dtypes and KV keys of the reference exporter
+    (tools/export_gguf/convert_bert.py:38-88): embeddings, norms and biases F32, attention / FFN
+    matrices `mat_type` (its --spec attn=..,ffn=..). Values N(0, 0.02), LayerNorm weights 1 + N(0, 0.02)."""
+    import gguf
+
+    d = dims or BertDims()
+    rng = np.random.default_rng(seed)
+    types = {"f32": gguf.GGMLQuantizationType.F32, "f16": gguf.GGMLQuantizationType.F16,
+             "q8_0": gguf.GGMLQuantizationType.Q8_0}
+
+    def n(*shape, s=0.02):
+        return (rng.standard_normal(shape, dtype=np.float32) * np.float32(s)).astype(np.float32)
+
+    w = gguf.GGUFWriter(path, "gsv.bert")
+    w.add_uint32("bert.n_layer", d.NL)
+    w.add_uint32("bert.hidden", d.D)
+    w.add_uint32("bert.head", d.NH)
+    w.add_uint32("bert.inter", d.FF)
+    w.add_float32("bert.ln_eps", 1e-12)
+    w.add_uint32("bert.vocab", d.VOCAB)
+    w.add_uint32("bert.max_pos", d.MAXPOS)
+    w.add_uint32("bert.layers_used", d.NL - 2)
+
+    def add(name, arr, qt=gguf.GGMLQuantizationType.F32):
+        arr = np.ascontiguousarray(arr, dtype=np.float32)
+        if qt == gguf.GGMLQuantizationType.F32:
+            w.add_tensor(name, arr, raw_dtype=qt)
+        elif qt == gguf.GGMLQuantizationType.F16:
+            w.add_tensor(name, arr.astype(np.float16), raw_dtype=qt)
+        else:
+            w.add_tensor(name, gguf.quants.quantize(arr, qt), raw_dtype=qt)
+
+    mt = types[mat_type]
+    add("bert.word_emb", n(d.VOCAB, d.D))
+    add("bert.pos_emb", n(d.MAXPOS, d.D))
+    add("bert.type_emb", n(2, d.D))
+    add("bert.emb_ln_w", 1.0 + n(d.D))
+    add("bert.emb_ln_b", n(d.D))
+    for li in range(d.NL):
+        p = f"bert.l{li}."
+        add(p + "qkv_w", n(3 * d.D, d.D), mt)
+        add(p + "qkv_b", n(3 * d.D))
+        add(p + "attn_out_w", n(d.D, d.D), mt)
+        add(p + "attn_out_b", n(d.D))
+        add(p + "attn_ln_w", 1.0 + n(d.D))
+        add(p + "attn_ln_b", n(d.D))
+        add(p + "ff1_w", n(d.FF, d.D), mt)
+        add(p + "ff1_b", n(d.FF))
+        add(p + "ff2_w", n(d.D, d.FF), mt)
+        add(p + "ff2_b", n(d.D))
+        add(p + "out_ln_w", 1.0 + n(d.D))
+        add(p + "out_ln_b", n(d.D))
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    return path

@@ -388,11 +388,13 @@ void ln_affine(const float* x, const float* r, const float* bias, const float* w
 }
 
 // add_act (P:1587-1620): act(a[i] + b[i % n]); act 1 = ReLU, 0 = identity.
+// act: 0 identity, 1 ReLU, 2 GELU (erf form: 0.5*v*(1 + erff(v/sqrt(2))), P:1615)
 void add_act(const float* a, const float* b, int64_t rows, int64_t n, int act, float* y) {
     for (int64_t r = 0; r < rows; r++)
         for (int64_t i = 0; i < n; i++) {
             const float v = a[r * n + i] + b[i];
-            y[r * n + i] = act == 1 ? (v > 0.0f ? v : 0.0f) : v;
+            if (act == 2) y[r * n + i] = 0.5f * v * (1.0f + erff(v * 0.70710678118654752440f));
+            else y[r * n + i] = act == 1 ? (v > 0.0f ? v : 0.0f) : v;
         }
 }
 
@@ -1306,6 +1308,125 @@ int orc_generate(orc_model* m, int B, const int32_t* phones, const int32_t* n_ph
         n_tokens_out[b] = (int32_t)res[b].size();
         lens_out[b] = lens[b];
     }
+    return 0;
+}
+
+
+// ================================================================== BERT feature producer
+// chinese-roberta-wwm-ext-large as src/gsv_bert.cpp runs it (gsv_bert::impl::run_g, :102-183) for one
+// sequence: x = (word_emb[id] + pos_emb[t]) + type_emb[0], LayerNorm; per layer (post-LN, HF BertLayer):
+// qkv = W_qkv x + b, per head flash_attn_ext over all keys (scale 1/sqrt(HD), no mask), cur = LN(cur +
+// W_out attn + b_out), h = GELU_erf(W1 cur + b1), cur = LN(cur + W2 h + b2). Only the first
+// bert.layers_used layers run (hidden_states[-3]); the output is [D][T]. The matrices take the layer
+// mul_mat semantics above (F32 / F16 in the FMA-vectorised order, quantized types by their dots); the
+// attention is attn_row; LayerNorm is ln_affine with eps = bert.ln_eps.
+struct orc_bert_layer {
+    Mat qkv_w, out_w, f1w, f2w;
+    std::vector<float> qkv_b, out_b, ln1_w, ln1_b, f1b, f2b, ln2_w, ln2_b;
+};
+
+struct orc_bert {
+    int D = 1024, NH = 16, HD = 64, FF = 4096, NL = 22, VOCAB = 21128, MAXPOS = 512;
+    float EPS = 1e-12f;
+    std::vector<float> word, pos, type, eln_w, eln_b;
+    std::vector<orc_bert_layer> L;
+    std::string err;
+};
+
+orc_bert* orc_bert_new(int D, int NH, int FF, int NL, int vocab, int maxpos, float eps) {
+    orc_bert* m = new orc_bert();
+    m->D = D; m->NH = NH; m->HD = NH > 0 ? D / NH : 0; m->FF = FF; m->NL = NL; m->VOCAB = vocab; m->MAXPOS = maxpos;
+    m->EPS = eps;
+    m->L.resize((size_t)std::max(NL, 0));
+    return m;
+}
+void orc_bert_free(orc_bert* m) { delete m; }
+const char* orc_bert_error(const orc_bert* m) { return m ? m->err.c_str() : "null model"; }
+
+// Tensor names of tools/export_gguf/convert_bert.py:62-88 (bert.word_emb, bert.l<i>.qkv_w, ...); tensors
+// of layers >= layers_used are ignored (0), unknown names are an error (-1).
+int orc_bert_set(orc_bert* m, const char* name, int type, const void* data, int64_t nbytes) {
+    const std::string n(name);
+    const int D = m->D, FF = m->FF;
+    if (n == "bert.word_emb") return set_emb(m->word, type, data, nbytes, (int64_t)m->VOCAB * D, m->err, name) ? 0 : -1;
+    if (n == "bert.pos_emb") return set_emb(m->pos, type, data, nbytes, (int64_t)m->MAXPOS * D, m->err, name) ? 0 : -1;
+    if (n == "bert.type_emb") {
+        if (nbytes < (int64_t)D * (type == T_F32 ? 4 : 2)) { m->err = "bad size for bert.type_emb"; return -1; }
+        return set_emb(m->type, type, data, nbytes, nbytes / (type == T_F32 ? 4 : 2), m->err, name) ? 0 : -1;
+    }
+    if (n == "bert.emb_ln_w") return set_vec(m->eln_w, type, data, nbytes, D, m->err, name) ? 0 : -1;
+    if (n == "bert.emb_ln_b") return set_vec(m->eln_b, type, data, nbytes, D, m->err, name) ? 0 : -1;
+    int li = -1, off = 0;
+    if (std::sscanf(name, "bert.l%d.%n", &li, &off) == 1 && off > 0) {
+        if (li < 0) { m->err = std::string("bad layer in ") + name; return -1; }
+        if (li >= m->NL) return 0;
+        orc_bert_layer& L = m->L[(size_t)li];
+        const std::string f = n.substr((size_t)off);
+        if (f == "qkv_w") return set_mat(L.qkv_w, type, data, nbytes, 3 * D, D, m->err, name, true) ? 0 : -1;
+        if (f == "attn_out_w") return set_mat(L.out_w, type, data, nbytes, D, D, m->err, name, true) ? 0 : -1;
+        if (f == "ff1_w") return set_mat(L.f1w, type, data, nbytes, FF, D, m->err, name, true) ? 0 : -1;
+        if (f == "ff2_w") return set_mat(L.f2w, type, data, nbytes, D, FF, m->err, name, true) ? 0 : -1;
+        if (f == "qkv_b") return set_vec(L.qkv_b, type, data, nbytes, 3 * D, m->err, name) ? 0 : -1;
+        if (f == "attn_out_b") return set_vec(L.out_b, type, data, nbytes, D, m->err, name) ? 0 : -1;
+        if (f == "attn_ln_w") return set_vec(L.ln1_w, type, data, nbytes, D, m->err, name) ? 0 : -1;
+        if (f == "attn_ln_b") return set_vec(L.ln1_b, type, data, nbytes, D, m->err, name) ? 0 : -1;
+        if (f == "ff1_b") return set_vec(L.f1b, type, data, nbytes, FF, m->err, name) ? 0 : -1;
+        if (f == "ff2_b") return set_vec(L.f2b, type, data, nbytes, D, m->err, name) ? 0 : -1;
+        if (f == "out_ln_w") return set_vec(L.ln2_w, type, data, nbytes, D, m->err, name) ? 0 : -1;
+        if (f == "out_ln_b") return set_vec(L.ln2_b, type, data, nbytes, D, m->err, name) ? 0 : -1;
+    }
+    m->err = std::string("unknown tensor ") + name;
+    return -1;
+}
+
+int orc_bert_finalize(orc_bert* m) {
+    if (m->D <= 0 || m->NH <= 0 || m->D % m->NH || m->HD > 256 || m->word.empty() || m->pos.empty() ||
+        m->type.size() < (size_t)m->D || m->eln_w.empty() || m->eln_b.empty()) {
+        m->err = "incomplete BERT model (embeddings / dims)";
+        return -1;
+    }
+    for (const orc_bert_layer& L : m->L)
+        if (L.qkv_w.N == 0 || L.out_w.N == 0 || L.f1w.N == 0 || L.f2w.N == 0 || L.qkv_b.empty() || L.ln2_b.empty()) {
+            m->err = "incomplete BERT layer";
+            return -1;
+        }
+    return 0;
+}
+
+// ids [T] (with [CLS] / [SEP], T <= max_pos) -> out [D][T] after the first n_layers layers (n_layers < 0 or
+// > layers_used: all of them; 0: the embedding LayerNorm output), as gsv_bert::encode / encode_layers.
+int orc_bert_run(orc_bert* m, const int32_t* ids, int T, int n_layers, float* out) {
+    const int D = m->D, HD = m->HD, NH = m->NH, FF = m->FF;
+    if (T < 1 || T > m->MAXPOS) { m->err = "bad sequence length"; return -1; }
+    for (int t = 0; t < T; t++)
+        if (ids[t] < 0 || ids[t] >= m->VOCAB) { m->err = "token id out of range"; return -1; }
+    if (n_layers < 0 || n_layers > m->NL) n_layers = m->NL;
+    std::vector<float> x((size_t)T * D), cur((size_t)T * D);
+    for (int t = 0; t < T; t++)
+        for (int d = 0; d < D; d++)
+            x[(size_t)t * D + d] = (m->word[(size_t)ids[t] * D + d] + m->pos[(size_t)t * D + d]) + m->type[(size_t)d];
+    ln_affine(x.data(), nullptr, nullptr, m->eln_w.data(), m->eln_b.data(), T, D, m->EPS, cur.data());
+    const float scale = 1.0f / std::sqrt((float)HD);
+    std::vector<float> qkv((size_t)T * 3 * D), att((size_t)T * D), ao((size_t)T * D), h((size_t)T * FF), fo((size_t)T * D);
+    for (int li = 0; li < n_layers; li++) {
+        const orc_bert_layer& L = m->L[(size_t)li];
+        mul_mat(L.qkv_w, cur.data(), T, qkv.data());
+        for (int t = 0; t < T; t++)
+            for (int j = 0; j < 3 * D; j++) qkv[(size_t)t * 3 * D + j] += L.qkv_b[(size_t)j];
+        #pragma omp parallel for num_threads(nthreads()) schedule(static) collapse(2)
+        for (int t = 0; t < T; t++)
+            for (int hh = 0; hh < NH; hh++)
+                attn_row(qkv.data() + (size_t)t * 3 * D + hh * HD, qkv.data() + D + hh * HD, qkv.data() + 2 * D + hh * HD,
+                         3 * D, T, HD, scale, [](int64_t) { return true; }, att.data() + (size_t)t * D + hh * HD);
+        mul_mat(L.out_w, att.data(), T, ao.data());
+        ln_affine(cur.data(), ao.data(), L.out_b.data(), L.ln1_w.data(), L.ln1_b.data(), T, D, m->EPS, x.data());
+        mul_mat(L.f1w, x.data(), T, h.data());
+        add_act(h.data(), L.f1b.data(), T, FF, 2, h.data());
+        mul_mat(L.f2w, h.data(), T, fo.data());
+        ln_affine(x.data(), fo.data(), L.f2b.data(), L.ln2_w.data(), L.ln2_b.data(), T, D, m->EPS, cur.data());
+    }
+    for (int d = 0; d < D; d++)
+        for (int t = 0; t < T; t++) out[(size_t)d * T + t] = cur[(size_t)t * D + d];
     return 0;
 }
 

@@ -54,6 +54,17 @@ def _load():
     lib.orc_model_set.restype = C.c_int
     lib.orc_model_finalize.argtypes = [C.c_void_p, C.c_int]
     lib.orc_model_finalize.restype = C.c_int
+    lib.orc_bert_new.argtypes = [C.c_int] * 6 + [C.c_float]
+    lib.orc_bert_new.restype = C.c_void_p
+    lib.orc_bert_free.argtypes = [C.c_void_p]
+    lib.orc_bert_error.argtypes = [C.c_void_p]
+    lib.orc_bert_error.restype = C.c_char_p
+    lib.orc_bert_set.argtypes = [C.c_void_p, C.c_char_p, C.c_int, C.c_void_p, C.c_int64]
+    lib.orc_bert_set.restype = C.c_int
+    lib.orc_bert_finalize.argtypes = [C.c_void_p]
+    lib.orc_bert_finalize.restype = C.c_int
+    lib.orc_bert_run.argtypes = [C.c_void_p, _i32p, C.c_int, C.c_int, _f32p]
+    lib.orc_bert_run.restype = C.c_int
     lib.orc_model_pe.argtypes = [C.c_void_p]
     lib.orc_model_pe.restype = C.POINTER(C.c_float)
     req = [C.c_void_p, C.c_int, _i32p, _i32p, _f32p, _i32p, _i32p]
@@ -193,6 +204,53 @@ def pack_requests(reqs, bert_dim=1024):
                                                   + [np.zeros(0, np.int32)]), np.int32)
     n_pr = np.array([len(r.prompt) for r in reqs], np.int32)
     return phones, n_ph, bert, prompts, n_pr
+
+
+class BertOracle:
+    """CPU restatement of gsv_bert (reference src/gsv_bert.{h,cpp}) over a GGUF file of
+    tools/export_gguf/convert_bert.py."""
+
+    def __init__(self, gguf_path: str):
+        import gguf  # gguf-py
+
+        rd = gguf.GGUFReader(gguf_path)
+
+        def kv(key, default, cast=int):
+            f = rd.fields.get(key)
+            return default if f is None else cast(f.parts[f.data[0]][0])
+
+        self.D = kv("bert.hidden", 1024)
+        self.NH = kv("bert.head", 16)
+        self.FF = kv("bert.inter", 4096)
+        self.NL = kv("bert.layers_used", 22)
+        self.VOCAB = kv("bert.vocab", 21128)
+        self.MAXPOS = kv("bert.max_pos", 512)
+        self.EPS = kv("bert.ln_eps", 1e-12, float)
+        L = lib()
+        self._m = L.orc_bert_new(self.D, self.NH, self.FF, self.NL, self.VOCAB, self.MAXPOS, self.EPS)
+        for t in rd.tensors:
+            data = np.ascontiguousarray(t.data)
+            if L.orc_bert_set(self._m, t.name.encode(), int(t.tensor_type), data.ctypes.data, data.nbytes) < 0:
+                raise ValueError(L.orc_bert_error(self._m).decode())
+        if L.orc_bert_finalize(self._m) != 0:
+            raise ValueError(L.orc_bert_error(self._m).decode())
+
+    def __del__(self):
+        if getattr(self, "_m", None) and _LIB is not None:
+            _LIB.orc_bert_free(self._m)
+            self._m = None
+
+    def encode(self, ids, n_layers=-1) -> np.ndarray:
+        """gsv_bert::encode (n_layers < 0) / encode_layers: features [D][T]."""
+        ids = np.ascontiguousarray(ids, np.int32)
+        out = np.empty((self.D, ids.size), np.float32)
+        if lib().orc_bert_run(self._m, ids, ids.size, n_layers, out):
+            raise ValueError(lib().orc_bert_error(self._m).decode())
+        return out
+
+    def encode_feat(self, ids) -> np.ndarray:
+        """gsv_bert::encode_feat: features without [CLS] / [SEP], [D][T-2]."""
+        return self.encode(ids)[:, 1:-1].copy()
 
 
 class OracleModel:

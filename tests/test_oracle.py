@@ -496,3 +496,55 @@ def test_oracle_kquant_restated(kind, wtype):
     for l in range(8):
         sumf = (sumf + sums[..., l]).astype(np.float32)
     assert np.array_equal(O.mul_mat(raw, wtype, N, K, X), sumf)
+
+
+# ------------------------------------------------------------------ BERT feature producer
+def _np_bert(path, ids, n_layers):
+    """float64 numpy BERT (HF BertModel semantics, post-LN, GELU erf) over the GGUF weights -> [D][T]."""
+    import gguf
+    from scipy.special import erf
+    rd = gguf.GGUFReader(path)
+    kv = {f.name: f.parts[f.data[0]][0] for f in rd.fields.values() if f.name.startswith("bert.")}
+    D, NH, FF, eps = int(kv["bert.hidden"]), int(kv["bert.head"]), int(kv["bert.inter"]), float(kv["bert.ln_eps"])
+    HD = D // NH
+    T = {t.name: np.array(t.data, dtype=np.float64) for t in rd.tensors}
+
+    def ln(v, w, b):
+        return (v - v.mean(-1, keepdims=True)) / np.sqrt(v.var(-1, keepdims=True) + eps) * w + b
+
+    S = len(ids)
+    x = T["bert.word_emb"].reshape(-1, D)[ids] + T["bert.pos_emb"].reshape(-1, D)[:S] + T["bert.type_emb"].reshape(-1, D)[0]
+    x = ln(x, T["bert.emb_ln_w"], T["bert.emb_ln_b"])
+    for li in range(n_layers):
+        p = f"bert.l{li}."
+        qkv = x @ T[p + "qkv_w"].reshape(3 * D, D).T + T[p + "qkv_b"]
+        q, k, v = (qkv[:, i * D:(i + 1) * D].reshape(S, NH, HD) for i in range(3))
+        s = np.einsum("qhd,khd->hqk", q, k) / np.sqrt(HD)
+        a = np.exp(s - s.max(-1, keepdims=True))
+        att = np.einsum("hqk,khd->qhd", a / a.sum(-1, keepdims=True), v).reshape(S, D)
+        x = ln(x + att @ T[p + "attn_out_w"].reshape(D, D).T + T[p + "attn_out_b"], T[p + "attn_ln_w"], T[p + "attn_ln_b"])
+        hpre = x @ T[p + "ff1_w"].reshape(FF, D).T + T[p + "ff1_b"]
+        h = 0.5 * hpre * (1.0 + erf(hpre / np.sqrt(2.0)))
+        x = ln(x + h @ T[p + "ff2_w"].reshape(D, FF).T + T[p + "ff2_b"], T[p + "out_ln_w"], T[p + "out_ln_b"])
+    return x.T
+
+
+@pytest.mark.parametrize("mat_type,tol", [("f32", 1e-6), ("f16", 2e-4)])
+def test_bert_oracle_vs_float64(tmp_path, mat_type, tol):
+    """The BERT feature producer (src/gsv_bert.cpp): embeddings + LayerNorm, post-LN layers with GELU-erf
+    FFN, only bert.layers_used layers run; [D][T] features, encode_feat drops [CLS] / [SEP]. Against an
+    independent float64 numpy BERT on the same GGUF: F32 matrices within float accumulation, F16 matrices
+    within the F16 rounding of the activations (ggml's vec_dot_type)."""
+    dims = S.BertDims(D=128, NH=2, FF=512, NL=5, VOCAB=300, MAXPOS=48)
+    path = S.write_bert_model(str(tmp_path / f"bert_{mat_type}.gguf"), seed=7, dims=dims, mat_type=mat_type)
+    orc = O.BertOracle(path)
+    assert orc.NL == 3 and orc.D == 128
+    rng = np.random.default_rng(8)
+    ids = rng.integers(0, 300, 37).astype(np.int32)
+    for k in (0, 1, 3):
+        got = orc.encode(ids, n_layers=k)
+        assert got.shape == (128, 37)
+        assert rel_l2(got, _np_bert(path, ids, k)) < (5e-7 if k == 0 else tol), k
+    full = orc.encode(ids)
+    assert np.array_equal(full, orc.encode(ids, n_layers=3))
+    assert np.array_equal(orc.encode_feat(ids), full[:, 1:-1])
