@@ -252,6 +252,22 @@ class BertOracle:
         """gsv_bert::encode_feat: features without [CLS] / [SEP], [D][T-2]."""
         return self.encode(ids)[:, 1:-1].copy()
 
+    def encode_layers(self, ids):
+        """gsv_bert::encode_layers: (features, per_layer) with per_layer[0] the embedding LayerNorm output
+        and per_layer[k] the output of layer k-1, layers_used + 1 entries."""
+        per_layer = [self.encode(ids, n_layers=k) for k in range(self.NL + 1)]
+        return per_layer[-1], per_layer
+
+    def encode_feat_batch(self, ids_flat, lens, tmax):
+        """gsv_bert::encode_feat_batch (src/gsv_bert.cpp:271-311): B sequences of lens[b] tokens in slots of
+        tmax. The reference runs them as one block-diagonally masked sequence; here each row's dot and each
+        masked attention row do not depend on the batch, so this equals encode_feat per sequence."""
+        ids_flat = np.asarray(ids_flat, np.int32)
+        if tmax < 3 or tmax > self.MAXPOS or len(lens) == 0 or ids_flat.size < len(lens) * tmax:
+            raise ValueError("encode_feat_batch: bad args")
+        return [self.encode_feat(ids_flat[b * tmax: b * tmax + lens[b]]) if lens[b] > 2 else
+                np.zeros((self.D, 0), np.float32) for b in range(len(lens))]
+
 
 class OracleModel:
     """CPU restatement of gsv_ar (reference src/gsv_ar.{h,cpp}) over a GGUF file."""

@@ -548,3 +548,12 @@ def test_bert_oracle_vs_float64(tmp_path, mat_type, tol):
     full = orc.encode(ids)
     assert np.array_equal(full, orc.encode(ids, n_layers=3))
     assert np.array_equal(orc.encode_feat(ids), full[:, 1:-1])
+    feats, per = orc.encode_layers(ids)
+    assert len(per) == 4 and np.array_equal(feats, full) and np.array_equal(per[1], orc.encode(ids, n_layers=1))
+    lens = [37, 5, 2]
+    flat = np.concatenate([ids, ids[:5], ids[:2]] + [np.zeros(0, np.int32)])
+    slots = np.zeros(3 * 40, np.int32)
+    for b, (o, n) in enumerate(zip([0, 37, 42], lens)):
+        slots[b * 40: b * 40 + n] = flat[o: o + n]
+    bat = orc.encode_feat_batch(slots, lens, 40)
+    assert np.array_equal(bat[0], orc.encode_feat(ids)) and bat[1].shape == (128, 3) and bat[2].shape == (128, 0)
