@@ -557,3 +557,49 @@ def test_bert_oracle_vs_float64(tmp_path, mat_type, tol):
         slots[b * 40: b * 40 + n] = flat[o: o + n]
     bat = orc.encode_feat_batch(slots, lens, 40)
     assert np.array_equal(bat[0], orc.encode_feat(ids)) and bat[1].shape == (128, 3) and bat[2].shape == (128, 0)
+
+
+def test_bert_oracle_vs_transformers(tmp_path):
+    """The BERT restatement against Hugging Face's BertModel (the model GPT-SoVITS takes hidden_states[-3]
+    from) in float64, with the synthetic GGUF weights mapped back the way tools/export_gguf/convert_bert.py
+    wrote them (q|k|v rows concatenated): embeddings, post-LN layers, GELU (erf), and layers_used =
+    n_layer - 2 = hidden_states[-3]."""
+    torch = pytest.importorskip("torch")
+    transformers = pytest.importorskip("transformers")
+    import gguf
+    dims = S.BertDims(D=128, NH=2, FF=512, NL=5, VOCAB=300, MAXPOS=48)
+    path = S.write_bert_model(str(tmp_path / "bert_hf.gguf"), seed=11, dims=dims)
+    T = {t.name: torch.from_numpy(np.array(t.data, dtype=np.float64)) for t in gguf.GGUFReader(path).tensors}
+    D = dims.D
+    cfg = transformers.BertConfig(vocab_size=dims.VOCAB, hidden_size=D, num_hidden_layers=dims.NL,
+                                  num_attention_heads=dims.NH, intermediate_size=dims.FF,
+                                  max_position_embeddings=dims.MAXPOS, type_vocab_size=2, layer_norm_eps=1e-12,
+                                  hidden_act="gelu", hidden_dropout_prob=0.0, attention_probs_dropout_prob=0.0)
+    model = transformers.BertModel(cfg, add_pooling_layer=False).double().eval()
+    sd = {"embeddings.word_embeddings.weight": T["bert.word_emb"].reshape(-1, D),
+          "embeddings.position_embeddings.weight": T["bert.pos_emb"].reshape(-1, D),
+          "embeddings.token_type_embeddings.weight": T["bert.type_emb"].reshape(-1, D),
+          "embeddings.LayerNorm.weight": T["bert.emb_ln_w"], "embeddings.LayerNorm.bias": T["bert.emb_ln_b"]}
+    for li in range(dims.NL):
+        p, h = f"bert.l{li}.", f"encoder.layer.{li}."
+        w, b = T[p + "qkv_w"].reshape(3 * D, D), T[p + "qkv_b"]
+        for i, n in enumerate(("query", "key", "value")):
+            sd[h + f"attention.self.{n}.weight"] = w[i * D:(i + 1) * D]
+            sd[h + f"attention.self.{n}.bias"] = b[i * D:(i + 1) * D]
+        sd[h + "attention.output.dense.weight"] = T[p + "attn_out_w"].reshape(D, D)
+        sd[h + "attention.output.dense.bias"] = T[p + "attn_out_b"]
+        sd[h + "attention.output.LayerNorm.weight"] = T[p + "attn_ln_w"]
+        sd[h + "attention.output.LayerNorm.bias"] = T[p + "attn_ln_b"]
+        sd[h + "intermediate.dense.weight"] = T[p + "ff1_w"].reshape(dims.FF, D)
+        sd[h + "intermediate.dense.bias"] = T[p + "ff1_b"]
+        sd[h + "output.dense.weight"] = T[p + "ff2_w"].reshape(D, dims.FF)
+        sd[h + "output.dense.bias"] = T[p + "ff2_b"]
+        sd[h + "output.LayerNorm.weight"] = T[p + "out_ln_w"]
+        sd[h + "output.LayerNorm.bias"] = T[p + "out_ln_b"]
+    missing, unexpected = model.load_state_dict(sd, strict=False)
+    assert not unexpected and all("position_ids" in k or "token_type_ids" in k for k in missing), missing
+    ids = np.random.default_rng(12).integers(0, dims.VOCAB, 29).astype(np.int32)
+    with torch.no_grad():
+        hs = model(torch.from_numpy(ids.astype(np.int64))[None], output_hidden_states=True).hidden_states
+    ref = hs[-3][0].numpy().T                                          # [D][T]
+    assert rel_l2(O.BertOracle(path).encode(ids), ref) < 1e-6
