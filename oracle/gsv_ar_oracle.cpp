@@ -54,6 +54,7 @@
 #ifdef _OPENMP
 #include <omp.h>
 #endif
+#include <immintrin.h>
 
 namespace {
 
@@ -181,14 +182,25 @@ void quantize_q8_k(const float* x, int64_t n, int8_t* q, float* d_out, int32_t* 
     }
 }
 
+// fp16 -> f32 of every bit pattern, tabulated once from f16_to_f32 (same values, no per-call work).
+const float* f16_table() {
+    static const std::vector<float> t = [] {
+        std::vector<float> v(65536);
+        for (uint32_t h = 0; h < 65536; h++) v[h] = f16_to_f32((uint16_t)h);
+        return v;
+    }();
+    return t.data();
+}
+
 inline float q8_d(const uint8_t* blk) {
     uint16_t h;
     std::memcpy(&h, blk, 2);
-    return f16_to_f32(h);
+    return f16_table()[h];
 }
 
 // ggml_vec_dot_q8_0_q8_0 semantics: exact integer block dot, float accumulation in block order.
-inline float vec_dot_q8_0(int64_t K, const uint8_t* w, const uint8_t* x) {
+// Scalar statement; vec_dot_q8_0 below is the same arithmetic with the integer dot in AVX2.
+inline float vec_dot_q8_0_scalar(int64_t K, const uint8_t* w, const uint8_t* x) {
     const int64_t nb = K / QK;
     float sumf = 0.0f;
     for (int64_t ib = 0; ib < nb; ib++) {
@@ -201,6 +213,34 @@ inline float vec_dot_q8_0(int64_t K, const uint8_t* w, const uint8_t* x) {
     }
     return sumf;
 }
+
+// Exact int32 sum of the 32 products of one block pair. |a| (unsigned) times sign(a)*b is a*b for
+// every int8 a and every b in [-127, 127] (Q8_0 quantizers never write -128 for the activations);
+// pairs of such products fit int16 (<= 2 * 128 * 127), so the sums are exact.
+inline __m256i block_dot_i32x8(const uint8_t* wq, const uint8_t* xq) {
+    const __m256i a = _mm256_loadu_si256((const __m256i*)wq);
+    const __m256i b = _mm256_loadu_si256((const __m256i*)xq);
+    const __m256i p16 = _mm256_maddubs_epi16(_mm256_sign_epi8(a, a), _mm256_sign_epi8(b, a));
+    return _mm256_madd_epi16(p16, _mm256_set1_epi16(1));
+}
+inline int32_t hsum_i32x8(__m256i v) {
+    __m128i s = _mm_add_epi32(_mm256_castsi256_si128(v), _mm256_extracti128_si256(v, 1));
+    s = _mm_add_epi32(s, _mm_shuffle_epi32(s, 0x4e));
+    s = _mm_add_epi32(s, _mm_shuffle_epi32(s, 0xb1));
+    return _mm_cvtsi128_si32(s);
+}
+
+inline float vec_dot_q8_0(int64_t K, const uint8_t* w, const uint8_t* x) {
+    const int64_t nb = K / QK;
+    float sumf = 0.0f;
+    for (int64_t ib = 0; ib < nb; ib++) {
+        const int32_t sumi = hsum_i32x8(block_dot_i32x8(w + ib * Q8_BYTES + 2, x + ib * Q8_BYTES + 2));
+        const float d = q8_d(w + ib * Q8_BYTES) * q8_d(x + ib * Q8_BYTES);
+        sumf = std::fmaf((float)sumi, d, sumf);
+    }
+    return sumf;
+}
+
 
 // ggml_vec_dot_f32 (the F32 matrices: BERT projection, logits) with products exact in double,
 // accumulated in double, rounded once. ggml's scalar path rounds each product to float first and its
@@ -349,11 +389,39 @@ void mul_mat(const Mat& W, const float* X, int64_t M, float* Y) {
         std::vector<uint8_t> xq((size_t)M * (K / QK) * Q8_BYTES);
         #pragma omp parallel for num_threads(nthreads()) schedule(static)
         for (int64_t m = 0; m < M; m++) quantize_q8_0(X + m * K, K, xq.data() + m * (K / QK) * Q8_BYTES);
+        const int64_t rowb = (K / QK) * Q8_BYTES, nb = K / QK, N8 = N / 8 * 8;
+        // groups of 8 weight rows: the 8 rows' float chains run in the lanes of one vector (block
+        // order per lane, as vec_dot_q8_0); the int32 block sums of the 8 rows are reduced together
+        std::vector<float> dsc((size_t)(N8 * nb));   // [N/8][nb][8] weight scales
+        for (int64_t n = 0; n < N8; n++)
+            for (int64_t b = 0; b < nb; b++) dsc[(size_t)(((n >> 3) * nb + b) * 8 + (n & 7))] = q8_d(W.q.data() + n * rowb + b * Q8_BYTES);
         #pragma omp parallel for num_threads(nthreads()) schedule(static)
-        for (int64_t n = 0; n < N; n++) {
-            const uint8_t* w = W.q.data() + n * (K / QK) * Q8_BYTES;
-            for (int64_t m = 0; m < M; m++)
-                Y[m * N + n] = vec_dot_q8_0(K, w, xq.data() + m * (K / QK) * Q8_BYTES);
+        for (int64_t g = 0; g < N8 / 8; g++) {
+            const uint8_t* w0 = W.q.data() + g * 8 * rowb;
+            const float* ds = dsc.data() + (size_t)(g * nb * 8);
+            for (int64_t m = 0; m < M; m++) {
+                const uint8_t* x = xq.data() + m * rowb;
+                __m256 acc = _mm256_setzero_ps();
+                for (int64_t b = 0; b < nb; b++) {
+                    const size_t o = (size_t)b * Q8_BYTES;
+                    __m256i p[8];
+                    for (int r = 0; r < 8; r++) p[r] = block_dot_i32x8(w0 + r * rowb + o + 2, x + o + 2);
+                    const __m256i h01 = _mm256_hadd_epi32(p[0], p[1]), h23 = _mm256_hadd_epi32(p[2], p[3]);
+                    const __m256i h45 = _mm256_hadd_epi32(p[4], p[5]), h67 = _mm256_hadd_epi32(p[6], p[7]);
+                    const __m256i a = _mm256_hadd_epi32(h01, h23), c = _mm256_hadd_epi32(h45, h67);
+                    const __m256i sumi = _mm256_add_epi32(_mm256_permute2x128_si256(a, c, 0x20),
+                                                          _mm256_permute2x128_si256(a, c, 0x31));
+                    const __m256 d = _mm256_mul_ps(_mm256_loadu_ps(ds + b * 8), _mm256_set1_ps(q8_d(x + o)));
+                    acc = _mm256_fmadd_ps(_mm256_cvtepi32_ps(sumi), d, acc);
+                }
+                float out[8];
+                _mm256_storeu_ps(out, acc);
+                for (int r = 0; r < 8; r++) Y[m * N + g * 8 + r] = out[r];
+            }
+        }
+        for (int64_t n = N8; n < N; n++) {
+            const uint8_t* w = W.q.data() + n * rowb;
+            for (int64_t m = 0; m < M; m++) Y[m * N + n] = vec_dot_q8_0(K, w, xq.data() + m * rowb);
         }
     } else {
         #pragma omp parallel for num_threads(nthreads()) schedule(static)
@@ -508,6 +576,120 @@ void decode_attention_canonical(const float* q, const float* K, const float* Vv,
         for (int d = 0; d < HD; d++) O[d] = std::fma(w, po[(size_t)c * HD + d], O[d]);
     }
     for (int d = 0; d < HD; d++) out[d] = O[d] / L;
+}
+
+// exp_c on 8 lanes: the same operations as the scalar exp_c, lane by lane.
+inline __m256 exp_c8(__m256 x) {
+    const __m256 valid = _mm256_cmp_ps(x, _mm256_set1_ps(-87.0f), _CMP_GE_OQ);
+    const __m256 n = _mm256_round_ps(_mm256_mul_ps(x, _mm256_set1_ps(0x1.715476p+0f)),
+                                     _MM_FROUND_TO_NEAREST_INT | _MM_FROUND_NO_EXC);
+    const __m256 nn = _mm256_sub_ps(_mm256_setzero_ps(), n);
+    __m256 r = _mm256_fmadd_ps(nn, _mm256_set1_ps(0x1.62e4p-1f), x);
+    r = _mm256_fmadd_ps(nn, _mm256_set1_ps(0x1.7f7d1cp-20f), r);
+    __m256 p = _mm256_set1_ps(0x1.a01a02p-13f);
+    p = _mm256_fmadd_ps(p, r, _mm256_set1_ps(0x1.6c16c2p-10f));
+    p = _mm256_fmadd_ps(p, r, _mm256_set1_ps(0x1.111112p-7f));
+    p = _mm256_fmadd_ps(p, r, _mm256_set1_ps(0x1.555556p-5f));
+    p = _mm256_fmadd_ps(p, r, _mm256_set1_ps(0x1.555556p-3f));
+    p = _mm256_fmadd_ps(p, r, _mm256_set1_ps(0.5f));
+    p = _mm256_fmadd_ps(p, r, _mm256_set1_ps(1.0f));
+    p = _mm256_fmadd_ps(p, r, _mm256_set1_ps(1.0f));
+    const __m256i bits = _mm256_slli_epi32(_mm256_add_epi32(_mm256_cvtps_epi32(n), _mm256_set1_epi32(127)), 23);
+    return _mm256_and_ps(_mm256_mul_ps(p, _mm256_castsi256_ps(bits)), valid);
+}
+
+// K cache layout of the oracle's sequences: per (layer, head), blocks of 8 keys, dims major inside a
+// block ([key / 8][32 dims][key % 8]), so the 8 keys of a block sit in one vector per dimension.
+inline size_t kt_index(int64_t li, int h, int64_t t, int d, int NH, int64_t capb) {
+    return ((((size_t)li * NH + h) * capb + (size_t)(t >> 3)) * 32 + d) * 8 + (size_t)(t & 7);
+}
+
+// decode_attention_canonical over the blocked K layout (Kt: one head's blocks, V rows at vstride),
+// evaluated 8 keys per vector: every key's score, weight and sums go through the same operations in
+// the same order as the scalar statement, so the results are identical.
+void decode_attention_kt(const float* q, const float* Kt, const float* Vv, int64_t vstride, int64_t nk, float scale,
+                         float* out) {
+    constexpr int HD = 32, PG = 64;
+    const int64_t npg = (nk + PG - 1) / PG;
+    thread_local std::vector<float> pm, pl, po;
+    pm.resize((size_t)npg);
+    pl.resize((size_t)npg);
+    po.resize((size_t)npg * HD);
+    __m256 qb[HD];
+    for (int d = 0; d < HD; d++) qb[d] = _mm256_set1_ps(q[d]);
+    const __m256 vscale = _mm256_set1_ps(scale), ninf = _mm256_set1_ps(-INFINITY);
+    const __m256i lane = _mm256_setr_epi32(0, 1, 2, 3, 4, 5, 6, 7);
+    float M = -INFINITY;
+    alignas(32) float og[8][HD];
+    for (int64_t c = 0; c < npg; c++) {
+        const int n = (int)std::min<int64_t>(PG, nk - c * PG);
+        const int nblk = (n + 7) >> 3;
+        __m256 sc[8];
+        __m256 vm = ninf;
+        for (int u = 0; u < nblk; u++) {
+            const float* kb = Kt + (size_t)(c * 8 + u) * HD * 8;
+            __m256 D0 = _mm256_setzero_ps(), D1 = D0, D2 = D0, D3 = D0;
+            for (int e = 0; e < 8; e++) {
+                D0 = _mm256_fmadd_ps(qb[e], _mm256_loadu_ps(kb + (0 + e) * 8), D0);
+                D1 = _mm256_fmadd_ps(qb[8 + e], _mm256_loadu_ps(kb + (8 + e) * 8), D1);
+                D2 = _mm256_fmadd_ps(qb[16 + e], _mm256_loadu_ps(kb + (16 + e) * 8), D2);
+                D3 = _mm256_fmadd_ps(qb[24 + e], _mm256_loadu_ps(kb + (24 + e) * 8), D3);
+            }
+            __m256 sv = _mm256_mul_ps(_mm256_add_ps(_mm256_add_ps(D0, D1), _mm256_add_ps(D2, D3)), vscale);
+            const __m256 live = _mm256_castsi256_ps(_mm256_cmpgt_epi32(_mm256_set1_epi32(n - u * 8), lane));
+            sv = _mm256_blendv_ps(ninf, sv, live);
+            sc[u] = sv;
+            vm = _mm256_max_ps(vm, sv);
+        }
+        float mv[8];
+        _mm256_storeu_ps(mv, vm);
+        float m = -INFINITY;
+        for (int j = 0; j < 8; j++) m = std::max(m, mv[j]);
+        const __m256 vmm = _mm256_set1_ps(m);
+        alignas(32) float pbuf[PG];
+        __m256 Lg = _mm256_setzero_ps();
+        for (int u = 0; u < nblk; u++) {
+            const __m256 p = exp_c8(_mm256_sub_ps(sc[u], vmm));
+            _mm256_store_ps(pbuf + u * 8, p);
+            Lg = _mm256_add_ps(Lg, p);   // masked lanes add +0
+        }
+        for (int g = 0; g < 8; g++) {   // group g: keys g, g + 8, ... in ascending order
+            __m256 O0 = _mm256_setzero_ps(), O1 = O0, O2 = O0, O3 = O0;
+            for (int t = g; t < n; t += 8) {
+                const __m256 pt = _mm256_set1_ps(pbuf[t]);
+                const float* v = Vv + (c * PG + t) * vstride;
+                O0 = _mm256_fmadd_ps(pt, _mm256_loadu_ps(v + 0), O0);
+                O1 = _mm256_fmadd_ps(pt, _mm256_loadu_ps(v + 8), O1);
+                O2 = _mm256_fmadd_ps(pt, _mm256_loadu_ps(v + 16), O2);
+                O3 = _mm256_fmadd_ps(pt, _mm256_loadu_ps(v + 24), O3);
+            }
+            _mm256_store_ps(og[g] + 0, O0);
+            _mm256_store_ps(og[g] + 8, O1);
+            _mm256_store_ps(og[g] + 16, O2);
+            _mm256_store_ps(og[g] + 24, O3);
+        }
+        for (int j = 0; j < 4; j++) {   // ((0+1)+(2+3))+((4+5)+(6+7)) over the groups
+            auto ld = [&](int gg) { return _mm256_load_ps(og[gg] + 8 * j); };
+            const __m256 o = _mm256_add_ps(_mm256_add_ps(_mm256_add_ps(ld(0), ld(1)), _mm256_add_ps(ld(2), ld(3))),
+                                           _mm256_add_ps(_mm256_add_ps(ld(4), ld(5)), _mm256_add_ps(ld(6), ld(7))));
+            _mm256_storeu_ps(po.data() + (size_t)c * HD + 8 * j, o);
+        }
+        float lg[8];
+        _mm256_storeu_ps(lg, Lg);
+        pm[c] = m;
+        pl[c] = ((lg[0] + lg[1]) + (lg[2] + lg[3])) + ((lg[4] + lg[5]) + (lg[6] + lg[7]));
+        M = std::max(M, m);
+    }
+    float L = 0.0f;
+    __m256 O[4] = {_mm256_setzero_ps(), _mm256_setzero_ps(), _mm256_setzero_ps(), _mm256_setzero_ps()};
+    for (int64_t c = 0; c < npg; c++) {
+        const float w = exp_c(pm[c] - M);
+        L = std::fma(w, pl[c], L);
+        const __m256 vw = _mm256_set1_ps(w);
+        for (int j = 0; j < 4; j++) O[j] = _mm256_fmadd_ps(vw, _mm256_loadu_ps(po.data() + (size_t)c * HD + 8 * j), O[j]);
+    }
+    const __m256 vl = _mm256_set1_ps(L);
+    for (int j = 0; j < 4; j++) _mm256_storeu_ps(out + 8 * j, _mm256_div_ps(O[j], vl));
 }
 
 // ------------------------------------------------------------------ sampler (src/gsv_sampler.cpp)
@@ -809,10 +991,12 @@ struct Req {
     int P;
 };
 
-// Per-sequence KV cache, [layer][pos][D] with head h at dims h*HD.. (F32, or values rounded
-// through fp16 when emulating an F16 cache).
+// Per-sequence KV cache (F32, or values rounded through fp16 when emulating an F16 cache): V as
+// [layer][pos][D] with head h at dims h*HD..; K in the blocked layout of kt_index (capb blocks of 8
+// positions per layer and head).
 struct SeqCache {
     int len = 0, cap = 0;
+    int64_t capb = 0;
     std::vector<float> k, v;
 };
 
@@ -859,7 +1043,7 @@ void prefill_one(const orc_model& m, const Req& r, bool kv_f16, SeqCache& cache,
         for (int t = 0; t < S; t++)
             for (int d = 0; d < D; d++) {
                 const float kk = qkv[(size_t)t * 3 * D + D + d], vv = qkv[(size_t)t * 3 * D + 2 * D + d];
-                cache.k[((size_t)li * cache.cap + t) * D + d] = kv_f16 ? round_f16(kk) : kk;
+                cache.k[kt_index(li, d / HD, t, d % HD, NH, cache.capb)] = kv_f16 ? round_f16(kk) : kk;
                 cache.v[((size_t)li * cache.cap + t) * D + d] = kv_f16 ? round_f16(vv) : vv;
             }
         // prefix-masked attention on the F32 K/V of this pass (src/gsv_ar.cpp:257, mask :215-223)
@@ -911,7 +1095,7 @@ void decode_step(const orc_model& m, std::vector<SeqCache*>& caches, const float
             SeqCache& c = *caches[b];
             for (int d = 0; d < D; d++) {
                 const float kk = qkv[(size_t)b * 3 * D + D + d], vv = qkv[(size_t)b * 3 * D + 2 * D + d];
-                c.k[((size_t)li * c.cap + c.len) * D + d] = kv_f16 ? round_f16(kk) : kk;
+                c.k[kt_index(li, d / HD, c.len, d % HD, NH, c.capb)] = kv_f16 ? round_f16(kk) : kk;
                 c.v[((size_t)li * c.cap + c.len) * D + d] = kv_f16 ? round_f16(vv) : vv;
             }
         }
@@ -920,9 +1104,9 @@ void decode_step(const orc_model& m, std::vector<SeqCache*>& caches, const float
             for (int hh = 0; hh < NH; hh++) {
                 SeqCache& c = *caches[b];
                 const float* q = qkv.data() + (size_t)b * 3 * D + hh * HD;
-                const float* K = c.k.data() + (size_t)li * c.cap * D + hh * HD;
+                const float* Kt = c.k.data() + kt_index(li, hh, 0, 0, NH, c.capb);
                 const float* Vv = c.v.data() + (size_t)li * c.cap * D + hh * HD;
-                decode_attention_canonical(q, K, Vv, D, c.len + 1, scale, att.data() + (size_t)b * D + hh * HD);
+                decode_attention_kt(q, Kt, Vv, D, c.len + 1, scale, att.data() + (size_t)b * D + hh * HD);
             }
         mul_mat(w.out_w, att.data(), B, o.data());
         ln_affine(cur.data(), o.data(), w.out_b.data(), w.n1w.data(), w.n1b.data(), B, D, 1e-5f, n1.data());
@@ -974,8 +1158,9 @@ bool check_reqs(orc_model* m, const std::vector<Req>& reqs) {
 
 void init_cache(const orc_model& m, SeqCache& c, int cap) {
     c.cap = cap;
+    c.capb = (cap + 63) / 64 * 8;   // whole 64-key pages
     c.len = 0;
-    c.k.assign((size_t)m.NL * cap * m.D, 0.0f);
+    c.k.assign((size_t)m.NL * m.NH * c.capb * 8 * m.HD, 0.0f);
     c.v.assign((size_t)m.NL * cap * m.D, 0.0f);
 }
 
@@ -1309,6 +1494,196 @@ int orc_generate(orc_model* m, int B, const int32_t* phones, const int32_t* n_ph
         lens_out[b] = lens[b];
     }
     return 0;
+}
+
+// ------------------------------------------------------------------ continuous batching
+// CPU restatement of the serving entry (gsv_engine::ar_generate_batch behind svc::ArBatcher,
+// tools/svc_core.h:1244-1340, generalised to refill as the library's gsvcu_serve_* do): a fixed set
+// of slots; admitted sequences prefill at once; one iteration samples one token for every slot in
+// flight, applies the stop rules of src/gsv_ar.cpp:764-815 per sequence (EOS, early stop on the
+// sequence's own count, max_steps), then runs one batched decode step over the slots still in
+// flight. Each sequence therefore produces exactly the tokens of orc_generate on that sequence
+// alone. Also the timed CPU arm of the serving benchmark.
+struct orc_server {
+    orc_model* m = nullptr;
+    bool kv_f16 = false;
+    int max_ctx = 0;
+    struct Slot {
+        bool used = false, active = false;
+        SeqCache cache;
+        std::vector<int32_t> y;
+        std::vector<float> logits;
+        int P = 0, idx = 0, max_steps = 0, early_stop = -1, tag = 0, kind = -1, n_gen = 0;
+        uint64_t rng = 1;
+        SamplerCfg sc;
+    };
+    std::vector<Slot> s;
+    int64_t tokens_done = 0;
+    double prefill_s = 0.0, decode_s = 0.0;
+    int64_t decode_rows = 0;
+};
+
+orc_server* orc_serve_new(orc_model* m, int slots, int max_ctx, int kv_f16) {
+    if (!m || slots <= 0 || max_ctx <= 0) return nullptr;
+    orc_server* v = new orc_server();
+    v->m = m;
+    v->kv_f16 = kv_f16 != 0;
+    v->max_ctx = max_ctx;
+    v->s.resize(slots);
+    for (auto& sl : v->s) {
+        init_cache(*m, sl.cache, max_ctx);
+        sl.logits.assign(m->V, 0.0f);
+    }
+    return v;
+}
+
+void orc_serve_free(orc_server* v) { delete v; }
+
+// Admit n sequences (packed as for orc_generate) into free slots, lowest index first; returns 0, or
+// -1 with the model's error (no free slot, context too long, bad ids).
+int orc_serve_admit(orc_server* v, int n, const int32_t* phones, const int32_t* n_phones, const float* bert,
+                    const int32_t* prompts, const int32_t* n_prompt, const uint64_t* seeds, const int32_t* tags,
+                    int max_steps, int early_stop, int top_k, float top_p, float temperature, float rep) {
+    orc_model* m = v->m;
+    std::vector<Req> reqs = make_reqs(*m, n, phones, n_phones, bert, prompts, n_prompt);
+    if (!check_reqs(m, reqs)) return -1;
+    int free_slots = 0;
+    for (auto& sl : v->s) free_slots += !sl.used;
+    if (free_slots < n) { m->err = "no free sequence slot"; return -1; }
+    for (const Req& r : reqs)
+        if (max_steps < 1 || r.T + r.P + max_steps + 1 > v->max_ctx) { m->err = "sequence longer than the context"; return -1; }
+    using clk = std::chrono::steady_clock;
+    const auto t0 = clk::now();
+    int next = 0;
+    for (int i = 0; i < n; i++) {
+        while (v->s[next].used) next++;
+        orc_server::Slot& sl = v->s[next++];
+        const Req& r = reqs[i];
+        sl.used = sl.active = true;
+        sl.P = r.P;
+        sl.idx = 0;
+        sl.max_steps = max_steps;
+        sl.early_stop = early_stop;
+        sl.tag = tags ? tags[i] : i;
+        sl.kind = -1;
+        sl.n_gen = 0;
+        const uint64_t seed = seeds ? seeds[i] : (uint64_t)i;
+        sl.rng = seed ? seed : 1;   // gsv_rng(seed) (src/gsv_sampler.h:35)
+        sl.sc.top_k = top_k; sl.sc.top_p = top_p; sl.sc.temperature = temperature; sl.sc.rep = rep;
+        sl.y.assign(r.prompt, r.prompt + r.P);
+        prefill_one(*m, r, v->kv_f16, sl.cache, sl.logits.data(), nullptr);
+    }
+    v->prefill_s += std::chrono::duration<double>(clk::now() - t0).count();
+    return 0;
+}
+
+// Run n_steps iterations, then report the finished sequences: done [max_done][5] = {slot, tag,
+// finish_kind (0 EOS, 1 early stop, 2 max_steps), generated count (gsv_ar_result::lens value), tokens
+// copied}, their generated tokens (prompt excluded, stopping token excluded) concatenated into tokens
+// (capacity tok_cap, may be NULL). Finished slots are freed. Returns the number of records.
+int orc_serve_step(orc_server* v, int n_steps, int32_t* done, int max_done, int32_t* tokens, int tok_cap) {
+    orc_model* m = v->m;
+    const int D = m->D, V = m->V;
+    std::vector<float> row(V), probs(V), x, lg2;
+    std::vector<int32_t> prev;
+    std::vector<SeqCache*> ptrs;
+    std::vector<int> which;
+    using clk = std::chrono::steady_clock;
+    for (int it = 0; it < n_steps; it++) {
+        for (auto& sl : v->s) {
+            if (!sl.active) continue;
+            Rng rng(sl.rng);
+            std::memcpy(row.data(), sl.logits.data(), (size_t)V * 4);
+            if (sl.idx < 11) row[m->EOS] = -INFINITY;
+            const int np = (int)std::min<size_t>(sl.y.size(), 4096);
+            prev.assign(sl.y.end() - np, sl.y.end());
+            logits_to_probs(sl.sc, row.data(), V, prev.data(), np, probs.data());
+            const int tok = sample(probs.data(), V, rng);
+            sl.rng = rng.s;
+            sl.y.push_back(tok);
+            const int n_samp = (int)sl.y.size() - sl.P;
+            if (tok == m->EOS) sl.kind = 0;
+            else if (sl.early_stop != -1 && n_samp > sl.early_stop) sl.kind = 1;
+            else if (n_samp >= sl.max_steps) sl.kind = 2;
+            if (sl.kind >= 0) {
+                sl.active = false;
+                sl.n_gen = sl.kind == 2 ? sl.max_steps : sl.idx;
+            }
+        }
+        ptrs.clear();
+        which.clear();
+        for (int i = 0; i < (int)v->s.size(); i++)
+            if (v->s[i].active) {
+                ptrs.push_back(&v->s[i].cache);
+                which.push_back(i);
+            }
+        if (which.empty()) break;
+        x.assign(which.size() * D, 0.0f);
+        for (size_t j = 0; j < which.size(); j++) {
+            const orc_server::Slot& sl = v->s[which[j]];
+            const int pos = sl.P + sl.idx;
+            const int tok = sl.y.back();
+            for (int d = 0; d < D; d++)
+                x[j * D + d] = std::fmaf(m->audio_alpha, m->pe[(size_t)pos * D + d], m->audio_emb[(size_t)tok * D + d]);
+        }
+        lg2.resize(which.size() * V);
+        const auto t0 = clk::now();
+        decode_step(*m, ptrs, x.data(), v->kv_f16, lg2.data(), nullptr);
+        v->decode_s += std::chrono::duration<double>(clk::now() - t0).count();
+        v->decode_rows += (int64_t)which.size();
+        for (size_t j = 0; j < which.size(); j++) {
+            orc_server::Slot& sl = v->s[which[j]];
+            std::memcpy(sl.logits.data(), lg2.data() + j * V, (size_t)V * 4);
+            sl.idx++;
+        }
+    }
+    int nd = 0, used = 0;
+    for (int i = 0; i < (int)v->s.size() && nd < max_done; i++) {
+        orc_server::Slot& sl = v->s[i];
+        if (!sl.used || sl.active) continue;
+        const int keep = (int)sl.y.size() - sl.P - (sl.kind == 2 ? 0 : 1);
+        int32_t* rec = done + (size_t)nd * 5;
+        rec[0] = i;
+        rec[1] = sl.tag;
+        rec[2] = sl.kind;
+        rec[3] = sl.n_gen;
+        rec[4] = 0;
+        if (tokens && keep > 0 && used + keep <= tok_cap) {
+            std::memcpy(tokens + used, sl.y.data() + sl.P, (size_t)keep * 4);
+            rec[4] = keep;
+            used += keep;
+        }
+        v->tokens_done += keep;
+        sl.used = false;
+        nd++;
+    }
+    return nd;
+}
+
+// Generated tokens so far: finished sequences plus those sampled by the sequences in flight.
+int64_t orc_serve_tokens_total(const orc_server* v) {
+    int64_t t = v->tokens_done;
+    for (const auto& sl : v->s)
+        if (sl.used) t += (int64_t)sl.y.size() - sl.P;
+    return t;
+}
+
+// Drop every sequence in flight (nothing reported).
+void orc_serve_reset(orc_server* v) {
+    for (auto& sl : v->s) sl.used = sl.active = false;
+}
+
+int orc_serve_active(const orc_server* v) {
+    int n = 0;
+    for (const auto& sl : v->s) n += sl.used;
+    return n;
+}
+
+// Seconds spent in prefills and in batched decode steps, and decoded rows, since orc_serve_new.
+void orc_serve_seconds(const orc_server* v, double* prefill_s, double* decode_s, int64_t* decode_rows) {
+    *prefill_s = v->prefill_s;
+    *decode_s = v->decode_s;
+    *decode_rows = v->decode_rows;
 }
 
 

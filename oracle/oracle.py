@@ -78,6 +78,21 @@ def _load():
     lib.orc_generate.restype = C.c_int
     lib.orc_last_generate_seconds.argtypes = [C.POINTER(C.c_double), C.POINTER(C.c_double), C.POINTER(C.c_int)]
     lib.orc_last_generate_seconds.restype = None
+    lib.orc_serve_new.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int]
+    lib.orc_serve_new.restype = C.c_void_p
+    lib.orc_serve_free.argtypes = [C.c_void_p]
+    lib.orc_serve_admit.argtypes = [C.c_void_p, C.c_int, _i32p, _i32p, _f32p, _i32p, _i32p, C.c_void_p, C.c_void_p,
+                                    C.c_int, C.c_int, C.c_int, C.c_float, C.c_float, C.c_float]
+    lib.orc_serve_admit.restype = C.c_int
+    lib.orc_serve_step.argtypes = [C.c_void_p, C.c_int, _i32p, C.c_int, C.c_void_p, C.c_int]
+    lib.orc_serve_step.restype = C.c_int
+    lib.orc_serve_tokens_total.argtypes = [C.c_void_p]
+    lib.orc_serve_tokens_total.restype = C.c_int64
+    lib.orc_serve_reset.argtypes = [C.c_void_p]
+    lib.orc_serve_active.argtypes = [C.c_void_p]
+    lib.orc_serve_active.restype = C.c_int
+    lib.orc_serve_seconds.argtypes = [C.c_void_p, C.POINTER(C.c_double), C.POINTER(C.c_double), C.POINTER(C.c_int64)]
+    lib.orc_serve_seconds.restype = None
     return lib
 
 
@@ -358,6 +373,66 @@ class OracleModel:
         if with_first_logits:
             return out, lens.tolist(), fl
         return out, lens.tolist()
+
+
+class OracleServer:
+    """CPU restatement of the continuous-batching entry (gsvcu_serve_*; the role of svc::ArBatcher,
+    reference tools/svc_core.h:1244-1340): `slots` sequence slots over one OracleModel; every admitted
+    sequence decodes exactly as OracleModel.generate of that sequence alone."""
+
+    def __init__(self, model: "OracleModel", slots: int, max_ctx: int, kv_f16: bool = False):
+        self.model = model
+        self.slots = slots
+        self._s = lib().orc_serve_new(model._m, slots, max_ctx, int(kv_f16))
+        if not self._s:
+            raise ValueError("orc_serve_new failed")
+
+    def close(self):
+        if getattr(self, "_s", None) and _LIB is not None:
+            _LIB.orc_serve_free(self._s)
+            self._s = None
+
+    __del__ = close
+
+    def admit(self, reqs, seeds, tags=None, max_steps=1500, early_stop=-1, top_k=15, top_p=1.0, temperature=1.0,
+              rep=1.35):
+        ph, nph, bert, pr, npr = pack_requests(reqs, self.model.BERT)
+        sd = np.ascontiguousarray(seeds, np.uint64)
+        tg = np.ascontiguousarray(tags if tags is not None else range(len(reqs)), np.int32)
+        if lib().orc_serve_admit(self._s, len(reqs), ph, nph, bert, pr, npr, sd.ctypes.data, tg.ctypes.data,
+                                 max_steps, early_stop, top_k, top_p, temperature, rep):
+            raise self.model._err()
+
+    def step(self, n_steps, max_done=None, tok_cap=0):
+        """Run n_steps iterations; returns the finished sequences as dicts (slot, tag, finish_kind,
+        n_generated, tokens)."""
+        max_done = self.slots if max_done is None else max_done
+        done = np.zeros((max(max_done, 1), 5), np.int32)
+        toks = np.zeros(max(tok_cap, 1), np.int32) if tok_cap else None
+        nd = lib().orc_serve_step(self._s, n_steps, done, max_done, toks.ctypes.data if toks is not None else None,
+                                  tok_cap)
+        out, at = [], 0
+        for i in range(nd):
+            k = int(done[i, 4])
+            out.append(dict(slot=int(done[i, 0]), tag=int(done[i, 1]), finish_kind=int(done[i, 2]),
+                            n_generated=int(done[i, 3]), tokens=toks[at:at + k].copy() if toks is not None else None))
+            at += k
+        return out
+
+    def tokens_total(self) -> int:
+        return int(lib().orc_serve_tokens_total(self._s))
+
+    def active(self) -> int:
+        return int(lib().orc_serve_active(self._s))
+
+    def reset(self):
+        lib().orc_serve_reset(self._s)
+
+    def seconds(self):
+        """(prefill seconds, decode seconds, decoded rows) since creation."""
+        p, d, n = C.c_double(), C.c_double(), C.c_int64()
+        lib().orc_serve_seconds(self._s, C.byref(p), C.byref(d), C.byref(n))
+        return p.value, d.value, n.value
 
 
 def last_generate_seconds():
