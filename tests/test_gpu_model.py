@@ -306,8 +306,8 @@ def test_cpp_ar_server_matches_generate(gctx, model_full, tmp_path):
     and empty BERT sides, each return exactly the tokens of gsv_ar::generate of that one sequence
     (prompt_phones ++ phones, prompt_bert ++ bert, prompt codes; as gsv_engine::ar_generate_batch)."""
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    exe = os.path.join(root, "gsv.cpp_b200", "lib", "gsv_ar_server_test")
-    assert os.path.exists(exe), "build with `make -C gsv.cpp_b200`"
+    exe = os.path.join(root, "tests", "cpp", "bin", "gsv_ar_server_test")
+    assert os.path.exists(exe), "build with `make -C tests/cpp`"
     rng = np.random.default_rng(91)
     cfgs = [(15, 1.0, 1.0, 1.35), (5, 0.8, 0.7, 1.1), (1, 1.0, 1.0, 1.0), (30, 0.95, 1.3, 1.35)]
     pp = rng.integers(0, 732, 11).astype(np.int32)            # one reference text for most tasks
@@ -356,8 +356,8 @@ def test_cpp_ar_server_matches_generate(gctx, model_full, tmp_path):
 def test_cpp_dropin_class(gctx, model_full, tmp_path):
     """The C++ `class gsv_ar` shim (csrc/gsv_ar.cpp) gives the C ABI's results."""
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    exe = os.path.join(root, "gsv.cpp_b200", "lib", "gsv_ar_smoke")
-    assert os.path.exists(exe), "build with `make -C gsv.cpp_b200`"
+    exe = os.path.join(root, "tests", "cpp", "bin", "gsv_ar_smoke")
+    assert os.path.exists(exe), "build with `make -C tests/cpp`"
     rng = np.random.default_rng(77)
     reqs = [S.make_request(rng, 33, 12), S.make_request(rng, 21, 12)]
     f = tmp_path / "reqs.bin"
