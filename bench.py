@@ -46,8 +46,10 @@ def parse():
                          "preset: F16 matrices, predict and embeddings), f32 (no flags) or q6_k (--spec "
                          "attn=q8_0,ffn=q6_k,predict=f16,emb=f16)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-sample-seqs", type=int, default=16,
-                    help="sequences of the bounded CPU sample the baseline / reference arm extrapolates from")
+    ap.add_argument("--cpu-sample-chunks", type=int, default=3,
+                    help="chunks (of --refill-every iterations) of the job the cpu_baseline sample runs")
+    ap.add_argument("--kv-f32-steps", type=int, default=3,
+                    help="jobs of the extra F32-KV (reference-exact) measurement; 0 skips it")
     ap.add_argument("--lookahead", action="store_true",
                     help="serve with gsvcu_set_serve_lookahead (the next chunk runs while the host handles results)")
     ap.add_argument("--workload", default="serve", choices=["serve", "attn", "gemv", "prefill", "single"],
@@ -339,10 +341,13 @@ def reduce_over_ranks(ms, tokens, seqs, world, device):
     return float(t[0]), float(t[1]), float(t[2])
 
 
-def run_job(ctx, queue, args, counters):
-    """One serving job: returns generated tokens."""
-    ctx.serve_reset()
-    t0 = ctx.serve_tokens_total()
+def job_chunks(srv, queue, args, counters):
+    """One serving job as a generator: admits the first `slots` requests, then runs chunks of
+    `refill_every` decode iterations, refilling finished slots from the queue after each chunk, for
+    `iters` iterations; yields after each chunk. `srv` is the library context (gsvcu.Context) or the
+    CPU arm's OracleServing, which expose the same serve_* calls."""
+    srv.serve_reset()
+    t0 = srv.serve_tokens_total()
     at = 0
 
     def admit(k):
@@ -352,7 +357,7 @@ def run_job(ctx, queue, args, counters):
         items = queue[at:at + k]
         at += k
         reqs = [r for r, _ in items]
-        ctx.serve_admit(reqs, [s for _, s in items], list(range(at - k, at)), max_steps=args.iters)
+        srv.serve_admit(reqs, [s for _, s in items], list(range(at - k, at)), max_steps=args.iters)
         for r in reqs:
             T, P = len(r.phones), len(r.prompt)
             counters["h2d"] += 4 * T + 4 * P + (0 if hasattr(r.bert, "data_ptr") else 4 * 1024 * T)
@@ -360,26 +365,60 @@ def run_job(ctx, queue, args, counters):
 
     admit(args.slots)
     lookahead = args.lookahead
-    ctx.set_serve_lookahead(lookahead)
+    srv.set_serve_lookahead(lookahead)
     it = 0
     if lookahead:   # the first call only starts a chunk; each later call reports the previous one
         it = min(args.refill_every, args.iters)
-        ctx.serve_step(it, max_done=args.slots, tok_cap=args.slots * args.iters)
+        srv.serve_step(it, max_done=args.slots, tok_cap=args.slots * args.iters)
     while True:
         n = min(args.refill_every, args.iters - it)
         if not lookahead and n == 0:
             break
-        done = ctx.serve_step(n, max_done=args.slots, tok_cap=args.slots * args.iters)
-        counters["d2h"] += 64 * ctx.lib.gsvcu_serve_active(ctx.h) + sum(4 * len(d["tokens"]) for d in done)
+        done = srv.serve_step(n, max_done=args.slots, tok_cap=args.slots * args.iters)
+        counters["d2h"] += 64 * srv.serve_active() + sum(4 * len(d["tokens"]) for d in done)
         if lookahead and n == 0:
             break
         it += n
         if done and it < args.iters:
             admit(len(done))
-    tokens = ctx.serve_tokens_total() - t0
-    ctx.serve_reset()
-    ctx.set_serve_lookahead(False)
-    return tokens
+        yield it
+    counters["tokens"] = srv.serve_tokens_total() - t0
+    srv.serve_reset()
+    srv.set_serve_lookahead(False)
+
+
+def run_job(ctx, queue, args, counters):
+    """One serving job: returns generated tokens."""
+    for _ in job_chunks(ctx, queue, args, counters):
+        pass
+    return counters["tokens"]
+
+
+class OracleServing:
+    """The serve_* calls of gsvcu.Context on the CPU oracle's serving loop (oracle.OracleServer), so the
+    CPU arm runs the job loop of job_chunks unchanged."""
+
+    def __init__(self, orc, slots, max_ctx, kv_f16=False):
+        import oracle as O
+        self.srv = O.OracleServer(orc, slots, max_ctx, kv_f16=kv_f16)
+
+    def serve_reset(self):
+        self.srv.reset()
+
+    def serve_tokens_total(self):
+        return self.srv.tokens_total()
+
+    def serve_admit(self, reqs, seeds, tags, max_steps):
+        self.srv.admit(reqs, seeds, tags, max_steps=max_steps)
+
+    def serve_step(self, n, max_done, tok_cap):
+        return self.srv.step(n, max_done=max_done, tok_cap=tok_cap)
+
+    def serve_active(self):
+        return self.srv.active()
+
+    def set_serve_lookahead(self, on):
+        pass
 
 
 def sample_clocks(local_rank):
@@ -435,34 +474,102 @@ def traffic_per_key():
     return None
 
 
-def cpu_baseline(args, job_tokens, job_seqs):
-    """The oracle (CPU restatement of the reference's ggml CPU path) on a bounded sample of the job:
-    n = --cpu-sample-seqs (16) config-4 sequences generated for 1 + 24 steps at B=n. The oracle times its
-    prefills and its batched decode steps separately, so per-sequence prefill = prefill time / n and
-    per-token decode = decode time / (n x decode steps); the job's time is extrapolated from these
-    measured costs for the job's sequence and token counts."""
+def _oracle_setup(args):
     import gsv_synth as S
     import oracle as O
-    model = S.cached_model(MODEL_CACHE, seed=0, n_layer=24)
+    fmt_kw = FORMATS[args.format][0]
+    model = S.cached_model(MODEL_CACHE, seed=0, n_layer=24, **fmt_kw)
     cores = os.cpu_count() or 1
     O.set_threads(cores)
     orc = O.OracleModel(model)
-    stream = RequestStream(99, 0)
-    n = max(1, getattr(args, "cpu_sample_seqs", 16))
-    reqs = [stream.next()[0] for _ in range(n)]
-    seeds = list(range(n))
-    orc.generate(reqs[:2], seeds=seeds[:2], max_steps=2)   # warm caches / thread pool
-    steps = 24
-    orc.generate(reqs, seeds=seeds, max_steps=1 + steps)
-    t_pre, t_dec, n_dec = O.last_generate_seconds()
-    per_seq_prefill = t_pre / len(reqs)
-    per_token_decode = t_dec / (len(reqs) * max(n_dec, 1))
-    est = job_seqs * per_seq_prefill + job_tokens * per_token_decode
-    return {"value": job_tokens / est, "unit": "tokens/s", "cores": cores, "kind": "port",
-            "job_ms": est * 1e3,
-            "sample": f"{n} config-4 sequences at B={n} on {cores} threads: prefill {t_pre:.2f} s, {n_dec} batched "
-                      f"decode steps {t_dec:.2f} s; job time extrapolated for {job_seqs} prefills + {job_tokens} "
-                      f"tokens"}
+    return orc, cores
+
+
+def cpu_baseline(args):
+    """The oracle (CPU restatement of the reference's ggml CPU path, F32 KV as the reference caches) on a
+    bounded sample of the same workload: the first --cpu-sample-chunks chunks of job 2000 of rank 0 (the
+    GPU arm's first timed job), initial 64-sequence admission and the refills included, timed on the host
+    clock. Early iterations have the shortest contexts, so this sample is optimistic for the CPU; the
+    reference arm (--impl reference) times the whole job."""
+    orc, cores = _oracle_setup(args)
+    srv = OracleServing(orc, args.slots, 400 + args.iters + 8)
+    queue = stage(RequestStream(0, 2000), args.slots * 5, None)
+    counters = {"h2d": 0, "d2h": 0, "seqs": 0}
+    n_chunks = max(1, args.cpu_sample_chunks)
+    t0 = time.perf_counter()
+    gen = job_chunks(srv, queue, args, counters)
+    it = 0
+    for _ in range(n_chunks):
+        it = next(gen)
+    sec = time.perf_counter() - t0
+    tokens = srv.serve_tokens_total()
+    srv.serve_reset()
+    return {"value": tokens / sec, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"config-4 job 2000 of rank 0 (64 slots) on the oracle, {cores} threads, F32 KV: admission of "
+                      f"{counters['seqs']} sequences and iterations 0-{it} ({tokens} tokens) in {sec:.1f} s; "
+                      f"contexts of these early iterations are short (<= {400 + it} keys)"}
+
+
+def reference_arm(args, n_gpus):
+    """--impl reference: the reference's CPU path (the oracle port of the ggml CPU backend; ggml itself is
+    not buildable offline) runs one whole config-4 job -- rank 0's job 2000, the GPU arm's first timed job:
+    64 slots, 1500 iterations, refills every 16, F32 KV as the reference caches -- on all host threads. The
+    job's chunks are split into the K timed steps (step k = its share of the chunks, host clock), so the
+    timed region is exactly one job and value = its tokens / its time."""
+    orc, cores = _oracle_setup(args)
+    srv = OracleServing(orc, args.slots, 400 + args.iters + 8)
+    counters = {"h2d": 0, "d2h": 0, "seqs": 0}
+    # warm-up (untimed): W decode iterations of a 4-slot batch from another stream
+    wq = stage(RequestStream(0, 999), 8, None)
+    wa = argparse.Namespace(**{**vars(args), "slots": 4, "iters": max(args.warmup, 1), "refill_every": 1})
+    for _ in job_chunks(srv, wq, wa, dict(counters)):
+        pass
+    queue = stage(RequestStream(0, 2000), args.slots * 5, None)
+    n_chunks = -(-args.iters // args.refill_every)
+    K = max(1, min(args.steps, n_chunks))
+    bounds = [round(k * n_chunks / K) for k in range(K + 1)]
+    gen = job_chunks(srv, queue, args, counters)
+    step_s = []
+    done = 0
+    t_start = time.perf_counter()
+    for k in range(K):
+        t0 = time.perf_counter()
+        for _ in range(bounds[k + 1] - bounds[k]):
+            next(gen)
+            done += 1
+        step_s.append(time.perf_counter() - t0)
+    tokens = srv.serve_tokens_total()
+    for _ in gen:   # nothing left: closes the job (counts, reset)
+        pass
+    total = time.perf_counter() - t_start
+    value = tokens / sum(step_s)
+    return {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": n_gpus, "steps": K,
+        "warmup": args.warmup, "ms_per_step": 1e3 * sum(step_s) / K, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "q8_0 int8 dot / f32 softmax / f32 KV", "data": DATA,
+        "config": serve_config(args, n_gpus),
+        "kv_cache": "f32 per sequence (the reference's cache type, src/gsv_ar.cpp:107-108)",
+        "job": {"tokens": tokens, "sequences": counters["seqs"], "iterations": args.iters, "chunks": done,
+                "seconds": total},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"one whole config-4 job (rank 0, job 2000: {counters['seqs']} sequences, "
+                                   f"{args.iters} iterations, {tokens} tokens) on the oracle port of the ggml CPU "
+                                   f"path, {cores} threads, F32 KV; the K steps are consecutive shares of its "
+                                   f"{n_chunks} chunks"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+DATA = "synthetic (seeded GGUF weights N(0,0.02), requests U[80,400])"
+
+
+def serve_config(args, n_gpus):
+    """The config key both arms print for the serve workload."""
+    return {"workload": "cfg4: box-wide serving shard per GPU (BASELINE configs[4])",
+            "model": f"gsv AR 24 x 512, 16 heads x 32, FFN 2048, vocab 1025, {FORMATS[args.format][2]}",
+            "slots_per_gpu": args.slots, "iters_per_job": args.iters, "refill_every": args.refill_every,
+            "sampler": "top_k 15, top_p 1.0, temperature 1.0, rep 1.35, EOS 1024",
+            "parallelism": f"dp{n_gpus} (replicas, batch-sharded)",
+            "l2": "no flush; KV working set per step (>1 GB) exceeds the 126 MB L2"}
 
 
 # serve-workload model formats: cached_model arguments and the weight bytes one decode step reads
@@ -492,15 +599,7 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        cb = cpu_baseline(args, job_tokens=args.slots * args.iters, job_seqs=args.slots)
-        print(json.dumps({
-            "impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tokens/s", "n_gpus": n_gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": cb["job_ms"], "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "q8_0 int8 dot / f32", "data": "synthetic",
-            "config": {"workload": "cfg4 shard extrapolated from a bounded CPU sample",
-                       "slots_per_gpu": args.slots, "iters": args.iters},
-            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
-            "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+        print(json.dumps(reference_arm(args, n_gpus)))
         return
 
     import torch
@@ -583,6 +682,22 @@ def main():
     tpk = traffic_per_key()
     keys_launch = bytes_launch / (2 * 512 * (2 if args.kv == "f16" else 4))
 
+    # the reference-exact configuration: the same jobs with an F32 KV cache (the reference caches F32,
+    # src/gsv_ar.cpp:107-108; with it every token equals the oracle's). Every rank takes these steps.
+    kv32 = None
+    if args.kv == "f16" and args.kv_f32_steps > 0:
+        ctx.kv_reserve(args.slots, max_ctx, gsvcu.KV_F32)
+        run_job(ctx, stage(RequestStream(rank, 1000), queue_len, None), args, counters)   # warm-up
+        steps_saved = args.steps
+        args.steps = args.kv_f32_steps
+        ms_32, tok_32, seqs_32, _, _ = timed(True, 2000)
+        args.steps = steps_saved
+        kv32 = {"value": tok_32 / (ms_32 * 1e-3), "unit": "tokens/s", "steps": args.kv_f32_steps,
+                "ms_per_step": ms_32 / args.kv_f32_steps, "kv_cache": "paged f32, 64-token pages",
+                "jobs": "the first jobs of the timed set above, device-resident inputs",
+                "parity": "tokens identical to the oracle with the reference's F32 cache (the F16 cache rounds "
+                          "K/V and diverges from it after a few to ~100 greedy steps)"}
+
     value = tok_v / (ms_v * 1e-3)
     e2e = tok_e / (ms_e * 1e-3)
     if rank != 0:
@@ -596,15 +711,11 @@ def main():
         "dtype": ("q8_0 int8 MMA" if args.format == "q8_0" else
                   "q8_0 int8 MMA + q6_k dp2a" if args.format == "q6_k" else f"{args.format} weights / f32 FMA") +
                  f" / f32 softmax / {args.kv} KV",
-        "data": "synthetic (seeded GGUF weights N(0,0.02), requests U[80,400])",
-        "config": {"workload": "cfg4: box-wide serving shard per GPU (BASELINE configs[4])",
-                   "model": f"gsv AR 24 x 512, 16 heads x 32, FFN 2048, vocab 1025, {fmt_desc}",
-                   "slots_per_gpu": args.slots, "iters_per_job": args.iters, "refill_every": args.refill_every,
-                   "sampler": "top_k 15, top_p 1.0, temperature 1.0, rep 1.35, EOS 1024",
-                   "kv_cache": f"paged {args.kv}, 64-token pages", "parallelism": f"dp{n_gpus} (replicas, batch-sharded)",
-                   "serve_lookahead": args.lookahead,
-                   "l2": "no flush; KV working set per step (>1 GB) exceeds the 126 MB L2",
-                   "tokens_per_step": tok_v / args.steps, "sequences_per_step": seqs_v / args.steps},
+        "data": DATA,
+        "config": serve_config(args, n_gpus),
+        "kv_cache": f"paged {args.kv}, 64-token pages",
+        "serve_lookahead": args.lookahead,
+        "job": {"tokens_per_step": tok_v / args.steps, "sequences_per_step": seqs_v / args.steps},
         "gpu_launches": launches_v,
         "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": cnt_e["h2d"] // args.steps,
                 "d2h_bytes_per_step": cnt_e["d2h"] // args.steps},
@@ -621,9 +732,10 @@ def main():
         "step_profile_ms": {k: round(v / prof_steps, 4) for k, v in ms_cls.items()},
         "clocks": clocks,
     }
+    if kv32:
+        line["kv_f32"] = kv32
     if n_gpus == 1 and not args.no_cpu_baseline:
-        cb = cpu_baseline(args, job_tokens=int(tok_v / args.steps), job_seqs=int(seqs_v / args.steps))
-        line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        line["cpu_baseline"] = cpu_baseline(args)
     print(json.dumps(line))
     if world > 1:
         dist.destroy_process_group()

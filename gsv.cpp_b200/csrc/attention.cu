@@ -60,14 +60,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait for phase 0 of an mbarrier; warp-uniform result (false: the limit was reached).
+// Bounded wait for phase 0 of an mbarrier; warp-uniform result (false: `limit` polls went by).
 constexpr uint32_t MBAR_POLL_LIMIT = 1u << 22;
-__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar) {
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t limit) {
     uint32_t it = 0;
     while (!mbar_try_wait(bar, 0)) {
-        if (++it == MBAR_POLL_LIMIT) break;
+        if (++it == limit) break;
     }
-    return __all_sync(0xffffffffu, it < MBAR_POLL_LIMIT);
+    return __all_sync(0xffffffffu, it < limit);
 }
 
 // 8 consecutive values of a K/V row slice from shared memory, as floats.
@@ -245,7 +245,7 @@ __global__ void __launch_bounds__(128) k_decode_attn(const DecAttnParams p) {
         const KT* kp = (const KT*)p.pool + (size_t)page * p.n_layer * 2 * NH * PAGE * HD +
                        ((size_t)p.layer * 2 * NH + h) * PAGE * HD;
         const uint32_t bytes = (uint32_t)n * S::ROWB;
-        mbar_expect_tx(bar, 2 * bytes);
+        mbar_expect_tx(bar, 2 * bytes + p.fault_extra_tx);   // fault_extra_tx: 0 except under a test's fault
         bulk_g2s(smem_u32(ks), kp, bytes, bar);
         bulk_g2s(smem_u32(vs), kp + (size_t)NH * PAGE * HD, bytes, bar);
     };
@@ -267,9 +267,10 @@ __global__ void __launch_bounds__(128) k_decode_attn(const DecAttnParams p) {
         q[4] = b.x; q[5] = b.y; q[6] = b.z; q[7] = b.w;
     }
     __syncwarp();
-    if (!mbar_wait_bounded(bar)) {   // the page never arrived: flag it, drain (bounded), poison
+    const uint32_t limit = p.poll_limit ? p.poll_limit : MBAR_POLL_LIMIT;
+    if (!mbar_wait_bounded(bar, limit)) {   // the page never arrived: flag it, wait (bounded) for the copies
         if (lane == 0 && p.err) atomicExch(p.err, 1);
-        (void)mbar_wait_bounded(bar);
+        (void)mbar_wait_bounded(bar, limit);
     }
 
     float m, l, o[8];
@@ -300,7 +301,7 @@ __global__ void __launch_bounds__(128) k_decode_merge(const DecAttnParams p) {
     const int slot = p.slot0 + item / NH, h = item % NH;
     int kvpos;
     if (!decode_slot(p, slot, kvpos)) return;
-    const int nch = (kvpos + PAGE) / PAGE;
+    const int nch = min((kvpos + PAGE) / PAGE, p.max_chunks);   // the page grid covers max_chunks pages
     if (nch <= 1) return;
     const int sub = lane & 3, g = lane >> 2;
     const size_t item0 = ((size_t)slot * NH + h) * p.max_chunks;

@@ -408,8 +408,11 @@ struct gsvcu_ctx {
     // op-entry scratch
     float* op_part = nullptr;
     size_t op_part_n = 0;
-    // set by decode attention when a bounded wait for its staged K/V gave up (checked on status reads)
+    // set by decode attention when a bounded wait for its staged K/V gave up: [0] by the decode steps
+    // (read and cleared with the slot state), [1] by gsvcu_op_decode_attention (read and cleared by gsvcu_sync)
     int32_t* att_err = nullptr;
+    // test-only fault injection (gsvcu_set_wait_fault): extra bytes each K/V page wait expects, poll limit
+    uint32_t fault_extra_tx = 0, fault_poll_limit = 0;
     // decode steps run the fused layer tail (dense.cu) when the device can hold its cluster
     bool dense_ok = false, fused = true;
     bool two_groups = false;   // fused step: split the slots into two groups on forked streams (mode 2)
@@ -1114,6 +1117,7 @@ int gsvcu_ctx::launch_step(cudaStream_t s, float* dump, int dump_row, const int*
                 a.max_chunks = max_chunks; a.scale = scale; a.out_q = aq; a.out_d = ad; a.part = part;
                 a.part_ml = part_ml_of(part, (size_t)max_slots * NH * max_chunks);
                 a.partials_only = 1; a.err = att_err;
+                a.fault_extra_tx = fault_extra_tx; a.poll_limit = fault_poll_limit;
                 a.work = work; a.work_base = work_base; a.group = s0 ? 1 : 0;
                 nk += launch_decode_attention(a, cs);
                 TRY(mark(GSVCU_PROF_DECODE_ATTN));
@@ -1171,6 +1175,7 @@ int gsvcu_ctx::launch_step(cudaStream_t s, float* dump, int dump_row, const int*
         a.block_table = block_table; a.max_pages = max_pages; a.st = st; a.B = M; a.max_chunks = max_chunks;
         a.scale = scale; a.out_q = aq; a.out_d = ad; a.out_f32 = dump || w.mt[1] != 8 ? attn_f32 : nullptr;
         a.part = part; a.part_ml = part_ml_of(part, (size_t)max_slots * NH * max_chunks); a.err = att_err;
+        a.fault_extra_tx = fault_extra_tx; a.poll_limit = fault_poll_limit;
         nk += launch_decode_attention(a, s);
         TRY(mark(3));
         layer_gemm(li, 1, io, M, KvWrite(), s);
@@ -1241,7 +1246,11 @@ int gsvcu_ctx::read_status() {
     CK(cudaMemcpyAsync(h_st.data(), st, sizeof(SlotState) * max_slots, cudaMemcpyDeviceToHost, stream));
     CK(cudaMemcpyAsync(&aerr, att_err, sizeof(aerr), cudaMemcpyDeviceToHost, stream));
     CK(cudaStreamSynchronize(stream));
-    if (aerr) return fail(GSVCU_ERR_CUDA, "decode attention: staged K/V never arrived (bounded wait gave up)");
+    if (aerr) {   // reported once: the word is cleared so the context stays usable
+        CK(cudaMemsetAsync(att_err, 0, sizeof(int32_t), stream));
+        CK(cudaStreamSynchronize(stream));
+        return fail(GSVCU_ERR_CUDA, "decode attention: staged K/V never arrived (bounded wait gave up)");
+    }
     return GSVCU_OK;
 }
 
@@ -1303,8 +1312,8 @@ int gsvcu_create(int device, gsvcu_ctx** out) {
     c->device = device;
     c->dense_ok = dense_usable;
     if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaMalloc((void**)&c->att_err, sizeof(int32_t)) != cudaSuccess ||
-        cudaMemset(c->att_err, 0, sizeof(int32_t)) != cudaSuccess ||
+        cudaMalloc((void**)&c->att_err, 2 * sizeof(int32_t)) != cudaSuccess ||
+        cudaMemset(c->att_err, 0, 2 * sizeof(int32_t)) != cudaSuccess ||
         cudaStreamCreateWithFlags(&c->gstream[0], cudaStreamNonBlocking) != cudaSuccess ||
         cudaStreamCreateWithFlags(&c->gstream[1], cudaStreamNonBlocking) != cudaSuccess ||
         cudaEventCreateWithFlags(&c->gevent[0], cudaEventDisableTiming) != cudaSuccess ||
@@ -1668,7 +1677,8 @@ int gsvcu_op_decode_attention(gsvcu_ctx* ctx, const float* q_dev, int32_t q_stri
     a.q = q_dev; a.q_stride = q_stride; a.pool = pool_dev; a.kv_f32 = kv_dtype; a.n_layer = n_layer; a.layer = layer;
     a.block_table = block_table_dev; a.max_pages = max_pages; a.kvpos = kvpos_dev; a.active = active_dev; a.B = B;
     a.max_chunks = max_chunks; a.scale = 1.0f / std::sqrt((float)HD); a.out_q = out_q_dev; a.out_d = out_d_dev;
-    a.out_f32 = out_f32_dev; a.part = ctx->op_part; a.err = ctx->att_err;
+    a.out_f32 = out_f32_dev; a.part = ctx->op_part; a.err = ctx->att_err + 1;
+    a.fault_extra_tx = ctx->fault_extra_tx; a.poll_limit = ctx->fault_poll_limit;
     a.part_ml = part_ml_of(ctx->op_part, (size_t)B * NH * max_chunks);
     launch_decode_attention(a, ctx->stream);
     CKC(ctx, cudaGetLastError());
@@ -1855,7 +1865,24 @@ int gsvcu_fused_decode(const gsvcu_ctx* ctx) {
 int gsvcu_sync(gsvcu_ctx* ctx) {
     if (!ctx) return GSVCU_ERR_ARG;
     DeviceGuard g(ctx->device);
+    int32_t oerr = 0;
+    CKC(ctx, cudaMemcpyAsync(&oerr, ctx->att_err + 1, sizeof(oerr), cudaMemcpyDeviceToHost, ctx->stream));
     CKC(ctx, cudaStreamSynchronize(ctx->stream));
+    if (oerr) {
+        CKC(ctx, cudaMemsetAsync(ctx->att_err + 1, 0, sizeof(int32_t), ctx->stream));
+        CKC(ctx, cudaStreamSynchronize(ctx->stream));
+        return ctx->fail(GSVCU_ERR_CUDA, "gsvcu_op_decode_attention: staged K/V never arrived (bounded wait gave up)");
+    }
+    return GSVCU_OK;
+}
+
+int gsvcu_set_wait_fault(gsvcu_ctx* ctx, int32_t on) {
+    if (!ctx || on < 0 || on > 1) return GSVCU_ERR_ARG;
+    DeviceGuard g(ctx->device);
+    CKC(ctx, cudaStreamSynchronize(ctx->stream));
+    ctx->drop_graphs();   // captured steps hold the launch parameters
+    ctx->fault_extra_tx = on ? 16u : 0u;
+    ctx->fault_poll_limit = on ? 4096u : 0u;
     return GSVCU_OK;
 }
 

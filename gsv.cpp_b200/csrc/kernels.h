@@ -143,6 +143,10 @@ struct DecAttnParams {
     const int32_t* work_base = nullptr;
     int group = 0;
     int32_t* err = nullptr;              // set to 1 if a bounded wait gave up (may be null)
+    // fault injection for the failure-path tests (gsvcu_set_wait_fault): bytes each page's mbarrier expects
+    // beyond what is staged (so the wait runs out), and the wait's poll limit (0: the default)
+    uint32_t fault_extra_tx = 0;
+    uint32_t poll_limit = 0;
 };
 // Split-KV work items of decode attention: one per 64-key page. Page partials of item
 // (slot * NH + head) * max_chunks + page: o, HD floats (a 128-byte row), in one array, and {m, l} in a

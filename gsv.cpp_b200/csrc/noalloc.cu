@@ -22,7 +22,7 @@ constexpr size_t kPartFloats = (size_t)kItems * NH * PART_STRIDE;    // partials
 // Scratch shared by every call on a device.
 struct NoallocScratch {
     float part[kPartFloats];
-    int32_t err;   // set by the kernel when a bounded wait for staged K/V gave up (outputs are NaN then)
+    int32_t err;   // set by the kernels when a bounded wait for staged K/V gave up; cleared by every call
 };
 static __device__ __align__(256) NoallocScratch g_scratch;
 
@@ -89,7 +89,18 @@ extern "C" int gsvcu_op_decode_attention_noalloc(void* stream, const float* q_de
     a.max_chunks = max_chunks; a.scale = 1.0f / sqrtf((float)HD); a.out_q = out_q_dev; a.out_d = out_d_dev;
     a.out_f32 = out_f32_dev; a.part = s->part; a.err = &s->err;
     a.part_ml = part_ml_of(s->part, (size_t)B * NH * max_chunks);
+    // the status word starts every call at zero; after the kernels it is read back (one 4-byte copy into
+    // this stack frame, then the stream is synchronised), so a wait that gave up fails this call
+    if (cudaMemsetAsync(&s->err, 0, sizeof(int32_t), st) != cudaSuccess) return GSVCU_ERR_CUDA;
     launch_decode_attention(a, st);
     if (cudaGetLastError() != cudaSuccess) return GSVCU_ERR_CUDA;
+    int32_t err = 0;
+    if (cudaMemcpyAsync(&err, &s->err, sizeof(err), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return GSVCU_ERR_CUDA;
+    if (err) {
+        std::fprintf(stderr, "gsvcu_op_decode_attention_noalloc: staged K/V never arrived (bounded wait gave up)\n");
+        return GSVCU_ERR_CUDA;
+    }
     return GSVCU_OK;
 }

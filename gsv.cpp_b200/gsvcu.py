@@ -88,6 +88,7 @@ SIGNATURES = {
     "gsvcu_set_fused_decode": ([_P, _I], C.c_int),
     "gsvcu_set_serve_lookahead": ([_P, _I], C.c_int),
     "gsvcu_fused_decode": ([_P], C.c_int),
+    "gsvcu_set_wait_fault": ([_P, _I], C.c_int),
 }
 
 PROF_CLASSES = ["sampler", "step_prep", "qkv_gemm", "decode_attn", "out_gemm", "layernorm", "ffn1_gemm", "ffn2_gemm",
@@ -288,6 +289,10 @@ class Context:
 
     def fused_decode(self):
         return int(self.lib.gsvcu_fused_decode(self.h))
+
+    def set_wait_fault(self, on):
+        """Test-only: make this context's decode-attention page waits run out (gsvcu_set_wait_fault)."""
+        self._check(self.lib.gsvcu_set_wait_fault(self.h, 1 if on else 0))
 
     def stream_handle(self):
         return int(self.lib.gsvcu_stream(self.h) or 0)

@@ -218,6 +218,10 @@ int gsvcu_op_decode_attention(gsvcu_ctx* ctx, const float* q_dev, int32_t q_stri
                               int32_t max_pages, const int32_t* kvpos_dev, const int32_t* active_dev, int32_t B,
                               int8_t* out_q_dev, uint16_t* out_d_dev, float* out_f32_dev);
 
+/* A page wait of this entry that gives up (bounded, see gsvcu_set_wait_fault) is reported by the next
+ * gsvcu_sync of the context as GSVCU_ERR_CUDA, once. kvpos at or beyond max_pages * 64 is clamped to the
+ * last page of the block table. */
+
 /* Decode attention that allocates nothing (no counterpart in the reference; added for callers of
  * this library that may not allocate device memory where they run attention -- e.g. code running
  * while a framework's caching allocator owns the device, a real-time callback that must not block
@@ -228,7 +232,9 @@ int gsvcu_op_decode_attention(gsvcu_ctx* ctx, const float* q_dev, int32_t q_stri
  * the process exits), sized for B * max_pages <= GSVCU_NOALLOC_MAX_ITEMS (one split-KV work item per
  * 64-key page); larger calls return GSVCU_ERR_ARG with a message on stderr. The first call on a device looks up the
  * array's device address (cudaGetSymbolAddress); make that first call before any stream capture.
- * All calls share the array: calls that overlap on the GPU (other streams, other threads) race. */
+ * All calls share the array: calls that overlap on the GPU (other streams, other threads) race.
+ * The call returns once its kernels have finished on `stream` (it reads back their status word): a
+ * bounded wait for staged K/V that gave up returns GSVCU_ERR_CUDA instead of GSVCU_OK. */
 #define GSVCU_NOALLOC_MAX_ITEMS 1024
 int gsvcu_op_decode_attention_noalloc(void* stream, const float* q_dev, int32_t q_stride, const void* pool_dev,
                                       int32_t kv_dtype, int32_t n_layer, int32_t layer,
@@ -284,8 +290,17 @@ int64_t gsvcu_kernel_launches(const gsvcu_ctx* ctx);
  * it with events. */
 void* gsvcu_stream(const gsvcu_ctx* ctx);
 
-/* Synchronise the context's stream. */
+/* Synchronise the context's stream. Also reports (GSVCU_ERR_CUDA, once) a bounded wait of
+ * gsvcu_op_decode_attention that gave up since the last call. */
 int gsvcu_sync(gsvcu_ctx* ctx);
+
+/* Failure-path testing (no counterpart in the reference, whose KV allocation failure exits the process,
+ * src/gsv_ar.cpp:111). on = 1: every decode-attention launch of this context declares 16 bytes more on
+ * its page mbarrier than it stages and gives up after 4096 polls, so its bounded wait runs out: the
+ * next status read of generate / serve (or gsvcu_sync after an op call) returns GSVCU_ERR_CUDA with
+ * "staged K/V never arrived", and the context stays usable. Nothing faults: the staged copies all
+ * complete, only the expected count is never reached. on = 0 (default) restores normal operation. */
+int gsvcu_set_wait_fault(gsvcu_ctx* ctx, int32_t on);
 
 #ifdef __cplusplus
 }

@@ -84,6 +84,25 @@ def test_layer_outputs_teacher_forced(gctx, orc, kv):
     for s in range(lg.shape[0]):
         for b in range(lg.shape[1]):
             assert cosine(lg[s, b], rlg[s, b]) >= COS
+    if kv == 0:
+        # The F16 cache against the reference's F32 cache (src/gsv_ar.cpp:107-108). Prefill does not read
+        # the cache, so step 0 is identical. In the decode steps the attention outputs stay within the
+        # 2e-3 bar (measured ~5e-4); the Q8_0 re-quantization of every activation then amplifies that
+        # difference to ~1.2e-2 in the later layer outputs -- above the north star's 2e-3 bar. Only the
+        # F32 cache (kv=1 above, bit-exact) meets the bar at every layer.
+        _, pdump32 = orc.first_logits(reqs, kv_f16=False, dump=True)
+        _, rdump32 = orc.decode_trace(reqs, forced, kv_f16=False, dump=True)
+        ref32 = np.concatenate([pdump32[None], rdump32], axis=0)
+        assert np.array_equal(dump[0].view(np.uint32), ref32[0].view(np.uint32))
+        worst32 = np.zeros(4)
+        for s in range(dump.shape[0]):
+            for b in range(dump.shape[1]):
+                for li in range(dump.shape[2]):
+                    for it in range(4):
+                        worst32[it] = max(worst32[it], rel_l2(dump[s, b, li, it], ref32[s, b, li, it]))
+        print("f16 cache vs f32 reference, worst rel-L2 [attention, LN1, pre-LN2, layer out]:", worst32)
+        assert worst32[0] <= REL_L2
+        assert worst32.max() <= 2e-2
 
 
 @pytest.mark.parametrize("kv", [1, 0])
@@ -101,13 +120,14 @@ def test_decode_logits_trace(gctx, orc, kv):
     assert cos >= COS and rl <= REL_L2
     if kv == 0:
         # The F16 cache against the reference's F32 cache: F16 rounding of stored K/V (~3e-4 relative)
-        # is amplified by the Q8_0 re-quantization of every activation; measured min cosine 0.99990,
-        # max rel-L2 1.4e-2 on this trace. Reference-exact results need GSVCU_KV_F32 (bit-exact above).
+        # is amplified by the Q8_0 re-quantization of every activation (measured max rel-L2 ~1.4e-2 on
+        # this trace, above the 2e-3 bar that only the bit-exact F32 cache meets); the logits cosine bar
+        # holds.
         rlg32 = orc.decode_trace(reqs, forced, kv_f16=False)
         cos32 = min(cosine(lg[s, b], rlg32[s, b]) for s, b in pairs)
         rl32 = max(rel_l2(lg[s, b], rlg32[s, b]) for s, b in pairs)
         print(f"f16 cache vs f32 reference: min cosine {cos32:.9f} max rel-L2 {rl32:.3e}")
-        assert cos32 >= 0.999 and rl32 <= 0.05
+        assert cos32 >= COS and rl32 <= 0.05
 
 
 def test_fused_and_unfused_decode_steps_agree(gctx, orc):
@@ -173,6 +193,38 @@ def test_greedy_streams_config1(gctx, orc, kv):
     print(f"kv={'f32' if kv else 'f16'} identical greedy streams: {same}/{len(reqs)}; "
           f"first divergences (seq, step): {report}")
     assert same / len(reqs) >= 0.95
+    if kv == 0:
+        _f16_streams_against_f32_reference(orc, reqs, got, steps)
+
+
+def _f16_streams_against_f32_reference(orc, reqs, got, steps):
+    """The F16 cache's greedy streams against the reference's F32 cache (src/gsv_ar.cpp:107-108).
+
+    Measured (B200 and oracle agree bit for bit on the F16 side): no stream stays identical for 200 steps;
+    first divergences fall between steps 1 and ~90. The north star's ">= 95 % identical over 200 steps"
+    is therefore met only by the F32 cache (kv=1, bit-exact). What this asserts instead: along each F16
+    stream (teacher-forced into both caches), the two caches' logits stay within cosine 0.9999 of each
+    other at every one of the 200 steps -- so a divergence is a flip between near-tied candidates, after
+    which the streams are unrelated."""
+    ref32, _ = orc.generate(reqs, top_k=1, seed_base=1000, max_steps=steps, kv_f16=False)
+    report = []
+    for b in range(len(reqs)):
+        P = len(reqs[b].prompt)
+        report.append(_first_divergence(got[b][P:], ref32[b][P:]))
+    same = sum(d is None for d in report)
+    print(f"f16 cache vs f32 reference: identical greedy streams {same}/{len(reqs)}; first divergence steps "
+          f"{report}")
+    # each stream's tokens (a stream that stopped early is padded with its last token; only its own
+    # steps are compared)
+    gen = [np.asarray(got[b][len(reqs[b].prompt):], np.int32) for b in range(len(reqs))]
+    forced = np.stack([np.concatenate([g, np.full(steps, g[-1] if len(g) else 0, np.int32)])[:steps - 1] for g in gen])
+    lg16 = orc.decode_trace(reqs, forced, kv_f16=True)
+    lg32 = orc.decode_trace(reqs, forced, kv_f16=False)
+    pairs = [(s, b) for b in range(len(reqs)) for s in range(min(len(gen[b]), steps - 1) + 1)]
+    cos = min(cosine(lg16[s, b], lg32[s, b]) for s, b in pairs)
+    rl = max(rel_l2(lg16[s, b], lg32[s, b]) for s, b in pairs)
+    print(f"f16 vs f32 cache along the f16 streams, {steps} steps: min logits cosine {cos:.7f}, max rel-L2 {rl:.3e}")
+    assert cos >= COS
 
 
 def test_sampled_generate_matches_oracle(gctx, orc):
@@ -216,16 +268,26 @@ def test_eos_finish_and_lens_order(gctx, orc):
         assert len(got[b]) == 10 + 14
 
 
-def test_serving_refill_equals_generate(gctx):
-    """Continuous batching: a sequence admitted into a refilled slot decodes exactly as alone."""
+def _alone(orc, gctx, reqs, seeds, steps, **cfg):
+    """Each sequence generated alone by the oracle (F16-cache emulation, as the serving slots below use);
+    the library's own generate gives the same tokens."""
+    out = []
+    for i in range(len(reqs)):
+        t, _ = orc.generate([reqs[i]], seeds=[seeds[i]], max_steps=steps[i], kv_f16=True, **cfg)
+        g, _ = gctx.generate([reqs[i]], seeds=[seeds[i]], max_steps=steps[i], **cfg)
+        assert np.array_equal(g[0], t[0]), i
+        out.append(t[0][len(reqs[i].prompt):])
+    return out
+
+
+def test_serving_refill_equals_generate(gctx, orc):
+    """Continuous batching: a sequence admitted into a refilled slot decodes exactly as the oracle
+    generates it alone."""
     reqs = S.ragged_requests(55, 6, lo=40, hi=120)
     seeds = [500 + i for i in range(6)]
     steps = [40, 40, 40, 40, 68, 75]
     _reserve(gctx, 0, slots=4, ctx=512)
-    alone = []
-    for i in range(6):
-        t, _ = gctx.generate([reqs[i]], seeds=[seeds[i]], max_steps=steps[i])
-        alone.append(t[0][len(reqs[i].prompt):])
+    alone = _alone(orc, gctx, reqs, seeds, steps)
     gctx.serve_admit(reqs[:4], seeds[:4], list(range(4)), max_steps=40)
     served, pending = {}, 4
     for _ in range(200):
@@ -241,17 +303,14 @@ def test_serving_refill_equals_generate(gctx):
         assert np.array_equal(served[i], alone[i]), i
 
 
-def test_serving_lookahead_refill_equals_generate(gctx):
+def test_serving_lookahead_refill_equals_generate(gctx, orc):
     """With the serving lookahead the next chunk runs while results are collected; refilled sequences
-    join one chunk later and every sequence still decodes exactly as alone."""
+    join one chunk later and every sequence still decodes exactly as the oracle generates it alone."""
     reqs = S.ragged_requests(56, 6, lo=40, hi=120)
     seeds = [600 + i for i in range(6)]
     steps = [40, 40, 40, 40, 68, 75]
     _reserve(gctx, 0, slots=4, ctx=512)
-    alone = []
-    for i in range(6):
-        t, _ = gctx.generate([reqs[i]], seeds=[seeds[i]], max_steps=steps[i])
-        alone.append(t[0][len(reqs[i].prompt):])
+    alone = _alone(orc, gctx, reqs, seeds, steps)
     gctx.serve_admit(reqs[:4], seeds[:4], list(range(4)), max_steps=40)
     gctx.set_serve_lookahead(True)
     try:
@@ -275,18 +334,15 @@ def test_serving_lookahead_refill_equals_generate(gctx):
         assert np.array_equal(served[i], alone[i]), i
 
 
-def test_serving_mixed_sampler_settings(gctx):
+def test_serving_mixed_sampler_settings(gctx, orc):
     """Sequences admitted with different sampler settings share the running batch (every slot keeps the
-    settings it was admitted with) and each decodes exactly as alone."""
+    settings it was admitted with) and each decodes exactly as the oracle generates it alone."""
     reqs = S.ragged_requests(57, 4, lo=40, hi=120)
     seeds = [700 + i for i in range(4)]
     cfgs = [dict(top_k=15, top_p=1.0, temperature=1.0, rep=1.35), dict(top_k=5, top_p=0.8, temperature=0.7, rep=1.1),
             dict(top_k=1, top_p=1.0, temperature=1.0, rep=1.0), dict(top_k=30, top_p=0.95, temperature=1.3, rep=1.35)]
     _reserve(gctx, 0, slots=4, ctx=512)
-    alone = []
-    for i in range(4):
-        t, _ = gctx.generate([reqs[i]], seeds=[seeds[i]], max_steps=48, **cfgs[i])
-        alone.append(t[0][len(reqs[i].prompt):])
+    alone = [_alone(orc, gctx, [reqs[i]], [seeds[i]], [48], **cfgs[i])[0] for i in range(4)]
     for i in range(4):
         gctx.serve_admit([reqs[i]], [seeds[i]], [i], max_steps=48, **cfgs[i])
     served = {}
@@ -300,11 +356,11 @@ def test_serving_mixed_sampler_settings(gctx):
         assert np.array_equal(served[i], alone[i]), i
 
 
-def test_cpp_ar_server_matches_generate(gctx, model_full, tmp_path):
+def test_cpp_ar_server_matches_generate(gctx, orc, model_full, tmp_path):
     """The C++ continuous-batching front end (include/gsv_ar_server.h, the role of svc::ArBatcher): tasks
     submitted from 3 threads into 4 slots, with different sampler settings, early-stop limits, lengths
-    and empty BERT sides, each return exactly the tokens of gsv_ar::generate of that one sequence
-    (prompt_phones ++ phones, prompt_bert ++ bert, prompt codes; as gsv_engine::ar_generate_batch)."""
+    and empty BERT sides, each return exactly the tokens the oracle (and gsv_ar::generate) gives that one
+    sequence (prompt_phones ++ phones, prompt_bert ++ bert, prompt codes; as gsv_engine::ar_generate_batch)."""
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     exe = os.path.join(root, "tests", "cpp", "bin", "gsv_ar_server_test")
     assert os.path.exists(exe), "build with `make -C tests/cpp`"
@@ -349,8 +405,11 @@ def test_cpp_ar_server_matches_generate(gctx, model_full, tmp_path):
         k, tp, temp, rp = t["cfg"]
         toks, _ = gctx.generate([req], top_k=k, top_p=tp, temperature=temp, rep=rp, early_stop=t["early_stop"],
                                 max_steps=t["max_steps"], seeds=[t["seed"]])
+        ref, _ = orc.generate([req], top_k=k, top_p=tp, temperature=temp, rep=rp, early_stop=t["early_stop"],
+                              max_steps=t["max_steps"], seeds=[t["seed"]], kv_f16=True)
+        assert np.array_equal(toks[0], ref[0]), i
         assert lines[i]["task"] == i
-        assert lines[i]["tokens"] == toks[0][len(t["codes"]):].tolist(), i
+        assert lines[i]["tokens"] == ref[0][len(t["codes"]):].tolist(), i
 
 
 def test_cpp_dropin_class(gctx, model_full, tmp_path):

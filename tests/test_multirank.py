@@ -77,12 +77,15 @@ def test_request_stream_is_reproducible():
 
 def test_reference_arm_line():
     """`bench.py --impl reference` (the CPU reference arm the driver runs beside this library's arm) prints
-    one JSON line with the bench contract's keys, on a 2-sequence CPU sample."""
+    one JSON line with the bench contract's keys; here on a small job (4 slots, 32 iterations) split into
+    2 timed steps. Its config is the one the GPU arm prints for the same arguments."""
     import json
     import subprocess
-    out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "1",
-                          "--warmup", "3", "--cpu-sample-seqs", "2"], capture_output=True, text=True, timeout=600,
-                         cwd=ROOT)
+    sys.path.insert(0, ROOT)
+    import bench
+    out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "2",
+                          "--warmup", "3", "--slots", "4", "--iters", "32"], capture_output=True, text=True,
+                         timeout=600, cwd=ROOT)
     assert out.returncode == 0, out.stderr
     line = json.loads(out.stdout.strip().splitlines()[-1])
     for k in ("impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
@@ -90,3 +93,6 @@ def test_reference_arm_line():
         assert k in line, k
     assert line["impl"] == "reference" and line["value"] > 0 and line["ms_per_step"] > 0
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["cpu_baseline"]["kind"] == "port"
+    args = bench.argparse.Namespace(slots=4, iters=32, refill_every=16, format="q8_0")
+    assert line["config"] == bench.serve_config(args, 1)
+    assert line["steps"] == 2 and line["job"]["chunks"] == 2 and line["job"]["tokens"] > 0

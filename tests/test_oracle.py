@@ -603,3 +603,39 @@ def test_bert_oracle_vs_transformers(tmp_path):
         hs = model(torch.from_numpy(ids.astype(np.int64))[None], output_hidden_states=True).hidden_states
     ref = hs[-3][0].numpy().T                                          # [D][T]
     assert rel_l2(O.BertOracle(path).encode(ids), ref) < 1e-6
+
+
+def test_oracle_serving_equals_generate(model_small):
+    """The oracle's continuous-batching loop (OracleServer: the CPU arm of the serving benchmark and the
+    reference for the library's gsvcu_serve_*): sequences admitted into refilled slots, with different
+    sampler settings and an early-stop limit, each produce exactly the tokens of generate alone."""
+    orc = O.OracleModel(model_small)
+    reqs = S.ragged_requests(55, 6, lo=40, hi=120)
+    seeds = [500 + i for i in range(6)]
+    steps = [40, 40, 40, 40, 68, 75]
+    cfgs = [dict(), dict(top_k=5, top_p=0.8, temperature=0.7, rep=1.1), dict(top_k=1),
+            dict(top_k=30, top_p=0.95, temperature=1.3), dict(), dict(top_k=3)]
+    early = [-1, 30, -1, -1, 50, -1]
+    alone = []
+    for i in range(6):
+        t, _ = orc.generate([reqs[i]], seeds=[seeds[i]], max_steps=steps[i], early_stop=early[i], **cfgs[i])
+        alone.append(t[0][len(reqs[i].prompt):])
+    srv = O.OracleServer(orc, 4, 512)
+    for i in range(4):
+        srv.admit([reqs[i]], [seeds[i]], [i], max_steps=steps[i], early_stop=early[i], **cfgs[i])
+    served, pending = {}, 4
+    for _ in range(200):
+        if len(served) == 6:
+            break
+        for f in srv.step(8, tok_cap=100000):
+            served[f["tag"]] = f
+            if pending < 6:
+                srv.admit([reqs[pending]], [seeds[pending]], [pending], max_steps=steps[pending],
+                          early_stop=early[pending], **cfgs[pending])
+                pending += 1
+    assert len(served) == 6 and srv.active() == 0
+    for i in range(6):
+        assert np.array_equal(served[i]["tokens"], alone[i]), i
+        kind = served[i]["finish_kind"]
+        assert served[i]["n_generated"] == (steps[i] if kind == 2 else len(alone[i]))
+    assert srv.tokens_total() == sum(len(a) for a in alone)

@@ -9,7 +9,8 @@ last on purpose; it passes alone in a fresh process as well as after the other t
 Checked: through the C ABI, on two calls in a row (the shared scratch keeps the first call's
 contents), its outputs equal those of gsvcu_op_decode_attention on the same inputs, bit for bit --
 the tolerance the decode-attention parity test holds that kernel to -- for F16 and F32 KV pools with
-multi-chunk sequences; and sizes beyond the fixed scratch are rejected.
+multi-chunk sequences; at exactly the scratch's capacity (16 sequences x 64 pages, some at the last
+key) it is accepted and also equals the oracle bit for bit; sizes beyond the fixed scratch are rejected.
 """
 import ctypes as C
 
@@ -75,6 +76,51 @@ def test_noalloc_matches_existing_entry_point_twice(kv_dtype):
     ctx.close()
 
 
+def test_noalloc_at_full_capacity_matches_oracle():
+    """B x max_pages exactly at the limit (16 x 64 = GSVCU_NOALLOC_MAX_ITEMS), several sequences at the
+    last key the block table holds: accepted, equal to gsvcu_op_decode_attention and to the oracle bit for
+    bit (the kernels and the oracle share one fixed float order), twice in a row."""
+    import gsvcu
+    import oracle as O
+    lib = gsvcu.load_library()
+    ctx = gsvcu.Context(0)
+    stream = torch.cuda.current_stream().cuda_stream
+    B, maxp, n_layer, layer = 16, 64, 2, 1
+    for call in range(2):
+        rng = np.random.default_rng(300 + call)
+        lens = [maxp * 64] * 4 + [int(l) for l in rng.integers(1, maxp * 64 + 1, B - 4)]
+        npages = B * maxp
+        pool = rng.standard_normal((npages, n_layer, 2, 16, 64, 32)).astype(np.float16)
+        bt = rng.permutation(npages).astype(np.int32).reshape(B, maxp)
+        q = rng.standard_normal((B, 512)).astype(np.float32)
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+        x = dict(q=t(q), pool=t(pool), bt=t(bt), kvpos=t(np.array(lens, np.int32) - 1), active=t(np.ones(B, np.int32)))
+        ref_q, ref_d, ref_f = _outs(B)
+        ctx.op_decode_attention(x["q"], 512, x["pool"], 0, n_layer, layer, x["bt"], maxp, x["kvpos"], x["active"], B,
+                                ref_q, ref_d, ref_f)
+        ctx.sync()
+        got_q, got_d, got_f = _outs(B)
+        p = lambda a: C.c_void_p(a.data_ptr())
+        rc = lib.gsvcu_op_decode_attention_noalloc(C.c_void_p(stream), p(x["q"]), 512, p(x["pool"]), 0, n_layer, layer,
+                                                   p(x["bt"]), maxp, p(x["kvpos"]), p(x["active"]), B, p(got_q),
+                                                   p(got_d), p(got_f))
+        assert rc == 0
+        torch.cuda.synchronize()
+        assert torch.equal(got_f.view(torch.int32), ref_f.view(torch.int32)), call
+        assert torch.equal(got_q, ref_q) and torch.equal(got_d, ref_d), call
+        Lmax = max(lens)
+        kk = np.zeros((B, Lmax, 16, 32), np.float32)
+        vv = np.zeros((B, Lmax, 16, 32), np.float32)
+        for b, l in enumerate(lens):
+            pages = pool[bt[b, :(l + 63) // 64], layer].astype(np.float32)     # [pages][K,V][16][64][32]
+            kk[b, :l] = pages[:, 0].transpose(0, 2, 1, 3).reshape(-1, 16, 32)[:l]
+            vv[b, :l] = pages[:, 1].transpose(0, 2, 1, 3).reshape(-1, 16, 32)[:l]
+        want = O.decode_attention(q.reshape(B, 16, 32), kk, vv, np.array(lens, np.int32),
+                                  1.0 / np.sqrt(np.float32(32))).reshape(B, 512)
+        assert np.array_equal(got_f.cpu().numpy().view(np.uint32), want.view(np.uint32)), call
+    ctx.close()
+
+
 def test_noalloc_rejects_sizes_beyond_its_scratch():
     import gsvcu
     lib = gsvcu.load_library()
@@ -85,4 +131,7 @@ def test_noalloc_rejects_sizes_beyond_its_scratch():
     assert rc == -1
     # nor does 64 x 17 = 1088 (F32 pool)
     rc = lib.gsvcu_op_decode_attention_noalloc(None, p, 1536, p, 1, 1, 0, p, 17, p, p, 64, p, p, None)
+    assert rc == -1
+    # nor 1025 sequences of one page
+    rc = lib.gsvcu_op_decode_attention_noalloc(None, p, 1536, p, 0, 1, 0, p, 1, p, p, 1025, p, p, None)
     assert rc == -1
