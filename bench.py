@@ -57,6 +57,8 @@ def parse():
                          "gemv: config-3 Q8_0 GEMV sweep; prefill: config-2 prefill attention + GEMMs; "
                          "single: config-0 single-sequence decode latency")
     ap.add_argument("--attn-batches", default="1,8,32,64,128")
+    ap.add_argument("--prefill-gemm", default="auto", choices=["auto", "tc", "mma"],
+                    help="prefill Q8_0 GEMMs: tc = tcgen05/TMEM kernel, mma = mma.sync tiles, auto = the library default")
     return ap.parse_args()
 
 
@@ -239,6 +241,11 @@ def prefill_bench(args):
         best = min(best, e0.elapsed_time(e1))
     int8_tops = 2 * 8192 ** 3 / (best * 1e-3) / 1e12
     del a, b
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            bf16_peak = float(json.load(f)["bf16_tflops"])
+    except Exception:
+        bf16_peak = 1590.0
     rng = np.random.default_rng(4)
     for (N, K) in [(1536, 512), (512, 512), (2048, 512), (512, 2048)]:
         raw = _rand_q8(rng, N, K)
@@ -251,14 +258,22 @@ def prefill_bench(args):
                               .reshape(M, K // 32)).cuda()
         y = torch.empty((M, N), device="cuda")
         bias = torch.randn(N, device="cuda")
-        call = lambda: ctx.op_q8_gemm(xq, xd, M, wq, wd, N, K, bias, None, gsvcu.EPI_BIAS, y=y)
-        for _ in range(max(args.warmup, 10)):
-            call()
-        ms = _flush_and_time(ext, flush, call, max(args.steps, 5))
-        tops = 2 * M * N * K / (ms * 1e-3) / 1e12
-        print(json.dumps({"workload": "cfg2 prefill Q8_0 GEMM", "M": M, "shape": f"{K}x{N}", "ms": ms,
-                          "TOPs": tops, "peak_int8_TOPs_measured_here": int8_tops, "frac": tops / int8_tops,
-                          "kernel": "k_gemm_q8_tile (mma.m16n8k32 s8 per Q8_0 block + pinned float chain)"}))
+        w16 = torch.empty(N * K, dtype=torch.float16, device="cuda")
+        ctx.op_pack_q8_0_f16(raw, N, K, w16)
+        variants = [("k_gemm_q8_tile (mma.m16n8k32 s8 per Q8_0 block + pinned float chain)",
+                     lambda: ctx.op_q8_gemm(xq, xd, M, wq, wd, N, K, bias, None, gsvcu.EPI_BIAS, y=y)),
+                    ("k_q8_to_f16 + k_gemm_q8_tc (tcgen05.mma kind::f16 into TMEM, TMA tiles, per-block float "
+                     "chain in the epilogue warps)",
+                     lambda: ctx.op_q8_gemm_tc(xq, xd, M, w16, wd, N, K, bias, None, gsvcu.EPI_BIAS, y=y))]
+        for name, call in variants:
+            for _ in range(max(args.warmup, 10)):
+                call()
+            ms = _flush_and_time(ext, flush, call, max(args.steps, 5))
+            tops = 2 * M * N * K / (ms * 1e-3) / 1e12
+            print(json.dumps({"workload": "cfg2 prefill Q8_0 GEMM", "M": M, "shape": f"{K}x{N}", "ms": ms,
+                              "TOPs": tops, "peak_int8_TOPs_measured_here": int8_tops, "frac_int8": tops / int8_tops,
+                              "peak_bf16_TFLOPs_measured": bf16_peak, "frac_bf16": tops / bf16_peak,
+                              "kernel": name}))
     ctx.close()
 
 
@@ -621,6 +636,8 @@ def main():
 
     ctx = gsvcu.Context(local_rank)
     ctx.load(model)
+    if args.prefill_gemm != "auto":
+        ctx.set_prefill_gemm(1 if args.prefill_gemm == "tc" else 0)
     max_ctx = 400 + args.iters + 8
     ctx.kv_reserve(args.slots, max_ctx, gsvcu.KV_F16 if args.kv == "f16" else gsvcu.KV_F32)
     ext = torch.cuda.ExternalStream(ctx.stream_handle())

@@ -22,6 +22,7 @@ struct LayerW {
     uint8_t* wmins[4] = {nullptr, nullptr, nullptr, nullptr};  // Q4_K / Q5_K: sub-block mins
     uint4* wq[4] = {nullptr, nullptr, nullptr, nullptr};     // Q8_0: fragment planes
     uint16_t* wd[4] = {nullptr, nullptr, nullptr, nullptr};  //       matching fp16 scale planes
+    __half* w16[4] = {nullptr, nullptr, nullptr, nullptr};   //       the integers as fp16 [N][K] (tcgen05 prefill)
     const void* wf[4] = {nullptr, nullptr, nullptr, nullptr};  // F32 / F16: the GGUF rows [N][K] as stored
     float *b_qkv = nullptr, *b_out = nullptr, *n1w = nullptr, *n1b = nullptr;
     float *b_f1 = nullptr, *b_f2 = nullptr, *n2w = nullptr, *n2b = nullptr;
@@ -31,6 +32,7 @@ constexpr int PE_MAX = 8192;          // positional table rows (reference: 4096,
 constexpr int PREFILL_ROWS = 16384;   // rows of one prefill pass
 constexpr int STEP_CHUNK = 16;        // decode steps between host status reads in generate
 constexpr int GRAPH_CHUNK = 16;       // decode steps captured in one graph (no launch gap between them)
+constexpr int TC_MIN_ROWS = 128;      // prefill rows from which the Q8_0 GEMMs run on tcgen05
 
 struct DeviceGuard {
     int prev = -1;
@@ -192,6 +194,15 @@ void unpack_kquant(const GgufTensor* t, std::vector<int16_t>& w, std::vector<uin
         }
         for (int e = 0; e < 256; e++) dst[(e % 8) * 32 + e / 8] = (int16_t)(val[e] * scl[e]);
     }
+}
+
+// fp16 bit pattern of a small integer (|v| <= 128: exact)
+uint16_t i8_as_f16_bits(int8_t v) {
+    if (v == 0) return 0;
+    const uint32_t a = (uint32_t)(v < 0 ? -(int)v : (int)v);
+    int e = 31 - __builtin_clz(a);                        // a = 1.m * 2^e, e <= 7
+    const uint32_t mant = (a << (10 - e)) & 0x3ffu;
+    return (uint16_t)((v < 0 ? 0x8000u : 0u) | ((uint32_t)(e + 15) << 10) | mant);
 }
 
 std::vector<uint8_t> to_q8_0_blocks(const GgufTensor* t) {
@@ -408,11 +419,19 @@ struct gsvcu_ctx {
     // op-entry scratch
     float* op_part = nullptr;
     size_t op_part_n = 0;
-    // set by decode attention when a bounded wait for its staged K/V gave up: [0] by the decode steps
-    // (read and cleared with the slot state), [1] by gsvcu_op_decode_attention (read and cleared by gsvcu_sync)
+    __half* op_a16 = nullptr;
+    size_t op_a16_n = 0;
+    // set when a bounded wait in a kernel gave up: [0] decode attention in the decode steps (read and
+    // cleared with the slot state), [1] gsvcu_op_decode_attention (read and cleared by gsvcu_sync),
+    // [2] the tcgen05 prefill GEMM (read and cleared at the end of each prefill pass)
     int32_t* att_err = nullptr;
     // test-only fault injection (gsvcu_set_wait_fault): extra bytes each K/V page wait expects, poll limit
     uint32_t fault_extra_tx = 0, fault_poll_limit = 0;
+    // prefill GEMMs of Q8_0 matrices on the tcgen05 tensor cores (gemm_tc.cu) from TC_MIN_ROWS rows on
+    // (gsvcu_set_prefill_gemm; off by default: measured on B200 the mma.sync tiles are 8 % faster at
+    // 4096 rows and the serving job 1.6 % faster); a16: the fp16 copy of the GEMM's activation integers
+    bool tc_prefill = false;
+    __half* a16 = nullptr;
     // decode steps run the fused layer tail (dense.cu) when the device can hold its cluster
     bool dense_ok = false, fused = true;
     bool two_groups = false;   // fused step: split the slots into two groups on forked streams (mode 2)
@@ -472,6 +491,7 @@ gsvcu_ctx::~gsvcu_ctx() {
     free_cache();
     for (void* p : wallocs) cudaFree(p);
     if (op_part) cudaFree(op_part);
+    if (op_a16) cudaFree(op_a16);
     if (att_err) cudaFree(att_err);
     for (cudaStream_t gs : gstream)
         if (gs) cudaStreamDestroy(gs);
@@ -620,10 +640,22 @@ int gsvcu_ctx::load(const char* path) {
             }
             wq_tmp.resize((size_t)N * K);
             wd_tmp.resize((size_t)N * K / QK);
+            std::vector<uint16_t> w16_tmp;
             if (t->type == 8) pack_q8_0_host(t->data, N, K, wq_tmp.data(), wd_tmp.data());
             else pack_q8_0_host(to_q8_0_blocks(t).data(), N, K, wq_tmp.data(), wd_tmp.data());
             TRY(upload(wq_tmp.data(), wq_tmp.size(), (void**)&L[li].wq[m]));
             TRY(upload(wd_tmp.data(), wd_tmp.size() * 2, (void**)&L[li].wd[m]));
+            {   // the same integers as fp16, row-major [N][K]: the tensor-core prefill GEMM's operand
+                const std::vector<uint8_t> conv = t->type == 8 ? std::vector<uint8_t>() : to_q8_0_blocks(t);
+                const uint8_t* blocks = t->type == 8 ? (const uint8_t*)t->data : conv.data();
+                w16_tmp.resize((size_t)N * K);
+                for (size_t r = 0; r < (size_t)N; r++)
+                    for (int kb = 0; kb < K / QK; kb++) {
+                        const int8_t* qv = (const int8_t*)(blocks + (r * (K / QK) + kb) * 34 + 2);
+                        for (int j = 0; j < QK; j++) w16_tmp[r * K + kb * QK + j] = i8_as_f16_bits(qv[j]);
+                    }
+                TRY(upload(w16_tmp.data(), w16_tmp.size() * 2, (void**)&L[li].w16[m]));
+            }
         }
         float** dst[8] = {&L[li].b_qkv, &L[li].b_out, &L[li].n1w, &L[li].n1b,
                           &L[li].b_f1, &L[li].b_f2, &L[li].n2w, &L[li].n2b};
@@ -658,6 +690,7 @@ void gsvcu_ctx::free_cache() {
     for (void* p : callocs) cudaFree(p);
     callocs.clear();
     p_feat = nullptr;
+    a16 = nullptr;
     reserved = false;
     max_slots = max_ctx = n_pages = max_pages = 0;
     h_bt.clear();
@@ -713,6 +746,7 @@ int gsvcu_ctx::reserve(int slots, int ctx, int kvd) {
         {(void**)&p_tiles, (M / PREF_QTILE + max_slots) * sizeof(PrefillTile)},
         {(void**)&p_xl, (size_t)max_slots * D * 4}, {(void**)&p_lg, (size_t)max_slots * V * 4},
         {(void**)&hf, ffn_float ? M * FF * 4 : 0},
+        {(void**)&a16, M * FF * 2},
     };
     for (const A& a : list) {
         if (!a.bytes) {
@@ -917,7 +951,14 @@ int gsvcu_ctx::prefill_pass(const int* slots, const gsvcu_request* reqs, int n, 
     launches += 3 + (int64_t)NL * 7 + 2 + nlg;
     CK(cudaGetLastError());
     // host staging vectors die at return: finish the pass before they go
+    int32_t gerr = 0;
+    CK(cudaMemcpyAsync(&gerr, att_err + 2, sizeof(gerr), cudaMemcpyDeviceToHost, s));
     CK(cudaStreamSynchronize(s));
+    if (gerr) {
+        CK(cudaMemsetAsync(att_err + 2, 0, sizeof(int32_t), s));
+        CK(cudaStreamSynchronize(s));
+        return fail(GSVCU_ERR_CUDA, "prefill GEMM: staged tiles never arrived (bounded wait gave up)");
+    }
     return GSVCU_OK;
 }
 
@@ -931,6 +972,12 @@ void gsvcu_ctx::layer_gemm(int li, int m, const LayerIO& io, int M, const KvWrit
     if (w.mt[m] == 8) {
         GemmQ8Params g;
         g.M = M; g.wq = w.wq[m]; g.wd = w.wd[m]; g.N = N[m]; g.K = K[m]; g.bias = bias[m];
+        const int8_t* xsrc[4] = {io.xq, io.aq, io.n1q, hq};
+        if (tc_prefill && a16 && w.w16[m] && M >= TC_MIN_ROWS) {   // tcgen05 path: fp16 copy of the X integers
+            launch_q8_to_f16(xsrc[m], a16, (size_t)M * K[m], s);
+            g.x16 = a16; g.w16 = w.w16[m]; g.err = att_err + 2;
+            launches++;
+        }
         if (m == 0) { g.xq = io.xq; g.xd = io.xd; g.y = io.qkv; g.kv = kv; launch_gemm_q8(g, EPI_BIAS, s); }
         if (m == 1) { g.xq = io.aq; g.xd = io.ad; g.resid = io.x; g.y = io.pre; launch_gemm_q8(g, EPI_RESID, s); }
         if (m == 2) { g.xq = io.n1q; g.xd = io.n1d; g.yq = hq; g.yd = hd; launch_gemm_q8(g, EPI_RELU_Q8, s); }
@@ -1303,7 +1350,8 @@ int gsvcu_create(int device, gsvcu_ctx** out) {
     if (cudaGetDeviceProperties(&prop, device) != cudaSuccess || prop.major != 10) return GSVCU_ERR_DEVICE;
     DeviceGuard g(device);
     bool dense_usable = false;
-    if (gemm_q8_init_device() != cudaSuccess || attention_init_device() != cudaSuccess ||
+    if (gemm_q8_init_device() != cudaSuccess || gemm_tc_init_device() != cudaSuccess ||
+        attention_init_device() != cudaSuccess ||
         logits_init_device() != cudaSuccess || dense_init_device(&dense_usable) != cudaSuccess) {
         cudaGetLastError();
         return GSVCU_ERR_CUDA;
@@ -1312,8 +1360,8 @@ int gsvcu_create(int device, gsvcu_ctx** out) {
     c->device = device;
     c->dense_ok = dense_usable;
     if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaMalloc((void**)&c->att_err, 2 * sizeof(int32_t)) != cudaSuccess ||
-        cudaMemset(c->att_err, 0, 2 * sizeof(int32_t)) != cudaSuccess ||
+        cudaMalloc((void**)&c->att_err, 3 * sizeof(int32_t)) != cudaSuccess ||
+        cudaMemset(c->att_err, 0, 3 * sizeof(int32_t)) != cudaSuccess ||
         cudaStreamCreateWithFlags(&c->gstream[0], cudaStreamNonBlocking) != cudaSuccess ||
         cudaStreamCreateWithFlags(&c->gstream[1], cudaStreamNonBlocking) != cudaSuccess ||
         cudaEventCreateWithFlags(&c->gevent[0], cudaEventDisableTiming) != cudaSuccess ||
@@ -1619,6 +1667,49 @@ int gsvcu_op_q8_gemm(gsvcu_ctx* ctx, const int8_t* xq_dev, const uint16_t* xd_de
     return GSVCU_OK;
 }
 
+int gsvcu_op_pack_q8_0_f16(gsvcu_ctx* ctx, const uint8_t* raw_host, int32_t N, int32_t K, void* w16_dev) {
+    if (!ctx || !raw_host || !w16_dev || N <= 0 || K <= 0 || K % QK) return GSVCU_ERR_ARG;
+    DeviceGuard g(ctx->device);
+    std::vector<uint16_t> h((size_t)N * K);
+    for (size_t r = 0; r < (size_t)N; r++)
+        for (int kb = 0; kb < K / QK; kb++)
+            for (int j = 0; j < QK; j++)
+                h[r * K + kb * QK + j] = i8_as_f16_bits((int8_t)raw_host[(r * (K / QK) + kb) * 34 + 2 + j]);
+    CKC(ctx, cudaMemcpy(w16_dev, h.data(), h.size() * 2, cudaMemcpyHostToDevice));
+    return GSVCU_OK;
+}
+
+int gsvcu_op_q8_gemm_tc(gsvcu_ctx* ctx, const int8_t* xq_dev, const uint16_t* xd_dev, int32_t M, const void* w16_dev,
+                        const void* wd_dev, int32_t N, int32_t K, const float* bias_dev, const float* resid_dev,
+                        int32_t epi, float* y_dev, int8_t* yq_dev, uint16_t* yd_dev) {
+    if (!ctx || !xq_dev || !xd_dev || !w16_dev || !wd_dev || M <= 0 || N <= 0 || N % 128 || K % 64 || K > 2048 ||
+        ((uintptr_t)xq_dev & 15) || ((uintptr_t)w16_dev & 15))
+        return GSVCU_ERR_ARG;
+    if (epi < 0 || epi > 2 || (epi < 2 && !y_dev) || (epi == 1 && !resid_dev) || (epi == 2 && (!yq_dev || !yd_dev)))
+        return GSVCU_ERR_ARG;
+    DeviceGuard g(ctx->device);
+    const size_t need = (size_t)M * K;
+    if (need > ctx->op_a16_n) {
+        if (ctx->op_a16) {
+            cudaStreamSynchronize(ctx->stream);
+            cudaFree(ctx->op_a16);
+        }
+        ctx->op_a16 = nullptr;
+        ctx->op_a16_n = 0;
+        CKC(ctx, cudaMalloc((void**)&ctx->op_a16, need * 2));
+        ctx->op_a16_n = need;
+    }
+    GemmQ8Params p;
+    p.xq = xq_dev; p.xd = xd_dev; p.M = M; p.wd = (const uint16_t*)wd_dev; p.N = N; p.K = K;
+    p.bias = bias_dev; p.resid = resid_dev; p.y = y_dev; p.yq = yq_dev; p.yd = yd_dev;
+    p.x16 = ctx->op_a16; p.w16 = (const __half*)w16_dev; p.err = ctx->att_err + 1;
+    if (!gemm_tc_usable(p)) return ctx->fail(GSVCU_ERR_ARG, "tensor-core GEMM not usable for this shape / driver");
+    launch_q8_to_f16(xq_dev, ctx->op_a16, need, ctx->stream);
+    if (!launch_gemm_q8_tc(p, epi, ctx->stream)) return ctx->fail(GSVCU_ERR_CUDA, "tensor map encoding failed");
+    CKC(ctx, cudaGetLastError());
+    return GSVCU_OK;
+}
+
 int gsvcu_op_layernorm_q8(gsvcu_ctx* ctx, const float* v_dev, int32_t rows, const float* w_dev, const float* b_dev,
                           float* y_dev, int8_t* yq_dev, uint16_t* yd_dev) {
     if (!ctx || !v_dev || !w_dev || !b_dev || !y_dev || !yq_dev || !yd_dev || rows < 0) return GSVCU_ERR_ARG;
@@ -1873,6 +1964,12 @@ int gsvcu_sync(gsvcu_ctx* ctx) {
         CKC(ctx, cudaStreamSynchronize(ctx->stream));
         return ctx->fail(GSVCU_ERR_CUDA, "gsvcu_op_decode_attention: staged K/V never arrived (bounded wait gave up)");
     }
+    return GSVCU_OK;
+}
+
+int gsvcu_set_prefill_gemm(gsvcu_ctx* ctx, int32_t mode) {
+    if (!ctx || mode < 0 || mode > 1) return GSVCU_ERR_ARG;
+    ctx->tc_prefill = mode == 1;
     return GSVCU_OK;
 }
 

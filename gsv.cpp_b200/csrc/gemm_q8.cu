@@ -394,6 +394,7 @@ cudaError_t gemm_q8_init_device() {
 void launch_gemm_q8(const GemmQ8Params& p, int epi, cudaStream_t s) {
     // K = 512 -> KS 4 (one chunk of 16 blocks); K = 2048 -> KS 8 at small M (two chunks of 32)
     const int KB = p.K / QK;
+    if (p.M > 64 && gemm_tc_usable(p) && launch_gemm_q8_tc(p, epi, s)) return;   // tcgen05 path (prefill)
     if (p.M <= 64) {
         if (KB % 32 == 0) launch_t<1, 8>(p, epi, s);
         else launch_t<1, 4>(p, epi, s);

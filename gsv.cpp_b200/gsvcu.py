@@ -89,6 +89,9 @@ SIGNATURES = {
     "gsvcu_set_serve_lookahead": ([_P, _I], C.c_int),
     "gsvcu_fused_decode": ([_P], C.c_int),
     "gsvcu_set_wait_fault": ([_P, _I], C.c_int),
+    "gsvcu_set_prefill_gemm": ([_P, _I], C.c_int),
+    "gsvcu_op_q8_gemm_tc": ([_P, _P, _P, _I, _P, _P, _I, _I, _P, _P, _I, _P, _P, _P], C.c_int),
+    "gsvcu_op_pack_q8_0_f16": ([_P, _P, _I, _I, _P], C.c_int),
 }
 
 PROF_CLASSES = ["sampler", "step_prep", "qkv_gemm", "decode_attn", "out_gemm", "layernorm", "ffn1_gemm", "ffn2_gemm",
@@ -290,6 +293,10 @@ class Context:
     def fused_decode(self):
         return int(self.lib.gsvcu_fused_decode(self.h))
 
+    def set_prefill_gemm(self, mode):
+        """1: prefill Q8_0 GEMMs on tcgen05 (default); 0: on mma.sync tiles (gsvcu_set_prefill_gemm)."""
+        self._check(self.lib.gsvcu_set_prefill_gemm(self.h, int(mode)))
+
     def set_wait_fault(self, on):
         """Test-only: make this context's decode-attention page waits run out (gsvcu_set_wait_fault)."""
         self._check(self.lib.gsvcu_set_wait_fault(self.h, 1 if on else 0))
@@ -314,6 +321,14 @@ class Context:
     def op_q8_gemm(self, xq, xd, M, wq, wd, N, K, bias, resid, epi, y=None, yq=None, yd=None):
         self._check(self.lib.gsvcu_op_q8_gemm(self.h, _ptr(xq), _ptr(xd), M, _ptr(wq), _ptr(wd), N, K, _ptr(bias),
                                               _ptr(resid), epi, _ptr(y), _ptr(yq), _ptr(yd)))
+
+    def op_q8_gemm_tc(self, xq, xd, M, w16, wd, N, K, bias, resid, epi, y=None, yq=None, yd=None):
+        self._check(self.lib.gsvcu_op_q8_gemm_tc(self.h, _ptr(xq), _ptr(xd), M, _ptr(w16), _ptr(wd), N, K, _ptr(bias),
+                                                 _ptr(resid), epi, _ptr(y), _ptr(yq), _ptr(yd)))
+
+    def op_pack_q8_0_f16(self, raw: np.ndarray, N: int, K: int, w16):
+        raw = np.ascontiguousarray(raw, np.uint8)
+        self._check(self.lib.gsvcu_op_pack_q8_0_f16(self.h, raw.ctypes.data, N, K, _ptr(w16)))
 
     def op_layernorm_q8(self, v, rows, w, b, y, yq, yd):
         self._check(self.lib.gsvcu_op_layernorm_q8(self.h, _ptr(v), rows, _ptr(w), _ptr(b), _ptr(y), _ptr(yq),

@@ -185,6 +185,19 @@ int gsvcu_op_q8_gemm(gsvcu_ctx* ctx, const int8_t* xq_dev, const uint16_t* xd_de
                      const void* wd_dev, int32_t N, int32_t K, const float* bias_dev, const float* resid_dev,
                      int32_t epi, float* y_dev, int8_t* yq_dev, uint16_t* yd_dev);
 
+/* The tensor-core form of gsvcu_op_q8_gemm (the prefill GEMM of the layers, src/gsv_ar.cpp:244,260,262,263):
+ * the same semantics and results bit for bit, computed with tcgen05.mma (fp16 operands holding the
+ * Q8_0 integers, fp32 accumulators in tensor memory, per-block float chains on the CUDA cores). w16_dev
+ * holds the weight integers as fp16 [N][K] (gsvcu_op_pack_q8_0_f16), wd_dev their scales [N][K/32]. N a
+ * multiple of 128, K a multiple of 64 up to 2048, xq_dev and w16_dev 16-byte aligned. Scratch for the
+ * fp16 copy of X is owned by the context (grown on demand). */
+int gsvcu_op_q8_gemm_tc(gsvcu_ctx* ctx, const int8_t* xq_dev, const uint16_t* xd_dev, int32_t M, const void* w16_dev,
+                        const void* wd_dev, int32_t N, int32_t K, const float* bias_dev, const float* resid_dev,
+                        int32_t epi, float* y_dev, int8_t* yq_dev, uint16_t* yd_dev);
+/* Raw GGUF Q8_0 blocks (host, [N][K/32] x 34 bytes) -> their integers as fp16 [N][K] on the device
+ * (w16_dev: N*K*2 bytes), the weight operand of gsvcu_op_q8_gemm_tc. */
+int gsvcu_op_pack_q8_0_f16(gsvcu_ctx* ctx, const uint8_t* raw_host, int32_t N, int32_t K, void* w16_dev);
+
 /* Fused LayerNorm (layernorm_affine, P:1535-1585; ln_affine src/gsv_ar.cpp:157-165) over rows of 512
  * already summed as (x + r) + bias, writing f32 and Q8_0 planes. */
 int gsvcu_op_layernorm_q8(gsvcu_ctx* ctx, const float* v_dev, int32_t rows, const float* w_dev, const float* b_dev,
@@ -283,6 +296,11 @@ int gsvcu_step_profile(gsvcu_ctx* ctx, int32_t n_steps, float* ms_by_class, int6
  * another mode); gsvcu_fused_decode returns the mode in use (0 when the cluster does not fit, or
  * when the model has F32 / F16 layer matrices: the fused tail reads Q8_0 weights only). */
 int gsvcu_set_fused_decode(gsvcu_ctx* ctx, int32_t mode);
+/* Prefill GEMM variant (no counterpart in the reference; an implementation switch of this library) for
+ * Q8_0-class matrices at 128 rows or more: mode 1 runs them on the tcgen05 tensor cores (TMA tiles, TMEM
+ * accumulators, the per-block float chains on CUDA cores), mode 0 (default, measured faster on B200) on
+ * mma.sync tiles. Results are identical bit for bit. */
+int gsvcu_set_prefill_gemm(gsvcu_ctx* ctx, int32_t mode);
 int gsvcu_fused_decode(const gsvcu_ctx* ctx);
 /* Number of kernels this context has launched (graph replays count their kernels). */
 int64_t gsvcu_kernel_launches(const gsvcu_ctx* ctx);

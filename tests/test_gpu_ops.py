@@ -91,6 +91,45 @@ def test_q8_gemm_bitexact(ctx, M, NK):
     assert np.array_equal(yd.cpu().numpy().view(np.uint16), rd)
 
 
+@pytest.mark.parametrize("M", [65, 128, 300, 1000, 4096])
+@pytest.mark.parametrize("NK", [(1536, 512), (512, 512), (2048, 512), (512, 2048)])
+def test_q8_gemm_tensor_cores_bitexact(ctx, M, NK):
+    """The tcgen05 / TMEM / TMA prefill GEMM (gsvcu_op_q8_gemm_tc) equals the oracle's ggml Q8_0 mul_mat
+    bit for bit in all three epilogues (ragged M: the tail tile's rows past M are zero-filled by TMA and
+    not stored), and so equals the mma.sync kernels. The activations include blocks of +-127 everywhere,
+    the largest integer sums a block can have."""
+    import gsvcu
+    N, K = NK
+    rng = np.random.default_rng(M * 11 + N + K)
+    W = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    W[:3] = 0.02 * np.sign(rng.standard_normal((3, K)))            # rows of +-amax: all values +-127
+    raw = O.quantize_q8_0(W)
+    X = rand_acts(rng, M, K)
+    X[: min(M, 5)] = np.sign(rng.standard_normal((min(M, 5), K))).astype(np.float32)
+    xq, xd = split_blocks(O.quantize_q8_0(X), M, K)
+    bias = (rng.standard_normal(N) * 0.02).astype(np.float32)
+    resid = rng.standard_normal((M, N)).astype(np.float32)
+    w16 = torch.empty(N * K, dtype=torch.float16, device="cuda")
+    ctx.op_pack_q8_0_f16(raw, N, K, w16)
+    wd = dev(split_blocks(raw, N, K)[1].view(np.int16))
+    Y = O.mul_mat(raw, 8, N, K, X)
+    txq, txd = dev(xq), dev(xd.view(np.int16))
+    y = torch.full((M, N), -9.0, dtype=torch.float32, device="cuda")
+    ctx.op_q8_gemm_tc(txq, txd, M, w16, wd, N, K, dev(bias), None, gsvcu.EPI_BIAS, y=y)
+    ctx.sync()
+    assert np.array_equal(y.cpu().numpy().view(np.uint32), (Y + bias).view(np.uint32))
+    ctx.op_q8_gemm_tc(txq, txd, M, w16, wd, N, K, dev(bias), dev(resid), gsvcu.EPI_RESID, y=y)
+    ctx.sync()
+    assert np.array_equal(y.cpu().numpy().view(np.uint32), ((resid + Y) + bias).view(np.uint32))
+    yq = torch.empty((M, N), dtype=torch.int8, device="cuda")
+    yd = torch.empty((M, N // 32), dtype=torch.int16, device="cuda")
+    ctx.op_q8_gemm_tc(txq, txd, M, w16, wd, N, K, dev(bias), None, gsvcu.EPI_RELU_Q8, yq=yq, yd=yd)
+    ctx.sync()
+    rq, rd = split_blocks(O.quantize_q8_0(O.add_act(Y, bias, 1)), M, N)
+    assert np.array_equal(yq.cpu().numpy(), rq)
+    assert np.array_equal(yd.cpu().numpy().view(np.uint16), rd)
+
+
 def test_layernorm_bitexact(ctx):
     rng = np.random.default_rng(3)
     rows = 300
