@@ -384,7 +384,7 @@ static cudaError_t init_t(int K) {
 cudaError_t gemm_q8_init_device() {
     cudaError_t e;
     if ((e = init_t<1, 4>(512))) return e;
-    if ((e = init_t<1, 8>(2048))) return e;
+    if ((e = init_t<1, 8>(4096))) return e;   // K up to 4096 (the BERT FFN's second matrix)
     if ((e = init_t<4, 4>(2048))) return e;
     if ((e = cudaFuncSetAttribute(k_gemm_q8_tile<EPI_BIAS>, cudaFuncAttributeMaxDynamicSharedMemorySize, TSMEM))) return e;
     if ((e = cudaFuncSetAttribute(k_gemm_q8_tile<EPI_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, TSMEM))) return e;
@@ -395,7 +395,7 @@ void launch_gemm_q8(const GemmQ8Params& p, int epi, cudaStream_t s) {
     // K = 512 -> KS 4 (one chunk of 16 blocks); K = 2048 -> KS 8 at small M (two chunks of 32)
     const int KB = p.K / QK;
     if (p.M > 64 && gemm_tc_usable(p) && launch_gemm_q8_tc(p, epi, s)) return;   // tcgen05 path (prefill)
-    if (p.M <= 64) {
+    if (p.M <= 64 && KB % 16 == 0) {   // the small-M kernels take K in chunks of 16 (KS 4) or 32 (KS 8) blocks
         if (KB % 32 == 0) launch_t<1, 8>(p, epi, s);
         else launch_t<1, 4>(p, epi, s);
     } else if (p.N % TF == 0 && KB % TKC == 0) {

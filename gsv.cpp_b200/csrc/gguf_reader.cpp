@@ -107,6 +107,10 @@ bool GgufFile::open(const std::string& path, std::string& err) {
             if (!c.ok) { err = "corrupt GGUF KV section"; return false; }
             u64_[key] = v;
             if (key == "general.alignment") alignment = v;
+        } else if (t == F32) {
+            const float v = c.get<float>();
+            if (!c.ok) { err = "corrupt GGUF KV section"; return false; }
+            f32_[key] = v;
         } else if (!skip_value(c, t)) {
             err = "corrupt GGUF value for key " + key;
             return false;
@@ -168,6 +172,13 @@ bool GgufFile::open(const std::string& path, std::string& err) {
 const GgufTensor* GgufFile::tensor(const std::string& name) const {
     auto it = index_.find(name);
     return it == index_.end() ? nullptr : &tensors_[it->second];
+}
+
+bool GgufFile::get_f32(const std::string& key, float& out) const {
+    auto it = f32_.find(key);
+    if (it == f32_.end()) return false;
+    out = it->second;
+    return true;
 }
 
 bool GgufFile::get_u32(const std::string& key, uint32_t& out) const {

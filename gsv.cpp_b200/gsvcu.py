@@ -94,6 +94,20 @@ SIGNATURES = {
     "gsvcu_op_pack_q8_0_f16": ([_P, _P, _I, _I, _P], C.c_int),
 }
 
+class BertHParams(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in ("hidden", "n_head", "inter", "layers_used", "vocab", "max_pos")] + \
+               [("ln_eps", C.c_float)]
+
+
+SIGNATURES.update({
+    "gsvcu_bert_load": ([C.c_int, C.c_char_p, C.POINTER(C.c_void_p)], C.c_int),
+    "gsvcu_bert_destroy": ([_P], None),
+    "gsvcu_bert_last_error": ([_P], C.c_char_p),
+    "gsvcu_bert_get_hparams": ([_P, C.POINTER(BertHParams)], C.c_int),
+    "gsvcu_bert_encode": ([_P, _P, _I, _I, _P], C.c_int),
+    "gsvcu_bert_encode_feat_batch": ([_P, _I, _P, _P, _I, _P, _I], C.c_int),
+})
+
 PROF_CLASSES = ["sampler", "step_prep", "qkv_gemm", "decode_attn", "out_gemm", "layernorm", "ffn1_gemm", "ffn2_gemm",
                 "predict", "dense_fused"]
 
@@ -372,3 +386,60 @@ class Context:
         self._check(self.lib.gsvcu_op_sample(self.h, _ptr(logits), B, V, eos, C.byref(sc), _ptr(pv), _ptr(npv),
                                              stride, _ptr(st), _ptr(rs), _ptr(tok)))
         return tok, rs
+
+
+class Bert:
+    """The BERT feature producer on the GPU (gsvcu_bert_*; the role of gsv.cpp's gsv_bert)."""
+
+    def __init__(self, path: str, device: int = 0):
+        self.lib = load_library()
+        h = C.c_void_p()
+        rc = self.lib.gsvcu_bert_load(device, path.encode(), C.byref(h))
+        if rc != OK:
+            raise GsvcuError(rc, "gsvcu_bert_load failed (see stderr)")
+        self.h = h
+        hp = BertHParams()
+        self.lib.gsvcu_bert_get_hparams(self.h, C.byref(hp))
+        self.hp = hp
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.gsvcu_bert_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _check(self, rc):
+        if rc != OK:
+            raise GsvcuError(rc, self.lib.gsvcu_bert_last_error(self.h).decode(errors="replace"))
+
+    def encode(self, ids, n_layers=-1) -> np.ndarray:
+        """gsv_bert::encode / encode_layers: [hidden][T]."""
+        ids = np.ascontiguousarray(ids, np.int32)
+        out = np.empty((self.hp.hidden, ids.size), np.float32)
+        self._check(self.lib.gsvcu_bert_encode(self.h, ids.ctypes.data, ids.size, n_layers, out.ctypes.data))
+        return out
+
+    def encode_feat_batch(self, ids_flat, lens, tmax, out=None):
+        """gsv_bert::encode_feat_batch: a list of [hidden][lens[b] - 2] arrays (empty for lens[b] <= 2); with
+        out (a device tensor) the features are written there, concatenated, and out is returned."""
+        ids_flat = np.ascontiguousarray(ids_flat, np.int32)
+        lens = np.ascontiguousarray(lens, np.int32)
+        D = self.hp.hidden
+        sizes = [D * max(int(l) - 2, 0) for l in lens]
+        if out is not None:
+            self._check(self.lib.gsvcu_bert_encode_feat_batch(self.h, len(lens), ids_flat.ctypes.data, lens.ctypes.data,
+                                                              tmax, _ptr(out), 1))
+            return out
+        flat = np.empty(max(sum(sizes), 1), np.float32)
+        self._check(self.lib.gsvcu_bert_encode_feat_batch(self.h, len(lens), ids_flat.ctypes.data, lens.ctypes.data,
+                                                          tmax, flat.ctypes.data, 0))
+        res, at = [], 0
+        for l, n in zip(lens, sizes):
+            res.append(flat[at:at + n].reshape(D, max(int(l) - 2, 0)).copy())
+            at += n
+        return res

@@ -271,6 +271,36 @@ int gsvcu_op_sample(gsvcu_ctx* ctx, const float* logits_dev, int32_t B, int32_t 
                     const gsvcu_sampler_cfg* cfg, const int32_t* prev_host, const int32_t* n_prev_host,
                     int32_t prev_stride, const int32_t* step_host, uint64_t* rng_host, int32_t* tokens_host);
 
+/* ---------------------------------------------------------------- BERT feature producer
+ * gsv.cpp's gsv_bert (reference src/gsv_bert.{h,cpp}, chinese-roberta-wwm-ext-large up to
+ * hidden_states[-3]) on the same device, producing the AR path's `bert` input. A BERT context owns its
+ * weights, stream and buffers; use it from one host thread at a time. */
+typedef struct gsvcu_bert gsvcu_bert;
+typedef struct {
+    int32_t hidden, n_head, inter, layers_used, vocab, max_pos;
+    float ln_eps;
+} gsvcu_bert_hparams;
+
+/* Load a BERT GGUF of tools/export_gguf/convert_bert.py (gsv_bert::load, src/gsv_bert.cpp:311-420):
+ * attention / FFN matrices F32, F16, BF16 or Q8_0 (others GSVCU_ERR_FORMAT), embeddings and norms F32 /
+ * F16; hidden a multiple of 128 up to 1024, head dim 64. */
+int gsvcu_bert_load(int device, const char* path, gsvcu_bert** out);
+void gsvcu_bert_destroy(gsvcu_bert* ctx);
+const char* gsvcu_bert_last_error(const gsvcu_bert* ctx);
+int gsvcu_bert_get_hparams(const gsvcu_bert* ctx, gsvcu_bert_hparams* out);
+/* gsv_bert::encode / encode_layers (src/gsv_bert.cpp:207-236): ids [T] with [CLS] / [SEP], T <= max_pos;
+ * out (host) [hidden][T] after the first n_layers layers (n_layers < 0: all layers_used; 0: the embedding
+ * LayerNorm). */
+int gsvcu_bert_encode(gsvcu_bert* ctx, const int32_t* ids, int32_t T, int32_t n_layers, float* out);
+/* gsv_bert::encode_feat_batch (src/gsv_bert.cpp:271-301; encode_feat is B = 1): B sequences, sequence b
+ * the first lens[b] ids of the slot ids_flat[b * Tmax ..], 3 <= Tmax <= max_pos, 1 <= lens[b] <= Tmax.
+ * out gets, for every sequence with lens[b] > 2 and in order, its features without [CLS] / [SEP] as
+ * [hidden][lens[b] - 2], concatenated; out is host memory, or device memory of the context's device
+ * when out_on_device != 0 (then it can be handed to gsvcu_request.bert directly). Each sequence's
+ * features equal those of its own call. */
+int gsvcu_bert_encode_feat_batch(gsvcu_bert* ctx, int32_t B, const int32_t* ids_flat, const int32_t* lens,
+                                 int32_t Tmax, float* out, int32_t out_on_device);
+
 /* ---------------------------------------------------------------- profiling (GSV_AR_PROFILE buckets,
  * reference src/gsv_ar.cpp:18-42) */
 

@@ -456,12 +456,14 @@ void ln_affine(const float* x, const float* r, const float* bias, const float* w
 }
 
 // add_act (P:1587-1620): act(a[i] + b[i % n]); act 1 = ReLU, 0 = identity.
-// act: 0 identity, 1 ReLU, 2 GELU (erf form: 0.5*v*(1 + erff(v/sqrt(2))), P:1615)
+// act: 0 identity, 1 ReLU, 2 GELU (erf form: 0.5*v*(1 + erff(v/sqrt(2))), P:1615, with erf in double)
 void add_act(const float* a, const float* b, int64_t rows, int64_t n, int act, float* y) {
     for (int64_t r = 0; r < rows; r++)
         for (int64_t i = 0; i < n; i++) {
             const float v = a[r * n + i] + b[i];
-            if (act == 2) y[r * n + i] = 0.5f * v * (1.0f + erff(v * 0.70710678118654752440f));
+            // erf evaluated in double and rounded to float: the value glibc's erff approximates to within
+            // an ulp (the CUDA path evaluates the same expression)
+            if (act == 2) y[r * n + i] = 0.5f * v * (1.0f + (float)std::erf((double)(v * 0.70710678118654752440f)));
             else y[r * n + i] = act == 1 ? (v > 0.0f ? v : 0.0f) : v;
         }
 }

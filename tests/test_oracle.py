@@ -73,6 +73,16 @@ def test_add_act_reference_test_inputs():
         ref = a + b if act == 0 else np.maximum(a + b, 0)
         assert np.abs(O.add_act(a, b, act) - ref).max() <= 2e-3
         assert np.array_equal(O.add_act(a, b, act), ref.astype(np.float32))
+    # act 2, GELU (erf form): the test's formula in float64 within its 2e-3 bar, and the oracle's own
+    # float evaluation ((0.5 v) (1 + erf(v / sqrt 2)), erf in double) bit for bit
+    import math
+    v = (a + b).astype(np.float32)
+    ref = np.array([0.5 * x * (1.0 + math.erf(x / math.sqrt(2.0))) for x in v.astype(np.float64).ravel()]).reshape(v.shape)
+    got = O.add_act(a, b, 2)
+    assert np.abs(got - ref).max() <= 2e-3
+    e = np.array([math.erf(float(np.float32(x) * np.float32(0.70710678118654752440))) for x in v.ravel()],
+                 np.float64).astype(np.float32).reshape(v.shape)
+    assert np.array_equal(got, (np.float32(0.5) * v) * (np.float32(1.0) + e))
 
 
 def test_layernorm_vs_float64():
