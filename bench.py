@@ -52,10 +52,11 @@ def parse():
                     help="jobs of the extra F32-KV (reference-exact) measurement; 0 skips it")
     ap.add_argument("--lookahead", action="store_true",
                     help="serve with gsvcu_set_serve_lookahead (the next chunk runs while the host handles results)")
-    ap.add_argument("--workload", default="serve", choices=["serve", "attn", "gemv", "prefill", "single"],
+    ap.add_argument("--workload", default="serve", choices=["serve", "attn", "gemv", "prefill", "single", "bert"],
                     help="serve: config-4 serving shard (the bench line); attn: config-3 decode-attention sweep; "
                          "gemv: config-3 Q8_0 GEMV sweep; prefill: config-2 prefill attention + GEMMs; "
-                         "single: config-0 single-sequence decode latency")
+                         "single: config-0 single-sequence decode latency; bert: the BERT feature producer "
+                         "(published 1024 / 16 / 4096 shape, 22 layers used, F16 matrices)")
     ap.add_argument("--attn-batches", default="1,8,32,64,128")
     ap.add_argument("--prefill-gemm", default="auto", choices=["auto", "tc", "mma"],
                     help="prefill Q8_0 GEMMs: tc = tcgen05/TMEM kernel, mma = mma.sync tiles, auto = the library default")
@@ -308,6 +309,55 @@ def single_bench(args):
                       "note": "wall time on the library stream incl. prefill and the 16-step status reads",
                       "reference_cpu_ms_per_token": 12.55}))
     ctx.close()
+
+
+def bert_bench(args):
+    """The BERT feature producer (gsv.cpp's gsv_bert, the AR path's `bert` input) at the published
+    chinese-roberta-wwm-ext-large shape (hidden 1024, 16 heads, FFN 4096, 24 layers of which 22 run, F16
+    matrices as the exporter's --spec writes them, seeded synthetic weights): encode_feat_batch of 16
+    sentences of 20-60 tokens, features to host memory; tokens/s over all sentence tokens. Beside it the
+    CPU restatement (oracle) on the box's host cores for the first 4 sentences."""
+    import torch
+    import gsv_synth as S
+    import gsvcu
+    import oracle as O
+    path = os.path.join(MODEL_CACHE, "bert_large_f16_seed21.gguf")
+    if not os.path.exists(path):
+        os.makedirs(MODEL_CACHE, exist_ok=True)
+        S.write_bert_model(path + ".tmp", seed=21, dims=S.BertDims(), mat_type="f16")
+        os.replace(path + ".tmp", path)
+    g = gsvcu.Bert(path)
+    rng = np.random.default_rng(22)
+    B, tmax = 16, 64
+    lens = rng.integers(20, 61, B).astype(np.int32)
+    ids = rng.integers(672, 8000, (B, tmax)).astype(np.int32)
+    ids[:, 0] = 101
+    for b in range(B):
+        ids[b, lens[b] - 1] = 102
+    for _ in range(max(args.warmup, 3)):
+        g.encode_feat_batch(ids.ravel(), lens, tmax)
+    times = []
+    for _ in range(max(args.steps, 5)):
+        t0 = time.perf_counter()
+        g.encode_feat_batch(ids.ravel(), lens, tmax)
+        times.append(time.perf_counter() - t0)
+    ms = 1e3 * float(np.median(times))
+    ntok = int(lens.sum())
+    cores = os.cpu_count() or 1
+    O.set_threads(cores)
+    orc = O.BertOracle(path)
+    t0 = time.perf_counter()
+    for b in range(4):
+        orc.encode_feat(ids[b, :lens[b]])
+    cpu_s = time.perf_counter() - t0
+    cpu_tok = int(lens[:4].sum())
+    print(json.dumps({"workload": "BERT features (gsv_bert::encode_feat_batch)", "model": "1024 / 16 heads / 4096, "
+                      "22 layers used, F16 matrices", "sentences": B, "tokens": ntok, "ms": ms,
+                      "tokens_per_s": ntok / (ms * 1e-3), "timing": "host wall clock around the call (inputs and "
+                      "features in host memory)",
+                      "cpu_baseline": {"tokens_per_s": cpu_tok / cpu_s, "cores": cores, "kind": "port",
+                                       "sample": f"oracle encode_feat of 4 sentences ({cpu_tok} tokens)"}}))
+    g.close()
 
 
 class RequestStream:
@@ -608,7 +658,8 @@ def main():
 
     if args.workload != "serve":
         if rank == 0:
-            {"attn": attn_sweep, "gemv": gemv_sweep, "prefill": prefill_bench, "single": single_bench}[args.workload](args)
+            {"attn": attn_sweep, "gemv": gemv_sweep, "prefill": prefill_bench, "single": single_bench,
+             "bert": bert_bench}[args.workload](args)
         return
 
     if args.impl == "reference":

@@ -110,3 +110,43 @@ def test_bert_rejects_bad_inputs(tmp_path_factory):
     with pytest.raises(gsvcu.GsvcuError):
         g.encode_feat_batch(np.zeros(8, np.int32), [5, 9], 4)   # length beyond its slot
     g.close()
+
+
+def test_cpp_dropin_bert_class(tmp_path_factory, tmp_path):
+    """The C++ `class gsv_bert` shim (include/gsv_bert.h, csrc/gsv_bert.cpp) gives the C ABI's features:
+    encode_feat_batch, encode_feat and encode_feat_cached agree per sequence, the LRU counts hits and
+    misses as the reference's (src/gsv_bert.cpp:241-266), encode_layers returns layers_used + 1 arrays."""
+    import json
+    import os
+    import struct
+    import subprocess
+    import gsvcu
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    exe = os.path.join(root, "tests", "cpp", "bin", "gsv_bert_smoke")
+    assert os.path.exists(exe), "build with `make -C tests/cpp`"
+    path = _model(tmp_path_factory, "small_f16", SMALL, "f16")
+    rng = np.random.default_rng(6)
+    lens, tmax = [9, 30, 2, 17], 32
+    ids = rng.integers(0, 500, (len(lens), tmax)).astype(np.int32)
+    f = tmp_path / "ids.bin"
+    with open(f, "wb") as fh:
+        fh.write(struct.pack("<ii", len(lens), tmax))
+        fh.write(np.array(lens, np.int32).tobytes())
+        fh.write(ids.tobytes())
+    out = subprocess.run([exe, path, str(f)], capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stderr
+    lines = [json.loads(x) for x in out.stdout.strip().splitlines()]
+    assert (lines[0]["hidden"], lines[0]["layers_used"], lines[0]["max_pos"]) == (256, 2, 128)
+    g = gsvcu.Bert(path)
+    feats = g.encode_feat_batch(ids.ravel(), lens, tmax)
+    w = lambda a: float((a.ravel().astype(np.float64) * ((np.arange(a.size) % 7) + 1)).sum())
+    for b in range(len(lens)):
+        rec = lines[1 + b]
+        assert rec["n"] == feats[b].size
+        assert rec["batch"] == rec["single"] == rec["cached"]
+        np.testing.assert_allclose(rec["batch"], w(feats[b]), rtol=1e-9, atol=1e-9)
+    last = lines[-1]
+    assert (last["hits"], last["misses"]) == (0, 5)   # sequence 0 was evicted by the 2-entry LRU
+    assert last["layers"] == 3
+    np.testing.assert_allclose(last["full"], w(g.encode(ids[0, :lens[0]])), rtol=1e-9)
+    g.close()
