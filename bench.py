@@ -263,7 +263,7 @@ def prefill_bench(args):
         ctx.op_pack_q8_0_f16(raw, N, K, w16)
         variants = [("k_gemm_q8_tile (mma.m16n8k32 s8 per Q8_0 block + pinned float chain)",
                      lambda: ctx.op_q8_gemm(xq, xd, M, wq, wd, N, K, bias, None, gsvcu.EPI_BIAS, y=y)),
-                    ("k_q8_to_f16 + k_gemm_q8_tc (tcgen05.mma kind::f16 into TMEM, TMA tiles, per-block float "
+                    ("k_tc_prep + k_gemm_q8_tc (persistent; tcgen05.mma kind::f16 into TMEM, TMA tiles, per-block float "
                      "chain in the epilogue warps)",
                      lambda: ctx.op_q8_gemm_tc(xq, xd, M, w16, wd, N, K, bias, None, gsvcu.EPI_BIAS, y=y))]
         for name, call in variants:

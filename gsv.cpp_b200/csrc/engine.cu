@@ -419,7 +419,7 @@ struct gsvcu_ctx {
     // op-entry scratch
     float* op_part = nullptr;
     size_t op_part_n = 0;
-    __half* op_a16 = nullptr;
+    void* op_a16 = nullptr;   // scratch of gsvcu_op_q8_gemm_tc (bytes)
     size_t op_a16_n = 0;
     // set when a bounded wait in a kernel gave up: [0] decode attention in the decode steps (read and
     // cleared with the slot state), [1] gsvcu_op_decode_attention (read and cleared by gsvcu_sync),
@@ -429,9 +429,10 @@ struct gsvcu_ctx {
     uint32_t fault_extra_tx = 0, fault_poll_limit = 0;
     // prefill GEMMs of Q8_0 matrices on the tcgen05 tensor cores (gemm_tc.cu) from TC_MIN_ROWS rows on
     // (gsvcu_set_prefill_gemm; off by default: measured on B200 the mma.sync tiles are 8 % faster at
-    // 4096 rows and the serving job 1.6 % faster); a16: the fp16 copy of the GEMM's activation integers
+    // 4096 rows and the serving job 1.6 % faster); a16: the scratch of its activation side
     bool tc_prefill = false;
-    __half* a16 = nullptr;
+    void* a16 = nullptr;
+    size_t a16_n = 0;
     // decode steps run the fused layer tail (dense.cu) when the device can hold its cluster
     bool dense_ok = false, fused = true;
     bool two_groups = false;   // fused step: split the slots into two groups on forked streams (mode 2)
@@ -746,7 +747,7 @@ int gsvcu_ctx::reserve(int slots, int ctx, int kvd) {
         {(void**)&p_tiles, (M / PREF_QTILE + max_slots) * sizeof(PrefillTile)},
         {(void**)&p_xl, (size_t)max_slots * D * 4}, {(void**)&p_lg, (size_t)max_slots * V * 4},
         {(void**)&hf, ffn_float ? M * FF * 4 : 0},
-        {(void**)&a16, M * FF * 2},
+        {(void**)&a16, a16_n = tc_scratch_bytes((int)M, FF, FF)},
     };
     for (const A& a : list) {
         if (!a.bytes) {
@@ -972,10 +973,8 @@ void gsvcu_ctx::layer_gemm(int li, int m, const LayerIO& io, int M, const KvWrit
     if (w.mt[m] == 8) {
         GemmQ8Params g;
         g.M = M; g.wq = w.wq[m]; g.wd = w.wd[m]; g.N = N[m]; g.K = K[m]; g.bias = bias[m];
-        const int8_t* xsrc[4] = {io.xq, io.aq, io.n1q, hq};
-        if (tc_prefill && a16 && w.w16[m] && M >= TC_MIN_ROWS) {   // tcgen05 path: fp16 copy of the X integers
-            launch_q8_to_f16(xsrc[m], a16, (size_t)M * K[m], s);
-            g.x16 = a16; g.w16 = w.w16[m]; g.err = att_err + 2;
+        if (tc_prefill && a16 && w.w16[m] && M >= TC_MIN_ROWS) {   // tcgen05 path (k_tc_prep + k_gemm_q8_tc)
+            g.w16 = w.w16[m]; g.tc_scratch = a16; g.tc_scratch_n = a16_n; g.err = att_err + 2;
             launches++;
         }
         if (m == 0) { g.xq = io.xq; g.xd = io.xd; g.y = io.qkv; g.kv = kv; launch_gemm_q8(g, EPI_BIAS, s); }
@@ -1688,7 +1687,7 @@ int gsvcu_op_q8_gemm_tc(gsvcu_ctx* ctx, const int8_t* xq_dev, const uint16_t* xd
     if (epi < 0 || epi > 2 || (epi < 2 && !y_dev) || (epi == 1 && !resid_dev) || (epi == 2 && (!yq_dev || !yd_dev)))
         return GSVCU_ERR_ARG;
     DeviceGuard g(ctx->device);
-    const size_t need = (size_t)M * K;
+    const size_t need = tc_scratch_bytes(M, N, K);
     if (need > ctx->op_a16_n) {
         if (ctx->op_a16) {
             cudaStreamSynchronize(ctx->stream);
@@ -1696,15 +1695,15 @@ int gsvcu_op_q8_gemm_tc(gsvcu_ctx* ctx, const int8_t* xq_dev, const uint16_t* xd
         }
         ctx->op_a16 = nullptr;
         ctx->op_a16_n = 0;
-        CKC(ctx, cudaMalloc((void**)&ctx->op_a16, need * 2));
+        CKC(ctx, cudaMalloc(&ctx->op_a16, need));
         ctx->op_a16_n = need;
     }
     GemmQ8Params p;
     p.xq = xq_dev; p.xd = xd_dev; p.M = M; p.wd = (const uint16_t*)wd_dev; p.N = N; p.K = K;
     p.bias = bias_dev; p.resid = resid_dev; p.y = y_dev; p.yq = yq_dev; p.yd = yd_dev;
-    p.x16 = ctx->op_a16; p.w16 = (const __half*)w16_dev; p.err = ctx->att_err + 1;
+    p.w16 = (const __half*)w16_dev; p.tc_scratch = ctx->op_a16; p.tc_scratch_n = ctx->op_a16_n;
+    p.err = ctx->att_err + 1;
     if (!gemm_tc_usable(p)) return ctx->fail(GSVCU_ERR_ARG, "tensor-core GEMM not usable for this shape / driver");
-    launch_q8_to_f16(xq_dev, ctx->op_a16, need, ctx->stream);
     if (!launch_gemm_q8_tc(p, epi, ctx->stream)) return ctx->fail(GSVCU_ERR_CUDA, "tensor map encoding failed");
     CKC(ctx, cudaGetLastError());
     return GSVCU_OK;

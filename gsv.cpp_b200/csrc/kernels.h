@@ -58,20 +58,22 @@ struct GemmQ8Params {
     int8_t* yq = nullptr;           // [M][N]   (EPI_RELU_Q8)
     uint16_t* yd = nullptr;         // [M][N/32]
     KvWrite kv;
-    // tensor-core path (gemm_tc.cu): the same Q8_0 integers as fp16 numbers, X [M][K] and W [N][K]
-    // row-major; when both are given and the shape allows, launch_gemm_q8 runs k_gemm_q8_tc
-    const __half* x16 = nullptr;
+    // tensor-core path (gemm_tc.cu): W's Q8_0 integers as fp16 numbers [N][K] row-major, and a device
+    // scratch area of tc_scratch_bytes(M, N, K) bytes (128-byte aligned) for the activation side; when
+    // both are given and the shape allows, launch_gemm_q8 runs k_tc_prep + k_gemm_q8_tc
     const __half* w16 = nullptr;
+    void* tc_scratch = nullptr;
+    size_t tc_scratch_n = 0;
     int32_t* err = nullptr;         // set to 1 if a bounded wait of k_gemm_q8_tc gave up (may be null)
 };
 
 void launch_gemm_q8(const GemmQ8Params& p, int epi, cudaStream_t s);
-// tcgen05 / TMEM / TMA Q8_0 GEMM (prefill): usable for this call, and its launch (false: not launched)
+// tcgen05 / TMEM / TMA Q8_0 GEMM (prefill): scratch it needs, usable for this call, and its launch (two
+// kernels; false: not launched)
+size_t tc_scratch_bytes(int M, int N, int K);
 bool gemm_tc_usable(const GemmQ8Params& p);
 bool launch_gemm_q8_tc(const GemmQ8Params& p, int epi, cudaStream_t s);
 cudaError_t gemm_tc_init_device();
-// Q8_0 integer plane (n values, n % 16 == 0, 16-byte aligned) -> the same integers as fp16
-void launch_q8_to_f16(const int8_t* q, __half* out, size_t n, cudaStream_t s);
 // Raise the dynamic shared-memory limit of every GEMM instantiation on the current device.
 cudaError_t gemm_q8_init_device();
 
