@@ -425,7 +425,7 @@ int gsvcu_bert_load(int device, const char* path, gsvcu_bert** out) {
         }
         return rc;
     };
-    if (gemm_q8_init_device() != cudaSuccess ||
+    if (gemm_q8_init_device() != cudaSuccess || gemm_fx_init_device() != cudaSuccess ||
         cudaFuncSetAttribute(k_bert_attn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              2 * B_QT * BHD * (int)sizeof(double)) != cudaSuccess ||
         cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {

@@ -348,8 +348,13 @@ struct gsvcu_ctx {
     uint16_t *predict_qd = nullptr, *predict_qm = nullptr;   // Q4_1 / Q5_1 predict: d, m (K-quants: d, dmin)
     uint8_t* predict_mins = nullptr;                          // Q4_K / Q5_K predict: sub-block mins
     // layer matrices: all Q8_0 (the fused decode step needs that), any F32 / F16 FFN (needs hf)
-    bool all_q8 = true, ffn_float = false;
+    bool all_q8 = true, ffn_float = false, any_qx = false;
     float* hf = nullptr;                 // F32 / F16 FFN: relu(W1 n1 + b1) rows [Mmax][FF]
+    // K-quant / Q4_1 / Q5_1 matrices: rows quantized to Q8_K or Q8_1 [Mmax][FF], their d [Mmax][FF/32],
+    // sums of 16 or s [Mmax][FF/16]
+    int8_t* qx_q = nullptr;
+    float* qx_d = nullptr;
+    void* qx_s = nullptr;
     int launch_logits(const float* xr, int M, int8_t* xq_s, uint16_t* xd_s, float* out, cudaStream_t s);
     // the four GEMMs of layer li over rows [r0, r0 + M) (Q8_0 or F32 / F16 per matrix); kv: K/V store of QKV
     struct LayerIO {
@@ -596,6 +601,7 @@ int gsvcu_ctx::load(const char* path) {
     const int NK[4][2] = {{3 * D, D}, {D, D}, {FF, D}, {D, FF}};
     all_q8 = true;
     ffn_float = false;
+    any_qx = (predict_fx_type == FX_QK || predict_fx_type == FX_QM) && predict_fx;
     for (int li = 0; li < NL; li++) {
         for (int m = 0; m < 4; m++) {
             const GgufTensor* t = mv.mats[(size_t)li * 4 + m];
@@ -603,6 +609,7 @@ int gsvcu_ctx::load(const char* path) {
             L[li].mt[m] = q8_class(t->type) ? 8 : t->type == 7 ? 3 : (t->type == 13 || t->type == 14) ? 12 : (int)t->type;
             if (t->type == 12 || t->type == 13 || t->type == 14) {   // K-quants: k_gemm_qk planes
                 all_q8 = false;
+                any_qx = true;
                 ffn_float |= m >= 2;
                 std::vector<int16_t> kw;
                 std::vector<uint16_t> kd, kdm;
@@ -620,6 +627,7 @@ int gsvcu_ctx::load(const char* path) {
             }
             if (t->type == 3 || t->type == 7) {   // Q4_1 / Q5_1: value bytes + d, m planes (k_gemm_qm)
                 all_q8 = false;
+                any_qx = true;
                 ffn_float |= m >= 2;
                 std::vector<uint8_t> q;
                 std::vector<uint16_t> qd, qm;
@@ -747,6 +755,8 @@ int gsvcu_ctx::reserve(int slots, int ctx, int kvd) {
         {(void**)&p_tiles, (M / PREF_QTILE + max_slots) * sizeof(PrefillTile)},
         {(void**)&p_xl, (size_t)max_slots * D * 4}, {(void**)&p_lg, (size_t)max_slots * V * 4},
         {(void**)&hf, ffn_float ? M * FF * 4 : 0},
+        {(void**)&qx_q, any_qx ? M * FF : 0}, {(void**)&qx_d, any_qx ? M * (FF / 32) * 4 : 0},
+        {&qx_s, any_qx ? M * (FF / 16) * 4 : 0},
         {(void**)&a16, a16_n = tc_scratch_bytes((int)M, FF, FF)},
     };
     for (const A& a : list) {
@@ -811,6 +821,7 @@ int gsvcu_ctx::launch_logits(const float* xr, int M, int8_t* xq_s, uint16_t* xd_
         GemmFxParams g;
         g.x = xr; g.ldx = D; g.M = M; g.w = predict_fx; g.wtype = predict_fx_type; g.N = V; g.K = D; g.y = out;
         g.ldy = V; g.wd = predict_qd; g.wm = predict_qm; g.wmins = predict_mins;
+        g.qx_q = qx_q; g.qx_d = qx_d; g.qx_s = qx_s;
         launch_gemm_fx(g, FXE_BIAS, s);
         return 1;
     }
@@ -988,6 +999,7 @@ void gsvcu_ctx::layer_gemm(int li, int m, const LayerIO& io, int M, const KvWrit
     g.wtype = w.mt[m] == 1 ? FX_F16 : w.mt[m] == 30 ? FX_BF16 : w.mt[m] == 3 ? FX_QM : w.mt[m] == 12 ? FX_QK : FX_F32;
     g.wd = w.wd[m]; g.wm = w.wm[m]; g.wmins = w.wmins[m]; g.N = N[m]; g.K = K[m]; g.bias = bias[m];
     g.ldx = K[m];
+    g.qx_q = qx_q; g.qx_d = qx_d; g.qx_s = qx_s;
     if (m == 0) { g.x = io.x; g.y = io.qkv; g.kv = kv; launch_gemm_fx(g, FXE_BIAS, s); }
     if (m == 1) { g.x = io.attn; g.resid = io.x; g.y = io.pre; launch_gemm_fx(g, FXE_RESID, s); }
     if (m == 2) { g.x = io.n1; g.y = hf; launch_gemm_fx(g, FXE_RELU, s); }
@@ -1350,7 +1362,7 @@ int gsvcu_create(int device, gsvcu_ctx** out) {
     DeviceGuard g(device);
     bool dense_usable = false;
     if (gemm_q8_init_device() != cudaSuccess || gemm_tc_init_device() != cudaSuccess ||
-        attention_init_device() != cudaSuccess ||
+        gemm_fx_init_device() != cudaSuccess || attention_init_device() != cudaSuccess ||
         logits_init_device() != cudaSuccess || dense_init_device(&dense_usable) != cudaSuccess) {
         cudaGetLastError();
         return GSVCU_ERR_CUDA;
@@ -1729,7 +1741,7 @@ int gsvcu_op_f32_gemm(gsvcu_ctx* ctx, const float* x_dev, int32_t M, const float
 
 int gsvcu_op_fx_gemm(gsvcu_ctx* ctx, const float* x_dev, int32_t M, const void* w_dev, int32_t wtype, int32_t N,
                      int32_t K, const float* bias_dev, float* y_dev) {
-    if (!ctx || !x_dev || !w_dev || !y_dev || M < 0 || N <= 0 || K <= 0 || K % 64 || wtype < 0 || wtype > 2 ||
+    if (!ctx || !x_dev || !w_dev || !y_dev || M < 0 || N <= 0 || K <= 0 || K % 256 || wtype < 0 || wtype > 2 ||
         ((uintptr_t)x_dev & 15) || ((uintptr_t)w_dev & 15))
         return GSVCU_ERR_ARG;
     DeviceGuard g(ctx->device);

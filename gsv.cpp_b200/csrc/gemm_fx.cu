@@ -17,9 +17,9 @@
 // value feeds 8 FMAs, each weight 8); the pairwise fold is a transposing butterfly that halves the
 // values a lane holds at each level (32 + 16 + 8 + 4 + 2 shuffles for 64 outputs), after which each
 // lane holds two finished outputs. A CTA of 4 warps covers 16 rows x 16 columns and streams its x rows
-// and weight rows through a 4-stage cp.async pipeline of 64-value slices (a lane reads k = 32t + c of
-// a slice from shared memory, conflict-free); the weight slices of the first stages are requested
-// before the wait for the predecessor kernel. K is a multiple of 64 here.
+// and weight rows through a cp.async pipeline of 256-value (F16 / BF16) or 128-value (F32) slices (a
+// lane reads k = 32t + c of a slice from shared memory, conflict-free); the weight slices of the first
+// stages are requested before the wait for the predecessor kernel. K is a multiple of 256 here.
 #include <cuda_bf16.h>
 
 #include <type_traits>
@@ -33,8 +33,11 @@ constexpr int FX_RW = 8, FX_CW = 8;              // warp tile: rows x columns
 constexpr int FX_WM = 2, FX_WN = 2;              // warps per CTA along rows / columns
 constexpr int FX_TM = FX_RW * FX_WM, FX_TN = FX_CW * FX_WN;
 constexpr int FX_NV = FX_RW * FX_CW;             // outputs per warp
-constexpr int FX_KC = 64;                        // k values per pipeline stage (two chain steps)
-constexpr int FX_ST = 4;                         // pipeline stages
+// Pipeline: stages of FX_KC<WT> k values (8 or 4 chain steps), FX_ST<WT> of them in flight, 48 KB of
+// shared memory: at decode sizes a GEMM is a few long stages, so it pays few load round trips.
+template <int WT> constexpr int FX_KC = WT == FX_F32 ? 128 : 256;
+template <int WT> constexpr int FX_ST = WT == FX_F32 ? 3 : 2;
+constexpr int FX_KMULT = 256;                    // K must be a multiple of this (every type's stage)
 
 template <int WT>
 using fx_wt = typename std::conditional<WT == FX_F16, __half,
@@ -42,8 +45,8 @@ using fx_wt = typename std::conditional<WT == FX_F16, __half,
 
 template <int WT>
 struct FxSmem {
-    float x[FX_ST][FX_TM][FX_KC];
-    fx_wt<WT> w[FX_ST][FX_TN][FX_KC];
+    float x[FX_ST<WT>][FX_TM][FX_KC<WT>];
+    fx_wt<WT> w[FX_ST<WT>][FX_TN][FX_KC<WT>];
 };
 
 __device__ __forceinline__ void fx_cp16(void* dst, const void* src) {
@@ -123,14 +126,15 @@ __global__ void __launch_bounds__(128) k_gemm_fx(const GemmFxParams p) {
     const int mt = blockIdx.y * FX_TM, nt = blockIdx.x * FX_TN;   // the CTA's first row / column
     const int wr = (warp / FX_WN) * FX_RW, wc = (warp % FX_WN) * FX_CW;
     const int m0 = mt + wr, n0 = nt + wc;
-    const int nch = p.K / FX_KC;
+    constexpr int KC = FX_KC<WT>, ST = FX_ST<WT>;
+    const int nch = p.K / KC;
     // one stage = the CTA's 16 x rows and 16 weight rows over 64 k values, in 16-byte copies; rows /
     // columns past the edge copy the last valid one (their sums are never stored)
-    constexpr int XCH = FX_KC * 4 / 16, WCH = FX_KC * (int)sizeof(fx_wt<WT>) / 16;   // 16-byte chunks per row
+    constexpr int XCH = KC * 4 / 16, WCH = KC * (int)sizeof(fx_wt<WT>) / 16;   // 16-byte chunks per row
     auto load_w = [&](int st, int c) {
         for (int q = tid; q < FX_TN * WCH; q += 128) {
             const int j = q / WCH, part = q % WCH;
-            const fx_wt<WT>* src = (const fx_wt<WT>*)p.w + (size_t)min(nt + j, p.N - 1) * p.K + c * FX_KC +
+            const fx_wt<WT>* src = (const fx_wt<WT>*)p.w + (size_t)min(nt + j, p.N - 1) * p.K + c * KC +
                                    part * (16 / (int)sizeof(fx_wt<WT>));
             fx_cp16(&sm.w[st][j][part * (16 / (int)sizeof(fx_wt<WT>))], src);
         }
@@ -138,32 +142,32 @@ __global__ void __launch_bounds__(128) k_gemm_fx(const GemmFxParams p) {
     auto load_x = [&](int st, int c) {
         for (int q = tid; q < FX_TM * XCH; q += 128) {
             const int r = q / XCH, part = q % XCH;
-            fx_cp16(&sm.x[st][r][part * 4], p.x + (size_t)min(mt + r, p.M - 1) * p.ldx + c * FX_KC + part * 4);
+            fx_cp16(&sm.x[st][r][part * 4], p.x + (size_t)min(mt + r, p.M - 1) * p.ldx + c * KC + part * 4);
         }
     };
     float acc[FX_NV];
 #pragma unroll
     for (int i = 0; i < FX_NV; i++) acc[i] = 0.0f;
-    for (int s = 0; s < FX_ST - 1; s++)   // weights do not depend on the predecessor kernel
+    for (int s = 0; s < ST - 1; s++)   // weights do not depend on the predecessor kernel
         if (s < nch) load_w(s, s);
     griddep_wait();
     griddep_launch();
-    for (int s = 0; s < FX_ST - 1; s++) {   // group s: stage s's x (group 0 also the weights above)
+    for (int s = 0; s < ST - 1; s++) {   // group s: stage s's x (group 0 also the weights above)
         if (s < nch) load_x(s, s);
         asm volatile("cp.async.commit_group;" ::: "memory");
     }
     for (int c = 0; c < nch; c++) {
-        asm volatile("cp.async.wait_group %0;" ::"n"(FX_ST - 2) : "memory");   // stage c has landed
+        asm volatile("cp.async.wait_group %0;" ::"n"(ST - 2) : "memory");   // stage c has landed
         __syncthreads();   // ... for every thread, and stage c - 1 is free again
-        const int cn = c + FX_ST - 1;
+        const int cn = c + ST - 1;
         if (cn < nch) {
-            load_w(cn % FX_ST, cn);
-            load_x(cn % FX_ST, cn);
+            load_w(cn % ST, cn);
+            load_x(cn % ST, cn);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
-        const int st = c % FX_ST;
+        const int st = c % ST;
 #pragma unroll
-        for (int t = 0; t < FX_KC / 32; t++) {   // chain step k = c*64 + 32t + lane
+        for (int t = 0; t < KC / 32; t++) {   // chain step k = c*KC + 32t + lane
             float xv[FX_RW], wv[FX_CW];
 #pragma unroll
             for (int r = 0; r < FX_RW; r++) {
@@ -191,54 +195,79 @@ __global__ void __launch_bounds__(128) k_gemm_fx(const GemmFxParams p) {
     for (int e = 0; e < 2; e++) fx_store<EPI>(p, m, nb + e, acc[e]);
 }
 
-// Q4_1 / Q5_1 matrices: ggml's Q4_1 / Q5_1 x Q8_1 mul_mat in the order of its portable C dot. The CTA
-// first quantizes its 16 activation rows to Q8_1 in shared memory (quantize_row_q8_1_ref: the Q8_0
-// values and fp16 scale, plus s = fp16(sum of the values * d) with the unrounded d); thread (r, c) then
-// runs output (row r, column c) block by block: sumi = the exact integer dot of the weight's unsigned
-// 4- / 5-bit values (bytes since load) with the activation block, acc = acc + fma(d_w*d_x, sumi,
-// m_w*s_x). K is a multiple of 32, at most QM_KMAX.
-constexpr int QM_T = 16, QM_KMAX = 2048;
+// Q4_1 / Q5_1 matrices: ggml's Q4_1 / Q5_1 x Q8_1 mul_mat in the order of its portable C dot, in two
+// kernels. k_quant_q8_1 quantizes every activation row once to Q8_1 (quantize_row_q8_1_ref: the Q8_0
+// values and fp16 scale, plus s = fp16(sum of the values * d) with the unrounded d), a thread per block.
+// k_gemm_qm: a CTA owns 32 rows x 8 columns; the columns' weights (before the wait for the predecessor)
+// and the rows' Q8_1 values are staged in shared memory by cp.async. Warp w runs column w for the 32
+// rows, lane = row, block by block: sumi = the exact integer dot of the weight's unsigned 4- / 5-bit
+// values (bytes since load) with the activation block, acc = acc + fma(d_w*d_x, sumi, m_w*s_x). K is a
+// multiple of 32, at most QM_KMAX.
+constexpr int QM_R = 32, QM_C = 8, QM_KMAX = 2048;
+constexpr size_t qm_smem_bytes(int K) { return (size_t)QM_C * K + (size_t)QM_R * (K + 16); }
+constexpr size_t QM_SMEM = qm_smem_bytes(QM_KMAX);
+
+__global__ void __launch_bounds__(256) k_quant_q8_1(const float* __restrict__ x, int ldx, int M, int K,
+                                                    int8_t* __restrict__ xq, float* __restrict__ xd,
+                                                    float* __restrict__ xs) {
+    griddep_wait();
+    griddep_launch();
+    const int nb = K / 32;
+    const int i = blockIdx.x * 256 + threadIdx.x;
+    if (i >= M * nb) return;
+    const int r = i / nb, b = i - r * nb;
+    const float* src = x + (size_t)r * ldx + b * 32;
+    float v[32], amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+        *(float4*)&v[j] = *(const float4*)(src + j);
+#pragma unroll
+        for (int k = 0; k < 4; k++) amax = fmaxf(amax, fabsf(v[j + k]));
+    }
+    float d, id;
+    q8_scale(amax, d, id);
+    int sum = 0;
+    int8_t* dst = xq + (size_t)r * K + b * 32;
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+        const int8_t q0 = q8_val(v[j], id), q1 = q8_val(v[j + 1], id), q2 = q8_val(v[j + 2], id),
+                     q3 = q8_val(v[j + 3], id);
+        *(uint32_t*)(dst + j) = (uint32_t)(uint8_t)q0 | ((uint32_t)(uint8_t)q1 << 8) | ((uint32_t)(uint8_t)q2 << 16) |
+                                ((uint32_t)(uint8_t)q3 << 24);
+        sum += q0 + q1 + q2 + q3;
+    }
+    xd[(size_t)r * nb + b] = h2f(f2h(d));
+    xs[(size_t)r * nb + b] = h2f(f2h(__fmul_rn((float)sum, d)));
+}
 
 template <int EPI>
 __global__ void __launch_bounds__(256) k_gemm_qm(const GemmFxParams p) {
-    __shared__ __align__(16) int8_t xq[QM_T][QM_KMAX];
-    __shared__ float xd[QM_T][QM_KMAX / 32], xs[QM_T][QM_KMAX / 32];
-    const int tid = threadIdx.x, nb = p.K / 32;
-    const int mt = blockIdx.y * QM_T, nt = blockIdx.x * QM_T;
+    extern __shared__ __align__(16) uint8_t qm_smem[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nb = p.K / 32, ldx = p.K + 16;
+    uint8_t* ws = qm_smem;                                     // [8 columns][K]
+    int8_t* xs = (int8_t*)(qm_smem + (size_t)QM_C * p.K);      // [32 rows][K + 16]
+    const int mt = blockIdx.y * QM_R, nt = blockIdx.x * QM_C;
+    for (int q = tid; q < QM_C * p.K / 16; q += 256) {   // weights: before the wait for the predecessor
+        const int c = q / (p.K / 16), part = q - c * (p.K / 16);
+        fx_cp16(ws + (size_t)c * p.K + part * 16, (const uint8_t*)p.w + (size_t)min(nt + c, p.N - 1) * p.K + part * 16);
+    }
     griddep_wait();
     griddep_launch();
-    for (int i = tid; i < QM_T * nb; i += 256) {
-        const int r = i / nb, b = i - r * nb;
-        const float* src = p.x + (size_t)min(mt + r, p.M - 1) * p.ldx + b * 32;
-        float v[32], amax = 0.0f;
-#pragma unroll
-        for (int j = 0; j < 32; j++) {
-            v[j] = src[j];
-            amax = fmaxf(amax, fabsf(v[j]));
-        }
-        float d, id;
-        q8_scale(amax, d, id);
-        int sum = 0;
-#pragma unroll
-        for (int j = 0; j < 32; j++) {
-            const int8_t q = q8_val(v[j], id);
-            xq[r][b * 32 + j] = q;
-            sum += q;
-        }
-        xd[r][b] = h2f(f2h(d));
-        xs[r][b] = h2f(f2h(__fmul_rn((float)sum, d)));
+    for (int q = tid; q < QM_R * p.K / 16; q += 256) {
+        const int r = q / (p.K / 16), part = q - r * (p.K / 16);
+        fx_cp16(xs + (size_t)r * ldx + part * 16, p.qx_q + (size_t)min(mt + r, p.M - 1) * p.K + part * 16);
     }
+    asm volatile("cp.async.commit_group;\n cp.async.wait_group 0;" ::: "memory");
     __syncthreads();
-    const int r = tid / QM_T, c = tid % QM_T;
-    const int nc = min(nt + c, p.N - 1);
-    const int4* wrow = (const int4*)((const int8_t*)p.w + (size_t)nc * p.K);
-    const uint16_t* wdr = p.wd + (size_t)nc * nb;
-    const uint16_t* wmr = p.wm + (size_t)nc * nb;
+    const int col = nt + warp, row = mt + lane;
+    if (col >= p.N || row >= p.M) return;
+    const int4* wl = (const int4*)(ws + (size_t)warp * p.K);
+    const int4* xl = (const int4*)(xs + (size_t)lane * ldx);
+    const float* xdr = p.qx_d + (size_t)row * nb;
+    const float* xsr = (const float*)p.qx_s + (size_t)row * nb;
     float acc = 0.0f;
     for (int b = 0; b < nb; b++) {
-        const int4 w0 = __ldg(wrow + 2 * b), w1 = __ldg(wrow + 2 * b + 1);
-        const int4* xr = (const int4*)&xq[r][b * 32];
-        const int4 x0 = xr[0], x1 = xr[1];
+        const int4 w0 = wl[2 * b], w1 = wl[2 * b + 1], x0 = xl[2 * b], x1 = xl[2 * b + 1];
         int sumi = __dp4a(w0.x, x0.x, 0);
         sumi = __dp4a(w0.y, x0.y, sumi);
         sumi = __dp4a(w0.z, x0.z, sumi);
@@ -247,96 +276,163 @@ __global__ void __launch_bounds__(256) k_gemm_qm(const GemmFxParams p) {
         sumi = __dp4a(w1.y, x1.y, sumi);
         sumi = __dp4a(w1.z, x1.z, sumi);
         sumi = __dp4a(w1.w, x1.w, sumi);
-        const float dd = __fmul_rn(h2f(wdr[b]), xd[r][b]);
-        const float ms = __fmul_rn(h2f(wmr[b]), xs[r][b]);
+        const float dd = __fmul_rn(h2f(__ldg(p.wd + (size_t)col * nb + b)), xdr[b]);
+        const float ms = __fmul_rn(h2f(__ldg(p.wm + (size_t)col * nb + b)), xsr[b]);
         acc = __fadd_rn(acc, fmaf(dd, (float)sumi, ms));
     }
-    fx_store<EPI>(p, mt + r, nt + c, acc);
+    fx_store<EPI>(p, row, col, acc);
 }
 
 // K-quant matrices (Q4_K / Q5_K / Q6_K): ggml's K-quant x Q8_K mul_mat in the order of its portable C
-// dot. The CTA quantizes its 16 activation rows to Q8_K in shared memory (quantize_row_q8_K_ref, per 256
-// values: max = the value of largest magnitude, first one winning; iscale = -127/max; q = min(127,
-// round-half-even(iscale*x)); d = 1/iscale; sums of 16), storing each super-block lane-major like the
-// weights (value e at (e % 8) * 32 + e / 8). Thread (r, c) runs output (row r, column c): per
-// super-block eight exact lane sums (value e to lane e % 8) of the pre-scaled int16 weights times the
-// int8 activations (16 dp2a per lane), sums[l] = fma(d_w*d_x, lane, sums[l]); Q4_K / Q5_K also sumf =
-// fma(-dmin_w*d_x, sum_g bsums[g]*min[g/2], sumf); at the end sumf + sums[0] + ... + sums[7]. K is a
-// multiple of 256, at most QK_KMAX.
-constexpr int QK_T = 16, QK_KMAX = 2048;
+// dot, in two kernels.
+// k_quant_q8k quantizes every activation row once to Q8_K (quantize_row_q8_K_ref, per 256 values: max =
+// the value of largest magnitude, first one winning; iscale = -127/max; q = min(127,
+// round-half-even(iscale*x)); d = 1/iscale; sums of 16), a warp per (row, super-block): lane l holds
+// values 8l..8l+7, the max is a shuffle reduction of (|v|, first index), and the super-block is stored
+// lane-major like the weights (value e at (e % 8) * 32 + e / 8).
+// k_gemm_qk: a CTA owns 32 rows x 8 columns; the columns' weights (before the wait for the predecessor)
+// and the rows' Q8_K values are staged in shared memory by cp.async. Its warps then take (column,
+// super-block) tasks: lane = row, the column's weights one broadcast load for the warp, the eight exact
+// lane sums of a super-block (value e to lane e % 8) of the pre-scaled int16 weights times the int8
+// activations (16 dp2a per lane) into shared memory. Then thread (row, column) runs the float chain in super-block order: sums[l] =
+// fma(d_w*d_x, lane_l, sums[l]); Q4_K / Q5_K also sumf = fma(-dmin_w*d_x, sum_g bsums[g]*min[g/2],
+// sumf); at the end sumf + sums[0] + ... + sums[7]. K is a multiple of 256, at most QK_KMAX.
+constexpr int QK_R = 32, QK_C = 8, QK_KMAX = 2048;
+// shared memory: the columns' weights, the rows' Q8_K values (padded rows), the int32 lane sums
+constexpr size_t qk_smem_bytes(int K) {
+    return (size_t)QK_C * K * 2 + (size_t)QK_R * (K + 16) + (size_t)QK_C * (K / 256) * 8 * QK_R * 4;
+}
+constexpr size_t QK_SMEM = qk_smem_bytes(QK_KMAX);
+
+__global__ void __launch_bounds__(256) k_quant_q8k(const float* __restrict__ x, int ldx, int M, int K,
+                                                   int8_t* __restrict__ xq, float* __restrict__ xd,
+                                                   int32_t* __restrict__ xbs) {
+    griddep_wait();
+    griddep_launch();
+    const int lane = threadIdx.x & 31, nsb = K / 256;
+    const int task = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (task >= M * nsb) return;
+    const int r = task / nsb, sb = task - r * nsb;
+    const float* src = x + (size_t)r * ldx + sb * 256 + lane * 8;
+    float v[8];
+    *(float4*)&v[0] = *(const float4*)src;
+    *(float4*)&v[4] = *(const float4*)(src + 4);
+    float amax = 0.0f, mx = 0.0f;
+    int idx = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+        if (fabsf(v[i]) > amax) {
+            amax = fabsf(v[i]);
+            mx = v[i];
+            idx = lane * 8 + i;
+        }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {   // larger magnitude wins, the first index on a tie
+        const float oa = __shfl_xor_sync(0xffffffffu, amax, off), om = __shfl_xor_sync(0xffffffffu, mx, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, off);
+        if (oa > amax || (oa == amax && oi < idx)) {
+            amax = oa;
+            mx = om;
+            idx = oi;
+        }
+    }
+    const float iscale = amax != 0.0f ? __fdiv_rn(-127.0f, mx) : 0.0f;
+    int8_t* dst = xq + (size_t)r * K + sb * 256;
+    int s = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {   // value e = 8 lane + i at (e % 8) * 32 + e / 8 = i * 32 + lane
+        const int q = amax != 0.0f ? min(127, __float2int_rn(__fmul_rn(iscale, v[i]))) : 0;
+        dst[i * 32 + lane] = (int8_t)q;
+        s += q;
+    }
+    s += __shfl_xor_sync(0xffffffffu, s, 1);   // sum of 16: lanes 2g, 2g + 1
+    if ((lane & 1) == 0) xbs[(size_t)r * (K / 16) + sb * 16 + (lane >> 1)] = s;
+    if (lane == 0) xd[(size_t)r * nsb + sb] = amax != 0.0f ? __fdiv_rn(1.0f, iscale) : 0.0f;
+}
 
 template <int EPI>
 __global__ void __launch_bounds__(256) k_gemm_qk(const GemmFxParams p) {
-    __shared__ __align__(16) int8_t xq[QK_T][QK_KMAX];
-    __shared__ float xd[QK_T][QK_KMAX / 256];
-    __shared__ int32_t xbs[QK_T][QK_KMAX / 16];
-    const int tid = threadIdx.x, nsb = p.K / 256;
-    const int mt = blockIdx.y * QK_T, nt = blockIdx.x * QK_T;
+    extern __shared__ __align__(16) uint8_t qk_smem[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nsb = p.K / 256, ldx = p.K + 16;
+    int16_t* ws = (int16_t*)qk_smem;                                  // [8 columns][K]
+    int8_t* xs = (int8_t*)(qk_smem + (size_t)QK_C * p.K * 2);         // [32 rows][K + 16]
+    int32_t* ls = (int32_t*)(xs + (size_t)QK_R * ldx);                // [column][super-block][lane 8][row 32]
+    const int mt = blockIdx.y * QK_R, nt = blockIdx.x * QK_C;
+    // the columns' weights do not depend on the predecessor kernel: staged before its wait
+    for (int q = tid; q < QK_C * p.K / 8; q += 256) {
+        const int c = q / (p.K / 8), part = q - c * (p.K / 8);
+        fx_cp16(ws + (size_t)c * p.K + part * 8, (const int16_t*)p.w + (size_t)min(nt + c, p.N - 1) * p.K + part * 8);
+    }
     griddep_wait();
     griddep_launch();
-    for (int i = tid; i < QK_T * nsb; i += 256) {
-        const int r = i / nsb, sb = i - r * nsb;
-        const float* src = p.x + (size_t)min(mt + r, p.M - 1) * p.ldx + sb * 256;
-        float amax = 0.0f, mx = 0.0f;
-        for (int j = 0; j < 256; j++) {
-            const float v = src[j];
-            if (fabsf(v) > amax) {
-                amax = fabsf(v);
-                mx = v;
+    for (int q = tid; q < QK_R * p.K / 16; q += 256) {
+        const int r = q / (p.K / 16), part = q - r * (p.K / 16);
+        fx_cp16(xs + (size_t)r * ldx + part * 16, p.qx_q + (size_t)min(mt + r, p.M - 1) * p.K + part * 16);
+    }
+    asm volatile("cp.async.commit_group;\n cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    // (column, super-block) tasks: lane = row, the eight exact lane sums of the super-block; the 16 dp2a
+    // of a lane sum run as two chains (integer sums: exact in any order)
+    for (int task = warp; task < QK_C * nsb; task += 8) {
+        const int c = task / nsb, sb = task - c * nsb;
+        const int4* wl = (const int4*)(ws + (size_t)c * p.K) + sb * 32;
+        const int4* xl = (const int4*)(xs + (size_t)lane * ldx + sb * 256);
+        int32_t* dst = ls + ((size_t)(c * nsb + sb) * 8) * QK_R + lane;
+#pragma unroll
+        for (int l = 0; l < 8; l++) {   // lane l of the super-block: 32 activations, 32 weights
+            const int4 x0 = xl[2 * l], x1 = xl[2 * l + 1];
+            const int xw[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+            int a0 = 0, a1 = 0;
+#pragma unroll
+            for (int k = 0; k < 4; k += 2) {
+                const int4 w = wl[l * 4 + k], v = wl[l * 4 + k + 1];
+                a0 = __dp2a_lo(w.x, xw[2 * k], a0);
+                a0 = __dp2a_hi(w.y, xw[2 * k], a0);
+                a0 = __dp2a_lo(w.z, xw[2 * k + 1], a0);
+                a0 = __dp2a_hi(w.w, xw[2 * k + 1], a0);
+                a1 = __dp2a_lo(v.x, xw[2 * k + 2], a1);
+                a1 = __dp2a_hi(v.y, xw[2 * k + 2], a1);
+                a1 = __dp2a_lo(v.z, xw[2 * k + 3], a1);
+                a1 = __dp2a_hi(v.w, xw[2 * k + 3], a1);
             }
+            dst[l * QK_R] = a0 + a1;
         }
-        const float iscale = amax != 0.0f ? __fdiv_rn(-127.0f, mx) : 0.0f;
-        int8_t* dst = &xq[r][sb * 256];
-        for (int g = 0; g < 16; g++) {
-            int s = 0;
-            for (int j = 0; j < 16; j++) {
-                const int e = g * 16 + j;
-                const int v = amax != 0.0f ? min(127, __float2int_rn(__fmul_rn(iscale, src[e]))) : 0;
-                dst[(e & 7) * 32 + (e >> 3)] = (int8_t)v;
-                s += v;
-            }
-            xbs[r][sb * 16 + g] = s;
-        }
-        xd[r][sb] = amax != 0.0f ? __fdiv_rn(1.0f, iscale) : 0.0f;
     }
     __syncthreads();
-    const int r = tid / QK_T, c = tid % QK_T;
-    const int nc = min(nt + c, p.N - 1);
-    const int4* wrow = (const int4*)((const int16_t*)p.w + (size_t)nc * p.K);
+    // thread (row = lane, column = warp): the float chain over the super-blocks
+    const int col = nt + warp, row = mt + lane;
+    if (col >= p.N || row >= p.M) return;
     float sums[8], sumf = 0.0f;
 #pragma unroll
     for (int l = 0; l < 8; l++) sums[l] = 0.0f;
     for (int sb = 0; sb < nsb; sb++) {
-        const int4* xr = (const int4*)&xq[r][sb * 256];
-        const float xds = xd[r][sb];
-        const float dd = __fmul_rn(h2f(p.wd[(size_t)nc * nsb + sb]), xds);
+        const float xds = p.qx_d[(size_t)row * nsb + sb];
+        const float dd = __fmul_rn(h2f(__ldg(p.wd + (size_t)col * nsb + sb)), xds);
+        const int32_t* lsb = ls + ((size_t)(warp * nsb + sb) * 8) * QK_R + lane;
 #pragma unroll
-        for (int l = 0; l < 8; l++) {   // lane l: 32 pre-scaled weights (4 x int4) and 32 activations (2 x int4)
-            const int4 x0 = xr[l * 2], x1 = xr[l * 2 + 1];
-            const int xw[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-            int acc = 0;
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-                const int4 w = __ldg(wrow + (size_t)sb * 32 + l * 4 + k);
-                acc = __dp2a_lo(w.x, xw[2 * k], acc);
-                acc = __dp2a_hi(w.y, xw[2 * k], acc);
-                acc = __dp2a_lo(w.z, xw[2 * k + 1], acc);
-                acc = __dp2a_hi(w.w, xw[2 * k + 1], acc);
-            }
-            sums[l] = fmaf(dd, (float)acc, sums[l]);
-        }
+        for (int l = 0; l < 8; l++) sums[l] = fmaf(dd, (float)lsb[l * QK_R], sums[l]);
         if (p.wmins) {
-            const uint8_t* mn = p.wmins + ((size_t)nc * nsb + sb) * 8;
+            const int4* bs4 = (const int4*)((const int32_t*)p.qx_s + (size_t)row * (p.K / 16) + sb * 16);
+            const uint2 m8 = __ldg((const uint2*)(p.wmins + ((size_t)col * nsb + sb) * 8));
+            const uint32_t mw[2] = {m8.x, m8.y};
             int sumi = 0;
 #pragma unroll
-            for (int g = 0; g < 16; g++) sumi += xbs[r][sb * 16 + g] * (int)mn[g >> 1];
-            const float dmin = __fmul_rn(h2f(p.wm[(size_t)nc * nsb + sb]), xds);
+            for (int g4 = 0; g4 < 4; g4++) {
+                const int4 b = __ldg(bs4 + g4);
+                const int bg[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const int g = g4 * 4 + k;
+                    sumi += bg[k] * (int)((mw[g >> 3] >> (8 * ((g >> 1) & 3))) & 0xff);
+                }
+            }
+            const float dmin = __fmul_rn(h2f(__ldg(p.wm + (size_t)col * nsb + sb)), xds);
             sumf = fmaf(-dmin, (float)sumi, sumf);
         }
     }
 #pragma unroll
     for (int l = 0; l < 8; l++) sumf = __fadd_rn(sumf, sums[l]);
-    fx_store<EPI>(p, mt + r, nt + c, sumf);
+    fx_store<EPI>(p, row, col, sumf);
 }
 
 template <int WT>
@@ -351,29 +447,52 @@ void launch_wt(const GemmFxParams& p, int epi, cudaStream_t s) {
 
 }  // namespace
 
+cudaError_t gemm_fx_init_device() {
+    cudaError_t e;
+#define GSVCU_QK_SMEM(EPI_)                                                                                     \
+    if ((e = cudaFuncSetAttribute(k_gemm_qk<EPI_>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QK_SMEM)))    \
+        return e;
+    GSVCU_QK_SMEM(FXE_BIAS) GSVCU_QK_SMEM(FXE_RESID) GSVCU_QK_SMEM(FXE_RELU)
+#undef GSVCU_QK_SMEM
+#define GSVCU_QM_SMEM(EPI_)                                                                                     \
+    if ((e = cudaFuncSetAttribute(k_gemm_qm<EPI_>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QM_SMEM)))    \
+        return e;
+    GSVCU_QM_SMEM(FXE_BIAS) GSVCU_QM_SMEM(FXE_RESID) GSVCU_QM_SMEM(FXE_RELU)
+#undef GSVCU_QM_SMEM
+    return cudaSuccess;
+}
+
 void launch_gemm_fx(const GemmFxParams& p, int epi, cudaStream_t s) {
     if (p.M <= 0 || p.N <= 0) return;
     if (p.wtype == FX_QK) {
-        if (p.K % 256 || p.K > QK_KMAX) return;
-        const dim3 grid((p.N + QK_T - 1) / QK_T, (p.M + QK_T - 1) / QK_T), block(256);
+        if (p.K % 256 || p.K > QK_KMAX || !p.qx_q || !p.qx_d || !p.qx_s) return;
+        const int tasks = p.M * (p.K / 256);
+        launch_pdl(k_quant_q8k, dim3((tasks + 7) / 8), dim3(256), 0, s, p.x, p.ldx, p.M, p.K, p.qx_q, p.qx_d,
+                   (int32_t*)p.qx_s);
+        const dim3 grid((p.N + QK_C - 1) / QK_C, (p.M + QK_R - 1) / QK_R), block(256);
+        const size_t smem = qk_smem_bytes(p.K);
         switch (epi) {
-            case FXE_BIAS: launch_pdl(k_gemm_qk<FXE_BIAS>, grid, block, 0, s, p); break;
-            case FXE_RESID: launch_pdl(k_gemm_qk<FXE_RESID>, grid, block, 0, s, p); break;
-            default: launch_pdl(k_gemm_qk<FXE_RELU>, grid, block, 0, s, p); break;
+            case FXE_BIAS: launch_pdl(k_gemm_qk<FXE_BIAS>, grid, block, smem, s, p); break;
+            case FXE_RESID: launch_pdl(k_gemm_qk<FXE_RESID>, grid, block, smem, s, p); break;
+            default: launch_pdl(k_gemm_qk<FXE_RELU>, grid, block, smem, s, p); break;
         }
         return;
     }
     if (p.wtype == FX_QM) {
-        if (p.K % 32 || p.K > QM_KMAX) return;
-        const dim3 grid((p.N + QM_T - 1) / QM_T, (p.M + QM_T - 1) / QM_T), block(256);
+        if (p.K % 32 || p.K > QM_KMAX || !p.qx_q || !p.qx_d || !p.qx_s) return;
+        const int blocks = p.M * (p.K / 32);
+        launch_pdl(k_quant_q8_1, dim3((blocks + 255) / 256), dim3(256), 0, s, p.x, p.ldx, p.M, p.K, p.qx_q, p.qx_d,
+                   (float*)p.qx_s);
+        const dim3 grid((p.N + QM_C - 1) / QM_C, (p.M + QM_R - 1) / QM_R), block(256);
+        const size_t smem = qm_smem_bytes(p.K);
         switch (epi) {
-            case FXE_BIAS: launch_pdl(k_gemm_qm<FXE_BIAS>, grid, block, 0, s, p); break;
-            case FXE_RESID: launch_pdl(k_gemm_qm<FXE_RESID>, grid, block, 0, s, p); break;
-            default: launch_pdl(k_gemm_qm<FXE_RELU>, grid, block, 0, s, p); break;
+            case FXE_BIAS: launch_pdl(k_gemm_qm<FXE_BIAS>, grid, block, smem, s, p); break;
+            case FXE_RESID: launch_pdl(k_gemm_qm<FXE_RESID>, grid, block, smem, s, p); break;
+            default: launch_pdl(k_gemm_qm<FXE_RELU>, grid, block, smem, s, p); break;
         }
         return;
     }
-    if (p.K % FX_KC) return;
+    if (p.K % FX_KMULT) return;
     if (p.wtype == FX_F16) launch_wt<FX_F16>(p, epi, s);
     else if (p.wtype == FX_BF16) launch_wt<FX_BF16>(p, epi, s);
     else launch_wt<FX_F32>(p, epi, s);

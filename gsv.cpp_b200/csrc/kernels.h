@@ -106,8 +106,15 @@ struct GemmFxParams {
     int ldy = 0;                    // FXE_BIAS: row stride of y (0: N)
     int n_store = 0;                // FXE_BIAS: columns of y stored (0: N)
     KvWrite kv;                     // FXE_BIAS: optional K/V store of columns [D, 3D)
+    // FX_QK / FX_QM: device scratch for the rows quantized to Q8_K (values [M][K] lane-major per
+    // super-block, d [M][K/256], int32 sums of 16 [M][K/16]) or to Q8_1 (values [M][K], d [M][K/32], f32 s
+    // [M][K/32]); sized for the larger of the two
+    int8_t* qx_q = nullptr;
+    float* qx_d = nullptr;
+    void* qx_s = nullptr;
 };
 void launch_gemm_fx(const GemmFxParams& p, int epi, cudaStream_t s);
+cudaError_t gemm_fx_init_device();   // shared-memory attributes of the Q4_1 / Q5_1 and K-quant GEMMs
 
 // ------------------------------------------------------------ F32 GEMM, double accumulation
 // y[m][n] = (float) sum_k (double)w[n][k] * (double)x(m, k)  (+ add[m][n]); x(m,k) = x[m*ldx + k], or,

@@ -212,7 +212,7 @@ int gsvcu_op_f32_gemm(gsvcu_ctx* ctx, const float* x_dev, int32_t M, const float
  * (wtype 2) layer matrix (ggml F32 / F16 / BF16 mul_mat, src/gsv_ar.cpp:244,260,262,263) in the order of
  * ggml's FMA-vectorised dot: X rounded to F16 / BF16 for an F16 / BF16 W, 32 float FMA chains (chain c
  * over k = c, c + 32, ...) added
- * pairwise as chains c^16, ^8, ^4, ^1, ^2. K a multiple of 64; x_dev and w_dev 16-byte aligned. */
+ * pairwise as chains c^16, ^8, ^4, ^1, ^2. K a multiple of 256; x_dev and w_dev 16-byte aligned. */
 int gsvcu_op_fx_gemm(gsvcu_ctx* ctx, const float* x_dev, int32_t M, const void* w_dev, int32_t wtype, int32_t N,
                      int32_t K, const float* bias_dev, float* y_dev);
 
