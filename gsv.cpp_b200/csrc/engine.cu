@@ -433,9 +433,9 @@ struct gsvcu_ctx {
     // test-only fault injection (gsvcu_set_wait_fault): extra bytes each K/V page wait expects, poll limit
     uint32_t fault_extra_tx = 0, fault_poll_limit = 0;
     // prefill GEMMs of Q8_0 matrices on the tcgen05 tensor cores (gemm_tc.cu) from TC_MIN_ROWS rows on
-    // (gsvcu_set_prefill_gemm; off by default: measured on B200 the mma.sync tiles are 8 % faster at
-    // 4096 rows and the serving job 1.6 % faster); a16: the scratch of its activation side
-    bool tc_prefill = false;
+    // (gsvcu_set_prefill_gemm; the default: measured on B200 1.4x faster than the mma.sync tiles at 4096
+    // rows); a16: the scratch of its activation side
+    bool tc_prefill = true;
     void* a16 = nullptr;
     size_t a16_n = 0;
     // decode steps run the fused layer tail (dense.cu) when the device can hold its cluster

@@ -327,9 +327,9 @@ int gsvcu_step_profile(gsvcu_ctx* ctx, int32_t n_steps, float* ms_by_class, int6
  * when the model has F32 / F16 layer matrices: the fused tail reads Q8_0 weights only). */
 int gsvcu_set_fused_decode(gsvcu_ctx* ctx, int32_t mode);
 /* Prefill GEMM variant (no counterpart in the reference; an implementation switch of this library) for
- * Q8_0-class matrices at 128 rows or more: mode 1 runs them on the tcgen05 tensor cores (TMA tiles, TMEM
- * accumulators, the per-block float chains on CUDA cores), mode 0 (default, measured faster on B200) on
- * mma.sync tiles. Results are identical bit for bit. */
+ * Q8_0-class matrices at 128 rows or more: mode 1 (default) runs them on the tcgen05 tensor cores (TMA
+ * tiles, TMEM accumulators, the per-block float chains on CUDA cores), mode 0 on mma.sync tiles. Results
+ * are identical bit for bit. */
 int gsvcu_set_prefill_gemm(gsvcu_ctx* ctx, int32_t mode);
 int gsvcu_fused_decode(const gsvcu_ctx* ctx);
 /* Number of kernels this context has launched (graph replays count their kernels). */

@@ -62,18 +62,19 @@ def test_first_logits_parity(gctx, orc):
 
 
 def test_prefill_on_tensor_cores_matches_oracle(gctx, orc):
-    """With gsvcu_set_prefill_gemm(1) prefill passes of >= 128 rows run their Q8_0 GEMMs on tcgen05: the
-    per-layer outputs and logits of a batch of config-2-like prefixes (8 x ~300 rows, one pass) equal the
-    oracle's bit for bit and equal the default mma.sync path's."""
+    """Prefill passes of >= 128 rows run their Q8_0 GEMMs on tcgen05 (gsvcu_set_prefill_gemm(1), the
+    default): the per-layer outputs and logits of a batch of config-2-like prefixes (8 x ~300 rows, one
+    pass) equal the oracle's bit for bit and equal those of the mma.sync tiles (mode 0)."""
     reqs = S.ragged_requests(31, 8, lo=200, hi=400)
     _reserve(gctx, 1)
     forced = np.zeros((8, 1), np.int32)
     gctx.set_prefill_gemm(1)
+    lg, dump = gctx.debug_trace(reqs, forced, dump=True)
+    gctx.set_prefill_gemm(0)
     try:
-        lg, dump = gctx.debug_trace(reqs, forced, dump=True)
+        lg0, dump0 = gctx.debug_trace(reqs, forced, dump=True)
     finally:
-        gctx.set_prefill_gemm(0)
-    lg0, dump0 = gctx.debug_trace(reqs, forced, dump=True)
+        gctx.set_prefill_gemm(1)
     assert np.array_equal(lg.view(np.uint32), lg0.view(np.uint32))
     assert np.array_equal(dump.view(np.uint32), dump0.view(np.uint32))
     ref, rdump = orc.first_logits(reqs, dump=True)
