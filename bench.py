@@ -225,7 +225,7 @@ def prefill_bench(args):
     print(json.dumps({"workload": "cfg2 prefill attention (one layer)", "B": B, "S": S, "text": T,
                       "visible_pairs_per_seq": pairs, "mask_density": pairs / (S * S), "algorithmic_flops": flops,
                       "ms": ms, "TFLOPs": flops / (ms * 1e-3) / 1e12,
-                      "bound": "FP64 CUDA cores (pinned double-precision softmax, thread per query)"}))
+                      "bound": "FP64 tensor cores (k_prefill_attn_mma: mma.sync m8n8k4 .f64 for q.k and P.V, softmax in double)"}))
     # int8 tensor-core peak measured here (the GEMMs' denominator)
     a = torch.randint(-127, 128, (8192, 8192), dtype=torch.int8, device="cuda")
     b = torch.randint(-127, 128, (8192, 8192), dtype=torch.int8, device="cuda")

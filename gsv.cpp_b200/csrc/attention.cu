@@ -513,10 +513,141 @@ __global__ void __launch_bounds__(PREF_QTILE) k_prefill_attn(const PrefAttnParam
     }
 }
 
+// The same attention on the FP64 tensor cores (mma.sync m8n8k4 .f64). Scores q.k are products exact in
+// double summed in double, rounded to float and scaled in float as above; the softmax weights
+// exp(s - m) and their sums and the weighted sum of V are carried in double and rounded once. The
+// running maximum is taken per 64-key tile instead of per key; in double the result differs from
+// the key-by-key form only at the 1e-16 level, so it rounds to the same float (except at a rounding
+// tie, as any change of double summation order).
+// CTA = 64 queries of one head of one sequence (the tiles of k_prefill_attn), 8 warps of 8 queries.
+// Per 64-key tile, staged in shared memory as double: warp w computes its 8 x 64 score block as 8
+// n-tiles of 8 keys (8 k-steps of 4 dims each), lane holding S[row = lane / 4][key = 8t + 2 (lane % 4)
+// + i]. That is exactly the A operand of P.V when k-step (t, i) takes keys 8t + 2k + i (k = 0..3): the
+// weights never move between lanes, and the V operand is read in that key order.
+constexpr int PA_KSTR = HD + 4;   // doubles per staged K / V row: the fragment loads are conflict-free
+
+__device__ __forceinline__ void dmma884(double& d0, double& d1, double a, double b) {
+    asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0, %1}, {%2}, {%3}, {%0, %1};"
+                 : "+d"(d0), "+d"(d1)
+                 : "d"(a), "d"(b));
+}
+
+__global__ void __launch_bounds__(256) k_prefill_attn_mma(const PrefAttnParams p) {
+    __shared__ __align__(16) double Ks[PREF_QTILE][PA_KSTR];
+    __shared__ __align__(16) double Vs[PREF_QTILE][PA_KSTR];
+    const int h = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int r = lane >> 2, c = lane & 3;   // fragment row (query) and column group
+    griddep_wait();
+    griddep_launch();
+    const PrefillTile tile = p.tiles[blockIdx.y];
+    const int sq = tile.seq, q0 = tile.q0;
+    const int start = p.seq_start[sq], S = p.seq_len[sq], T = p.text_len[sq];
+    const int qi = q0 + warp * 8 + r;   // this lane's query row
+    const bool valid = qi < S;
+    double qa[HD / 4];                   // A fragments of Q: Q[qi][4 ks + c]
+#pragma unroll
+    for (int ks = 0; ks < HD / 4; ks++)
+        qa[ks] = valid ? (double)p.qkv[(size_t)(start + qi) * 3 * D + h * HD + 4 * ks + c] : 0.0;
+    float m = -INFINITY;
+    double lp = 0.0;                     // this lane's share of the row's weight sum
+    double o[HD / 8][2];                 // O[qi][8 dn + 2c + e]
+#pragma unroll
+    for (int dn = 0; dn < HD / 8; dn++) o[dn][0] = o[dn][1] = 0.0;
+    const int kend = (q0 + PREF_QTILE <= T) ? T : max(T, min(S, q0 + PREF_QTILE));
+    for (int kt = 0; kt < kend; kt += PREF_QTILE) {
+        __syncthreads();
+        for (int i = tid; i < PREF_QTILE * HD / 4; i += 256) {   // 64 keys x 8 float4 of K and of V
+            const int key = i >> 3, d4 = (i & 7) * 4;
+            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+            if (kt + key < S) {
+                const float* kr = p.qkv + (size_t)(start + kt + key) * 3 * D + D + h * HD + d4;
+                kv = *(const float4*)kr;
+                vv = *(const float4*)(kr + D);
+            }
+            *(double2*)&Ks[key][d4] = make_double2(kv.x, kv.y);
+            *(double2*)&Ks[key][d4 + 2] = make_double2(kv.z, kv.w);
+            *(double2*)&Vs[key][d4] = make_double2(vv.x, vv.y);
+            *(double2*)&Vs[key][d4 + 2] = make_double2(vv.z, vv.w);
+        }
+        __syncthreads();
+        // scores: n-tile t = keys kt + 8t .. +7
+        float sc[8][2];
+        float tmax = -INFINITY;
+#pragma unroll
+        for (int t = 0; t < 8; t++) {
+            double d0 = 0.0, d1 = 0.0;
+#pragma unroll
+            for (int ks = 0; ks < HD / 4; ks++) dmma884(d0, d1, qa[ks], Ks[8 * t + r][4 * ks + c]);
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const int key = kt + 8 * t + 2 * c + e;
+                const bool vis = valid && key < kend && (qi < T ? key < T : key <= qi);
+                const float sv = __fmul_rn((float)(e ? d1 : d0), p.scale);
+                sc[t][e] = vis ? sv : -INFINITY;
+                tmax = fmaxf(tmax, sc[t][e]);
+            }
+        }
+        tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
+        tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
+        const float mn = fmaxf(m, tmax);
+        if (mn > m && m != -INFINITY) {   // rescale the row's sums to the new maximum
+            const double rs = exp((double)m - (double)mn);
+            lp *= rs;
+#pragma unroll
+            for (int dn = 0; dn < HD / 8; dn++) {
+                o[dn][0] *= rs;
+                o[dn][1] *= rs;
+            }
+        }
+        m = mn;
+        // weights and O += P.V
+#pragma unroll
+        for (int t = 0; t < 8; t++) {
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const double pw = sc[t][e] == -INFINITY ? 0.0 : exp((double)sc[t][e] - (double)m);
+                lp += pw;
+#pragma unroll
+                for (int dn = 0; dn < HD / 8; dn++) dmma884(o[dn][0], o[dn][1], pw, Vs[8 * t + 2 * c + e][8 * dn + r]);
+            }
+        }
+    }
+    double l = lp;
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    float of[HD / 8][2], amax = 0.0f;
+#pragma unroll
+    for (int dn = 0; dn < HD / 8; dn++)
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            of[dn][e] = l > 0.0 ? (float)(o[dn][e] / l) : 0.0f;
+            amax = fmaxf(amax, fabsf(of[dn][e]));
+        }
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    if (!valid) return;
+    float dsc, id;
+    q8_scale(amax, dsc, id);
+    const size_t row = (size_t)(start + qi);
+    int8_t* qo = p.out_q + row * D + h * HD;
+#pragma unroll
+    for (int dn = 0; dn < HD / 8; dn++)
+#pragma unroll
+        for (int e = 0; e < 2; e++) qo[8 * dn + 2 * c + e] = q8_val(of[dn][e], id);
+    if (c == 0) p.out_d[row * (D / QK) + h] = f2h(dsc);
+    if (p.out_f32) {
+#pragma unroll
+        for (int dn = 0; dn < HD / 8; dn++)
+#pragma unroll
+            for (int e = 0; e < 2; e++) p.out_f32[row * D + h * HD + 8 * dn + 2 * c + e] = of[dn][e];
+    }
+}
+
 void launch_prefill_attention(const PrefAttnParams& p, cudaStream_t s) {
     if (p.n_tiles == 0) return;
     dim3 grid(NH, p.n_tiles);
-    launch_pdl(k_prefill_attn, grid, dim3(PREF_QTILE), 0, s, p);
+    if (p.fp64_mma) launch_pdl(k_prefill_attn_mma, grid, dim3(256), 0, s, p);
+    else launch_pdl(k_prefill_attn, grid, dim3(PREF_QTILE), 0, s, p);
 }
 
 }  // namespace gsvcu
