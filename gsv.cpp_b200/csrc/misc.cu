@@ -225,6 +225,66 @@ __global__ void __launch_bounds__(256) k_logits512(const float* __restrict__ x, 
     }
 }
 
+// The same product on the FP64 tensor cores (mma.sync m8n8k4 .f64): a CTA owns 64 rows x 8 columns,
+// warp w the 8 rows 64 blockIdx.y + 8 w. K is permuted between the k-steps (the double sums do not depend
+// on their order at float precision): lane (r, c) supplies k = 128 c + ks of its row (A) and of column r
+// (B) at k-step ks, so each lane streams two contiguous 512-byte runs with 16-byte loads. Two accumulator
+// pairs (even / odd k-steps) are added at the end; the sum is rounded to float once.
+__device__ __forceinline__ void lg_dmma(double& d0, double& d1, double a, double b) {
+    asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0, %1}, {%2}, {%3}, {%0, %1};"
+                 : "+d"(d0), "+d"(d1)
+                 : "d"(a), "d"(b));
+}
+
+__global__ void __launch_bounds__(256) k_logits_mma(const float* __restrict__ x, int ldx, int M,
+                                                   const float* __restrict__ w, int N, const float* __restrict__ add,
+                                                   int ldadd, float* __restrict__ y, int ldy) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, r = lane >> 2, c = lane & 3;
+    const int n0 = blockIdx.x * 8, m0 = blockIdx.y * 64 + warp * 8;
+    // the weights (constant) stream from before the wait for the rows
+    const float4* wr = (const float4*)(w + (size_t)min(n0 + r, N - 1) * D + 128 * c);
+    float4 wv[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) wv[j] = __ldg(wr + j);
+    griddep_wait();
+    griddep_launch();
+    if (m0 >= M) return;
+    const float4* xr = (const float4*)(x + (size_t)min(m0 + r, M - 1) * ldx + 128 * c);
+    double a0 = 0.0, a1 = 0.0, b0 = 0.0, b1 = 0.0;
+#pragma unroll
+    for (int ch = 0; ch < 4; ch++) {   // 4 chunks of 32 k-steps (8 float4 of x and of w per lane)
+        float4 xv[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) xv[j] = __ldg(xr + ch * 8 + j);
+        float4 wn[8];
+        if (ch < 3) {
+#pragma unroll
+            for (int j = 0; j < 8; j++) wn[j] = __ldg(wr + (ch + 1) * 8 + j);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            lg_dmma(a0, a1, (double)xv[j].x, (double)wv[j].x);
+            lg_dmma(b0, b1, (double)xv[j].y, (double)wv[j].y);
+            lg_dmma(a0, a1, (double)xv[j].z, (double)wv[j].z);
+            lg_dmma(b0, b1, (double)xv[j].w, (double)wv[j].w);
+        }
+        if (ch < 3) {
+#pragma unroll
+            for (int j = 0; j < 8; j++) wv[j] = wn[j];
+        }
+    }
+    // D[row r][column 2c + e]
+#pragma unroll
+    for (int e = 0; e < 2; e++) {
+        const int m = m0 + r, n = n0 + 2 * c + e;
+        if (m < M && n < N) {
+            float v = (float)(e ? a1 + b1 : a0 + b0);
+            if (add) v = __fadd_rn(add[(size_t)m * ldadd + n], v);
+            y[(size_t)m * ldy + n] = v;
+        }
+    }
+}
+
 cudaError_t logits_init_device() {
     return cudaFuncSetAttribute(k_logits512, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)LG_SMEM);
 }
@@ -233,8 +293,8 @@ void launch_gemm_f32d(const float* x, int ldx, const F32Gather* gather, int M, c
                       const float* add, int ldadd, float* y, int ldy, cudaStream_t s) {
     if (M <= 0) return;
     if (!gather && K == D && M <= 256 && (ldx & 3) == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)w & 15) == 0) {
-        launch_pdl(k_logits512, dim3((N + LG_COLS - 1) / LG_COLS, (M + LG_ROWS - 1) / LG_ROWS), dim3(256), LG_SMEM, s,
-                   x, ldx, M, w, N, add, ldadd, y, ldy);
+        launch_pdl(k_logits_mma, dim3((N + 7) / 8, (M + 63) / 64), dim3(256), 0, s, x, ldx, M, w, N, add, ldadd, y,
+                   ldy);
         return;
     }
     dim3 grid((N + 31) / 32, (M + 31) / 32);
