@@ -341,10 +341,13 @@ __global__ void __launch_bounds__(128) k_decode_merge(const DecAttnParams p) {
     decode_write_out(p, slot, h, g, sub, O, L);
 }
 
+cudaError_t prefill_attn_init_device();   // below, after the prefill kernels
+
 cudaError_t attention_init_device() {
     cudaError_t e = cudaFuncSetAttribute(k_decode_attn<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)DecShape<__half>::SMEM);
     if (e != cudaSuccess) return e;
+    if ((e = prefill_attn_init_device()) != cudaSuccess) return e;
     return cudaFuncSetAttribute(k_decode_attn<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)DecShape<float>::SMEM);
 }
@@ -525,6 +528,7 @@ __global__ void __launch_bounds__(PREF_QTILE) k_prefill_attn(const PrefAttnParam
 // + i]. That is exactly the A operand of P.V when k-step (t, i) takes keys 8t + 2k + i (k = 0..3): the
 // weights never move between lanes, and the V operand is read in that key order.
 constexpr int PA_KSTR = HD + 4;   // doubles per staged K / V row: the fragment loads are conflict-free
+constexpr size_t PA_SMEM = (size_t)4 * PREF_QTILE * PA_KSTR * 8;   // K and V, two tiles each
 
 __device__ __forceinline__ void dmma884(double& d0, double& d1, double a, double b) {
     asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0, %1}, {%2}, {%3}, {%0, %1};"
@@ -533,8 +537,10 @@ __device__ __forceinline__ void dmma884(double& d0, double& d1, double a, double
 }
 
 __global__ void __launch_bounds__(256) k_prefill_attn_mma(const PrefAttnParams p) {
-    __shared__ __align__(16) double Ks[PREF_QTILE][PA_KSTR];
-    __shared__ __align__(16) double Vs[PREF_QTILE][PA_KSTR];
+    // two key tiles: the next tile's K / V rows are loaded into registers while this one is used
+    extern __shared__ __align__(16) double pa_sm[];
+    double(*Ks)[PREF_QTILE][PA_KSTR] = (double(*)[PREF_QTILE][PA_KSTR])pa_sm;
+    double(*Vs)[PREF_QTILE][PA_KSTR] = (double(*)[PREF_QTILE][PA_KSTR])(pa_sm + 2 * PREF_QTILE * PA_KSTR);
     const int h = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int r = lane >> 2, c = lane & 3;   // fragment row (query) and column group
     griddep_wait();
@@ -544,6 +550,32 @@ __global__ void __launch_bounds__(256) k_prefill_attn_mma(const PrefAttnParams p
     const int start = p.seq_start[sq], S = p.seq_len[sq], T = p.text_len[sq];
     const int qi = q0 + warp * 8 + r;   // this lane's query row
     const bool valid = qi < S;
+    const int kend = (q0 + PREF_QTILE <= T) ? T : max(T, min(S, q0 + PREF_QTILE));
+    // thread tid stages float4 number tid and tid + 256 of the tile's 64 keys x 8 float4 (K and V)
+    float4 kr[2], vr[2];
+    auto fetch = [&](int kt) {
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            const int i = tid + 256 * u, key = i >> 3, d4 = (i & 7) * 4;
+            kr[u] = vr[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (kt + key < S) {
+                const float* src = p.qkv + (size_t)(start + kt + key) * 3 * D + D + h * HD + d4;
+                kr[u] = *(const float4*)src;
+                vr[u] = *(const float4*)(src + D);
+            }
+        }
+    };
+    auto put = [&](int b) {
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            const int i = tid + 256 * u, key = i >> 3, d4 = (i & 7) * 4;
+            *(double2*)&Ks[b][key][d4] = make_double2(kr[u].x, kr[u].y);
+            *(double2*)&Ks[b][key][d4 + 2] = make_double2(kr[u].z, kr[u].w);
+            *(double2*)&Vs[b][key][d4] = make_double2(vr[u].x, vr[u].y);
+            *(double2*)&Vs[b][key][d4 + 2] = make_double2(vr[u].z, vr[u].w);
+        }
+    };
+    fetch(0);
     double qa[HD / 4];                   // A fragments of Q: Q[qi][4 ks + c]
 #pragma unroll
     for (int ks = 0; ks < HD / 4; ks++)
@@ -553,23 +585,11 @@ __global__ void __launch_bounds__(256) k_prefill_attn_mma(const PrefAttnParams p
     double o[HD / 8][2];                 // O[qi][8 dn + 2c + e]
 #pragma unroll
     for (int dn = 0; dn < HD / 8; dn++) o[dn][0] = o[dn][1] = 0.0;
-    const int kend = (q0 + PREF_QTILE <= T) ? T : max(T, min(S, q0 + PREF_QTILE));
-    for (int kt = 0; kt < kend; kt += PREF_QTILE) {
-        __syncthreads();
-        for (int i = tid; i < PREF_QTILE * HD / 4; i += 256) {   // 64 keys x 8 float4 of K and of V
-            const int key = i >> 3, d4 = (i & 7) * 4;
-            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
-            if (kt + key < S) {
-                const float* kr = p.qkv + (size_t)(start + kt + key) * 3 * D + D + h * HD + d4;
-                kv = *(const float4*)kr;
-                vv = *(const float4*)(kr + D);
-            }
-            *(double2*)&Ks[key][d4] = make_double2(kv.x, kv.y);
-            *(double2*)&Ks[key][d4 + 2] = make_double2(kv.z, kv.w);
-            *(double2*)&Vs[key][d4] = make_double2(vv.x, vv.y);
-            *(double2*)&Vs[key][d4 + 2] = make_double2(vv.z, vv.w);
-        }
-        __syncthreads();
+    put(0);
+    int b = 0;
+    for (int kt = 0; kt < kend; kt += PREF_QTILE, b ^= 1) {
+        __syncthreads();   // tile b staged; every warp is done with tile b ^ 1
+        if (kt + PREF_QTILE < kend) fetch(kt + PREF_QTILE);
         // scores: n-tile t = keys kt + 8t .. +7
         float sc[8][2];
         float tmax = -INFINITY;
@@ -577,7 +597,7 @@ __global__ void __launch_bounds__(256) k_prefill_attn_mma(const PrefAttnParams p
         for (int t = 0; t < 8; t++) {
             double d0 = 0.0, d1 = 0.0;
 #pragma unroll
-            for (int ks = 0; ks < HD / 4; ks++) dmma884(d0, d1, qa[ks], Ks[8 * t + r][4 * ks + c]);
+            for (int ks = 0; ks < HD / 4; ks++) dmma884(d0, d1, qa[ks], Ks[b][8 * t + r][4 * ks + c]);
 #pragma unroll
             for (int e = 0; e < 2; e++) {
                 const int key = kt + 8 * t + 2 * c + e;
@@ -608,9 +628,11 @@ __global__ void __launch_bounds__(256) k_prefill_attn_mma(const PrefAttnParams p
                 const double pw = sc[t][e] == -INFINITY ? 0.0 : exp((double)sc[t][e] - (double)m);
                 lp += pw;
 #pragma unroll
-                for (int dn = 0; dn < HD / 8; dn++) dmma884(o[dn][0], o[dn][1], pw, Vs[8 * t + 2 * c + e][8 * dn + r]);
+                for (int dn = 0; dn < HD / 8; dn++)
+                    dmma884(o[dn][0], o[dn][1], pw, Vs[b][8 * t + 2 * c + e][8 * dn + r]);
             }
         }
+        if (kt + PREF_QTILE < kend) put(b ^ 1);
     }
     double l = lp;
     l += __shfl_xor_sync(0xffffffffu, l, 1);
@@ -643,10 +665,14 @@ __global__ void __launch_bounds__(256) k_prefill_attn_mma(const PrefAttnParams p
     }
 }
 
+cudaError_t prefill_attn_init_device() {
+    return cudaFuncSetAttribute(k_prefill_attn_mma, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PA_SMEM);
+}
+
 void launch_prefill_attention(const PrefAttnParams& p, cudaStream_t s) {
     if (p.n_tiles == 0) return;
     dim3 grid(NH, p.n_tiles);
-    if (p.fp64_mma) launch_pdl(k_prefill_attn_mma, grid, dim3(256), 0, s, p);
+    if (p.fp64_mma) launch_pdl(k_prefill_attn_mma, grid, dim3(256), PA_SMEM, s, p);
     else launch_pdl(k_prefill_attn, grid, dim3(PREF_QTILE), 0, s, p);
 }
 
