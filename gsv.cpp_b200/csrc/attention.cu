@@ -422,107 +422,15 @@ int launch_decode_attention(const DecAttnParams& p, cudaStream_t s) {
 }
 
 // ------------------------------------------------------------------ prefill
-// One thread per query row of one head; keys visited in order, softmax-weighted sum carried in
-// double and rounded once (see the decode kernel). Key/value tiles of 64 rows are staged in shared memory
-// and read as broadcasts. Mask (src/gsv_ar.cpp:215-223) in-tile: text query (qi < T) sees text keys
-// [0, T); semantic query sees keys [0, qi].
-__global__ void __launch_bounds__(PREF_QTILE) k_prefill_attn(const PrefAttnParams p) {
-    // the tile's K and V rows, widened to double once when loaded (the values every product uses)
-    __shared__ __align__(16) double Ks[PREF_QTILE][HD];
-    __shared__ __align__(16) double Vs[PREF_QTILE][HD];
-    const int h = blockIdx.x;
-    griddep_wait();
-    griddep_launch();
-    const PrefillTile tile = p.tiles[blockIdx.y];
-    const int sq = tile.seq, q0 = tile.q0;
-    const int start = p.seq_start[sq], S = p.seq_len[sq], T = p.text_len[sq];
-    const int qi = q0 + threadIdx.x;
-    const bool valid = qi < S;
-    double qd[HD];
-    float o[HD];
-#pragma unroll
-    for (int d = 0; d < HD; d++) qd[d] = valid ? (double)p.qkv[(size_t)(start + qi) * 3 * D + h * HD + d] : 0.0;
-    float m = -INFINITY;
-    double l = 0.0, od[HD];
-#pragma unroll
-    for (int d = 0; d < HD; d++) od[d] = 0.0;
-    const int kend = (q0 + PREF_QTILE <= T) ? T : max(T, min(S, q0 + PREF_QTILE));
-    for (int kt = 0; kt < kend; kt += PREF_QTILE) {
-        __syncthreads();
-        {
-            const int key = kt + threadIdx.x;
-            const float* kr = p.qkv + (size_t)(start + key) * 3 * D + D + h * HD;
-#pragma unroll
-            for (int d4 = 0; d4 < HD / 4; d4++) {
-                float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
-                if (key < S) {
-                    kv = *(const float4*)(kr + d4 * 4);
-                    vv = *(const float4*)(kr + D + d4 * 4);
-                }
-                *(double2*)&Ks[threadIdx.x][d4 * 4] = make_double2(kv.x, kv.y);
-                *(double2*)&Ks[threadIdx.x][d4 * 4 + 2] = make_double2(kv.z, kv.w);
-                *(double2*)&Vs[threadIdx.x][d4 * 4] = make_double2(vv.x, vv.y);
-                *(double2*)&Vs[threadIdx.x][d4 * 4 + 2] = make_double2(vv.z, vv.w);
-            }
-        }
-        __syncthreads();
-        const int nk = min(PREF_QTILE, kend - kt);
-        // four keys per step: four independent dot chains (each sequential over the dims), then the
-        // softmax updates in key order
-        for (int j0 = 0; j0 < nk; j0 += 4) {
-            double dot[4] = {0.0, 0.0, 0.0, 0.0};
-#pragma unroll
-            for (int d = 0; d < HD; d++) {
-#pragma unroll
-                for (int u = 0; u < 4; u++) dot[u] = fma(qd[d], Ks[j0 + u][d], dot[u]);
-            }
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int j = j0 + u, key = kt + j;
-                const bool vis = valid && j < nk && (qi < T ? key < T : key <= qi);
-                if (!vis) continue;
-                const float s = __fmul_rn((float)dot[u], p.scale);
-                if (s > m) {
-                    const double r = m == -INFINITY ? 0.0 : exp((double)m - (double)s);
-                    l *= r;
-#pragma unroll
-                    for (int d = 0; d < HD; d++) od[d] *= r;
-                    m = s;
-                }
-                const double pj = exp((double)s - (double)m);
-                l += pj;
-#pragma unroll
-                for (int d = 0; d < HD; d++) od[d] = fma(pj, Vs[j][d], od[d]);
-            }
-        }
-    }
-    if (!valid) return;
-    float amax = 0.0f;
-#pragma unroll
-    for (int d = 0; d < HD; d++) {
-        o[d] = l > 0.0 ? (float)(od[d] / l) : 0.0f;
-        amax = fmaxf(amax, fabsf(o[d]));
-    }
-    float dsc, id;
-    q8_scale(amax, dsc, id);
-    const size_t row = (size_t)(start + qi);
-    int8_t* qo = p.out_q + row * D + h * HD;
-#pragma unroll
-    for (int d = 0; d < HD; d++) qo[d] = q8_val(o[d], id);
-    p.out_d[row * (D / QK) + h] = f2h(dsc);
-    if (p.out_f32) {
-#pragma unroll
-        for (int d = 0; d < HD; d++) p.out_f32[row * D + h * HD + d] = o[d];
-    }
-}
-
-// The same attention on the FP64 tensor cores (mma.sync m8n8k4 .f64). Scores q.k are products exact in
-// double summed in double, rounded to float and scaled in float as above; the softmax weights
+// Mask (src/gsv_ar.cpp:215-223): a text query (qi < T) sees the text keys [0, T); a semantic query
+// sees the keys [0, qi].
+// Prefill attention on the FP64 tensor cores (mma.sync m8n8k4 .f64). Scores q.k are products exact in
+// double summed in double, rounded to float and scaled in float (ggml's order); the softmax weights
 // exp(s - m) and their sums and the weighted sum of V are carried in double and rounded once. The
-// running maximum is taken per 64-key tile instead of per key; in double the result differs from
-// the key-by-key form only at the 1e-16 level, so it rounds to the same float (except at a rounding
-// tie, as any change of double summation order).
-// CTA = 64 queries of one head of one sequence (the tiles of k_prefill_attn), 8 warps of 8 queries.
+// running maximum is taken per 64-key tile; in double the result differs from a key-by-key running
+// maximum only at the 1e-16 level, so it rounds to the same float (except at a rounding tie, as any
+// change of double summation order).
+// CTA = 64 queries of one head of one sequence (one PrefillTile), 8 warps of 8 queries.
 // Per 64-key tile, staged in shared memory as double: warp w computes its 8 x 64 score block as 8
 // n-tiles of 8 keys (8 k-steps of 4 dims each), lane holding S[row = lane / 4][key = 8t + 2 (lane % 4)
 // + i]. That is exactly the A operand of P.V when k-step (t, i) takes keys 8t + 2k + i (k = 0..3): the
@@ -672,8 +580,7 @@ cudaError_t prefill_attn_init_device() {
 void launch_prefill_attention(const PrefAttnParams& p, cudaStream_t s) {
     if (p.n_tiles == 0) return;
     dim3 grid(NH, p.n_tiles);
-    if (p.fp64_mma) launch_pdl(k_prefill_attn_mma, grid, dim3(256), PA_SMEM, s, p);
-    else launch_pdl(k_prefill_attn, grid, dim3(PREF_QTILE), 0, s, p);
+    launch_pdl(k_prefill_attn_mma, grid, dim3(256), PA_SMEM, s, p);
 }
 
 }  // namespace gsvcu

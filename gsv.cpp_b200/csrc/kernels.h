@@ -230,7 +230,6 @@ struct PrefAttnParams {
     int8_t* out_q = nullptr;
     uint16_t* out_d = nullptr;
     float* out_f32 = nullptr;
-    bool fp64_mma = true;                // FP64 tensor cores (k_prefill_attn_mma) or FP64 CUDA cores
 };
 constexpr int PREF_QTILE = 64;
 void launch_prefill_attention(const PrefAttnParams& p, cudaStream_t s);
