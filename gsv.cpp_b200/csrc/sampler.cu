@@ -44,17 +44,28 @@ __device__ __forceinline__ uint64_t xs_step(uint64_t s) {
 __global__ void __launch_bounds__(SAMP_T) k_sampler(const SamplerParams p) {
     const int slot = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    // the jump matrices (constant since initialisation) are staged before the wait for the logits,
-    // transposed to [bit][lane] so that the 32 lanes read 32 consecutive words
+    // Before the wait for the logits: the jump matrices (constant since initialisation), transposed to
+    // [bit][lane] so that the 32 lanes read 32 consecutive words, and the slot's state and repetition
+    // counts, which the previous step's sampler and step preparation wrote (two or more kernels ago).
     __shared__ uint64_t jmp[64 * 32];
     for (int e = tid; e < 64 * 32; e += SAMP_T) jmp[(e & 63) * 32 + (e >> 6)] = p.jump[e];
-    griddep_wait();
-    griddep_launch();
     SlotState* st = p.st + slot;
-    if (!st->active) return;
+    if (!st->active) {
+        griddep_wait();
+        return;
+    }
     const int V = p.V;
     const int top_k = st->top_k;
     const float top_p = st->top_p, temperature = st->temperature, rep = st->rep;
+    const uint16_t* cnt_row = p.counts + (size_t)slot * V;
+    int cnt4[(VMAX + SAMP_T - 1) / SAMP_T];   // this thread's counts, i = tid + SAMP_T * j
+#pragma unroll
+    for (int j = 0; j < (VMAX + SAMP_T - 1) / SAMP_T; j++) {
+        const int i = tid + SAMP_T * j;
+        cnt4[j] = (rep != 1.0f && i < V) ? cnt_row[i] : 0;
+    }
+    griddep_wait();
+    griddep_launch();
     __shared__ float lg[VMAX];
     __shared__ float pr[VMAX];
     __shared__ float sv[SORT_N];
@@ -72,9 +83,9 @@ __global__ void __launch_bounds__(SAMP_T) k_sampler(const SamplerParams p) {
 
     // 1) repetition penalty
     if (rep != 1.0f) {
-        const uint16_t* cnt = p.counts + (size_t)slot * V;
-        for (int i = tid; i < V; i += SAMP_T) {
-            const int c = cnt[i];
+#pragma unroll
+        for (int j = 0; j < (VMAX + SAMP_T - 1) / SAMP_T; j++) {
+            const int i = tid + SAMP_T * j, c = cnt4[j];
             if (c) {
                 float l = lg[i];
                 for (int r = 0; r < c; r++) l = l < 0.0f ? __fmul_rn(l, rep) : __fdiv_rn(l, rep);
@@ -219,13 +230,18 @@ __global__ void __launch_bounds__(SAMP_T) k_sampler(const SamplerParams p) {
         const int i0 = lane * dpl, i1 = min(V, i0 + dpl);
         for (int i = i0; i < i1; i++) {
             s = xs_step(s);
-            const uint64_t out = s * 0x2545F4914F6CDD1Dull;
-            const float U = (float)((double)(out >> 40) * (1.0 / 16777216.0));
-            const float pi = __fmul_rn(pr[i], inv);
+            // U = (xorshift64*() >> 40) / 2^24: a 24-bit integer times 2^-24, exact in float; only
+            // entries of non-zero probability need it (a zero weight gives v = 0)
+            const float pv = pr[i];
             float v = 0.0f;
-            if (pi > 0.0f) {
-                const float q = -log_f(__fsub_rn(1.0f, U));
-                v = __fdiv_rn(pi, q);
+            if (pv != 0.0f) {
+                const float pi = __fmul_rn(pv, inv);
+                if (pi > 0.0f) {
+                    const uint64_t out = s * 0x2545F4914F6CDD1Dull;
+                    const float U = __fmul_rn(__uint2float_rn((uint32_t)(out >> 40)), 1.0f / 16777216.0f);
+                    const float q = -log_f(__fsub_rn(1.0f, U));
+                    v = __fdiv_rn(pi, q);
+                }
             }
             if (best_i == 0x7fffffff || v > best_v) {   // first element of the range, then strict >
                 best_v = v;
