@@ -301,6 +301,53 @@ def _alone(orc, gctx, reqs, seeds, steps, **cfg):
     return out
 
 
+class _Recorder:
+    """A serving context (GPU or oracle) whose serve_step records every finished sequence by tag."""
+
+    def __init__(self, srv):
+        self.srv, self.done = srv, {}
+
+    def __getattr__(self, name):
+        return getattr(self.srv, name)
+
+    def serve_step(self, n, max_done, tok_cap):
+        out = self.srv.serve_step(n, max_done=max_done, tok_cap=tok_cap)
+        for d in out:
+            self.done[d["tag"]] = (d["finish_kind"], d["n_generated"], np.asarray(d["tokens"]).tolist())
+        return out
+
+
+def test_config4_job_prefix_matches_oracle(gctx, orc):
+    """The benchmarked configuration against the oracle: the first 96 iterations of bench.py's config-4
+    serving job (rank 0's job 2000: 64 slots, admission of 64 requests with prefixes U[80,400], refills
+    every 16 iterations from the same seeded queue, top_k 15 / rep 1.35 sampling with per-request seeds,
+    F16 paged KV), every sequence capped at 96 steps so that all finish inside the window. The job loop is
+    bench.job_chunks itself, driven once through the library and once through the oracle's serve loop
+    (its F16-KV emulation): every finished sequence (tokens, finish kind, count) and the token total
+    are equal."""
+    import argparse
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import bench
+    args = argparse.Namespace(slots=64, iters=96, refill_every=16, lookahead=False)
+    counters = {"h2d": 0, "d2h": 0, "seqs": 0}
+    _reserve(gctx, 0, slots=64, ctx=400 + 96 + 8)
+    g = _Recorder(gctx)
+    for _ in bench.job_chunks(g, bench.stage(bench.RequestStream(0, 2000), 64 * 3, "cuda"), args, counters):
+        pass
+    g_tokens, g_seqs = counters["tokens"], counters["seqs"]
+    counters = {"h2d": 0, "d2h": 0, "seqs": 0}
+    o = _Recorder(bench.OracleServing(orc, 64, 400 + 96 + 8, kv_f16=True))
+    for _ in bench.job_chunks(o, bench.stage(bench.RequestStream(0, 2000), 64 * 3, None), args, counters):
+        pass
+    print(f"config-4 job prefix: {g_seqs} sequences, {g_tokens} tokens (GPU) / {counters['seqs']}, "
+          f"{counters['tokens']} (oracle)")
+    assert g_seqs == counters["seqs"] and g_tokens == counters["tokens"]
+    assert sorted(g.done) == sorted(o.done) and len(g.done) == g_seqs
+    for tag in g.done:
+        assert g.done[tag] == o.done[tag], tag
+
+
 def test_serving_refill_equals_generate(gctx, orc):
     """Continuous batching: a sequence admitted into a refilled slot decodes exactly as the oracle
     generates it alone."""
