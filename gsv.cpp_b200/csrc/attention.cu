@@ -138,7 +138,8 @@ template <typename KT> struct DecShape {
 
 // One warp: the pinned-order softmax of one head over one staged page (n keys of K rows ks, V rows vs)
 // for query q (lane (g, s) holds dims 8s..8s+7); returns the page max m, sum l and o (lane's 8 dims).
-template <typename KT>
+// FULL: n == PAGE, so no key needs the bound test (straight-line code for the common, full pages).
+template <typename KT, bool FULL>
 __device__ __forceinline__ void page_softmax(const uint8_t* ks, const uint8_t* vs, int n, const float (&q)[8],
                                              float scale, float& m_out, float& l_out, float (&o)[8]) {
     using S = DecShape<KT>;
@@ -149,7 +150,7 @@ __device__ __forceinline__ void page_softmax(const uint8_t* ks, const uint8_t* v
     for (int u = 0; u < 8; u++) {
         const int t = 8 * u + g;
         float d = 0.0f;
-        if (t < n) {
+        if (FULL || t < n) {
             float kf[8];
             load8<KT>(ks + (size_t)t * S::ROWB + sub * 8 * sizeof(KT), kf);
 #pragma unroll
@@ -157,7 +158,7 @@ __device__ __forceinline__ void page_softmax(const uint8_t* ks, const uint8_t* v
         }
         d = __fadd_rn(d, __shfl_xor_sync(0xffffffffu, d, 1));
         d = __fadd_rn(d, __shfl_xor_sync(0xffffffffu, d, 2));
-        sc[u] = t < n ? __fmul_rn(d, scale) : -INFINITY;
+        sc[u] = (FULL || t < n) ? __fmul_rn(d, scale) : -INFINITY;
         m = fmaxf(m, sc[u]);
     }
 #pragma unroll
@@ -175,7 +176,7 @@ __device__ __forceinline__ void page_softmax(const uint8_t* ks, const uint8_t* v
     for (int u = 0; u < 8; u++) {
         const float pu = __shfl_sync(0xffffffffu, u < 4 ? pa : pb, 4 * g + (u & 3));
         const int t = 8 * u + g;
-        if (t < n) {
+        if (FULL || t < n) {
             float vf[8];
             load8<KT>(vs + (size_t)t * S::ROWB + sub * 8 * sizeof(KT), vf);
             l = __fadd_rn(l, pu);
@@ -274,7 +275,8 @@ __global__ void __launch_bounds__(128) k_decode_attn(const DecAttnParams p) {
     }
 
     float m, l, o[8];
-    page_softmax<KT>(ks, vs, n, q, p.scale, m, l, o);
+    if (n == PAGE) page_softmax<KT, true>(ks, vs, n, q, p.scale, m, l, o);
+    else page_softmax<KT, false>(ks, vs, n, q, p.scale, m, l, o);
     if (nkeys <= PAGE && !p.partials_only) {
         decode_write_out(p, slot, h, g, sub, o, l);
         return;
