@@ -126,6 +126,23 @@ def test_layer_outputs_teacher_forced(gctx, orc, kv):
         assert worst32.max() <= 2e-2
 
 
+def test_edge_prefixes_match_oracle(gctx, orc):
+    """Ragged extremes through prefill and 8 teacher-forced decode steps with the reference's F32 cache,
+    logits bit for bit: a one-phone / one-code prefix, no prompt codes, one phone before a long prompt,
+    one code after a long text, and a 2,000-position prefix (32 key tiles of prefill attention, 32 KV
+    pages merged per decode step)."""
+    rng = np.random.default_rng(77)
+    reqs = [S.make_request(rng, 1, 1), S.make_request(rng, 5, 0), S.make_request(rng, 1, 300),
+            S.make_request(rng, 300, 1), S.make_request(rng, 1400, 600)]
+    forced = rng.integers(0, 1024, (len(reqs), 8)).astype(np.int32)
+    _reserve(gctx, 1, slots=16, ctx=2100)
+    lg = gctx.debug_trace(reqs, forced)
+    ref = orc.decode_trace(reqs, forced, kv_f16=False)
+    for s in range(lg.shape[0]):
+        for b in range(lg.shape[1]):
+            assert np.array_equal(lg[s, b].view(np.uint32), ref[s, b].view(np.uint32)), (s, b)
+
+
 @pytest.mark.parametrize("kv", [1, 0])
 def test_decode_logits_trace(gctx, orc, kv):
     rng = np.random.default_rng(8)
