@@ -43,8 +43,8 @@ def parse():
     ap.add_argument("--kv", default="f16", choices=["f16", "f32"])
     ap.add_argument("--format", default="q8_0", choices=list(FORMATS),
                     help="model file of the serve workload: q8_0 (the exporter's --q8, the headline), f16 (its --f16 "
-                         "preset: F16 matrices, predict and embeddings), f32 (no flags) or q6_k (--spec "
-                         "attn=q8_0,ffn=q6_k,predict=f16,emb=f16)")
+                         "preset: F16 matrices, predict and embeddings), f32 (no flags), q6_k (--spec "
+                         "attn=q8_0,ffn=q6_k,predict=f16,emb=f16) or q4_1 (--spec attn=q4_1,ffn=q4_1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-chunks", type=int, default=3,
                     help="chunks (of --refill-every iterations) of the job the cpu_baseline sample runs")
@@ -646,6 +646,8 @@ FORMATS = {
     # the exporter's own example: --spec attn=q8_0,ffn=q6_k,predict=f16,emb=f16 (file bytes of the matrices)
     "q6_k": (dict(mat_type="q8_0", ffn_type="q6_k", predict_type="f16", emb_type="f16"), 69714944,
              "Q8_0 attn, Q6_K FFN, F16 predict/embeddings"),
+    # --spec attn=q4_1,ffn=q4_1 (the k_gemm_qm path), F32 predict
+    "q4_1": (dict(mat_type="q4_1"), 49924096, "Q4_1 attn/FFN, F32 predict"),
 }
 
 
@@ -777,7 +779,8 @@ def main():
         "warmup": args.warmup, "ms_per_step": ms_v / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None,
         "dtype": ("q8_0 int8 MMA" if args.format == "q8_0" else
-                  "q8_0 int8 MMA + q6_k dp2a" if args.format == "q6_k" else f"{args.format} weights / f32 FMA") +
+                  "q8_0 int8 MMA + q6_k dp2a" if args.format == "q6_k" else
+                  "q4_1 dp4a" if args.format == "q4_1" else f"{args.format} weights / f32 FMA") +
                  f" / f32 softmax / {args.kv} KV",
         "data": DATA,
         "config": serve_config(args, n_gpus),

@@ -204,7 +204,11 @@ __global__ void __launch_bounds__(128) k_gemm_fx(const GemmFxParams p) {
 // values (bytes since load) with the activation block, acc = acc + fma(d_w*d_x, sumi, m_w*s_x). K is a
 // multiple of 32, at most QM_KMAX.
 constexpr int QM_R = 32, QM_C = 8, QM_KMAX = 2048;
-constexpr size_t qm_smem_bytes(int K) { return (size_t)QM_C * K + (size_t)QM_R * (K + 16); }
+// shared memory: the columns' weights, the rows' Q8_1 values (padded rows), the rows' d and s
+// block-major, the columns' (d, m) block-major
+constexpr size_t qm_smem_bytes(int K) {
+    return (size_t)QM_C * K + (size_t)QM_R * (K + 16) + (size_t)(K / 32) * QM_R * 8 + (size_t)(K / 32) * QM_C * 8;
+}
 constexpr size_t QM_SMEM = qm_smem_bytes(QM_KMAX);
 
 __global__ void __launch_bounds__(256) k_quant_q8_1(const float* __restrict__ x, int ldx, int M, int K,
@@ -246,10 +250,18 @@ __global__ void __launch_bounds__(256) k_gemm_qm(const GemmFxParams p) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nb = p.K / 32, ldx = p.K + 16;
     uint8_t* ws = qm_smem;                                     // [8 columns][K]
     int8_t* xs = (int8_t*)(qm_smem + (size_t)QM_C * p.K);      // [32 rows][K + 16]
+    float* sd = (float*)(xs + (size_t)QM_R * ldx);              // [block][32 rows] d of the rows
+    float* ss = sd + nb * QM_R;                                 // [block][32 rows] s of the rows
+    float2* swm = (float2*)(ss + nb * QM_R);                    // [block][8 columns] (d, m) of the weights
     const int mt = blockIdx.y * QM_R, nt = blockIdx.x * QM_C;
-    for (int q = tid; q < QM_C * p.K / 16; q += 256) {   // weights: before the wait for the predecessor
+    // the weights and their scales do not depend on the predecessor: staged before its wait
+    for (int q = tid; q < QM_C * p.K / 16; q += 256) {
         const int c = q / (p.K / 16), part = q - c * (p.K / 16);
         fx_cp16(ws + (size_t)c * p.K + part * 16, (const uint8_t*)p.w + (size_t)min(nt + c, p.N - 1) * p.K + part * 16);
+    }
+    for (int i = tid; i < nb * QM_C; i += 256) {
+        const int b = i / QM_C, col = min(nt + i % QM_C, p.N - 1);
+        swm[i] = make_float2(h2f(p.wd[(size_t)col * nb + b]), h2f(p.wm[(size_t)col * nb + b]));
     }
     griddep_wait();
     griddep_launch();
@@ -257,14 +269,17 @@ __global__ void __launch_bounds__(256) k_gemm_qm(const GemmFxParams p) {
         const int r = q / (p.K / 16), part = q - r * (p.K / 16);
         fx_cp16(xs + (size_t)r * ldx + part * 16, p.qx_q + (size_t)min(mt + r, p.M - 1) * p.K + part * 16);
     }
+    for (int i = tid; i < nb * QM_R; i += 256) {
+        const int b = i / QM_R, row = min(mt + i % QM_R, p.M - 1);
+        sd[i] = p.qx_d[(size_t)row * nb + b];
+        ss[i] = ((const float*)p.qx_s)[(size_t)row * nb + b];
+    }
     asm volatile("cp.async.commit_group;\n cp.async.wait_group 0;" ::: "memory");
     __syncthreads();
     const int col = nt + warp, row = mt + lane;
     if (col >= p.N || row >= p.M) return;
     const int4* wl = (const int4*)(ws + (size_t)warp * p.K);
     const int4* xl = (const int4*)(xs + (size_t)lane * ldx);
-    const float* xdr = p.qx_d + (size_t)row * nb;
-    const float* xsr = (const float*)p.qx_s + (size_t)row * nb;
     float acc = 0.0f;
     for (int b = 0; b < nb; b++) {
         const int4 w0 = wl[2 * b], w1 = wl[2 * b + 1], x0 = xl[2 * b], x1 = xl[2 * b + 1];
@@ -276,8 +291,9 @@ __global__ void __launch_bounds__(256) k_gemm_qm(const GemmFxParams p) {
         sumi = __dp4a(w1.y, x1.y, sumi);
         sumi = __dp4a(w1.z, x1.z, sumi);
         sumi = __dp4a(w1.w, x1.w, sumi);
-        const float dd = __fmul_rn(h2f(__ldg(p.wd + (size_t)col * nb + b)), xdr[b]);
-        const float ms = __fmul_rn(h2f(__ldg(p.wm + (size_t)col * nb + b)), xsr[b]);
+        const float2 wm2 = swm[b * QM_C + warp];
+        const float dd = __fmul_rn(wm2.x, sd[b * QM_R + lane]);
+        const float ms = __fmul_rn(wm2.y, ss[b * QM_R + lane]);
         acc = __fadd_rn(acc, fmaf(dd, (float)sumi, ms));
     }
     fx_store<EPI>(p, row, col, acc);
