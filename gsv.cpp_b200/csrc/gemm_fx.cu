@@ -316,7 +316,10 @@ __global__ void __launch_bounds__(256) k_gemm_qm(const GemmFxParams p) {
 constexpr int QK_R = 32, QK_C = 8, QK_KMAX = 2048;
 // shared memory: the columns' weights, the rows' Q8_K values (padded rows), the int32 lane sums
 constexpr size_t qk_smem_bytes(int K) {
-    return (size_t)QK_C * K * 2 + (size_t)QK_R * (K + 16) + (size_t)QK_C * (K / 256) * 8 * QK_R * 4;
+    return (size_t)QK_C * K * 2 + (size_t)QK_R * (K + 16) + (size_t)QK_C * (K / 256) * 8 * QK_R * 4 +
+           (size_t)(K / 256) * QK_R * 4              // the rows' d, super-block-major
+           + (size_t)(K / 256) * QK_C * (8 + 8)      // the columns' (d, dmin) and 8 sub-block mins
+           + (size_t)(K / 16) * QK_R * 4;            // the rows' sums of 16, group-major
 }
 constexpr size_t QK_SMEM = qk_smem_bytes(QK_KMAX);
 
@@ -373,11 +376,21 @@ __global__ void __launch_bounds__(256) k_gemm_qk(const GemmFxParams p) {
     int16_t* ws = (int16_t*)qk_smem;                                  // [8 columns][K]
     int8_t* xs = (int8_t*)(qk_smem + (size_t)QK_C * p.K * 2);         // [32 rows][K + 16]
     int32_t* ls = (int32_t*)(xs + (size_t)QK_R * ldx);                // [column][super-block][lane 8][row 32]
+    float* sxd = (float*)(ls + (size_t)QK_C * nsb * 8 * QK_R);        // [super-block][row 32]
+    float2* swd = (float2*)(sxd + nsb * QK_R);                         // [super-block][column 8] (d, dmin)
+    uint2* smn = (uint2*)(swd + nsb * QK_C);                           // [super-block][column 8] mins
+    int32_t* sbs = (int32_t*)(smn + nsb * QK_C);                       // [group of 16][row 32]
     const int mt = blockIdx.y * QK_R, nt = blockIdx.x * QK_C;
-    // the columns' weights do not depend on the predecessor kernel: staged before its wait
+    // the columns' weights and scales do not depend on the predecessor kernel: staged before its wait
     for (int q = tid; q < QK_C * p.K / 8; q += 256) {
         const int c = q / (p.K / 8), part = q - c * (p.K / 8);
         fx_cp16(ws + (size_t)c * p.K + part * 8, (const int16_t*)p.w + (size_t)min(nt + c, p.N - 1) * p.K + part * 8);
+    }
+    for (int i = tid; i < nsb * QK_C; i += 256) {
+        const int sb = i / QK_C, col = min(nt + i % QK_C, p.N - 1);
+        const size_t e = (size_t)col * nsb + sb;
+        swd[i] = make_float2(h2f(p.wd[e]), p.wmins ? h2f(p.wm[e]) : 0.0f);
+        smn[i] = p.wmins ? *(const uint2*)(p.wmins + e * 8) : make_uint2(0u, 0u);
     }
     griddep_wait();
     griddep_launch();
@@ -385,6 +398,15 @@ __global__ void __launch_bounds__(256) k_gemm_qk(const GemmFxParams p) {
         const int r = q / (p.K / 16), part = q - r * (p.K / 16);
         fx_cp16(xs + (size_t)r * ldx + part * 16, p.qx_q + (size_t)min(mt + r, p.M - 1) * p.K + part * 16);
     }
+    for (int i = tid; i < nsb * QK_R; i += 256) {
+        const int sb = i / QK_R, row = min(mt + i % QK_R, p.M - 1);
+        sxd[i] = p.qx_d[(size_t)row * nsb + sb];
+    }
+    if (p.wmins)
+        for (int i = tid; i < (p.K / 16) * QK_R; i += 256) {
+            const int gg = i / QK_R, row = min(mt + i % QK_R, p.M - 1);
+            sbs[i] = ((const int32_t*)p.qx_s)[(size_t)row * (p.K / 16) + gg];
+        }
     asm volatile("cp.async.commit_group;\n cp.async.wait_group 0;" ::: "memory");
     __syncthreads();
     // (column, super-block) tasks: lane = row, the eight exact lane sums of the super-block; the 16 dp2a
@@ -422,27 +444,20 @@ __global__ void __launch_bounds__(256) k_gemm_qk(const GemmFxParams p) {
 #pragma unroll
     for (int l = 0; l < 8; l++) sums[l] = 0.0f;
     for (int sb = 0; sb < nsb; sb++) {
-        const float xds = p.qx_d[(size_t)row * nsb + sb];
-        const float dd = __fmul_rn(h2f(__ldg(p.wd + (size_t)col * nsb + sb)), xds);
+        const float xds = sxd[sb * QK_R + lane];
+        const float2 wdm = swd[sb * QK_C + warp];
+        const float dd = __fmul_rn(wdm.x, xds);
         const int32_t* lsb = ls + ((size_t)(warp * nsb + sb) * 8) * QK_R + lane;
 #pragma unroll
         for (int l = 0; l < 8; l++) sums[l] = fmaf(dd, (float)lsb[l * QK_R], sums[l]);
         if (p.wmins) {
-            const int4* bs4 = (const int4*)((const int32_t*)p.qx_s + (size_t)row * (p.K / 16) + sb * 16);
-            const uint2 m8 = __ldg((const uint2*)(p.wmins + ((size_t)col * nsb + sb) * 8));
+            const uint2 m8 = smn[sb * QK_C + warp];
             const uint32_t mw[2] = {m8.x, m8.y};
             int sumi = 0;
 #pragma unroll
-            for (int g4 = 0; g4 < 4; g4++) {
-                const int4 b = __ldg(bs4 + g4);
-                const int bg[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-                for (int k = 0; k < 4; k++) {
-                    const int g = g4 * 4 + k;
-                    sumi += bg[k] * (int)((mw[g >> 3] >> (8 * ((g >> 1) & 3))) & 0xff);
-                }
-            }
-            const float dmin = __fmul_rn(h2f(__ldg(p.wm + (size_t)col * nsb + sb)), xds);
+            for (int g = 0; g < 16; g++)
+                sumi += sbs[(sb * 16 + g) * QK_R + lane] * (int)((mw[g >> 3] >> (8 * ((g >> 1) & 3))) & 0xff);
+            const float dmin = __fmul_rn(wdm.y, xds);
             sumf = fmaf(-dmin, (float)sumi, sumf);
         }
     }
