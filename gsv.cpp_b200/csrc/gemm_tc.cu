@@ -34,6 +34,7 @@
 // memory.
 #include <cuda.h>
 
+#include <atomic>
 #include <cstdio>
 #include <mutex>
 
@@ -623,7 +624,7 @@ TcScratch carve(const GemmQ8Params& p) {
     return s;
 }
 
-int g_num_sms = 0;
+std::atomic<int> g_num_sms{0};   // SMs of the device (148 on B200): the persistent grid size
 
 }  // namespace
 
@@ -644,7 +645,9 @@ cudaError_t gemm_tc_init_device() {
     cudaError_t e;
     int dev = 0;
     if ((e = cudaGetDevice(&dev))) return e;
-    if ((e = cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev))) return e;
+    int sms = 0;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev))) return e;
+    g_num_sms.store(sms, std::memory_order_relaxed);
 #define GSVCU_TC_SMEM(EPI_, KBM_)                                                                                \
     if ((e = cudaFuncSetAttribute(k_gemm_q8_tc<EPI_, KBM_>, cudaFuncAttributeMaxDynamicSharedMemorySize,          \
                                   (int)TcLayout<KBM_>::SMEM)))                                                   \
@@ -666,12 +669,12 @@ bool launch_gemm_q8_tc(const GemmQ8Params& p, int epi, cudaStream_t s) {
     if (KB <= 16 && epi != EPI_RELU_Q8 && !make_map_out(&maps.y, p.y, p.M, p.N)) return false;
     {   // the activation side: fp16 integers and both transposed scale planes
         const size_t n16 = (size_t)p.M * p.K / 16, work = n16 + (size_t)KB * ((size_t)p.M + p.N);
-        const int blocks = (int)std::min<size_t>((work + 255) / 256, (size_t)std::max(g_num_sms, 1) * 8);
+        const int blocks = (int)std::min<size_t>((work + 255) / 256, (size_t)std::max(g_num_sms.load(), 1) * 8);
         launch_pdl(k_tc_prep, dim3(std::max(blocks, 1)), dim3(256), 0, s, p.xq, sc.x16, n16, p.xd, p.M, KB, sc.dxT,
                    ld, p.wd, p.N, sc.dwT);
     }
     const int ntiles = (p.N / TC_BM) * ((p.M + TC_BN - 1) / TC_BN);
-    const dim3 grid(std::max(1, std::min(ntiles, std::max(g_num_sms, 1))));
+    const dim3 grid(std::max(1, std::min(ntiles, std::max(g_num_sms.load(), 1))));
 #define GSVCU_TC_LAUNCH(KBM_)                                                                                          \
     switch (epi) {                                                                                                 \
         case EPI_BIAS: launch_pdl(k_gemm_q8_tc<EPI_BIAS, KBM_>, grid, dim3(TC_THREADS), TcLayout<KBM_>::SMEM, s, maps, p); break; \
