@@ -1,0 +1,1180 @@
+// dit.cu -- the v5 DiT / CFM velocity estimator (reference src/gsv_dit.cpp, class gsv_dit) on B200.
+//
+// One estimator pass (gsv_dit::velocity, src/gsv_dit.cpp:1325; graph build_step :592-620):
+//   x   = proj_mel(x_mel) + condition                      (build_trunk :533-549, static cache :508-516)
+//   x  += mask * Mish(conv2(Mish(conv1(mask * x))))        (grouped conv1d k=31, 16 groups, :195-217)
+//   22 x DiTBlock: AdaLN-Zero(t) -> QKV (RoPE on head 0) -> attention -> to_out * mask, gated residual
+//                  -> AdaLN -> FFN (GELU tanh) -> gated residual                         (:286-433)
+//   vel = proj_out(LN(x) * (1 + scale) + shift)            (build_head :563-576)
+// and the CFM Euler loop with classifier-free guidance (gsv_dit::sample, :1410-1478). The positive and
+// the negative (unconditional) branch share x_mel and t and differ only in the condition rows, so a
+// guided step runs both as one batch of 2T rows.
+//
+// Kernels (sm_100a):
+//   k_dit_gemm    every linear layer and both convolutions: a tcgen05.mma kind::f16 GEMM, f16 operands
+//                 staged by TMA (128-byte swizzle, no multicast), f32 accumulator in TMEM (128 frames x BN
+//                 features per CTA), fused epilogues (bias, GELU / Mish, RoPE of head 0, gated and
+//                 masked residual add into the f32 hidden state, condition add). The convolutions are
+//                 implicit GEMMs: K runs over the 31 taps x 64 input channels of a group, and the tap's
+//                 activation tile is a TMA load at frame offset tap - 15 of a 3D [branch][frame][channel]
+//                 map, whose out-of-range frames read as zero (the conv's zero padding, per branch).
+//   k_dit_attn    16 heads x 64 dims, non-causal, key padding mask: flash attention on mma.sync
+//                 m16n8k16 f16 with f32 accumulators and an online softmax.
+//   k_dit_lnmod   LayerNorm (eps 1e-6, no affine) * (1 + scale) + shift -> f16 GEMM operand.
+//   k_dit_gemv    the time MLP and every block's AdaLN projection (one launch for all blocks per step).
+//   small kernels for the mel packing, the masked conv input and the Euler / guidance update.
+// Numerics: f16 GEMM operands (what ggml's mul_mat does with F16 weights: the activations are
+// converted to F16 first), f32 accumulation, f32 elsewhere; parity with the CPU restatement is within
+// a relative L2 tolerance, not bitwise.
+#include <cuda.h>
+#include <cuda_fp16.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "gguf_reader.h"
+#include "gsvcu.h"
+#include "kernels.h"
+#include "tc_common.cuh"
+
+namespace gsvcu {
+namespace dit {
+
+using namespace tc;
+
+constexpr int DM = 1024;          // dim
+constexpr int NHD = 16;           // heads
+constexpr int HDD = 64;           // head dim
+constexpr int MEL = 100;          // mel channels
+constexpr int MELP = 128;         // mel channels padded (GEMM K)
+constexpr int FFD = 2048;         // FFN width
+constexpr int ADA = 6 * DM;       // AdaLN-Zero modulation per block
+constexpr int KCP = 31;           // conv_pos kernel
+constexpr int GCP = 16;           // conv_pos groups
+constexpr int ICG = 64;           // channels per group
+constexpr int KCONV = KCP * ICG;  // conv GEMM K per group (tap-major)
+constexpr int TSIN = 256;         // sinusoidal time features
+constexpr float LN_EPS = 1e-6f;
+constexpr float ATTN_SCALE = 0.125f;   // 1/sqrt(64)
+
+// ------------------------------------------------------------------ tcgen05 GEMM
+constexpr int GM = 128;           // frames per tile (UMMA M, TMEM lanes)
+constexpr int GK = 64;            // K per stage (one 128-byte swizzle row of f16)
+constexpr int GS = 3;             // stages (about 97 KB of shared memory: two CTAs per SM)
+constexpr int G_THREADS = 192;    // warp 0 TMA, warp 1 TMEM + MMA, warps 2-5 epilogue
+
+enum { DE_F16 = 0, DE_QKV = 1, DE_RESID = 2, DE_F32 = 3 };
+enum { ACT_NONE = 0, ACT_GELU_TANH = 1, ACT_MISH = 2 };
+
+struct DitGemmArgs {
+    int R;                  // rows (frames of every branch)
+    int T;                  // frames per branch (row r is frame r % T of branch r / T)
+    int N, K;
+    int act;
+    const float* bias;      // [N] or null
+    __half* out16;          // DE_F16 / DE_QKV: [R][ld]
+    float* out32;           // DE_RESID (in place) / DE_F32: [R][ld]
+    int ld;
+    const float* add;       // DE_F32: [R][ld] addend or null
+    const float* gate;      // DE_RESID: [N] per-feature gate or null (1)
+    int x_lens;             // DE_RESID with mask: frames >= x_lens add nothing
+    int use_mask;
+    const float* rcos;      // DE_QKV: [T][32] RoPE tables of head 0
+    const float* rsin;
+    int* err;
+};
+
+template <int BN>
+struct GemmSmem {
+    static constexpr int STAGE_A = GM * GK * 2;
+    static constexpr int STAGE_B = BN * GK * 2;
+    static constexpr size_t OFF_B = (size_t)GS * STAGE_A;
+    static constexpr size_t OFF_BAR = OFF_B + (size_t)GS * STAGE_B;
+    static constexpr size_t SMEM = OFF_BAR + (2 * GS + 1) * 8 + 16 + 1024;   // + slack for the 1024 alignment
+};
+
+__device__ __forceinline__ float act_f(float v, int act) {
+    if (act == ACT_GELU_TANH) {   // torch GELU(approximate="tanh")
+        const float u = 0.7978845608028654f * (v + 0.044715f * v * v * v);
+        return 0.5f * v * (1.0f + tanhf(u));
+    }
+    if (act == ACT_MISH) {        // x * tanh(softplus(x)), softplus with torch's threshold 20
+        const float sp = v > 20.0f ? v : log1pf(expf(v));
+        return v * tanhf(sp);
+    }
+    return v;
+}
+
+// D[frames][features] = A[frames][K] . B[features][K]^T, K-major f16 operands. CONV: A is the 3D map
+// [branch][frame][1024] and stage s is tap s of group blockIdx.x (channels 64 g .. 64 g + 63).
+template <int EPI, int BN, bool CONV>
+__global__ void __launch_bounds__(G_THREADS) k_dit_gemm(const __grid_constant__ CUtensorMap ma,
+                                                        const __grid_constant__ CUtensorMap mb, const DitGemmArgs p) {
+    using L = GemmSmem<BN>;
+    constexpr uint32_t IDESC = idesc_f16(GM, BN);
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* sm = smem_raw + ((1024u - (su32(smem_raw) & 1023u)) & 1023u);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t bar0 = su32(sm + L::OFF_BAR);
+    auto full = [&](int s) { return bar0 + 8u * s; };
+    auto empty = [&](int s) { return bar0 + 8u * (GS + s); };
+    const uint32_t tfull = bar0 + 8u * (2 * GS);
+    uint32_t* tmem_slot = (uint32_t*)(sm + L::OFF_BAR + (2 * GS + 1) * 8);
+    volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+
+    const int n0 = blockIdx.x * BN;
+    int row0, branch = 0, f0 = 0;
+    if (CONV) {
+        const int tpb = (p.T + GM - 1) / GM;
+        branch = blockIdx.y / tpb;
+        f0 = (blockIdx.y % tpb) * GM;
+        row0 = branch * p.T + f0;
+    } else {
+        row0 = blockIdx.y * GM;
+    }
+    const int nstage = CONV ? KCP : p.K / GK;
+
+    if (tid == 0) {
+        for (int s = 0; s < GS; s++) { bar_init(full(s), 1); bar_init(empty(s), 1); }
+        bar_init(tfull, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&ma) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&mb) : "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_slot)),
+                     "r"(BN)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    griddep_wait();
+    griddep_launch();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {   // TMA producer
+            int ks = 0;
+            for (; ks < nstage; ks++) {
+                const int s = ks % GS;
+                if (!bar_wait(empty(s), ((uint32_t)(ks / GS) & 1u) ^ 1u, abort_flag)) break;
+                bar_expect_tx(full(s), L::STAGE_A + L::STAGE_B);
+                const uint32_t da = su32(sm + (size_t)s * L::STAGE_A), db = su32(sm + L::OFF_B + (size_t)s * L::STAGE_B);
+                if (CONV) {
+                    tma_load_3d(da, &ma, n0, f0 + ks - KCP / 2, branch, full(s));
+                    tma_load_2d(db, &mb, ks * GK, n0, full(s));
+                } else {
+                    tma_load_2d(da, &ma, ks * GK, row0, full(s));
+                    tma_load_2d(db, &mb, ks * GK, n0, full(s));
+                }
+            }
+            if (ks < nstage) {
+                if (p.err) atomicExch(p.err, 1);
+                *abort_flag = 1;
+            }
+            // the copies issued have landed before the CTA may exit (bounded)
+            for (int k = ks - 1; k >= 0 && k >= ks - GS; k--)
+                for (uint32_t it = 0; it < TC_POLL_LIMIT; it++)
+                    if (bar_try(full(k % GS), (uint32_t)(k / GS) & 1u)) break;
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {   // MMA issuer
+            int ks = 0;
+            for (; ks < nstage; ks++) {
+                const int s = ks % GS;
+                if (!bar_wait(full(s), (uint32_t)(ks / GS) & 1u, abort_flag)) break;
+                tc_fence_after();
+                const uint32_t a = su32(sm + (size_t)s * L::STAGE_A), b = su32(sm + L::OFF_B + (size_t)s * L::STAGE_B);
+#pragma unroll
+                for (int kk = 0; kk < GK / 16; kk++)
+                    umma_f16(tmem, umma_desc(a + 32u * kk), umma_desc(b + 32u * kk), IDESC, (uint32_t)(ks | kk));
+                umma_commit(empty(s));
+            }
+            if (ks < nstage) {
+                if (p.err) atomicExch(p.err, 1);
+                *abort_flag = 1;
+            }
+            umma_commit(tfull);   // every MMA issued above has completed when tfull completes
+            for (uint32_t it = 0; it < TC_POLL_LIMIT; it++)
+                if (bar_try(tfull, 0)) break;
+        }
+    } else {
+        // epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 = frames of this tile
+        const int q = warp & 3;
+        const int fr = 32 * q + lane;   // frame (row) within the tile
+        int row;
+        bool valid;
+        if (CONV) {
+            valid = f0 + fr < p.T;
+            row = row0 + fr;
+        } else {
+            row = row0 + fr;
+            valid = row < p.R;
+        }
+        const bool ok = bar_wait_warp(tfull, 0, abort_flag) && !*abort_flag;
+        tc_fence_after();
+        if (ok) {
+            const int t = row % p.T;
+            const float mask = (EPI == DE_RESID && p.use_mask && t >= p.x_lens) ? 0.0f : 1.0f;
+            const uint32_t tb = tmem + ((uint32_t)(32 * q) << 16);
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 16) {
+                float v[16];
+                __syncwarp();   // converged for the .sync.aligned TMEM load
+                tmem_ld16(tb + (uint32_t)c, v);
+                tmem_wait_ld();
+                tmem_bind(v);
+                const int f = n0 + c;
+                if (p.bias) {
+#pragma unroll
+                    for (int i = 0; i < 16; i += 4) {
+                        const float4 b4 = __ldg((const float4*)(p.bias + f + i));
+                        v[i] += b4.x; v[i + 1] += b4.y; v[i + 2] += b4.z; v[i + 3] += b4.w;
+                    }
+                }
+                if (valid) {
+                if (EPI == DE_QKV && (n0 == 0 || n0 == DM) && c < HDD) {
+                    // RoPE on head 0 of q and k: pairs (2i, 2i + 1) share angle t * inv_freq[i]
+#pragma unroll
+                    for (int i = 0; i < 16; i += 2) {
+                        const int pi = (c + i) >> 1;
+                        const float cs = __ldg(p.rcos + (size_t)t * 32 + pi), sn = __ldg(p.rsin + (size_t)t * 32 + pi);
+                        const float x0 = v[i], x1 = v[i + 1];
+                        v[i] = x0 * cs - x1 * sn;
+                        v[i + 1] = x0 * sn + x1 * cs;
+                    }
+                }
+                if (EPI == DE_F16 || EPI == DE_QKV) {
+                    uint32_t w[8];
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        const __half2 h = __floats2half2_rn(act_f(v[2 * i], p.act), act_f(v[2 * i + 1], p.act));
+                        w[i] = *(const uint32_t*)&h;
+                    }
+                    uint4* dst = (uint4*)(p.out16 + (size_t)row * p.ld + f);
+                    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+                } else if (EPI == DE_RESID) {
+                    float4* dst = (float4*)(p.out32 + (size_t)row * p.ld + f);
+#pragma unroll
+                    for (int i = 0; i < 16; i += 4) {
+                        float4 x = dst[i / 4];
+                        float g[4] = {1.0f, 1.0f, 1.0f, 1.0f};
+                        if (p.gate) {
+                            const float4 g4 = __ldg((const float4*)(p.gate + f + i));
+                            g[0] = g4.x; g[1] = g4.y; g[2] = g4.z; g[3] = g4.w;
+                        }
+                        x.x += act_f(v[i], p.act) * mask * g[0];
+                        x.y += act_f(v[i + 1], p.act) * mask * g[1];
+                        x.z += act_f(v[i + 2], p.act) * mask * g[2];
+                        x.w += act_f(v[i + 3], p.act) * mask * g[3];
+                        dst[i / 4] = x;
+                    }
+                } else {   // DE_F32
+                    float4* dst = (float4*)(p.out32 + (size_t)row * p.ld + f);
+                    const float4* ad = p.add ? (const float4*)(p.add + (size_t)row * p.ld + f) : nullptr;
+#pragma unroll
+                    for (int i = 0; i < 16; i += 4) {
+                        float4 y = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+                        if (ad) {
+                            const float4 a4 = ad[i / 4];
+                            y.x += a4.x; y.y += a4.y; y.z += a4.z; y.w += a4.w;
+                        }
+                        dst[i / 4] = y;
+                    }
+                }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN) : "memory");
+    }
+}
+
+// ------------------------------------------------------------------ attention
+constexpr int AQ = 64;     // queries per CTA (4 warps x 16)
+constexpr int AKT = 64;    // keys per tile
+constexpr int AST = 72;    // shared row stride in halves (conflict-free ldmatrix)
+
+__device__ __forceinline__ void ldsm_x4(uint32_t a, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(a));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t a, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(a));
+}
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool pred) {
+    const int n = pred ? 16 : 0;   // zero-fill when the row is out of range
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n) : "memory");
+}
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *(const uint32_t*)&h;
+}
+
+// qkv: [R][3072] f16 (q | k | v, head h at columns 64 h of each), rows b T + t. out: [R][1024] f16.
+// grid (ceil(T / 64), 16 heads, branches); keys t >= x_lens are masked out.
+__global__ void __launch_bounds__(128) k_dit_attn(const __half* __restrict__ qkv, __half* __restrict__ out, int T,
+                                                  int x_lens) {
+    __shared__ __align__(16) __half sq[AQ * AST];
+    __shared__ __align__(16) __half sk[2][AKT * AST];
+    __shared__ __align__(16) __half sv[2][AKT * AST];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int q0 = blockIdx.x * AQ, h = blockIdx.y, b = blockIdx.z;
+    const size_t rbase = (size_t)b * T;
+    const __half* Q = qkv + h * HDD;
+    const __half* Kp = qkv + DM + h * HDD;
+    const __half* Vp = qkv + 2 * DM + h * HDD;
+    griddep_wait();
+    griddep_launch();
+    // Q tile and the first K / V tile: 64 rows x 128 bytes = 512 chunks of 16 bytes, 4 per thread each
+    auto load_rows = [&](__half* dst, const __half* src, int r0, int rlim) {
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int ch = tid + 128 * i, r = ch >> 3, c = ch & 7;
+            const bool in = r0 + r < rlim;
+            const __half* g = src + (rbase + (size_t)(in ? r0 + r : 0)) * (3 * DM) + c * 8;
+            cp_async16((uint32_t)__cvta_generic_to_shared(dst + r * AST + c * 8), g, in);
+        }
+    };
+    const int nkt = (x_lens + AKT - 1) / AKT;
+    load_rows(sq, Q, q0, T);
+    load_rows(sk[0], Kp, 0, x_lens);
+    load_rows(sv[0], Vp, 0, x_lens);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+
+    const float sl2 = ATTN_SCALE * 1.4426950408889634f;   // scale * log2(e)
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;   // rows g and g + 8 of the warp's 16
+    float o[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+    uint32_t qa[4][4];   // Q fragments of the 4 k-steps (64 dims)
+    const int g = lane >> 2, tq = lane & 3;
+
+    for (int kt = 0; kt < nkt; kt++) {
+        const int buf = kt & 1;
+        if (kt + 1 < nkt) {
+            load_rows(sk[buf ^ 1], Kp, (kt + 1) * AKT, x_lens);
+            load_rows(sv[buf ^ 1], Vp, (kt + 1) * AKT, x_lens);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+        __syncthreads();
+        if (kt == 0) {
+#pragma unroll
+            for (int ks = 0; ks < 4; ks++) {
+                const int r = 16 * warp + (lane & 15), c = 16 * ks + 8 * (lane >> 4);
+                ldsm_x4((uint32_t)__cvta_generic_to_shared(sq + r * AST + c), qa[ks][0], qa[ks][1], qa[ks][2],
+                        qa[ks][3]);
+            }
+        }
+        // S = Q K^T: 16 queries x 64 keys per warp, 8 key blocks of 8
+        float s[8][4];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.0f;
+#pragma unroll
+            for (int kp = 0; kp < 2; kp++) {   // two k-steps per x4 load
+                uint32_t b0, b1, b2, b3;
+                const int key = 8 * j + (lane & 7), dim = 32 * kp + 8 * (lane >> 3);
+                ldsm_x4((uint32_t)__cvta_generic_to_shared(sk[buf] + key * AST + dim), b0, b1, b2, b3);
+                mma16816(s[j], qa[2 * kp][0], qa[2 * kp][1], qa[2 * kp][2], qa[2 * kp][3], b0, b1);
+                mma16816(s[j], qa[2 * kp + 1][0], qa[2 * kp + 1][1], qa[2 * kp + 1][2], qa[2 * kp + 1][3], b2, b3);
+            }
+        }
+        // mask, row max, online softmax (base 2)
+        float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int key = kt * AKT + 8 * j + 2 * tq;
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const bool in = key + e < x_lens;
+                s[j][e] = in ? s[j][e] * sl2 : -INFINITY;
+                s[j][2 + e] = in ? s[j][2 + e] * sl2 : -INFINITY;
+                mx0 = fmaxf(mx0, s[j][e]);
+                mx1 = fmaxf(mx1, s[j][2 + e]);
+            }
+        }
+#pragma unroll
+        for (int off = 1; off <= 2; off <<= 1) {
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+        }
+        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);   // finite: every tile has a valid key
+        const float c0 = exp2f(m0 - mn0), c1 = exp2f(m1 - mn1);
+        m0 = mn0;
+        m1 = mn1;
+        float rs0 = 0.0f, rs1 = 0.0f;
+        uint32_t pa[4][4];   // P as the A fragments of the 4 k-steps (64 keys)
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const float p0 = exp2f(s[j][0] - mn0), p1 = exp2f(s[j][1] - mn0);
+            const float p2 = exp2f(s[j][2] - mn1), p3 = exp2f(s[j][3] - mn1);
+            rs0 += p0 + p1;
+            rs1 += p2 + p3;
+            pa[j >> 1][(j & 1) * 2] = pack_h2(p0, p1);
+            pa[j >> 1][(j & 1) * 2 + 1] = pack_h2(p2, p3);
+        }
+        l0 = l0 * c0 + rs0;
+        l1 = l1 * c1 + rs1;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            o[j][0] *= c0; o[j][1] *= c0;
+            o[j][2] *= c1; o[j][3] *= c1;
+        }
+        // O += P V: V [key][dim] -> B fragments by transposed loads
+#pragma unroll
+        for (int ks = 0; ks < 4; ks++) {
+#pragma unroll
+            for (int jp = 0; jp < 4; jp++) {   // two dim blocks per x4 load
+                uint32_t b0, b1, b2, b3;
+                const int mtx = lane >> 3;
+                const int key = 16 * ks + (mtx & 1) * 8 + (lane & 7), dim = 16 * jp + 8 * (mtx >> 1);
+                ldsm_x4_t((uint32_t)__cvta_generic_to_shared(sv[buf] + key * AST + dim), b0, b1, b2, b3);
+                mma16816(o[2 * jp], pa[ks][0], pa[ks][1], pa[ks][2], pa[ks][3], b0, b1);
+                mma16816(o[2 * jp + 1], pa[ks][0], pa[ks][1], pa[ks][2], pa[ks][3], b2, b3);
+            }
+        }
+        __syncthreads();   // this buffer is refilled two tiles on
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+#pragma unroll
+    for (int off = 1; off <= 2; off <<= 1) {
+        l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+    }
+    const float i0 = 1.0f / l0, i1 = 1.0f / l1;
+    const int qa0 = q0 + 16 * warp + g, qa1 = qa0 + 8;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const int dim = h * HDD + 8 * j + 2 * tq;
+        if (qa0 < T) *(uint32_t*)(out + (rbase + qa0) * DM + dim) = pack_h2(o[j][0] * i0, o[j][1] * i0);
+        if (qa1 < T) *(uint32_t*)(out + (rbase + qa1) * DM + dim) = pack_h2(o[j][2] * i1, o[j][3] * i1);
+    }
+}
+
+// ------------------------------------------------------------------ row kernels
+// LayerNorm (no affine, eps 1e-6) * (1 + scale) + shift of each 1024-wide row -> f16. Warp per row.
+__global__ void __launch_bounds__(256) k_dit_lnmod(const float* __restrict__ x, int R, const float* __restrict__ shift,
+                                                   const float* __restrict__ scale, __half* __restrict__ out) {
+    griddep_wait();
+    griddep_launch();
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= R) return;
+    const float4* xr = (const float4*)(x + (size_t)row * DM);
+    float4 v[8];
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        v[i] = xr[lane + 32 * i];
+        s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    const float mean = s * (1.0f / DM);
+    float q = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+        q += (a * a + b * b) + (c * c + d * d);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) q += __shfl_xor_sync(0xffffffffu, q, off);
+    const float rstd = 1.0f / sqrtf(q * (1.0f / DM) + LN_EPS);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int c = 4 * (lane + 32 * i);
+        const float4 sc = __ldg((const float4*)(scale + c)), sh = __ldg((const float4*)(shift + c));
+        const float y0 = (v[i].x - mean) * rstd * (1.0f + sc.x) + sh.x;
+        const float y1 = (v[i].y - mean) * rstd * (1.0f + sc.y) + sh.y;
+        const float y2 = (v[i].z - mean) * rstd * (1.0f + sc.z) + sh.z;
+        const float y3 = (v[i].w - mean) * rstd * (1.0f + sc.w) + sh.w;
+        *(uint2*)(out + (size_t)row * DM + c) = make_uint2(pack_h2(y0, y1), pack_h2(y2, y3));
+    }
+}
+
+// f16(x * mask) of every row (the conv input).
+__global__ void __launch_bounds__(256) k_dit_mask16(const float* __restrict__ x, int R, int T, int x_lens,
+                                                    __half* __restrict__ out) {
+    griddep_wait();
+    griddep_launch();
+    const size_t n4 = (size_t)R * DM / 4;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+        const int row = (int)(i / (DM / 4));
+        const float m = (row % T) < x_lens ? 1.0f : 0.0f;
+        const float4 v = ((const float4*)x)[i];
+        ((uint2*)out)[i] = make_uint2(pack_h2(v.x * m, v.y * m), pack_h2(v.z * m, v.w * m));
+    }
+}
+
+// x_mel [100][T] f32 (torch layout) -> rows b T + t of [R][128] f16, channels 100..127 zero.
+__global__ void __launch_bounds__(256) k_dit_pack_mel(const float* __restrict__ xm, int T, int B, __half* __restrict__ out) {
+    griddep_wait();
+    griddep_launch();
+    const int n = B * T * MELP;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const int c = i / (B * T), r = i - c * (B * T), t = r % T;
+        out[(size_t)r * MELP + c] = __float2half_rn(c < MEL ? xm[(size_t)c * T + t] : 0.0f);
+    }
+}
+
+// Euler step with guidance (gsv_dit::sample, src/gsv_dit.cpp:1464-1469): v = vel + (vel - neg) * cfg
+// (branch 1 rows hold neg when guided), x += dt * v, then the prompt frames are zeroed.
+// update = 0: only the zeroing (before the first step).
+__global__ void __launch_bounds__(256) k_dit_euler(const float* __restrict__ vel, int T, int update, int guided, float cfg,
+                                                   float dt, int P, float* __restrict__ xm) {
+    griddep_wait();
+    griddep_launch();
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < MEL * T; i += gridDim.x * blockDim.x) {
+        const int c = i / T, t = i - c * T;
+        float x = xm[i];
+        if (update) {
+            float v = vel[(size_t)t * MELP + c];
+            if (guided) {
+                const float ng = vel[(size_t)(T + t) * MELP + c];
+                v = v + (v - ng) * cfg;
+            }
+            x = x + dt * v;
+        }
+        xm[i] = t < P ? 0.0f : x;
+    }
+}
+
+// [T][128] f32 rows -> vel [100][T] (torch layout).
+__global__ void __launch_bounds__(256) k_dit_vel_out(const float* __restrict__ vel, int T, float* __restrict__ out) {
+    griddep_wait();
+    griddep_launch();
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < MEL * T; i += gridDim.x * blockDim.x) {
+        const int c = i / T, t = i - c * T;
+        out[i] = vel[(size_t)t * MELP + c];
+    }
+}
+
+// y[n] = W[n] . f16(f(in)) + b[n] (f = SiLU when SILU_IN), then SiLU when SILU_OUT. W f16 [N][K], K <= 1024
+// and a multiple of 8. Warp per output, 16-byte weight loads.
+template <bool SILU_IN, bool SILU_OUT>
+__global__ void __launch_bounds__(256) k_dit_gemv(const __half* __restrict__ W, const float* __restrict__ bias,
+                                                  const float* __restrict__ in, int N, int K, float* __restrict__ y) {
+    __shared__ float sx[DM];
+    griddep_wait();
+    griddep_launch();
+    for (int k = threadIdx.x; k < K; k += blockDim.x) {
+        const float v = in[k];
+        // ggml's mul_mat with an F16 weight converts the activations to F16 first
+        sx[k] = __half2float(__float2half_rn(SILU_IN ? v / (1.0f + expf(-v)) : v));
+    }
+    __syncthreads();
+    const int n = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (n >= N) return;
+    const uint4* wr = (const uint4*)(W + (size_t)n * K);
+    float acc = 0.0f;
+    for (int c = lane; c < K / 8; c += 32) {
+        const uint4 w = __ldg(wr + c);
+        const __half2* h = (const __half2*)&w;
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const float2 f = __half22float2(h[e]);
+            acc += f.x * sx[8 * c + 2 * e] + f.y * sx[8 * c + 2 * e + 1];
+        }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (lane == 0) {
+        const float v = acc + (bias ? bias[n] : 0.0f);
+        y[n] = SILU_OUT ? v / (1.0f + expf(-v)) : v;
+    }
+}
+
+// ------------------------------------------------------------------ host side
+bool map_2d(CUtensorMap* m, const __half* base, uint64_t rows, uint64_t K, uint32_t box_rows) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {K, rows};
+    const cuuint64_t strides[1] = {K * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)GK, box_rows};
+    const cuuint32_t estr[2] = {1u, 1u};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void*)base, dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+// [B][T][1024] f16, box 64 channels x 128 frames x 1 branch; frames outside [0, T) read as zero.
+bool map_conv(CUtensorMap* m, const __half* base, int T, int B) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    const cuuint64_t dims[3] = {(cuuint64_t)DM, (cuuint64_t)T, (cuuint64_t)B};
+    const cuuint64_t strides[2] = {(cuuint64_t)DM * 2, (cuuint64_t)T * DM * 2};
+    const cuuint32_t box[3] = {(cuuint32_t)GK, (cuuint32_t)GM, 1u};
+    const cuuint32_t estr[3] = {1u, 1u, 1u};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, (void*)base, dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int EPI, int BN, bool CONV>
+cudaError_t set_gemm_smem() {
+    return cudaFuncSetAttribute(k_dit_gemm<EPI, BN, CONV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)GemmSmem<BN>::SMEM);
+}
+
+cudaError_t init_device() {
+    cudaError_t e;
+    if ((e = set_gemm_smem<DE_F16, 128, false>())) return e;
+    if ((e = set_gemm_smem<DE_QKV, 128, false>())) return e;
+    if ((e = set_gemm_smem<DE_RESID, 128, false>())) return e;
+    if ((e = set_gemm_smem<DE_F32, 128, false>())) return e;
+    if ((e = set_gemm_smem<DE_F16, 64, true>())) return e;
+    if ((e = set_gemm_smem<DE_RESID, 64, true>())) return e;
+    return cudaSuccess;
+}
+
+// Plain GEMM over R rows: A [R][K] f16, W [N][K] f16.
+bool gemm(int epi, const __half* A, const __half* W, const DitGemmArgs& a, cudaStream_t s) {
+    CUtensorMap ma, mb;
+    if (!map_2d(&ma, A, (uint64_t)a.R, (uint64_t)a.K, GM) || !map_2d(&mb, W, (uint64_t)a.N, (uint64_t)a.K, 128))
+        return false;
+    const dim3 grid(a.N / 128, (a.R + GM - 1) / GM);
+    const size_t sm = GemmSmem<128>::SMEM;
+    switch (epi) {
+        case DE_F16: launch_pdl(k_dit_gemm<DE_F16, 128, false>, grid, dim3(G_THREADS), sm, s, ma, mb, a); break;
+        case DE_QKV: launch_pdl(k_dit_gemm<DE_QKV, 128, false>, grid, dim3(G_THREADS), sm, s, ma, mb, a); break;
+        case DE_RESID: launch_pdl(k_dit_gemm<DE_RESID, 128, false>, grid, dim3(G_THREADS), sm, s, ma, mb, a); break;
+        default: launch_pdl(k_dit_gemm<DE_F32, 128, false>, grid, dim3(G_THREADS), sm, s, ma, mb, a); break;
+    }
+    return true;
+}
+
+// Grouped conv (16 groups of 64 channels, 31 taps, zero padding 15) over B branches of T frames:
+// X [B][T][1024] f16, Wc [1024][31 * 64] f16 (tap-major K).
+bool conv(int epi, const __half* X, const __half* Wc, int B, const DitGemmArgs& a, cudaStream_t s) {
+    CUtensorMap ma, mb;
+    if (!map_conv(&ma, X, a.T, B) || !map_2d(&mb, Wc, (uint64_t)DM, (uint64_t)KCONV, 64)) return false;
+    const dim3 grid(GCP, B * ((a.T + GM - 1) / GM));
+    const size_t sm = GemmSmem<64>::SMEM;
+    if (epi == DE_F16) launch_pdl(k_dit_gemm<DE_F16, 64, true>, grid, dim3(G_THREADS), sm, s, ma, mb, a);
+    else launch_pdl(k_dit_gemm<DE_RESID, 64, true>, grid, dim3(G_THREADS), sm, s, ma, mb, a);
+    return true;
+}
+
+struct Block {
+    __half *wqkv = nullptr, *wo = nullptr, *w1 = nullptr, *w2 = nullptr;
+    float *bqkv = nullptr, *bo = nullptr, *b1 = nullptr, *b2 = nullptr;
+};
+
+}  // namespace dit
+}  // namespace gsvcu
+
+using namespace gsvcu;
+using namespace gsvcu::dit;
+
+struct gsvcu_dit {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    std::string err;
+    gsvcu_dit_hparams hp{};
+    std::vector<float> inv_freq;   // [32] (the checkpoint's stored values)
+    std::vector<void*> wallocs;
+    // weights
+    __half *w_mel = nullptr, *w_c0 = nullptr, *w_c2 = nullptr, *w_t0 = nullptr, *w_t2 = nullptr, *w_ada = nullptr,
+           *w_out = nullptr;
+    float *b_c0 = nullptr, *b_c2 = nullptr, *b_t0 = nullptr, *b_t2 = nullptr, *b_ada = nullptr, *b_out = nullptr;
+    std::vector<Block> L;
+    // per-shape state (set_condition)
+    int T = 0, x_lens = 0, cap_rows = 0;
+    std::vector<void*> ballocs;
+    float *cond = nullptr;        // [2][T][1024]: condition, negative condition
+    float *rcos = nullptr, *rsin = nullptr;   // [T][32]
+    float *xmel = nullptr;        // [100][T]
+    float *x = nullptr;           // [R][1024]
+    __half *a16 = nullptr;        // [R][1024] GEMM / conv operand
+    __half *c16 = nullptr;        // [R][1024] conv 1 output
+    __half *qkv16 = nullptr;      // [R][3072]
+    __half *h16 = nullptr;        // [R][2048]
+    __half *mel16 = nullptr;      // [R][128]
+    float *vel = nullptr;         // [R][128]
+    float *tsin = nullptr;        // [steps][256]
+    int cap_steps = 0;
+    float *temb = nullptr, *th = nullptr, *ada = nullptr;   // [1024], [1024], [depth * 6144 + 2048]
+    float *vout = nullptr;        // [100][T]
+    int* errw = nullptr;
+
+    int fail(int code, const std::string& m) {
+        err = m;
+        return code;
+    }
+    ~gsvcu_dit() {
+        int prev = -1;
+        cudaGetDevice(&prev);
+        cudaSetDevice(device);
+        if (stream) cudaStreamSynchronize(stream);
+        for (void* p : wallocs) cudaFree(p);
+        for (void* p : ballocs) cudaFree(p);
+        cudaFree(tsin);
+        cudaFree(errw);
+        if (stream) cudaStreamDestroy(stream);
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+    template <typename TT>
+    int upload(const std::vector<TT>& h, TT** dst) {
+        if (cudaMalloc((void**)dst, h.size() * sizeof(TT)) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(GSVCU_ERR_OOM, "cudaMalloc of DiT weights failed");
+        }
+        wallocs.push_back(*dst);
+        if (cudaMemcpy(*dst, h.data(), h.size() * sizeof(TT), cudaMemcpyHostToDevice) != cudaSuccess)
+            return fail(GSVCU_ERR_CUDA, "DiT weight upload failed");
+        return GSVCU_OK;
+    }
+    int reserve(int T_, int rows);
+    int forward(int B, int negative, const float* tsin_dev, int n_blocks, bool head);
+};
+
+namespace {
+
+uint16_t h16_of(float f) { return __half_as_ushort(__float2half_rn(f)); }
+
+// F32 / F16 tensor widened to f32 on the host.
+bool tensor_f32(const GgufTensor* t, size_t n, std::vector<float>& out) {
+    if (!t) return false;
+    out.resize(n);
+    if (t->type == 0 && t->nbytes >= n * 4) {
+        std::memcpy(out.data(), t->data, n * 4);
+        return true;
+    }
+    if (t->type == 1 && t->nbytes >= n * 2) {
+        const __half* h = (const __half*)t->data;
+        for (size_t i = 0; i < n; i++) out[i] = __half2float(h[i]);
+        return true;
+    }
+    return false;
+}
+
+}  // namespace
+
+int gsvcu_dit::reserve(int T_, int rows) {
+    if (T_ == T && rows <= cap_rows) return GSVCU_OK;
+    cudaStreamSynchronize(stream);
+    for (void* p : ballocs) cudaFree(p);
+    ballocs.clear();
+    cap_rows = 0;
+    T = 0;
+    const size_t R = (size_t)rows, TT = (size_t)T_;
+    const size_t nada = (size_t)hp.depth * ADA + 2 * DM;
+    struct A { void** p; size_t bytes; };
+    const A list[] = {{(void**)&cond, 2 * TT * DM * 4}, {(void**)&rcos, TT * 32 * 4}, {(void**)&rsin, TT * 32 * 4},
+                      {(void**)&xmel, MEL * TT * 4}, {(void**)&x, R * DM * 4}, {(void**)&a16, R * DM * 2},
+                      {(void**)&c16, R * DM * 2}, {(void**)&qkv16, R * 3 * DM * 2}, {(void**)&h16, R * FFD * 2},
+                      {(void**)&mel16, R * MELP * 2}, {(void**)&vel, R * MELP * 4}, {(void**)&temb, DM * 4},
+                      {(void**)&th, DM * 4}, {(void**)&ada, nada * 4}, {(void**)&vout, MEL * TT * 4}};
+    for (const A& a : list) {
+        if (cudaMalloc(a.p, a.bytes) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(GSVCU_ERR_OOM, "cudaMalloc of DiT activations failed");
+        }
+        ballocs.push_back(*a.p);
+    }
+    // rows past R of the padded operands stay zero (the GEMMs' A tiles read them)
+    cudaMemsetAsync(mel16, 0, R * MELP * 2, stream);
+    cap_rows = rows;
+    T = T_;
+    return GSVCU_OK;
+}
+
+// One estimator pass over B branches (B = 2: rows [0, T) use the condition, [T, 2T) the negative one;
+// B = 1: the condition selected by `negative`) from xmel and the time features at tsin_dev: the trunk,
+// n_blocks DiT blocks and, with `head`, the output projection into vel ([R][128]).
+int gsvcu_dit::forward(int B, int negative, const float* tsin_dev, int n_blocks, bool head) {
+    const int R = B * T;
+    cudaStream_t s = stream;
+    const int depth = hp.depth;
+    auto gemv_blocks = [](int n) { return dim3((unsigned)((n + 7) / 8)); };
+    // time embedding, then every block's AdaLN modulation and norm_out's in one launch
+    launch_pdl(k_dit_gemv<false, true>, gemv_blocks(DM), dim3(256), 0, s, (const __half*)w_t0, (const float*)b_t0,
+               tsin_dev, DM, TSIN, th);
+    launch_pdl(k_dit_gemv<false, false>, gemv_blocks(DM), dim3(256), 0, s, (const __half*)w_t2, (const float*)b_t2,
+               (const float*)th, DM, DM, temb);
+    const int nada = depth * ADA + 2 * DM;
+    launch_pdl(k_dit_gemv<true, false>, gemv_blocks(nada), dim3(256), 0, s, (const __half*)w_ada, (const float*)b_ada,
+               (const float*)temb, nada, DM, ada);
+    // trunk
+    launch_pdl(k_dit_pack_mel, dim3(std::min(1024, (R * MELP + 255) / 256)), dim3(256), 0, s, (const float*)xmel, T, B,
+               mel16);
+    DitGemmArgs a{};
+    a.R = R; a.T = T; a.x_lens = x_lens; a.err = errw;
+    {
+        DitGemmArgs g = a;
+        g.N = DM; g.K = MELP; g.out32 = x; g.ld = DM;
+        g.add = cond + (B == 1 && negative ? (size_t)T * DM : 0);
+        if (!gemm(DE_F32, mel16, w_mel, g, s)) return fail(GSVCU_ERR_CUDA, "tensor map encoding failed");
+    }
+    launch_pdl(k_dit_mask16, dim3(std::min(2048, (R * DM / 4 + 255) / 256)), dim3(256), 0, s, (const float*)x, R, T,
+               x_lens, a16);
+    {
+        DitGemmArgs g = a;
+        g.N = DM; g.K = KCONV; g.bias = b_c0; g.act = ACT_MISH; g.out16 = c16; g.ld = DM;
+        if (!conv(DE_F16, a16, w_c0, B, g, s)) return fail(GSVCU_ERR_CUDA, "tensor map encoding failed");
+        g.bias = b_c2; g.out16 = nullptr; g.out32 = x; g.use_mask = 1;
+        if (!conv(DE_RESID, c16, w_c2, B, g, s)) return fail(GSVCU_ERR_CUDA, "tensor map encoding failed");
+    }
+    const dim3 rows8((unsigned)((R + 7) / 8));
+    for (int li = 0; li < n_blocks; li++) {
+        const Block& w = L[(size_t)li];
+        const float* m = ada + (size_t)li * ADA;   // shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp
+        launch_pdl(k_dit_lnmod, rows8, dim3(256), 0, s, (const float*)x, R, m, m + DM, a16);
+        DitGemmArgs g = a;
+        g.N = 3 * DM; g.K = DM; g.bias = w.bqkv; g.out16 = qkv16; g.ld = 3 * DM; g.rcos = rcos; g.rsin = rsin;
+        if (!gemm(DE_QKV, a16, w.wqkv, g, s)) return fail(GSVCU_ERR_CUDA, "tensor map encoding failed");
+        launch_pdl(k_dit_attn, dim3((unsigned)((T + AQ - 1) / AQ), NHD, (unsigned)B), dim3(128), 0, s,
+                   (const __half*)qkv16, a16, T, x_lens);
+        g = a;
+        g.N = DM; g.K = DM; g.bias = w.bo; g.out32 = x; g.ld = DM; g.gate = m + 2 * DM; g.use_mask = 1;
+        if (!gemm(DE_RESID, a16, w.wo, g, s)) return fail(GSVCU_ERR_CUDA, "tensor map encoding failed");
+        launch_pdl(k_dit_lnmod, rows8, dim3(256), 0, s, (const float*)x, R, m + 3 * DM, m + 4 * DM, a16);
+        g = a;
+        g.N = FFD; g.K = DM; g.bias = w.b1; g.act = ACT_GELU_TANH; g.out16 = h16; g.ld = FFD;
+        if (!gemm(DE_F16, a16, w.w1, g, s)) return fail(GSVCU_ERR_CUDA, "tensor map encoding failed");
+        g = a;
+        g.N = DM; g.K = FFD; g.bias = w.b2; g.out32 = x; g.ld = DM; g.gate = m + 5 * DM;
+        if (!gemm(DE_RESID, h16, w.w2, g, s)) return fail(GSVCU_ERR_CUDA, "tensor map encoding failed");
+    }
+    if (head) {
+        const float* m = ada + (size_t)depth * ADA;   // norm_out: scale, shift
+        launch_pdl(k_dit_lnmod, rows8, dim3(256), 0, s, (const float*)x, R, m + DM, m, a16);
+        DitGemmArgs g = a;
+        g.N = MELP; g.K = DM; g.bias = b_out; g.out32 = vel; g.ld = MELP;
+        if (!gemm(DE_F32, a16, w_out, g, s)) return fail(GSVCU_ERR_CUDA, "tensor map encoding failed");
+    }
+    if (cudaPeekAtLastError() != cudaSuccess) return fail(GSVCU_ERR_CUDA, cudaGetErrorString(cudaGetLastError()));
+    return GSVCU_OK;
+}
+
+namespace {
+
+// SinusPositionEmbedding(256) of the time t as the reference evaluates it (src/gsv_dit.cpp:755-769).
+void time_sin(float t, float* out) {
+    const float e = (float)(std::log(10000.0) / 127.0);
+    for (int i = 0; i < 128; i++) {
+        const float a = 1000.0f * t * std::exp(-e * (float)i);
+        out[i] = std::sin(a);
+        out[128 + i] = std::cos(a);
+    }
+}
+
+int check_err(gsvcu_dit* c) {
+    int e = 0;
+    if (cudaStreamSynchronize(c->stream) != cudaSuccess) return c->fail(GSVCU_ERR_CUDA, cudaGetErrorString(cudaGetLastError()));
+    if (cudaMemcpy(&e, c->errw, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return c->fail(GSVCU_ERR_CUDA, "error word read failed");
+    if (e) {
+        cudaMemset(c->errw, 0, 4);
+        return c->fail(GSVCU_ERR_CUDA, "a DiT GEMM wait timed out");
+    }
+    return GSVCU_OK;
+}
+
+int upload_tsin(gsvcu_dit* c, const std::vector<float>& h) {
+    const int steps = (int)(h.size() / TSIN);
+    if (steps > c->cap_steps) {
+        cudaStreamSynchronize(c->stream);
+        cudaFree(c->tsin);
+        c->tsin = nullptr;
+        c->cap_steps = 0;
+        if (cudaMalloc((void**)&c->tsin, h.size() * 4) != cudaSuccess) {
+            cudaGetLastError();
+            return c->fail(GSVCU_ERR_OOM, "cudaMalloc of time features failed");
+        }
+        c->cap_steps = steps;
+    }
+    if (cudaMemcpyAsync(c->tsin, h.data(), h.size() * 4, cudaMemcpyHostToDevice, c->stream) != cudaSuccess)
+        return c->fail(GSVCU_ERR_CUDA, "time feature upload failed");
+    return GSVCU_OK;
+}
+
+struct DevGuard {
+    int prev = -1;
+    explicit DevGuard(int dev) {
+        cudaGetDevice(&prev);
+        cudaSetDevice(dev);
+    }
+    ~DevGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+}  // namespace
+
+extern "C" {
+
+int gsvcu_dit_load(int device, const char* path, gsvcu_dit** out) {
+    if (!out || !path) return GSVCU_ERR_ARG;
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) {
+        cudaGetLastError();
+        return GSVCU_ERR_DEVICE;
+    }
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess || prop.major != 10) return GSVCU_ERR_DEVICE;
+    DevGuard dg(device);
+    gsvcu_dit* c = new gsvcu_dit();
+    c->device = device;
+    auto done = [&](int rc) {
+        if (rc == GSVCU_OK) *out = c;
+        else {
+            std::fprintf(stderr, "gsvcu_dit_load: %s\n", c->err.c_str());
+            delete c;
+        }
+        return rc;
+    };
+    if (init_device() != cudaSuccess || encode_fn() == nullptr ||
+        cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaMalloc((void**)&c->errw, 4) != cudaSuccess || cudaMemset(c->errw, 0, 4) != cudaSuccess) {
+        cudaGetLastError();
+        return done(c->fail(GSVCU_ERR_CUDA, "device set-up failed"));
+    }
+    GgufFile f;
+    std::string e;
+    if (!f.open(path, e)) return done(c->fail(GSVCU_ERR_IO, e));
+    uint32_t v = 0;
+    auto u32 = [&](const char* k, int def) { return f.get_u32(k, v) ? (int)v : def; };
+    gsvcu_dit_hparams& hp = c->hp;
+    hp.dim = u32("dit.dim", DM);
+    hp.depth = u32("dit.depth", 22);
+    hp.heads = u32("dit.heads", NHD);
+    hp.dim_head = u32("dit.dim_head", HDD);
+    hp.ff_mult = u32("dit.ff_mult", 2);
+    hp.mel_dim = u32("dit.mel_dim", MEL);
+    hp.text_dim = u32("dit.text_dim", 512);
+    if (hp.dim != DM || hp.heads != NHD || hp.dim_head != HDD || hp.ff_mult != 2 || hp.mel_dim != MEL ||
+        u32("dit.conv_pos_groups", GCP) != GCP || u32("dit.conv_pos_kernel", KCP) != KCP ||
+        u32("dit.rope_dims", HDD) != HDD || hp.depth <= 0 || hp.depth > 64)
+        return done(c->fail(GSVCU_ERR_FORMAT, "unsupported DiT dims (1024 / 16 heads x 64 / FFN 2048 / mel 100, "
+                                              "conv_pos 16 groups x 31 taps, RoPE on 64 dims)"));
+    // f16 rows [N][Kp] from a [N][K] tensor (K <= Kp, zero padded); rows past N of Np zero
+    auto mat = [&](const std::string& name, int N, int K, int Np, int Kp, std::vector<uint16_t>& dst, size_t row0) -> int {
+        const GgufTensor* t = f.tensor(name);
+        std::vector<float> hst;
+        if (!t || !tensor_f32(t, (size_t)N * K, hst)) return c->fail(GSVCU_ERR_FORMAT, "missing or bad tensor " + name);
+        (void)Np;
+        for (int r = 0; r < N; r++)
+            for (int k = 0; k < K; k++) dst[(row0 + r) * (size_t)Kp + k] = h16_of(hst[(size_t)r * K + k]);
+        return GSVCU_OK;
+    };
+    auto vecf = [&](const std::string& name, int n, std::vector<float>& dst, size_t off) -> int {
+        std::vector<float> hst;
+        if (!tensor_f32(f.tensor(name), (size_t)n, hst)) return c->fail(GSVCU_ERR_FORMAT, "missing or bad tensor " + name);
+        std::memcpy(dst.data() + off, hst.data(), (size_t)n * 4);
+        return GSVCU_OK;
+    };
+    int rc;
+    std::vector<uint16_t> hw;
+    std::vector<float> hb;
+    // input projection of the mel channels (no bias: the condition rows carry it), K padded to 128
+    hw.assign((size_t)DM * MELP, 0);
+    if ((rc = mat("dit.input_embed.proj.weight_mel", DM, MEL, DM, MELP, hw, 0)) ||
+        (rc = c->upload(hw, (uint16_t**)&c->w_mel)))
+        return done(rc);
+    // conv_pos: [G][OCg][ICg * 31] with inner index ic * 31 + tap -> [1024][tap * 64 + ic]
+    for (int li = 0; li < 2; li++) {
+        const std::string base = std::string("dit.input_embed.conv_pos_embed.conv1d.") + (li ? "2" : "0");
+        const GgufTensor* t = f.tensor(base + ".weight");
+        std::vector<float> hst;
+        if (!t || !tensor_f32(t, (size_t)DM * KCONV, hst)) return done(c->fail(GSVCU_ERR_FORMAT, "missing or bad " + base));
+        hw.assign((size_t)DM * KCONV, 0);
+        for (int o = 0; o < DM; o++)
+            for (int ic = 0; ic < ICG; ic++)
+                for (int k = 0; k < KCP; k++)
+                    hw[(size_t)o * KCONV + (size_t)k * ICG + ic] = h16_of(hst[(size_t)o * KCONV + (size_t)ic * KCP + k]);
+        hb.assign(DM, 0.0f);
+        if ((rc = c->upload(hw, (uint16_t**)(li ? &c->w_c2 : &c->w_c0))) || (rc = vecf(base + ".bias", DM, hb, 0)) ||
+            (rc = c->upload(hb, li ? &c->b_c2 : &c->b_c0)))
+            return done(rc);
+    }
+    // time MLP 256 -> 1024 -> 1024
+    hw.assign((size_t)DM * TSIN, 0);
+    hb.assign(DM, 0.0f);
+    if ((rc = mat("dit.time_embed.time_mlp.0.weight", DM, TSIN, DM, TSIN, hw, 0)) || (rc = c->upload(hw, (uint16_t**)&c->w_t0)) ||
+        (rc = vecf("dit.time_embed.time_mlp.0.bias", DM, hb, 0)) || (rc = c->upload(hb, &c->b_t0)))
+        return done(rc);
+    hw.assign((size_t)DM * DM, 0);
+    if ((rc = mat("dit.time_embed.time_mlp.2.weight", DM, DM, DM, DM, hw, 0)) || (rc = c->upload(hw, (uint16_t**)&c->w_t2)) ||
+        (rc = vecf("dit.time_embed.time_mlp.2.bias", DM, hb, 0)) || (rc = c->upload(hb, &c->b_t2)))
+        return done(rc);
+    // AdaLN projections of every block, then norm_out's, as one matrix
+    const size_t nada = (size_t)hp.depth * ADA + 2 * DM;
+    hw.assign(nada * DM, 0);
+    hb.assign(nada, 0.0f);
+    for (int li = 0; li < hp.depth; li++) {
+        const std::string b = "dit.transformer_blocks." + std::to_string(li) + ".attn_norm.linear.";
+        if ((rc = mat(b + "weight", ADA, DM, ADA, DM, hw, (size_t)li * ADA)) || (rc = vecf(b + "bias", ADA, hb, (size_t)li * ADA)))
+            return done(rc);
+    }
+    if ((rc = mat("dit.norm_out.linear.weight", 2 * DM, DM, 2 * DM, DM, hw, (size_t)hp.depth * ADA)) ||
+        (rc = vecf("dit.norm_out.linear.bias", 2 * DM, hb, (size_t)hp.depth * ADA)) ||
+        (rc = c->upload(hw, (uint16_t**)&c->w_ada)) || (rc = c->upload(hb, &c->b_ada)))
+        return done(rc);
+    // output projection, 100 rows padded to 128
+    hw.assign((size_t)MELP * DM, 0);
+    hb.assign(MELP, 0.0f);
+    if ((rc = mat("dit.proj_out.weight", MEL, DM, MELP, DM, hw, 0)) || (rc = vecf("dit.proj_out.bias", MEL, hb, 0)) ||
+        (rc = c->upload(hw, (uint16_t**)&c->w_out)) || (rc = c->upload(hb, &c->b_out)))
+        return done(rc);
+    // blocks
+    c->L.resize((size_t)hp.depth);
+    for (int li = 0; li < hp.depth; li++) {
+        Block& w = c->L[(size_t)li];
+        const std::string b = "dit.transformer_blocks." + std::to_string(li) + ".";
+        hw.assign((size_t)3 * DM * DM, 0);
+        hb.assign((size_t)3 * DM, 0.0f);
+        const char* qkv[3] = {"attn.to_q.", "attn.to_k.", "attn.to_v."};
+        for (int j = 0; j < 3; j++)
+            if ((rc = mat(b + qkv[j] + "weight", DM, DM, DM, DM, hw, (size_t)j * DM)) ||
+                (rc = vecf(b + qkv[j] + "bias", DM, hb, (size_t)j * DM)))
+                return done(rc);
+        if ((rc = c->upload(hw, (uint16_t**)&w.wqkv)) || (rc = c->upload(hb, &w.bqkv))) return done(rc);
+        hw.assign((size_t)DM * DM, 0);
+        hb.assign(DM, 0.0f);
+        if ((rc = mat(b + "attn.to_out.0.weight", DM, DM, DM, DM, hw, 0)) || (rc = vecf(b + "attn.to_out.0.bias", DM, hb, 0)) ||
+            (rc = c->upload(hw, (uint16_t**)&w.wo)) || (rc = c->upload(hb, &w.bo)))
+            return done(rc);
+        hw.assign((size_t)FFD * DM, 0);
+        hb.assign(FFD, 0.0f);
+        if ((rc = mat(b + "ff.ff.0.0.weight", FFD, DM, FFD, DM, hw, 0)) || (rc = vecf(b + "ff.ff.0.0.bias", FFD, hb, 0)) ||
+            (rc = c->upload(hw, (uint16_t**)&w.w1)) || (rc = c->upload(hb, &w.b1)))
+            return done(rc);
+        hw.assign((size_t)DM * FFD, 0);
+        hb.assign(DM, 0.0f);
+        if ((rc = mat(b + "ff.ff.2.weight", DM, FFD, DM, FFD, hw, 0)) || (rc = vecf(b + "ff.ff.2.bias", DM, hb, 0)) ||
+            (rc = c->upload(hw, (uint16_t**)&w.w2)) || (rc = c->upload(hb, &w.b2)))
+            return done(rc);
+    }
+    c->inv_freq.assign(32, 0.0f);
+    if ((rc = vecf("dit.rotary_embed.inv_freq", 32, c->inv_freq, 0))) return done(rc);
+    return done(GSVCU_OK);
+}
+
+void gsvcu_dit_destroy(gsvcu_dit* c) { delete c; }
+
+const char* gsvcu_dit_last_error(const gsvcu_dit* c) { return c ? c->err.c_str() : "null DiT context"; }
+
+int gsvcu_dit_get_hparams(const gsvcu_dit* c, gsvcu_dit_hparams* out) {
+    if (!c || !out) return GSVCU_ERR_ARG;
+    *out = c->hp;
+    return GSVCU_OK;
+}
+
+int gsvcu_dit_set_condition(gsvcu_dit* c, const float* cond, const float* neg, int32_t T, int32_t x_lens) {
+    if (!c || !cond || !neg || T <= 0 || T > 65536) return GSVCU_ERR_ARG;
+    DevGuard dg(c->device);
+    if (x_lens <= 0 || x_lens > T) x_lens = T;
+    int rc;
+    if ((rc = c->reserve(T, 2 * T))) return rc;
+    c->x_lens = x_lens;
+    // RoPE tables of head 0: angle = n * inv_freq[i] in float (src/gsv_dit.cpp:787-793)
+    std::vector<float> cs((size_t)T * 32), sn((size_t)T * 32);
+    for (int n = 0; n < T; n++)
+        for (int i = 0; i < 32; i++) {
+            const float a = (float)n * c->inv_freq[(size_t)i];
+            cs[(size_t)n * 32 + i] = std::cos(a);
+            sn[(size_t)n * 32 + i] = std::sin(a);
+        }
+    const size_t cb = (size_t)T * DM * 4;
+    if (cudaMemcpyAsync(c->cond, cond, cb, cudaMemcpyHostToDevice, c->stream) != cudaSuccess ||
+        cudaMemcpyAsync(c->cond + (size_t)T * DM, neg, cb, cudaMemcpyHostToDevice, c->stream) != cudaSuccess ||
+        cudaMemcpyAsync(c->rcos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice, c->stream) != cudaSuccess ||
+        cudaMemcpyAsync(c->rsin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice, c->stream) != cudaSuccess)
+        return c->fail(GSVCU_ERR_CUDA, "condition upload failed");
+    if (cudaStreamSynchronize(c->stream) != cudaSuccess) return c->fail(GSVCU_ERR_CUDA, "condition upload failed");
+    return GSVCU_OK;
+}
+
+int gsvcu_dit_velocity(gsvcu_dit* c, const float* x_mel, float t, int32_t negative, float* vel) {
+    if (!c || !x_mel || !vel) return GSVCU_ERR_ARG;
+    if (c->T <= 0) return c->fail(GSVCU_ERR_ARG, "velocity() before set_condition()");
+    DevGuard dg(c->device);
+    std::vector<float> ts(TSIN);
+    time_sin(t, ts.data());
+    int rc;
+    if ((rc = upload_tsin(c, ts))) return rc;
+    if (cudaMemcpyAsync(c->xmel, x_mel, (size_t)MEL * c->T * 4, cudaMemcpyHostToDevice, c->stream) != cudaSuccess)
+        return c->fail(GSVCU_ERR_CUDA, "input upload failed");
+    if ((rc = c->forward(1, negative, c->tsin, c->hp.depth, true))) return rc;
+    launch_pdl(k_dit_vel_out, dim3((unsigned)std::min(1024, (MEL * c->T + 255) / 256)), dim3(256), 0, c->stream,
+               (const float*)c->vel, c->T, c->vout);
+    if (cudaMemcpyAsync(vel, c->vout, (size_t)MEL * c->T * 4, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess)
+        return c->fail(GSVCU_ERR_CUDA, "output read failed");
+    return check_err(c);
+}
+
+int gsvcu_dit_sample(gsvcu_dit* c, const float* x0, int32_t P, int32_t steps, float cfg, float* mel_out) {
+    if (!c || !x0 || !mel_out || steps <= 0) return GSVCU_ERR_ARG;
+    if (c->T <= 0) return c->fail(GSVCU_ERR_ARG, "sample() before set_condition()");
+    const int T = c->T;
+    if (P <= 0 || P >= T) return c->fail(GSVCU_ERR_ARG, "bad prompt length");
+    DevGuard dg(c->device);
+    std::vector<float> ts((size_t)steps * TSIN);
+    const float dt = 1.0f / (float)steps;
+    for (int j = 0; j < steps; j++) time_sin((float)j * dt, ts.data() + (size_t)j * TSIN);
+    int rc;
+    if ((rc = upload_tsin(c, ts))) return rc;
+    if (cudaMemcpyAsync(c->xmel, x0, (size_t)MEL * T * 4, cudaMemcpyHostToDevice, c->stream) != cudaSuccess)
+        return c->fail(GSVCU_ERR_CUDA, "input upload failed");
+    const bool guided = cfg > 1e-5f;
+    const dim3 eg((unsigned)std::min(1024, (MEL * T + 255) / 256));
+    // x[:, :P] = 0 before the first step (src/gsv_dit.cpp:1440-1441)
+    launch_pdl(k_dit_euler, eg, dim3(256), 0, c->stream, (const float*)c->vel, T, 0, 0, 0.0f, 0.0f, P, c->xmel);
+    for (int j = 0; j < steps; j++) {
+        if ((rc = c->forward(guided ? 2 : 1, 0, c->tsin + (size_t)j * TSIN, c->hp.depth, true))) return rc;
+        launch_pdl(k_dit_euler, eg, dim3(256), 0, c->stream, (const float*)c->vel, T, 1, guided ? 1 : 0, cfg, dt, P,
+                   c->xmel);
+    }
+    for (int ch = 0; ch < MEL; ch++)
+        if (cudaMemcpyAsync(mel_out + (size_t)ch * (T - P), c->xmel + (size_t)ch * T + P, (size_t)(T - P) * 4,
+                            cudaMemcpyDeviceToHost, c->stream) != cudaSuccess)
+            return c->fail(GSVCU_ERR_CUDA, "output read failed");
+    return check_err(c);
+}
+
+int gsvcu_dit_op_hidden(gsvcu_dit* c, const float* x_mel, float t, int32_t n_blocks, float* hidden) {
+    if (!c || !x_mel || !hidden || n_blocks < 0) return GSVCU_ERR_ARG;
+    if (c->T <= 0) return c->fail(GSVCU_ERR_ARG, "op before set_condition()");
+    if (n_blocks > c->hp.depth) n_blocks = c->hp.depth;
+    DevGuard dg(c->device);
+    std::vector<float> ts(TSIN);
+    time_sin(t, ts.data());
+    int rc;
+    if ((rc = upload_tsin(c, ts))) return rc;
+    if (cudaMemcpyAsync(c->xmel, x_mel, (size_t)MEL * c->T * 4, cudaMemcpyHostToDevice, c->stream) != cudaSuccess)
+        return c->fail(GSVCU_ERR_CUDA, "input upload failed");
+    if ((rc = c->forward(2, 0, c->tsin, n_blocks, false))) return rc;
+    if (cudaMemcpyAsync(hidden, c->x, (size_t)2 * c->T * DM * 4, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess)
+        return c->fail(GSVCU_ERR_CUDA, "output read failed");
+    return check_err(c);
+}
+
+int gsvcu_dit_stream(gsvcu_dit* c, void** out) {
+    if (!c || !out) return GSVCU_ERR_ARG;
+    *out = (void*)c->stream;
+    return GSVCU_OK;
+}
+
+}  // extern "C"

@@ -293,3 +293,80 @@ def write_bert_model(path: str, seed: int = 0, dims: BertDims | None = None, mat
     w.write_tensors_to_file()
     w.close()
     return path
+
+
+def write_dit_model(path: str, seed: int = 0, depth: int = 22, mat_type: str = "f16") -> str:
+    """Seeded synthetic DiT GGUF with the names, shapes, dtypes and KV keys of the reference exporter
+    (tools/export_gguf/convert_dit.py:40-152): 2D weights `mat_type` (its --spec lin=..), biases, norms and
+    inv_freq F32; conv_pos weights in the exporter's [G][OCg][ICg * K] order (inner index ic * 31 + tap).
+    Values N(0, 0.02); the AdaLN biases N(0, 0.3) so the gates and modulations are not negligible;
+    inv_freq the fp16-stored 10000^(-2i/64). The text_embed tensors (used only by prepare) are left out."""
+    import gguf
+
+    D, MEL = 1024, 100
+    rng = np.random.default_rng(seed)
+    qt = {"f32": gguf.GGMLQuantizationType.F32, "f16": gguf.GGMLQuantizationType.F16}[mat_type]
+
+    def n(*shape, s=0.02):
+        return (rng.standard_normal(shape, dtype=np.float32) * np.float32(s)).astype(np.float32)
+
+    w = gguf.GGUFWriter(path, "gsv.dit")
+    for k, v in (("dit.dim", D), ("dit.depth", depth), ("dit.heads", 16), ("dit.dim_head", 64), ("dit.ff_mult", 2),
+                 ("dit.mel_dim", MEL), ("dit.text_dim", 512), ("dit.conv_layers", 4), ("dit.conv_pos_groups", 16),
+                 ("dit.conv_pos_kernel", 31), ("dit.rope_dims", 64), ("dit.text_max_pos", 4096),
+                 ("dit.time_freq_dim", 256)):
+        w.add_uint32(k, v)
+    w.add_float32("dit.norm_eps", 1e-6)
+
+    def add(name, arr, mat=False):
+        arr = np.ascontiguousarray(arr, dtype=np.float32)
+        if mat and qt == gguf.GGMLQuantizationType.F16:
+            w.add_tensor(name, arr.astype(np.float16), raw_dtype=qt)
+        else:
+            w.add_tensor(name, arr, raw_dtype=gguf.GGMLQuantizationType.F32)
+
+    add("dit.time_embed.time_mlp.0.weight", n(D, 256), True)
+    add("dit.time_embed.time_mlp.0.bias", n(D))
+    add("dit.time_embed.time_mlp.2.weight", n(D, D), True)
+    add("dit.time_embed.time_mlp.2.bias", n(D))
+    add("dit.input_embed.proj.weight_mel", n(D, MEL), True)
+    add("dit.input_embed.proj.weight_ctx", n(D, 612), True)
+    add("dit.input_embed.proj.bias", n(D))
+    for li in (0, 2):
+        add(f"dit.input_embed.conv_pos_embed.conv1d.{li}.weight", n(16, 64, 64 * 31), True)
+        add(f"dit.input_embed.conv_pos_embed.conv1d.{li}.bias", n(D))
+    inv = (1.0 / (10000.0 ** (np.arange(0, 64, 2, dtype=np.float32) / 64.0))).astype(np.float16).astype(np.float32)
+    add("dit.rotary_embed.inv_freq", inv)
+    for li in range(depth):
+        p = f"dit.transformer_blocks.{li}."
+        add(p + "attn_norm.linear.weight", n(6 * D, D), True)
+        add(p + "attn_norm.linear.bias", n(6 * D, s=0.3))
+        for m in ("to_q", "to_k", "to_v"):
+            add(p + f"attn.{m}.weight", n(D, D), True)
+            add(p + f"attn.{m}.bias", n(D))
+        add(p + "attn.to_out.0.weight", n(D, D), True)
+        add(p + "attn.to_out.0.bias", n(D))
+        add(p + "ff.ff.0.0.weight", n(2048, D), True)
+        add(p + "ff.ff.0.0.bias", n(2048))
+        add(p + "ff.ff.2.weight", n(D, 2048), True)
+        add(p + "ff.ff.2.bias", n(D))
+    add("dit.norm_out.linear.weight", n(2 * D, D), True)
+    add("dit.norm_out.linear.bias", n(2 * D, s=0.3))
+    add("dit.proj_out.weight", n(MEL, D), True)
+    add("dit.proj_out.bias", n(MEL))
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    return path
+
+
+def cached_dit_model(cache_dir: str, seed: int = 0, depth: int = 22, mat_type: str = "f16") -> str:
+    """Path of a synthetic DiT GGUF, written once per (seed, depth, mat_type) under cache_dir."""
+    os.makedirs(cache_dir, exist_ok=True)
+    path = os.path.join(cache_dir, f"dit_s{seed}_d{depth}_{mat_type}.gguf")
+    if not os.path.exists(path):
+        tmp = path + f".tmp{os.getpid()}"
+        write_dit_model(tmp, seed, depth, mat_type)
+        os.replace(tmp, path)
+    return path

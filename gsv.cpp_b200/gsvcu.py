@@ -108,6 +108,22 @@ SIGNATURES.update({
     "gsvcu_bert_encode_feat_batch": ([_P, _I, _P, _P, _I, _P, _I], C.c_int),
 })
 
+class DitHParams(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in ("dim", "depth", "heads", "dim_head", "ff_mult", "mel_dim", "text_dim")]
+
+
+SIGNATURES.update({
+    "gsvcu_dit_load": ([C.c_int, C.c_char_p, C.POINTER(C.c_void_p)], C.c_int),
+    "gsvcu_dit_destroy": ([_P], None),
+    "gsvcu_dit_last_error": ([_P], C.c_char_p),
+    "gsvcu_dit_get_hparams": ([_P, C.POINTER(DitHParams)], C.c_int),
+    "gsvcu_dit_set_condition": ([_P, _P, _P, _I, _I], C.c_int),
+    "gsvcu_dit_velocity": ([_P, _P, C.c_float, _I, _P], C.c_int),
+    "gsvcu_dit_sample": ([_P, _P, _I, _I, C.c_float, _P], C.c_int),
+    "gsvcu_dit_op_hidden": ([_P, _P, C.c_float, _I, _P], C.c_int),
+    "gsvcu_dit_stream": ([_P, C.POINTER(C.c_void_p)], C.c_int),
+})
+
 PROF_CLASSES = ["sampler", "step_prep", "qkv_gemm", "decode_attn", "out_gemm", "layernorm", "ffn1_gemm", "ffn2_gemm",
                 "predict", "dense_fused"]
 
@@ -443,3 +459,68 @@ class Bert:
             res.append(flat[at:at + n].reshape(D, max(int(l) - 2, 0)).copy())
             at += n
         return res
+
+
+class Dit:
+    """The DiT / CFM velocity estimator on the GPU (gsvcu_dit_*; the role of gsv.cpp's gsv_dit)."""
+
+    def __init__(self, path: str, device: int = 0):
+        self.lib = load_library()
+        h = C.c_void_p()
+        rc = self.lib.gsvcu_dit_load(device, path.encode(), C.byref(h))
+        if rc != OK:
+            raise GsvcuError(rc, "gsvcu_dit_load failed (see stderr)")
+        self.h = h
+        hp = DitHParams()
+        self.lib.gsvcu_dit_get_hparams(self.h, C.byref(hp))
+        self.hp = hp
+        self.T = 0
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.gsvcu_dit_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _check(self, rc):
+        if rc != OK:
+            raise GsvcuError(rc, self.lib.gsvcu_dit_last_error(self.h).decode(errors="replace"))
+
+    def set_condition(self, cond, neg, x_lens=0):
+        """The static cache of gsv_dit::prepare: condition / negative-condition rows [T][1024]."""
+        cond = np.ascontiguousarray(cond, np.float32)
+        neg = np.ascontiguousarray(neg, np.float32)
+        assert cond.shape == neg.shape and cond.shape[1] == self.hp.dim
+        self._check(self.lib.gsvcu_dit_set_condition(self.h, cond.ctypes.data, neg.ctypes.data, cond.shape[0], x_lens))
+        self.T = cond.shape[0]
+
+    def velocity(self, x_mel, t, negative=False) -> np.ndarray:
+        """gsv_dit::velocity: x_mel [100][T] -> vel [100][T]."""
+        x_mel = np.ascontiguousarray(x_mel, np.float32)
+        vel = np.empty_like(x_mel)
+        self._check(self.lib.gsvcu_dit_velocity(self.h, x_mel.ctypes.data, float(t), int(bool(negative)), vel.ctypes.data))
+        return vel
+
+    def sample(self, x0, P, steps, cfg) -> np.ndarray:
+        """gsv_dit::sample's CFM loop on the set condition: x0 [100][T] -> mel [100][T - P]."""
+        x0 = np.ascontiguousarray(x0, np.float32)
+        out = np.empty((x0.shape[0], x0.shape[1] - P), np.float32)
+        self._check(self.lib.gsvcu_dit_sample(self.h, x0.ctypes.data, P, steps, float(cfg), out.ctypes.data))
+        return out
+
+    def hidden(self, x_mel, t, n_blocks) -> np.ndarray:
+        """Hidden state [2][T][1024] (conditioned, negative) after the trunk and n_blocks blocks."""
+        x_mel = np.ascontiguousarray(x_mel, np.float32)
+        out = np.empty((2, self.T, self.hp.dim), np.float32)
+        self._check(self.lib.gsvcu_dit_op_hidden(self.h, x_mel.ctypes.data, float(t), n_blocks, out.ctypes.data))
+        return out
+
+    def stream_handle(self) -> int:
+        s = C.c_void_p()
+        self._check(self.lib.gsvcu_dit_stream(self.h, C.byref(s)))
+        return s.value or 0

@@ -301,6 +301,39 @@ int gsvcu_bert_encode(gsvcu_bert* ctx, const int32_t* ids, int32_t T, int32_t n_
 int gsvcu_bert_encode_feat_batch(gsvcu_bert* ctx, int32_t B, const int32_t* ids_flat, const int32_t* lens,
                                  int32_t Tmax, float* out, int32_t out_on_device);
 
+/* ---------------------------------------------------------------- DiT / CFM velocity estimator
+ * gsv.cpp's gsv_dit (reference src/gsv_dit.{h,cpp}: F5-style DiT, 22 blocks of 1024 / 16 heads x 64,
+ * CFM Euler sampling with classifier-free guidance) on the same device. A DiT context owns its weights,
+ * stream and buffers; use it from one host thread at a time. Arrays are host memory in the reference's
+ * torch layouts: mel [100][T] (index c * T + t), condition rows [T][1024]. */
+typedef struct gsvcu_dit gsvcu_dit;
+typedef struct {
+    int32_t dim, depth, heads, dim_head, ff_mult, mel_dim, text_dim;
+} gsvcu_dit_hparams;
+
+/* Load a DiT GGUF of tools/export_gguf/convert_dit.py (gsv_dit::load, src/gsv_dit.cpp:640-750): 2D weights
+ * F32 or F16 (held as F16 on the device), biases / norms / inv_freq F32; dims 1024 / 16 x 64 / FFN 2048 /
+ * mel 100, any depth. */
+int gsvcu_dit_load(int device, const char* path, gsvcu_dit** out);
+void gsvcu_dit_destroy(gsvcu_dit* ctx);
+const char* gsvcu_dit_last_error(const gsvcu_dit* ctx);
+int gsvcu_dit_get_hparams(const gsvcu_dit* ctx, gsvcu_dit_hparams* out);
+/* The static cache of gsv_dit::prepare (src/gsv_dit.cpp:771-830): `cond` and `neg` are the condition and
+ * negative-condition rows [T][1024] (input_embed.proj of [prompt_x | text_embed] and [0 | text_embed], with
+ * its bias), x_lens the valid frames (<= 0: T). Also sets the RoPE tables. */
+int gsvcu_dit_set_condition(gsvcu_dit* ctx, const float* cond, const float* neg, int32_t T, int32_t x_lens);
+/* gsv_dit::velocity (src/gsv_dit.cpp:1325-1338): one estimator pass at time t; x_mel and vel [100][T]. */
+int gsvcu_dit_velocity(gsvcu_dit* ctx, const float* x_mel, float t, int32_t negative, float* vel);
+/* gsv_dit::sample's CFM loop (src/gsv_dit.cpp:1410-1478) on the set condition: x0 [100][T] the initial
+ * noise, the first P frames zeroed, `steps` Euler steps t = j / steps, guidance v + (v - v_neg) * cfg when
+ * cfg > 1e-5 (both branches in one batch); mel_out [100][T - P]. */
+int gsvcu_dit_sample(gsvcu_dit* ctx, const float* x0, int32_t P, int32_t steps, float cfg, float* mel_out);
+/* Test entry: the hidden state [2T][1024] (rows [0, T) conditioned, [T, 2T) negative) after the trunk and
+ * the first n_blocks blocks at time t. */
+int gsvcu_dit_op_hidden(gsvcu_dit* ctx, const float* x_mel, float t, int32_t n_blocks, float* hidden);
+/* The context's CUDA stream (cudaStream_t), for timing. */
+int gsvcu_dit_stream(gsvcu_dit* ctx, void** out);
+
 /* ---------------------------------------------------------------- profiling (GSV_AR_PROFILE buckets,
  * reference src/gsv_ar.cpp:18-42) */
 

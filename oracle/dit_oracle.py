@@ -1,0 +1,198 @@
+"""CPU restatement of gsv.cpp's DiT / CFM velocity estimator -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline / --impl reference leg use this
+module; it checks the CUDA library and is never a fallback for it.
+
+It follows the reference graph (src/gsv_dit.cpp) op by op in numpy:
+  time_sin              :755-769   SinusPositionEmbedding(256), float32 expf / sinf / cosf
+  time_embed            :278-284   Linear 256 -> 1024, SiLU, Linear 1024 -> 1024
+  build_trunk           :533-549   x = proj_mel(x_mel) + condition; conv_pos twice (grouped conv1d,
+                                   k = 31, 16 groups, zero padding 15, bias + Mish), * mask, + x
+  dit_block             :407-433   AdaLN-Zero modulation, LN * (1 + scale) + shift (layernorm_affine,
+                                   eps 1e-6), to_q / to_k / to_v, RoPE of head 0 (:191-200: adjacent
+                                   pairs, angle n * inv_freq[i]), flash attention with the key padding
+                                   mask (:333-346), to_out * mask, gated residual, FFN with GELU (tanh),
+                                   gated residual
+  build_head            :563-576   norm_out (scale, shift) + proj_out
+  sample                :1410-1478 Euler steps t = j / steps with guidance v + (v - v_neg) * cfg, the
+                                   prompt frames zeroed
+Numerics: ggml's mul_mat with F16 weights converts the activations to F16 before the dot products,
+so every matrix product here takes f16-rounded activations against the f16 weights, summed in
+float64 and rounded to float32 once; everything else is float32 (LayerNorm statistics float64).
+GELU is evaluated with the tanh formula in float32 (torch's approximate="tanh"), not with ggml's
+fp16 lookup table. Parity with the CUDA path is a relative-L2 tolerance, not bitwise.
+Parity unpinned: the reference DiT needs ggml (absent here) and ships no DiT golden vectors, so this
+restatement is checked against the reference's formulas only, not against a run of the reference.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+D, NH, HD, MEL, FF = 1024, 16, 64, 100, 2048
+KCP, GCP, ICG = 31, 16, 64
+
+
+def load(path: str) -> dict:
+    """Tensors of a DiT GGUF as float32 numpy arrays (shapes in torch order: [out][in])."""
+    from gguf import GGUFReader
+
+    r = GGUFReader(path)
+    W = {}
+    for t in r.tensors:
+        a = np.asarray(t.data)
+        shape = tuple(int(x) for x in reversed(t.shape.tolist()))
+        W[t.name] = a.astype(np.float32).reshape(shape)
+    depth = 0
+    while f"dit.transformer_blocks.{depth}.attn.to_q.weight" in W:
+        depth += 1
+    W["depth"] = depth
+    return W
+
+
+def f16(x: np.ndarray) -> np.ndarray:
+    return np.asarray(x, dtype=np.float32).astype(np.float16).astype(np.float32)
+
+
+def mm(x: np.ndarray, w: np.ndarray, b: np.ndarray | None = None) -> np.ndarray:
+    """ggml mul_mat with an F16 weight: x [R][K] (f16-rounded) . w[N][K]^T, double sums, + bias."""
+    y = (f16(x).astype(np.float64) @ w.astype(np.float64).T).astype(np.float32)
+    return y + b.astype(np.float32) if b is not None else y
+
+
+def silu(x):
+    x = np.asarray(x, dtype=np.float32)
+    return (x / (np.float32(1) + np.exp(-x))).astype(np.float32)
+
+
+def mish(x):
+    x = np.asarray(x, dtype=np.float32)
+    sp = np.where(x > 20, x, np.log1p(np.exp(np.minimum(x, 20)))).astype(np.float32)
+    return (x * np.tanh(sp)).astype(np.float32)
+
+
+def gelu_tanh(x):
+    x = np.asarray(x, dtype=np.float32)
+    u = np.float32(0.7978845608028654) * (x + np.float32(0.044715) * x * x * x)
+    return (np.float32(0.5) * x * (np.float32(1) + np.tanh(u))).astype(np.float32)
+
+
+def time_sin(t: float) -> np.ndarray:
+    e = np.float32(np.log(10000.0) / 127.0)
+    freq = np.exp(-e * np.arange(128, dtype=np.float32)).astype(np.float32)
+    a = (np.float32(1000.0) * np.float32(t) * freq).astype(np.float32)
+    return np.concatenate([np.sin(a), np.cos(a)]).astype(np.float32)
+
+
+def layernorm_mod(x: np.ndarray, scale: np.ndarray, shift: np.ndarray) -> np.ndarray:
+    x64 = x.astype(np.float64)
+    mean = x64.mean(axis=-1, keepdims=True)
+    var = ((x64 - mean) ** 2).mean(axis=-1, keepdims=True)
+    y = ((x64 - mean) / np.sqrt(var + 1e-6)).astype(np.float32)
+    return (y * (np.float32(1) + scale) + shift).astype(np.float32)
+
+
+def rope_tables(inv_freq: np.ndarray, T: int):
+    a = (np.arange(T, dtype=np.float32)[:, None] * inv_freq[None, :].astype(np.float32)).astype(np.float32)
+    return np.cos(a).astype(np.float32), np.sin(a).astype(np.float32)
+
+
+def rope64(x: np.ndarray, cs: np.ndarray, sn: np.ndarray) -> np.ndarray:
+    """Adjacent pairs (2i, 2i + 1) of the first 64 columns rotated by angle t * inv_freq[i]."""
+    y = x.copy()
+    x0, x1 = x[:, 0:64:2], x[:, 1:64:2]
+    y[:, 0:64:2] = x0 * cs - x1 * sn
+    y[:, 1:64:2] = x0 * sn + x1 * cs
+    return y
+
+
+def conv_pos(x: np.ndarray, w: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """Grouped conv1d (16 groups of 64 channels, 31 taps, zero padding 15) of x [T][1024], + bias.
+    w: the exporter's [G][OCg][ICg * 31] with inner index ic * 31 + tap."""
+    T = x.shape[0]
+    xp = np.zeros((T + KCP - 1, D), dtype=np.float32)
+    xp[KCP // 2:KCP // 2 + T] = f16(x)
+    out = np.empty((T, D), dtype=np.float32)
+    idx = np.arange(T)[:, None] + np.arange(KCP)[None, :]   # [T][31]
+    for g in range(GCP):
+        win = xp[:, g * ICG:(g + 1) * ICG][idx]                # [T][31][64]
+        cols = win.transpose(0, 2, 1).reshape(T, ICG * KCP)   # inner index ic * 31 + tap
+        out[:, g * ICG:(g + 1) * ICG] = (cols.astype(np.float64) @ w[g].astype(np.float64).T).astype(np.float32)
+    return out + b
+
+
+def attention(q, k, v, x_lens):
+    """Softmax(q k^T / 8) v per head over keys < x_lens; q, k, v [T][1024] -> [T][1024]."""
+    T = q.shape[0]
+    out = np.empty((T, D), dtype=np.float32)
+    for h in range(NH):
+        sl = slice(h * HD, (h + 1) * HD)
+        s = (q[:, sl].astype(np.float64) @ k[:x_lens, sl].astype(np.float64).T) * 0.125
+        s -= s.max(axis=1, keepdims=True)
+        p = np.exp(s)
+        p /= p.sum(axis=1, keepdims=True)
+        out[:, sl] = (p @ v[:x_lens, sl].astype(np.float64)).astype(np.float32)
+    return out
+
+
+def time_embed(W, t: float) -> np.ndarray:
+    h = silu(mm(time_sin(t)[None, :], W["dit.time_embed.time_mlp.0.weight"], W["dit.time_embed.time_mlp.0.bias"]))
+    return mm(h, W["dit.time_embed.time_mlp.2.weight"], W["dit.time_embed.time_mlp.2.bias"])[0]
+
+
+def branch(W, x_mel: np.ndarray, t: float, cond: np.ndarray, x_lens: int, n_blocks: int | None = None,
+           head: bool = True) -> np.ndarray:
+    """One estimator pass of one branch: x_mel [100][T] and cond [T][1024] -> vel [100][T] (head) or the
+    hidden state [T][1024] after n_blocks blocks."""
+    T = x_mel.shape[1]
+    depth = W["depth"] if n_blocks is None else min(n_blocks, W["depth"])
+    mask = (np.arange(T) < x_lens).astype(np.float32)[:, None]
+    temb = time_embed(W, t)
+    st = silu(temb)[None, :]
+    x = mm(x_mel.T, W["dit.input_embed.proj.weight_mel"]) + cond
+    cp = mish(conv_pos(x * mask, W["dit.input_embed.conv_pos_embed.conv1d.0.weight"],
+                       W["dit.input_embed.conv_pos_embed.conv1d.0.bias"]))
+    cp = mish(conv_pos(cp, W["dit.input_embed.conv_pos_embed.conv1d.2.weight"],
+                       W["dit.input_embed.conv_pos_embed.conv1d.2.bias"])) * mask
+    x = (x + cp).astype(np.float32)
+    cs, sn = rope_tables(W["dit.rotary_embed.inv_freq"], T)
+    for li in range(depth):
+        p = f"dit.transformer_blocks.{li}."
+        m = mm(st, W[p + "attn_norm.linear.weight"], W[p + "attn_norm.linear.bias"])[0].reshape(6, D)
+        xn = layernorm_mod(x, m[1], m[0])
+        q = rope64(mm(xn, W[p + "attn.to_q.weight"], W[p + "attn.to_q.bias"]), cs, sn)
+        k = rope64(mm(xn, W[p + "attn.to_k.weight"], W[p + "attn.to_k.bias"]), cs, sn)
+        v = mm(xn, W[p + "attn.to_v.weight"], W[p + "attn.to_v.bias"])
+        a = mm(attention(q, k, v, x_lens), W[p + "attn.to_out.0.weight"], W[p + "attn.to_out.0.bias"]) * mask
+        x = (x + a * m[2]).astype(np.float32)
+        xn2 = layernorm_mod(x, m[4], m[3])
+        f = mm(gelu_tanh(mm(xn2, W[p + "ff.ff.0.0.weight"], W[p + "ff.ff.0.0.bias"])),
+               W[p + "ff.ff.2.weight"], W[p + "ff.ff.2.bias"])
+        x = (x + f * m[5]).astype(np.float32)
+    if not head:
+        return x
+    e2 = mm(st, W["dit.norm_out.linear.weight"], W["dit.norm_out.linear.bias"])[0]
+    xo = layernorm_mod(x, e2[:D], e2[D:])
+    return mm(xo, W["dit.proj_out.weight"], W["dit.proj_out.bias"]).T.copy()
+
+
+def sample(W, x0: np.ndarray, cond: np.ndarray, neg: np.ndarray, P: int, steps: int, cfg: float) -> np.ndarray:
+    """The CFM Euler loop on set conditions: x0 [100][T] -> mel [100][T - P]."""
+    x = x0.astype(np.float32).copy()
+    T = x.shape[1]
+    x[:, :P] = 0
+    dt = np.float32(1.0) / np.float32(steps)
+    for j in range(steps):
+        t = float(np.float32(j) * dt)
+        vel = branch(W, x, t, cond, T)
+        if cfg > 1e-5:
+            ng = branch(W, x, t, neg, T)
+            vel = (vel + (vel - ng) * np.float32(cfg)).astype(np.float32)
+        x = (x + dt * vel).astype(np.float32)
+        x[:, :P] = 0
+    return x[:, P:].copy()
+
+
+def rel_l2(a: np.ndarray, b: np.ndarray) -> float:
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))

@@ -1,0 +1,115 @@
+"""The DiT / CFM velocity estimator on B200 (gsvcu_dit_*, the role of gsv.cpp's gsv_dit,
+src/gsv_dit.cpp) against the CPU restatement (oracle/dit_oracle.py).
+
+Both take f16 activations into every matrix product against the f16 weights (ggml's mul_mat with F16
+weights), so the remaining differences are summation order and the attention: the GPU runs q, k, v and
+the softmax weights in f16 on the tensor cores (f32 accumulation), the oracle in float64. Bar: relative
+L2 <= 2e-3 on the hidden state after the trunk and after every block, and on the velocity."""
+import numpy as np
+import pytest
+
+import dit_oracle as O
+import gsv_synth as S
+from conftest import MODEL_CACHE, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-3
+
+
+@pytest.fixture(scope="module")
+def dit_small():
+    """2-block synthetic DiT (full width: 1024 / 16 x 64 / FFN 2048), F16 matrices."""
+    path = S.cached_dit_model(MODEL_CACHE, seed=1, depth=2)
+    return path, O.load(path)
+
+
+def _inputs(T, seed):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((100, T)).astype(np.float32)
+    cond = rng.standard_normal((T, 1024)).astype(np.float32)
+    neg = rng.standard_normal((T, 1024)).astype(np.float32)
+    return x, cond, neg
+
+
+@pytest.mark.parametrize("T,x_lens", [(300, 300), (300, 261), (64, 64)])
+def test_dit_hidden_after_each_block(dit_small, T, x_lens):
+    """Trunk (mel projection + condition, both grouped convolutions with Mish and the mask) and each DiT
+    block, both branches in one batch, T not a multiple of the 128-frame tile, with and without padding
+    frames (x_lens < T: masked keys, masked to_out and conv rows)."""
+    import gsvcu
+    path, W = dit_small
+    x, cond, neg = _inputs(T, 7 + T + x_lens)
+    d = gsvcu.Dit(path)
+    d.set_condition(cond, neg, x_lens)
+    for nb in range(W["depth"] + 1):
+        got = d.hidden(x, 0.35, nb)
+        for b, c in enumerate((cond, neg)):
+            ref = O.branch(W, x, 0.35, c, x_lens, n_blocks=nb, head=False)
+            r = rel_l2(got[b], ref)
+            print(f"T={T} x_lens={x_lens} blocks={nb} branch={b}: rel_l2 {r:.2e}")
+            assert r <= TOL, (nb, b, r)
+    d.close()
+
+
+def test_dit_velocity_matches_oracle(dit_small):
+    """gsv_dit::velocity for the positive and the negative branch."""
+    import gsvcu
+    path, W = dit_small
+    T = 300
+    x, cond, neg = _inputs(T, 3)
+    d = gsvcu.Dit(path)
+    d.set_condition(cond, neg)
+    for negative, c in ((False, cond), (True, neg)):
+        got = d.velocity(x, 0.6, negative)
+        ref = O.branch(W, x, 0.6, c, T)
+        r = rel_l2(got, ref)
+        print(f"velocity negative={negative}: rel_l2 {r:.2e}")
+        assert got.shape == (100, T) and r <= TOL
+    d.close()
+
+
+@pytest.mark.parametrize("cfg", [0.0, 2.0])
+def test_dit_sample_matches_oracle(dit_small, cfg):
+    """gsv_dit::sample's CFM loop: 4 Euler steps, prompt frames zeroed, with and without guidance."""
+    import gsvcu
+    path, W = dit_small
+    T, P, steps = 200, 40, 4
+    x0, cond, neg = _inputs(T, 11)
+    d = gsvcu.Dit(path)
+    d.set_condition(cond, neg)
+    got = d.sample(x0, P, steps, cfg)
+    ref = O.sample(W, x0, cond, neg, P, steps, cfg)
+    r = rel_l2(got, ref)
+    print(f"sample cfg={cfg}: rel_l2 {r:.2e}")
+    assert got.shape == (100, T - P) and r <= TOL
+    d.close()
+
+
+def test_dit_full_depth_runs_and_is_deterministic():
+    """The 22-block model at a production chunk length (500 prompt + 640 frames): finite, and two runs of
+    the guided sampler give identical bytes."""
+    import gsvcu
+    path = S.cached_dit_model(MODEL_CACHE, seed=0, depth=22)
+    T, P = 1140, 500
+    x0, cond, neg = _inputs(T, 5)
+    d = gsvcu.Dit(path)
+    assert d.hp.depth == 22
+    d.set_condition(cond, neg)
+    a = d.sample(x0, P, 2, 2.0)
+    b = d.sample(x0, P, 2, 2.0)
+    assert np.isfinite(a).all() and np.array_equal(a, b)
+    d.close()
+
+
+def test_dit_rejects_bad_calls(dit_small):
+    import gsvcu
+    path, _ = dit_small
+    d = gsvcu.Dit(path)
+    with pytest.raises(gsvcu.GsvcuError):
+        d.velocity(np.zeros((100, 10), np.float32), 0.1)   # before set_condition
+    x, cond, neg = _inputs(50, 1)
+    d.set_condition(cond, neg)
+    with pytest.raises(gsvcu.GsvcuError):
+        d.sample(x, 0, 2, 1.0)   # P must be in (0, T)
+    d.close()
