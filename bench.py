@@ -48,11 +48,12 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-chunks", type=int, default=3,
                     help="chunks (of --refill-every iterations) of the job the cpu_baseline sample runs")
+    ap.add_argument("--dit-steps", type=int, default=8, help="Euler steps per sample call of the dit workload")
     ap.add_argument("--kv-f32-steps", type=int, default=3,
                     help="jobs of the extra F32-KV (reference-exact) measurement; 0 skips it")
     ap.add_argument("--lookahead", action="store_true",
                     help="serve with gsvcu_set_serve_lookahead (the next chunk runs while the host handles results)")
-    ap.add_argument("--workload", default="serve", choices=["serve", "attn", "gemv", "prefill", "single", "bert"],
+    ap.add_argument("--workload", default="serve", choices=["serve", "attn", "gemv", "prefill", "single", "bert", "dit"],
                     help="serve: config-4 serving shard (the bench line); attn: config-3 decode-attention sweep; "
                          "gemv: config-3 Q8_0 GEMV sweep; prefill: config-2 prefill attention + GEMMs; "
                          "single: config-0 single-sequence decode latency; bert: the BERT feature producer "
@@ -309,6 +310,73 @@ def single_bench(args):
                       "note": "wall time on the library stream incl. prefill and the 16-step status reads",
                       "reference_cpu_ms_per_token": 12.55}))
     ctx.close()
+
+
+def dit_bench(args):
+    """The DiT / CFM estimator (gsv.cpp's gsv_dit, the stage after the AR path) at a production chunk: T =
+    1140 frames (500 reference frames + 640 generated, src/gsv_dit.cpp synthesize's chunk), 22 blocks of
+    1024 / 16 x 64 / FFN 2048, F16 matrices (the exporter's --spec lin=f16), seeded synthetic weights,
+    guided sampling (cfg 2: both branches, 2T rows, per step). Device time per guided step by CUDA events
+    on the DiT stream over `sample` calls of --dit-steps steps (inputs and outputs in host memory, so the
+    events also cover one H2D of x0 and one D2H of the mel per call), tensor FLOP/s against the measured
+    bf16 peak; beside it the CPU restatement (oracle) timed on one DiT block of one branch."""
+    import torch
+    import gsv_synth as S
+    import gsvcu
+    import dit_oracle as DO
+    path = S.cached_dit_model(MODEL_CACHE, seed=0, depth=22)
+    d = gsvcu.Dit(path)
+    T, P, steps, cfg = 1140, 500, args.dit_steps, 2.0
+    rng = np.random.default_rng(0)
+    x0 = rng.standard_normal((100, T)).astype(np.float32)
+    cond = rng.standard_normal((T, 1024)).astype(np.float32)
+    neg = rng.standard_normal((T, 1024)).astype(np.float32)
+    d.set_condition(cond, neg)
+    stream = torch.cuda.ExternalStream(d.stream_handle())
+    for _ in range(max(args.warmup, 3)):
+        d.sample(x0, P, steps, cfg)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dev_ms, wall_ms = [], []
+    for _ in range(max(args.steps, 3)):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        ev0.record(stream)
+        d.sample(x0, P, steps, cfg)
+        ev1.record(stream)
+        ev1.synchronize()
+        wall_ms.append(1e3 * (time.perf_counter() - t0))
+        dev_ms.append(ev0.elapsed_time(ev1))
+    ms = float(np.median(dev_ms)) / steps
+    R = 2 * T
+    flop_gemm = 2 * R * (4 * 1024 * 1024 + 2 * 1024 * 2048) * 22 + 2 * 2 * R * 1024 * 64 * 31 + 2 * R * 1024 * (128 + 128)
+    flop_attn = 4 * R * T * 1024 * 22
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak = float(json.load(f)["bf16_tflops"])
+    except (OSError, KeyError, ValueError):
+        peak = 1590.0   # the pool's earlier measurement, when the file is absent
+    tflops = (flop_gemm + flop_attn) / (ms * 1e-3) / 1e12
+    # CPU restatement: one block of one branch (the step runs 44 plus trunk and head)
+    W = DO.load(path)
+    W1 = {k: v for k, v in W.items() if not k.startswith("dit.transformer_blocks.") or k.startswith("dit.transformer_blocks.0.")}
+    W1["depth"] = 1
+    t0 = time.perf_counter()
+    DO.branch(W1, x0, 0.5, cond, T, n_blocks=1, head=False)
+    t1 = time.perf_counter()
+    DO.branch(W1, x0, 0.5, cond, T, n_blocks=0, head=False)
+    t2 = time.perf_counter()
+    blk = (t1 - t0) - (t2 - t1)
+    cpu_step_s = 44 * max(blk, 1e-3) + 2 * (t2 - t1)
+    print(json.dumps({"workload": "DiT / CFM guided sampling (gsv_dit::sample)", "model": "22 blocks, 1024 / 16 x 64 / "
+                      "FFN 2048, F16 matrices", "T": T, "prompt_frames": P, "steps_per_call": steps, "cfg": cfg,
+                      "ms_per_guided_step": ms, "frames_per_s": (T - P) / (ms * steps * 1e-3),
+                      "wall_ms_per_call": float(np.median(wall_ms)),
+                      "gflop_per_step": {"gemm": flop_gemm / 1e9, "attention": flop_attn / 1e9},
+                      "tflops": tflops, "peak_bf16_tflops": peak, "frac_of_peak": tflops / peak if peak else None,
+                      "cpu_baseline": {"ms_per_guided_step": 1e3 * cpu_step_s, "cores": os.cpu_count() or 1,
+                                       "kind": "port", "sample": "oracle (numpy) DiT block 0 of one branch timed, "
+                                       "x 44 blocks + 2 x trunk per guided step"}}))
+    d.close()
 
 
 def bert_bench(args):
@@ -661,7 +729,7 @@ def main():
     if args.workload != "serve":
         if rank == 0:
             {"attn": attn_sweep, "gemv": gemv_sweep, "prefill": prefill_bench, "single": single_bench,
-             "bert": bert_bench}[args.workload](args)
+             "bert": bert_bench, "dit": dit_bench}[args.workload](args)
         return
 
     if args.impl == "reference":

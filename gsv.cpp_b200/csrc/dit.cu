@@ -29,6 +29,7 @@
 #include <cuda.h>
 #include <cuda_fp16.h>
 
+#include <atomic>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -63,7 +64,8 @@ constexpr float ATTN_SCALE = 0.125f;   // 1/sqrt(64)
 // ------------------------------------------------------------------ tcgen05 GEMM
 constexpr int GM = 128;           // frames per tile (UMMA M, TMEM lanes)
 constexpr int GK = 64;            // K per stage (one 128-byte swizzle row of f16)
-constexpr int GS = 3;             // stages (about 97 KB of shared memory: two CTAs per SM)
+// stages: 3 (about 97 KB of shared memory at BN = 128: two CTAs per SM) when the grid has more tiles than
+// SMs, else 6 (one CTA per SM keeps 192 KB of operands in flight)
 constexpr int G_THREADS = 192;    // warp 0 TMA, warp 1 TMEM + MMA, warps 2-5 epilogue
 
 enum { DE_F16 = 0, DE_QKV = 1, DE_RESID = 2, DE_F32 = 3 };
@@ -73,7 +75,6 @@ struct DitGemmArgs {
     int R;                  // rows (frames of every branch)
     int T;                  // frames per branch (row r is frame r % T of branch r / T)
     int N, K;
-    int act;
     const float* bias;      // [N] or null
     __half* out16;          // DE_F16 / DE_QKV: [R][ld]
     float* out32;           // DE_RESID (in place) / DE_F32: [R][ld]
@@ -87,33 +88,54 @@ struct DitGemmArgs {
     int* err;
 };
 
-template <int BN>
+// Shared memory: the operand stages (1024-byte aligned), barriers, TMEM address and abort flag, the tile's
+// bias and gate (f32), and for PRE epilogues the tile's rows of the residual / addend (f32, rows padded by
+// 16 bytes so that 32 lanes reading 32 rows hit distinct banks).
+template <int BN, int GS, bool PRE>
 struct GemmSmem {
     static constexpr int STAGE_A = GM * GK * 2;
     static constexpr int STAGE_B = BN * GK * 2;
+    static constexpr int XSTR = BN * 4 + 16;
     static constexpr size_t OFF_B = (size_t)GS * STAGE_A;
     static constexpr size_t OFF_BAR = OFF_B + (size_t)GS * STAGE_B;
-    static constexpr size_t SMEM = OFF_BAR + (2 * GS + 1) * 8 + 16 + 1024;   // + slack for the 1024 alignment
+    static constexpr size_t OFF_PAR = OFF_BAR + (2 * GS + 1) * 8 + 8;
+    static constexpr size_t OFF_X = OFF_PAR + 2 * BN * 4;
+    static constexpr size_t SMEM = OFF_X + (PRE ? (size_t)GM * XSTR : 0) + 1024;   // + slack for the alignment
 };
 
-__device__ __forceinline__ float act_f(float v, int act) {
-    if (act == ACT_GELU_TANH) {   // torch GELU(approximate="tanh")
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *(const uint32_t*)&h;
+}
+
+static_assert(GemmSmem<128, 6, false>::SMEM <= 232448 && 2 * GemmSmem<128, 3, false>::SMEM <= 233472 &&
+                  GemmSmem<128, 4, true>::SMEM <= 232448 && 2 * GemmSmem<64, 3, true>::SMEM <= 233472,
+              "shared memory per SM");
+
+template <int ACT>
+__device__ __forceinline__ float act_f(float v) {
+    if (ACT == ACT_GELU_TANH) {   // torch GELU(approximate="tanh")
         const float u = 0.7978845608028654f * (v + 0.044715f * v * v * v);
         return 0.5f * v * (1.0f + tanhf(u));
     }
-    if (act == ACT_MISH) {        // x * tanh(softplus(x)), softplus with torch's threshold 20
+    if (ACT == ACT_MISH) {        // x * tanh(softplus(x)), softplus with torch's threshold 20
         const float sp = v > 20.0f ? v : log1pf(expf(v));
         return v * tanhf(sp);
     }
     return v;
 }
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool pred) {
+    const int n = pred ? 16 : 0;   // zero-fill when the row is out of range
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n) : "memory");
+}
 
 // D[frames][features] = A[frames][K] . B[features][K]^T, K-major f16 operands. CONV: A is the 3D map
 // [branch][frame][1024] and stage s is tap s of group blockIdx.x (channels 64 g .. 64 g + 63).
-template <int EPI, int BN, bool CONV>
+template <int EPI, int ACT, int BN, bool CONV, int GS>
 __global__ void __launch_bounds__(G_THREADS) k_dit_gemm(const __grid_constant__ CUtensorMap ma,
                                                         const __grid_constant__ CUtensorMap mb, const DitGemmArgs p) {
-    using L = GemmSmem<BN>;
+    constexpr bool PRE = EPI == DE_RESID || EPI == DE_F32;
+    using L = GemmSmem<BN, GS, PRE>;
     constexpr uint32_t IDESC = idesc_f16(GM, BN);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = smem_raw + ((1024u - (su32(smem_raw) & 1023u)) & 1023u);
@@ -205,24 +227,42 @@ __global__ void __launch_bounds__(G_THREADS) k_dit_gemm(const __grid_constant__ 
                 if (bar_try(tfull, 0)) break;
         }
     } else {
-        // epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 = frames of this tile
+        // epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 = frames of this tile. While the MMAs run,
+        // the tile's bias and gate go to shared memory and the tile's rows of the residual (or addend) are
+        // copied in by coalesced cp.async, so no dependent global load is left for after the accumulator.
         const int q = warp & 3;
         const int fr = 32 * q + lane;   // frame (row) within the tile
-        int row;
-        bool valid;
-        if (CONV) {
-            valid = f0 + fr < p.T;
-            row = row0 + fr;
-        } else {
-            row = row0 + fr;
-            valid = row < p.R;
+        const int row = row0 + fr;
+        const bool valid = CONV ? f0 + fr < p.T : row < p.R;
+        const int et = tid - 64;        // 0..127 over the epilogue warps
+        float* sbias = (float*)(sm + L::OFF_PAR);
+        float* sgate = sbias + BN;
+        for (int i = et; i < BN; i += 128) {
+            sbias[i] = p.bias ? p.bias[n0 + i] : 0.0f;
+            sgate[i] = (EPI == DE_RESID && p.gate) ? p.gate[n0 + i] : 1.0f;
         }
+        const float* xsrc = EPI == DE_RESID ? p.out32 : p.add;
+        uint8_t* sx = sm + L::OFF_X;
+        if (PRE && xsrc) {
+            constexpr int CPR = BN / 4;   // 16-byte chunks per row
+#pragma unroll 4
+            for (int i = et; i < GM * CPR; i += 128) {
+                const int r = i / CPR, ch = i - r * CPR;
+                const bool in = CONV ? f0 + r < p.T : row0 + r < p.R;
+                const float* g = xsrc + (size_t)(in ? row0 + r : 0) * p.ld + n0 + 4 * ch;
+                cp_async16(su32(sx + (size_t)r * L::XSTR + 16 * ch), g, in);
+            }
+            asm volatile("cp.async.commit_group;" ::: "memory");
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");   // the four epilogue warps: staging complete
         const bool ok = bar_wait_warp(tfull, 0, abort_flag) && !*abort_flag;
         tc_fence_after();
         if (ok) {
             const int t = row % p.T;
             const float mask = (EPI == DE_RESID && p.use_mask && t >= p.x_lens) ? 0.0f : 1.0f;
             const uint32_t tb = tmem + ((uint32_t)(32 * q) << 16);
+            const float* xrow = (const float*)(sx + (size_t)fr * L::XSTR);
 #pragma unroll 1
             for (int c = 0; c < BN; c += 16) {
                 float v[16];
@@ -231,64 +271,46 @@ __global__ void __launch_bounds__(G_THREADS) k_dit_gemm(const __grid_constant__ 
                 tmem_wait_ld();
                 tmem_bind(v);
                 const int f = n0 + c;
-                if (p.bias) {
 #pragma unroll
-                    for (int i = 0; i < 16; i += 4) {
-                        const float4 b4 = __ldg((const float4*)(p.bias + f + i));
-                        v[i] += b4.x; v[i + 1] += b4.y; v[i + 2] += b4.z; v[i + 3] += b4.w;
-                    }
-                }
+                for (int i = 0; i < 16; i++) v[i] += sbias[c + i];
                 if (valid) {
-                if (EPI == DE_QKV && (n0 == 0 || n0 == DM) && c < HDD) {
-                    // RoPE on head 0 of q and k: pairs (2i, 2i + 1) share angle t * inv_freq[i]
+                    if (EPI == DE_QKV && (n0 == 0 || n0 == DM) && c < HDD) {
+                        // RoPE on head 0 of q and k: pairs (2i, 2i + 1) share angle t * inv_freq[i]
 #pragma unroll
-                    for (int i = 0; i < 16; i += 2) {
-                        const int pi = (c + i) >> 1;
-                        const float cs = __ldg(p.rcos + (size_t)t * 32 + pi), sn = __ldg(p.rsin + (size_t)t * 32 + pi);
-                        const float x0 = v[i], x1 = v[i + 1];
-                        v[i] = x0 * cs - x1 * sn;
-                        v[i + 1] = x0 * sn + x1 * cs;
-                    }
-                }
-                if (EPI == DE_F16 || EPI == DE_QKV) {
-                    uint32_t w[8];
-#pragma unroll
-                    for (int i = 0; i < 8; i++) {
-                        const __half2 h = __floats2half2_rn(act_f(v[2 * i], p.act), act_f(v[2 * i + 1], p.act));
-                        w[i] = *(const uint32_t*)&h;
-                    }
-                    uint4* dst = (uint4*)(p.out16 + (size_t)row * p.ld + f);
-                    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-                    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-                } else if (EPI == DE_RESID) {
-                    float4* dst = (float4*)(p.out32 + (size_t)row * p.ld + f);
-#pragma unroll
-                    for (int i = 0; i < 16; i += 4) {
-                        float4 x = dst[i / 4];
-                        float g[4] = {1.0f, 1.0f, 1.0f, 1.0f};
-                        if (p.gate) {
-                            const float4 g4 = __ldg((const float4*)(p.gate + f + i));
-                            g[0] = g4.x; g[1] = g4.y; g[2] = g4.z; g[3] = g4.w;
+                        for (int i = 0; i < 16; i += 2) {
+                            const int pi = (c + i) >> 1;
+                            const float cs = __ldg(p.rcos + (size_t)t * 32 + pi), sn = __ldg(p.rsin + (size_t)t * 32 + pi);
+                            const float x0 = v[i], x1 = v[i + 1];
+                            v[i] = x0 * cs - x1 * sn;
+                            v[i + 1] = x0 * sn + x1 * cs;
                         }
-                        x.x += act_f(v[i], p.act) * mask * g[0];
-                        x.y += act_f(v[i + 1], p.act) * mask * g[1];
-                        x.z += act_f(v[i + 2], p.act) * mask * g[2];
-                        x.w += act_f(v[i + 3], p.act) * mask * g[3];
-                        dst[i / 4] = x;
                     }
-                } else {   // DE_F32
-                    float4* dst = (float4*)(p.out32 + (size_t)row * p.ld + f);
-                    const float4* ad = p.add ? (const float4*)(p.add + (size_t)row * p.ld + f) : nullptr;
+                    if (EPI == DE_F16 || EPI == DE_QKV) {
+                        uint32_t w[8];
 #pragma unroll
-                    for (int i = 0; i < 16; i += 4) {
-                        float4 y = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-                        if (ad) {
-                            const float4 a4 = ad[i / 4];
-                            y.x += a4.x; y.y += a4.y; y.z += a4.z; y.w += a4.w;
+                        for (int i = 0; i < 8; i++) w[i] = pack_h2(act_f<ACT>(v[2 * i]), act_f<ACT>(v[2 * i + 1]));
+                        uint4* dst = (uint4*)(p.out16 + (size_t)row * p.ld + f);
+                        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+                    } else if (EPI == DE_RESID) {
+                        float4* dst = (float4*)(p.out32 + (size_t)row * p.ld + f);
+#pragma unroll
+                        for (int i = 0; i < 16; i += 4) {
+                            float4 x = *(const float4*)(xrow + c + i);
+                            x.x += act_f<ACT>(v[i]) * mask * sgate[c + i];
+                            x.y += act_f<ACT>(v[i + 1]) * mask * sgate[c + i + 1];
+                            x.z += act_f<ACT>(v[i + 2]) * mask * sgate[c + i + 2];
+                            x.w += act_f<ACT>(v[i + 3]) * mask * sgate[c + i + 3];
+                            dst[i / 4] = x;
                         }
-                        dst[i / 4] = y;
+                    } else {   // DE_F32: + the addend row (none: + 0)
+                        float4* dst = (float4*)(p.out32 + (size_t)row * p.ld + f);
+#pragma unroll
+                        for (int i = 0; i < 16; i += 4) {
+                            const float4 a4 = xsrc ? *(const float4*)(xrow + c + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+                            dst[i / 4] = make_float4(v[i] + a4.x, v[i + 1] + a4.y, v[i + 2] + a4.z, v[i + 3] + a4.w);
+                        }
                     }
-                }
                 }
             }
         }
@@ -322,14 +344,6 @@ __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool pred) {
-    const int n = pred ? 16 : 0;   // zero-fill when the row is out of range
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n) : "memory");
-}
-__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
-    const __half2 h = __floats2half2_rn(lo, hi);
-    return *(const uint32_t*)&h;
 }
 
 // qkv: [R][3072] f16 (q | k | v, head h at columns 64 h of each), rows b T + t. out: [R][1024] f16.
@@ -631,48 +645,69 @@ bool map_conv(CUtensorMap* m, const __half* base, int T, int B) {
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int EPI, int BN, bool CONV>
+template <int EPI, int ACT, int BN, bool CONV, int GS>
 cudaError_t set_gemm_smem() {
-    return cudaFuncSetAttribute(k_dit_gemm<EPI, BN, CONV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)GemmSmem<BN>::SMEM);
+    return cudaFuncSetAttribute(k_dit_gemm<EPI, ACT, BN, CONV, GS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)GemmSmem<BN, GS, EPI == DE_RESID || EPI == DE_F32>::SMEM);
+}
+template <int EPI, int ACT, int BN, bool CONV, int GS>
+void launch_gemm(dim3 grid, const CUtensorMap& ma, const CUtensorMap& mb, const DitGemmArgs& a, cudaStream_t s) {
+    launch_pdl(k_dit_gemm<EPI, ACT, BN, CONV, GS>, grid, dim3(G_THREADS),
+               GemmSmem<BN, GS, EPI == DE_RESID || EPI == DE_F32>::SMEM, s, ma, mb, a);
 }
 
+std::atomic<int> g_sms{148};   // SMs of the device (set by init_device; contexts may load from several threads)
+
+// The variants the estimator launches: the residual / addend epilogues stage their rows (4 stages, one
+// CTA per SM); the others run 3 stages, two CTAs per SM, or 6 when the grid has at most one tile per SM.
 cudaError_t init_device() {
     cudaError_t e;
-    if ((e = set_gemm_smem<DE_F16, 128, false>())) return e;
-    if ((e = set_gemm_smem<DE_QKV, 128, false>())) return e;
-    if ((e = set_gemm_smem<DE_RESID, 128, false>())) return e;
-    if ((e = set_gemm_smem<DE_F32, 128, false>())) return e;
-    if ((e = set_gemm_smem<DE_F16, 64, true>())) return e;
-    if ((e = set_gemm_smem<DE_RESID, 64, true>())) return e;
+    int dev = 0;
+    int sms = 0;
+    if ((e = cudaGetDevice(&dev)) || (e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev))) return e;
+    g_sms.store(sms, std::memory_order_relaxed);
+    if ((e = set_gemm_smem<DE_F32, ACT_NONE, 128, false, 4>())) return e;
+    if ((e = set_gemm_smem<DE_RESID, ACT_NONE, 128, false, 4>())) return e;
+    if ((e = set_gemm_smem<DE_QKV, ACT_NONE, 128, false, 3>())) return e;
+    if ((e = set_gemm_smem<DE_QKV, ACT_NONE, 128, false, 6>())) return e;
+    if ((e = set_gemm_smem<DE_F16, ACT_GELU_TANH, 128, false, 3>())) return e;
+    if ((e = set_gemm_smem<DE_F16, ACT_GELU_TANH, 128, false, 6>())) return e;
+    if ((e = set_gemm_smem<DE_F16, ACT_MISH, 64, true, 3>())) return e;
+    if ((e = set_gemm_smem<DE_RESID, ACT_MISH, 64, true, 3>())) return e;
     return cudaSuccess;
 }
 
-// Plain GEMM over R rows: A [R][K] f16, W [N][K] f16.
+// Plain GEMM over R rows: A [R][K] f16, W [N][K] f16. epi / act: DE_F32 and DE_RESID without activation,
+// DE_QKV, DE_F16 with GELU (tanh).
 bool gemm(int epi, const __half* A, const __half* W, const DitGemmArgs& a, cudaStream_t s) {
     CUtensorMap ma, mb;
     if (!map_2d(&ma, A, (uint64_t)a.R, (uint64_t)a.K, GM) || !map_2d(&mb, W, (uint64_t)a.N, (uint64_t)a.K, 128))
         return false;
     const dim3 grid(a.N / 128, (a.R + GM - 1) / GM);
-    const size_t sm = GemmSmem<128>::SMEM;
+    const bool wide = (int)(grid.x * grid.y) > g_sms.load(std::memory_order_relaxed);
     switch (epi) {
-        case DE_F16: launch_pdl(k_dit_gemm<DE_F16, 128, false>, grid, dim3(G_THREADS), sm, s, ma, mb, a); break;
-        case DE_QKV: launch_pdl(k_dit_gemm<DE_QKV, 128, false>, grid, dim3(G_THREADS), sm, s, ma, mb, a); break;
-        case DE_RESID: launch_pdl(k_dit_gemm<DE_RESID, 128, false>, grid, dim3(G_THREADS), sm, s, ma, mb, a); break;
-        default: launch_pdl(k_dit_gemm<DE_F32, 128, false>, grid, dim3(G_THREADS), sm, s, ma, mb, a); break;
+        case DE_F32: launch_gemm<DE_F32, ACT_NONE, 128, false, 4>(grid, ma, mb, a, s); break;
+        case DE_RESID: launch_gemm<DE_RESID, ACT_NONE, 128, false, 4>(grid, ma, mb, a, s); break;
+        case DE_QKV:
+            if (wide) launch_gemm<DE_QKV, ACT_NONE, 128, false, 3>(grid, ma, mb, a, s);
+            else launch_gemm<DE_QKV, ACT_NONE, 128, false, 6>(grid, ma, mb, a, s);
+            break;
+        default:
+            if (wide) launch_gemm<DE_F16, ACT_GELU_TANH, 128, false, 3>(grid, ma, mb, a, s);
+            else launch_gemm<DE_F16, ACT_GELU_TANH, 128, false, 6>(grid, ma, mb, a, s);
+            break;
     }
     return true;
 }
 
-// Grouped conv (16 groups of 64 channels, 31 taps, zero padding 15) over B branches of T frames:
-// X [B][T][1024] f16, Wc [1024][31 * 64] f16 (tap-major K).
+// Grouped conv (16 groups of 64 channels, 31 taps, zero padding 15) over B branches of T frames, bias +
+// Mish: X [B][T][1024] f16, Wc [1024][31 * 64] f16 (tap-major K); DE_F16 or DE_RESID.
 bool conv(int epi, const __half* X, const __half* Wc, int B, const DitGemmArgs& a, cudaStream_t s) {
     CUtensorMap ma, mb;
     if (!map_conv(&ma, X, a.T, B) || !map_2d(&mb, Wc, (uint64_t)DM, (uint64_t)KCONV, 64)) return false;
     const dim3 grid(GCP, B * ((a.T + GM - 1) / GM));
-    const size_t sm = GemmSmem<64>::SMEM;
-    if (epi == DE_F16) launch_pdl(k_dit_gemm<DE_F16, 64, true>, grid, dim3(G_THREADS), sm, s, ma, mb, a);
-    else launch_pdl(k_dit_gemm<DE_RESID, 64, true>, grid, dim3(G_THREADS), sm, s, ma, mb, a);
+    if (epi == DE_F16) launch_gemm<DE_F16, ACT_MISH, 64, true, 3>(grid, ma, mb, a, s);
+    else launch_gemm<DE_RESID, ACT_MISH, 64, true, 3>(grid, ma, mb, a, s);
     return true;
 }
 
@@ -831,7 +866,7 @@ int gsvcu_dit::forward(int B, int negative, const float* tsin_dev, int n_blocks,
                x_lens, a16);
     {
         DitGemmArgs g = a;
-        g.N = DM; g.K = KCONV; g.bias = b_c0; g.act = ACT_MISH; g.out16 = c16; g.ld = DM;
+        g.N = DM; g.K = KCONV; g.bias = b_c0; g.out16 = c16; g.ld = DM;
         if (!conv(DE_F16, a16, w_c0, B, g, s)) return fail(GSVCU_ERR_CUDA, "tensor map encoding failed");
         g.bias = b_c2; g.out16 = nullptr; g.out32 = x; g.use_mask = 1;
         if (!conv(DE_RESID, c16, w_c2, B, g, s)) return fail(GSVCU_ERR_CUDA, "tensor map encoding failed");
@@ -851,7 +886,7 @@ int gsvcu_dit::forward(int B, int negative, const float* tsin_dev, int n_blocks,
         if (!gemm(DE_RESID, a16, w.wo, g, s)) return fail(GSVCU_ERR_CUDA, "tensor map encoding failed");
         launch_pdl(k_dit_lnmod, rows8, dim3(256), 0, s, (const float*)x, R, m + 3 * DM, m + 4 * DM, a16);
         g = a;
-        g.N = FFD; g.K = DM; g.bias = w.b1; g.act = ACT_GELU_TANH; g.out16 = h16; g.ld = FFD;
+        g.N = FFD; g.K = DM; g.bias = w.b1; g.out16 = h16; g.ld = FFD;
         if (!gemm(DE_F16, a16, w.w1, g, s)) return fail(GSVCU_ERR_CUDA, "tensor map encoding failed");
         g = a;
         g.N = DM; g.K = FFD; g.bias = w.b2; g.out32 = x; g.ld = DM; g.gate = m + 5 * DM;
