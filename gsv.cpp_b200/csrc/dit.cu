@@ -18,8 +18,10 @@
 //                 implicit GEMMs: K runs over the 31 taps x 64 input channels of a group, and the tap's
 //                 activation tile is a TMA load at frame offset tap - 15 of a 3D [branch][frame][channel]
 //                 map, whose out-of-range frames read as zero (the conv's zero padding, per branch).
-//   k_dit_attn    16 heads x 64 dims, non-causal, key padding mask: flash attention on mma.sync
-//                 m16n8k16 f16 with f32 accumulators and an online softmax.
+//   k_dit_attn_tc 16 heads x 64 dims, non-causal, key padding mask, on tcgen05: S = Q K^T and O += P V^T
+//                 in TMEM, the softmax in registers (thread = query row), P through shared memory; two
+//                 passes (row maxima, then exponentials) so O is never rescaled. The QKV epilogue writes v
+//                 transposed ([branch][head][dim][frame]) for the K-major P V^T operand.
 //   k_dit_lnmod   LayerNorm (eps 1e-6, no affine) * (1 + scale) + shift -> f16 GEMM operand.
 //   k_dit_gemv    the time MLP and every block's AdaLN projection (one launch for all blocks per step).
 //   small kernels for the mel packing, the masked conv input and the Euler / guidance update.
@@ -85,6 +87,8 @@ struct DitGemmArgs {
     int use_mask;
     const float* rcos;      // DE_QKV: [T][32] RoPE tables of head 0
     const float* rsin;
+    __half* vt16;           // DE_QKV: v transposed, [branch][head][64 dims][tp frames], or null
+    int tp;
     int* err;
 };
 
@@ -185,7 +189,7 @@ __global__ void __launch_bounds__(G_THREADS) k_dit_gemm(const __grid_constant__ 
             int ks = 0;
             for (; ks < nstage; ks++) {
                 const int s = ks % GS;
-                if (!bar_wait(empty(s), ((uint32_t)(ks / GS) & 1u) ^ 1u, abort_flag)) break;
+                if (!bar_wait_short(empty(s), ((uint32_t)(ks / GS) & 1u) ^ 1u, abort_flag)) break;
                 bar_expect_tx(full(s), L::STAGE_A + L::STAGE_B);
                 const uint32_t da = su32(sm + (size_t)s * L::STAGE_A), db = su32(sm + L::OFF_B + (size_t)s * L::STAGE_B);
                 if (CONV) {
@@ -210,7 +214,7 @@ __global__ void __launch_bounds__(G_THREADS) k_dit_gemm(const __grid_constant__ 
             int ks = 0;
             for (; ks < nstage; ks++) {
                 const int s = ks % GS;
-                if (!bar_wait(full(s), (uint32_t)(ks / GS) & 1u, abort_flag)) break;
+                if (!bar_wait_short(full(s), (uint32_t)(ks / GS) & 1u, abort_flag)) break;
                 tc_fence_after();
                 const uint32_t a = su32(sm + (size_t)s * L::STAGE_A), b = su32(sm + L::OFF_B + (size_t)s * L::STAGE_B);
 #pragma unroll
@@ -285,7 +289,14 @@ __global__ void __launch_bounds__(G_THREADS) k_dit_gemm(const __grid_constant__ 
                             v[i + 1] = x0 * sn + x1 * cs;
                         }
                     }
-                    if (EPI == DE_F16 || EPI == DE_QKV) {
+                    if (EPI == DE_QKV && p.vt16 && n0 >= 2 * DM) {
+                        // v also as [branch][head][dim][frame]: 32 lanes = 32 consecutive frames of one dim
+                        const int bq = row / p.T, hd0 = f - 2 * DM;
+                        __half* vt = p.vt16 + ((size_t)bq * DM + hd0) * p.tp + t;
+#pragma unroll
+                        for (int i = 0; i < 16; i++) vt[(size_t)i * p.tp] = __float2half_rn(v[i]);
+                    }
+                    if (EPI == DE_F16 || (EPI == DE_QKV && !(p.vt16 && n0 >= 2 * DM))) {
                         uint32_t w[8];
 #pragma unroll
                         for (int i = 0; i < 8; i++) w[i] = pack_h2(act_f<ACT>(v[2 * i]), act_f<ACT>(v[2 * i + 1]));
@@ -323,168 +334,239 @@ __global__ void __launch_bounds__(G_THREADS) k_dit_gemm(const __grid_constant__ 
     }
 }
 
-// ------------------------------------------------------------------ attention
-constexpr int AQ = 64;     // queries per CTA (4 warps x 16)
-constexpr int AKT = 64;    // keys per tile
-constexpr int AST = 72;    // shared row stride in halves (conflict-free ldmatrix)
+// ------------------------------------------------------------------ attention on tcgen05
+// One CTA per (128 queries, head, branch). Two passes over the key tiles of 64 (keys < x_lens): pass 1
+// S = Q K^T into TMEM and the row maxima; pass 2 S again, P = exp2((S - max) * scale * log2 e) as f16 into
+// shared memory (the 128-byte-swizzled K-major layout the MMA reads), row sums, O += P V^T in TMEM. With the
+// exact row maximum known before any exponential, O needs no rescaling (the cost: Q K^T twice).
+// Warps: 0 TMA (Q once, then K or K + V^T tiles into a 3-stage ring), 1 TMEM + MMA, 2-5 softmax (thread =
+// query row = TMEM lane). S and P are double-buffered, so the MMAs of tile j + 1 overlap the softmax of
+// tile j.
+constexpr int FQ = 128, FK = 64, FKS = 3;
+struct AttnMaps {
+    CUtensorMap q;    // qkv16 [R][3072], box 64 x 128
+    CUtensorMap k;    // qkv16 [R][3072], box 64 x 64
+    CUtensorMap vt;   // vt16 [B * 16 * 64][T (pitch tp)], box 64 x 64
+};
+struct FaSmem {
+    static constexpr size_t OFF_Q = 0;                          // 16 KB
+    static constexpr size_t OFF_K = OFF_Q + FQ * HDD * 2;       // FKS x 8 KB
+    static constexpr size_t OFF_V = OFF_K + FKS * FK * HDD * 2; // FKS x 8 KB
+    static constexpr size_t OFF_P = OFF_V + FKS * HDD * FK * 2; // 2 x 16 KB
+    static constexpr size_t OFF_BAR = OFF_P + 2 * FQ * FK * 2;
+    // qfull, kvfull[FKS], kvempty[FKS], sfull[2], sfree[2], pfull[2], pfree[2], ofull
+    static constexpr int NBAR = 1 + 2 * FKS + 8 + 1;
+    static constexpr size_t SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
+};
+constexpr uint32_t FA_TMEM_COLS = 256;   // S0, S1, O (64 columns each)
 
-__device__ __forceinline__ void ldsm_x4(uint32_t a, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-                 : "r"(a));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t a, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-                 : "r"(a));
-}
-__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                         uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+__device__ __forceinline__ float ex2f(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
 
-// qkv: [R][3072] f16 (q | k | v, head h at columns 64 h of each), rows b T + t. out: [R][1024] f16.
-// grid (ceil(T / 64), 16 heads, branches); keys t >= x_lens are masked out.
-__global__ void __launch_bounds__(128) k_dit_attn(const __half* __restrict__ qkv, __half* __restrict__ out, int T,
-                                                  int x_lens) {
-    __shared__ __align__(16) __half sq[AQ * AST];
-    __shared__ __align__(16) __half sk[2][AKT * AST];
-    __shared__ __align__(16) __half sv[2][AKT * AST];
+__global__ void __launch_bounds__(G_THREADS) k_dit_attn_tc(const __grid_constant__ AttnMaps m, __half* __restrict__ out,
+                                                           int T, int x_lens, int* err) {
+    using L = FaSmem;
+    constexpr uint32_t IDS = idesc_f16(FQ, FK);    // S: 128 x 64 keys
+    constexpr uint32_t IDO = idesc_f16(FQ, HDD);   // O: 128 x 64 dims
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* sm = smem_raw + ((1024u - (su32(smem_raw) & 1023u)) & 1023u);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int q0 = blockIdx.x * AQ, h = blockIdx.y, b = blockIdx.z;
-    const size_t rbase = (size_t)b * T;
-    const __half* Q = qkv + h * HDD;
-    const __half* Kp = qkv + DM + h * HDD;
-    const __half* Vp = qkv + 2 * DM + h * HDD;
+    const int q0 = blockIdx.x * FQ, h = blockIdx.y, b = blockIdx.z;
+    const uint32_t bar0 = su32(sm + L::OFF_BAR);
+    const uint32_t qfull = bar0;
+    auto kvfull = [&](int s) { return bar0 + 8u * (1 + s); };
+    auto kvempty = [&](int s) { return bar0 + 8u * (1 + FKS + s); };
+    const uint32_t bx = bar0 + 8u * (1 + 2 * FKS);
+    auto sfull = [&](int i) { return bx + 8u * i; };
+    auto sfree = [&](int i) { return bx + 16u + 8u * i; };
+    auto pfull = [&](int i) { return bx + 32u + 8u * i; };
+    auto pfree = [&](int i) { return bx + 48u + 8u * i; };
+    const uint32_t ofull = bx + 64u;
+    uint32_t* tmem_slot = (uint32_t*)(sm + L::OFF_BAR + L::NBAR * 8);
+    volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+    const int nt = (x_lens + FK - 1) / FK;
+
+    if (tid == 0) {
+        bar_init(qfull, 1);
+        for (int s = 0; s < FKS; s++) { bar_init(kvfull(s), 1); bar_init(kvempty(s), 1); }
+        for (int i = 0; i < 2; i++) {
+            bar_init(sfull(i), 1);
+            bar_init(sfree(i), 128);
+            bar_init(pfull(i), 128);
+            bar_init(pfree(i), 1);
+        }
+        bar_init(ofull, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_slot)),
+                     "r"(FA_TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
     griddep_wait();
     griddep_launch();
-    // Q tile and the first K / V tile: 64 rows x 128 bytes = 512 chunks of 16 bytes, 4 per thread each
-    auto load_rows = [&](__half* dst, const __half* src, int r0, int rlim) {
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int ch = tid + 128 * i, r = ch >> 3, c = ch & 7;
-            const bool in = r0 + r < rlim;
-            const __half* g = src + (rbase + (size_t)(in ? r0 + r : 0)) * (3 * DM) + c * 8;
-            cp_async16((uint32_t)__cvta_generic_to_shared(dst + r * AST + c * 8), g, in);
-        }
-    };
-    const int nkt = (x_lens + AKT - 1) / AKT;
-    load_rows(sq, Q, q0, T);
-    load_rows(sk[0], Kp, 0, x_lens);
-    load_rows(sv[0], Vp, 0, x_lens);
-    asm volatile("cp.async.commit_group;" ::: "memory");
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;   // S0 at columns 0..63, S1 at 64..127, O at 128..191
 
-    const float sl2 = ATTN_SCALE * 1.4426950408889634f;   // scale * log2(e)
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;   // rows g and g + 8 of the warp's 16
-    float o[8][4];
-#pragma unroll
-    for (int j = 0; j < 8; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
-    uint32_t qa[4][4];   // Q fragments of the 4 k-steps (64 dims)
-    const int g = lane >> 2, tq = lane & 3;
-
-    for (int kt = 0; kt < nkt; kt++) {
-        const int buf = kt & 1;
-        if (kt + 1 < nkt) {
-            load_rows(sk[buf ^ 1], Kp, (kt + 1) * AKT, x_lens);
-            load_rows(sv[buf ^ 1], Vp, (kt + 1) * AKT, x_lens);
+    if (warp == 0) {
+        if (lane == 0) {   // TMA producer
+            bar_expect_tx(qfull, FQ * HDD * 2);
+            tma_load_2d(su32(sm + L::OFF_Q), &m.q, h * HDD, b * T + q0, qfull);
+            int g = 0;
+            bool ok = true;
+            for (int pass = 0; pass < 2 && ok; pass++)
+                for (int j = 0; j < nt; j++, g++) {
+                    const int s = g % FKS;
+                    if (!bar_wait_short(kvempty(s), ((uint32_t)(g / FKS) & 1u) ^ 1u, abort_flag)) { ok = false; break; }
+                    bar_expect_tx(kvfull(s), (pass ? 2u : 1u) * FK * HDD * 2);
+                    tma_load_2d(su32(sm + L::OFF_K + (size_t)s * FK * HDD * 2), &m.k, DM + h * HDD, b * T + j * FK, kvfull(s));
+                    if (pass)
+                        tma_load_2d(su32(sm + L::OFF_V + (size_t)s * HDD * FK * 2), &m.vt, j * FK, (b * NHD + h) * HDD,
+                                    kvfull(s));
+                }
+            if (!ok) {
+                if (err) atomicExch(err, 1);
+                *abort_flag = 1;
+            }
+            for (int k = g - 1; k >= 0 && k >= g - FKS; k--)
+                for (uint32_t it = 0; it < TC_POLL_LIMIT; it++)
+                    if (bar_try(kvfull(k % FKS), (uint32_t)(k / FKS) & 1u)) break;
+            for (uint32_t it = 0; it < TC_POLL_LIMIT; it++)
+                if (bar_try(qfull, 0)) break;
         }
-        asm volatile("cp.async.commit_group;" ::: "memory");
-        asm volatile("cp.async.wait_group 1;" ::: "memory");
-        __syncthreads();
-        if (kt == 0) {
+    } else if (warp == 1) {
+        if (lane == 0) {   // MMA issuer
+            bool ok = bar_wait_short(qfull, 0, abort_flag);
+            const uint32_t qa = su32(sm + L::OFF_Q);
+            int g = 0, u = 0, v = 0;   // ring stages, S tiles, P tiles consumed
+            int prev_s = -1;            // ring stage of the tile whose P V^T is still to be issued
+            // P V^T of the previous tile once its P is written: O += P V^T
+            auto pv = [&](int j) -> bool {
+                const int pb = v & 1;
+                if (!bar_wait_short(pfull(pb), ((uint32_t)v >> 1) & 1u, abort_flag)) return false;
+                tc_fence_after();
+                const uint32_t pa = su32(sm + L::OFF_P + (size_t)pb * FQ * FK * 2);
+                const uint32_t va = su32(sm + L::OFF_V + (size_t)prev_s * HDD * FK * 2);
 #pragma unroll
-            for (int ks = 0; ks < 4; ks++) {
-                const int r = 16 * warp + (lane & 15), c = 16 * ks + 8 * (lane >> 4);
-                ldsm_x4((uint32_t)__cvta_generic_to_shared(sq + r * AST + c), qa[ks][0], qa[ks][1], qa[ks][2],
-                        qa[ks][3]);
+                for (int kk = 0; kk < FK / 16; kk++)
+                    umma_f16(tmem + 2 * FK, umma_desc(pa + 32u * kk), umma_desc(va + 32u * kk), IDO, (uint32_t)(j | kk));
+                umma_commit(kvempty(prev_s));
+                umma_commit(pfree(pb));
+                v++;
+                return true;
+            };
+            for (int pass = 0; pass < 2 && ok; pass++) {
+                for (int j = 0; j < nt; j++, g++, u++) {
+                    const int s = g % FKS, sb = u & 1;
+                    if (!bar_wait_short(kvfull(s), (uint32_t)(g / FKS) & 1u, abort_flag) ||
+                        !bar_wait_short(sfree(sb), (((uint32_t)u >> 1) & 1u) ^ 1u, abort_flag)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t ka = su32(sm + L::OFF_K + (size_t)s * FK * HDD * 2);
+#pragma unroll
+                    for (int kk = 0; kk < HDD / 16; kk++)
+                        umma_f16(tmem + (uint32_t)(sb * FK), umma_desc(qa + 32u * kk), umma_desc(ka + 32u * kk), IDS,
+                                 (uint32_t)kk);
+                    umma_commit(sfull(sb));
+                    if (pass == 0) {
+                        umma_commit(kvempty(s));
+                        continue;
+                    }
+                    if (j > 0 && !pv(j - 1)) { ok = false; break; }
+                    prev_s = s;
+                }
+                if (ok && pass == 1 && !pv(nt - 1)) ok = false;
+            }
+            if (!ok) {
+                if (err) atomicExch(err, 1);
+                *abort_flag = 1;
+            }
+            umma_commit(ofull);   // every MMA issued above has completed when ofull completes
+            for (uint32_t it = 0; it < TC_POLL_LIMIT; it++)
+                if (bar_try(ofull, 0)) break;
+        }
+    } else {
+        // softmax: thread = query row fr (TMEM lane), keys of tile j in its S buffer's 64 columns
+        const int q = warp & 3, fr = 32 * q + lane;
+        const uint32_t tl = tmem + ((uint32_t)(32 * q) << 16);
+        const float c = ATTN_SCALE * 1.4426950408889634f;
+        float mx = -INFINITY, l = 0.0f;
+        int u = 0, v = 0;
+        bool ok = true;
+        for (int pass = 0; pass < 2 && ok; pass++) {
+            const float mc = mx * c;
+            for (int j = 0; j < nt; j++, u++) {
+                const int sb = u & 1;
+                if (!bar_wait_short_warp(sfull(sb), ((uint32_t)u >> 1) & 1u, abort_flag)) { ok = false; break; }
+                tc_fence_after();
+                float sv[4][16];
+#pragma unroll
+                for (int k = 0; k < 4; k++) tmem_ld16(tl + (uint32_t)(sb * FK + 16 * k), sv[k]);
+                tmem_wait_ld();
+#pragma unroll
+                for (int k = 0; k < 4; k++) tmem_bind(sv[k]);
+                tc_fence_before();
+                bar_arrive(sfree(sb));
+                const int kv = x_lens - j * FK;   // valid keys in this tile (>= 1)
+                if (pass == 0) {
+#pragma unroll
+                    for (int i = 0; i < 64; i++)
+                        if (i < kv) mx = fmaxf(mx, sv[i >> 4][i & 15]);
+                    continue;
+                }
+                uint32_t pw[32];
+#pragma unroll
+                for (int i = 0; i < 64; i += 2) {
+                    const float p0 = i < kv ? ex2f(__fmaf_rn(sv[i >> 4][i & 15], c, -mc)) : 0.0f;
+                    const float p1 = i + 1 < kv ? ex2f(__fmaf_rn(sv[i >> 4][(i + 1) & 15], c, -mc)) : 0.0f;
+                    l += p0 + p1;
+                    pw[i / 2] = pack_h2(p0, p1);
+                }
+                const int pb = v & 1;
+                if (!bar_wait_short_warp(pfree(pb), (((uint32_t)v >> 1) & 1u) ^ 1u, abort_flag)) { ok = false; break; }
+                uint8_t* prow = sm + L::OFF_P + (size_t)pb * FQ * FK * 2 + (size_t)fr * 128;
+#pragma unroll
+                for (int ch = 0; ch < 8; ch++)   // 128-byte swizzle: chunk ch of row r at ch ^ (r % 8)
+                    *(uint4*)(prow + 16 * (ch ^ (fr & 7))) = make_uint4(pw[4 * ch], pw[4 * ch + 1], pw[4 * ch + 2], pw[4 * ch + 3]);
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                bar_arrive(pfull(pb));
+                v++;
             }
         }
-        // S = Q K^T: 16 queries x 64 keys per warp, 8 key blocks of 8
-        float s[8][4];
+        ok = bar_wait_short_warp(ofull, 0, abort_flag) && ok && !*abort_flag;
+        tc_fence_after();
+        if (ok) {
+            float o4[4][16];
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.0f;
+            for (int k = 0; k < 4; k++) tmem_ld16(tl + (uint32_t)(2 * FK + 16 * k), o4[k]);
+            tmem_wait_ld();
 #pragma unroll
-            for (int kp = 0; kp < 2; kp++) {   // two k-steps per x4 load
-                uint32_t b0, b1, b2, b3;
-                const int key = 8 * j + (lane & 7), dim = 32 * kp + 8 * (lane >> 3);
-                ldsm_x4((uint32_t)__cvta_generic_to_shared(sk[buf] + key * AST + dim), b0, b1, b2, b3);
-                mma16816(s[j], qa[2 * kp][0], qa[2 * kp][1], qa[2 * kp][2], qa[2 * kp][3], b0, b1);
-                mma16816(s[j], qa[2 * kp + 1][0], qa[2 * kp + 1][1], qa[2 * kp + 1][2], qa[2 * kp + 1][3], b2, b3);
+            for (int k = 0; k < 4; k++) tmem_bind(o4[k]);
+            if (q0 + fr < T) {
+                const float il = 1.0f / l;
+                uint4* dst = (uint4*)(out + ((size_t)b * T + q0 + fr) * DM + h * HDD);
+#pragma unroll
+                for (int ch = 0; ch < 8; ch++) {
+                    const float* o = o4[ch >> 1] + 8 * (ch & 1);
+                    dst[ch] = make_uint4(pack_h2(o[0] * il, o[1] * il), pack_h2(o[2] * il, o[3] * il),
+                                         pack_h2(o[4] * il, o[5] * il), pack_h2(o[6] * il, o[7] * il));
+                }
             }
+        } else if (err && lane == 0) {
+            atomicExch(err, 1);
         }
-        // mask, row max, online softmax (base 2)
-        float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-            const int key = kt * AKT + 8 * j + 2 * tq;
-#pragma unroll
-            for (int e = 0; e < 2; e++) {
-                const bool in = key + e < x_lens;
-                s[j][e] = in ? s[j][e] * sl2 : -INFINITY;
-                s[j][2 + e] = in ? s[j][2 + e] * sl2 : -INFINITY;
-                mx0 = fmaxf(mx0, s[j][e]);
-                mx1 = fmaxf(mx1, s[j][2 + e]);
-            }
-        }
-#pragma unroll
-        for (int off = 1; off <= 2; off <<= 1) {
-            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
-            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
-        }
-        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);   // finite: every tile has a valid key
-        const float c0 = exp2f(m0 - mn0), c1 = exp2f(m1 - mn1);
-        m0 = mn0;
-        m1 = mn1;
-        float rs0 = 0.0f, rs1 = 0.0f;
-        uint32_t pa[4][4];   // P as the A fragments of the 4 k-steps (64 keys)
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-            const float p0 = exp2f(s[j][0] - mn0), p1 = exp2f(s[j][1] - mn0);
-            const float p2 = exp2f(s[j][2] - mn1), p3 = exp2f(s[j][3] - mn1);
-            rs0 += p0 + p1;
-            rs1 += p2 + p3;
-            pa[j >> 1][(j & 1) * 2] = pack_h2(p0, p1);
-            pa[j >> 1][(j & 1) * 2 + 1] = pack_h2(p2, p3);
-        }
-        l0 = l0 * c0 + rs0;
-        l1 = l1 * c1 + rs1;
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-            o[j][0] *= c0; o[j][1] *= c0;
-            o[j][2] *= c1; o[j][3] *= c1;
-        }
-        // O += P V: V [key][dim] -> B fragments by transposed loads
-#pragma unroll
-        for (int ks = 0; ks < 4; ks++) {
-#pragma unroll
-            for (int jp = 0; jp < 4; jp++) {   // two dim blocks per x4 load
-                uint32_t b0, b1, b2, b3;
-                const int mtx = lane >> 3;
-                const int key = 16 * ks + (mtx & 1) * 8 + (lane & 7), dim = 16 * jp + 8 * (mtx >> 1);
-                ldsm_x4_t((uint32_t)__cvta_generic_to_shared(sv[buf] + key * AST + dim), b0, b1, b2, b3);
-                mma16816(o[2 * jp], pa[ks][0], pa[ks][1], pa[ks][2], pa[ks][3], b0, b1);
-                mma16816(o[2 * jp + 1], pa[ks][0], pa[ks][1], pa[ks][2], pa[ks][3], b2, b3);
-            }
-        }
-        __syncthreads();   // this buffer is refilled two tiles on
     }
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-#pragma unroll
-    for (int off = 1; off <= 2; off <<= 1) {
-        l0 += __shfl_xor_sync(0xffffffffu, l0, off);
-        l1 += __shfl_xor_sync(0xffffffffu, l1, off);
-    }
-    const float i0 = 1.0f / l0, i1 = 1.0f / l1;
-    const int qa0 = q0 + 16 * warp + g, qa1 = qa0 + 8;
-#pragma unroll
-    for (int j = 0; j < 8; j++) {
-        const int dim = h * HDD + 8 * j + 2 * tq;
-        if (qa0 < T) *(uint32_t*)(out + (rbase + qa0) * DM + dim) = pack_h2(o[j][0] * i0, o[j][1] * i0);
-        if (qa1 < T) *(uint32_t*)(out + (rbase + qa1) * DM + dim) = pack_h2(o[j][2] * i1, o[j][3] * i1);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(FA_TMEM_COLS) : "memory");
     }
 }
 
@@ -674,6 +756,7 @@ cudaError_t init_device() {
     if ((e = set_gemm_smem<DE_F16, ACT_GELU_TANH, 128, false, 6>())) return e;
     if ((e = set_gemm_smem<DE_F16, ACT_MISH, 64, true, 3>())) return e;
     if ((e = set_gemm_smem<DE_RESID, ACT_MISH, 64, true, 3>())) return e;
+    if ((e = cudaFuncSetAttribute(k_dit_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)FaSmem::SMEM))) return e;
     return cudaSuccess;
 }
 
@@ -697,6 +780,30 @@ bool gemm(int epi, const __half* A, const __half* W, const DitGemmArgs& a, cudaS
             else launch_gemm<DE_F16, ACT_GELU_TANH, 128, false, 6>(grid, ma, mb, a, s);
             break;
     }
+    return true;
+}
+
+// Attention of B branches of T frames over the keys < x_lens: q, k from qkv16 [B T][3072], v from vt16
+// [B][16][64][tp]; output [B T][1024] f16.
+bool attention_tc(const __half* qkv16, const __half* vt16, int tp, int T, int B, int x_lens, __half* out, int* err,
+                  cudaStream_t s) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    AttnMaps m;
+    if (!map_2d(&m.q, qkv16, (uint64_t)B * T, 3 * DM, FQ) || !map_2d(&m.k, qkv16, (uint64_t)B * T, 3 * DM, FK))
+        return false;
+    {
+        const cuuint64_t dims[2] = {(cuuint64_t)T, (cuuint64_t)B * NHD * HDD};
+        const cuuint64_t strides[1] = {(cuuint64_t)tp * 2};
+        const cuuint32_t box[2] = {(cuuint32_t)FK, (cuuint32_t)HDD};
+        const cuuint32_t estr[2] = {1u, 1u};
+        if (enc(&m.vt, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void*)vt16, dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return false;
+    }
+    launch_pdl(k_dit_attn_tc, dim3((unsigned)((T + FQ - 1) / FQ), NHD, (unsigned)B), dim3(G_THREADS), FaSmem::SMEM, s, m,
+               out, T, x_lens, err);
     return true;
 }
 
@@ -744,6 +851,8 @@ struct gsvcu_dit {
     __half *a16 = nullptr;        // [R][1024] GEMM / conv operand
     __half *c16 = nullptr;        // [R][1024] conv 1 output
     __half *qkv16 = nullptr;      // [R][3072]
+    __half *vt16 = nullptr;       // [2][16][64][tp]: v transposed for the attention's P V^T
+    int tp = 0;                   // T rounded up to 8 (16-byte rows)
     __half *h16 = nullptr;        // [R][2048]
     __half *mel16 = nullptr;      // [R][128]
     float *vel = nullptr;         // [R][128]
@@ -819,6 +928,7 @@ int gsvcu_dit::reserve(int T_, int rows) {
     const A list[] = {{(void**)&cond, 2 * TT * DM * 4}, {(void**)&rcos, TT * 32 * 4}, {(void**)&rsin, TT * 32 * 4},
                       {(void**)&xmel, MEL * TT * 4}, {(void**)&x, R * DM * 4}, {(void**)&a16, R * DM * 2},
                       {(void**)&c16, R * DM * 2}, {(void**)&qkv16, R * 3 * DM * 2}, {(void**)&h16, R * FFD * 2},
+                      {(void**)&vt16, 2 * (size_t)DM * ((TT + 7) & ~(size_t)7) * 2},
                       {(void**)&mel16, R * MELP * 2}, {(void**)&vel, R * MELP * 4}, {(void**)&temb, DM * 4},
                       {(void**)&th, DM * 4}, {(void**)&ada, nada * 4}, {(void**)&vout, MEL * TT * 4}};
     for (const A& a : list) {
@@ -832,6 +942,7 @@ int gsvcu_dit::reserve(int T_, int rows) {
     cudaMemsetAsync(mel16, 0, R * MELP * 2, stream);
     cap_rows = rows;
     T = T_;
+    tp = (T_ + 7) & ~7;
     return GSVCU_OK;
 }
 
@@ -878,9 +989,9 @@ int gsvcu_dit::forward(int B, int negative, const float* tsin_dev, int n_blocks,
         launch_pdl(k_dit_lnmod, rows8, dim3(256), 0, s, (const float*)x, R, m, m + DM, a16);
         DitGemmArgs g = a;
         g.N = 3 * DM; g.K = DM; g.bias = w.bqkv; g.out16 = qkv16; g.ld = 3 * DM; g.rcos = rcos; g.rsin = rsin;
+        g.vt16 = vt16; g.tp = tp;
         if (!gemm(DE_QKV, a16, w.wqkv, g, s)) return fail(GSVCU_ERR_CUDA, "tensor map encoding failed");
-        launch_pdl(k_dit_attn, dim3((unsigned)((T + AQ - 1) / AQ), NHD, (unsigned)B), dim3(128), 0, s,
-                   (const __half*)qkv16, a16, T, x_lens);
+        if (!attention_tc(qkv16, vt16, tp, T, B, x_lens, a16, errw, s)) return fail(GSVCU_ERR_CUDA, "tensor map encoding failed");
         g = a;
         g.N = DM; g.K = DM; g.bias = w.bo; g.out32 = x; g.ld = DM; g.gate = m + 2 * DM; g.use_mask = 1;
         if (!gemm(DE_RESID, a16, w.wo, g, s)) return fail(GSVCU_ERR_CUDA, "tensor map encoding failed");

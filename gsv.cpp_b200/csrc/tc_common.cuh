@@ -73,6 +73,36 @@ __device__ __forceinline__ bool bar_wait_warp(uint32_t b, uint32_t parity, volat
     return __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
 }
 
+// Short waits (a phase expected within microseconds): mbarrier.try_wait without a suspend-time hint, which
+// returns after a short system-dependent window, so a completed phase is seen at once; bounded by
+// TC_SPIN_LIMIT polls.
+constexpr uint32_t TC_SPIN_LIMIT = 1u << 22;
+__device__ __forceinline__ bool bar_try_short(uint32_t b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(b), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool bar_wait_short(uint32_t b, uint32_t parity, volatile int* abort_flag) {
+    for (uint32_t it = 0; it < TC_SPIN_LIMIT; it++) {
+        if (bar_try_short(b, parity)) return true;
+        if (*abort_flag) return false;
+    }
+    return false;
+}
+// The same for a whole warp (warp-uniform result from lane 0's polls).
+__device__ __forceinline__ bool bar_wait_short_warp(uint32_t b, uint32_t parity, volatile int* abort_flag) {
+    bool ok = false;
+    for (uint32_t it = 0; it < TC_SPIN_LIMIT; it++) {
+        ok = __shfl_sync(0xffffffffu, (int)bar_try_short(b, parity), 0) != 0;
+        if (ok || *abort_flag) break;
+    }
+    return ok;
+}
+
 // 2D TMA tile store from shared memory (bulk-group completion); c0 = innermost coordinate (elements).
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int c0, int c1) {
     asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"((uint64_t)map),
