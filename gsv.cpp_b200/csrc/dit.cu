@@ -296,13 +296,16 @@ __global__ void __launch_bounds__(G_THREADS) k_dit_gemm(const __grid_constant__ 
 #pragma unroll
                         for (int i = 0; i < 16; i++) vt[(size_t)i * p.tp] = __float2half_rn(v[i]);
                     }
-                    if (EPI == DE_F16 || (EPI == DE_QKV && !(p.vt16 && n0 >= 2 * DM))) {
-                        uint32_t w[8];
+                    if (EPI == DE_F16 || EPI == DE_QKV) {
+                        // (v columns go only to vt16 when it is given)
+                        if (EPI == DE_F16 || !(p.vt16 && n0 >= 2 * DM)) {
+                            uint32_t w[8];
 #pragma unroll
-                        for (int i = 0; i < 8; i++) w[i] = pack_h2(act_f<ACT>(v[2 * i]), act_f<ACT>(v[2 * i + 1]));
-                        uint4* dst = (uint4*)(p.out16 + (size_t)row * p.ld + f);
-                        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-                        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+                            for (int i = 0; i < 8; i++) w[i] = pack_h2(act_f<ACT>(v[2 * i]), act_f<ACT>(v[2 * i + 1]));
+                            uint4* dst = (uint4*)(p.out16 + (size_t)row * p.ld + f);
+                            dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                            dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+                        }
                     } else if (EPI == DE_RESID) {
                         float4* dst = (float4*)(p.out32 + (size_t)row * p.ld + f);
 #pragma unroll
@@ -1267,7 +1270,7 @@ int gsvcu_dit_velocity(gsvcu_dit* c, const float* x_mel, float t, int32_t negati
     launch_pdl(k_dit_vel_out, dim3((unsigned)std::min(1024, (MEL * c->T + 255) / 256)), dim3(256), 0, c->stream,
                (const float*)c->vel, c->T, c->vout);
     if (cudaMemcpyAsync(vel, c->vout, (size_t)MEL * c->T * 4, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess)
-        return c->fail(GSVCU_ERR_CUDA, "output read failed");
+        return c->fail(GSVCU_ERR_CUDA, std::string("output read failed: ") + cudaGetErrorString(cudaGetLastError()));
     return check_err(c);
 }
 
@@ -1296,7 +1299,7 @@ int gsvcu_dit_sample(gsvcu_dit* c, const float* x0, int32_t P, int32_t steps, fl
     for (int ch = 0; ch < MEL; ch++)
         if (cudaMemcpyAsync(mel_out + (size_t)ch * (T - P), c->xmel + (size_t)ch * T + P, (size_t)(T - P) * 4,
                             cudaMemcpyDeviceToHost, c->stream) != cudaSuccess)
-            return c->fail(GSVCU_ERR_CUDA, "output read failed");
+            return c->fail(GSVCU_ERR_CUDA, std::string("output read failed: ") + cudaGetErrorString(cudaGetLastError()));
     return check_err(c);
 }
 
@@ -1313,7 +1316,7 @@ int gsvcu_dit_op_hidden(gsvcu_dit* c, const float* x_mel, float t, int32_t n_blo
         return c->fail(GSVCU_ERR_CUDA, "input upload failed");
     if ((rc = c->forward(2, 0, c->tsin, n_blocks, false))) return rc;
     if (cudaMemcpyAsync(hidden, c->x, (size_t)2 * c->T * DM * 4, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess)
-        return c->fail(GSVCU_ERR_CUDA, "output read failed");
+        return c->fail(GSVCU_ERR_CUDA, std::string("output read failed: ") + cudaGetErrorString(cudaGetLastError()));
     return check_err(c);
 }
 
