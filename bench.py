@@ -356,26 +356,28 @@ def dit_bench(args):
     except (OSError, KeyError, ValueError):
         peak = 1590.0   # the pool's earlier measurement, when the file is absent
     tflops = (flop_gemm + flop_attn) / (ms * 1e-3) / 1e12
-    # CPU restatement: one block of one branch (the step runs 44 plus trunk and head)
-    W = DO.load(path)
-    W1 = {k: v for k, v in W.items() if not k.startswith("dit.transformer_blocks.") or k.startswith("dit.transformer_blocks.0.")}
-    W1["depth"] = 1
-    t0 = time.perf_counter()
-    DO.branch(W1, x0, 0.5, cond, T, n_blocks=1, head=False)
-    t1 = time.perf_counter()
-    DO.branch(W1, x0, 0.5, cond, T, n_blocks=0, head=False)
-    t2 = time.perf_counter()
-    blk = (t1 - t0) - (t2 - t1)
-    cpu_step_s = 44 * max(blk, 1e-3) + 2 * (t2 - t1)
+    cpu = None
+    if not args.no_cpu_baseline:   # CPU restatement: one block of one branch (a step runs 44, trunk and head)
+        W = DO.load(path)
+        W1 = {k: v for k, v in W.items()
+              if not k.startswith("dit.transformer_blocks.") or k.startswith("dit.transformer_blocks.0.")}
+        W1["depth"] = 1
+        t0 = time.perf_counter()
+        DO.branch(W1, x0, 0.5, cond, T, n_blocks=1, head=False)
+        t1 = time.perf_counter()
+        DO.branch(W1, x0, 0.5, cond, T, n_blocks=0, head=False)
+        t2 = time.perf_counter()
+        blk = (t1 - t0) - (t2 - t1)
+        cpu = {"ms_per_guided_step": 1e3 * (44 * max(blk, 1e-3) + 2 * (t2 - t1)), "cores": os.cpu_count() or 1,
+               "kind": "port", "sample": "oracle (numpy) DiT block 0 of one branch timed, x 44 blocks + 2 x trunk "
+               "per guided step"}
     print(json.dumps({"workload": "DiT / CFM guided sampling (gsv_dit::sample)", "model": "22 blocks, 1024 / 16 x 64 / "
                       "FFN 2048, F16 matrices", "T": T, "prompt_frames": P, "steps_per_call": steps, "cfg": cfg,
                       "ms_per_guided_step": ms, "frames_per_s": (T - P) / (ms * steps * 1e-3),
                       "wall_ms_per_call": float(np.median(wall_ms)),
                       "gflop_per_step": {"gemm": flop_gemm / 1e9, "attention": flop_attn / 1e9},
                       "tflops": tflops, "peak_bf16_tflops": peak, "frac_of_peak": tflops / peak if peak else None,
-                      "cpu_baseline": {"ms_per_guided_step": 1e3 * cpu_step_s, "cores": os.cpu_count() or 1,
-                                       "kind": "port", "sample": "oracle (numpy) DiT block 0 of one branch timed, "
-                                       "x 44 blocks + 2 x trunk per guided step"}}))
+                      "cpu_baseline": cpu}))
     d.close()
 
 
