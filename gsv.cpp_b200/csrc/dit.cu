@@ -705,6 +705,130 @@ __global__ void __launch_bounds__(256) k_dit_gemv(const __half* __restrict__ W, 
     }
 }
 
+// ------------------------------------------------------------------ static cache (prepare)
+constexpr int TXD = 512;          // text dim
+constexpr int TXI = 1024;         // ConvNeXtV2 intermediate
+constexpr int CTXK = 640;         // [prompt_x (100) | text (512)] padded to a multiple of 64
+constexpr int MAXPOS = 4096;      // freqs_cis rows
+
+// tx[t][c] = mu[c][t] + freqs_cis[t][c] (mu in torch layout [512][T]).
+__global__ void __launch_bounds__(256) k_dit_text_in(const float* __restrict__ mu, const float* __restrict__ cis, int T,
+                                                     float* __restrict__ tx) {
+    griddep_wait();
+    griddep_launch();
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < TXD * T; i += gridDim.x * blockDim.x) {
+        const int t = i / TXD, c = i - t * TXD;
+        tx[i] = mu[(size_t)c * T + t] + cis[(size_t)t * TXD + c];
+    }
+}
+
+// Depthwise conv (k = 7, zero padding 3, taps summed in order) + bias, then LayerNorm (eps 1e-6) with
+// weight and bias -> f16 [T][512]. Warp per frame, lane = channels lane + 32 j.
+__global__ void __launch_bounds__(256) k_dit_dwconv_ln(const float* __restrict__ x, int T, const float* __restrict__ w7,
+                                                       const float* __restrict__ b, const float* __restrict__ nw,
+                                                       const float* __restrict__ nb, __half* __restrict__ out) {
+    griddep_wait();
+    griddep_launch();
+    const int t = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (t >= T) return;
+    float y[16];
+    float s = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+        const int c = lane + 32 * j;
+        float acc = 0.0f;
+#pragma unroll
+        for (int kw = 0; kw < 7; kw++) {
+            const int tt = t + kw - 3;
+            const float xv = (tt >= 0 && tt < T) ? x[(size_t)tt * TXD + c] : 0.0f;
+            acc = kw ? acc + xv * w7[kw * TXD + c] : xv * w7[c];
+        }
+        y[j] = acc + b[c];
+        s += y[j];
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    const float mean = s * (1.0f / TXD);
+    float q = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 16; j++) q += (y[j] - mean) * (y[j] - mean);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) q += __shfl_xor_sync(0xffffffffu, q, off);
+    const float rstd = 1.0f / sqrtf(q * (1.0f / TXD) + LN_EPS);
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+        const int c = lane + 32 * j;
+        out[(size_t)t * TXD + c] = __float2half_rn((y[j] - mean) * rstd * nw[c] + nb[c]);
+    }
+}
+
+// GELU (erf) in place on h [T][1024] and each channel's L2 norm over the frames, gx[c] = sqrt(sum_t h^2).
+// CTA = 32 channels x 8 frame groups; partial sums added in a fixed order.
+__global__ void __launch_bounds__(256) k_dit_gelu_colnorm(float* __restrict__ h, int T, float* __restrict__ gx) {
+    __shared__ float part[8][32];
+    griddep_wait();
+    griddep_launch();
+    const int c = blockIdx.x * 32 + (threadIdx.x & 31), g = threadIdx.x >> 5;
+    float s = 0.0f;
+    for (int t = g; t < T; t += 8) {
+        float* p = h + (size_t)t * TXI + c;
+        const float v = *p;
+        const float y = 0.5f * v * (1.0f + erff(v * 0.7071067811865476f));
+        *p = y;
+        s += y * y;
+    }
+    part[g][threadIdx.x & 31] = s;
+    __syncthreads();
+    if (g == 0) {
+        float a = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; i++) a += part[i][threadIdx.x];
+        gx[c] = sqrtf(a);
+    }
+}
+
+// GRN: out = f16(gamma * (h * Nx) + beta + h), Nx = gx / (mean(gx) + 1e-6). Every CTA sums the 1024 norms
+// in the same order.
+__global__ void __launch_bounds__(256) k_dit_grn(const float* __restrict__ h, int T, const float* __restrict__ gx,
+                                                 const float* __restrict__ gamma, const float* __restrict__ beta,
+                                                 __half* __restrict__ out) {
+    __shared__ float snx[TXI];
+    __shared__ float wsum[8];
+    griddep_wait();
+    griddep_launch();
+    float a = 0.0f;
+    for (int c = threadIdx.x; c < TXI; c += 256) a += gx[c];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
+    if ((threadIdx.x & 31) == 0) wsum[threadIdx.x >> 5] = a;
+    __syncthreads();
+    float tot = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) tot += wsum[i];
+    const float inv = 1.0f / (tot * (1.0f / TXI) + 1e-6f);
+    for (int c = threadIdx.x; c < TXI; c += 256) snx[c] = gx[c] * inv;
+    __syncthreads();
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < TXI * T; i += gridDim.x * blockDim.x) {
+        const int c = i & (TXI - 1);
+        const float v = h[i];
+        out[i] = __float2half_rn(gamma[c] * (v * snx[c]) + beta[c] + v);
+    }
+}
+
+// Rows [0, T): [prompt_x^T | text]; rows [T, 2T): [0 | text]; f16 [2T][640], columns 612.. zero.
+__global__ void __launch_bounds__(256) k_dit_pack_ctx(const float* __restrict__ px, const float* __restrict__ tx, int T,
+                                                      __half* __restrict__ out) {
+    griddep_wait();
+    griddep_launch();
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < 2 * T * CTXK; i += gridDim.x * blockDim.x) {
+        const int r = i / CTXK, k = i - r * CTXK, t = r % T;
+        float v = 0.0f;
+        if (k < MEL) v = r < T ? px[(size_t)k * T + t] : 0.0f;
+        else if (k < MEL + TXD) v = tx[(size_t)t * TXD + (k - MEL)];
+        out[i] = __float2half_rn(v);
+    }
+}
+
 // ------------------------------------------------------------------ host side
 bool map_2d(CUtensorMap* m, const __half* base, uint64_t rows, uint64_t K, uint32_t box_rows) {
     EncodeTiledFn enc = encode_fn();
@@ -844,7 +968,17 @@ struct gsvcu_dit {
            *w_out = nullptr;
     float *b_c0 = nullptr, *b_c2 = nullptr, *b_t0 = nullptr, *b_t2 = nullptr, *b_ada = nullptr, *b_out = nullptr;
     std::vector<Block> L;
-    // per-shape state (set_condition)
+    // static cache (prepare): text path and the context projection, when the file has them
+    bool has_text = false;
+    float* cis = nullptr;                       // [4096][512]
+    struct TextBlock {
+        float *w7 = nullptr, *b = nullptr, *nw = nullptr, *nb = nullptr, *b1 = nullptr, *gamma = nullptr,
+              *beta = nullptr, *b2 = nullptr;
+        __half *w1 = nullptr, *w2 = nullptr;    // [1024][512], [512][1024]
+    } TB[4];
+    __half* w_ctx = nullptr;                    // [1024][640] (612 used)
+    float* b_ctx = nullptr;
+    // per-shape state (set_condition / prepare)
     int T = 0, x_lens = 0, cap_rows = 0;
     std::vector<void*> ballocs;
     float *cond = nullptr;        // [2][T][1024]: condition, negative condition
@@ -863,6 +997,12 @@ struct gsvcu_dit {
     int cap_steps = 0;
     float *temb = nullptr, *th = nullptr, *ada = nullptr;   // [1024], [1024], [depth * 6144 + 2048]
     float *vout = nullptr;        // [100][T]
+    float *mu_d = nullptr, *px_d = nullptr;   // prepare inputs [512][T], [100][T]
+    float *txf = nullptr;         // [T][512] text path (f32)
+    __half *tx16 = nullptr;       // [T][512] ConvNeXt operand
+    float *hb = nullptr;          // [T][1024] ConvNeXt hidden (f32)
+    float *gx = nullptr;          // [1024] GRN norms
+    __half *ctx16 = nullptr;      // [2T][640] context projection operand
     int* errw = nullptr;
 
     int fail(int code, const std::string& m) {
@@ -893,6 +1033,7 @@ struct gsvcu_dit {
         return GSVCU_OK;
     }
     int reserve(int T_, int rows);
+    int prepare_dev(const float* prompt_x, const float* mu);
     int forward(int B, int negative, const float* tsin_dev, int n_blocks, bool head);
 };
 
@@ -933,7 +1074,10 @@ int gsvcu_dit::reserve(int T_, int rows) {
                       {(void**)&c16, R * DM * 2}, {(void**)&qkv16, R * 3 * DM * 2}, {(void**)&h16, R * FFD * 2},
                       {(void**)&vt16, 2 * (size_t)DM * ((TT + 7) & ~(size_t)7) * 2},
                       {(void**)&mel16, R * MELP * 2}, {(void**)&vel, R * MELP * 4}, {(void**)&temb, DM * 4},
-                      {(void**)&th, DM * 4}, {(void**)&ada, nada * 4}, {(void**)&vout, MEL * TT * 4}};
+                      {(void**)&th, DM * 4}, {(void**)&ada, nada * 4}, {(void**)&vout, MEL * TT * 4},
+                      {(void**)&mu_d, TXD * TT * 4}, {(void**)&px_d, MEL * TT * 4}, {(void**)&txf, TT * TXD * 4},
+                      {(void**)&tx16, TT * TXD * 2}, {(void**)&hb, TT * TXI * 4}, {(void**)&gx, TXI * 4},
+                      {(void**)&ctx16, 2 * TT * CTXK * 2}};
     for (const A& a : list) {
         if (cudaMalloc(a.p, a.bytes) != cudaSuccess) {
             cudaGetLastError();
@@ -946,6 +1090,41 @@ int gsvcu_dit::reserve(int T_, int rows) {
     cap_rows = rows;
     T = T_;
     tp = (T_ + 7) & ~7;
+    return GSVCU_OK;
+}
+
+// The static cache of gsv_dit::prepare (src/gsv_dit.cpp:486-531): text path (mu^T + freqs_cis, 4 ConvNeXtV2
+// blocks), then condition / negative condition = proj_ctx([prompt_x | text] / [0 | text]) + bias into `cond`.
+// prompt_x [100][T] and mu [512][T] are host arrays; T and the RoPE tables are set by the caller.
+int gsvcu_dit::prepare_dev(const float* prompt_x, const float* mu) {
+    cudaStream_t s = stream;
+    if (cudaMemcpyAsync(mu_d, mu, (size_t)TXD * T * 4, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+        cudaMemcpyAsync(px_d, prompt_x, (size_t)MEL * T * 4, cudaMemcpyHostToDevice, s) != cudaSuccess)
+        return fail(GSVCU_ERR_CUDA, "prepare input upload failed");
+    const unsigned gb = (unsigned)std::min(2048, (TXD * T + 255) / 256);
+    launch_pdl(k_dit_text_in, dim3(gb), dim3(256), 0, s, (const float*)mu_d, (const float*)cis, T, txf);
+    DitGemmArgs a{};
+    a.R = T; a.T = T; a.x_lens = T; a.err = errw;
+    for (int bi = 0; bi < 4; bi++) {
+        const TextBlock& w = TB[bi];
+        launch_pdl(k_dit_dwconv_ln, dim3((unsigned)((T + 7) / 8)), dim3(256), 0, s, (const float*)txf, T,
+                   (const float*)w.w7, (const float*)w.b, (const float*)w.nw, (const float*)w.nb, tx16);
+        DitGemmArgs g = a;
+        g.N = TXI; g.K = TXD; g.bias = w.b1; g.out32 = hb; g.ld = TXI;
+        if (!gemm(DE_F32, tx16, w.w1, g, s)) return fail(GSVCU_ERR_CUDA, "tensor map encoding failed");
+        launch_pdl(k_dit_gelu_colnorm, dim3(TXI / 32), dim3(256), 0, s, hb, T, gx);
+        launch_pdl(k_dit_grn, dim3((unsigned)std::min(1024, (TXI * T + 255) / 256)), dim3(256), 0, s, (const float*)hb,
+                   T, (const float*)gx, (const float*)w.gamma, (const float*)w.beta, h16);
+        g = a;
+        g.N = TXD; g.K = TXI; g.bias = w.b2; g.out32 = txf; g.ld = TXD;
+        if (!gemm(DE_RESID, h16, w.w2, g, s)) return fail(GSVCU_ERR_CUDA, "tensor map encoding failed");
+    }
+    launch_pdl(k_dit_pack_ctx, dim3((unsigned)std::min(2048, (2 * T * CTXK + 255) / 256)), dim3(256), 0, s,
+               (const float*)px_d, (const float*)txf, T, ctx16);
+    DitGemmArgs g = a;
+    g.R = 2 * T; g.N = DM; g.K = CTXK; g.bias = b_ctx; g.out32 = cond; g.ld = DM;
+    if (!gemm(DE_F32, ctx16, w_ctx, g, s)) return fail(GSVCU_ERR_CUDA, "tensor map encoding failed");
+    if (cudaPeekAtLastError() != cudaSuccess) return fail(GSVCU_ERR_CUDA, cudaGetErrorString(cudaGetLastError()));
     return GSVCU_OK;
 }
 
@@ -1218,6 +1397,41 @@ int gsvcu_dit_load(int device, const char* path, gsvcu_dit** out) {
     }
     c->inv_freq.assign(32, 0.0f);
     if ((rc = vecf("dit.rotary_embed.inv_freq", 32, c->inv_freq, 0))) return done(rc);
+    // the static cache's text path and context projection (prepare); optional
+    if (f.tensor("dit.text_embed.freqs_cis")) {
+        std::vector<float> cis;
+        if ((rc = [&]() -> int {
+                 cis.assign((size_t)MAXPOS * TXD, 0.0f);
+                 return vecf("dit.text_embed.freqs_cis", MAXPOS * TXD, cis, 0);
+             }()) ||
+            (rc = c->upload(cis, &c->cis)))
+            return done(rc);
+        for (int bi = 0; bi < 4; bi++) {
+            gsvcu_dit::TextBlock& w = c->TB[bi];
+            const std::string b = "dit.text_embed.text_blocks." + std::to_string(bi) + ".";
+            struct V { const char* n; int len; float** dst; };
+            const V vs[] = {{"dwconv.weight", 7 * TXD, &w.w7}, {"dwconv.bias", TXD, &w.b}, {"norm.weight", TXD, &w.nw},
+                            {"norm.bias", TXD, &w.nb}, {"pwconv1.bias", TXI, &w.b1}, {"grn.gamma", TXI, &w.gamma},
+                            {"grn.beta", TXI, &w.beta}, {"pwconv2.bias", TXD, &w.b2}};
+            for (const V& vv : vs) {
+                hb.assign((size_t)vv.len, 0.0f);
+                if ((rc = vecf(b + vv.n, vv.len, hb, 0)) || (rc = c->upload(hb, vv.dst))) return done(rc);
+            }
+            hw.assign((size_t)TXI * TXD, 0);
+            if ((rc = mat(b + "pwconv1.weight", TXI, TXD, TXI, TXD, hw, 0)) || (rc = c->upload(hw, (uint16_t**)&w.w1)))
+                return done(rc);
+            hw.assign((size_t)TXD * TXI, 0);
+            if ((rc = mat(b + "pwconv2.weight", TXD, TXI, TXD, TXI, hw, 0)) || (rc = c->upload(hw, (uint16_t**)&w.w2)))
+                return done(rc);
+        }
+        hw.assign((size_t)DM * CTXK, 0);
+        hb.assign(DM, 0.0f);
+        if ((rc = mat("dit.input_embed.proj.weight_ctx", DM, MEL + TXD, DM, CTXK, hw, 0)) ||
+            (rc = c->upload(hw, (uint16_t**)&c->w_ctx)) || (rc = vecf("dit.input_embed.proj.bias", DM, hb, 0)) ||
+            (rc = c->upload(hb, &c->b_ctx)))
+            return done(rc);
+        c->has_text = true;
+    }
     return done(GSVCU_OK);
 }
 
@@ -1231,14 +1445,17 @@ int gsvcu_dit_get_hparams(const gsvcu_dit* c, gsvcu_dit_hparams* out) {
     return GSVCU_OK;
 }
 
-int gsvcu_dit_set_condition(gsvcu_dit* c, const float* cond, const float* neg, int32_t T, int32_t x_lens) {
-    if (!c || !cond || !neg || T <= 0 || T > 65536) return GSVCU_ERR_ARG;
-    DevGuard dg(c->device);
+}  // extern "C"
+
+namespace {
+
+// Buffers for T frames, x_lens, and the RoPE tables of head 0: angle = n * inv_freq[i] in float
+// (src/gsv_dit.cpp:787-793).
+int set_shape(gsvcu_dit* c, int T, int x_lens) {
     if (x_lens <= 0 || x_lens > T) x_lens = T;
     int rc;
     if ((rc = c->reserve(T, 2 * T))) return rc;
     c->x_lens = x_lens;
-    // RoPE tables of head 0: angle = n * inv_freq[i] in float (src/gsv_dit.cpp:787-793)
     std::vector<float> cs((size_t)T * 32), sn((size_t)T * 32);
     for (int n = 0; n < T; n++)
         for (int i = 0; i < 32; i++) {
@@ -1246,14 +1463,82 @@ int gsvcu_dit_set_condition(gsvcu_dit* c, const float* cond, const float* neg, i
             cs[(size_t)n * 32 + i] = std::cos(a);
             sn[(size_t)n * 32 + i] = std::sin(a);
         }
+    if (cudaMemcpyAsync(c->rcos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice, c->stream) != cudaSuccess ||
+        cudaMemcpyAsync(c->rsin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice, c->stream) != cudaSuccess ||
+        cudaStreamSynchronize(c->stream) != cudaSuccess)
+        return c->fail(GSVCU_ERR_CUDA, "RoPE table upload failed");
+    return GSVCU_OK;
+}
+
+// randn01 * 0.875 of gsv_dit::sample (src/gsv_dit.cpp:1403-1408, 1436-1438): gsv_rng's xorshift64* draws
+// (src/gsv_sampler.h:33-40), two per value, Box-Muller in float.
+void seeded_noise(uint64_t seed, float* x, size_t n) {
+    uint64_t st = seed ? seed : 1;
+    auto uniform01 = [&]() {
+        st ^= st >> 12;
+        st ^= st << 25;
+        st ^= st >> 27;
+        return (float)(((st * 0x2545F4914F6CDD1Dull) >> 40) * (1.0 / 16777216.0));
+    };
+    for (size_t i = 0; i < n; i++) {
+        float u1 = uniform01();
+        const float u2 = uniform01();
+        if (u1 < 1e-30f) u1 = 1e-30f;
+        x[i] = sqrtf(-2.0f * logf(u1)) * cosf(6.283185307179586f * u2) * 0.875f;
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+int gsvcu_dit_set_condition(gsvcu_dit* c, const float* cond, const float* neg, int32_t T, int32_t x_lens) {
+    if (!c || !cond || !neg || T <= 0 || T > 65536) return GSVCU_ERR_ARG;
+    DevGuard dg(c->device);
+    int rc;
+    if ((rc = set_shape(c, T, x_lens))) return rc;
     const size_t cb = (size_t)T * DM * 4;
     if (cudaMemcpyAsync(c->cond, cond, cb, cudaMemcpyHostToDevice, c->stream) != cudaSuccess ||
         cudaMemcpyAsync(c->cond + (size_t)T * DM, neg, cb, cudaMemcpyHostToDevice, c->stream) != cudaSuccess ||
-        cudaMemcpyAsync(c->rcos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice, c->stream) != cudaSuccess ||
-        cudaMemcpyAsync(c->rsin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice, c->stream) != cudaSuccess)
+        cudaStreamSynchronize(c->stream) != cudaSuccess)
         return c->fail(GSVCU_ERR_CUDA, "condition upload failed");
-    if (cudaStreamSynchronize(c->stream) != cudaSuccess) return c->fail(GSVCU_ERR_CUDA, "condition upload failed");
     return GSVCU_OK;
+}
+
+int gsvcu_dit_prepare(gsvcu_dit* c, const float* prompt_mel, const float* mu, int32_t T, int32_t x_lens) {
+    if (!c || !prompt_mel || !mu || T <= 0) return GSVCU_ERR_ARG;
+    if (!c->has_text) return c->fail(GSVCU_ERR_FORMAT, "the model file has no text_embed / proj.weight_ctx tensors");
+    if (T > MAXPOS) return c->fail(GSVCU_ERR_ARG, "T beyond the 4096 text positions");
+    DevGuard dg(c->device);
+    int rc;
+    if ((rc = set_shape(c, T, x_lens)) || (rc = c->prepare_dev(prompt_mel, mu))) return rc;
+    return check_err(c);
+}
+
+int gsvcu_dit_op_condition(gsvcu_dit* c, float* out) {
+    if (!c || !out) return GSVCU_ERR_ARG;
+    if (c->T <= 0) return c->fail(GSVCU_ERR_ARG, "op before set_condition() / prepare()");
+    DevGuard dg(c->device);
+    if (cudaMemcpyAsync(out, c->cond, (size_t)2 * c->T * DM * 4, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess)
+        return c->fail(GSVCU_ERR_CUDA, std::string("output read failed: ") + cudaGetErrorString(cudaGetLastError()));
+    return check_err(c);
+}
+
+int gsvcu_dit_sample_full(gsvcu_dit* c, const float* mu, const float* prompt, int32_t P, int32_t T, int32_t steps,
+                          float cfg, uint64_t seed, const float* x0, float* mel_out) {
+    if (!c || !mu || !prompt || !mel_out || T <= 0 || steps <= 0) return GSVCU_ERR_ARG;
+    if (P <= 0 || P >= T) return c->fail(GSVCU_ERR_ARG, "bad prompt length");
+    std::vector<float> px((size_t)MEL * T, 0.0f);
+    for (int ch = 0; ch < MEL; ch++) std::memcpy(px.data() + (size_t)ch * T, prompt + (size_t)ch * P, (size_t)P * 4);
+    int rc;
+    if ((rc = gsvcu_dit_prepare(c, px.data(), mu, T, T))) return rc;
+    std::vector<float> noise;
+    if (!x0) {
+        noise.resize((size_t)MEL * T);
+        seeded_noise(seed, noise.data(), noise.size());
+        x0 = noise.data();
+    }
+    return gsvcu_dit_sample(c, x0, P, steps, cfg, mel_out);
 }
 
 int gsvcu_dit_velocity(gsvcu_dit* c, const float* x_mel, float t, int32_t negative, float* vel) {

@@ -300,7 +300,9 @@ def write_dit_model(path: str, seed: int = 0, depth: int = 22, mat_type: str = "
     (tools/export_gguf/convert_dit.py:40-152): 2D weights `mat_type` (its --spec lin=..), biases, norms and
     inv_freq F32; conv_pos weights in the exporter's [G][OCg][ICg * K] order (inner index ic * 31 + tap).
     Values N(0, 0.02); the AdaLN biases N(0, 0.3) so the gates and modulations are not negligible;
-    inv_freq the fp16-stored 10000^(-2i/64). The text_embed tensors (used only by prepare) are left out."""
+    inv_freq the fp16-stored 10000^(-2i/64); text_embed: freqs_cis by the exporter's formula, 4
+    ConvNeXtV2 blocks (depthwise taps [7][512] as the exporter transposes them, N(0, 0.2); GRN gamma and
+    beta N(0, 0.3))."""
     import gguf
 
     D, MEL = 1024, 100
@@ -329,6 +331,21 @@ def write_dit_model(path: str, seed: int = 0, depth: int = 22, mat_type: str = "
     add("dit.time_embed.time_mlp.0.bias", n(D))
     add("dit.time_embed.time_mlp.2.weight", n(D, D), True)
     add("dit.time_embed.time_mlp.2.bias", n(D))
+    freqs = (np.float32(1.0) / (np.float32(10000.0) ** (np.arange(0, 512, 2, dtype=np.float32) / np.float32(512))))
+    ang = np.outer(np.arange(4096, dtype=np.float32), freqs).astype(np.float32)
+    add("dit.text_embed.freqs_cis", np.concatenate([np.cos(ang), np.sin(ang)], axis=1))
+    for bi in range(4):
+        p = f"dit.text_embed.text_blocks.{bi}."
+        add(p + "dwconv.weight", n(7, 512, s=0.2))
+        add(p + "dwconv.bias", n(512))
+        add(p + "norm.weight", 1.0 + n(512))
+        add(p + "norm.bias", n(512))
+        add(p + "pwconv1.weight", n(1024, 512), True)
+        add(p + "pwconv1.bias", n(1024))
+        add(p + "grn.gamma", n(1, 1, 1024, s=0.3))
+        add(p + "grn.beta", n(1, 1, 1024, s=0.3))
+        add(p + "pwconv2.weight", n(512, 1024), True)
+        add(p + "pwconv2.bias", n(512))
     add("dit.input_embed.proj.weight_mel", n(D, MEL), True)
     add("dit.input_embed.proj.weight_ctx", n(D, 612), True)
     add("dit.input_embed.proj.bias", n(D))
@@ -364,7 +381,7 @@ def write_dit_model(path: str, seed: int = 0, depth: int = 22, mat_type: str = "
 def cached_dit_model(cache_dir: str, seed: int = 0, depth: int = 22, mat_type: str = "f16") -> str:
     """Path of a synthetic DiT GGUF, written once per (seed, depth, mat_type) under cache_dir."""
     os.makedirs(cache_dir, exist_ok=True)
-    path = os.path.join(cache_dir, f"dit_s{seed}_d{depth}_{mat_type}.gguf")
+    path = os.path.join(cache_dir, f"dit_s{seed}_d{depth}_{mat_type}_te.gguf")
     if not os.path.exists(path):
         tmp = path + f".tmp{os.getpid()}"
         write_dit_model(tmp, seed, depth, mat_type)

@@ -122,6 +122,9 @@ SIGNATURES.update({
     "gsvcu_dit_sample": ([_P, _P, _I, _I, C.c_float, _P], C.c_int),
     "gsvcu_dit_op_hidden": ([_P, _P, C.c_float, _I, _P], C.c_int),
     "gsvcu_dit_stream": ([_P, C.POINTER(C.c_void_p)], C.c_int),
+    "gsvcu_dit_prepare": ([_P, _P, _P, _I, _I], C.c_int),
+    "gsvcu_dit_sample_full": ([_P, _P, _P, _I, _I, _I, C.c_float, C.c_uint64, _P, _P], C.c_int),
+    "gsvcu_dit_op_condition": ([_P, _P], C.c_int),
 })
 
 PROF_CLASSES = ["sampler", "step_prep", "qkv_gemm", "decode_attn", "out_gemm", "layernorm", "ffn1_gemm", "ffn2_gemm",
@@ -498,6 +501,31 @@ class Dit:
         assert cond.shape == neg.shape and cond.shape[1] == self.hp.dim
         self._check(self.lib.gsvcu_dit_set_condition(self.h, cond.ctypes.data, neg.ctypes.data, cond.shape[0], x_lens))
         self.T = cond.shape[0]
+
+    def prepare(self, prompt_mel, mu, x_lens=0):
+        """gsv_dit::prepare: the static cache from prompt_mel [100][T] and mu [512][T]."""
+        prompt_mel = np.ascontiguousarray(prompt_mel, np.float32)
+        mu = np.ascontiguousarray(mu, np.float32)
+        self._check(self.lib.gsvcu_dit_prepare(self.h, prompt_mel.ctypes.data, mu.ctypes.data, mu.shape[1], x_lens))
+        self.T = mu.shape[1]
+
+    def condition(self) -> np.ndarray:
+        """The condition rows [2][T][1024] (condition, negative) in use."""
+        out = np.empty((2, self.T, self.hp.dim), np.float32)
+        self._check(self.lib.gsvcu_dit_op_condition(self.h, out.ctypes.data))
+        return out
+
+    def sample_full(self, mu, prompt, steps, cfg, seed=1, x0=None) -> np.ndarray:
+        """gsv_dit::sample: mu [512][T], prompt [100][P] -> mel [100][T - P] (seeded noise when x0 is None)."""
+        mu = np.ascontiguousarray(mu, np.float32)
+        prompt = np.ascontiguousarray(prompt, np.float32)
+        T, P = mu.shape[1], prompt.shape[1]
+        x0p = None if x0 is None else np.ascontiguousarray(x0, np.float32)
+        out = np.empty((100, T - P), np.float32)
+        self._check(self.lib.gsvcu_dit_sample_full(self.h, mu.ctypes.data, prompt.ctypes.data, P, T, steps, float(cfg),
+                                                   seed, None if x0p is None else x0p.ctypes.data, out.ctypes.data))
+        self.T = T
+        return out
 
     def velocity(self, x_mel, t, negative=False) -> np.ndarray:
         """gsv_dit::velocity: x_mel [100][T] -> vel [100][T]."""

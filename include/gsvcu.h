@@ -322,12 +322,24 @@ int gsvcu_dit_get_hparams(const gsvcu_dit* ctx, gsvcu_dit_hparams* out);
  * negative-condition rows [T][1024] (input_embed.proj of [prompt_x | text_embed] and [0 | text_embed], with
  * its bias), x_lens the valid frames (<= 0: T). Also sets the RoPE tables. */
 int gsvcu_dit_set_condition(gsvcu_dit* ctx, const float* cond, const float* neg, int32_t T, int32_t x_lens);
+/* gsv_dit::prepare (src/gsv_dit.cpp:771-830, cache graph :486-531): the static cache from prompt_mel [100][T]
+ * (the prompt frames, zeros after them) and mu [512][T]: text path (mu^T + freqs_cis, 4 ConvNeXtV2 blocks),
+ * condition = proj_ctx([prompt_x | text]) + bias, negative = proj_ctx([0 | text]) + bias. Needs the file's
+ * text_embed and proj.weight_ctx tensors (else GSVCU_ERR_FORMAT); T <= 4096; x_lens <= 0: T. */
+int gsvcu_dit_prepare(gsvcu_dit* ctx, const float* prompt_mel, const float* mu, int32_t T, int32_t x_lens);
 /* gsv_dit::velocity (src/gsv_dit.cpp:1325-1338): one estimator pass at time t; x_mel and vel [100][T]. */
 int gsvcu_dit_velocity(gsvcu_dit* ctx, const float* x_mel, float t, int32_t negative, float* vel);
 /* gsv_dit::sample's CFM loop (src/gsv_dit.cpp:1410-1478) on the set condition: x0 [100][T] the initial
  * noise, the first P frames zeroed, `steps` Euler steps t = j / steps, guidance v + (v - v_neg) * cfg when
  * cfg > 1e-5 (both branches in one batch); mel_out [100][T - P]. */
 int gsvcu_dit_sample(gsvcu_dit* ctx, const float* x0, int32_t P, int32_t steps, float cfg, float* mel_out);
+/* gsv_dit::sample (src/gsv_dit.cpp:1410-1478) in full: prompt [100][P] into the first P of T frames, prepare
+ * with mu [512][T], initial noise x0 [100][T] or, when x0 is null, randn * 0.875 from gsv_rng(seed) as the
+ * reference draws it; mel_out [100][T - P]. */
+int gsvcu_dit_sample_full(gsvcu_dit* ctx, const float* mu, const float* prompt, int32_t P, int32_t T, int32_t steps,
+                          float cfg, uint64_t seed, const float* x0, float* mel_out);
+/* Test entry: the condition rows [2][T][1024] (condition, negative) of the last set_condition / prepare. */
+int gsvcu_dit_op_condition(gsvcu_dit* ctx, float* out);
 /* Test entry: the hidden state [2T][1024] (rows [0, T) conditioned, [T, 2T) negative) after the trunk and
  * the first n_blocks blocks at time t. */
 int gsvcu_dit_op_hidden(gsvcu_dit* ctx, const float* x_mel, float t, int32_t n_blocks, float* hidden);

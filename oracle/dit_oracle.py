@@ -15,7 +15,11 @@ It follows the reference graph (src/gsv_dit.cpp) op by op in numpy:
                                    gated residual
   build_head            :563-576   norm_out (scale, shift) + proj_out
   sample                :1410-1478 Euler steps t = j / steps with guidance v + (v - v_neg) * cfg, the
-                                   prompt frames zeroed
+                                   prompt frames zeroed; x0 = randn * 0.875 from gsv_rng (:1403-1408)
+  prepare / build_prepare :486-531 text path: mu^T + freqs_cis, 4 ConvNeXtV2 blocks (:242-275: depthwise
+                                   conv k = 7 in tap order, LayerNorm with affine, pwconv1, GELU (erf), GRN
+                                   (:222-241), pwconv2, residual); condition = proj_ctx([prompt_x | text]) + b,
+                                   negative = proj_ctx([0 | text]) + b
 Numerics: ggml's mul_mat with F16 weights converts the activations to F16 before the dot products,
 so every matrix product here takes f16-rounded activations against the f16 weights, summed in
 float64 and rounded to float32 once; everything else is float32 (LayerNorm statistics float64).
@@ -190,6 +194,92 @@ def sample(W, x0: np.ndarray, cond: np.ndarray, neg: np.ndarray, P: int, steps: 
         x = (x + dt * vel).astype(np.float32)
         x[:, :P] = 0
     return x[:, P:].copy()
+
+
+def gelu_erf(x):
+    from scipy.special import erf
+    x = np.asarray(x, dtype=np.float32)
+    return (np.float32(0.5) * x * (np.float32(1) + erf(x / np.float32(np.sqrt(2.0))).astype(np.float32))).astype(np.float32)
+
+
+def text_embed(W, mu: np.ndarray) -> np.ndarray:
+    """The text path of the static cache: mu [512][T] -> [T][512]."""
+    T = mu.shape[1]
+    x = (mu.T.astype(np.float32) + W["dit.text_embed.freqs_cis"][:T]).astype(np.float32)
+    for bi in range(4):
+        p = f"dit.text_embed.text_blocks.{bi}."
+        w = W[p + "dwconv.weight"].reshape(7, 512)
+        xp = np.zeros((T + 6, 512), dtype=np.float32)
+        xp[3:3 + T] = x
+        y = xp[0:T] * w[0]
+        for kw in range(1, 7):
+            y = (y + xp[kw:kw + T] * w[kw]).astype(np.float32)
+        y = (y + W[p + "dwconv.bias"]).astype(np.float32)
+        y64 = y.astype(np.float64)
+        mean = y64.mean(axis=1, keepdims=True)
+        var = ((y64 - mean) ** 2).mean(axis=1, keepdims=True)
+        y = (((y64 - mean) / np.sqrt(var + 1e-6)).astype(np.float32) * W[p + "norm.weight"] + W[p + "norm.bias"]).astype(np.float32)
+        h = gelu_erf(mm(y, W[p + "pwconv1.weight"], W[p + "pwconv1.bias"]))
+        gx = np.sqrt((h.astype(np.float64) ** 2).sum(axis=0)).astype(np.float32)
+        nx = (gx / (np.float32(gx.astype(np.float64).mean()) + np.float32(1e-6))).astype(np.float32)
+        g = W[p + "grn.gamma"].reshape(-1)
+        bt = W[p + "grn.beta"].reshape(-1)
+        h = (g * (h * nx) + bt + h).astype(np.float32)
+        x = (x + mm(h, W[p + "pwconv2.weight"], W[p + "pwconv2.bias"])).astype(np.float32)
+    return x
+
+
+def prepare(W, prompt_x: np.ndarray, mu: np.ndarray):
+    """The static cache: condition and negative condition rows [T][1024] from prompt_x [100][T], mu [512][T]."""
+    tx = text_embed(W, mu)
+    T = tx.shape[0]
+    wc, bc = W["dit.input_embed.proj.weight_ctx"], W["dit.input_embed.proj.bias"]
+    cat = np.concatenate([prompt_x.T.astype(np.float32), tx], axis=1)
+    zcat = np.concatenate([np.zeros((T, 100), np.float32), tx], axis=1)
+    return mm(cat, wc, bc), mm(zcat, wc, bc)
+
+
+class Rng:
+    """gsv_rng (src/gsv_sampler.h:33-40): xorshift64*, uniform01 = (next >> 40) / 2^24."""
+
+    def __init__(self, seed: int):
+        self.s = seed if seed else 1
+
+    def next(self) -> int:
+        s = self.s
+        s ^= s >> 12
+        s ^= (s << 25) & 0xFFFFFFFFFFFFFFFF
+        s ^= s >> 27
+        self.s = s
+        return (s * 0x2545F4914F6CDD1D) & 0xFFFFFFFFFFFFFFFF
+
+    def uniform01(self) -> np.float32:
+        return np.float32((self.next() >> 40) * (1.0 / 16777216.0))
+
+
+def noise(seed: int, n: int) -> np.ndarray:
+    """randn01 * 0.875 for n values (src/gsv_dit.cpp:1403-1408, 1436-1438): Box-Muller in float."""
+    r = Rng(seed if seed else 1)
+    out = np.empty(n, np.float32)
+    for i in range(n):
+        u1 = r.uniform01()
+        u2 = r.uniform01()
+        if u1 < np.float32(1e-30):
+            u1 = np.float32(1e-30)
+        v = np.sqrt(np.float32(-2.0) * np.log(u1)) * np.cos(np.float32(6.283185307179586) * u2)
+        out[i] = np.float32(v) * np.float32(0.875)
+    return out
+
+
+def sample_full(W, mu, prompt, P, steps, cfg, seed, x0=None):
+    """gsv_dit::sample: mu [512][T], prompt [100][P] -> mel [100][T - P]."""
+    T = mu.shape[1]
+    prompt_x = np.zeros((100, T), np.float32)
+    prompt_x[:, :P] = prompt
+    cond, neg = prepare(W, prompt_x, mu)
+    if x0 is None:
+        x0 = noise(seed, 100 * T).reshape(100, T)
+    return sample(W, x0, cond, neg, P, steps, cfg)
 
 
 def rel_l2(a: np.ndarray, b: np.ndarray) -> float:

@@ -101,3 +101,33 @@ def test_sample_zeroes_prompt_and_steps(tmp_path, cfg):
     cond = rng.standard_normal((T, 1024)).astype(np.float32)
     out = O.sample(W, x0, cond, cond, P, 2, cfg)
     assert np.array_equal(out, x0[:, P:])
+
+
+def test_seeded_noise_follows_gsv_rng():
+    """x0 = randn01 * 0.875 from gsv_rng (src/gsv_sampler.h:33-40, src/gsv_dit.cpp:1403-1408): the first
+    values from the xorshift64* formula written out here, and the distribution."""
+    s = 99
+    def nxt():
+        nonlocal s
+        s ^= s >> 12
+        s ^= (s << 25) & (2 ** 64 - 1)
+        s ^= s >> 27
+        return (s * 0x2545F4914F6CDD1D) % 2 ** 64
+    u1 = np.float32((nxt() >> 40) / 16777216.0)
+    u2 = np.float32((nxt() >> 40) / 16777216.0)
+    v = np.float32(math.sqrt(-2.0 * math.log(u1)) * math.cos(6.283185307179586 * u2) * 0.875)
+    z = O.noise(99, 20000)
+    assert abs(z[0] - v) < 1e-5
+    assert abs(float(z.std()) - 0.875) < 0.02 and abs(float(z.mean())) < 0.02
+
+
+def test_prepare_negative_drops_the_prompt(tmp_path):
+    """The negative condition is the projection of [0 | text]: it does not depend on the prompt frames."""
+    p = S.write_dit_model(str(tmp_path / "d.gguf"), seed=6, depth=1)
+    W = O.load(p)
+    rng = np.random.default_rng(7)
+    T = 40
+    mu = rng.standard_normal((512, T)).astype(np.float32)
+    a = O.prepare(W, rng.standard_normal((100, T)).astype(np.float32), mu)
+    b = O.prepare(W, np.zeros((100, T), np.float32), mu)
+    assert np.array_equal(a[1], b[1]) and np.array_equal(b[0], b[1]) and not np.array_equal(a[0], b[0])
