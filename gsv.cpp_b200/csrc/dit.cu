@@ -31,6 +31,7 @@
 #include <cuda.h>
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdio>
@@ -1586,6 +1587,66 @@ int gsvcu_dit_sample(gsvcu_dit* c, const float* x0, int32_t P, int32_t steps, fl
                             cudaMemcpyDeviceToHost, c->stream) != cudaSuccess)
             return c->fail(GSVCU_ERR_CUDA, std::string("output read failed: ") + cudaGetErrorString(cudaGetLastError()));
     return check_err(c);
+}
+
+int gsvcu_dit_synthesize(gsvcu_dit* c, const float* fea_ref, int32_t R, const float* fea_todo, int32_t N,
+                         const float* mel_ref, int32_t mel_ref_T, int32_t steps, float cfg, uint64_t seed,
+                         int32_t block_override, const float* const* x0_chunks, int32_t n_x0, float* mel_out) {
+    if (!c || !fea_ref || !fea_todo || !mel_ref || !mel_out || steps <= 0) return GSVCU_ERR_ARG;
+    if (R <= 0 || N <= 0 || mel_ref_T <= 0) return c->fail(GSVCU_ERR_ARG, "synthesize(): bad R, N or mel_ref_T");
+    // synthesize_v5_mel's framing (src/gsv_dit.cpp:1480-1581): the reference frames are the last 500 of the
+    // common length of mel_ref and fea_ref; chunks of at most 640 frames (block_override > 0: that many),
+    // with reference + chunk <= 1000 frames; every chunk after the first takes as prompt the reference
+    // frames with their last 32 replaced by the previous chunk's last generated frames (and features).
+    constexpr int REF = 500, TAIL = 32, TOTAL = 1000, MAXCHUNK = 640;
+    const int ref_common = std::min(mel_ref_T, R);
+    const int ref_off = ref_common > REF ? ref_common - REF : 0;
+    const int rf = ref_common - ref_off;
+    const int chunk = std::min(TOTAL - rf, block_override > 0 ? block_override : MAXCHUNK);
+    if (chunk <= 0) return c->fail(GSVCU_ERR_ARG, "synthesize(): reference too long");
+    auto cols = [&](const float* src, int C, int ld, int off, int n, float* dst, int dld) {
+        for (int ch = 0; ch < C; ch++) std::memcpy(dst + (size_t)ch * dld, src + (size_t)ch * ld + off, (size_t)n * 4);
+    };
+    std::vector<float> mel_ref_s((size_t)MEL * rf), fea_ref_s((size_t)TXD * rf);
+    cols(mel_ref, MEL, mel_ref_T, ref_off, rf, mel_ref_s.data(), rf);
+    cols(fea_ref, TXD, R, ref_off, rf, fea_ref_s.data(), rf);
+    std::vector<float> roll_mel = mel_ref_s, roll_fea = fea_ref_s, prompt = mel_ref_s, feat = fea_ref_s;
+    int roll_n = rf;
+    uint64_t cseed = seed;
+    int ci = 0;
+    for (int start = 0; start < N; start += chunk, ci++) {
+        const int tlen = std::min(chunk, N - start);
+        if (start > 0) {
+            const int tail = std::min({TAIL, rf, roll_n});
+            const int prefix = rf - tail;
+            for (int ch = 0; ch < MEL; ch++) {
+                std::memcpy(prompt.data() + (size_t)ch * rf, mel_ref_s.data() + (size_t)ch * rf, (size_t)prefix * 4);
+                std::memcpy(prompt.data() + (size_t)ch * rf + prefix, roll_mel.data() + (size_t)ch * roll_n + (roll_n - tail),
+                            (size_t)tail * 4);
+            }
+            for (int ch = 0; ch < TXD; ch++) {
+                std::memcpy(feat.data() + (size_t)ch * rf, fea_ref_s.data() + (size_t)ch * rf, (size_t)prefix * 4);
+                std::memcpy(feat.data() + (size_t)ch * rf + prefix, roll_fea.data() + (size_t)ch * roll_n + (roll_n - tail),
+                            (size_t)tail * 4);
+            }
+        }
+        const int T = rf + tlen;   // mu = [features of the prompt | the chunk's target features]
+        std::vector<float> mu((size_t)TXD * T), gen((size_t)MEL * tlen);
+        cols(feat.data(), TXD, rf, 0, rf, mu.data(), T);
+        cols(fea_todo, TXD, N, start, tlen, mu.data() + rf, T);
+        const float* x0 = (x0_chunks && ci < n_x0) ? x0_chunks[ci] : nullptr;
+        int rc;
+        if ((rc = gsvcu_dit_sample_full(c, mu.data(), prompt.data(), rf, T, steps, cfg, cseed, x0, gen.data()))) return rc;
+        cseed = cseed * 6364136223846793005ull + 1442695040888963407ull;
+        cols(gen.data(), MEL, tlen, 0, tlen, mel_out + start, N);
+        const int keep = std::min(rf, tlen);   // roll: the chunk's last frames and their features
+        roll_n = keep;
+        roll_mel.resize((size_t)MEL * keep);
+        roll_fea.resize((size_t)TXD * keep);
+        cols(gen.data(), MEL, tlen, tlen - keep, keep, roll_mel.data(), keep);
+        cols(fea_todo, TXD, N, start + tlen - keep, keep, roll_fea.data(), keep);
+    }
+    return GSVCU_OK;
 }
 
 int gsvcu_dit_op_hidden(gsvcu_dit* c, const float* x_mel, float t, int32_t n_blocks, float* hidden) {

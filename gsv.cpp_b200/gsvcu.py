@@ -125,6 +125,7 @@ SIGNATURES.update({
     "gsvcu_dit_prepare": ([_P, _P, _P, _I, _I], C.c_int),
     "gsvcu_dit_sample_full": ([_P, _P, _P, _I, _I, _I, C.c_float, C.c_uint64, _P, _P], C.c_int),
     "gsvcu_dit_op_condition": ([_P, _P], C.c_int),
+    "gsvcu_dit_synthesize": ([_P, _P, _I, _P, _I, _P, _I, _I, C.c_float, C.c_uint64, _I, _P, _I, _P], C.c_int),
 })
 
 PROF_CLASSES = ["sampler", "step_prep", "qkv_gemm", "decode_attn", "out_gemm", "layernorm", "ffn1_gemm", "ffn2_gemm",
@@ -525,6 +526,17 @@ class Dit:
         self._check(self.lib.gsvcu_dit_sample_full(self.h, mu.ctypes.data, prompt.ctypes.data, P, T, steps, float(cfg),
                                                    seed, None if x0p is None else x0p.ctypes.data, out.ctypes.data))
         self.T = T
+        return out
+
+    def synthesize(self, fea_ref, fea_todo, mel_ref, steps, cfg, seed=1, block_override=0) -> np.ndarray:
+        """gsv_dit::synthesize: fea_ref [512][R], fea_todo [512][N], mel_ref [100][mel_ref_T] -> mel [100][N]."""
+        fea_ref = np.ascontiguousarray(fea_ref, np.float32)
+        fea_todo = np.ascontiguousarray(fea_todo, np.float32)
+        mel_ref = np.ascontiguousarray(mel_ref, np.float32)
+        out = np.empty((100, fea_todo.shape[1]), np.float32)
+        self._check(self.lib.gsvcu_dit_synthesize(self.h, fea_ref.ctypes.data, fea_ref.shape[1], fea_todo.ctypes.data,
+                                                  fea_todo.shape[1], mel_ref.ctypes.data, mel_ref.shape[1], steps,
+                                                  float(cfg), seed, block_override, None, 0, out.ctypes.data))
         return out
 
     def velocity(self, x_mel, t, negative=False) -> np.ndarray:

@@ -338,6 +338,14 @@ int gsvcu_dit_sample(gsvcu_dit* ctx, const float* x0, int32_t P, int32_t steps, 
  * reference draws it; mel_out [100][T - P]. */
 int gsvcu_dit_sample_full(gsvcu_dit* ctx, const float* mu, const float* prompt, int32_t P, int32_t T, int32_t steps,
                           float cfg, uint64_t seed, const float* x0, float* mel_out);
+/* gsv_dit::synthesize (src/gsv_dit.cpp:1480-1581): the reference frames (the last 500 of min(mel_ref_T, R))
+ * of mel_ref [100][mel_ref_T] and fea_ref [512][R] as prompt, fea_todo [512][N] cut into chunks of 640 frames
+ * (block_override > 0: that many; reference + chunk <= 1000), each chunk after the first prompted with the
+ * reference frames whose last 32 are the previous chunk's last generated frames; chunk i samples with seed
+ * LCG^i(seed) and, when i < n_x0, initial noise x0_chunks[i] ([100][reference + chunk]); mel_out [100][N]. */
+int gsvcu_dit_synthesize(gsvcu_dit* ctx, const float* fea_ref, int32_t R, const float* fea_todo, int32_t N,
+                         const float* mel_ref, int32_t mel_ref_T, int32_t steps, float cfg, uint64_t seed,
+                         int32_t block_override, const float* const* x0_chunks, int32_t n_x0, float* mel_out);
 /* Test entry: the condition rows [2][T][1024] (condition, negative) of the last set_condition / prepare. */
 int gsvcu_dit_op_condition(gsvcu_dit* ctx, float* out);
 /* Test entry: the hidden state [2T][1024] (rows [0, T) conditioned, [T, 2T) negative) after the trunk and

@@ -20,6 +20,8 @@ It follows the reference graph (src/gsv_dit.cpp) op by op in numpy:
                                    conv k = 7 in tap order, LayerNorm with affine, pwconv1, GELU (erf), GRN
                                    (:222-241), pwconv2, residual); condition = proj_ctx([prompt_x | text]) + b,
                                    negative = proj_ctx([0 | text]) + b
+  synthesize            :1480-1581 chunks of <= 640 frames after the last 500 reference frames, the prompt
+                                   of later chunks ending in the previous chunk's last 32 frames
 Numerics: ggml's mul_mat with F16 weights converts the activations to F16 before the dot products,
 so every matrix product here takes f16-rounded activations against the f16 weights, summed in
 float64 and rounded to float32 once; everything else is float32 (LayerNorm statistics float64).
@@ -280,6 +282,37 @@ def sample_full(W, mu, prompt, P, steps, cfg, seed, x0=None):
     if x0 is None:
         x0 = noise(seed, 100 * T).reshape(100, T)
     return sample(W, x0, cond, neg, P, steps, cfg)
+
+
+def synthesize(W, fea_ref, fea_todo, mel_ref, steps, cfg, seed, block_override=0):
+    """gsv_dit::synthesize (src/gsv_dit.cpp:1480-1581): chunked sampling with a rolling prompt -> mel [100][N]."""
+    REF, TAIL, TOTAL, MAXCHUNK = 500, 32, 1000, 640
+    R, N, MT = fea_ref.shape[1], fea_todo.shape[1], mel_ref.shape[1]
+    common = min(MT, R)
+    off = common - REF if common > REF else 0
+    rf = common - off
+    chunk = min(TOTAL - rf, block_override if block_override > 0 else MAXCHUNK)
+    mel_s = mel_ref[:, off:off + rf].astype(np.float32)
+    fea_s = fea_ref[:, off:off + rf].astype(np.float32)
+    roll_mel, roll_fea = mel_s, fea_s
+    out = np.zeros((100, N), np.float32)
+    cseed = seed
+    for start in range(0, N, chunk):
+        tlen = min(chunk, N - start)
+        if start == 0:
+            prompt, feat = mel_s, fea_s
+        else:
+            tail = min(TAIL, rf, roll_mel.shape[1], roll_fea.shape[1])
+            prompt = np.concatenate([mel_s[:, :rf - tail], roll_mel[:, roll_mel.shape[1] - tail:]], axis=1)
+            feat = np.concatenate([fea_s[:, :rf - tail], roll_fea[:, roll_fea.shape[1] - tail:]], axis=1)
+        mu = np.concatenate([feat, fea_todo[:, start:start + tlen]], axis=1).astype(np.float32)
+        gen = sample_full(W, mu, prompt, rf, steps, cfg, cseed)
+        cseed = (cseed * 6364136223846793005 + 1442695040888963407) % 2 ** 64
+        out[:, start:start + tlen] = gen
+        keep = min(rf, tlen)
+        roll_mel = gen[:, tlen - keep:]
+        roll_fea = fea_todo[:, start + tlen - keep:start + tlen].astype(np.float32)
+    return out
 
 
 def rel_l2(a: np.ndarray, b: np.ndarray) -> float:

@@ -152,3 +152,23 @@ def test_dit_sample_full_seeded_matches_oracle(dit_small):
     print(f"sample_full: rel_l2 {e:.2e}")
     assert got.shape == (100, T - P) and e <= TOL
     d.close()
+
+
+def test_dit_synthesize_matches_oracle(dit_small):
+    """gsv_dit::synthesize: three chunks (block_override 40: 40 + 40 + 15 frames) after 55 reference frames,
+    each later chunk prompted with the previous chunk's last 32 frames, chunk seeds from the LCG."""
+    import gsvcu
+    path, W = dit_small
+    rng = np.random.default_rng(23)
+    fea_ref = rng.standard_normal((512, 70)).astype(np.float32)
+    fea_todo = rng.standard_normal((512, 95)).astype(np.float32)
+    mel_ref = rng.standard_normal((100, 55)).astype(np.float32)
+    d = gsvcu.Dit(path)
+    got = d.synthesize(fea_ref, fea_todo, mel_ref, 2, 1.3, seed=77, block_override=40)
+    ref = O.synthesize(W, fea_ref, fea_todo, mel_ref, 2, 1.3, 77, block_override=40)
+    e = rel_l2(got, ref)
+    print(f"synthesize: rel_l2 {e:.2e}")
+    assert got.shape == (100, 95) and e <= TOL
+    for s0, s1 in ((0, 40), (40, 80), (80, 95)):
+        assert rel_l2(got[:, s0:s1], ref[:, s0:s1]) <= TOL
+    d.close()
