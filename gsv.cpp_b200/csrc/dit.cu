@@ -639,11 +639,12 @@ __global__ void __launch_bounds__(256) k_dit_pack_mel(const float* __restrict__ 
     }
 }
 
-// Euler step with guidance (gsv_dit::sample, src/gsv_dit.cpp:1464-1469): v = vel + (vel - neg) * cfg
-// (branch 1 rows hold neg when guided), x += dt * v, then the prompt frames are zeroed.
-// update = 0: only the zeroing (before the first step).
-__global__ void __launch_bounds__(256) k_dit_euler(const float* __restrict__ vel, int T, int update, int guided, float cfg,
-                                                   float dt, int P, float* __restrict__ xm) {
+// Euler step with guidance (gsv_dit::sample, src/gsv_dit.cpp:1449-1469): v = vel + (vel - ng) * cfg with the
+// unconditional velocity ng = neg (rows [T][128]) or, given neg2, the extrapolation 2 neg - neg2 (uncond_reuse
+// 2); x += dt * v; then the prompt frames are zeroed. update = 0: only the zeroing (before the first step).
+__global__ void __launch_bounds__(256) k_dit_euler(const float* __restrict__ vel, int T, int update,
+                                                   const float* __restrict__ neg, const float* __restrict__ neg2,
+                                                   float cfg, float dt, int P, float* __restrict__ xm) {
     griddep_wait();
     griddep_launch();
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < MEL * T; i += gridDim.x * blockDim.x) {
@@ -651,8 +652,9 @@ __global__ void __launch_bounds__(256) k_dit_euler(const float* __restrict__ vel
         float x = xm[i];
         if (update) {
             float v = vel[(size_t)t * MELP + c];
-            if (guided) {
-                const float ng = vel[(size_t)(T + t) * MELP + c];
+            if (neg) {
+                float ng = neg[(size_t)t * MELP + c];
+                if (neg2) ng = 2.0f * ng - neg2[(size_t)t * MELP + c];
                 v = v + (v - ng) * cfg;
             }
             x = x + dt * v;
@@ -998,6 +1000,8 @@ struct gsvcu_dit {
     int cap_steps = 0;
     float *temb = nullptr, *th = nullptr, *ada = nullptr;   // [1024], [1024], [depth * 6144 + 2048]
     float *vout = nullptr;        // [100][T]
+    float *neg1 = nullptr, *neg2 = nullptr;   // [T][128]: the last two computed unconditional velocities
+    int uncond_reuse = 0;         // gsv_dit_alg::uncond_reuse (0, 1 or 2)
     float *mu_d = nullptr, *px_d = nullptr;   // prepare inputs [512][T], [100][T]
     float *txf = nullptr;         // [T][512] text path (f32)
     __half *tx16 = nullptr;       // [T][512] ConvNeXt operand
@@ -1078,7 +1082,8 @@ int gsvcu_dit::reserve(int T_, int rows) {
                       {(void**)&th, DM * 4}, {(void**)&ada, nada * 4}, {(void**)&vout, MEL * TT * 4},
                       {(void**)&mu_d, TXD * TT * 4}, {(void**)&px_d, MEL * TT * 4}, {(void**)&txf, TT * TXD * 4},
                       {(void**)&tx16, TT * TXD * 2}, {(void**)&hb, TT * TXI * 4}, {(void**)&gx, TXI * 4},
-                      {(void**)&ctx16, 2 * TT * CTXK * 2}};
+                      {(void**)&ctx16, 2 * TT * CTXK * 2}, {(void**)&neg1, TT * MELP * 4},
+                      {(void**)&neg2, TT * MELP * 4}};
     for (const A& a : list) {
         if (cudaMalloc(a.p, a.bytes) != cudaSuccess) {
             cudaGetLastError();
@@ -1575,12 +1580,37 @@ int gsvcu_dit_sample(gsvcu_dit* c, const float* x0, int32_t P, int32_t steps, fl
         return c->fail(GSVCU_ERR_CUDA, "input upload failed");
     const bool guided = cfg > 1e-5f;
     const dim3 eg((unsigned)std::min(1024, (MEL * T + 255) / 256));
+    const float* none = nullptr;
     // x[:, :P] = 0 before the first step (src/gsv_dit.cpp:1440-1441)
-    launch_pdl(k_dit_euler, eg, dim3(256), 0, c->stream, (const float*)c->vel, T, 0, 0, 0.0f, 0.0f, P, c->xmel);
+    launch_pdl(k_dit_euler, eg, dim3(256), 0, c->stream, (const float*)c->vel, T, 0, none, none, 0.0f, 0.0f, P, c->xmel);
+    // uncond_reuse (src/gsv_dit.cpp:1449-1468): odd steps take the last computed unconditional velocity (1) or
+    // extrapolate the last two (2) instead of running the negative branch
+    float *p1 = c->neg1, *p2 = c->neg2;
+    int neg_count = 0;
+    const int ur = c->uncond_reuse;
     for (int j = 0; j < steps; j++) {
-        if ((rc = c->forward(guided ? 2 : 1, 0, c->tsin + (size_t)j * TSIN, c->hp.depth, true))) return rc;
-        launch_pdl(k_dit_euler, eg, dim3(256), 0, c->stream, (const float*)c->vel, T, 1, guided ? 1 : 0, cfg, dt, P,
-                   c->xmel);
+        const float* tj = c->tsin + (size_t)j * TSIN;
+        const bool odd = (j & 1) != 0;
+        if (guided && odd && ((ur == 1 && neg_count >= 1) || (ur == 2 && neg_count >= 2))) {
+            if ((rc = c->forward(1, 0, tj, c->hp.depth, true))) return rc;
+            launch_pdl(k_dit_euler, eg, dim3(256), 0, c->stream, (const float*)c->vel, T, 1, (const float*)p1,
+                       ur == 2 ? (const float*)p2 : none, cfg, dt, P, c->xmel);
+        } else if (guided) {
+            if ((rc = c->forward(2, 0, tj, c->hp.depth, true))) return rc;
+            const float* vneg = c->vel + (size_t)T * MELP;
+            if (ur) {   // keep the last two computed unconditional velocities
+                std::swap(p1, p2);
+                if (cudaMemcpyAsync(p1, vneg, (size_t)T * MELP * 4, cudaMemcpyDeviceToDevice, c->stream) != cudaSuccess)
+                    return c->fail(GSVCU_ERR_CUDA, "velocity copy failed");
+            }
+            neg_count++;
+            launch_pdl(k_dit_euler, eg, dim3(256), 0, c->stream, (const float*)c->vel, T, 1, vneg, none, cfg, dt, P,
+                       c->xmel);
+        } else {
+            if ((rc = c->forward(1, 0, tj, c->hp.depth, true))) return rc;
+            launch_pdl(k_dit_euler, eg, dim3(256), 0, c->stream, (const float*)c->vel, T, 1, none, none, cfg, dt, P,
+                       c->xmel);
+        }
     }
     for (int ch = 0; ch < MEL; ch++)
         if (cudaMemcpyAsync(mel_out + (size_t)ch * (T - P), c->xmel + (size_t)ch * T + P, (size_t)(T - P) * 4,
@@ -1646,6 +1676,18 @@ int gsvcu_dit_synthesize(gsvcu_dit* c, const float* fea_ref, int32_t R, const fl
         cols(gen.data(), MEL, tlen, tlen - keep, keep, roll_mel.data(), keep);
         cols(fea_todo, TXD, N, start + tlen - keep, keep, roll_fea.data(), keep);
     }
+    return GSVCU_OK;
+}
+
+int gsvcu_dit_set_alg(gsvcu_dit* c, int32_t uncond_reuse) {
+    if (!c) return GSVCU_ERR_ARG;
+    c->uncond_reuse = (uncond_reuse < 0 || uncond_reuse > 2) ? 0 : uncond_reuse;
+    return GSVCU_OK;
+}
+
+int gsvcu_dit_get_alg(const gsvcu_dit* c, int32_t* uncond_reuse) {
+    if (!c || !uncond_reuse) return GSVCU_ERR_ARG;
+    *uncond_reuse = c->uncond_reuse;
     return GSVCU_OK;
 }
 

@@ -125,6 +125,8 @@ SIGNATURES.update({
     "gsvcu_dit_prepare": ([_P, _P, _P, _I, _I], C.c_int),
     "gsvcu_dit_sample_full": ([_P, _P, _P, _I, _I, _I, C.c_float, C.c_uint64, _P, _P], C.c_int),
     "gsvcu_dit_op_condition": ([_P, _P], C.c_int),
+    "gsvcu_dit_set_alg": ([_P, _I], C.c_int),
+    "gsvcu_dit_get_alg": ([_P, C.POINTER(C.c_int32)], C.c_int),
     "gsvcu_dit_synthesize": ([_P, _P, _I, _P, _I, _P, _I, _I, C.c_float, C.c_uint64, _I, _P, _I, _P], C.c_int),
 })
 
@@ -538,6 +540,10 @@ class Dit:
                                                   fea_todo.shape[1], mel_ref.ctypes.data, mel_ref.shape[1], steps,
                                                   float(cfg), seed, block_override, None, 0, out.ctypes.data))
         return out
+
+    def set_alg(self, uncond_reuse: int):
+        """gsv_dit::set_alg: uncond_reuse 0, 1 (reuse on odd steps) or 2 (extrapolate on odd steps)."""
+        self._check(self.lib.gsvcu_dit_set_alg(self.h, uncond_reuse))
 
     def velocity(self, x_mel, t, negative=False) -> np.ndarray:
         """gsv_dit::velocity: x_mel [100][T] -> vel [100][T]."""

@@ -346,6 +346,11 @@ int gsvcu_dit_sample_full(gsvcu_dit* ctx, const float* mu, const float* prompt, 
 int gsvcu_dit_synthesize(gsvcu_dit* ctx, const float* fea_ref, int32_t R, const float* fea_todo, int32_t N,
                          const float* mel_ref, int32_t mel_ref_T, int32_t steps, float cfg, uint64_t seed,
                          int32_t block_override, const float* const* x0_chunks, int32_t n_x0, float* mel_out);
+/* gsv_dit::set_alg / alg (src/gsv_dit.h:46-49, the loop src/gsv_dit.cpp:1449-1468): uncond_reuse 0 computes
+ * the negative branch every guided step; 1 reuses the last computed one on odd steps; 2 extrapolates
+ * 2 neg[k-1] - neg[k-2] on odd steps (once two exist). Values outside 0..2 mean 0. */
+int gsvcu_dit_set_alg(gsvcu_dit* ctx, int32_t uncond_reuse);
+int gsvcu_dit_get_alg(const gsvcu_dit* ctx, int32_t* uncond_reuse);
 /* Test entry: the condition rows [2][T][1024] (condition, negative) of the last set_condition / prepare. */
 int gsvcu_dit_op_condition(gsvcu_dit* ctx, float* out);
 /* Test entry: the hidden state [2T][1024] (rows [0, T) conditioned, [T, 2T) negative) after the trunk and

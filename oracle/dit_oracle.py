@@ -181,17 +181,30 @@ def branch(W, x_mel: np.ndarray, t: float, cond: np.ndarray, x_lens: int, n_bloc
     return mm(xo, W["dit.proj_out.weight"], W["dit.proj_out.bias"]).T.copy()
 
 
-def sample(W, x0: np.ndarray, cond: np.ndarray, neg: np.ndarray, P: int, steps: int, cfg: float) -> np.ndarray:
-    """The CFM Euler loop on set conditions: x0 [100][T] -> mel [100][T - P]."""
+def sample(W, x0: np.ndarray, cond: np.ndarray, neg: np.ndarray, P: int, steps: int, cfg: float,
+           uncond_reuse: int = 0) -> np.ndarray:
+    """The CFM Euler loop on set conditions: x0 [100][T] -> mel [100][T - P]; uncond_reuse as the reference's
+    alg (src/gsv_dit.cpp:1449-1468): 1 reuses the last computed negative velocity on odd steps, 2
+    extrapolates 2 neg[k-1] - neg[k-2]."""
     x = x0.astype(np.float32).copy()
     T = x.shape[1]
     x[:, :P] = 0
     dt = np.float32(1.0) / np.float32(steps)
+    p1 = p2 = None
+    count = 0
     for j in range(steps):
         t = float(np.float32(j) * dt)
         vel = branch(W, x, t, cond, T)
         if cfg > 1e-5:
-            ng = branch(W, x, t, neg, T)
+            odd = (j & 1) == 1
+            if odd and uncond_reuse == 1 and count >= 1:
+                ng = p1
+            elif odd and uncond_reuse == 2 and count >= 2:
+                ng = (np.float32(2.0) * p1 - p2).astype(np.float32)
+            else:
+                ng = branch(W, x, t, neg, T)
+                count += 1
+                p2, p1 = p1, ng
             vel = (vel + (vel - ng) * np.float32(cfg)).astype(np.float32)
         x = (x + dt * vel).astype(np.float32)
         x[:, :P] = 0

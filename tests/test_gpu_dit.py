@@ -172,3 +172,22 @@ def test_dit_synthesize_matches_oracle(dit_small):
     for s0, s1 in ((0, 40), (40, 80), (80, 95)):
         assert rel_l2(got[:, s0:s1], ref[:, s0:s1]) <= TOL
     d.close()
+
+
+@pytest.mark.parametrize("ur", [1, 2])
+def test_dit_uncond_reuse_matches_oracle(dit_small, ur):
+    """gsv_dit_alg::uncond_reuse: odd guided steps reuse (1) or extrapolate (2) the negative velocity."""
+    import gsvcu
+    path, W = dit_small
+    T, P, steps = 120, 20, 5
+    x0, cond, neg = _inputs(T, 31)
+    d = gsvcu.Dit(path)
+    d.set_condition(cond, neg)
+    d.set_alg(ur)
+    got = d.sample(x0, P, steps, 2.0)
+    ref = O.sample(W, x0, cond, neg, P, steps, 2.0, uncond_reuse=ur)
+    full = O.sample(W, x0, cond, neg, P, steps, 2.0)
+    e = rel_l2(got, ref)
+    print(f"uncond_reuse={ur}: rel_l2 {e:.2e} (vs no reuse {rel_l2(ref, full):.2e})")
+    assert e <= TOL and rel_l2(ref, full) > 10 * e   # the reuse changes the result far more than the GPU error
+    d.close()
