@@ -343,9 +343,9 @@ __global__ void __launch_bounds__(G_THREADS) k_dit_gemm(const __grid_constant__ 
 // S = Q K^T into TMEM and the row maxima; pass 2 S again, P = exp2((S - max) * scale * log2 e) as f16 into
 // shared memory (the 128-byte-swizzled K-major layout the MMA reads), row sums, O += P V^T in TMEM. With the
 // exact row maximum known before any exponential, O needs no rescaling (the cost: Q K^T twice).
-// Warps: 0 TMA (Q once, then K or K + V^T tiles into a 3-stage ring), 1 TMEM + MMA, 2-5 softmax (thread =
-// query row = TMEM lane). S and P are double-buffered, so the MMAs of tile j + 1 overlap the softmax of
-// tile j.
+// Warps: 0 TMA (Q once, then K or K + V^T tiles into a 3-stage ring), 1 TMEM + MMA, 2-9 softmax: two threads
+// per query row (TMEM lane), each on 32 of a tile's 64 keys; row maxima and sums are combined once, through
+// shared memory. S and P are double-buffered, so the MMAs of tile j + 1 overlap the softmax of tile j.
 constexpr int FQ = 128, FK = 64, FKS = 3;
 struct AttnMaps {
     CUtensorMap q;    // qkv16 [R][3072], box 64 x 128
@@ -357,11 +357,13 @@ struct FaSmem {
     static constexpr size_t OFF_K = OFF_Q + FQ * HDD * 2;       // FKS x 8 KB
     static constexpr size_t OFF_V = OFF_K + FKS * FK * HDD * 2; // FKS x 8 KB
     static constexpr size_t OFF_P = OFF_V + FKS * HDD * FK * 2; // 2 x 16 KB
-    static constexpr size_t OFF_BAR = OFF_P + 2 * FQ * FK * 2;
+    static constexpr size_t OFF_X = OFF_P + 2 * FQ * FK * 2;   // [2 halves][128 rows] f32: row max, then row sum
+    static constexpr size_t OFF_BAR = OFF_X + 2 * FQ * 4;
     // qfull, kvfull[FKS], kvempty[FKS], sfull[2], sfree[2], pfull[2], pfree[2], ofull
     static constexpr int NBAR = 1 + 2 * FKS + 8 + 1;
     static constexpr size_t SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
 };
+constexpr int FA_THREADS = 320;   // warp 0 TMA, warp 1 MMA, warps 2-9 softmax (two per TMEM lane quarter)
 constexpr uint32_t FA_TMEM_COLS = 256;   // S0, S1, O (64 columns each)
 
 __device__ __forceinline__ float ex2f(float x) {
@@ -370,7 +372,7 @@ __device__ __forceinline__ float ex2f(float x) {
     return y;
 }
 
-__global__ void __launch_bounds__(G_THREADS) k_dit_attn_tc(const __grid_constant__ AttnMaps m, __half* __restrict__ out,
+__global__ void __launch_bounds__(FA_THREADS) k_dit_attn_tc(const __grid_constant__ AttnMaps m, __half* __restrict__ out,
                                                            int T, int x_lens, int* err) {
     using L = FaSmem;
     constexpr uint32_t IDS = idesc_f16(FQ, FK);    // S: 128 x 64 keys
@@ -398,8 +400,8 @@ __global__ void __launch_bounds__(G_THREADS) k_dit_attn_tc(const __grid_constant
         for (int s = 0; s < FKS; s++) { bar_init(kvfull(s), 1); bar_init(kvempty(s), 1); }
         for (int i = 0; i < 2; i++) {
             bar_init(sfull(i), 1);
-            bar_init(sfree(i), 128);
-            bar_init(pfull(i), 128);
+            bar_init(sfree(i), 256);
+            bar_init(pfull(i), 256);
             bar_init(pfree(i), 1);
         }
         bar_init(ofull, 1);
@@ -496,37 +498,44 @@ __global__ void __launch_bounds__(G_THREADS) k_dit_attn_tc(const __grid_constant
                 if (bar_try(ofull, 0)) break;
         }
     } else {
-        // softmax: thread = query row fr (TMEM lane), keys of tile j in its S buffer's 64 columns
-        const int q = warp & 3, fr = 32 * q + lane;
+        // softmax: thread = (query row fr = TMEM lane, half hf): keys 32 hf .. 32 hf + 31 of each tile
+        const int q = warp & 3, fr = 32 * q + lane, hf = (warp - 2) >> 2;
         const uint32_t tl = tmem + ((uint32_t)(32 * q) << 16);
+        float* xch = (float*)(sm + L::OFF_X);   // [half][row]
         const float c = ATTN_SCALE * 1.4426950408889634f;
         float mx = -INFINITY, l = 0.0f;
         int u = 0, v = 0;
         bool ok = true;
-        for (int pass = 0; pass < 2 && ok; pass++) {
+        // (every softmax thread runs the same named-barrier sequence, also after a failed wait)
+        for (int pass = 0; pass < 2; pass++) {
+            if (pass == 1) {   // the row maximum of both halves
+                xch[hf * FQ + fr] = mx;
+                asm volatile("bar.sync 1, 256;" ::: "memory");
+                mx = fmaxf(xch[fr], xch[FQ + fr]);
+            }
             const float mc = mx * c;
-            for (int j = 0; j < nt; j++, u++) {
+            for (int j = 0; j < nt && ok; j++, u++) {
                 const int sb = u & 1;
                 if (!bar_wait_short_warp(sfull(sb), ((uint32_t)u >> 1) & 1u, abort_flag)) { ok = false; break; }
                 tc_fence_after();
-                float sv[4][16];
+                float sv[2][16];
 #pragma unroll
-                for (int k = 0; k < 4; k++) tmem_ld16(tl + (uint32_t)(sb * FK + 16 * k), sv[k]);
+                for (int k = 0; k < 2; k++) tmem_ld16(tl + (uint32_t)(sb * FK + 32 * hf + 16 * k), sv[k]);
                 tmem_wait_ld();
 #pragma unroll
-                for (int k = 0; k < 4; k++) tmem_bind(sv[k]);
+                for (int k = 0; k < 2; k++) tmem_bind(sv[k]);
                 tc_fence_before();
                 bar_arrive(sfree(sb));
-                const int kv = x_lens - j * FK;   // valid keys in this tile (>= 1)
+                const int kv = x_lens - j * FK - 32 * hf;   // valid keys of this thread's 32 (may be <= 0)
                 if (pass == 0) {
 #pragma unroll
-                    for (int i = 0; i < 64; i++)
+                    for (int i = 0; i < 32; i++)
                         if (i < kv) mx = fmaxf(mx, sv[i >> 4][i & 15]);
                     continue;
                 }
-                uint32_t pw[32];
+                uint32_t pw[16];
 #pragma unroll
-                for (int i = 0; i < 64; i += 2) {
+                for (int i = 0; i < 32; i += 2) {
                     const float p0 = i < kv ? ex2f(__fmaf_rn(sv[i >> 4][i & 15], c, -mc)) : 0.0f;
                     const float p1 = i + 1 < kv ? ex2f(__fmaf_rn(sv[i >> 4][(i + 1) & 15], c, -mc)) : 0.0f;
                     l += p0 + p1;
@@ -536,28 +545,35 @@ __global__ void __launch_bounds__(G_THREADS) k_dit_attn_tc(const __grid_constant
                 if (!bar_wait_short_warp(pfree(pb), (((uint32_t)v >> 1) & 1u) ^ 1u, abort_flag)) { ok = false; break; }
                 uint8_t* prow = sm + L::OFF_P + (size_t)pb * FQ * FK * 2 + (size_t)fr * 128;
 #pragma unroll
-                for (int ch = 0; ch < 8; ch++)   // 128-byte swizzle: chunk ch of row r at ch ^ (r % 8)
-                    *(uint4*)(prow + 16 * (ch ^ (fr & 7))) = make_uint4(pw[4 * ch], pw[4 * ch + 1], pw[4 * ch + 2], pw[4 * ch + 3]);
+                for (int k = 0; k < 4; k++) {   // 128-byte swizzle: chunk ch of row r at ch ^ (r % 8)
+                    const int ch = 4 * hf + k;
+                    *(uint4*)(prow + 16 * (ch ^ (fr & 7))) = make_uint4(pw[4 * k], pw[4 * k + 1], pw[4 * k + 2], pw[4 * k + 3]);
+                }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 bar_arrive(pfull(pb));
                 v++;
             }
         }
+        // row sums of both halves (after every thread has read the maxima)
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        xch[hf * FQ + fr] = l;
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        l = xch[fr] + xch[FQ + fr];
         ok = bar_wait_short_warp(ofull, 0, abort_flag) && ok && !*abort_flag;
         tc_fence_after();
         if (ok) {
-            float o4[4][16];
+            float o2[2][16];
 #pragma unroll
-            for (int k = 0; k < 4; k++) tmem_ld16(tl + (uint32_t)(2 * FK + 16 * k), o4[k]);
+            for (int k = 0; k < 2; k++) tmem_ld16(tl + (uint32_t)(2 * FK + 32 * hf + 16 * k), o2[k]);
             tmem_wait_ld();
 #pragma unroll
-            for (int k = 0; k < 4; k++) tmem_bind(o4[k]);
+            for (int k = 0; k < 2; k++) tmem_bind(o2[k]);
             if (q0 + fr < T) {
                 const float il = 1.0f / l;
-                uint4* dst = (uint4*)(out + ((size_t)b * T + q0 + fr) * DM + h * HDD);
+                uint4* dst = (uint4*)(out + ((size_t)b * T + q0 + fr) * DM + h * HDD + 32 * hf);
 #pragma unroll
-                for (int ch = 0; ch < 8; ch++) {
-                    const float* o = o4[ch >> 1] + 8 * (ch & 1);
+                for (int ch = 0; ch < 4; ch++) {
+                    const float* o = o2[ch >> 1] + 8 * (ch & 1);
                     dst[ch] = make_uint4(pack_h2(o[0] * il, o[1] * il), pack_h2(o[2] * il, o[3] * il),
                                          pack_h2(o[4] * il, o[5] * il), pack_h2(o[6] * il, o[7] * il));
                 }
@@ -932,7 +948,7 @@ bool attention_tc(const __half* qkv16, const __half* vt16, int tp, int T, int B,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return false;
     }
-    launch_pdl(k_dit_attn_tc, dim3((unsigned)((T + FQ - 1) / FQ), NHD, (unsigned)B), dim3(G_THREADS), FaSmem::SMEM, s, m,
+    launch_pdl(k_dit_attn_tc, dim3((unsigned)((T + FQ - 1) / FQ), NHD, (unsigned)B), dim3(FA_THREADS), FaSmem::SMEM, s, m,
                out, T, x_lens, err);
     return true;
 }
