@@ -1547,7 +1547,7 @@ int gsvcu_dit_op_condition(gsvcu_dit* c, float* out) {
 }
 
 int gsvcu_dit_sample_full(gsvcu_dit* c, const float* mu, const float* prompt, int32_t P, int32_t T, int32_t steps,
-                          float cfg, uint64_t seed, const float* x0, float* mel_out) {
+                          float cfg, uint64_t seed, const float* x0, int32_t skip_steps, float* mel_out) {
     if (!c || !mu || !prompt || !mel_out || T <= 0 || steps <= 0) return GSVCU_ERR_ARG;
     if (P <= 0 || P >= T) return c->fail(GSVCU_ERR_ARG, "bad prompt length");
     std::vector<float> px((size_t)MEL * T, 0.0f);
@@ -1560,7 +1560,7 @@ int gsvcu_dit_sample_full(gsvcu_dit* c, const float* mu, const float* prompt, in
         seeded_noise(seed, noise.data(), noise.size());
         x0 = noise.data();
     }
-    return gsvcu_dit_sample(c, x0, P, steps, cfg, mel_out);
+    return gsvcu_dit_sample(c, x0, P, steps, cfg, skip_steps, mel_out);
 }
 
 int gsvcu_dit_velocity(gsvcu_dit* c, const float* x_mel, float t, int32_t negative, float* vel) {
@@ -1581,7 +1581,8 @@ int gsvcu_dit_velocity(gsvcu_dit* c, const float* x_mel, float t, int32_t negati
     return check_err(c);
 }
 
-int gsvcu_dit_sample(gsvcu_dit* c, const float* x0, int32_t P, int32_t steps, float cfg, float* mel_out) {
+int gsvcu_dit_sample(gsvcu_dit* c, const float* x0, int32_t P, int32_t steps, float cfg, int32_t skip_steps,
+                     float* mel_out) {
     if (!c || !x0 || !mel_out || steps <= 0) return GSVCU_ERR_ARG;
     if (c->T <= 0) return c->fail(GSVCU_ERR_ARG, "sample() before set_condition()");
     const int T = c->T;
@@ -1605,6 +1606,7 @@ int gsvcu_dit_sample(gsvcu_dit* c, const float* x0, int32_t P, int32_t steps, fl
     int neg_count = 0;
     const int ur = c->uncond_reuse;
     for (int j = 0; j < steps; j++) {
+        if (j < skip_steps) continue;   // the first skip_steps steps leave x as it is (src/gsv_dit.cpp:1444-1448)
         const float* tj = c->tsin + (size_t)j * TSIN;
         const bool odd = (j & 1) != 0;
         if (guided && odd && ((ur == 1 && neg_count >= 1) || (ur == 2 && neg_count >= 2))) {
@@ -1637,7 +1639,8 @@ int gsvcu_dit_sample(gsvcu_dit* c, const float* x0, int32_t P, int32_t steps, fl
 
 int gsvcu_dit_synthesize(gsvcu_dit* c, const float* fea_ref, int32_t R, const float* fea_todo, int32_t N,
                          const float* mel_ref, int32_t mel_ref_T, int32_t steps, float cfg, uint64_t seed,
-                         int32_t block_override, const float* const* x0_chunks, int32_t n_x0, float* mel_out) {
+                         int32_t block_override, const float* const* x0_chunks, int32_t n_x0, int32_t skip_steps,
+                         float* mel_out) {
     if (!c || !fea_ref || !fea_todo || !mel_ref || !mel_out || steps <= 0) return GSVCU_ERR_ARG;
     if (R <= 0 || N <= 0 || mel_ref_T <= 0) return c->fail(GSVCU_ERR_ARG, "synthesize(): bad R, N or mel_ref_T");
     // synthesize_v5_mel's framing (src/gsv_dit.cpp:1480-1581): the reference frames are the last 500 of the
@@ -1682,7 +1685,9 @@ int gsvcu_dit_synthesize(gsvcu_dit* c, const float* fea_ref, int32_t R, const fl
         cols(fea_todo, TXD, N, start, tlen, mu.data() + rf, T);
         const float* x0 = (x0_chunks && ci < n_x0) ? x0_chunks[ci] : nullptr;
         int rc;
-        if ((rc = gsvcu_dit_sample_full(c, mu.data(), prompt.data(), rf, T, steps, cfg, cseed, x0, gen.data()))) return rc;
+        if ((rc = gsvcu_dit_sample_full(c, mu.data(), prompt.data(), rf, T, steps, cfg, cseed, x0, ci == 0 ? skip_steps : 0,
+                                        gen.data())))
+            return rc;
         cseed = cseed * 6364136223846793005ull + 1442695040888963407ull;
         cols(gen.data(), MEL, tlen, 0, tlen, mel_out + start, N);
         const int keep = std::min(rf, tlen);   // roll: the chunk's last frames and their features
@@ -1692,6 +1697,16 @@ int gsvcu_dit_synthesize(gsvcu_dit* c, const float* fea_ref, int32_t R, const fl
         cols(gen.data(), MEL, tlen, tlen - keep, keep, roll_mel.data(), keep);
         cols(fea_todo, TXD, N, start + tlen - keep, keep, roll_fea.data(), keep);
     }
+    return GSVCU_OK;
+}
+
+void gsvcu_dit_time_sin(float t, float* out256) {
+    if (out256) time_sin(t, out256);
+}
+
+int gsvcu_dit_get_inv_freq(const gsvcu_dit* c, float* out32) {
+    if (!c || !out32) return GSVCU_ERR_ARG;
+    std::memcpy(out32, c->inv_freq.data(), 32 * 4);
     return GSVCU_OK;
 }
 

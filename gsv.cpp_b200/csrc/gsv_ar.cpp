@@ -9,6 +9,7 @@
 #include <string>
 #include <vector>
 
+#include "device_parse.h"
 #include "gsvcu.h"
 
 #if defined(__has_include)
@@ -20,24 +21,7 @@
 
 namespace {
 
-// Device string -> CUDA ordinal, with the meanings of gsv_device_parse (reference
-// src/gsv_device.h:19-37): "N" or "anything:N" selects GPU N, "gpu"/"cuda"/"vulkan" GPU 0. The CUDA
-// build has no CPU path, so "" also means GPU 0 and "cpu" is an error.
-bool parse_device(const std::string& d, int* idx) {
-    *idx = 0;
-    if (d == "cpu" || d == "CPU" || d == "CPUExecutionProvider") return false;
-    if (d.empty()) return true;
-    const size_t colon = d.rfind(':');
-    if (colon != std::string::npos) {
-        *idx = std::atoi(d.c_str() + colon + 1);
-        return true;
-    }
-    if (d.find_first_not_of("0123456789") == std::string::npos) {
-        *idx = std::atoi(d.c_str());
-        return true;
-    }
-    return true;
-}
+using gsvcu::parse_device;
 
 void on_progress(void* user, int32_t steps) {
     int* last = (int*)user;

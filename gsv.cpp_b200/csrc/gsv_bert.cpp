@@ -9,24 +9,12 @@
 #include <string>
 #include <vector>
 
+#include "device_parse.h"
 #include "gsvcu.h"
 
 namespace {
 
-// Device string -> CUDA ordinal with gsv_device_parse's meanings (reference src/gsv_device.h:19-37); the
-// CUDA build has no CPU path, so "" means GPU 0 and "cpu" is an error.
-bool parse_device(const std::string& d, int* idx) {
-    *idx = 0;
-    if (d == "cpu" || d == "CPU" || d == "CPUExecutionProvider") return false;
-    if (d.empty()) return true;
-    const size_t colon = d.rfind(':');
-    if (colon != std::string::npos) {
-        *idx = std::atoi(d.c_str() + colon + 1);
-        return true;
-    }
-    if (d.find_first_not_of("0123456789") == std::string::npos) *idx = std::atoi(d.c_str());
-    return true;
-}
+using gsvcu::parse_device;
 
 uint64_t hash_ids(const int32_t* ids, int T) {   // FNV-1a over the ids and T
     uint64_t h = 1469598103934665603ull;

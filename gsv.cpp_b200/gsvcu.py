@@ -119,15 +119,17 @@ SIGNATURES.update({
     "gsvcu_dit_get_hparams": ([_P, C.POINTER(DitHParams)], C.c_int),
     "gsvcu_dit_set_condition": ([_P, _P, _P, _I, _I], C.c_int),
     "gsvcu_dit_velocity": ([_P, _P, C.c_float, _I, _P], C.c_int),
-    "gsvcu_dit_sample": ([_P, _P, _I, _I, C.c_float, _P], C.c_int),
+    "gsvcu_dit_sample": ([_P, _P, _I, _I, C.c_float, _I, _P], C.c_int),
     "gsvcu_dit_op_hidden": ([_P, _P, C.c_float, _I, _P], C.c_int),
     "gsvcu_dit_stream": ([_P, C.POINTER(C.c_void_p)], C.c_int),
     "gsvcu_dit_prepare": ([_P, _P, _P, _I, _I], C.c_int),
-    "gsvcu_dit_sample_full": ([_P, _P, _P, _I, _I, _I, C.c_float, C.c_uint64, _P, _P], C.c_int),
+    "gsvcu_dit_sample_full": ([_P, _P, _P, _I, _I, _I, C.c_float, C.c_uint64, _P, _I, _P], C.c_int),
     "gsvcu_dit_op_condition": ([_P, _P], C.c_int),
     "gsvcu_dit_set_alg": ([_P, _I], C.c_int),
     "gsvcu_dit_get_alg": ([_P, C.POINTER(C.c_int32)], C.c_int),
-    "gsvcu_dit_synthesize": ([_P, _P, _I, _P, _I, _P, _I, _I, C.c_float, C.c_uint64, _I, _P, _I, _P], C.c_int),
+    "gsvcu_dit_synthesize": ([_P, _P, _I, _P, _I, _P, _I, _I, C.c_float, C.c_uint64, _I, _P, _I, _I, _P], C.c_int),
+    "gsvcu_dit_time_sin": ([C.c_float, _P], None),
+    "gsvcu_dit_get_inv_freq": ([_P, _P], C.c_int),
 })
 
 PROF_CLASSES = ["sampler", "step_prep", "qkv_gemm", "decode_attn", "out_gemm", "layernorm", "ffn1_gemm", "ffn2_gemm",
@@ -518,7 +520,7 @@ class Dit:
         self._check(self.lib.gsvcu_dit_op_condition(self.h, out.ctypes.data))
         return out
 
-    def sample_full(self, mu, prompt, steps, cfg, seed=1, x0=None) -> np.ndarray:
+    def sample_full(self, mu, prompt, steps, cfg, seed=1, x0=None, skip_steps=0) -> np.ndarray:
         """gsv_dit::sample: mu [512][T], prompt [100][P] -> mel [100][T - P] (seeded noise when x0 is None)."""
         mu = np.ascontiguousarray(mu, np.float32)
         prompt = np.ascontiguousarray(prompt, np.float32)
@@ -526,11 +528,12 @@ class Dit:
         x0p = None if x0 is None else np.ascontiguousarray(x0, np.float32)
         out = np.empty((100, T - P), np.float32)
         self._check(self.lib.gsvcu_dit_sample_full(self.h, mu.ctypes.data, prompt.ctypes.data, P, T, steps, float(cfg),
-                                                   seed, None if x0p is None else x0p.ctypes.data, out.ctypes.data))
+                                                   seed, None if x0p is None else x0p.ctypes.data, skip_steps,
+                                                   out.ctypes.data))
         self.T = T
         return out
 
-    def synthesize(self, fea_ref, fea_todo, mel_ref, steps, cfg, seed=1, block_override=0) -> np.ndarray:
+    def synthesize(self, fea_ref, fea_todo, mel_ref, steps, cfg, seed=1, block_override=0, skip_steps=0) -> np.ndarray:
         """gsv_dit::synthesize: fea_ref [512][R], fea_todo [512][N], mel_ref [100][mel_ref_T] -> mel [100][N]."""
         fea_ref = np.ascontiguousarray(fea_ref, np.float32)
         fea_todo = np.ascontiguousarray(fea_todo, np.float32)
@@ -538,7 +541,8 @@ class Dit:
         out = np.empty((100, fea_todo.shape[1]), np.float32)
         self._check(self.lib.gsvcu_dit_synthesize(self.h, fea_ref.ctypes.data, fea_ref.shape[1], fea_todo.ctypes.data,
                                                   fea_todo.shape[1], mel_ref.ctypes.data, mel_ref.shape[1], steps,
-                                                  float(cfg), seed, block_override, None, 0, out.ctypes.data))
+                                                  float(cfg), seed, block_override, None, 0, skip_steps,
+                                                  out.ctypes.data))
         return out
 
     def set_alg(self, uncond_reuse: int):
@@ -552,11 +556,11 @@ class Dit:
         self._check(self.lib.gsvcu_dit_velocity(self.h, x_mel.ctypes.data, float(t), int(bool(negative)), vel.ctypes.data))
         return vel
 
-    def sample(self, x0, P, steps, cfg) -> np.ndarray:
+    def sample(self, x0, P, steps, cfg, skip_steps=0) -> np.ndarray:
         """gsv_dit::sample's CFM loop on the set condition: x0 [100][T] -> mel [100][T - P]."""
         x0 = np.ascontiguousarray(x0, np.float32)
         out = np.empty((x0.shape[0], x0.shape[1] - P), np.float32)
-        self._check(self.lib.gsvcu_dit_sample(self.h, x0.ctypes.data, P, steps, float(cfg), out.ctypes.data))
+        self._check(self.lib.gsvcu_dit_sample(self.h, x0.ctypes.data, P, steps, float(cfg), skip_steps, out.ctypes.data))
         return out
 
     def hidden(self, x_mel, t, n_blocks) -> np.ndarray:

@@ -330,22 +330,30 @@ int gsvcu_dit_prepare(gsvcu_dit* ctx, const float* prompt_mel, const float* mu, 
 /* gsv_dit::velocity (src/gsv_dit.cpp:1325-1338): one estimator pass at time t; x_mel and vel [100][T]. */
 int gsvcu_dit_velocity(gsvcu_dit* ctx, const float* x_mel, float t, int32_t negative, float* vel);
 /* gsv_dit::sample's CFM loop (src/gsv_dit.cpp:1410-1478) on the set condition: x0 [100][T] the initial
- * noise, the first P frames zeroed, `steps` Euler steps t = j / steps, guidance v + (v - v_neg) * cfg when
- * cfg > 1e-5 (both branches in one batch); mel_out [100][T - P]. */
-int gsvcu_dit_sample(gsvcu_dit* ctx, const float* x0, int32_t P, int32_t steps, float cfg, float* mel_out);
+ * noise, the first P frames zeroed, `steps` Euler steps t = j / steps of which the first skip_steps leave x
+ * unchanged, guidance v + (v - v_neg) * cfg when cfg > 1e-5 (both branches in one batch); mel_out
+ * [100][T - P]. */
+int gsvcu_dit_sample(gsvcu_dit* ctx, const float* x0, int32_t P, int32_t steps, float cfg, int32_t skip_steps,
+                     float* mel_out);
 /* gsv_dit::sample (src/gsv_dit.cpp:1410-1478) in full: prompt [100][P] into the first P of T frames, prepare
  * with mu [512][T], initial noise x0 [100][T] or, when x0 is null, randn * 0.875 from gsv_rng(seed) as the
  * reference draws it; mel_out [100][T - P]. */
 int gsvcu_dit_sample_full(gsvcu_dit* ctx, const float* mu, const float* prompt, int32_t P, int32_t T, int32_t steps,
-                          float cfg, uint64_t seed, const float* x0, float* mel_out);
+                          float cfg, uint64_t seed, const float* x0, int32_t skip_steps, float* mel_out);
 /* gsv_dit::synthesize (src/gsv_dit.cpp:1480-1581): the reference frames (the last 500 of min(mel_ref_T, R))
  * of mel_ref [100][mel_ref_T] and fea_ref [512][R] as prompt, fea_todo [512][N] cut into chunks of 640 frames
  * (block_override > 0: that many; reference + chunk <= 1000), each chunk after the first prompted with the
  * reference frames whose last 32 are the previous chunk's last generated frames; chunk i samples with seed
- * LCG^i(seed) and, when i < n_x0, initial noise x0_chunks[i] ([100][reference + chunk]); mel_out [100][N]. */
+ * LCG^i(seed) and, when i < n_x0, initial noise x0_chunks[i] ([100][reference + chunk]); skip_steps applies to
+ * the first chunk; mel_out [100][N]. */
 int gsvcu_dit_synthesize(gsvcu_dit* ctx, const float* fea_ref, int32_t R, const float* fea_todo, int32_t N,
                          const float* mel_ref, int32_t mel_ref_T, int32_t steps, float cfg, uint64_t seed,
-                         int32_t block_override, const float* const* x0_chunks, int32_t n_x0, float* mel_out);
+                         int32_t block_override, const float* const* x0_chunks, int32_t n_x0, int32_t skip_steps,
+                         float* mel_out);
+/* gsv_dit::time_sin (src/gsv_dit.cpp:755-769): SinusPositionEmbedding(256) of t, host only. */
+void gsvcu_dit_time_sin(float t, float* out256);
+/* The checkpoint's RoPE inverse frequencies [32] (gsv_dit::debug_tables' angles are n * inv_freq[i]). */
+int gsvcu_dit_get_inv_freq(const gsvcu_dit* ctx, float* out32);
 /* gsv_dit::set_alg / alg (src/gsv_dit.h:46-49, the loop src/gsv_dit.cpp:1449-1468): uncond_reuse 0 computes
  * the negative branch every guided step; 1 reuses the last computed one on odd steps; 2 extrapolates
  * 2 neg[k-1] - neg[k-2] on odd steps (once two exist). Values outside 0..2 mean 0. */

@@ -182,7 +182,7 @@ def branch(W, x_mel: np.ndarray, t: float, cond: np.ndarray, x_lens: int, n_bloc
 
 
 def sample(W, x0: np.ndarray, cond: np.ndarray, neg: np.ndarray, P: int, steps: int, cfg: float,
-           uncond_reuse: int = 0) -> np.ndarray:
+           uncond_reuse: int = 0, skip_steps: int = 0) -> np.ndarray:
     """The CFM Euler loop on set conditions: x0 [100][T] -> mel [100][T - P]; uncond_reuse as the reference's
     alg (src/gsv_dit.cpp:1449-1468): 1 reuses the last computed negative velocity on odd steps, 2
     extrapolates 2 neg[k-1] - neg[k-2]."""
@@ -193,6 +193,8 @@ def sample(W, x0: np.ndarray, cond: np.ndarray, neg: np.ndarray, P: int, steps: 
     p1 = p2 = None
     count = 0
     for j in range(steps):
+        if j < skip_steps:   # src/gsv_dit.cpp:1444-1448: no model call, x unchanged
+            continue
         t = float(np.float32(j) * dt)
         vel = branch(W, x, t, cond, T)
         if cfg > 1e-5:
@@ -286,7 +288,7 @@ def noise(seed: int, n: int) -> np.ndarray:
     return out
 
 
-def sample_full(W, mu, prompt, P, steps, cfg, seed, x0=None):
+def sample_full(W, mu, prompt, P, steps, cfg, seed, x0=None, skip_steps=0):
     """gsv_dit::sample: mu [512][T], prompt [100][P] -> mel [100][T - P]."""
     T = mu.shape[1]
     prompt_x = np.zeros((100, T), np.float32)
@@ -294,10 +296,10 @@ def sample_full(W, mu, prompt, P, steps, cfg, seed, x0=None):
     cond, neg = prepare(W, prompt_x, mu)
     if x0 is None:
         x0 = noise(seed, 100 * T).reshape(100, T)
-    return sample(W, x0, cond, neg, P, steps, cfg)
+    return sample(W, x0, cond, neg, P, steps, cfg, skip_steps=skip_steps)
 
 
-def synthesize(W, fea_ref, fea_todo, mel_ref, steps, cfg, seed, block_override=0):
+def synthesize(W, fea_ref, fea_todo, mel_ref, steps, cfg, seed, block_override=0, skip_steps=0):
     """gsv_dit::synthesize (src/gsv_dit.cpp:1480-1581): chunked sampling with a rolling prompt -> mel [100][N]."""
     REF, TAIL, TOTAL, MAXCHUNK = 500, 32, 1000, 640
     R, N, MT = fea_ref.shape[1], fea_todo.shape[1], mel_ref.shape[1]
@@ -319,7 +321,7 @@ def synthesize(W, fea_ref, fea_todo, mel_ref, steps, cfg, seed, block_override=0
             prompt = np.concatenate([mel_s[:, :rf - tail], roll_mel[:, roll_mel.shape[1] - tail:]], axis=1)
             feat = np.concatenate([fea_s[:, :rf - tail], roll_fea[:, roll_fea.shape[1] - tail:]], axis=1)
         mu = np.concatenate([feat, fea_todo[:, start:start + tlen]], axis=1).astype(np.float32)
-        gen = sample_full(W, mu, prompt, rf, steps, cfg, cseed)
+        gen = sample_full(W, mu, prompt, rf, steps, cfg, cseed, skip_steps=skip_steps if start == 0 else 0)
         cseed = (cseed * 6364136223846793005 + 1442695040888963407) % 2 ** 64
         out[:, start:start + tlen] = gen
         keep = min(rf, tlen)

@@ -191,3 +191,53 @@ def test_dit_uncond_reuse_matches_oracle(dit_small, ur):
     print(f"uncond_reuse={ur}: rel_l2 {e:.2e} (vs no reuse {rel_l2(ref, full):.2e})")
     assert e <= TOL and rel_l2(ref, full) > 10 * e   # the reuse changes the result far more than the GPU error
     d.close()
+
+
+def test_cpp_dropin_dit_class(dit_small, tmp_path):
+    """The C++ `class gsv_dit` shim (include/gsv_dit.h, csrc/gsv_dit.cpp) as the reference's callers use it:
+    prepare + velocity, sample (seeded, skip_steps, uncond_reuse), synthesize, time_sin, debug_tables; its
+    outputs equal the C ABI's through the Python binding, and skip_steps follows the restatement."""
+    import json
+    import os
+    import subprocess
+    import gsvcu
+    path, W = dit_small
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    exe = os.path.join(root, "tests", "cpp", "bin", "gsv_dit_smoke")
+    assert os.path.exists(exe), "build with `make -C tests/cpp`"
+    rng = np.random.default_rng(41)
+    T, P, R, N, MT = 110, 30, 60, 85, 50
+    arr = {k: rng.standard_normal(s).astype(np.float32) for k, s in (
+        ("mu", (512, T)), ("prompt", (100, P)), ("x", (100, T)), ("fea_ref", (512, R)), ("fea_todo", (512, N)),
+        ("mel_ref", (100, MT)))}
+    f = tmp_path / "in.bin"
+    with open(f, "wb") as fh:
+        fh.write(np.array([T, P, R, N, MT], np.int32).tobytes())
+        for k in ("mu", "prompt", "x", "fea_ref", "fea_todo", "mel_ref"):
+            fh.write(arr[k].tobytes())
+    out = subprocess.run([exe, path, str(f)], capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0, out.stderr
+    lines = [json.loads(x) for x in out.stdout.strip().splitlines()]
+    assert (lines[0]["mel_dim"], lines[0]["dim"], lines[0]["depth"]) == (100, 1024, 2)
+    w = lambda a: float((a.ravel().astype(np.float64) * ((np.arange(a.size) % 7) + 1)).sum())
+    d = gsvcu.Dit(path)
+    px = np.zeros((100, T), np.float32)
+    px[:, :P] = arr["prompt"]
+    d.prepare(px, arr["mu"])
+    assert (lines[1]["cur_T"], lines[1]["cur_P"]) == (T, P)
+    np.testing.assert_allclose(lines[1]["vel"], w(d.velocity(arr["x"], 0.3, False)), rtol=1e-9)
+    np.testing.assert_allclose(lines[1]["vel_neg"], w(d.velocity(arr["x"], 0.3, True)), rtol=1e-9)
+    mel = d.sample_full(arr["mu"], arr["prompt"], 3, 1.3, seed=5, skip_steps=1)
+    np.testing.assert_allclose(lines[2]["sample"], w(mel), rtol=1e-9)
+    assert rel_l2(mel, O.sample_full(W, arr["mu"], arr["prompt"], P, 3, 1.3, 5, skip_steps=1)) <= TOL
+    d.set_alg(1)
+    np.testing.assert_allclose(lines[2]["sample_reuse"], w(d.sample_full(arr["mu"], arr["prompt"], 3, 1.3, seed=5)),
+                               rtol=1e-9)
+    assert lines[2]["alg"] == 1
+    d.set_alg(0)
+    syn = d.synthesize(arr["fea_ref"], arr["fea_todo"], arr["mel_ref"], 2, 1.3, seed=9, block_override=40)
+    np.testing.assert_allclose(lines[3]["synth"], w(syn), rtol=1e-9)
+    np.testing.assert_allclose(lines[3]["time_sin"], w(O.time_sin(0.25)), rtol=1e-5)
+    assert lines[3]["tables"] == 32 * T and lines[3]["dbcache_fn"] == 8 and lines[3]["hits"] == 0
+    assert lines[3]["debug_read"] == 0
+    d.close()
