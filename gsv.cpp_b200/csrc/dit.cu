@@ -848,6 +848,63 @@ __global__ void __launch_bounds__(256) k_dit_pack_ctx(const float* __restrict__ 
     }
 }
 
+// ------------------------------------------------------------------ cache-dit (DBCache)
+constexpr int FD_BLOCKS = 296;   // partial sums of the residual-difference criterion
+
+// The front residual of branch b as the reference's criterion reads it (src/gsv_dit.cpp:1157-1163):
+// r = x_front - x_trunk, then with ds > 1 the view ne {1024, T / ds} with a row stride of ds floats over r's
+// flat [T][1024] storage, i.e. r_cur[t'][i] = r_flat[t' ds + i]. Writes r_cur and per-block partial sums of
+// |r_cur - r_prev| and |r_prev| (double).
+__global__ void __launch_bounds__(256) k_dit_fd_partial(const float* __restrict__ xf, const float* __restrict__ xt,
+                                                        const float* __restrict__ r_prev, int n, int ds,
+                                                        float* __restrict__ r_cur, double* __restrict__ part) {
+    __shared__ double sa[8], sb[8];
+    griddep_wait();
+    griddep_launch();
+    double a = 0.0, bsum = 0.0;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const size_t src = ds > 1 ? (size_t)(i / DM) * ds + (i % DM) : (size_t)i;
+        const float r = xf[src] - xt[src];
+        r_cur[i] = r;
+        const float rp = r_prev[i];
+        a += fabsf(r - rp);
+        bsum += fabsf(rp);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        a += __shfl_xor_sync(0xffffffffu, a, off);
+        bsum += __shfl_xor_sync(0xffffffffu, bsum, off);
+    }
+    if ((threadIdx.x & 31) == 0) { sa[threadIdx.x >> 5] = a; sb[threadIdx.x >> 5] = bsum; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double x = 0.0, y = 0.0;
+        for (int w = 0; w < 8; w++) { x += sa[w]; y += sb[w]; }
+        part[2 * blockIdx.x] = x;
+        part[2 * blockIdx.x + 1] = y;
+    }
+}
+
+// fd = sum |r_cur - r_prev| / (sum |r_prev| + 1e-6), the partial sums added in block order.
+__global__ void __launch_bounds__(32) k_dit_fd_final(const double* __restrict__ part, int nblk, float* __restrict__ fd) {
+    griddep_wait();
+    griddep_launch();
+    if (threadIdx.x == 0) {
+        double x = 0.0, y = 0.0;
+        for (int i = 0; i < nblk; i++) { x += part[2 * i]; y += part[2 * i + 1]; }
+        *fd = (float)x / ((float)y + 1e-6f);
+    }
+}
+
+// dst = a + s * b over n floats (s = +1 or -1).
+__global__ void __launch_bounds__(256) k_dit_axpy(const float* __restrict__ a, const float* __restrict__ b, float sgn,
+                                                  size_t n, float* __restrict__ dst) {
+    griddep_wait();
+    griddep_launch();
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        dst[i] = a[i] + sgn * b[i];
+}
+
 // ------------------------------------------------------------------ host side
 bool map_2d(CUtensorMap* m, const __half* base, uint64_t rows, uint64_t K, uint32_t box_rows) {
     EncodeTiledFn enc = encode_fn();
@@ -1018,6 +1075,21 @@ struct gsvcu_dit {
     float *vout = nullptr;        // [100][T]
     float *neg1 = nullptr, *neg2 = nullptr;   // [T][128]: the last two computed unconditional velocities
     int uncond_reuse = 0;         // gsv_dit_alg::uncond_reuse (0, 1 or 2)
+    // cache-dit (DBCache, src/gsv_dit.cpp:1124-1323): settings, per-branch gates and device state
+    struct DbCfg {
+        int fn = 0, warmup = 8, warmup_interval = 1, max_cached = -1, max_cont = -1, ds = 4;
+        float thr = 0.08f, max_accum = 0.0f;
+    } dbc;
+    struct DbBranch {
+        int cached_steps = 0, cont = 0, hits = 0, misses = 0;
+        bool valid = false;
+        float acc = 0.0f, last_fd = 0.0f;
+    } dbb[2];
+    int db_step = 0;
+    float *xtrunk = nullptr, *xfront = nullptr, *rcur = nullptr;   // [T][1024]
+    float *rprev[2] = {nullptr, nullptr}, *mrprev[2] = {nullptr, nullptr};   // [T][1024] per branch
+    double* fdpart = nullptr;     // [FD_BLOCKS][2]
+    float* fd_dev = nullptr;      // [1]
     float *mu_d = nullptr, *px_d = nullptr;   // prepare inputs [512][T], [100][T]
     float *txf = nullptr;         // [T][512] text path (f32)
     __half *tx16 = nullptr;       // [T][512] ConvNeXt operand
@@ -1055,7 +1127,13 @@ struct gsvcu_dit {
     }
     int reserve(int T_, int rows);
     int prepare_dev(const float* prompt_x, const float* mu);
-    int forward(int B, int negative, const float* tsin_dev, int n_blocks, bool head);
+    int forward(int B, int negative, const float* tsin_dev, int l0, int l1, bool trunk, bool head,
+                float* save_trunk = nullptr);
+    int velocity_cached(int bi, const float* tsin_dev);
+    void db_reset_state() {
+        for (DbBranch& d : dbb) d = DbBranch();
+        db_step = 0;
+    }
 };
 
 namespace {
@@ -1099,7 +1177,10 @@ int gsvcu_dit::reserve(int T_, int rows) {
                       {(void**)&mu_d, TXD * TT * 4}, {(void**)&px_d, MEL * TT * 4}, {(void**)&txf, TT * TXD * 4},
                       {(void**)&tx16, TT * TXD * 2}, {(void**)&hb, TT * TXI * 4}, {(void**)&gx, TXI * 4},
                       {(void**)&ctx16, 2 * TT * CTXK * 2}, {(void**)&neg1, TT * MELP * 4},
-                      {(void**)&neg2, TT * MELP * 4}};
+                      {(void**)&neg2, TT * MELP * 4}, {(void**)&xtrunk, TT * DM * 4}, {(void**)&xfront, TT * DM * 4},
+                      {(void**)&rcur, TT * DM * 4}, {(void**)&rprev[0], TT * DM * 4}, {(void**)&rprev[1], TT * DM * 4},
+                      {(void**)&mrprev[0], TT * DM * 4}, {(void**)&mrprev[1], TT * DM * 4},
+                      {(void**)&fdpart, FD_BLOCKS * 16}, {(void**)&fd_dev, 16}};
     for (const A& a : list) {
         if (cudaMalloc(a.p, a.bytes) != cudaSuccess) {
             cudaGetLastError();
@@ -1109,6 +1190,9 @@ int gsvcu_dit::reserve(int T_, int rows) {
     }
     // rows past R of the padded operands stay zero (the GEMMs' A tiles read them)
     cudaMemsetAsync(mel16, 0, R * MELP * 2, stream);
+    // cache-dit's previous front residuals start at zero with new buffers (src/gsv_dit.cpp:1147-1149)
+    cudaMemsetAsync(rprev[0], 0, TT * DM * 4, stream);
+    cudaMemsetAsync(rprev[1], 0, TT * DM * 4, stream);
     cap_rows = rows;
     T = T_;
     tp = (T_ + 7) & ~7;
@@ -1150,14 +1234,75 @@ int gsvcu_dit::prepare_dev(const float* prompt_x, const float* mu) {
     return GSVCU_OK;
 }
 
+// One cache-dit step of branch bi (src/gsv_dit.cpp:1250-1323): the front (trunk + the first fn blocks), the
+// criterion fd of its residual against the last computed one, the host-side gates (warmup, threshold,
+// max_cached, max_cont, max_accum); on a hit the middle blocks are replaced by the residual they added at
+// the last miss, on a miss they run and their residual and the front residual are kept. The velocity goes to
+// rows [0, T) of vel.
+int gsvcu_dit::velocity_cached(int bi, const float* tsin_dev) {
+    cudaStream_t s = stream;
+    const int depth = hp.depth, fn = dbc.fn;
+    DbBranch& d = dbb[bi];
+    int rc;
+    if ((rc = forward(1, bi, tsin_dev, 0, fn, true, false, xtrunk))) return rc;
+    const int ds = (dbc.ds >= 1 && T % dbc.ds == 0) ? dbc.ds : 1;
+    const int n = (T / ds) * DM;
+    launch_pdl(k_dit_fd_partial, dim3(FD_BLOCKS), dim3(256), 0, s, (const float*)x, (const float*)xtrunk,
+               (const float*)rprev[bi], n, ds, rcur, fdpart);
+    launch_pdl(k_dit_fd_final, dim3(1), dim3(32), 0, s, (const double*)fdpart, FD_BLOCKS, fd_dev);
+    float fd = 0.0f;
+    if (cudaMemcpyAsync(&fd, fd_dev, 4, cudaMemcpyDeviceToHost, s) != cudaSuccess || cudaStreamSynchronize(s) != cudaSuccess)
+        return fail(GSVCU_ERR_CUDA, std::string("criterion read failed: ") + cudaGetErrorString(cudaGetLastError()));
+    d.last_fd = fd;
+    bool hit = false;
+    const int iv = dbc.warmup_interval < 1 ? 1 : dbc.warmup_interval;
+    const bool warm = db_step < dbc.warmup && (db_step % iv) == 0;
+    if (d.valid && dbc.thr > 0.0f && !warm) {
+        bool ok = fd < dbc.thr;
+        if (ok && dbc.max_cached >= 0 && d.cached_steps >= dbc.max_cached) ok = false;
+        if (ok && dbc.max_cont >= 0 && d.cont >= dbc.max_cont) {
+            ok = false;
+            d.cont = 0;
+        }
+        if (ok && dbc.max_accum > 0.0f && d.acc >= dbc.max_accum) ok = false;
+        hit = ok;
+    }
+    if (fd > 0.0f) d.acc += fd;
+    const size_t nx = (size_t)T * DM;
+    const unsigned gx = (unsigned)std::min<size_t>(4096, (nx + 255) / 256);
+    if (hit) {   // x_mid = x_front + the middle residual of the last miss
+        launch_pdl(k_dit_axpy, dim3(gx), dim3(256), 0, s, (const float*)x, (const float*)mrprev[bi], 1.0f, nx, x);
+        if ((rc = forward(1, bi, tsin_dev, depth, depth, false, true))) return rc;
+        d.hits++;
+        d.cached_steps++;
+        d.cont++;
+    } else {
+        if (cudaMemcpyAsync(xfront, x, nx * 4, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+            return fail(GSVCU_ERR_CUDA, "front copy failed");
+        if ((rc = forward(1, bi, tsin_dev, fn, depth, false, true))) return rc;
+        launch_pdl(k_dit_axpy, dim3(gx), dim3(256), 0, s, (const float*)x, (const float*)xfront, -1.0f, nx, mrprev[bi]);
+        if (cudaMemcpyAsync(rprev[bi], rcur, (size_t)n * 4, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+            return fail(GSVCU_ERR_CUDA, "residual copy failed");
+        d.misses++;
+        d.valid = true;
+        d.cont = 0;
+    }
+    return GSVCU_OK;
+}
+
 // One estimator pass over B branches (B = 2: rows [0, T) use the condition, [T, 2T) the negative one;
-// B = 1: the condition selected by `negative`) from xmel and the time features at tsin_dev: the trunk,
-// n_blocks DiT blocks and, with `head`, the output projection into vel ([R][128]).
-int gsvcu_dit::forward(int B, int negative, const float* tsin_dev, int n_blocks, bool head) {
+// B = 1: the condition selected by `negative`) from xmel and the time features at tsin_dev: with `trunk`
+// the time embedding, AdaLN modulations and the trunk (a copy of its output into save_trunk when given),
+// then DiT blocks [l0, l1) on x, and with `head` the output projection into vel ([R][128]).
+int gsvcu_dit::forward(int B, int negative, const float* tsin_dev, int l0, int l1, bool trunk, bool head,
+                       float* save_trunk) {
     const int R = B * T;
     cudaStream_t s = stream;
     const int depth = hp.depth;
     auto gemv_blocks = [](int n) { return dim3((unsigned)((n + 7) / 8)); };
+    DitGemmArgs a{};
+    a.R = R; a.T = T; a.x_lens = x_lens; a.err = errw;
+    if (trunk) {
     // time embedding, then every block's AdaLN modulation and norm_out's in one launch
     launch_pdl(k_dit_gemv<false, true>, gemv_blocks(DM), dim3(256), 0, s, (const __half*)w_t0, (const float*)b_t0,
                tsin_dev, DM, TSIN, th);
@@ -1169,8 +1314,6 @@ int gsvcu_dit::forward(int B, int negative, const float* tsin_dev, int n_blocks,
     // trunk
     launch_pdl(k_dit_pack_mel, dim3(std::min(1024, (R * MELP + 255) / 256)), dim3(256), 0, s, (const float*)xmel, T, B,
                mel16);
-    DitGemmArgs a{};
-    a.R = R; a.T = T; a.x_lens = x_lens; a.err = errw;
     {
         DitGemmArgs g = a;
         g.N = DM; g.K = MELP; g.out32 = x; g.ld = DM;
@@ -1186,8 +1329,11 @@ int gsvcu_dit::forward(int B, int negative, const float* tsin_dev, int n_blocks,
         g.bias = b_c2; g.out16 = nullptr; g.out32 = x; g.use_mask = 1;
         if (!conv(DE_RESID, c16, w_c2, B, g, s)) return fail(GSVCU_ERR_CUDA, "tensor map encoding failed");
     }
+    if (save_trunk && cudaMemcpyAsync(save_trunk, x, (size_t)R * DM * 4, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+        return fail(GSVCU_ERR_CUDA, "trunk copy failed");
+    }   // trunk
     const dim3 rows8((unsigned)((R + 7) / 8));
-    for (int li = 0; li < n_blocks; li++) {
+    for (int li = l0; li < l1; li++) {
         const Block& w = L[(size_t)li];
         const float* m = ada + (size_t)li * ADA;   // shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp
         launch_pdl(k_dit_lnmod, rows8, dim3(256), 0, s, (const float*)x, R, m, m + DM, a16);
@@ -1573,7 +1719,11 @@ int gsvcu_dit_velocity(gsvcu_dit* c, const float* x_mel, float t, int32_t negati
     if ((rc = upload_tsin(c, ts))) return rc;
     if (cudaMemcpyAsync(c->xmel, x_mel, (size_t)MEL * c->T * 4, cudaMemcpyHostToDevice, c->stream) != cudaSuccess)
         return c->fail(GSVCU_ERR_CUDA, "input upload failed");
-    if ((rc = c->forward(1, negative, c->tsin, c->hp.depth, true))) return rc;
+    if (c->dbc.fn > 0 && c->dbc.fn < c->hp.depth) {   // cache-dit path (src/gsv_dit.cpp:1325-1333)
+        if ((rc = c->velocity_cached(negative ? 1 : 0, c->tsin))) return rc;
+    } else if ((rc = c->forward(1, negative, c->tsin, 0, c->hp.depth, true, true))) {
+        return rc;
+    }
     launch_pdl(k_dit_vel_out, dim3((unsigned)std::min(1024, (MEL * c->T + 255) / 256)), dim3(256), 0, c->stream,
                (const float*)c->vel, c->T, c->vout);
     if (cudaMemcpyAsync(vel, c->vout, (size_t)MEL * c->T * 4, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess)
@@ -1601,32 +1751,45 @@ int gsvcu_dit_sample(gsvcu_dit* c, const float* x0, int32_t P, int32_t steps, fl
     // x[:, :P] = 0 before the first step (src/gsv_dit.cpp:1440-1441)
     launch_pdl(k_dit_euler, eg, dim3(256), 0, c->stream, (const float*)c->vel, T, 0, none, none, 0.0f, 0.0f, P, c->xmel);
     // uncond_reuse (src/gsv_dit.cpp:1449-1468): odd steps take the last computed unconditional velocity (1) or
-    // extrapolate the last two (2) instead of running the negative branch
+    // extrapolate the last two (2) instead of running the negative branch. With cache-dit each branch runs
+    // alone through its gates (the unconditional velocity goes to rows [T, 2T) of vel).
     float *p1 = c->neg1, *p2 = c->neg2;
     int neg_count = 0;
     const int ur = c->uncond_reuse;
+    const bool cached = c->dbc.fn > 0 && c->dbc.fn < c->hp.depth;
+    if (cached) c->db_reset_state();   // a new inference (src/gsv_dit.cpp:1427)
+    float* vneg = c->vel + (size_t)T * MELP;
     for (int j = 0; j < steps; j++) {
+        c->db_step = j;
         if (j < skip_steps) continue;   // the first skip_steps steps leave x as it is (src/gsv_dit.cpp:1444-1448)
         const float* tj = c->tsin + (size_t)j * TSIN;
         const bool odd = (j & 1) != 0;
-        if (guided && odd && ((ur == 1 && neg_count >= 1) || (ur == 2 && neg_count >= 2))) {
-            if ((rc = c->forward(1, 0, tj, c->hp.depth, true))) return rc;
-            launch_pdl(k_dit_euler, eg, dim3(256), 0, c->stream, (const float*)c->vel, T, 1, (const float*)p1,
-                       ur == 2 ? (const float*)p2 : none, cfg, dt, P, c->xmel);
-        } else if (guided) {
-            if ((rc = c->forward(2, 0, tj, c->hp.depth, true))) return rc;
-            const float* vneg = c->vel + (size_t)T * MELP;
+        const bool reuse = guided && odd && ((ur == 1 && neg_count >= 1) || (ur == 2 && neg_count >= 2));
+        if (guided && !reuse) {   // both velocities
+            if (cached) {
+                if ((rc = c->velocity_cached(1, tj))) return rc;
+                if (cudaMemcpyAsync(vneg, c->vel, (size_t)T * MELP * 4, cudaMemcpyDeviceToDevice, c->stream) != cudaSuccess)
+                    return c->fail(GSVCU_ERR_CUDA, "velocity copy failed");
+                if ((rc = c->velocity_cached(0, tj))) return rc;
+            } else if ((rc = c->forward(2, 0, tj, 0, c->hp.depth, true, true))) {
+                return rc;
+            }
             if (ur) {   // keep the last two computed unconditional velocities
                 std::swap(p1, p2);
                 if (cudaMemcpyAsync(p1, vneg, (size_t)T * MELP * 4, cudaMemcpyDeviceToDevice, c->stream) != cudaSuccess)
                     return c->fail(GSVCU_ERR_CUDA, "velocity copy failed");
             }
             neg_count++;
-            launch_pdl(k_dit_euler, eg, dim3(256), 0, c->stream, (const float*)c->vel, T, 1, vneg, none, cfg, dt, P,
-                       c->xmel);
-        } else {
-            if ((rc = c->forward(1, 0, tj, c->hp.depth, true))) return rc;
-            launch_pdl(k_dit_euler, eg, dim3(256), 0, c->stream, (const float*)c->vel, T, 1, none, none, cfg, dt, P,
+            launch_pdl(k_dit_euler, eg, dim3(256), 0, c->stream, (const float*)c->vel, T, 1, (const float*)vneg, none, cfg,
+                       dt, P, c->xmel);
+        } else {   // the conditional velocity only (unguided, or the unconditional one reused)
+            if (cached) {
+                if ((rc = c->velocity_cached(0, tj))) return rc;
+            } else if ((rc = c->forward(1, 0, tj, 0, c->hp.depth, true, true))) {
+                return rc;
+            }
+            launch_pdl(k_dit_euler, eg, dim3(256), 0, c->stream, (const float*)c->vel, T, 1,
+                       reuse ? (const float*)p1 : none, (reuse && ur == 2) ? (const float*)p2 : none, cfg, dt, P,
                        c->xmel);
         }
     }
@@ -1710,6 +1873,51 @@ int gsvcu_dit_get_inv_freq(const gsvcu_dit* c, float* out32) {
     return GSVCU_OK;
 }
 
+int gsvcu_dit_set_dbcache(gsvcu_dit* c, int32_t fn, float threshold, int32_t warmup, int32_t warmup_interval,
+                          int32_t max_cached, int32_t max_cont, float max_accum, int32_t downsample) {
+    if (!c) return GSVCU_ERR_ARG;
+    const int nfn = fn > 0 ? fn : 0, nds = downsample >= 1 ? downsample : 1;
+    const bool structural = nfn != c->dbc.fn || nds != c->dbc.ds;
+    c->dbc.fn = nfn;
+    c->dbc.thr = threshold;
+    c->dbc.warmup = warmup;
+    c->dbc.warmup_interval = warmup_interval;
+    c->dbc.max_cached = max_cached;
+    c->dbc.max_cont = max_cont;
+    c->dbc.max_accum = max_accum;
+    c->dbc.ds = nds;
+    if (structural) {   // new cache state: gates reset, previous residuals zero (src/gsv_dit.cpp:1097-1149)
+        c->db_reset_state();
+        if (c->T > 0) {
+            DevGuard dg(c->device);
+            for (int b = 0; b < 2; b++)
+                if (cudaMemsetAsync(c->rprev[b], 0, (size_t)c->T * DM * 4, c->stream) != cudaSuccess)
+                    return c->fail(GSVCU_ERR_CUDA, "cache reset failed");
+            if (cudaStreamSynchronize(c->stream) != cudaSuccess) return c->fail(GSVCU_ERR_CUDA, "cache reset failed");
+        }
+    }
+    return GSVCU_OK;
+}
+
+int gsvcu_dit_db_set_step(gsvcu_dit* c, int32_t step) {
+    if (!c) return GSVCU_ERR_ARG;
+    c->db_step = step;
+    return GSVCU_OK;
+}
+
+int gsvcu_dit_db_get_stats(const gsvcu_dit* c, int32_t* steps, int32_t* hits2, int32_t* misses2, float* last_fd2,
+                           float* acc2) {
+    if (!c || !steps || !hits2 || !misses2 || !last_fd2 || !acc2) return GSVCU_ERR_ARG;
+    *steps = c->db_step;
+    for (int b = 0; b < 2; b++) {
+        hits2[b] = c->dbb[b].hits;
+        misses2[b] = c->dbb[b].misses;
+        last_fd2[b] = c->dbb[b].last_fd;
+        acc2[b] = c->dbb[b].acc;
+    }
+    return GSVCU_OK;
+}
+
 int gsvcu_dit_set_alg(gsvcu_dit* c, int32_t uncond_reuse) {
     if (!c) return GSVCU_ERR_ARG;
     c->uncond_reuse = (uncond_reuse < 0 || uncond_reuse > 2) ? 0 : uncond_reuse;
@@ -1733,7 +1941,7 @@ int gsvcu_dit_op_hidden(gsvcu_dit* c, const float* x_mel, float t, int32_t n_blo
     if ((rc = upload_tsin(c, ts))) return rc;
     if (cudaMemcpyAsync(c->xmel, x_mel, (size_t)MEL * c->T * 4, cudaMemcpyHostToDevice, c->stream) != cudaSuccess)
         return c->fail(GSVCU_ERR_CUDA, "input upload failed");
-    if ((rc = c->forward(2, 0, c->tsin, n_blocks, false))) return rc;
+    if ((rc = c->forward(2, 0, c->tsin, 0, n_blocks, true, false))) return rc;
     if (cudaMemcpyAsync(hidden, c->x, (size_t)2 * c->T * DM * 4, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess)
         return c->fail(GSVCU_ERR_CUDA, std::string("output read failed: ") + cudaGetErrorString(cudaGetLastError()));
     return check_err(c);

@@ -15,9 +15,9 @@ struct gsv_dit::impl {
     gsvcu_dit* ctx = nullptr;
     gsvcu_dit_hparams hp{};
     bool verbose = false;
-    int db_fn = 0, db_warmup = 8, db_ds = 4, db_step = 0;
-    float db_thr = 0.08f;
-    bool db_warned = false;
+    // cache-dit settings (gsv_dit_cfg::dbcache_*), passed to the library whole on every change
+    int db_fn = 0, db_warmup = 8, db_iv = 1, db_max_cached = -1, db_max_cont = -1, db_ds = 4;
+    float db_thr = 0.08f, db_max_accum = 0.0f;
     std::vector<float> inv_freq;   // [32]
 
     bool ok(int rc, const char* what) {
@@ -25,11 +25,8 @@ struct gsv_dit::impl {
         std::fprintf(stderr, "[gsv_dit] %s: %s\n", what, gsvcu_dit_last_error(ctx));
         return false;
     }
-    void note_dbcache() {
-        if (db_fn > 0 && !db_warned) {
-            std::fprintf(stderr, "[gsv_dit] cache-dit is not implemented in the CUDA build: every block is computed\n");
-            db_warned = true;
-        }
+    void push_dbcache() {
+        gsvcu_dit_set_dbcache(ctx, db_fn, db_thr, db_warmup, db_iv, db_max_cached, db_max_cont, db_max_accum, db_ds);
     }
 };
 
@@ -57,11 +54,15 @@ gsv_dit* gsv_dit::load(const std::string& gguf_path, const gsv_dit_cfg& cfg) {
     s.db_fn = cfg.dbcache_fn > 0 ? cfg.dbcache_fn : 0;
     s.db_thr = cfg.dbcache_threshold;
     s.db_warmup = cfg.dbcache_warmup;
+    s.db_iv = cfg.dbcache_warmup_interval;
+    s.db_max_cached = cfg.dbcache_max_cached;
+    s.db_max_cont = cfg.dbcache_max_cont;
+    s.db_max_accum = cfg.dbcache_max_accum;
     s.db_ds = cfg.dbcache_downsample >= 1 ? cfg.dbcache_downsample : 1;
+    s.push_dbcache();
     s.inv_freq.assign(32, 0.0f);
     gsvcu_dit_get_inv_freq(s.ctx, s.inv_freq.data());
     gsvcu_dit_set_alg(s.ctx, cfg.alg_uncond_reuse);
-    s.note_dbcache();
     if (s.verbose)
         std::printf("[gsv_dit] loaded %s on GPU %d: dim %d, depth %d\n", gguf_path.c_str(), dev, s.hp.dim, s.hp.depth);
     return m;
@@ -88,7 +89,6 @@ bool gsv_dit::velocity(const float* x_mel, float t, bool negative, float* vel) {
 bool gsv_dit::sample(const float* mu, const float* prompt, int P, int T, int steps, float cfg, uint64_t seed,
                      const float* x0, std::vector<float>& mel_out, int skip_steps) {
     if (T <= 0 || steps <= 0 || P <= 0 || P >= T) return false;
-    p->note_dbcache();
     mel_out.resize((size_t)p->hp.mel_dim * (T - P));
     if (!p->ok(gsvcu_dit_sample_full(p->ctx, mu, prompt, P, T, steps, cfg, seed, x0, skip_steps, mel_out.data()),
                "sample"))
@@ -102,7 +102,6 @@ bool gsv_dit::synthesize(const float* fea_ref, int R, const float* fea_todo, int
                          int mel_ref_T, int steps, float cfg, uint64_t seed, int block_override,
                          const std::vector<const float*>* x0_chunks, std::vector<float>& mel_out, int skip_steps) {
     if (R <= 0 || N <= 0) return false;
-    p->note_dbcache();
     mel_out.resize((size_t)p->hp.mel_dim * N);
     const float* const* xc = x0_chunks ? x0_chunks->data() : nullptr;
     const int nx = x0_chunks ? (int)x0_chunks->size() : 0;
@@ -113,15 +112,15 @@ bool gsv_dit::synthesize(const float* fea_ref, int R, const float* fea_todo, int
 
 void gsv_dit::time_sin(float t, float* out256) { gsvcu_dit_time_sin(t, out256); }
 
-void gsv_dit::db_set_step(int j) { p->db_step = j; }
+void gsv_dit::db_set_step(int j) { gsvcu_dit_db_set_step(p->ctx, j); }
 
 void gsv_dit::db_get_stats(db_stats& st) const {
-    st.steps = p->db_step;
+    int32_t steps = 0, hits[2] = {0, 0}, misses[2] = {0, 0};
+    gsvcu_dit_db_get_stats(p->ctx, &steps, hits, misses, st.last_fd, st.acc);
+    st.steps = steps;
     for (int b = 0; b < 2; b++) {
-        st.hits[b] = 0;
-        st.misses[b] = 0;
-        st.last_fd[b] = 0.0f;
-        st.acc[b] = 0.0f;
+        st.hits[b] = hits[b];
+        st.misses[b] = misses[b];
     }
 }
 
@@ -130,7 +129,7 @@ void gsv_dit::set_dbcache(int fn, float threshold, int warmup, int downsample) {
     p->db_thr = threshold;
     p->db_warmup = warmup;
     p->db_ds = downsample >= 1 ? downsample : 1;
-    p->note_dbcache();
+    p->push_dbcache();
 }
 
 int gsv_dit::dbcache_fn() const { return p->db_fn; }

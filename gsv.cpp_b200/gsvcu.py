@@ -126,6 +126,9 @@ SIGNATURES.update({
     "gsvcu_dit_sample_full": ([_P, _P, _P, _I, _I, _I, C.c_float, C.c_uint64, _P, _I, _P], C.c_int),
     "gsvcu_dit_op_condition": ([_P, _P], C.c_int),
     "gsvcu_dit_set_alg": ([_P, _I], C.c_int),
+    "gsvcu_dit_set_dbcache": ([_P, _I, C.c_float, _I, _I, _I, _I, C.c_float, _I], C.c_int),
+    "gsvcu_dit_db_set_step": ([_P, _I], C.c_int),
+    "gsvcu_dit_db_get_stats": ([_P, _P, _P, _P, _P, _P], C.c_int),
     "gsvcu_dit_get_alg": ([_P, C.POINTER(C.c_int32)], C.c_int),
     "gsvcu_dit_synthesize": ([_P, _P, _I, _P, _I, _P, _I, _I, C.c_float, C.c_uint64, _I, _P, _I, _I, _P], C.c_int),
     "gsvcu_dit_time_sin": ([C.c_float, _P], None),
@@ -544,6 +547,21 @@ class Dit:
                                                   float(cfg), seed, block_override, None, 0, skip_steps,
                                                   out.ctypes.data))
         return out
+
+    def set_dbcache(self, fn, threshold=0.08, warmup=8, warmup_interval=1, max_cached=-1, max_cont=-1,
+                    max_accum=0.0, downsample=4):
+        """cache-dit (DBCache) settings (gsv_dit_cfg::dbcache_*); fn = 0 turns it off."""
+        self._check(self.lib.gsvcu_dit_set_dbcache(self.h, fn, float(threshold), warmup, warmup_interval, max_cached,
+                                                   max_cont, float(max_accum), downsample))
+
+    def db_stats(self):
+        """(steps, hits [2], misses [2], last_fd [2], acc [2])."""
+        st = np.zeros(1, np.int32)
+        h, m = np.zeros(2, np.int32), np.zeros(2, np.int32)
+        fd, acc = np.zeros(2, np.float32), np.zeros(2, np.float32)
+        self._check(self.lib.gsvcu_dit_db_get_stats(self.h, st.ctypes.data, h.ctypes.data, m.ctypes.data, fd.ctypes.data,
+                                                    acc.ctypes.data))
+        return int(st[0]), h, m, fd, acc
 
     def set_alg(self, uncond_reuse: int):
         """gsv_dit::set_alg: uncond_reuse 0, 1 (reuse on odd steps) or 2 (extrapolate on odd steps)."""

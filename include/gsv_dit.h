@@ -5,10 +5,7 @@
 // forwards to the gsvcu_dit_* entry points of gsvcu.h. Layouts are the reference's torch layouts
 // (mel [100][T], mu [512][T], index c * T + t).
 //
-// Differences a caller can see: cache-dit (DBCache) is not implemented -- set_dbcache and the
-// gsv_dit_cfg::dbcache_* fields are accepted and reported back, but every block is computed on every step
-// (the results a zero threshold would give), and db_get_stats counts no hits; debug_read has no
-// intermediate tensors and returns false.
+// Difference a caller can see: debug_read has no named intermediate tensors and returns false.
 #pragma once
 
 #include <cstdint>
@@ -20,7 +17,7 @@ struct gsv_dit_cfg {
     bool verbose   = false;
     std::string device;       // "" / "gpu" / "vulkan" / "cuda" -> GPU 0; "N" or "x:N" -> GPU N; "cpu" is rejected
 
-    // cache-dit (DBCache); accepted, not implemented (every block is computed)
+    // cache-dit (DBCache): fn > 0 caches the middle blocks' residual across steps behind the gates below
     int   dbcache_fn              = 0;
     float dbcache_threshold       = 0.08f;
     int   dbcache_warmup          = 8;

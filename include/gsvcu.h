@@ -354,6 +354,19 @@ int gsvcu_dit_synthesize(gsvcu_dit* ctx, const float* fea_ref, int32_t R, const 
 void gsvcu_dit_time_sin(float t, float* out256);
 /* The checkpoint's RoPE inverse frequencies [32] (gsv_dit::debug_tables' angles are n * inv_freq[i]). */
 int gsvcu_dit_get_inv_freq(const gsvcu_dit* ctx, float* out32);
+/* cache-dit (DBCache) of gsv_dit (gsv_dit_cfg::dbcache_*, set_dbcache; src/gsv_dit.cpp:1124-1323): with
+ * fn > 0 (and < depth) every velocity runs the trunk and the first fn blocks, compares their residual with the
+ * one of its branch's last full step (relative L1 over the reference's downsampled view), and, when the gates
+ * allow (not a warmup step, the difference below threshold, max_cached / max_cont / max_accum), adds the
+ * middle blocks' residual of that last full step instead of running them. Changing fn or downsample resets
+ * the cache state; sample() resets the gates and counters. */
+int gsvcu_dit_set_dbcache(gsvcu_dit* ctx, int32_t fn, float threshold, int32_t warmup, int32_t warmup_interval,
+                          int32_t max_cached, int32_t max_cont, float max_accum, int32_t downsample);
+/* The diffusion step the gates see (sample() sets it per step; velocity() callers set it). */
+int gsvcu_dit_db_set_step(gsvcu_dit* ctx, int32_t step);
+/* Counters per branch [2] (conditional, unconditional) since the last reset. */
+int gsvcu_dit_db_get_stats(const gsvcu_dit* ctx, int32_t* steps, int32_t* hits2, int32_t* misses2, float* last_fd2,
+                           float* acc2);
 /* gsv_dit::set_alg / alg (src/gsv_dit.h:46-49, the loop src/gsv_dit.cpp:1449-1468): uncond_reuse 0 computes
  * the negative branch every guided step; 1 reuses the last computed one on odd steps; 2 extrapolates
  * 2 neg[k-1] - neg[k-2] on odd steps (once two exist). Values outside 0..2 mean 0. */

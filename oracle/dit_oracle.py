@@ -145,23 +145,25 @@ def time_embed(W, t: float) -> np.ndarray:
     return mm(h, W["dit.time_embed.time_mlp.2.weight"], W["dit.time_embed.time_mlp.2.bias"])[0]
 
 
-def branch(W, x_mel: np.ndarray, t: float, cond: np.ndarray, x_lens: int, n_blocks: int | None = None,
-           head: bool = True) -> np.ndarray:
-    """One estimator pass of one branch: x_mel [100][T] and cond [T][1024] -> vel [100][T] (head) or the
-    hidden state [T][1024] after n_blocks blocks."""
+def trunk(W, x_mel: np.ndarray, cond: np.ndarray, x_lens: int) -> np.ndarray:
+    """build_trunk (src/gsv_dit.cpp:533-549): x_mel [100][T], cond [T][1024] -> hidden [T][1024]."""
     T = x_mel.shape[1]
-    depth = W["depth"] if n_blocks is None else min(n_blocks, W["depth"])
     mask = (np.arange(T) < x_lens).astype(np.float32)[:, None]
-    temb = time_embed(W, t)
-    st = silu(temb)[None, :]
     x = mm(x_mel.T, W["dit.input_embed.proj.weight_mel"]) + cond
     cp = mish(conv_pos(x * mask, W["dit.input_embed.conv_pos_embed.conv1d.0.weight"],
                        W["dit.input_embed.conv_pos_embed.conv1d.0.bias"]))
     cp = mish(conv_pos(cp, W["dit.input_embed.conv_pos_embed.conv1d.2.weight"],
                        W["dit.input_embed.conv_pos_embed.conv1d.2.bias"])) * mask
-    x = (x + cp).astype(np.float32)
+    return (x + cp).astype(np.float32)
+
+
+def blocks(W, x: np.ndarray, t: float, x_lens: int, l0: int, l1: int) -> np.ndarray:
+    """DiT blocks l0 .. l1 - 1 (dit_block, src/gsv_dit.cpp:407-433) on hidden x [T][1024]."""
+    T = x.shape[0]
+    mask = (np.arange(T) < x_lens).astype(np.float32)[:, None]
+    st = silu(time_embed(W, t))[None, :]
     cs, sn = rope_tables(W["dit.rotary_embed.inv_freq"], T)
-    for li in range(depth):
+    for li in range(l0, l1):
         p = f"dit.transformer_blocks.{li}."
         m = mm(st, W[p + "attn_norm.linear.weight"], W[p + "attn_norm.linear.bias"])[0].reshape(6, D)
         xn = layernorm_mod(x, m[1], m[0])
@@ -174,15 +176,96 @@ def branch(W, x_mel: np.ndarray, t: float, cond: np.ndarray, x_lens: int, n_bloc
         f = mm(gelu_tanh(mm(xn2, W[p + "ff.ff.0.0.weight"], W[p + "ff.ff.0.0.bias"])),
                W[p + "ff.ff.2.weight"], W[p + "ff.ff.2.bias"])
         x = (x + f * m[5]).astype(np.float32)
-    if not head:
-        return x
+    return x
+
+
+def head(W, x: np.ndarray, t: float) -> np.ndarray:
+    """build_head (src/gsv_dit.cpp:563-576): hidden [T][1024] -> vel [100][T]."""
+    st = silu(time_embed(W, t))[None, :]
     e2 = mm(st, W["dit.norm_out.linear.weight"], W["dit.norm_out.linear.bias"])[0]
     xo = layernorm_mod(x, e2[:D], e2[D:])
     return mm(xo, W["dit.proj_out.weight"], W["dit.proj_out.bias"]).T.copy()
 
 
+def branch(W, x_mel: np.ndarray, t: float, cond: np.ndarray, x_lens: int, n_blocks: int | None = None,
+           head_: bool = True, **kw) -> np.ndarray:
+    """One estimator pass of one branch: x_mel [100][T] and cond [T][1024] -> vel [100][T] (with the head) or
+    the hidden state [T][1024] after n_blocks blocks."""
+    if "head" in kw:
+        head_ = kw.pop("head")
+    depth = W["depth"] if n_blocks is None else min(n_blocks, W["depth"])
+    x = blocks(W, trunk(W, x_mel, cond, x_lens), t, x_lens, 0, depth)
+    return head(W, x, t) if head_ else x
+
+
+class DbCache:
+    """cache-dit (DBCache) of gsv_dit (src/gsv_dit.cpp:1124-1323): settings, per-branch gates and state."""
+
+    def __init__(self, fn, thr=0.08, warmup=8, warmup_interval=1, max_cached=-1, max_cont=-1, max_accum=0.0, ds=4):
+        self.fn, self.thr, self.warmup, self.iv = fn, np.float32(thr), warmup, warmup_interval
+        self.max_cached, self.max_cont, self.max_accum, self.ds = max_cached, max_cont, np.float32(max_accum), ds
+        self.r_prev = [None, None]
+        self.mr_prev = [None, None]
+        self.step = 0
+        self.reset()
+
+    def reset(self):
+        self.b = [dict(cached=0, cont=0, hits=0, misses=0, valid=False, acc=np.float32(0), last_fd=np.float32(0))
+                  for _ in range(2)]
+        self.step = 0
+
+
+def branch_cached(W, db: DbCache, bi: int, x_mel, t, cond, x_lens):
+    """run_step_cached (src/gsv_dit.cpp:1250-1323) of branch bi -> vel [100][T]."""
+    T = x_mel.shape[1]
+    xt = trunk(W, x_mel, cond, x_lens)
+    xf = blocks(W, xt, t, x_lens, 0, db.fn)
+    ds = db.ds if (db.ds >= 1 and T % db.ds == 0) else 1
+    rflat = (xf - xt).astype(np.float32).ravel()
+    Tds = T // ds
+    if ds > 1:   # the reference's view: row stride of ds floats over the flat residual
+        idx = (np.arange(Tds)[:, None] * ds + np.arange(D)[None, :]).ravel()
+        r_cur = rflat[idx]
+    else:
+        r_cur = rflat
+    if db.r_prev[bi] is None or db.r_prev[bi].size != r_cur.size:
+        db.r_prev[bi] = np.zeros_like(r_cur)
+    rp = db.r_prev[bi]
+    fd = np.float32(np.float32(np.abs(r_cur.astype(np.float64) - rp).sum()) /
+                    (np.float32(np.abs(rp.astype(np.float64)).sum()) + np.float32(1e-6)))
+    d = db.b[bi]
+    d["last_fd"] = fd
+    hit = False
+    warm = db.step < db.warmup and db.step % max(db.iv, 1) == 0
+    if d["valid"] and db.thr > 0 and not warm:
+        ok = fd < db.thr
+        if ok and db.max_cached >= 0 and d["cached"] >= db.max_cached:
+            ok = False
+        if ok and db.max_cont >= 0 and d["cont"] >= db.max_cont:
+            ok = False
+            d["cont"] = 0
+        if ok and db.max_accum > 0 and d["acc"] >= db.max_accum:
+            ok = False
+        hit = ok
+    if fd > 0:
+        d["acc"] = np.float32(d["acc"] + fd)
+    if hit:
+        xm = (xf + db.mr_prev[bi]).astype(np.float32)
+        d["hits"] += 1
+        d["cached"] += 1
+        d["cont"] += 1
+    else:
+        xm = blocks(W, xf, t, x_lens, db.fn, W["depth"])
+        db.mr_prev[bi] = (xm - xf).astype(np.float32)
+        db.r_prev[bi] = r_cur.copy()
+        d["misses"] += 1
+        d["valid"] = True
+        d["cont"] = 0
+    return head(W, xm, t)
+
+
 def sample(W, x0: np.ndarray, cond: np.ndarray, neg: np.ndarray, P: int, steps: int, cfg: float,
-           uncond_reuse: int = 0, skip_steps: int = 0) -> np.ndarray:
+           uncond_reuse: int = 0, skip_steps: int = 0, db: DbCache | None = None) -> np.ndarray:
     """The CFM Euler loop on set conditions: x0 [100][T] -> mel [100][T - P]; uncond_reuse as the reference's
     alg (src/gsv_dit.cpp:1449-1468): 1 reuses the last computed negative velocity on odd steps, 2
     extrapolates 2 neg[k-1] - neg[k-2]."""
@@ -192,11 +275,17 @@ def sample(W, x0: np.ndarray, cond: np.ndarray, neg: np.ndarray, P: int, steps: 
     dt = np.float32(1.0) / np.float32(steps)
     p1 = p2 = None
     count = 0
+    if db is not None:
+        db.reset()
+    vfun = (lambda bi, xx, tt, cc: branch_cached(W, db, bi, xx, tt, cc, T)) if db is not None else \
+        (lambda bi, xx, tt, cc: branch(W, xx, tt, cc, T))
     for j in range(steps):
+        if db is not None:
+            db.step = j
         if j < skip_steps:   # src/gsv_dit.cpp:1444-1448: no model call, x unchanged
             continue
         t = float(np.float32(j) * dt)
-        vel = branch(W, x, t, cond, T)
+        vel = vfun(0, x, t, cond)
         if cfg > 1e-5:
             odd = (j & 1) == 1
             if odd and uncond_reuse == 1 and count >= 1:
@@ -204,7 +293,7 @@ def sample(W, x0: np.ndarray, cond: np.ndarray, neg: np.ndarray, P: int, steps: 
             elif odd and uncond_reuse == 2 and count >= 2:
                 ng = (np.float32(2.0) * p1 - p2).astype(np.float32)
             else:
-                ng = branch(W, x, t, neg, T)
+                ng = vfun(1, x, t, neg)
                 count += 1
                 p2, p1 = p1, ng
             vel = (vel + (vel - ng) * np.float32(cfg)).astype(np.float32)

@@ -241,3 +241,31 @@ def test_cpp_dropin_dit_class(dit_small, tmp_path):
     assert lines[3]["tables"] == 32 * T and lines[3]["dbcache_fn"] == 8 and lines[3]["hits"] == 0
     assert lines[3]["debug_read"] == 0
     d.close()
+
+
+@pytest.mark.parametrize("T,thr,max_cont", [(120, 0.2, -1), (120, 0.2, 2), (120, 0.05, -1), (122, 0.2, -1)])
+def test_dit_cache_dit_matches_oracle(dit_small, T, thr, max_cont):
+    """cache-dit (DBCache, fn = 1 of 2 blocks): the front residual's relative L1 change against the branch's
+    last full step gates the middle blocks (reused residual on a hit). Thresholds sit far from the measured
+    criterion (0.09-0.14) so both sides take the same decisions: 0.2 hits after the first step (max_cont 2
+    forces every third step to run), 0.05 never hits; T = 120 uses the reference's downsampled view (ds 4),
+    T = 122 the whole residual."""
+    import gsvcu
+    path, W = dit_small
+    P, steps = 20, 6
+    x0, cond, neg = _inputs(T, 31)
+    d = gsvcu.Dit(path)
+    d.set_condition(cond, neg)
+    d.set_dbcache(1, threshold=thr, warmup=1, max_cont=max_cont, downsample=4)
+    got = d.sample(x0, P, steps, 2.0)
+    db = O.DbCache(1, thr=thr, warmup=1, max_cont=max_cont, ds=4)
+    ref = O.sample(W, x0, cond, neg, P, steps, 2.0, db=db)
+    e = rel_l2(got, ref)
+    st, hits, misses, fd, acc = d.db_stats()
+    print(f"cache-dit T={T} thr={thr} max_cont={max_cont}: rel_l2 {e:.2e}, hits {hits.tolist()} misses "
+          f"{misses.tolist()} (oracle {[(b['hits'], b['misses']) for b in db.b]}), last fd {fd.tolist()}")
+    assert [(int(hits[b]), int(misses[b])) for b in range(2)] == [(b["hits"], b["misses"]) for b in db.b]
+    assert st == steps - 1 and e <= TOL
+    np.testing.assert_allclose(fd, [db.b[0]["last_fd"], db.b[1]["last_fd"]], rtol=1e-2)
+    d.set_dbcache(0)
+    d.close()
