@@ -179,7 +179,7 @@ def blocks(W, x: np.ndarray, t: float, x_lens: int, l0: int, l1: int) -> np.ndar
     return x
 
 
-def head(W, x: np.ndarray, t: float) -> np.ndarray:
+def head_out(W, x: np.ndarray, t: float) -> np.ndarray:
     """build_head (src/gsv_dit.cpp:563-576): hidden [T][1024] -> vel [100][T]."""
     st = silu(time_embed(W, t))[None, :]
     e2 = mm(st, W["dit.norm_out.linear.weight"], W["dit.norm_out.linear.bias"])[0]
@@ -188,14 +188,12 @@ def head(W, x: np.ndarray, t: float) -> np.ndarray:
 
 
 def branch(W, x_mel: np.ndarray, t: float, cond: np.ndarray, x_lens: int, n_blocks: int | None = None,
-           head_: bool = True, **kw) -> np.ndarray:
+           head: bool = True) -> np.ndarray:
     """One estimator pass of one branch: x_mel [100][T] and cond [T][1024] -> vel [100][T] (with the head) or
     the hidden state [T][1024] after n_blocks blocks."""
-    if "head" in kw:
-        head_ = kw.pop("head")
     depth = W["depth"] if n_blocks is None else min(n_blocks, W["depth"])
     x = blocks(W, trunk(W, x_mel, cond, x_lens), t, x_lens, 0, depth)
-    return head(W, x, t) if head_ else x
+    return head_out(W, x, t) if head else x
 
 
 class DbCache:
@@ -261,7 +259,7 @@ def branch_cached(W, db: DbCache, bi: int, x_mel, t, cond, x_lens):
         d["misses"] += 1
         d["valid"] = True
         d["cont"] = 0
-    return head(W, xm, t)
+    return head_out(W, xm, t)
 
 
 def sample(W, x0: np.ndarray, cond: np.ndarray, neg: np.ndarray, P: int, steps: int, cfg: float,
