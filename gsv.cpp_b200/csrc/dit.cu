@@ -967,10 +967,12 @@ cudaError_t init_device() {
 // DE_QKV, DE_F16 with GELU (tanh).
 bool gemm(int epi, const __half* A, const __half* W, const DitGemmArgs& a, cudaStream_t s) {
     CUtensorMap ma, mb;
+    const int sms = g_sms.load(std::memory_order_relaxed);
+    const int rt = (a.R + GM - 1) / GM;
     if (!map_2d(&ma, A, (uint64_t)a.R, (uint64_t)a.K, GM) || !map_2d(&mb, W, (uint64_t)a.N, (uint64_t)a.K, 128))
         return false;
-    const dim3 grid(a.N / 128, (a.R + GM - 1) / GM);
-    const bool wide = (int)(grid.x * grid.y) > g_sms.load(std::memory_order_relaxed);
+    const dim3 grid(a.N / 128, rt);
+    const bool wide = (int)(grid.x * grid.y) > sms;
     switch (epi) {
         case DE_F32: launch_gemm<DE_F32, ACT_NONE, 128, false, 4>(grid, ma, mb, a, s); break;
         case DE_RESID: launch_gemm<DE_RESID, ACT_NONE, 128, false, 4>(grid, ma, mb, a, s); break;
@@ -1055,7 +1057,7 @@ struct gsvcu_dit {
     __half* w_ctx = nullptr;                    // [1024][640] (612 used)
     float* b_ctx = nullptr;
     // per-shape state (set_condition / prepare)
-    int T = 0, x_lens = 0, cap_rows = 0;
+    int T = 0, x_lens = 0, cap_rows = 0, cap_T = 0;
     std::vector<void*> ballocs;
     float *cond = nullptr;        // [2][T][1024]: condition, negative condition
     float *rcos = nullptr, *rsin = nullptr;   // [T][32]
@@ -1158,12 +1160,25 @@ bool tensor_f32(const GgufTensor* t, size_t n, std::vector<float>& out) {
 
 }  // namespace
 
+// Buffers for T_ frames and `rows` rows: reused while they are large enough (every buffer is indexed with
+// the current T), reallocated otherwise. A change of T zeroes cache-dit's previous front residuals, as the
+// reference's rebuilt cache does (src/gsv_dit.cpp:1124-1149).
 int gsvcu_dit::reserve(int T_, int rows) {
-    if (T_ == T && rows <= cap_rows) return GSVCU_OK;
+    if (T_ <= cap_T && rows <= cap_rows) {
+        if (T_ != T) {
+            T = T_;
+            tp = (T_ + 7) & ~7;
+            for (int b = 0; b < 2; b++)
+                if (cudaMemsetAsync(rprev[b], 0, (size_t)T_ * DM * 4, stream) != cudaSuccess)
+                    return fail(GSVCU_ERR_CUDA, "cache reset failed");
+        }
+        return GSVCU_OK;
+    }
     cudaStreamSynchronize(stream);
     for (void* p : ballocs) cudaFree(p);
     ballocs.clear();
     cap_rows = 0;
+    cap_T = 0;
     T = 0;
     const size_t R = (size_t)rows, TT = (size_t)T_;
     const size_t nada = (size_t)hp.depth * ADA + 2 * DM;
@@ -1194,6 +1209,7 @@ int gsvcu_dit::reserve(int T_, int rows) {
     cudaMemsetAsync(rprev[0], 0, TT * DM * 4, stream);
     cudaMemsetAsync(rprev[1], 0, TT * DM * 4, stream);
     cap_rows = rows;
+    cap_T = T_;
     T = T_;
     tp = (T_ + 7) & ~7;
     return GSVCU_OK;
