@@ -8,7 +8,9 @@
 //   vel = proj_out(LN(x) * (1 + scale) + shift)            (build_head :563-576)
 // and the CFM Euler loop with classifier-free guidance (gsv_dit::sample, :1410-1478). The positive and
 // the negative (unconditional) branch share x_mel and t and differ only in the condition rows, so a
-// guided step runs both as one batch of 2T rows.
+// guided step runs both as one batch of 2T rows. Also here: the static cache of prepare (text path with
+// 4 ConvNeXtV2 blocks and the context projection, :486-531), synthesize's chunking (:1480-1581), the
+// unconditional-velocity reuse of gsv_dit_alg, and cache-dit (DBCache, :1124-1323).
 //
 // Kernels (sm_100a):
 //   k_dit_gemm    every linear layer and both convolutions: a tcgen05.mma kind::f16 GEMM, f16 operands
@@ -19,11 +21,13 @@
 //                 activation tile is a TMA load at frame offset tap - 15 of a 3D [branch][frame][channel]
 //                 map, whose out-of-range frames read as zero (the conv's zero padding, per branch).
 //   k_dit_attn_tc 16 heads x 64 dims, non-causal, key padding mask, on tcgen05: S = Q K^T and O += P V^T
-//                 in TMEM, the softmax in registers (thread = query row), P through shared memory; two
-//                 passes (row maxima, then exponentials) so O is never rescaled. The QKV epilogue writes v
-//                 transposed ([branch][head][dim][frame]) for the K-major P V^T operand.
+//                 in TMEM, the softmax in registers (two threads per query row), P through shared memory;
+//                 two passes (row maxima, then exponentials) so O is never rescaled. The QKV epilogue
+//                 writes v transposed ([branch][head][dim][frame]) for the K-major P V^T operand.
 //   k_dit_lnmod   LayerNorm (eps 1e-6, no affine) * (1 + scale) + shift -> f16 GEMM operand.
 //   k_dit_gemv    the time MLP and every block's AdaLN projection (one launch for all blocks per step).
+//   k_dit_dwconv_ln, k_dit_gelu_colnorm, k_dit_grn: the ConvNeXtV2 pieces around two GEMMs (prepare).
+//   k_dit_fd_partial / _final: cache-dit's criterion (relative L1 change of the front residual).
 //   small kernels for the mel packing, the masked conv input and the Euler / guidance update.
 // Numerics: f16 GEMM operands (what ggml's mul_mat does with F16 weights: the activations are
 // converted to F16 first), f32 accumulation, f32 elsewhere; parity with the CPU restatement is within
