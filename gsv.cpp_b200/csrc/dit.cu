@@ -22,8 +22,8 @@
 //                 map, whose out-of-range frames read as zero (the conv's zero padding, per branch).
 //   k_dit_attn_tc 16 heads x 64 dims, non-causal, key padding mask, on tcgen05: S = Q K^T and O += P V^T
 //                 in TMEM, the softmax in registers (two threads per query row), P through shared memory;
-//                 two passes (row maxima, then exponentials) so O is never rescaled. The QKV epilogue
-//                 writes v transposed ([branch][head][dim][frame]) for the K-major P V^T operand.
+//                 one pass, O rescaled in TMEM only when a row's maximum grows by more than 2^8. The QKV
+//                 epilogue writes v transposed ([branch][head][dim][frame]) for the K-major P V^T operand.
 //   k_dit_lnmod   LayerNorm (eps 1e-6, no affine) * (1 + scale) + shift -> f16 GEMM operand.
 //   k_dit_gemv    the time MLP and every block's AdaLN projection (one launch for all blocks per step).
 //   k_dit_dwconv_ln, k_dit_gelu_colnorm, k_dit_grn: the ConvNeXtV2 pieces around two GEMMs (prepare).
@@ -343,13 +343,15 @@ __global__ void __launch_bounds__(G_THREADS) k_dit_gemm(const __grid_constant__ 
 }
 
 // ------------------------------------------------------------------ attention on tcgen05
-// One CTA per (128 queries, head, branch). Two passes over the key tiles of 64 (keys < x_lens): pass 1
-// S = Q K^T into TMEM and the row maxima; pass 2 S again, P = exp2((S - max) * scale * log2 e) as f16 into
-// shared memory (the 128-byte-swizzled K-major layout the MMA reads), row sums, O += P V^T in TMEM. With the
-// exact row maximum known before any exponential, O needs no rescaling (the cost: Q K^T twice).
-// Warps: 0 TMA (Q once, then K or K + V^T tiles into a 3-stage ring), 1 TMEM + MMA, 2-9 softmax: two threads
-// per query row (TMEM lane), each on 32 of a tile's 64 keys; row maxima and sums are combined once, through
-// shared memory. S and P are double-buffered, so the MMAs of tile j + 1 overlap the softmax of tile j.
+// One CTA per (128 queries, head, branch), one pass over the key tiles of 64 (keys < x_lens): S = Q K^T into
+// TMEM, P = exp2(S * scale * log2 e - m) as f16 into shared memory (the 128-byte-swizzled K-major layout the
+// MMA reads), row sums, O += P V^T in TMEM. The reference value m of a row is raised only when a tile's
+// maximum exceeds it by more than FA_TAU (so P <= 2^FA_TAU, well inside f16): then the row's O in TMEM and
+// its running sum are scaled by exp2(m_old - m_new), after the previous P V^T has completed. Rows raise
+// their m on the first tile and rarely after it.
+// Warps: 0 TMA (Q once, then K + V^T tiles into a 3-stage ring), 1 TMEM + MMA, 2-9 softmax: two threads per
+// query row (TMEM lane), each on 32 of a tile's 64 keys, exchanging their tile maxima through shared memory.
+// S and P are double-buffered, so the MMAs of tile j + 1 overlap the softmax of tile j.
 constexpr int FQ = 128, FK = 64, FKS = 3;
 struct AttnMaps {
     CUtensorMap q;    // qkv16 [R][3072], box 64 x 128
@@ -361,14 +363,15 @@ struct FaSmem {
     static constexpr size_t OFF_K = OFF_Q + FQ * HDD * 2;       // FKS x 8 KB
     static constexpr size_t OFF_V = OFF_K + FKS * FK * HDD * 2; // FKS x 8 KB
     static constexpr size_t OFF_P = OFF_V + FKS * HDD * FK * 2; // 2 x 16 KB
-    static constexpr size_t OFF_X = OFF_P + 2 * FQ * FK * 2;   // [2 halves][128 rows] f32: row max, then row sum
-    static constexpr size_t OFF_BAR = OFF_X + 2 * FQ * 4;
+    static constexpr size_t OFF_X = OFF_P + 2 * FQ * FK * 2;   // [2 tiles][2 halves][128 rows] f32 exchanges
+    static constexpr size_t OFF_BAR = OFF_X + 4 * FQ * 4;
     // qfull, kvfull[FKS], kvempty[FKS], sfull[2], sfree[2], pfull[2], pfree[2], ofull
     static constexpr int NBAR = 1 + 2 * FKS + 8 + 1;
     static constexpr size_t SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
 };
 constexpr int FA_THREADS = 320;   // warp 0 TMA, warp 1 MMA, warps 2-9 softmax (two per TMEM lane quarter)
 constexpr uint32_t FA_TMEM_COLS = 256;   // S0, S1, O (64 columns each)
+constexpr float FA_TAU = 8.0f;             // log2 headroom of P above the row's reference value
 
 __device__ __forceinline__ float ex2f(float x) {
     float y;
@@ -431,16 +434,13 @@ __global__ void __launch_bounds__(FA_THREADS) k_dit_attn_tc(const __grid_constan
             tma_load_2d(su32(sm + L::OFF_Q), &m.q, h * HDD, b * T + q0, qfull);
             int g = 0;
             bool ok = true;
-            for (int pass = 0; pass < 2 && ok; pass++)
-                for (int j = 0; j < nt; j++, g++) {
-                    const int s = g % FKS;
-                    if (!bar_wait_short(kvempty(s), ((uint32_t)(g / FKS) & 1u) ^ 1u, abort_flag)) { ok = false; break; }
-                    bar_expect_tx(kvfull(s), (pass ? 2u : 1u) * FK * HDD * 2);
-                    tma_load_2d(su32(sm + L::OFF_K + (size_t)s * FK * HDD * 2), &m.k, DM + h * HDD, b * T + j * FK, kvfull(s));
-                    if (pass)
-                        tma_load_2d(su32(sm + L::OFF_V + (size_t)s * HDD * FK * 2), &m.vt, j * FK, (b * NHD + h) * HDD,
-                                    kvfull(s));
-                }
+            for (int j = 0; j < nt; j++, g++) {
+                const int s = g % FKS;
+                if (!bar_wait_short(kvempty(s), ((uint32_t)(g / FKS) & 1u) ^ 1u, abort_flag)) { ok = false; break; }
+                bar_expect_tx(kvfull(s), 2u * FK * HDD * 2);
+                tma_load_2d(su32(sm + L::OFF_K + (size_t)s * FK * HDD * 2), &m.k, DM + h * HDD, b * T + j * FK, kvfull(s));
+                tma_load_2d(su32(sm + L::OFF_V + (size_t)s * HDD * FK * 2), &m.vt, j * FK, (b * NHD + h) * HDD, kvfull(s));
+            }
             if (!ok) {
                 if (err) atomicExch(err, 1);
                 *abort_flag = 1;
@@ -472,27 +472,21 @@ __global__ void __launch_bounds__(FA_THREADS) k_dit_attn_tc(const __grid_constan
                 v++;
                 return true;
             };
-            for (int pass = 0; pass < 2 && ok; pass++) {
-                for (int j = 0; j < nt; j++, g++, u++) {
-                    const int s = g % FKS, sb = u & 1;
-                    if (!bar_wait_short(kvfull(s), (uint32_t)(g / FKS) & 1u, abort_flag) ||
-                        !bar_wait_short(sfree(sb), (((uint32_t)u >> 1) & 1u) ^ 1u, abort_flag)) { ok = false; break; }
-                    tc_fence_after();
-                    const uint32_t ka = su32(sm + L::OFF_K + (size_t)s * FK * HDD * 2);
+            for (int j = 0; j < nt && ok; j++, g++, u++) {
+                const int s = g % FKS, sb = u & 1;
+                if (!bar_wait_short(kvfull(s), (uint32_t)(g / FKS) & 1u, abort_flag) ||
+                    !bar_wait_short(sfree(sb), (((uint32_t)u >> 1) & 1u) ^ 1u, abort_flag)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t ka = su32(sm + L::OFF_K + (size_t)s * FK * HDD * 2);
 #pragma unroll
-                    for (int kk = 0; kk < HDD / 16; kk++)
-                        umma_f16(tmem + (uint32_t)(sb * FK), umma_desc(qa + 32u * kk), umma_desc(ka + 32u * kk), IDS,
-                                 (uint32_t)kk);
-                    umma_commit(sfull(sb));
-                    if (pass == 0) {
-                        umma_commit(kvempty(s));
-                        continue;
-                    }
-                    if (j > 0 && !pv(j - 1)) { ok = false; break; }
-                    prev_s = s;
-                }
-                if (ok && pass == 1 && !pv(nt - 1)) ok = false;
+                for (int kk = 0; kk < HDD / 16; kk++)
+                    umma_f16(tmem + (uint32_t)(sb * FK), umma_desc(qa + 32u * kk), umma_desc(ka + 32u * kk), IDS,
+                             (uint32_t)kk);
+                umma_commit(sfull(sb));
+                if (j > 0 && !pv(j - 1)) { ok = false; break; }
+                prev_s = s;
             }
+            if (ok && !pv(nt - 1)) ok = false;
             if (!ok) {
                 if (err) atomicExch(err, 1);
                 *abort_flag = 1;
@@ -505,24 +499,22 @@ __global__ void __launch_bounds__(FA_THREADS) k_dit_attn_tc(const __grid_constan
         // softmax: thread = (query row fr = TMEM lane, half hf): keys 32 hf .. 32 hf + 31 of each tile
         const int q = warp & 3, fr = 32 * q + lane, hf = (warp - 2) >> 2;
         const uint32_t tl = tmem + ((uint32_t)(32 * q) << 16);
-        float* xch = (float*)(sm + L::OFF_X);   // [half][row]
+        float* xch = (float*)(sm + L::OFF_X);   // [tile parity][half][row]
         const float c = ATTN_SCALE * 1.4426950408889634f;
-        float mx = -INFINITY, l = 0.0f;
-        int u = 0, v = 0;
+        float mref = -INFINITY, l = 0.0f;       // the row's reference value (scaled log2 units) and sum
+        int v = 0;
         bool ok = true;
         // (every softmax thread runs the same named-barrier sequence, also after a failed wait)
-        for (int pass = 0; pass < 2; pass++) {
-            if (pass == 1) {   // the row maximum of both halves
-                xch[hf * FQ + fr] = mx;
-                asm volatile("bar.sync 1, 256;" ::: "memory");
-                mx = fmaxf(xch[fr], xch[FQ + fr]);
+        for (int j = 0; j < nt; j++) {
+            const int sb = j & 1;
+            float sv[2][16];
+            float lm = -INFINITY;
+            const int kv = x_lens - j * FK - 32 * hf;   // valid keys of this thread's 32 (may be <= 0)
+            if (ok) {
+                if (!bar_wait_short_warp(sfull(sb), ((uint32_t)j >> 1) & 1u, abort_flag)) ok = false;
             }
-            const float mc = mx * c;
-            for (int j = 0; j < nt && ok; j++, u++) {
-                const int sb = u & 1;
-                if (!bar_wait_short_warp(sfull(sb), ((uint32_t)u >> 1) & 1u, abort_flag)) { ok = false; break; }
+            if (ok) {
                 tc_fence_after();
-                float sv[2][16];
 #pragma unroll
                 for (int k = 0; k < 2; k++) tmem_ld16(tl + (uint32_t)(sb * FK + 32 * hf + 16 * k), sv[k]);
                 tmem_wait_ld();
@@ -530,39 +522,71 @@ __global__ void __launch_bounds__(FA_THREADS) k_dit_attn_tc(const __grid_constan
                 for (int k = 0; k < 2; k++) tmem_bind(sv[k]);
                 tc_fence_before();
                 bar_arrive(sfree(sb));
-                const int kv = x_lens - j * FK - 32 * hf;   // valid keys of this thread's 32 (may be <= 0)
-                if (pass == 0) {
 #pragma unroll
-                    for (int i = 0; i < 32; i++)
-                        if (i < kv) mx = fmaxf(mx, sv[i >> 4][i & 15]);
-                    continue;
-                }
-                uint32_t pw[16];
-#pragma unroll
-                for (int i = 0; i < 32; i += 2) {
-                    const float p0 = i < kv ? ex2f(__fmaf_rn(sv[i >> 4][i & 15], c, -mc)) : 0.0f;
-                    const float p1 = i + 1 < kv ? ex2f(__fmaf_rn(sv[i >> 4][(i + 1) & 15], c, -mc)) : 0.0f;
-                    l += p0 + p1;
-                    pw[i / 2] = pack_h2(p0, p1);
-                }
-                const int pb = v & 1;
-                if (!bar_wait_short_warp(pfree(pb), (((uint32_t)v >> 1) & 1u) ^ 1u, abort_flag)) { ok = false; break; }
-                uint8_t* prow = sm + L::OFF_P + (size_t)pb * FQ * FK * 2 + (size_t)fr * 128;
-#pragma unroll
-                for (int k = 0; k < 4; k++) {   // 128-byte swizzle: chunk ch of row r at ch ^ (r % 8)
-                    const int ch = 4 * hf + k;
-                    *(uint4*)(prow + 16 * (ch ^ (fr & 7))) = make_uint4(pw[4 * k], pw[4 * k + 1], pw[4 * k + 2], pw[4 * k + 3]);
-                }
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                bar_arrive(pfull(pb));
-                v++;
+                for (int i = 0; i < 32; i++)
+                    if (i < kv) lm = fmaxf(lm, sv[i >> 4][i & 15] * c);
             }
+            float* xt = xch + (size_t)(j & 1) * 2 * FQ;
+            xt[hf * FQ + fr] = lm;
+            asm volatile("bar.sync 1, 256;" ::: "memory");
+            const float mt = fmaxf(xt[fr], xt[FQ + fr]);   // the tile's row maximum (scaled)
+            if (!ok) continue;
+            if (mt > mref + FA_TAU) {   // raise the reference value; rescale what O and l hold so far
+                if (j > 0) {
+                    const float alpha = ex2f(mref - mt);
+                    // O may be rescaled only after the previous tile's P V^T has completed
+                    if (!bar_wait_short_warp(pfree((v - 1) & 1), ((uint32_t)(v - 1) >> 1) & 1u, abort_flag)) {
+                        ok = false;
+                        continue;
+                    }
+                    tc_fence_after();
+                    float o2[2][16];
+#pragma unroll
+                    for (int k = 0; k < 2; k++) tmem_ld16(tl + (uint32_t)(2 * FK + 32 * hf + 16 * k), o2[k]);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int k = 0; k < 2; k++) {
+                        tmem_bind(o2[k]);
+#pragma unroll
+                        for (int i = 0; i < 16; i++) o2[k][i] *= alpha;
+                        tmem_st16(tl + (uint32_t)(2 * FK + 32 * hf + 16 * k), o2[k]);
+                    }
+                    tmem_wait_st();
+                    l *= alpha;
+                }
+                mref = mt;
+            }
+            uint32_t pw[16];
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+                const float p0 = i < kv ? ex2f(__fmaf_rn(sv[i >> 4][i & 15], c, -mref)) : 0.0f;
+                const float p1 = i + 1 < kv ? ex2f(__fmaf_rn(sv[i >> 4][(i + 1) & 15], c, -mref)) : 0.0f;
+                l += p0 + p1;
+                pw[i / 2] = pack_h2(p0, p1);
+            }
+            const int pb = v & 1;
+            if (!bar_wait_short_warp(pfree(pb), (((uint32_t)v >> 1) & 1u) ^ 1u, abort_flag)) {
+                ok = false;
+                continue;
+            }
+            uint8_t* prow = sm + L::OFF_P + (size_t)pb * FQ * FK * 2 + (size_t)fr * 128;
+#pragma unroll
+            for (int k = 0; k < 4; k++) {   // 128-byte swizzle: chunk ch of row r at ch ^ (r % 8)
+                const int ch = 4 * hf + k;
+                *(uint4*)(prow + 16 * (ch ^ (fr & 7))) = make_uint4(pw[4 * k], pw[4 * k + 1], pw[4 * k + 2], pw[4 * k + 3]);
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            tc_fence_before();   // the O rescale's TMEM stores before the MMA that accumulates onto them
+            bar_arrive(pfull(pb));
+            v++;
         }
-        // row sums of both halves (after every thread has read the maxima)
-        asm volatile("bar.sync 1, 256;" ::: "memory");
-        xch[hf * FQ + fr] = l;
-        asm volatile("bar.sync 1, 256;" ::: "memory");
-        l = xch[fr] + xch[FQ + fr];
+        // row sums of both halves
+        {
+            float* xt = xch + (size_t)(nt & 1) * 2 * FQ;
+            xt[hf * FQ + fr] = l;
+            asm volatile("bar.sync 1, 256;" ::: "memory");
+            l = xt[fr] + xt[FQ + fr];
+        }
         ok = bar_wait_short_warp(ofull, 0, abort_flag) && ok && !*abort_flag;
         tc_fence_after();
         if (ok) {
