@@ -1666,7 +1666,13 @@ namespace {
 int set_shape(gsvcu_dit* c, int T, int x_lens) {
     if (x_lens <= 0 || x_lens > T) x_lens = T;
     int rc;
+    const int old_T = c->T;
     if ((rc = c->reserve(T, 2 * T))) return rc;
+    if (x_lens != c->x_lens && old_T == T) {   // the reference rebuilds its cache state on a new x_lens too
+        for (int b = 0; b < 2; b++)
+            if (cudaMemsetAsync(c->rprev[b], 0, (size_t)T * DM * 4, c->stream) != cudaSuccess)
+                return c->fail(GSVCU_ERR_CUDA, "cache reset failed");
+    }
     c->x_lens = x_lens;
     std::vector<float> cs((size_t)T * 32), sn((size_t)T * 32);
     for (int n = 0; n < T; n++)
