@@ -131,3 +131,18 @@ def test_prepare_negative_drops_the_prompt(tmp_path):
     a = O.prepare(W, rng.standard_normal((100, T)).astype(np.float32), mu)
     b = O.prepare(W, np.zeros((100, T), np.float32), mu)
     assert np.array_equal(a[1], b[1]) and np.array_equal(b[0], b[1]) and not np.array_equal(a[0], b[0])
+
+
+def test_synthesize_single_chunk_is_one_sample(tmp_path):
+    """synthesize with one chunk (N <= block) is sample() on [reference features | target features] with the
+    reference mel as prompt and the given seed; the reference frames are the last 500 of the common length."""
+    p = S.write_dit_model(str(tmp_path / "d.gguf"), seed=8, depth=1)
+    W = O.load(p)
+    rng = np.random.default_rng(9)
+    fea_ref = rng.standard_normal((512, 34)).astype(np.float32)
+    fea_todo = rng.standard_normal((512, 20)).astype(np.float32)
+    mel_ref = rng.standard_normal((100, 30)).astype(np.float32)
+    out = O.synthesize(W, fea_ref, fea_todo, mel_ref, 2, 1.5, 5, block_override=64)
+    mu = np.concatenate([fea_ref[:, :30], fea_todo], axis=1)
+    ref = O.sample_full(W, mu, mel_ref, 30, 2, 1.5, 5)
+    assert np.array_equal(out, ref)
