@@ -121,6 +121,45 @@ def test_null_arguments_are_rejected():
     assert lib.gsvcu_last_error(None) == b"null context"
 
 
+def test_dit_and_bert_null_arguments_are_rejected():
+    """The DiT and BERT entry points validate their pointers on the host before any device work."""
+    lib = gsvcu.load_library()
+    h = C.c_void_p()
+    assert lib.gsvcu_dit_load(0, None, C.byref(h)) == -1
+    assert lib.gsvcu_dit_load(0, b"x.gguf", None) == -1
+    assert lib.gsvcu_bert_load(0, None, C.byref(h)) == -1
+    assert lib.gsvcu_bert_load(0, b"x.gguf", None) == -1
+    buf = (C.c_float * 256)()
+    assert lib.gsvcu_dit_velocity(None, buf, C.c_float(0.5), 0, buf) == -1
+    assert lib.gsvcu_dit_set_alg(None, 1) == -1
+    assert lib.gsvcu_dit_set_dbcache(None, 1, C.c_float(0.1), 0, 0, -1, -1, C.c_float(-1.0), 1) == -1
+    assert lib.gsvcu_bert_encode(None, None, 1, 0, None) == -1
+    assert lib.gsvcu_dit_last_error(None) == b"null DiT context"
+    assert lib.gsvcu_bert_last_error(None) == b"null BERT context"
+
+
+@pytest.mark.skipif(HAVE_GPU, reason="checks the no-GPU refusal")
+def test_dit_and_bert_load_without_gpu_is_a_clean_error(tmp_path):
+    lib = gsvcu.load_library()
+    h = C.c_void_p()
+    assert lib.gsvcu_dit_load(0, str(tmp_path / "none.gguf").encode(), C.byref(h)) == -7
+    assert not h.value
+    assert lib.gsvcu_bert_load(0, str(tmp_path / "none.gguf").encode(), C.byref(h)) == -7
+    assert not h.value
+
+
+def test_dit_time_sin_is_host_code_matching_the_restatement():
+    """gsvcu_dit_time_sin (the DiT's sinusoidal time input, `gsv_dit::time_sin` at src/gsv_dit.cpp:754-768,
+    host code in both) runs without a GPU; it equals the restatement's formula to float rounding."""
+    import dit_oracle as O
+    lib = gsvcu.load_library()
+    out = np.zeros(256, np.float32)
+    for t in (0.0, 0.03125, 0.5, 0.96875, 1.0):
+        lib.gsvcu_dit_time_sin(C.c_float(t), out.ctypes.data_as(C.c_void_p))
+        assert np.allclose(out, O.time_sin(t), rtol=0, atol=2e-4), t
+    lib.gsvcu_dit_time_sin(C.c_float(0.25), None)   # a null output is ignored
+
+
 def test_bench_weight_bytes_per_format(tmp_path):
     """bench.py's per-format weight bytes per decode step equal the GGUF bytes of the matrices the step reads
     (24 layers of attention / FFN matrices, their F32 biases and LayerNorms, the predict matrix)."""
