@@ -522,9 +522,17 @@ __global__ void __launch_bounds__(FA_THREADS) k_dit_attn_tc(const __grid_constan
                 for (int k = 0; k < 2; k++) tmem_bind(sv[k]);
                 tc_fence_before();
                 bar_arrive(sfree(sb));
+                // max of the raw scores, scaled once (c > 0 and rounding is monotone: the same value)
+                float mx = -INFINITY;
+                if (kv >= 32) {
 #pragma unroll
-                for (int i = 0; i < 32; i++)
-                    if (i < kv) lm = fmaxf(lm, sv[i >> 4][i & 15] * c);
+                    for (int i = 0; i < 32; i++) mx = fmaxf(mx, sv[i >> 4][i & 15]);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; i++)
+                        if (i < kv) mx = fmaxf(mx, sv[i >> 4][i & 15]);
+                }
+                lm = mx * c;
             }
             float* xt = xch + (size_t)(j & 1) * 2 * FQ;
             xt[hf * FQ + fr] = lm;
@@ -557,12 +565,22 @@ __global__ void __launch_bounds__(FA_THREADS) k_dit_attn_tc(const __grid_constan
                 mref = mt;
             }
             uint32_t pw[16];
+            if (kv >= 32) {   // a full tile: no per-key predicate
 #pragma unroll
-            for (int i = 0; i < 32; i += 2) {
-                const float p0 = i < kv ? ex2f(__fmaf_rn(sv[i >> 4][i & 15], c, -mref)) : 0.0f;
-                const float p1 = i + 1 < kv ? ex2f(__fmaf_rn(sv[i >> 4][(i + 1) & 15], c, -mref)) : 0.0f;
-                l += p0 + p1;
-                pw[i / 2] = pack_h2(p0, p1);
+                for (int i = 0; i < 32; i += 2) {
+                    const float p0 = ex2f(__fmaf_rn(sv[i >> 4][i & 15], c, -mref));
+                    const float p1 = ex2f(__fmaf_rn(sv[i >> 4][(i + 1) & 15], c, -mref));
+                    l += p0 + p1;
+                    pw[i / 2] = pack_h2(p0, p1);
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; i += 2) {
+                    const float p0 = i < kv ? ex2f(__fmaf_rn(sv[i >> 4][i & 15], c, -mref)) : 0.0f;
+                    const float p1 = i + 1 < kv ? ex2f(__fmaf_rn(sv[i >> 4][(i + 1) & 15], c, -mref)) : 0.0f;
+                    l += p0 + p1;
+                    pw[i / 2] = pack_h2(p0, p1);
+                }
             }
             const int pb = v & 1;
             if (!bar_wait_short_warp(pfree(pb), (((uint32_t)v >> 1) & 1u) ^ 1u, abort_flag)) {
